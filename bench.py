@@ -1,0 +1,346 @@
+#!/usr/bin/env python3
+"""Benchmark of the TempLit B200 backend on BASELINE.json's headline metric:
+tokens/s of the GPT d384 training step (configuration 4: vocab 2048, T 192,
+d_model 384, 4 pre-RMSNorm blocks, 6 heads, FFN 1536, batch 64 per GPU,
+Zipf(1.1) tokens, N(0, 0.02) weights, AdamW 3e-4 (0.9, 0.95) wd 0.1,
+clip 1.0), run through the reference's own model and compiler
+(nn::GPT + passes::Compiled) on cuda::Runtime via include/templit_gpt.h.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cuda|reference]
+
+One process per GPU (torchrun for N > 1); data parallel with one NCCL
+gradient all-reduce per step inside the runtime, per-GPU batch fixed
+(weak scaling).  Rank 0 prints one JSON line.  --impl reference times the
+CPU implementation of the same step (the oracle port of the reference's
+runtime ops, all host threads) on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "GPT d384 train tokens/s at 1/2/4/8 B200; GEMM/attn/HBM % roofline"
+VOCAB, SEQ, DMODEL, BLOCKS, HEADS, FFN = 2048, 192, 384, 4, 6, 1536
+WORKLOAD = ("configs[3] GPT train step: vocab 2048, T=192, d=384, 4 pre-RMSNorm blocks, "
+            "6 heads, GELU FFN 1536, batch 64 per GPU, AdamW 3e-4 (0.9,0.95) wd 0.1, clip 1.0")
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
+    p.add_argument("--batch", type=int, default=64, help="sequences per GPU")
+    p.add_argument("--no-fusion", action="store_true")
+    p.add_argument("--no-graphs", action="store_true")
+    p.add_argument("--profile", default="", help="write the per-op profile JSON here")
+    return p.parse_args()
+
+
+# ------------------------------------------------------------------ inputs
+def zipf_batch(rng, batch, seq, vocab=VOCAB, s=1.1):
+    """One Zipf(1.1) token stream over [0, vocab) cut into `batch` windows of
+    seq + 1 (inputs = [:seq], targets = [1:], as the reference loader)."""
+    p = 1.0 / np.arange(1, vocab + 1, dtype=np.float64) ** s
+    stream = rng.choice(vocab, size=batch * (seq + 1), p=p / p.sum()).astype(np.uint32)
+    w = stream.reshape(batch, seq + 1)
+    return np.ascontiguousarray(w[:, :seq]), np.ascontiguousarray(w[:, 1:])
+
+
+# --------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) >= 9
+                          for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_baseline_gpt(steps=1, batch=2):
+    """The same GPT step on the host: the oracle port of the reference's
+    runtime ops (oracle/cpu_ref) driven by the reference's passes::Compiled,
+    all host threads.  Bounded sample: `batch` sequences of 192 tokens."""
+    from oracle import cpu_gpt
+    if not cpu_gpt.available():
+        return None
+    threads = os.cpu_count() or 1
+    tok_s, secs = cpu_gpt.train_tokens_per_s(batch=batch, seq=SEQ, steps=steps, threads=threads)
+    return {"value": tok_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{steps} GPT d384 train step(s) at batch {batch} x T {SEQ} "
+                      f"({secs:.1f} s of CPU work), oracle port of the reference runtime ops "
+                      "under the reference passes::Compiled executor"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    base = cpu_baseline_gpt(steps=max(1, min(args.steps, 3)), batch=2)
+    if base is None:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle CPU GPT port (oracle/_build/libgpt_cpu.so) is not built"}))
+        return 0
+    line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": max(1, min(args.steps, 3)), "warmup": 0,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (Zipf(1.1) tokens, N(0,0.02) weights)",
+            "config": {"workload": WORKLOAD, "global_batch": 2, "seq_len": SEQ,
+                       "parallelism": "host threads"},
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+# ----------------------------------------------------------------- roofline
+def gemm_roofline(profile_path, peak_tflops, peak_source):
+    """Dominant kernel: the tcgen05 GEMM.  Achieved = executed GEMM FLOPs of
+    one profiled step / the GEMM launches' CUDA-event time."""
+    with open(profile_path) as f:
+        prof = json.load(f)["ops"]
+    flops = ms = 0.0
+    launches = 0
+    total_ms = sum(o["ms"] for o in prof)
+    for o in prof:
+        if not o["op"].startswith("gemm"):
+            continue
+        parts = o["op"].split()
+        m, n, k = (int(v) for v in parts[1].split("x"))
+        batch = int(parts[2][1:]) if len(parts) > 2 and parts[2].startswith("b") else 1
+        flops += 2.0 * m * n * k * batch * o["calls"]
+        ms += o["ms"]
+        launches += o["calls"]
+    if ms == 0:
+        return None, prof
+    achieved = flops / (ms * 1e-3) / 1e12
+    return {"bound": "tensor", "kernel": "tc_gemm_kernel (tcgen05 kind::tf32)",
+            "achieved": round(achieved, 1), "peak": peak_tflops, "unit": "TFLOP/s",
+            "frac": round(achieved / peak_tflops, 4) if peak_tflops else None,
+            "peak_source": peak_source, "traffic": None,
+            "flops_per_step": flops, "gemm_ms_per_step": round(ms, 4),
+            "gemm_launches_per_step": launches,
+            "gemm_share_of_step": round(ms / total_ms, 3) if total_ms else None}, prof
+
+
+def measure_tf32_peak(torch):
+    """cuBLAS TF32 dense throughput on this GPU (8192^3, best of 10): the
+    denominator for the TF32 GEMM (MEASURED_PEAKS.json holds bf16 only)."""
+    torch.backends.cuda.matmul.allow_tf32 = True
+    n = 8192
+    a = torch.randn(n, n, device="cuda")
+    b = torch.randn(n, n, device="cuda")
+    for _ in range(3):
+        a @ b
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(10):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        a @ b
+        e.record()
+        e.synchronize()
+        t = s.elapsed_time(e)
+        best = t if best is None else min(best, t)
+    del a, b
+    return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+
+
+# ----------------------------------------------------------------- main arm
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from templit_b200 import capi
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    lib = capi.gpt_lib()
+    cfg = capi.TlgConfig(family=4, batch=args.batch, seq=SEQ, seed=1234, init_std=0.02,
+                         lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, clip=1.0,
+                         world=world, fusion=0 if args.no_fusion else 1,
+                         graphs=0 if args.no_graphs else 1)
+    h = ctypes.c_void_p()
+    capi.check(lib.tlg_create(ctypes.byref(cfg), ctypes.byref(h)), lib, "tlg_create")
+    if world > 1:
+        uid = (ctypes.c_uint8 * 128)()
+        if rank == 0:
+            capi.check(lib.tlg_nccl_unique_id(uid), lib, "nccl id")
+        box = [bytes(uid)]
+        dist.broadcast_object_list(box, src=0)
+        uid = (ctypes.c_uint8 * 128).from_buffer_copy(box[0])
+        capi.check(lib.tlg_set_communicator(h, uid, world, rank), lib, "communicator")
+
+    stream = torch.cuda.ExternalStream(lib.tlg_stream(h))
+    rng = np.random.default_rng(1000 + rank)
+    B, T = args.batch, SEQ
+    n_tok = B * T
+    pin_x = torch.empty(n_tok, dtype=torch.int32).pin_memory()
+    pin_y = torch.empty(n_tok, dtype=torch.int32).pin_memory()
+    u32 = ctypes.POINTER(ctypes.c_uint32)
+
+    def load(x, y):
+        pin_x.numpy().view(np.uint32)[:] = x.ravel()
+        pin_y.numpy().view(np.uint32)[:] = y.ravel()
+        capi.check(lib.tlg_set_batch(h, ctypes.cast(pin_x.data_ptr(), u32),
+                                     ctypes.cast(pin_y.data_ptr(), u32)), lib, "set_batch")
+
+    loss = ctypes.c_float()
+
+    def step():
+        capi.check(lib.tlg_train_step(h, ctypes.byref(loss)), lib, "train_step")
+        return loss.value
+
+    batches = [zipf_batch(rng, B, T) for _ in range(4)]
+    load(*batches[0])
+    losses = [step() for _ in range(max(3, args.warmup))]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def timed(with_host_io):
+        barrier()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for i in range(args.steps):
+            if with_host_io:
+                load(*batches[i % len(batches)])
+            losses.append(step())
+        ev1.record(stream)
+        ev1.synchronize()
+        barrier()
+        ms = ev0.elapsed_time(ev1)
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    stats0 = (ctypes.c_uint64 * 8)()
+    capi.check(lib.tlg_stats(h, stats0), lib, "stats")
+    with ClockSampler(local) as clocks:
+        ms_value = timed(with_host_io=False)
+        ms_e2e = timed(with_host_io=True)
+    stats1 = (ctypes.c_uint64 * 8)()
+    capi.check(lib.tlg_stats(h, stats1), lib, "stats")
+    kernels = int(stats1[3] - stats0[3]) // 2  # two timed regions of K steps each
+
+    total_tokens = n_tok * world * args.steps
+    value = total_tokens / (ms_value * 1e-3)
+    e2e = total_tokens / (ms_e2e * 1e-3)
+
+    roof = None
+    prof_path = args.profile or os.path.join(ROOT, "gpurun_out", f"gpt_profile_rank{rank}.json")
+    try:
+        os.makedirs(os.path.dirname(prof_path), exist_ok=True)
+        capi.check(lib.tlg_profile(h, prof_path.encode(), 1), lib, "profile")
+        step()
+        if rank == 0:
+            peak = measure_tf32_peak(torch)
+            roof, _ = gemm_roofline(prof_path, round(peak, 1),
+                                    "cuBLAS TF32 8192^3 measured in this run (burst)")
+    except Exception as exc:  # the bench line still prints
+        roof = {"error": str(exc)}
+
+    if world > 1:
+        dist.barrier()
+    capi.check(lib.tlg_destroy(h), lib, "destroy")
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    cpu = cpu_baseline_gpt(steps=1, batch=2) if world == 1 else None
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": max(3, args.warmup),
+        "ms_per_step": round(ms_value / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (Zipf(1.1) token windows, N(0,0.02) weights, zero biases)",
+        "config": {"workload": WORKLOAD, "model": "nn::GPT<2048,192,384,6> (4 blocks)",
+                   "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world}",
+                   "gemm_operands": "tf32 tensor cores, fp32 accumulate",
+                   "l2": "per-step activations (GBs) exceed the 126 MB L2"},
+        "e2e": {"value": round(e2e, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": 2 * n_tok * 4, "d2h_bytes_per_step": n_tok * 4},
+        "gpu_launches": kernels,
+        "roofline": roof, "cpu_baseline": cpu, "clocks": clocks.summary(),
+        "loss_first_last": [round(losses[0], 4), round(losses[-1], 4)],
+        "runtime": {"windows": int(stats1[0]), "ops_recorded": int(stats1[1]),
+                    "ops_launched": int(stats1[2]), "graph_replays": int(stats1[4]),
+                    "graph_captures": int(stats1[5]), "fused_ops": int(stats1[6]),
+                    "peak_device_bytes": int(stats1[7])},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,296 @@
+/*
+ * templit_cuda.h - C ABI of the B200 (sm_100a) kernel library behind the
+ * TempLit `cuda` runtime.
+ *
+ * Every entry point takes plain pointers and sizes, returns an int status
+ * (TL_OK == 0) and never throws.  Device pointers are CUDA device memory;
+ * `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ * All launches are asynchronous on `stream`; argument errors are reported
+ * before anything is launched, launch errors through the return value, and
+ * data-dependent errors (an embedding id outside the table) through the
+ * device status word read by tl_device_status().  Text for the last failure
+ * on the calling thread is returned by tl_last_error().
+ *
+ * Each function names the reference interface it replaces: the
+ * `metal::Runtime` method (src/my_metal/runtime.cpp) and the Metal kernel it
+ * dispatches (include/my_metal/math.metal) in JTPuffer/TempLit.  Tensors are
+ * dense row-major fp32 (uint32 for token ids), the only layout
+ * RTensor produces (include/RTensor/RTensor.h:110-137,245-281).
+ */
+#ifndef TEMPLIT_CUDA_H
+#define TEMPLIT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TL_MAX_RANK 8
+
+enum tl_status_code {
+  TL_OK = 0,
+  TL_ERR_INVALID = 1,     /* bad argument: shape, rank, null pointer      */
+  TL_ERR_CUDA = 2,        /* CUDA runtime or launch failure               */
+  TL_ERR_UNSUPPORTED = 3, /* valid request this build cannot serve        */
+  TL_ERR_RANGE = 4        /* axis / size outside the supported range      */
+};
+
+/* Bits of the device status word (tl_device_status). */
+enum tl_device_flag {
+  TL_FLAG_INDEX_RANGE = 1u, /* an id >= table rows reached a gather/scatter */
+  TL_FLAG_TIMEOUT = 2u      /* a bounded on-device wait gave up (kernel returned early) */
+};
+
+/* ---------------------------------------------------------------- library */
+
+/* ABI version of this library (bumped on any signature change). */
+int tl_version(void);
+/* Message of the last failing call on this thread ("" if none). */
+const char *tl_last_error(void);
+/* Select and initialise `device`; replaces metal::init() (src/my_metal/metal.cpp:18-30). */
+int tl_device_init(int device);
+/* Synchronise `stream`, then read and clear the device status word. */
+int tl_device_status(uint32_t *flags, void *stream);
+
+/* ------------------------------------------- memory (Storage<Metal,T> ops) */
+/* Device allocation; replaces MTL::Device::newBuffer (include/my_metal/storage.h:13-16). */
+int tl_malloc(void **ptr, size_t bytes);
+int tl_free(void *ptr);
+/* Pinned host allocation for staging host<->device copies. */
+int tl_host_alloc(void **ptr, size_t bytes);
+int tl_host_free(void *ptr);
+int tl_stream_create(void **stream);
+int tl_stream_destroy(void *stream);
+int tl_stream_sync(void *stream);
+/* Stream-ordered copies; replace Storage::write/read/clone memcpy (include/my_metal/storage.h:25-52). */
+int tl_memcpy_h2d(void *dst, const void *src, size_t bytes, void *stream);
+int tl_memcpy_d2h(void *dst, const void *src, size_t bytes, void *stream);
+int tl_memcpy_d2d(void *dst, const void *src, size_t bytes, void *stream);
+/* Fill with a 32-bit pattern; replaces Storage::fill (include/my_metal/storage.h:41-43). */
+int tl_fill_u32(void *dst, uint32_t pattern, size_t count, void *stream);
+
+/* ---------------------- command recording (MTL::CommandBuffer counterparts) */
+/* Events for device-side timing; replace the Metal capture-manager profile
+ * hooks (src/my_metal/runtime.cpp:42-63). */
+int tl_event_create(void **event);
+int tl_event_destroy(void *event);
+int tl_event_record(void *event, void *stream);
+/* Milliseconds between two recorded events (waits for `end`). */
+int tl_event_elapsed_ms(float *ms, void *start, void *end);
+/* Stream capture into a replayable graph: the counterpart of encoding a
+ * command buffer once and committing it again (src/my_metal/runtime.cpp:290-317). */
+int tl_graph_capture_begin(void *stream);
+/* Ends the capture on `stream`; *graph_exec receives an instantiated graph
+ * (NULL and an error status if anything in the capture failed). */
+int tl_graph_capture_end(void *stream, void **graph_exec);
+int tl_graph_launch(void *graph_exec, void *stream);
+int tl_graph_destroy(void *graph_exec);
+/* Kernels this library has launched on this host thread so far (stream
+ * captures included): the runtime's launch accounting. */
+uint64_t tl_kernel_launches(void);
+
+/* ------------------------------------------------------------ elementwise */
+enum tl_binary_op { TL_ADD = 0, TL_SUB = 1, TL_MUL = 2, TL_DIV = 3 };
+/*
+ * out = a (op) b with trailing-aligned size-1 broadcasting against
+ * out_shape.  Replaces Runtime::add/sub/hadamard/divide
+ * (src/my_metal/runtime.cpp:18-39,65-95,321-353; math.metal:401-510).
+ * out may alias a or b element-for-element.
+ */
+int tl_binary(int op, const float *a, const uint32_t *a_shape, int a_rank,
+              const float *b, const uint32_t *b_shape, int b_rank, float *out,
+              const uint32_t *out_shape, int out_rank, void *stream);
+
+enum tl_scalar_op { TL_SCALAR_ADD = 0, TL_SCALAR_DIV = 1, TL_SCALAR_POW = 2 };
+/* out = x (op) s.  Replaces Runtime::add(a,s)/divide(a,s)/pow
+ * (src/my_metal/runtime.cpp:116-136,327-330,350-353,365-368; math.metal:427-434,511-518,527-534). */
+int tl_scalar(int op, const float *x, float s, float *out, size_t count,
+              void *stream);
+
+enum tl_unary_op {
+  TL_SIGMOID = 0,
+  TL_SQRT = 1,
+  TL_EXP = 2,
+  TL_GELU = 3,
+  TL_GELU_DERIVATIVE = 4
+};
+/* out = f(x).  Replaces Runtime::sigmoid/sqrt/exp/GELU/GELU_derivative
+ * (src/my_metal/runtime.cpp:97-114,355-373,1073-1081; math.metal:519-548,821-855). */
+int tl_unary(int op, const float *x, float *out, size_t count, void *stream);
+
+/* out = GELU'(x) * grad in one pass: the executor's GELU_derivative followed
+ * by its chain-rule hadamard (include/passes/autograd.h GELU rule;
+ * math.metal:835-855,461-485). */
+int tl_gelu_backward(const float *x, const float *grad, float *out,
+                     size_t count, void *stream);
+
+/* out = x.  Replaces Runtime::copy (src/my_metal/runtime.cpp:1170-1186; math.metal:1045-1051). */
+int tl_copy(const float *x, float *out, size_t count, void *stream);
+
+/* ------------------------------------------------------------- reductions */
+enum tl_reduce_op { TL_REDUCE_SUM = 0, TL_REDUCE_MAX = 1 };
+/*
+ * Reduce x to out_shape (trailing-aligned; every out dim equal to the x dim
+ * or 1).  Replaces Runtime::sum_to_shape / max_to_shape / reduce_to_shape
+ * (src/my_metal/runtime.cpp:595-745; math.metal:618-714).  Deterministic.
+ * workspace may be NULL when tl_reduce_workspace_size() returns 0.
+ */
+int tl_reduce(int op, const float *x, const uint32_t *x_shape, int x_rank,
+              float *out, const uint32_t *out_shape, int out_rank,
+              void *workspace, size_t workspace_bytes, void *stream);
+size_t tl_reduce_workspace_size(const uint32_t *x_shape, int x_rank,
+                                const uint32_t *out_shape, int out_rank);
+
+/* First index of the maximum of x[0..count) (NaN ignored, 0 if none).
+ * Replaces Runtime::argmax (src/my_metal/runtime.cpp:850-918; math.metal:715-777). */
+int tl_argmax(const float *x, size_t count, uint32_t *out_index,
+              void *workspace, size_t workspace_bytes, void *stream);
+size_t tl_argmax_workspace_size(size_t count);
+
+/* Materialised swap of axes dim_a, dim_b of a dense tensor.
+ * Replaces Runtime::transpose (src/my_metal/runtime.cpp:529-569; math.metal:566-584). */
+int tl_transpose(const float *x, const uint32_t *shape, int rank, int dim_a,
+                 int dim_b, float *out, void *stream);
+
+/* --------------------------------------------------------- row operators */
+/* Row softmax over the last dim.  Replaces Runtime::softmax
+ * (src/my_metal/runtime.cpp:747-766; math.metal:857-882). */
+int tl_softmax_rows(const float *x, float *out, uint32_t rows, uint32_t cols,
+                    void *stream);
+/* dx = y * (g - sum_row(g * y)): the SFTMX_DERIVATIVE rule
+ * (include/passes/execute.h:291-308) in one pass. */
+int tl_softmax_backward_rows(const float *grad, const float *y, float *dx,
+                             uint32_t rows, uint32_t cols, void *stream);
+/* rms[r] = sqrt(sum(x^2)/cols + 1e-6).  Replaces Runtime::RMS
+ * (src/my_metal/runtime.cpp:1031-1059). */
+int tl_rms_rows(const float *x, float *rms, uint32_t rows, uint32_t cols,
+                void *stream);
+/* out = x / rms(x) (rms_out optional).  Replaces Runtime::RMSNorm
+ * (src/my_metal/runtime.cpp:1061-1072). */
+int tl_rmsnorm_rows(const float *x, float *out, float *rms_out, uint32_t rows,
+                    uint32_t cols, void *stream);
+/* dx = (g - y * mean(g * y)) / rms(x): the RMSN_DERIVATIVE rule
+ * (include/passes/execute.h:330-356) in one pass. */
+int tl_rmsnorm_backward_rows(const float *grad, const float *x, const float *y,
+                             float *dx, uint32_t rows, uint32_t cols,
+                             void *stream);
+/* loss[r] = max + log(sum(exp(z - max))) - z[t]; +inf when t >= vocab.
+ * Replaces Runtime::cross_entropy (src/my_metal/runtime.cpp:768-804; math.metal:884-910). */
+int tl_xent_rows(const float *logits, const uint32_t *targets, float *loss,
+                 uint32_t rows, uint32_t vocab, void *stream);
+/* dz = (softmax(z) - onehot(t)) * row_scale[r] (row_scale NULL => 1); a row
+ * with t >= vocab is +inf.  Replaces Runtime::cross_entropy_derivative
+ * (src/my_metal/runtime.cpp:806-841; math.metal:912-953), optionally fused
+ * with the executor's hadamard by the root gradient. */
+int tl_xent_backward_rows(const float *logits, const uint32_t *targets,
+                          const float *row_scale, float *dlogits,
+                          uint32_t rows, uint32_t vocab, void *stream);
+
+/* -------------------------------------------------------------- embedding */
+/* out[i,:] = weights[ids[i],:].  Replaces Runtime::embedding_lookup /
+ * gather_rows (src/my_metal/runtime.cpp:920-950; math.metal:778-793).
+ * An id >= n_rows yields a zero row and sets TL_FLAG_INDEX_RANGE. */
+int tl_embedding_gather(const float *weights, uint32_t n_rows, uint32_t dim,
+                        const uint32_t *ids, uint32_t n_ids, float *out,
+                        void *stream);
+/* dst[r,:] = base[r,:] + sum of values[i,:] over i with ids[i] == r
+ * (base NULL => zeros; base may equal dst).  Replaces
+ * Runtime::scatter_add_rows (base given) and Runtime::scatter_index (base
+ * NULL) (src/my_metal/runtime.cpp:952-1030; math.metal:794-820).
+ * Deterministic: rows are bucketed by id (stable) and summed in input order.
+ * An id >= n_rows is skipped and sets TL_FLAG_INDEX_RANGE. */
+int tl_embedding_scatter_add(const float *values, const uint32_t *ids,
+                             uint32_t n_ids, uint32_t dim, const float *base,
+                             float *dst, uint32_t n_rows, void *workspace,
+                             size_t workspace_bytes, void *stream);
+size_t tl_embedding_scatter_workspace_size(uint32_t n_ids, uint32_t n_rows);
+
+/* -------------------------------------------------------------- optimiser */
+/* sqnorm[0] += sum(grad^2).  Replaces Runtime::accumulate_gradient_squared_norm
+ * (src/my_metal/runtime.cpp:1083-1101; math.metal:955-983).  Deterministic. */
+int tl_grad_sqnorm_accumulate(const float *grad, size_t count, float *sqnorm,
+                              void *workspace, size_t workspace_bytes,
+                              void *stream);
+size_t tl_grad_sqnorm_workspace_size(size_t count);
+/* out = grad * min(1, max_norm * rsqrt(max(sqnorm, 1e-12))).  Replaces
+ * Runtime::clip_gradient (src/my_metal/runtime.cpp:1103-1127; math.metal:985-1006). */
+int tl_clip_gradient(const float *grad, const float *sqnorm, float max_norm,
+                     float *out, size_t count, void *stream);
+/* AdamW with decoupled decay p*decay (decay = 1 - lr*wd).  Replaces
+ * Runtime::adamW (src/my_metal/runtime.cpp:1129-1168; math.metal:1008-1043;
+ * include/optimiser/AdamW.h:75-82).  beta1/beta2/decay/lr are device scalars. */
+int tl_adamw(const float *param, const float *grad, float *out, float *m1,
+             float *m2, const float *beta1, const float *beta2,
+             const float *decay, const float *lr, float epsilon, uint32_t step,
+             size_t count, void *stream);
+
+/* One parameter tensor of a fused multi-tensor optimiser pass. */
+typedef struct tl_param_slot {
+  const float *param; /* parameter read                                  */
+  float *out;         /* destination (may equal param)                   */
+  float *grad;        /* gradient (clipped in place when clipping)       */
+  float *m1;          /* first moment                                    */
+  float *m2;          /* second moment                                   */
+  uint64_t count;     /* elements                                        */
+  uint32_t chunk0;    /* index of this slot's first chunk: the sum of
+                         ceil(count / TL_OPT_CHUNK) over earlier slots   */
+  uint32_t step;      /* per-tensor AdamW step (>= 1)                    */
+} tl_param_slot;
+/* Elements per work chunk of the multi-tensor optimiser kernels. */
+#define TL_OPT_CHUNK 8192u
+/*
+ * The whole `Compiled::step(max_norm)` program (include/passes/compile.h:236-258)
+ * in two launches: sqnorm[0] += sum over all slots of grad^2, then for every
+ * slot grad = clip(grad), and the AdamW update.  max_norm <= 0 skips the norm
+ * and the clip (Compiled::step() without clipping, compile.h:223-234).
+ * `slots` is device memory holding n_slots records.
+ */
+int tl_multi_clip_adamw(const tl_param_slot *slots, uint32_t n_slots,
+                        uint32_t n_chunks, float *sqnorm, float max_norm,
+                        const float *beta1, const float *beta2,
+                        const float *decay, const float *lr, float epsilon,
+                        void *workspace, size_t workspace_bytes, void *stream);
+size_t tl_multi_clip_adamw_workspace_size(uint32_t n_chunks);
+
+/* ------------------------------------------------------------------- GEMM */
+enum tl_gemm_precision {
+  TL_GEMM_TF32 = 0,   /* tcgen05 kind::tf32 tensor cores, fp32 accumulate */
+  TL_GEMM_FP32 = 1,   /* CUDA-core fp32 FMA (exact fp32 products)         */
+  TL_GEMM_3XTF32 = 2  /* tcgen05 with split big/small tf32 operands        */
+};
+#define TL_GEMM_MAX_BATCH_RANK 6
+/*
+ * C[b] = op(A[b]) * op(B[b]) (+ bias) (+ beta * C[b]) for every batch index
+ * b of batch_shape, with per-operand batch strides in elements (0 =
+ * broadcast).  trans_a = 0: A[b] is [M,K] row-major, 1: stored [K,M].
+ * trans_b = 0: B[b] is [K,N] row-major, 1: stored [N,K].  Replaces
+ * Runtime::mult (src/my_metal/runtime.cpp:375-505; math.metal:13-400) and,
+ * through trans_a/trans_b, the executor's transpose+mult pairs of
+ * EXPR_MULT_{LHS,RHS}_DERIVATIVE (include/passes/execute.h:187-232).
+ * gelu_out (optional) receives GELU of the final value.
+ */
+typedef struct tl_gemm_desc {
+  const float *a;
+  const float *b;
+  float *c;
+  const float *bias; /* optional [N], added to every row               */
+  float *gelu_out;   /* optional, same layout as c                     */
+  uint32_t m, n, k;
+  int32_t trans_a, trans_b;
+  int32_t precision; /* tl_gemm_precision                               */
+  float beta;        /* 0 or 1                                          */
+  uint32_t batch_rank;
+  uint32_t batch_shape[TL_GEMM_MAX_BATCH_RANK];
+  uint64_t a_batch_stride[TL_GEMM_MAX_BATCH_RANK];
+  uint64_t b_batch_stride[TL_GEMM_MAX_BATCH_RANK];
+  uint64_t c_batch_stride[TL_GEMM_MAX_BATCH_RANK];
+} tl_gemm_desc;
+int tl_gemm(const tl_gemm_desc *desc, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TEMPLIT_CUDA_H */

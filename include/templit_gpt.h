@@ -1,0 +1,70 @@
+/*
+ * templit_gpt.h - C ABI of the GPT training step built from TempLit's own
+ * model and compiler (include/nn/GPT.h, include/passes/compile.h in
+ * JTPuffer/TempLit) on the `cuda` runtime.
+ *
+ * One handle owns a compiled `nn::GPT<Mat, vocab, max_seq, d_model, heads>`
+ * with its cross-entropy loss and AdamW optimiser, exactly as
+ * src/train.cpp:89-157 builds it, with the backend alias switched to
+ * RTensor<cuda::CUDA, float>.  tlg_train_step runs one iteration of the
+ * reference training loop: set inputs, zero_grad, forward, read the losses,
+ * backward with root gradient 1/(rank-local tokens * world), step(clip).
+ *
+ * Model families: `family` 4 is the reference's 4-block GPT (d_model 384,
+ * 6 heads, vocab 2048, max sequence 192); `family` 12 the 12-block,
+ * d_model 768, 12-head, max-sequence-1024 variant of the data-parallel
+ * configuration.  All calls return 0 on success; tlg_last_error() explains
+ * a failure.
+ */
+#ifndef TEMPLIT_GPT_H
+#define TEMPLIT_GPT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct tlg_config {
+  uint32_t family;       /* 4 or 12 (see above)                                */
+  uint32_t batch;        /* sequences per rank                                 */
+  uint32_t seq;          /* tokens per sequence (<= the family's max sequence) */
+  uint32_t seed;         /* std::mt19937 seed of the reference initialiser     */
+  float init_std;        /* > 0: re-draw every weight N(0, init_std), biases 0 */
+  float lr, beta1, beta2, eps, weight_decay;
+  float clip;            /* > 0: Compiled::step(clip), else Compiled::step()    */
+  uint32_t world;        /* data-parallel ranks sharing the global batch       */
+  int32_t fusion;        /* runtime program fusion on/off                      */
+  int32_t graphs;        /* CUDA-graph replay on/off                           */
+} tlg_config;
+
+const char *tlg_last_error(void);
+int tlg_create(const tlg_config *config, void **handle);
+int tlg_destroy(void *handle);
+/* Host token ids and targets, batch*seq each (row-major [batch, seq]). */
+int tlg_set_batch(void *handle, const uint32_t *tokens, const uint32_t *targets);
+/* One training iteration; *mean_loss receives the mean loss of this rank's batch. */
+int tlg_train_step(void *handle, float *mean_loss);
+/* Forward only; losses receives batch*seq per-token losses. */
+int tlg_forward(void *handle, float *losses);
+/* Parameters in the compiler's gradient-path order, concatenated. */
+int tlg_param_count(void *handle, uint64_t *count, uint32_t *tensors);
+int tlg_get_params(void *handle, float *out, uint64_t count);
+int tlg_set_params(void *handle, const float *in, uint64_t count);
+/* The backend stream (cudaStream_t) every launch of this handle uses. */
+void *tlg_stream(void *handle);
+/* Runtime counters: windows, recorded ops, launched ops, kernels, graph replays. */
+int tlg_stats(void *handle, uint64_t out[8]);
+/* Data parallelism: NCCL unique id (128 bytes) made on rank 0 and shared
+ * by the caller, then a communicator on every rank. */
+int tlg_nccl_unique_id(uint8_t id[128]);
+int tlg_set_communicator(void *handle, const uint8_t id[128], int nranks, int rank);
+/* Per-op device timing of the next `steps` train steps, written as JSON. */
+int tlg_profile(void *handle, const char *path, int steps);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TEMPLIT_GPT_H */

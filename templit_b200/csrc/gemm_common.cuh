@@ -1,0 +1,60 @@
+// Shared GEMM argument block, batch decoding and epilogue for the tensor-core
+// (tcgen05) and CUDA-core GEMM kernels behind tl_gemm.
+#pragma once
+
+#include "tl_common.cuh"
+
+namespace tl {
+
+struct GemmArgs {
+  const float *a;
+  const float *b;
+  float *c;
+  const float *bias;
+  float *gelu_out;
+  uint32_t m, n, k;
+  int trans_a, trans_b;
+  float beta;
+  uint32_t batch_rank;
+  uint32_t batch_shape[TL_GEMM_MAX_BATCH_RANK];
+  uint64_t sa[TL_GEMM_MAX_BATCH_RANK];
+  uint64_t sb[TL_GEMM_MAX_BATCH_RANK];
+  uint64_t sc[TL_GEMM_MAX_BATCH_RANK];
+  uint64_t batch_count;
+  uint64_t batch_base;  // first batch index of this launch
+};
+
+// Element offsets of batch `z` (relative to batch_base) in A, B and C.
+__device__ __forceinline__ void batch_offsets(const GemmArgs &g, uint64_t z,
+                                              uint64_t &oa, uint64_t &ob,
+                                              uint64_t &oc) {
+  uint64_t b = g.batch_base + z;
+  oa = ob = oc = 0;
+  for (int d = static_cast<int>(g.batch_rank) - 1; d >= 0; --d) {
+    const uint64_t c = b % g.batch_shape[d];
+    b /= g.batch_shape[d];
+    oa += c * g.sa[d];
+    ob += c * g.sb[d];
+    oc += c * g.sc[d];
+  }
+}
+
+// Final value of C[idx] (idx relative to the batch's C base `Cb`, column n):
+// v = A*B (+ bias[n]) (+ C) - the reference adds the bias after the product
+// (EXPR_LINEAR: mult then add, include/passes/execute.h:241-252) and gradient
+// accumulation adds the new term to the old (context.h:74-89).
+__device__ __forceinline__ void epilogue_store(const GemmArgs &g, float *Cb,
+                                               uint64_t oc, size_t idx,
+                                               uint32_t n, float v) {
+  if (g.bias) v = v + g.bias[n];
+  if (g.beta != 0.0f) v = Cb[idx] + v;
+  Cb[idx] = v;
+  if (g.gelu_out) g.gelu_out[oc + idx] = gelu_f(v);
+}
+
+int launch_sgemm(const GemmArgs &g, cudaStream_t s);
+// Returns TL_ERR_UNSUPPORTED when the operands do not meet the tensor-core
+// path's alignment rules; the caller then falls back to launch_sgemm.
+int launch_tc_gemm(const GemmArgs &g, cudaStream_t s);
+
+}  // namespace tl

@@ -1,0 +1,71 @@
+// tl_gemm: validates the descriptor and routes to the tcgen05 tensor-core
+// kernel (TL_GEMM_TF32) or the CUDA-core fp32 kernel (TL_GEMM_FP32, tiny
+// problems, and operands TMA cannot address).
+#include "gemm_common.cuh"
+
+#include <cstdlib>
+#include <cstring>
+
+namespace tl {
+namespace {
+
+// Problems below this many multiply-adds finish faster on CUDA cores than a
+// persistent tensor-core launch can be set up.
+constexpr uint64_t kTcMinMacs = 1ull << 20;
+
+bool force_fp32_from_env() {
+  static const bool v = [] {
+    const char *e = std::getenv("TL_GEMM_FORCE_FP32");
+    return e && std::strcmp(e, "0") != 0;
+  }();
+  return v;
+}
+
+}  // namespace
+}  // namespace tl
+
+using namespace tl;
+
+extern "C" int tl_gemm(const tl_gemm_desc *d, void *stream) {
+  if (!d) return fail(TL_ERR_INVALID, "tl_gemm: null descriptor");
+  if (d->batch_rank > TL_GEMM_MAX_BATCH_RANK)
+    return fail(TL_ERR_INVALID, "tl_gemm: batch rank too large");
+  if (d->beta != 0.0f && d->beta != 1.0f)
+    return fail(TL_ERR_INVALID, "tl_gemm: beta must be 0 or 1");
+  if (d->precision < TL_GEMM_TF32 || d->precision > TL_GEMM_3XTF32)
+    return fail(TL_ERR_INVALID, "tl_gemm: unknown precision");
+  GemmArgs g{};
+  g.a = d->a;
+  g.b = d->b;
+  g.c = d->c;
+  g.bias = d->bias;
+  g.gelu_out = d->gelu_out;
+  g.m = d->m;
+  g.n = d->n;
+  g.k = d->k;
+  g.trans_a = d->trans_a != 0;
+  g.trans_b = d->trans_b != 0;
+  g.beta = d->beta;
+  g.batch_rank = d->batch_rank;
+  g.batch_count = 1;
+  for (uint32_t i = 0; i < d->batch_rank; ++i) {
+    g.batch_shape[i] = d->batch_shape[i];
+    g.sa[i] = d->a_batch_stride[i];
+    g.sb[i] = d->b_batch_stride[i];
+    g.sc[i] = d->c_batch_stride[i];
+    g.batch_count *= d->batch_shape[i];
+  }
+  if (g.m == 0 || g.n == 0 || g.batch_count == 0) return TL_OK;
+  if (!g.c || (g.k && (!g.a || !g.b))) return fail(TL_ERR_INVALID, "tl_gemm: null pointer");
+  cudaStream_t s = as_stream(stream);
+  const uint64_t macs = static_cast<uint64_t>(g.m) * g.n * g.k * g.batch_count;
+  const bool want_tc = d->precision != TL_GEMM_FP32 && !force_fp32_from_env() &&
+                       macs >= kTcMinMacs && g.k > 0;
+  if (want_tc) {
+    if (d->precision == TL_GEMM_3XTF32)
+      return fail(TL_ERR_UNSUPPORTED, "tl_gemm: 3xTF32 is not built in this version");
+    const int rc = launch_tc_gemm(g, s);
+    if (rc != TL_ERR_UNSUPPORTED) return rc;
+  }
+  return launch_sgemm(g, s);
+}

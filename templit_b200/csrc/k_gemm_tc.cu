@@ -1,0 +1,393 @@
+// Tensor-core GEMM for sm_100a: tcgen05.mma kind::tf32 with fp32
+// accumulation in TMEM, operands staged by TMA (no multicast).
+//
+// Persistent, warp-specialised CTA of 192 threads (one CTA per SM):
+//   warp 0      TMA producer: STAGES-deep ring of (A, B) k-tiles in smem
+//   warp 1      TMEM owner + MMA issuer (one thread issues tcgen05.mma)
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator, bias / accumulate /
+//               GELU, 128-bit stores to C
+// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
+// the MMAs of tile i+1.  CTA tile 128 x BN x 32 (32 fp32 = one 128-byte
+// swizzle row).  Operand majorness follows the stored layout:
+//   A [M,K] row-major  -> K-major, TMA SWIZZLE_128B
+//   A stored [K,M]     -> MN-major, TMA SWIZZLE_128B_ATOM_32B (tf32 MN-major
+//                         operands only accept this 32-byte-atom swizzle)
+//   B [K,N] row-major  -> MN-major;  B stored [N,K] -> K-major
+// so the executor's NN, NT (transposed B) and TN (transposed A) products
+// need no transpose pass.  Batched operands use a 3-D tensor map whose third
+// dimension walks whole matrices, so a k-tile never reads a neighbour's rows.
+//
+// Every mbarrier wait is bounded (2 s): on timeout the CTA raises
+// TL_FLAG_TIMEOUT in the device status word, drains what it issued and
+// returns instead of hanging the GPU.
+#include "gemm_common.cuh"
+#include "tc_ptx.cuh"
+
+#include <cuda.h>
+
+#include <mutex>
+
+namespace tl {
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int BM = 128, BK = 32;
+constexpr uint32_t kA_BYTES = BM * BK * 4;  // 16 KB
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr uint32_t kFlagTimeout = TL_FLAG_TIMEOUT;
+
+struct TcArgs {
+  GemmArgs g;
+  uint32_t mt, nt;        // tiles along M and N
+  uint64_t num_tiles;     // batch * mt * nt
+  uint64_t a_mat, b_mat;  // elements per A / B matrix
+  uint32_t *status;
+};
+
+template <int BN>
+struct Cfg {
+  static constexpr uint32_t B_BYTES = BN * BK * 4;
+  static constexpr uint32_t STAGE_BYTES = kA_BYTES + B_BYTES;
+  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + 256;
+};
+
+__device__ __forceinline__ void decode_tile(const TcArgs &t, uint64_t tile, uint64_t &z,
+                                            uint32_t &mb, uint32_t &nb) {
+  mb = static_cast<uint32_t>(tile % t.mt);
+  const uint64_t r = tile / t.mt;
+  nb = static_cast<uint32_t>(r % t.nt);
+  z = r / t.nt;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+               const __grid_constant__ CUtensorMap tmB, const TcArgs t) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *stage_base = smem;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + C::STAGES;
+  uint64_t *tfull = bars + 2 * C::STAGES;
+  uint64_t *tempty = tfull + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+  volatile uint32_t *abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const GemmArgs &g = t.g;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(&tfull[a], 1);
+      ptx::mbar_init(&tempty[a], 128);
+    }
+    *abort_flag = 0;
+    ptx::fence_barrier_init();
+    ptx::fence_proxy_async_smem();
+    ptx::prefetch_tensormap(&tmA);
+    ptx::prefetch_tensormap(&tmB);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, C::TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t ktiles = (g.k + BK - 1) / BK;
+
+  auto timeout = [&]() {
+    *abort_flag = 1;
+    raise_flag(t.status, kFlagTimeout);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      uint64_t issued = 0;
+      for (uint64_t tile = blockIdx.x; tile < t.num_tiles && !*abort_flag;
+           tile += gridDim.x) {
+        uint64_t z;
+        uint32_t mb, nb;
+        decode_tile(t, tile, z, mb, nb);
+        uint64_t oa, ob, oc;
+        batch_offsets(g, z, oa, ob, oc);
+        const int32_t za = static_cast<int32_t>(oa / t.a_mat);
+        const int32_t zb = static_cast<int32_t>(ob / t.b_mat);
+        const int32_t m0 = static_cast<int32_t>(mb * BM), n0 = static_cast<int32_t>(nb * BN);
+        for (uint32_t kb = 0; kb < ktiles; ++kb) {
+          if (!ptx::mbar_wait_bounded(&empty[stage], phase ^ 1, kWaitLimitNs)) {
+            timeout();
+            break;
+          }
+          uint8_t *sa = stage_base + stage * C::STAGE_BYTES;
+          uint8_t *sb = sa + kA_BYTES;
+          ptx::mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          const int32_t k0 = static_cast<int32_t>(kb * BK);
+          if (!A_MN) {
+            ptx::tma_load_3d(sa, &tmA, &full[stage], k0, m0, za);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 32; ++j)
+              ptx::tma_load_3d(sa + j * 4096, &tmA, &full[stage], m0 + 32 * j, k0, za);
+          }
+          if (!B_MN) {
+            ptx::tma_load_3d(sb, &tmB, &full[stage], k0, n0, zb);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 32; ++j)
+              ptx::tma_load_3d(sb + j * 4096, &tmB, &full[stage], n0 + 32 * j, k0, zb);
+          }
+          ++issued;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: every issued k-tile must have landed before the CTA may exit.
+      uint64_t back = issued < static_cast<uint64_t>(C::STAGES) ? issued : C::STAGES;
+      uint32_t s = stage, p = phase;
+      for (uint64_t i = 0; i < back; ++i) {
+        if (s == 0) {
+          s = C::STAGES - 1;
+          p ^= 1;
+        } else {
+          --s;
+        }
+        if (!ptx::mbar_wait_bounded(&full[s], p, kWaitLimitNs)) {
+          timeout();
+          break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = ptx::idesc_tf32(BM, BN, A_MN, B_MN);
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool issued_any = false;
+      for (uint64_t tile = blockIdx.x; tile < t.num_tiles && !*abort_flag;
+           tile += gridDim.x) {
+        if (!ptx::mbar_wait_bounded(&tempty[acc], acc_phase ^ 1, kWaitLimitNs)) {
+          timeout();
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (uint32_t kb = 0; kb < ktiles; ++kb) {
+          if (!ptx::mbar_wait_bounded(&full[stage], phase, kWaitLimitNs)) {
+            timeout();
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t sa = ptx::smem_addr(stage_base + stage * C::STAGE_BYTES);
+          const uint32_t sb = sa + kA_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; ++kk) {
+            const uint64_t ad =
+                A_MN ? ptx::smem_desc(sa + kk * 1024, 4096, 512, ptx::kSwizzle128B32BAtom)
+                     : ptx::smem_desc(sa + kk * 32, 16, 1024, ptx::kSwizzle128B);
+            const uint64_t bd =
+                B_MN ? ptx::smem_desc(sb + kk * 1024, 4096, 512, ptx::kSwizzle128B32BAtom)
+                     : ptx::smem_desc(sb + kk * 32, 16, 1024, ptx::kSwizzle128B);
+            ptx::mma_tf32(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          ptx::mma_commit(&empty[stage]);  // stage reusable once these MMAs finish
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        ptx::mma_commit(&tfull[acc]);  // accumulator ready for the epilogue
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (*abort_flag && issued_any) {
+        // let in-flight MMAs finish before TMEM is released
+        ptx::mma_commit(&tfull[acc]);
+        ptx::mbar_wait_bounded(&tfull[acc], acc_phase, kWaitLimitNs);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    uint32_t acc = 0, acc_phase = 0;
+    for (uint64_t tile = blockIdx.x; tile < t.num_tiles; tile += gridDim.x) {
+      // warp-uniform decisions: tcgen05.ld below needs all 32 lanes
+      const bool got = ptx::mbar_wait_bounded(&tfull[acc], acc_phase, kWaitLimitNs);
+      if (!__all_sync(0xffffffffu, got)) {
+        if (lane == 0) timeout();
+        break;
+      }
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+      ptx::tc_fence_after();
+      uint64_t z;
+      uint32_t mb, nb;
+      decode_tile(t, tile, z, mb, nb);
+      uint64_t oa, ob, oc;
+      batch_offsets(g, z, oa, ob, oc);
+      float *Cb = g.c + oc;
+      const uint32_t m = mb * BM + q * 32 + lane;
+      const uint32_t n_base = nb * BN;
+      const bool row_ok = m < g.m;
+      const bool fast = (g.n % 4) == 0 && aligned16(Cb) && !g.gelu_out && !g.bias &&
+                        g.beta == 0.0f;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        ptx::tmem_load_32x32b_x32(tmem_base + acc * BN + c * 32 + ((q * 32u) << 16), r);
+        ptx::tmem_load_wait();
+        const uint32_t n0 = n_base + c * 32;
+        if (!row_ok || n0 >= g.n) continue;
+        const size_t rowoff = static_cast<size_t>(m) * g.n;
+        if (fast && n0 + 32 <= g.n) {
+          float4 *dst = reinterpret_cast<float4 *>(Cb + rowoff + n0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const uint32_t n = n0 + j;
+            if (n < g.n) epilogue_store(g, Cb, oc, rowoff + n, n, __uint_as_float(r[j]));
+          }
+        }
+      }
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  if (warp == 1) ptx::tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+// ---------------------------------------------------------------- host side
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 3-D map over `nmat` matrices of [outer][inner] fp32 with a box of
+// box_inner x box_outer x 1.
+bool make_map(CUtensorMap *map, const float *base, uint64_t inner, uint64_t outer,
+              uint64_t nmat, uint32_t box_inner, uint32_t box_outer,
+              CUtensorMapSwizzle swz) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {inner, outer, nmat};
+  const cuuint64_t strides[2] = {inner * 4, inner * outer * 4};
+  const cuuint32_t box[3] = {box_inner, box_outer, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides,
+             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+uint64_t matrices_spanned(const GemmArgs &g, const uint64_t *strides, uint64_t mat) {
+  uint64_t last = 0;
+  for (uint32_t d = 0; d < g.batch_rank; ++d) last += (g.batch_shape[d] - 1) * strides[d];
+  return last / mat + 1;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+int launch_variant(const GemmArgs &g, cudaStream_t s) {
+  using C = Cfg<BN>;
+  TcArgs t{};
+  t.g = g;
+  t.mt = (g.m + BM - 1) / BM;
+  t.nt = (g.n + BN - 1) / BN;
+  t.num_tiles = g.batch_count * t.mt * t.nt;
+  t.a_mat = static_cast<uint64_t>(g.m) * g.k;
+  t.b_mat = static_cast<uint64_t>(g.k) * g.n;
+  t.status = device_status_ptr();
+  if (!t.status) return fail(TL_ERR_CUDA, "tl_gemm: no status word");
+  CUtensorMap ma, mb;
+  const uint64_t na = matrices_spanned(g, g.sa, t.a_mat);
+  const uint64_t nbm = matrices_spanned(g, g.sb, t.b_mat);
+  bool ok = A_MN ? make_map(&ma, g.a, g.m, g.k, na, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)
+                 : make_map(&ma, g.a, g.k, g.m, na, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  ok = ok && (B_MN ? make_map(&mb, g.b, g.n, g.k, nbm, 32, 32,
+                              CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)
+                   : make_map(&mb, g.b, g.k, g.n, nbm, 32, BN, CU_TENSOR_MAP_SWIZZLE_128B));
+  if (!ok) return fail(TL_ERR_UNSUPPORTED, "tl_gemm: tensor map rejected");
+  static bool attr_set = false;
+  if (!attr_set) {
+    int rc = check_cuda(cudaFuncSetAttribute(tc_gemm_kernel<BN, A_MN, B_MN>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(C::SMEM)),
+                        "tl_gemm smem attribute");
+    if (rc) return rc;
+    attr_set = true;
+  }
+  const uint64_t grid = t.num_tiles < static_cast<uint64_t>(kNumSMs) ? t.num_tiles : kNumSMs;
+  tc_gemm_kernel<BN, A_MN, B_MN><<<static_cast<unsigned>(grid), kThreads, C::SMEM, s>>>(ma, mb, t);
+  return launch_status("tl_gemm tf32");
+}
+
+template <int BN>
+int launch_bn(const GemmArgs &g, cudaStream_t s) {
+  const bool a_mn = g.trans_a != 0, b_mn = g.trans_b == 0;
+  if (a_mn && b_mn) return launch_variant<BN, true, true>(g, s);
+  if (a_mn) return launch_variant<BN, true, false>(g, s);
+  if (b_mn) return launch_variant<BN, false, true>(g, s);
+  return launch_variant<BN, false, false>(g, s);
+}
+
+}  // namespace
+
+int launch_tc_gemm(const GemmArgs &g, cudaStream_t s) {
+  // TMA rules: 16-byte aligned bases, row strides and matrix strides.
+  const uint32_t a_inner = g.trans_a ? g.m : g.k;
+  const uint32_t b_inner = g.trans_b ? g.k : g.n;
+  if (g.k == 0 || a_inner % 4 || b_inner % 4 || !aligned16(g.a) || !aligned16(g.b))
+    return TL_ERR_UNSUPPORTED;
+  for (uint32_t d = 0; d < g.batch_rank; ++d)
+    if (g.sa[d] % 4 || g.sb[d] % 4) return TL_ERR_UNSUPPORTED;
+  if (g.m > 0x7fffffffu || g.n > 0x7fffffffu || g.k > 0x7fffffffu) return TL_ERR_UNSUPPORTED;
+  if (g.n > 128) return launch_bn<256>(g, s);
+  if (g.n > 64) return launch_bn<128>(g, s);
+  return launch_bn<64>(g, s);
+}
+
+}  // namespace tl

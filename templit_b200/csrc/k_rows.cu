@@ -1,0 +1,339 @@
+// Row operators over the last dimension: softmax (+ backward), RMS, RMSNorm
+// (+ backward) and softmax cross-entropy (+ backward).
+//
+// The reference runs these one thread per row with three serial passes
+// (include/my_metal/math.metal:857-953) and composes RMS/RMSNorm and their
+// derivatives from five to seven separate dispatches
+// (src/my_metal/runtime.cpp:1031-1072; include/passes/execute.h:291-356).
+// Here one warp owns a row: a first pass over the row keeps a per-lane online
+// (max, sum-of-exp) or sum-of-squares in registers and merges it across the
+// warp with shuffles, a second pass writes the result (the re-read is served
+// from L1/L2).  Rows are 128-bit vectorised when the row length allows.
+#include "tl_common.cuh"
+
+#include <initializer_list>
+
+namespace tl {
+namespace {
+
+constexpr int kWarpsPerBlock = 8;
+
+__device__ __forceinline__ void online_add(float &m, float &s, float x) {
+  if (x > m) {
+    s = s * expf(m - x) + 1.0f;
+    m = x;
+  } else {
+    s += expf(x - m);
+  }
+}
+
+__device__ __forceinline__ void warp_online(float &m, float &s) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    online_merge(m, s, m2, s2);
+  }
+}
+
+// Per-lane (max, sum exp) over a row, merged across the warp.
+__device__ __forceinline__ void row_logsumexp(const float *xr, uint32_t cols,
+                                              bool vec, uint32_t lane, float &m,
+                                              float &s) {
+  m = -INFINITY;
+  s = 0.0f;
+  if (vec) {
+    for (uint32_t c = lane * 4; c < cols; c += 128) {
+      const float4 v = *reinterpret_cast<const float4 *>(xr + c);
+      online_add(m, s, v.x);
+      online_add(m, s, v.y);
+      online_add(m, s, v.z);
+      online_add(m, s, v.w);
+    }
+  } else {
+    for (uint32_t c = lane; c < cols; c += 32) online_add(m, s, xr[c]);
+  }
+  warp_online(m, s);
+}
+
+__device__ __forceinline__ float row_dot(const float *a, const float *b,
+                                         uint32_t cols, bool vec, uint32_t lane) {
+  float acc = 0.0f;
+  if (vec) {
+    for (uint32_t c = lane * 4; c < cols; c += 128) {
+      const float4 u = *reinterpret_cast<const float4 *>(a + c);
+      const float4 w = *reinterpret_cast<const float4 *>(b + c);
+      acc += u.x * w.x + u.y * w.y + u.z * w.z + u.w * w.w;
+    }
+  } else {
+    for (uint32_t c = lane; c < cols; c += 32) acc += a[c] * b[c];
+  }
+  return warp_sum(acc);
+}
+
+#define ROW_LOOP                                                             \
+  const uint32_t lane = threadIdx.x & 31;                                    \
+  const uint32_t warps = gridDim.x * kWarpsPerBlock;                         \
+  for (uint32_t row = blockIdx.x * kWarpsPerBlock + threadIdx.x / 32;        \
+       row < rows; row += warps)
+
+__global__ void __launch_bounds__(256)
+softmax_kernel(const float *__restrict__ x, float *out, uint32_t rows,
+               uint32_t cols, bool vec) {
+  ROW_LOOP {
+    const float *xr = x + static_cast<size_t>(row) * cols;
+    float *yr = out + static_cast<size_t>(row) * cols;
+    float m, s;
+    row_logsumexp(xr, cols, vec, lane, m, s);
+    if (vec) {
+      for (uint32_t c = lane * 4; c < cols; c += 128) {
+        float4 v = *reinterpret_cast<const float4 *>(xr + c);
+        v.x = expf(v.x - m) / s;
+        v.y = expf(v.y - m) / s;
+        v.z = expf(v.z - m) / s;
+        v.w = expf(v.w - m) / s;
+        *reinterpret_cast<float4 *>(yr + c) = v;
+      }
+    } else {
+      for (uint32_t c = lane; c < cols; c += 32) yr[c] = expf(xr[c] - m) / s;
+    }
+  }
+}
+
+// dx = y * (g - sum(g*y))
+__global__ void __launch_bounds__(256)
+softmax_backward_kernel(const float *__restrict__ g, const float *__restrict__ y,
+                        float *dx, uint32_t rows, uint32_t cols, bool vec) {
+  ROW_LOOP {
+    const size_t off = static_cast<size_t>(row) * cols;
+    const float dot = row_dot(g + off, y + off, cols, vec, lane);
+    if (vec) {
+      for (uint32_t c = lane * 4; c < cols; c += 128) {
+        const float4 gv = *reinterpret_cast<const float4 *>(g + off + c);
+        const float4 yv = *reinterpret_cast<const float4 *>(y + off + c);
+        float4 r;
+        r.x = yv.x * (gv.x - dot);
+        r.y = yv.y * (gv.y - dot);
+        r.z = yv.z * (gv.z - dot);
+        r.w = yv.w * (gv.w - dot);
+        *reinterpret_cast<float4 *>(dx + off + c) = r;
+      }
+    } else {
+      for (uint32_t c = lane; c < cols; c += 32) dx[off + c] = y[off + c] * (g[off + c] - dot);
+    }
+  }
+}
+
+__device__ __forceinline__ float row_rms(const float *xr, uint32_t cols, bool vec,
+                                         uint32_t lane) {
+  const float ss = row_dot(xr, xr, cols, vec, lane);
+  return sqrtf(ss / static_cast<float>(cols) + 1e-6f);
+}
+
+__global__ void __launch_bounds__(256)
+rms_kernel(const float *__restrict__ x, float *rms, uint32_t rows, uint32_t cols,
+           bool vec) {
+  ROW_LOOP {
+    const float r = row_rms(x + static_cast<size_t>(row) * cols, cols, vec, lane);
+    if (lane == 0) rms[row] = r;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+rmsnorm_kernel(const float *__restrict__ x, float *out, float *rms_out,
+               uint32_t rows, uint32_t cols, bool vec) {
+  ROW_LOOP {
+    const float *xr = x + static_cast<size_t>(row) * cols;
+    float *yr = out + static_cast<size_t>(row) * cols;
+    const float r = row_rms(xr, cols, vec, lane);
+    if (rms_out && lane == 0) rms_out[row] = r;
+    if (vec) {
+      for (uint32_t c = lane * 4; c < cols; c += 128) {
+        float4 v = *reinterpret_cast<const float4 *>(xr + c);
+        v.x /= r;
+        v.y /= r;
+        v.z /= r;
+        v.w /= r;
+        *reinterpret_cast<float4 *>(yr + c) = v;
+      }
+    } else {
+      for (uint32_t c = lane; c < cols; c += 32) yr[c] = xr[c] / r;
+    }
+  }
+}
+
+// dx = (g - y * (sum(g*y)/D)) / rms(x)
+__global__ void __launch_bounds__(256)
+rmsnorm_backward_kernel(const float *__restrict__ g, const float *__restrict__ x,
+                        const float *__restrict__ y, float *dx, uint32_t rows,
+                        uint32_t cols, bool vec) {
+  ROW_LOOP {
+    const size_t off = static_cast<size_t>(row) * cols;
+    const float r = row_rms(x + off, cols, vec, lane);
+    const float mean = row_dot(g + off, y + off, cols, vec, lane) / static_cast<float>(cols);
+    if (vec) {
+      for (uint32_t c = lane * 4; c < cols; c += 128) {
+        const float4 gv = *reinterpret_cast<const float4 *>(g + off + c);
+        const float4 yv = *reinterpret_cast<const float4 *>(y + off + c);
+        float4 o;
+        o.x = (gv.x - yv.x * mean) / r;
+        o.y = (gv.y - yv.y * mean) / r;
+        o.z = (gv.z - yv.z * mean) / r;
+        o.w = (gv.w - yv.w * mean) / r;
+        *reinterpret_cast<float4 *>(dx + off + c) = o;
+      }
+    } else {
+      for (uint32_t c = lane; c < cols; c += 32)
+        dx[off + c] = (g[off + c] - y[off + c] * mean) / r;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256)
+xent_kernel(const float *__restrict__ z, const uint32_t *__restrict__ t,
+            float *loss, uint32_t rows, uint32_t vocab, bool vec) {
+  ROW_LOOP {
+    const uint32_t target = t[row];
+    if (target >= vocab) {
+      if (lane == 0) loss[row] = INFINITY;
+      continue;
+    }
+    const float *zr = z + static_cast<size_t>(row) * vocab;
+    float m, s;
+    row_logsumexp(zr, vocab, vec, lane, m, s);
+    if (lane == 0) loss[row] = m + logf(s) - zr[target];
+  }
+}
+
+__global__ void __launch_bounds__(256)
+xent_backward_kernel(const float *__restrict__ z, const uint32_t *__restrict__ t,
+                     const float *__restrict__ scale, float *dz, uint32_t rows,
+                     uint32_t vocab, bool vec) {
+  ROW_LOOP {
+    const uint32_t target = t[row];
+    const float *zr = z + static_cast<size_t>(row) * vocab;
+    float *dr = dz + static_cast<size_t>(row) * vocab;
+    if (target >= vocab) {
+      for (uint32_t c = lane; c < vocab; c += 32) dr[c] = INFINITY;
+      continue;
+    }
+    float m, s;
+    row_logsumexp(zr, vocab, vec, lane, m, s);
+    const bool scaled = scale != nullptr;
+    const float k = scaled ? scale[row] : 1.0f;
+    if (vec) {
+      for (uint32_t c = lane * 4; c < vocab; c += 128) {
+        float4 v = *reinterpret_cast<const float4 *>(zr + c);
+        float p[4] = {expf(v.x - m) / s, expf(v.y - m) / s, expf(v.z - m) / s,
+                      expf(v.w - m) / s};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (c + j == target) p[j] -= 1.0f;
+          if (scaled) p[j] = k * p[j];
+        }
+        *reinterpret_cast<float4 *>(dr + c) = make_float4(p[0], p[1], p[2], p[3]);
+      }
+    } else {
+      for (uint32_t c = lane; c < vocab; c += 32) {
+        float p = expf(zr[c] - m) / s;
+        if (c == target) p -= 1.0f;
+        dr[c] = scaled ? k * p : p;
+      }
+    }
+  }
+}
+
+unsigned row_grid(uint32_t rows) {
+  return grid_for(rows, kWarpsPerBlock, 16);
+}
+
+bool row_vec(uint32_t cols, std::initializer_list<const void *> ptrs) {
+  if (cols % 4) return false;
+  for (const void *p : ptrs)
+    if (p && !aligned16(p)) return false;
+  return true;
+}
+
+}  // namespace
+}  // namespace tl
+
+using namespace tl;
+
+extern "C" {
+
+int tl_softmax_rows(const float *x, float *out, uint32_t rows, uint32_t cols,
+                    void *stream) {
+  if (cols == 0) return fail(TL_ERR_INVALID, "softmax requires a non-empty final dimension");
+  if (rows == 0) return TL_OK;
+  if (!x || !out) return fail(TL_ERR_INVALID, "tl_softmax_rows: null pointer");
+  softmax_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(x, out, rows, cols,
+                                                                row_vec(cols, {x, out}));
+  return launch_status("tl_softmax_rows");
+}
+
+int tl_softmax_backward_rows(const float *grad, const float *y, float *dx,
+                             uint32_t rows, uint32_t cols, void *stream) {
+  if (rows == 0 || cols == 0) return TL_OK;
+  if (!grad || !y || !dx) return fail(TL_ERR_INVALID, "tl_softmax_backward_rows: null pointer");
+  softmax_backward_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
+      grad, y, dx, rows, cols, row_vec(cols, {grad, y, dx}));
+  return launch_status("tl_softmax_backward_rows");
+}
+
+int tl_rms_rows(const float *x, float *rms, uint32_t rows, uint32_t cols,
+                void *stream) {
+  if (rows == 0) return TL_OK;
+  if (cols == 0) return fail(TL_ERR_INVALID, "tl_rms_rows: empty rows");
+  if (!x || !rms) return fail(TL_ERR_INVALID, "tl_rms_rows: null pointer");
+  rms_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(x, rms, rows, cols,
+                                                            row_vec(cols, {x}));
+  return launch_status("tl_rms_rows");
+}
+
+int tl_rmsnorm_rows(const float *x, float *out, float *rms_out, uint32_t rows,
+                    uint32_t cols, void *stream) {
+  if (rows == 0) return TL_OK;
+  if (cols == 0) return fail(TL_ERR_INVALID, "tl_rmsnorm_rows: empty rows");
+  if (!x || !out) return fail(TL_ERR_INVALID, "tl_rmsnorm_rows: null pointer");
+  rmsnorm_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
+      x, out, rms_out, rows, cols, row_vec(cols, {x, out}));
+  return launch_status("tl_rmsnorm_rows");
+}
+
+int tl_rmsnorm_backward_rows(const float *grad, const float *x, const float *y,
+                             float *dx, uint32_t rows, uint32_t cols, void *stream) {
+  if (rows == 0) return TL_OK;
+  if (cols == 0) return fail(TL_ERR_INVALID, "tl_rmsnorm_backward_rows: empty rows");
+  if (!grad || !x || !y || !dx)
+    return fail(TL_ERR_INVALID, "tl_rmsnorm_backward_rows: null pointer");
+  rmsnorm_backward_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
+      grad, x, y, dx, rows, cols, row_vec(cols, {grad, x, y, dx}));
+  return launch_status("tl_rmsnorm_backward_rows");
+}
+
+int tl_xent_rows(const float *logits, const uint32_t *targets, float *loss,
+                 uint32_t rows, uint32_t vocab, void *stream) {
+  if (vocab == 0)
+    return fail(TL_ERR_INVALID, "cross_entropy requires logits with a non-empty final dimension");
+  if (rows == 0) return TL_OK;
+  if (!logits || !targets || !loss) return fail(TL_ERR_INVALID, "tl_xent_rows: null pointer");
+  xent_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
+      logits, targets, loss, rows, vocab, row_vec(vocab, {logits}));
+  return launch_status("tl_xent_rows");
+}
+
+int tl_xent_backward_rows(const float *logits, const uint32_t *targets,
+                          const float *row_scale, float *dlogits, uint32_t rows,
+                          uint32_t vocab, void *stream) {
+  if (vocab == 0)
+    return fail(TL_ERR_INVALID,
+                "cross_entropy_derivative requires logits with a non-empty final dimension");
+  if (rows == 0) return TL_OK;
+  if (!logits || !targets || !dlogits)
+    return fail(TL_ERR_INVALID, "tl_xent_backward_rows: null pointer");
+  xent_backward_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
+      logits, targets, row_scale, dlogits, rows, vocab, row_vec(vocab, {logits, dlogits}));
+  return launch_status("tl_xent_backward_rows");
+}
+
+}  // extern "C"

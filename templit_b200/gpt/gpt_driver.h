@@ -1,0 +1,185 @@
+// GPT training driver over any TempLit runtime: builds the model, the
+// cross-entropy loss and the AdamW optimiser and compiles them with
+// passes::compile exactly as src/train.cpp:89-113 (JTPuffer/TempLit) does,
+// then runs the loop body of train.cpp:120-157 one iteration at a time.
+// Instantiated for cuda::Runtime by gpt_step.cpp.
+#pragma once
+
+#include "expr/cross-entropy.h"
+#include "nn/GPT.h"
+#include "optimiser/AdamW.h"
+#include "passes/compile.h"
+#include "templit_gpt.h"
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <random>
+#include <span>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace templit_b200 {
+
+// Flat in-memory archive (WritableArchive + ReadableArchive with scopes) used
+// to move parameters in and out through Compiled::save / Compiled::load.
+class FlatArchive {
+  std::map<std::string, std::vector<std::byte>> *store_;
+  std::string prefix_;
+
+public:
+  explicit FlatArchive(std::map<std::string, std::vector<std::byte>> *s, std::string p = "")
+      : store_(s), prefix_(std::move(p)) {}
+  void write(const std::string &name, std::span<const std::byte> v) {
+    (*store_)[prefix_ + name].assign(v.begin(), v.end());
+  }
+  void read(const std::string &name, std::span<std::byte> v) const {
+    auto it = store_->find(prefix_ + name);
+    if (it == store_->end() || it->second.size() != v.size())
+      throw std::runtime_error("archive entry missing or mis-sized: " + prefix_ + name);
+    std::memcpy(v.data(), it->second.data(), v.size());
+  }
+  FlatArchive scope(const std::string &name) const { return FlatArchive(store_, prefix_ + name + "/"); }
+};
+
+struct DriverBase {
+  virtual ~DriverBase() = default;
+  virtual void set_batch(const uint32_t *tokens, const uint32_t *targets) = 0;
+  virtual float train_step() = 0;
+  virtual void forward(float *losses) = 0;
+  virtual void params(std::vector<float> &out, uint32_t &tensors) = 0;
+  virtual void set_params(const float *in, uint64_t count) = 0;
+};
+
+template <typename Mat, typename Run, typename Model>
+class GptDriver final : public DriverBase {
+  using IndexMat = typename Mat::template rebind<uint32_t>;
+  using Opt = Optimiser::AdamW<Mat>;
+  using Indices = expr::tensor::Tensor<IndexMat>;
+  using Loss = decltype(expr::loss::cross_entropy(std::declval<const Model &>()(std::declval<Indices &>()),
+                                                  std::declval<Indices &>()));
+  using CompiledT = passes::Compiled<Mat, std::remove_cvref_t<Loss>, Run, Opt>;
+
+  tlg_config cfg_;
+  Run &runtime_;
+  Indices input_;
+  Indices targets_;
+  std::mt19937 gen_;
+  Model model_;
+  std::unique_ptr<CompiledT> compiled_;
+  Mat root_grad_;
+  std::vector<float> losses_;
+
+  static std::unique_ptr<CompiledT> build(const Model &model, Indices &input, Indices &targets,
+                                          Run &runtime, const tlg_config &c) {
+    auto graph = model(input);
+    auto loss = expr::loss::cross_entropy(std::move(graph), targets);
+    auto params = Opt::generate_params(c.lr, c.beta1, c.beta2, c.eps, c.weight_decay);
+    return std::make_unique<CompiledT>(std::move(loss), runtime, std::move(params));
+  }
+
+public:
+  GptDriver(const tlg_config &c, Run &runtime)
+      : cfg_(c), runtime_(runtime), input_(IndexMat({c.batch, c.seq})),
+        targets_(IndexMat({c.batch, c.seq})), gen_(c.seed), model_(c.batch, c.seq, gen_),
+        compiled_(build(model_, input_, targets_, runtime_, c)),
+        root_grad_(Mat({c.batch, c.seq, 1})),
+        losses_(static_cast<size_t>(c.batch) * c.seq) {
+    // zero ids so prepare() sees valid inputs
+    std::vector<uint32_t> zeros(losses_.size(), 0);
+    input_.get_value().set(zeros);
+    targets_.get_value().set(zeros);
+    compiled_->prepare();
+    const float world = static_cast<float>(c.world ? c.world : 1);
+    root_grad_.set(std::vector<float>(losses_.size(),
+                                      1.0f / (static_cast<float>(losses_.size()) * world)));
+    if (c.init_std > 0.0f) redraw(c.init_std);
+  }
+
+  // Re-draws every weight N(0, std) and zeroes every bias (the synthetic
+  // initialisation of the benchmark configurations).
+  void redraw(float std) {
+    std::vector<float> all;
+    uint32_t tensors = 0;
+    params(all, tensors);
+    std::map<std::string, std::vector<std::byte>> store;
+    FlatArchive ar(&store);
+    compiled_->save(ar);
+    std::normal_distribution<float> dist(0.0f, std);
+    std::mt19937 g(cfg_.seed + 7919u);
+    size_t off = 0;
+    for (uint32_t i = 0; i < tensors; ++i) {
+      const std::string key = "parameters/" + std::to_string(i) + "/";
+      const auto &size = store[key + "size"];
+      std::vector<uint32_t> shape(size.size() / 4);
+      std::memcpy(shape.data(), size.data(), size.size());
+      size_t n = 1;
+      for (uint32_t d : shape) n *= d;
+      const bool bias = shape.size() == 2 && shape[0] == 1;
+      for (size_t j = 0; j < n; ++j) all[off + j] = bias ? 0.0f : dist(g);
+      off += n;
+    }
+    set_params(all.data(), all.size());
+  }
+
+  void set_batch(const uint32_t *tokens, const uint32_t *targets) override {
+    const size_t n = losses_.size();
+    input_.get_value().set(std::span<const uint32_t>(tokens, n));
+    targets_.get_value().set(std::span<const uint32_t>(targets, n));
+  }
+
+  float train_step() override {
+    compiled_->zero_grad();
+    const Mat loss = compiled_->forward();
+    loss.read(losses_);
+    double acc = 0.0;
+    for (float v : losses_) acc += v;
+    compiled_->backward(root_grad_);
+    if (cfg_.clip > 0.0f) compiled_->step(cfg_.clip);
+    else compiled_->step();
+    return static_cast<float>(acc / static_cast<double>(losses_.size()));
+  }
+
+  void forward(float *losses) override {
+    const Mat loss = compiled_->forward();
+    loss.read(std::span<float>(losses, losses_.size()));
+  }
+
+  void params(std::vector<float> &out, uint32_t &tensors) override {
+    std::map<std::string, std::vector<std::byte>> store;
+    FlatArchive ar(&store);
+    compiled_->save(ar);
+    out.clear();
+    tensors = 0;
+    for (;; ++tensors) {
+      auto it = store.find("parameters/" + std::to_string(tensors) + "/data");
+      if (it == store.end()) break;
+      const size_t n = it->second.size() / sizeof(float);
+      const size_t o = out.size();
+      out.resize(o + n);
+      std::memcpy(out.data() + o, it->second.data(), it->second.size());
+    }
+  }
+
+  void set_params(const float *in, uint64_t count) override {
+    std::map<std::string, std::vector<std::byte>> store;
+    FlatArchive ar(&store);
+    compiled_->save(ar);
+    uint64_t off = 0;
+    for (uint32_t i = 0;; ++i) {
+      auto it = store.find("parameters/" + std::to_string(i) + "/data");
+      if (it == store.end()) break;
+      const size_t n = it->second.size() / sizeof(float);
+      if (off + n > count) throw std::invalid_argument("too few parameter values");
+      std::memcpy(it->second.data(), in + off, n * sizeof(float));
+      off += n;
+    }
+    if (off != count) throw std::invalid_argument("parameter count mismatch");
+    compiled_->load(ar);
+  }
+};
+
+}  // namespace templit_b200

@@ -1,0 +1,175 @@
+// The GPT training step on cuda::Runtime behind the C ABI of
+// include/templit_gpt.h.  Family 4 is the reference's own nn::GPT
+// (include/nn/GPT.h: vocab 2048, max sequence 192, d_model 384, 6 heads,
+// 4 blocks - the model of src/train.cpp:23-27,98-99); family 12 the
+// 12-block d_model 768 variant (deep_gpt.h).
+#include "templit_gpt.h"
+
+#include "deep_gpt.h"
+#include "gpt_driver.h"
+#include "my_cuda/runtime.h"
+#include "my_cuda/storage.h"
+
+#include <nccl.h>
+
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <string>
+
+namespace {
+
+using Mat = RTensor<cuda::CUDA, cuda::kernel_type>;
+using GPT4 = nn::GPT<Mat, 2048, 192, 384, 6>;
+
+thread_local std::string g_error;
+
+struct Handle {
+  std::unique_ptr<cuda::Runtime> runtime;
+  std::unique_ptr<templit_b200::DriverBase> driver;
+  ncclComm_t comm = nullptr;
+  int profile_steps = 0;
+};
+
+template <typename F> int guarded(F &&f) {
+  try {
+    f();
+    return 0;
+  } catch (const std::exception &e) {
+    g_error = e.what();
+  } catch (...) {
+    g_error = "unknown exception";
+  }
+  return 1;
+}
+
+std::unique_ptr<templit_b200::DriverBase> make_driver(const tlg_config &c, cuda::Runtime &rt) {
+  if (c.family == 4) {
+    if (c.seq == 0 || c.seq > 192) throw std::invalid_argument("family 4 takes seq in [1, 192]");
+    return std::make_unique<templit_b200::GptDriver<Mat, cuda::Runtime, GPT4>>(c, rt);
+  }
+#ifdef TLG_WITH_DEEP
+  if (c.family == 12) return templit_b200::make_deep_driver(c, rt);
+#endif
+  throw std::invalid_argument("unsupported GPT family " + std::to_string(c.family));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *tlg_last_error(void) { return g_error.c_str(); }
+
+int tlg_create(const tlg_config *config, void **handle) {
+  return guarded([&] {
+    if (!config || !handle) throw std::invalid_argument("null argument");
+    *handle = nullptr;
+    cuda::init();
+    auto h = std::make_unique<Handle>();
+    h->runtime = std::make_unique<cuda::Runtime>();
+    h->runtime->set_fusion(config->fusion != 0);
+    h->runtime->set_graphs(config->graphs != 0);
+    h->driver = make_driver(*config, *h->runtime);
+    *handle = h.release();
+  });
+}
+
+int tlg_destroy(void *handle) {
+  return guarded([&] {
+    Handle *h = static_cast<Handle *>(handle);
+    if (!h) return;
+    h->driver.reset();
+    h->runtime.reset();
+    if (h->comm) ncclCommDestroy(h->comm);
+    delete h;
+  });
+}
+
+int tlg_set_batch(void *handle, const uint32_t *tokens, const uint32_t *targets) {
+  return guarded([&] { static_cast<Handle *>(handle)->driver->set_batch(tokens, targets); });
+}
+
+int tlg_train_step(void *handle, float *mean_loss) {
+  return guarded([&] {
+    Handle *h = static_cast<Handle *>(handle);
+    const float l = h->driver->train_step();
+    if (mean_loss) *mean_loss = l;
+    if (h->profile_steps > 0 && --h->profile_steps == 0) h->runtime->end_profile();
+  });
+}
+
+int tlg_forward(void *handle, float *losses) {
+  return guarded([&] { static_cast<Handle *>(handle)->driver->forward(losses); });
+}
+
+int tlg_param_count(void *handle, uint64_t *count, uint32_t *tensors) {
+  return guarded([&] {
+    std::vector<float> all;
+    uint32_t t = 0;
+    static_cast<Handle *>(handle)->driver->params(all, t);
+    if (count) *count = all.size();
+    if (tensors) *tensors = t;
+  });
+}
+
+int tlg_get_params(void *handle, float *out, uint64_t count) {
+  return guarded([&] {
+    std::vector<float> all;
+    uint32_t t = 0;
+    static_cast<Handle *>(handle)->driver->params(all, t);
+    if (count != all.size()) throw std::invalid_argument("parameter count mismatch");
+    std::memcpy(out, all.data(), all.size() * sizeof(float));
+  });
+}
+
+int tlg_set_params(void *handle, const float *in, uint64_t count) {
+  return guarded([&] { static_cast<Handle *>(handle)->driver->set_params(in, count); });
+}
+
+void *tlg_stream(void *) { return cuda::stream(); }
+
+int tlg_stats(void *handle, uint64_t out[8]) {
+  return guarded([&] {
+    const cuda::RuntimeStats &s = static_cast<Handle *>(handle)->runtime->stats();
+    out[0] = s.windows;
+    out[1] = s.ops_recorded;
+    out[2] = s.ops_launched;
+    out[3] = s.kernel_launches;
+    out[4] = s.graph_replays;
+    out[5] = s.graph_captures;
+    out[6] = s.fused_ops;
+    out[7] = cuda::memory_stats().peak_in_use;
+  });
+}
+
+int tlg_nccl_unique_id(uint8_t id[128]) {
+  return guarded([&] {
+    static_assert(sizeof(ncclUniqueId) == 128);
+    ncclUniqueId u;
+    const ncclResult_t r = ncclGetUniqueId(&u);
+    if (r != ncclSuccess) throw std::runtime_error(ncclGetErrorString(r));
+    std::memcpy(id, &u, 128);
+  });
+}
+
+int tlg_set_communicator(void *handle, const uint8_t id[128], int nranks, int rank) {
+  return guarded([&] {
+    Handle *h = static_cast<Handle *>(handle);
+    ncclUniqueId u;
+    std::memcpy(&u, id, 128);
+    cuda::init();
+    const ncclResult_t r = ncclCommInitRank(&h->comm, nranks, u, rank);
+    if (r != ncclSuccess) throw std::runtime_error(ncclGetErrorString(r));
+    h->runtime->set_communicator(h->comm);
+  });
+}
+
+int tlg_profile(void *handle, const char *path, int steps) {
+  return guarded([&] {
+    Handle *h = static_cast<Handle *>(handle);
+    h->runtime->start_profile(path);
+    h->profile_steps = steps;
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,212 @@
+// Process-wide device state of the `cuda` backend: device selection, the
+// backend stream, the caching device-memory pool and the Storage data paths.
+// Counterpart of src/my_metal/metal.cpp and the MTL::Buffer handling in
+// include/my_metal/storage.h (JTPuffer/TempLit).
+//
+// Pool.  Device memory is obtained from the driver in size-rounded blocks
+// and cached on release; a request takes the smallest cached block of at
+// least its rounded size (within 2x), so the executor's per-step
+// temporaries are served without driver calls and, for a repeated program,
+// at the same addresses (which is what lets a captured CUDA graph replay).
+// Reuse is stream-ordered: every launch goes to one stream, so memory freed
+// by the host while a program is queued can only be rewritten by work
+// queued after it.
+#include "internal.h"
+
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+namespace cuda {
+namespace {
+
+struct State {
+  bool initialised = false;
+  int device = 0;
+  void *stream = nullptr;
+  std::multimap<size_t, void *> free_blocks;
+  std::unordered_map<void *, size_t> block_size;  // every block obtained
+  size_t reserved = 0;
+  size_t in_use = 0;
+  size_t peak = 0;
+  uint64_t next_id = 1;
+  uint64_t window_counter = 0;
+  internal::Recorder *recorder = nullptr;
+};
+
+State &state() {
+  static State s;
+  return s;
+}
+
+size_t round_size(size_t bytes) {
+  if (bytes == 0) bytes = 1;
+  const size_t small = 512, large = size_t(2) << 20;
+  return bytes < (size_t(1) << 20) ? (bytes + small - 1) / small * small
+                                   : (bytes + large - 1) / large * large;
+}
+
+void release_cached() {
+  State &s = state();
+  if (s.free_blocks.empty()) return;
+  tl_stream_sync(s.stream);
+  for (auto &kv : s.free_blocks) {
+    tl_free(kv.second);
+    s.reserved -= kv.first;
+    s.block_size.erase(kv.second);
+  }
+  s.free_blocks.clear();
+}
+
+}  // namespace
+
+namespace internal {
+
+void ensure_init() {
+  if (!state().initialised) cuda::init(-1);
+}
+
+Recorder *active_recorder() { return state().recorder; }
+void set_active_recorder(Recorder *r) { state().recorder = r; }
+uint64_t next_window_id() { return ++state().window_counter; }
+
+}  // namespace internal
+
+void init(int device) {
+  State &s = state();
+  if (s.initialised) return;
+  if (device < 0) {
+    const char *lr = std::getenv("LOCAL_RANK");
+    device = lr ? std::atoi(lr) : 0;
+  }
+  internal::check(tl_device_init(device), "cuda::init");
+  void *stream = nullptr;
+  internal::check(tl_stream_create(&stream), "cuda::init stream");
+  s.device = device;
+  s.stream = stream;
+  s.initialised = true;
+}
+
+void shutdown() {
+  State &s = state();
+  if (!s.initialised) return;
+  tl_stream_sync(s.stream);
+  release_cached();
+  tl_stream_destroy(s.stream);
+  s.stream = nullptr;
+  s.initialised = false;
+}
+
+bool initialised() { return state().initialised; }
+
+void *stream() {
+  internal::ensure_init();
+  return state().stream;
+}
+
+void synchronize() {
+  internal::ensure_init();
+  internal::check(tl_stream_sync(state().stream), "cuda::synchronize");
+}
+
+MemoryStats memory_stats() {
+  const State &s = state();
+  return MemoryStats{s.reserved, s.in_use, s.peak};
+}
+
+namespace detail {
+
+Block allocate(size_t bytes) {
+  internal::ensure_init();
+  State &s = state();
+  const size_t want = round_size(bytes);
+  Block b;
+  b.bytes = want;
+  auto it = s.free_blocks.lower_bound(want);
+  if (it != s.free_blocks.end() && it->first <= 2 * want) {
+    b.ptr = it->second;
+    b.bytes = it->first;
+    s.free_blocks.erase(it);
+  } else {
+    void *p = nullptr;
+    if (tl_malloc(&p, want) != TL_OK) {
+      release_cached();
+      internal::check(tl_malloc(&p, want), "device allocation");
+    }
+    b.ptr = p;
+    s.block_size[p] = want;
+    s.reserved += want;
+  }
+  b.id = s.next_id++;
+  internal::Recorder *r = s.recorder;
+  b.window = r ? r->window() : 0;
+  s.in_use += b.bytes;
+  if (s.in_use > s.peak) s.peak = s.in_use;
+  return b;
+}
+
+void release(const Block &block) noexcept {
+  if (!block.ptr) return;
+  State &s = state();
+  if (s.recorder) s.recorder->record_release(block);
+  s.in_use -= block.bytes;
+  s.free_blocks.emplace(block.bytes, block.ptr);
+}
+
+namespace {
+bool recorded_here(const Block &b) {
+  internal::Recorder *r = state().recorder;
+  return r && b.window != 0 && b.window == r->window();
+}
+}  // namespace
+
+void write(const Block &dst, size_t offset_bytes, const void *src, size_t bytes) {
+  if (bytes == 0) return;
+  if (recorded_here(dst)) {
+    state().recorder->record_write(dst, offset_bytes, src, bytes);
+    return;
+  }
+  internal::check(tl_memcpy_h2d(static_cast<char *>(dst.ptr) + offset_bytes, src, bytes,
+                                state().stream),
+                  "Storage::write");
+}
+
+void read(const Block &src, size_t offset_bytes, void *dst, size_t bytes) {
+  if (bytes == 0) return;
+  internal::check(tl_memcpy_d2h(dst, static_cast<const char *>(src.ptr) + offset_bytes, bytes,
+                                state().stream),
+                  "Storage::read");
+  internal::check(tl_stream_sync(state().stream), "Storage::read sync");
+}
+
+void fill32(const Block &dst, uint32_t pattern, size_t count) {
+  if (count == 0) return;
+  if (recorded_here(dst)) {
+    state().recorder->record_fill(dst, pattern, count);
+    return;
+  }
+  internal::check(tl_fill_u32(dst.ptr, pattern, count, state().stream), "Storage::fill");
+}
+
+void copy(const Block &dst, const Block &src, size_t bytes) {
+  if (bytes == 0) return;
+  if (recorded_here(dst) || recorded_here(src)) {
+    state().recorder->record_copy(dst, src, bytes);
+    return;
+  }
+  internal::check(tl_memcpy_d2d(dst.ptr, src.ptr, bytes, state().stream), "Storage::clone");
+}
+
+bool equal(const Block &a, const Block &b, size_t bytes) {
+  if (bytes == 0) return true;
+  std::vector<unsigned char> ha(bytes), hb(bytes);
+  read(a, 0, ha.data(), bytes);
+  read(b, 0, hb.data(), bytes);
+  return std::memcmp(ha.data(), hb.data(), bytes) == 0;
+}
+
+}  // namespace detail
+}  // namespace cuda

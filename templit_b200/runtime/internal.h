@@ -1,0 +1,42 @@
+// Internal interfaces shared by the backend's device layer (device.cpp) and
+// the recording runtime (runtime.cpp).  Not installed.
+#pragma once
+
+#include "my_cuda/cuda.h"
+#include "templit_cuda.h"
+
+#include <cstddef>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+namespace cuda::internal {
+
+// The open recording window of a Runtime.  Storage operations on blocks
+// allocated inside the window are appended to its program; releases are
+// noted so the optimiser knows which values die inside the program.
+struct Recorder {
+  virtual ~Recorder() = default;
+  virtual uint64_t window() const = 0;
+  virtual void record_write(const detail::Block &dst, size_t offset, const void *src,
+                            size_t bytes) = 0;
+  virtual void record_fill(const detail::Block &dst, uint32_t pattern, size_t count) = 0;
+  virtual void record_copy(const detail::Block &dst, const detail::Block &src,
+                           size_t bytes) = 0;
+  virtual void record_release(const detail::Block &block) = 0;
+};
+
+Recorder *active_recorder();
+void set_active_recorder(Recorder *r);
+uint64_t next_window_id();
+
+// Throws std::runtime_error with the library's message unless status == TL_OK.
+inline void check(int status, const char *what) {
+  if (status != TL_OK) {
+    throw std::runtime_error(std::string(what) + ": " + tl_last_error());
+  }
+}
+
+void ensure_init();
+
+}  // namespace cuda::internal

@@ -1,0 +1,1048 @@
+// cuda::Runtime: argument validation and recording of every runtime call,
+// program execution (eager or CUDA-graph replay) and the window lifecycle.
+//
+// Each op method mirrors the corresponding metal::Runtime method of
+// JTPuffer/TempLit (src/my_metal/runtime.cpp, cited per method): it throws
+// the same exception type with the same text on the same bad arguments
+// (with "CUDA" in place of "Metal"), then appends one Op to the window.
+#include "my_cuda/runtime.h"
+
+#include "RTensor/dimension.h"
+#include "RTensor/infer_shape.h"
+#include "optimize.h"
+#include "program.h"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <numeric>
+#include <stdexcept>
+#include <unordered_map>
+
+namespace cuda {
+
+using internal::check;
+using internal::Kind;
+using internal::Op;
+using internal::TRef;
+
+namespace {
+
+using Mat = RTensor<CUDA, kernel_type>;
+using IndexMat = RTensor<CUDA, index_type>;
+
+template <typename T>
+TRef ref(const RTensor<CUDA, T> &m) {
+  TRef r;
+  const Storage<CUDA, T> *s = m.get_storage();
+  if (!s) throw std::logic_error("runtime op on an uninitialised tensor");
+  if (m.shape().size() > static_cast<size_t>(internal::kMaxRank))
+    throw std::invalid_argument("tensor rank exceeds the CUDA runtime limit of 8");
+  r.p = const_cast<T *>(s->data());
+  r.id = s->block().id;
+  r.rank = static_cast<uint8_t>(m.shape().size());
+  for (size_t i = 0; i < m.shape().size(); ++i) r.shape[i] = m.shape()[i];
+  return r;
+}
+
+TRef ref_block(const detail::Block &b, uint64_t bytes) {
+  TRef r;
+  r.p = b.ptr;
+  r.id = b.id;
+  r.rank = 1;
+  r.shape[0] = static_cast<uint32_t>(bytes);
+  return r;
+}
+
+// Broadcast check of an operand against the destination shape
+// (src/my_metal/runtime.cpp:18-39).
+void check_broadcast(std::span<const uint32_t> shape, std::span<const uint32_t> out) {
+  if (shape.size() > out.size()) throw std::runtime_error("invalid broadcast");
+  const size_t off = out.size() - shape.size();
+  for (size_t i = 0; i < shape.size(); ++i)
+    if (shape[i] != out[off + i] && shape[i] != 1) throw std::runtime_error("invalid broadcast");
+}
+
+const char *const kKindNames[] = {
+    "binary",  "scalar",    "unary",      "copy",       "reduce",    "argmax",   "transpose",
+    "softmax", "rms",       "rmsnorm",    "xent",       "xent_bwd",  "gather",   "scatter",
+    "sqnorm",  "clip",      "adamw",      "gemm",       "host_write", "fill",    "dev_copy",
+    "release", "gelu_bwd",  "softmax_bwd", "rmsnorm_bwd", "multi_adamw", "allreduce"};
+
+}  // namespace
+
+namespace internal {
+const char *kind_name(Kind k) { return kKindNames[static_cast<int>(k)]; }
+}  // namespace internal
+
+// ---------------------------------------------------------------------------
+struct Runtime::Impl : internal::Recorder {
+  enum class State { Idle, Recording, Submitted };
+  State state = State::Idle;
+  uint64_t window_id = 0;
+  std::vector<Op> prog;
+  RuntimeStats stats;
+  bool fusion = true;
+  bool graphs = true;
+  int gemm_precision = TL_GEMM_TF32;
+  void *comm = nullptr;
+
+  // scratch shared by the ops of a program (they run one after another)
+  detail::Block workspace;
+  // fused optimiser slot tables: device copy + pinned host staging
+  detail::Block slot_dev;
+  void *slot_host = nullptr;
+  size_t slot_capacity = 0;
+
+  // graph cache: program signature -> instantiated graph
+  struct Cached {
+    void *exec = nullptr;
+    uint64_t kernels = 0;
+    uint64_t last_use = 0;
+  };
+  std::unordered_map<std::string, Cached> graph_cache;
+  std::string last_signature;
+  uint64_t use_clock = 0;
+
+  // profiling
+  bool profiling = false;
+  std::string profile_path;
+  struct Prof {
+    uint64_t calls = 0;
+    double ms = 0.0;
+  };
+  std::map<std::string, Prof> profile;
+
+  ~Impl() override { release_resources(); }
+
+  // ---- Recorder
+  uint64_t window() const override { return state == State::Recording ? window_id : 0; }
+  void record_write(const detail::Block &dst, size_t offset, const void *src,
+                    size_t bytes) override {
+    Op &op = push(Kind::HostWrite);
+    op.t[0] = ref_block(dst, dst.bytes);
+    op.n = offset;
+    op.host.assign(static_cast<const uint8_t *>(src), static_cast<const uint8_t *>(src) + bytes);
+  }
+  void record_fill(const detail::Block &dst, uint32_t pattern, size_t count) override {
+    Op &op = push(Kind::Fill);
+    op.t[0] = ref_block(dst, dst.bytes);
+    op.u0 = pattern;
+    op.n = count;
+  }
+  void record_copy(const detail::Block &dst, const detail::Block &src, size_t bytes) override {
+    Op &op = push(Kind::DevCopy);
+    op.t[0] = ref_block(dst, dst.bytes);
+    op.t[1] = ref_block(src, src.bytes);
+    op.n = bytes;
+  }
+  void record_release(const detail::Block &b) override {
+    if (state != State::Recording) return;
+    Op &op = push(Kind::Release);
+    op.t[0].id = b.id;
+    op.t[0].p = b.ptr;
+  }
+
+  Op &push(Kind k) {
+    prog.emplace_back();
+    Op &op = prog.back();
+    op.kind = k;
+    return op;
+  }
+
+  Op &record(Kind k) {
+    if (state != State::Recording)
+      throw std::logic_error("CUDA runtime execution has not started");
+    ++stats.ops_recorded;
+    return push(k);
+  }
+
+  void release_resources() noexcept {
+    for (auto &kv : graph_cache) tl_graph_destroy(kv.second.exec);
+    graph_cache.clear();
+    last_signature.clear();
+    if (workspace.ptr) {
+      detail::release(workspace);
+      workspace = detail::Block{};
+    }
+    if (slot_dev.ptr) {
+      detail::release(slot_dev);
+      slot_dev = detail::Block{};
+    }
+    if (slot_host) {
+      tl_host_free(slot_host);
+      slot_host = nullptr;
+    }
+    slot_capacity = 0;
+  }
+
+  // ---- execution
+  void ensure_workspace(size_t bytes) {
+    if (bytes <= workspace.bytes) return;
+    if (workspace.ptr) detail::release(workspace);
+    workspace = detail::allocate(bytes);
+  }
+
+  void ensure_slots(size_t count) {
+    if (count <= slot_capacity) return;
+    if (slot_dev.ptr) detail::release(slot_dev);
+    if (slot_host) tl_host_free(slot_host);
+    slot_host = nullptr;
+    const size_t bytes = count * sizeof(tl_param_slot);
+    slot_dev = detail::allocate(bytes);
+    check(tl_host_alloc(&slot_host, bytes), "optimiser slot staging");
+    slot_capacity = count;
+  }
+
+  // Fills the pinned slot table of a fused optimiser op; returns chunk count.
+  uint32_t stage_slots(const Op &op, size_t base) {
+    tl_param_slot *h = static_cast<tl_param_slot *>(slot_host) + base;
+    uint32_t chunk = 0;
+    for (size_t i = 0; i < op.multi.size(); ++i) {
+      const auto &s = op.multi[i];
+      h[i].param = s.param.f();
+      h[i].out = s.out.f();
+      h[i].grad = s.grad.f();
+      h[i].m1 = s.m1.f();
+      h[i].m2 = s.m2.f();
+      h[i].count = s.param.numel();
+      h[i].chunk0 = chunk;
+      h[i].step = s.step;
+      chunk += static_cast<uint32_t>((h[i].count + TL_OPT_CHUNK - 1) / TL_OPT_CHUNK);
+    }
+    return chunk;
+  }
+
+  void execute(const Op &op, void *s, size_t slot_base) {
+    void *ws = workspace.ptr;
+    const size_t wsb = workspace.bytes;
+    const TRef *t = op.t.data();
+    switch (op.kind) {
+      case Kind::Binary:
+        check(tl_binary(op.code, t[0].f(), t[0].shape, t[0].rank, t[1].f(), t[1].shape, t[1].rank,
+                        t[2].f(), t[2].shape, t[2].rank, s),
+              "binary op");
+        break;
+      case Kind::Scalar:
+        check(tl_scalar(op.code, t[0].f(), op.f0, t[1].f(), t[1].numel(), s), "scalar op");
+        break;
+      case Kind::Unary:
+        check(tl_unary(op.code, t[0].f(), t[1].f(), t[1].numel(), s), "unary op");
+        break;
+      case Kind::Copy:
+        check(tl_copy(t[0].f(), t[1].f(), t[1].numel(), s), "copy");
+        break;
+      case Kind::Reduce:
+        check(tl_reduce(op.code, t[0].f(), t[0].shape, t[0].rank, t[1].f(), t[1].shape, t[1].rank,
+                        ws, wsb, s),
+              "reduce");
+        break;
+      case Kind::Argmax:
+        check(tl_argmax(t[0].f(), t[0].numel(), t[1].u(), ws, wsb, s), "argmax");
+        break;
+      case Kind::Transpose:
+        check(tl_transpose(t[0].f(), t[0].shape, t[0].rank, op.i0, op.i1, t[1].f(), s),
+              "transpose");
+        break;
+      case Kind::Softmax:
+        check(tl_softmax_rows(t[0].f(), t[1].f(), static_cast<uint32_t>(t[0].numel() / t[0].last()),
+                              t[0].last(), s),
+              "softmax");
+        break;
+      case Kind::Rms:
+        check(tl_rms_rows(t[0].f(), t[1].f(), static_cast<uint32_t>(t[0].numel() / t[0].last()),
+                          t[0].last(), s),
+              "RMS");
+        break;
+      case Kind::RmsNorm:
+        check(tl_rmsnorm_rows(t[0].f(), t[1].f(), nullptr,
+                              static_cast<uint32_t>(t[0].numel() / t[0].last()), t[0].last(), s),
+              "RMSNorm");
+        break;
+      case Kind::Xent:
+        check(tl_xent_rows(t[0].f(), t[1].u(), t[2].f(), static_cast<uint32_t>(t[1].numel()),
+                           t[0].last(), s),
+              "cross_entropy");
+        break;
+      case Kind::XentBwd:
+        check(tl_xent_backward_rows(t[0].f(), t[1].u(), t[3].p ? t[3].f() : nullptr, t[2].f(),
+                                    static_cast<uint32_t>(t[1].numel()), t[0].last(), s),
+              "cross_entropy_derivative");
+        break;
+      case Kind::Gather:
+        check(tl_embedding_gather(t[0].f(), t[0].shape[0], t[0].shape[1], t[1].u(),
+                                  static_cast<uint32_t>(t[1].numel()), t[2].f(), s),
+              "embedding_lookup");
+        break;
+      case Kind::Scatter:
+        check(tl_embedding_scatter_add(t[0].f(), t[1].u(), static_cast<uint32_t>(t[1].numel()),
+                                       t[3].shape[1], t[2].p ? t[2].f() : nullptr, t[3].f(),
+                                       t[3].shape[0], ws, wsb, s),
+              "scatter");
+        break;
+      case Kind::SqNorm:
+        check(tl_grad_sqnorm_accumulate(t[0].f(), t[0].numel(), t[1].f(), ws, wsb, s),
+              "accumulate_gradient_squared_norm");
+        break;
+      case Kind::Clip:
+        check(tl_clip_gradient(t[0].f(), t[1].f(), op.f0, t[2].f(), t[2].numel(), s),
+              "clip_gradient");
+        break;
+      case Kind::AdamW:
+        check(tl_adamw(t[0].f(), t[1].f(), t[2].f(), t[3].f(), t[4].f(), t[5].f(), t[6].f(),
+                       t[7].f(), t[8].f(), op.f0, op.u0, t[0].numel(), s),
+              "adamW");
+        break;
+      case Kind::Gemm:
+        check(tl_gemm(&op.gemm, s), "mult");
+        break;
+      case Kind::HostWrite:
+        check(tl_memcpy_h2d(static_cast<char *>(t[0].p) + op.n, op.host.data(), op.host.size(), s),
+              "Storage::write");
+        break;
+      case Kind::Fill:
+        check(tl_fill_u32(t[0].p, op.u0, op.n, s), "Storage::fill");
+        break;
+      case Kind::DevCopy:
+        check(tl_memcpy_d2d(t[0].p, t[1].p, op.n, s), "Storage::clone");
+        break;
+      case Kind::Release:
+        break;
+      case Kind::GeluBwd:
+        check(tl_gelu_backward(t[0].f(), t[1].f(), t[2].f(), t[2].numel(), s), "GELU backward");
+        break;
+      case Kind::SoftmaxBwd:
+        check(tl_softmax_backward_rows(t[0].f(), t[1].f(), t[2].f(),
+                                       static_cast<uint32_t>(t[2].numel() / t[2].last()),
+                                       t[2].last(), s),
+              "softmax backward");
+        break;
+      case Kind::RmsNormBwd:
+        check(tl_rmsnorm_backward_rows(t[0].f(), t[1].f(), t[2].f(), t[3].f(),
+                                       static_cast<uint32_t>(t[3].numel() / t[3].last()),
+                                       t[3].last(), s),
+              "RMSNorm backward");
+        break;
+      case Kind::MultiAdamW: {
+        const uint32_t chunks = stage_slots(op, slot_base);
+        tl_param_slot *dev = static_cast<tl_param_slot *>(slot_dev.ptr) + slot_base;
+        check(tl_memcpy_h2d(dev, static_cast<tl_param_slot *>(slot_host) + slot_base,
+                            op.multi.size() * sizeof(tl_param_slot), s),
+              "optimiser slots");
+        check(tl_multi_clip_adamw(dev, static_cast<uint32_t>(op.multi.size()), chunks,
+                                  t[0].p ? t[0].f() : nullptr, op.f0, t[5].f(), t[6].f(),
+                                  t[7].f(), t[8].f(), op.f1, ws, wsb, s),
+              "fused clip + AdamW");
+        break;
+      }
+      case Kind::AllReduce:
+        internal::all_reduce_gradients(op, comm, s);
+        break;
+    }
+  }
+
+  // Signature of a program for graph reuse: everything a launch depends on
+  // except the values graphs re-read at replay (optimiser slot tables).
+  static std::string signature(const std::vector<Op> &p) {
+    std::string sig;
+    sig.reserve(p.size() * 96);
+    auto put = [&](const void *d, size_t n) { sig.append(static_cast<const char *>(d), n); };
+    for (const Op &op : p) {
+      if (op.dead || op.kind == Kind::Release) continue;
+      put(&op.kind, sizeof(op.kind));
+      put(&op.code, sizeof(op.code));
+      for (const TRef &r : op.t) {
+        if (!r.p) continue;
+        put(&r.p, sizeof(r.p));
+        put(&r.rank, 1);
+        put(r.shape, r.rank * sizeof(uint32_t));
+      }
+      put(&op.f0, sizeof(float));
+      put(&op.f1, sizeof(float));
+      put(&op.i0, sizeof(int32_t));
+      put(&op.i1, sizeof(int32_t));
+      put(&op.n, sizeof(op.n));
+      if (op.kind == Kind::AdamW) put(&op.u0, sizeof(op.u0));
+      if (op.kind == Kind::Fill) put(&op.u0, sizeof(op.u0));
+      if (op.kind == Kind::Gemm) put(&op.gemm, sizeof(op.gemm));
+      if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce) {
+        for (const auto &s : op.multi) {
+          put(&s.param.p, sizeof(void *));
+          put(&s.grad.p, sizeof(void *));
+          put(&s.out.p, sizeof(void *));
+          put(&s.m1.p, sizeof(void *));
+          put(&s.m2.p, sizeof(void *));
+        }
+      }
+    }
+    return sig;
+  }
+
+  static bool capturable(const std::vector<Op> &p) {
+    for (const Op &op : p)
+      if (!op.dead && (op.kind == Kind::HostWrite || op.kind == Kind::AllReduce)) return false;
+    return true;
+  }
+
+  void run_ops(void *s) {
+    size_t slot_base = 0;
+    for (const Op &op : prog) {
+      if (op.dead) continue;
+      execute(op, s, slot_base);
+      if (op.kind == Kind::MultiAdamW) slot_base += op.multi.size();
+    }
+  }
+
+  void run_profiled(void *s) {
+    void *e0 = nullptr, *e1 = nullptr;
+    check(tl_event_create(&e0), "profile event");
+    check(tl_event_create(&e1), "profile event");
+    size_t slot_base = 0;
+    for (const Op &op : prog) {
+      if (op.dead || op.kind == Kind::Release) continue;
+      check(tl_event_record(e0, s), "profile event");
+      execute(op, s, slot_base);
+      check(tl_event_record(e1, s), "profile event");
+      float ms = 0.0f;
+      check(tl_event_elapsed_ms(&ms, e0, e1), "profile event");
+      std::string key = internal::kind_name(op.kind);
+      if (op.kind == Kind::Gemm) {
+        key += " " + std::to_string(op.gemm.m) + "x" + std::to_string(op.gemm.n) + "x" +
+               std::to_string(op.gemm.k);
+        uint64_t batch = 1;
+        for (uint32_t i = 0; i < op.gemm.batch_rank; ++i) batch *= op.gemm.batch_shape[i];
+        if (batch > 1) key += " b" + std::to_string(batch);
+        key += op.gemm.trans_a ? " T" : " N";
+        key += op.gemm.trans_b ? "T" : "N";
+      }
+      Prof &p = profile[key];
+      ++p.calls;
+      p.ms += ms;
+      if (op.kind == Kind::MultiAdamW) slot_base += op.multi.size();
+    }
+    tl_event_destroy(e0);
+    tl_event_destroy(e1);
+  }
+
+  void run_program() {
+    void *s = cuda::stream();
+    size_t ws = 0, slots = 0;
+    uint64_t live = 0;
+    for (const Op &op : prog) {
+      if (op.dead) continue;
+      ws = std::max(ws, op.workspace);
+      if (op.kind == Kind::MultiAdamW) slots += op.multi.size();
+      if (op.kind != Kind::Release) ++live;
+    }
+    ensure_workspace(ws);
+    if (slots) ensure_slots(slots);
+    stats.ops_launched += live;
+    const uint64_t k0 = tl_kernel_launches();
+    if (profiling) {
+      run_profiled(s);
+      stats.kernel_launches += tl_kernel_launches() - k0;
+      return;
+    }
+    if (!graphs || !capturable(prog)) {
+      run_ops(s);
+      stats.kernel_launches += tl_kernel_launches() - k0;
+      return;
+    }
+    std::string sig = signature(prog);
+    auto it = graph_cache.find(sig);
+    if (it != graph_cache.end()) {
+      // slot tables are re-read from pinned memory by the graph's copies
+      size_t base = 0;
+      for (const Op &op : prog)
+        if (!op.dead && op.kind == Kind::MultiAdamW) {
+          stage_slots(op, base);
+          base += op.multi.size();
+        }
+      check(tl_graph_launch(it->second.exec, s), "graph replay");
+      it->second.last_use = ++use_clock;
+      ++stats.graph_replays;
+      stats.kernel_launches += it->second.kernels;
+      return;
+    }
+    if (sig != last_signature) {
+      // first sighting: run eagerly, capture if the same program comes back
+      last_signature = std::move(sig);
+      run_ops(s);
+      stats.kernel_launches += tl_kernel_launches() - k0;
+      return;
+    }
+    check(tl_graph_capture_begin(s), "graph capture");
+    try {
+      run_ops(s);
+    } catch (...) {
+      void *junk = nullptr;
+      tl_graph_capture_end(s, &junk);
+      tl_graph_destroy(junk);
+      throw;
+    }
+    void *exec = nullptr;
+    check(tl_graph_capture_end(s, &exec), "graph capture");
+    const uint64_t kernels = tl_kernel_launches() - k0;
+    if (graph_cache.size() >= 8) {
+      auto victim = std::min_element(graph_cache.begin(), graph_cache.end(),
+                                     [](const auto &a, const auto &b) {
+                                       return a.second.last_use < b.second.last_use;
+                                     });
+      tl_graph_destroy(victim->second.exec);
+      graph_cache.erase(victim);
+    }
+    graph_cache[last_signature] = Cached{exec, kernels, ++use_clock};
+    ++stats.graph_captures;
+    check(tl_graph_launch(exec, s), "graph launch");
+    stats.kernel_launches += kernels;
+  }
+
+  void write_profile() {
+    std::ofstream out(profile_path);
+    out << "{\n  \"ops\": [\n";
+    bool first = true;
+    for (const auto &kv : profile) {
+      out << (first ? "" : ",\n") << "    {\"op\": \"" << kv.first << "\", \"calls\": "
+          << kv.second.calls << ", \"ms\": " << kv.second.ms << "}";
+      first = false;
+    }
+    out << "\n  ]\n}\n";
+  }
+};
+
+// ---------------------------------------------------------------- lifecycle
+Runtime::Runtime() : impl_(std::make_unique<Impl>()) { internal::ensure_init(); }
+
+Runtime::~Runtime() { cleanup(); }
+
+// src/my_metal/runtime.cpp:290-297
+void Runtime::start() {
+  if (impl_->state != Impl::State::Idle)
+    throw std::logic_error("CUDA runtime execution already started");
+  impl_->prog.clear();
+  impl_->window_id = internal::next_window_id();
+  impl_->state = Impl::State::Recording;
+  internal::set_active_recorder(impl_.get());
+}
+
+// src/my_metal/runtime.cpp:299-309
+void Runtime::submit() {
+  if (impl_->state != Impl::State::Recording)
+    throw std::logic_error("CUDA runtime execution has not started");
+  if (internal::active_recorder() == impl_.get()) internal::set_active_recorder(nullptr);
+  const uint64_t recorded = impl_->prog.size();
+  (void)recorded;
+  if (impl_->fusion) impl_->stats.fused_ops += internal::optimize(impl_->prog, impl_->comm);
+  else if (impl_->comm) internal::add_gradient_allreduce(impl_->prog);
+  impl_->state = Impl::State::Submitted;
+  ++impl_->stats.windows;
+  try {
+    impl_->run_program();
+  } catch (...) {
+    impl_->prog.clear();
+    throw;
+  }
+  impl_->prog.clear();
+}
+
+// src/my_metal/runtime.cpp:310-317
+void Runtime::wait() {
+  if (impl_->state != Impl::State::Submitted)
+    throw std::logic_error("CUDA runtime execution has not been submitted");
+  impl_->state = Impl::State::Idle;
+  uint32_t flags = 0;
+  check(tl_device_status(&flags, cuda::stream()), "CUDA runtime wait");
+  if (flags & TL_FLAG_INDEX_RANGE)
+    throw std::out_of_range("embedding index out of range of the embedding table");
+  if (flags & TL_FLAG_TIMEOUT)
+    throw std::runtime_error("a CUDA kernel gave up waiting on the device (timeout)");
+}
+
+// src/my_metal/runtime.cpp:170-177
+void Runtime::abort() noexcept {
+  if (internal::active_recorder() == impl_.get()) internal::set_active_recorder(nullptr);
+  impl_->prog.clear();
+  impl_->state = Impl::State::Idle;
+}
+
+// src/my_metal/runtime.cpp:179-230
+void Runtime::cleanup() noexcept {
+  if (!impl_) return;
+  if (impl_->state == Impl::State::Recording) abort();
+  if (impl_->state == Impl::State::Submitted) {
+    tl_stream_sync(cuda::initialised() ? cuda::stream() : nullptr);
+    impl_->state = Impl::State::Idle;
+  }
+  if (cuda::initialised()) {
+    tl_stream_sync(cuda::stream());
+    impl_->release_resources();
+  }
+}
+
+// src/my_metal/runtime.cpp:42-63
+void Runtime::start_profile(std::string_view output_path) {
+  impl_->profiling = true;
+  impl_->profile_path = std::string(output_path);
+  impl_->profile.clear();
+}
+
+void Runtime::end_profile() {
+  if (!impl_->profiling) return;
+  impl_->profiling = false;
+  impl_->write_profile();
+}
+
+void Runtime::set_fusion(bool enabled) { impl_->fusion = enabled; }
+void Runtime::set_graphs(bool enabled) { impl_->graphs = enabled; }
+void Runtime::set_gemm_precision(int precision) {
+  if (precision != TL_GEMM_TF32 && precision != TL_GEMM_FP32)
+    throw std::invalid_argument("unsupported GEMM precision");
+  impl_->gemm_precision = precision;
+}
+void Runtime::set_communicator(void *nccl_comm) { impl_->comm = nccl_comm; }
+const RuntimeStats &Runtime::stats() const { return impl_->stats; }
+
+// ---------------------------------------------------------------- elementwise
+namespace {
+void binary(Runtime::Impl &im, int code, const Mat &a, const Mat &b, Mat &out) {
+  check_broadcast(a.shape(), out.shape());
+  check_broadcast(b.shape(), out.shape());
+  Op &op = im.record(Kind::Binary);
+  op.code = code;
+  op.t[0] = ref(a);
+  op.t[1] = ref(b);
+  op.t[2] = ref(out);
+}
+
+// src/my_metal/runtime.cpp:116-136
+void scalar(Runtime::Impl &im, int code, const Mat &a, float s, Mat &out) {
+  if (a.shape() != out.shape())
+    throw std::invalid_argument("scalar operation input and output shapes must match");
+  Op &op = im.record(Kind::Scalar);
+  op.code = code;
+  op.t[0] = ref(a);
+  op.t[1] = ref(out);
+  op.f0 = s;
+}
+
+// src/my_metal/runtime.cpp:97-114 (dispatched over the output's elements)
+void unary(Runtime::Impl &im, int code, const Mat &a, Mat &out) {
+  if (a.numel() != out.numel())
+    throw std::invalid_argument("unary operation input and output sizes must match");
+  Op &op = im.record(Kind::Unary);
+  op.code = code;
+  op.t[0] = ref(a);
+  op.t[1] = ref(out);
+}
+}  // namespace
+
+// src/my_metal/runtime.cpp:321-353
+void Runtime::add(const Mat &a, const Mat &b, Mat &o) { binary(*impl_, TL_ADD, a, b, o); }
+void Runtime::add(const Mat &a, kernel_type s, Mat &o) { scalar(*impl_, TL_SCALAR_ADD, a, s, o); }
+void Runtime::sub(const Mat &a, const Mat &b, Mat &o) { binary(*impl_, TL_SUB, a, b, o); }
+void Runtime::hadamard(const Mat &a, const Mat &b, Mat &o) { binary(*impl_, TL_MUL, a, b, o); }
+void Runtime::divide(const Mat &a, const Mat &b, Mat &o) { binary(*impl_, TL_DIV, a, b, o); }
+void Runtime::divide(const Mat &a, kernel_type s, Mat &o) {
+  scalar(*impl_, TL_SCALAR_DIV, a, s, o);
+}
+// src/my_metal/runtime.cpp:355-373
+void Runtime::sigmoid(const Mat &a, Mat &o) { unary(*impl_, TL_SIGMOID, a, o); }
+void Runtime::sqrt(const Mat &a, Mat &o) { unary(*impl_, TL_SQRT, a, o); }
+void Runtime::pow(const Mat &a, kernel_type e, Mat &o) { scalar(*impl_, TL_SCALAR_POW, a, e, o); }
+void Runtime::exp(const Mat &a, Mat &o) { unary(*impl_, TL_EXP, a, o); }
+// src/my_metal/runtime.cpp:1073-1081
+void Runtime::GELU(const Mat &a, Mat &o) { unary(*impl_, TL_GELU, a, o); }
+void Runtime::GELU_derivative(const Mat &a, Mat &o) { unary(*impl_, TL_GELU_DERIVATIVE, a, o); }
+
+// src/my_metal/runtime.cpp:1170-1186
+void Runtime::copy(const Mat &a, Mat &output) {
+  if (a.shape() != output.shape())
+    throw std::invalid_argument("copy destination has incorrect shape");
+  Op &op = impl_->record(Kind::Copy);
+  op.t[0] = ref(a);
+  op.t[1] = ref(output);
+}
+
+// src/my_metal/runtime.cpp:843-848
+void Runtime::sqe(const Mat &pred, const Mat &target, Mat &output) {
+  sub(pred, target, output);
+  hadamard(output, output, output);
+}
+
+// ----------------------------------------------------------------------- GEMM
+// src/my_metal/runtime.cpp:375-505: C = A*B over the last two dims with
+// broadcast batch dims.
+void Runtime::mult(const Mat &a, const Mat &b, Mat &output) {
+  const auto expected = rtensor::infer_mult(a.shape(), b.shape());  // same throws as Metal
+  if (output.shape() != expected)
+    throw std::invalid_argument("matmul destination has incorrect shape");
+  Op &op = impl_->record(Kind::Gemm);
+  op.t[0] = ref(a);
+  op.t[1] = ref(b);
+  op.t[2] = ref(output);
+  tl_gemm_desc &g = op.gemm;
+  const auto &as = a.shape(), &bs = b.shape(), &cs = output.shape();
+  g.a = static_cast<const float *>(op.t[0].p);
+  g.b = static_cast<const float *>(op.t[1].p);
+  g.c = op.t[2].f();
+  g.m = as[as.size() - 2];
+  g.k = as[as.size() - 1];
+  g.n = bs[bs.size() - 1];
+  g.precision = impl_->gemm_precision;
+  const size_t batch_rank = cs.size() - 2;
+  // merge batch dims into at most TL_GEMM_MAX_BATCH_RANK (they are dense)
+  std::vector<uint32_t> bshape;
+  std::vector<uint64_t> sa, sb, sc;
+  const uint64_t amat = uint64_t(g.m) * g.k, bmat = uint64_t(g.k) * g.n, cmat = uint64_t(g.m) * g.n;
+  auto dense_strides = [&](const std::vector<uint32_t> &shape, size_t rank, uint64_t mat) {
+    std::vector<uint64_t> st(batch_rank, 0);
+    const size_t r = shape.size() - 2;
+    uint64_t acc = mat;
+    for (size_t i = r; i-- > 0;) {
+      const size_t oi = batch_rank - r + i;
+      st[oi] = shape[i] == 1 ? 0 : acc;
+      acc *= shape[i];
+    }
+    (void)rank;
+    return st;
+  };
+  const auto full_a = dense_strides(as, as.size(), amat);
+  const auto full_b = dense_strides(bs, bs.size(), bmat);
+  const auto full_c = dense_strides(cs, cs.size(), cmat);
+  for (size_t i = 0; i < batch_rank; ++i) {
+    if (cs[i] == 1) continue;
+    if (!bshape.empty() && sa.back() == full_a[i] * cs[i] && sb.back() == full_b[i] * cs[i] &&
+        sc.back() == full_c[i] * cs[i]) {
+      bshape.back() *= cs[i];
+      sa.back() = full_a[i];
+      sb.back() = full_b[i];
+      sc.back() = full_c[i];
+      continue;
+    }
+    bshape.push_back(cs[i]);
+    sa.push_back(full_a[i]);
+    sb.push_back(full_b[i]);
+    sc.push_back(full_c[i]);
+  }
+  if (bshape.size() > TL_GEMM_MAX_BATCH_RANK)
+    throw std::invalid_argument("matmul batch rank exceeds the CUDA runtime limit");
+  g.batch_rank = static_cast<uint32_t>(bshape.size());
+  for (size_t i = 0; i < bshape.size(); ++i) {
+    g.batch_shape[i] = bshape[i];
+    g.a_batch_stride[i] = sa[i];
+    g.b_batch_stride[i] = sb[i];
+    g.c_batch_stride[i] = sc[i];
+  }
+}
+
+// --------------------------------------------------------------- reductions
+// src/my_metal/runtime.cpp:506-518
+void Runtime::sum(const Mat &input, Mat &output) {
+  if (output.numel() < 1) throw std::invalid_argument("sum destination must hold a value");
+  Op &op = impl_->record(Kind::Reduce);
+  op.code = TL_REDUCE_SUM;
+  op.t[0] = ref(input);
+  op.t[1] = ref(output);
+  op.t[1].rank = 1;
+  op.t[1].shape[0] = 1;
+  op.workspace = tl_reduce_workspace_size(op.t[0].shape, op.t[0].rank, op.t[1].shape, 1);
+}
+
+// src/my_metal/runtime.cpp:520-527
+void Runtime::sum(const Mat &input, size_t axis, Mat &output) {
+  if (axis >= input.shape().size()) throw std::out_of_range("sum axis out of range");
+  sum_to_shape(input, output.shape(), output);
+}
+
+// src/my_metal/runtime.cpp:661-739
+void Runtime::sum_to_shape(const Mat &a, std::span<const uint32_t> output_shape, Mat &output) {
+  const auto &a_shape = a.shape();
+  if (output_shape.size() > a_shape.size())
+    throw std::invalid_argument("cannot reduce to a shape with a higher rank");
+  if (output.shape().size() != output_shape.size() ||
+      !std::equal(output.shape().begin(), output.shape().end(), output_shape.begin()))
+    throw std::invalid_argument("sum_to_shape destination has incorrect shape");
+  const size_t off = a_shape.size() - output_shape.size();
+  bool reduced = false;
+  for (size_t i = 0; i < a_shape.size(); ++i) {
+    const uint32_t o = i < off ? 1u : output_shape[i - off];
+    if (a_shape[i] != o) {
+      if (o != 1) throw std::invalid_argument("invalid reduce_to_shape");
+      reduced = true;
+    }
+  }
+  if (!reduced) {  // same element order: a copy (Metal adds 0 through a view)
+    Op &op = impl_->record(Kind::Copy);
+    op.t[0] = ref(a);
+    op.t[1] = ref(output);
+    return;
+  }
+  Op &op = impl_->record(Kind::Reduce);
+  op.code = TL_REDUCE_SUM;
+  op.t[0] = ref(a);
+  op.t[1] = ref(output);
+  op.workspace = tl_reduce_workspace_size(op.t[0].shape, op.t[0].rank, op.t[1].shape,
+                                          op.t[1].rank);
+}
+
+// src/my_metal/runtime.cpp:595-659
+void Runtime::reduce_to_shape(const Mat &a, std::span<const uint32_t> output_shape, Mat &output,
+                              ReduceKind kind) {
+  if (output_shape.size() != a.shape().size())
+    throw std::invalid_argument("cannot reduce to shape if ranks differ");
+  size_t shrink = 0;
+  for (size_t i = 0; i < output_shape.size(); ++i) {
+    if (a.shape()[i] != output_shape[i]) {
+      if (output_shape[i] != 1) throw std::invalid_argument("invalid reduce_to_shape");
+      if (++shrink > 1)
+        throw std::invalid_argument(
+            "reduce_to_shape currently supports only one shrinking dimension");
+    }
+  }
+  if (shrink == 0) {
+    output = a;
+    return;
+  }
+  Op &op = impl_->record(Kind::Reduce);
+  op.code = kind == ReduceKind::Sum ? TL_REDUCE_SUM : TL_REDUCE_MAX;
+  op.t[0] = ref(a);
+  op.t[1] = ref(output);
+  op.workspace = tl_reduce_workspace_size(op.t[0].shape, op.t[0].rank, op.t[1].shape,
+                                          op.t[1].rank);
+}
+
+// src/my_metal/runtime.cpp:741-745
+void Runtime::max_to_shape(const Mat &a, std::span<const uint32_t> output_shape, Mat &output) {
+  reduce_to_shape(a, output_shape, output, ReduceKind::Max);
+}
+
+// src/my_metal/runtime.cpp:850-918
+void Runtime::argmax(const Mat &a, IndexMat &output) {
+  if (a.numel() == 0) throw std::invalid_argument("argmax requires a non-empty tensor");
+  if (output.numel() < 1) throw std::invalid_argument("argmax destination must hold an index");
+  Op &op = impl_->record(Kind::Argmax);
+  op.t[0] = ref(a);
+  op.t[1] = ref(output);
+  op.workspace = tl_argmax_workspace_size(a.numel());
+}
+
+// ---------------------------------------------------------------- layout ops
+// src/my_metal/runtime.cpp:529-569
+void Runtime::transpose(const Mat &a, Mat &output, int32_t dim_a, int32_t dim_b) {
+  if (a.shape().size() < 2) throw std::invalid_argument("transpose requires rank >= 2");
+  const size_t axis_a = rtensor::normalise_dimension(a.shape().size(), dim_a);
+  const size_t axis_b = rtensor::normalise_dimension(a.shape().size(), dim_b);
+  if (axis_a == axis_b) throw std::invalid_argument("transpose dimensions must be different");
+  if (output.shape() != rtensor::infer_transpose(a.shape(), dim_a, dim_b))
+    throw std::invalid_argument("transpose destination has incorrect shape");
+  Op &op = impl_->record(Kind::Transpose);
+  op.t[0] = ref(a);
+  op.t[1] = ref(output);
+  op.i0 = static_cast<int32_t>(axis_a);
+  op.i1 = static_cast<int32_t>(axis_b);
+}
+
+// src/my_metal/runtime.cpp:571-581
+void Runtime::split_last_dim(const Mat &a, Mat &output, uint32_t outer, uint32_t inner) {
+  if (output.shape() != rtensor::infer_split_last_dim(a.shape(), outer, inner))
+    throw std::invalid_argument("split_last_dim destination has incorrect shape");
+  Op &op = impl_->record(Kind::Copy);
+  op.t[0] = ref(a);
+  op.t[1] = ref(output);
+}
+
+// src/my_metal/runtime.cpp:583-593
+void Runtime::merge_last_dims(const Mat &a, Mat &output, uint32_t outer, uint32_t inner) {
+  if (output.shape() != rtensor::infer_merge_last_dims(a.shape(), outer, inner))
+    throw std::invalid_argument("merge_last_dims destination has incorrect shape");
+  Op &op = impl_->record(Kind::Copy);
+  op.t[0] = ref(a);
+  op.t[1] = ref(output);
+}
+
+// -------------------------------------------------------------- row operators
+// src/my_metal/runtime.cpp:747-766
+void Runtime::softmax(const Mat &x, Mat &output) {
+  if (x.shape().empty() || x.shape().back() == 0)
+    throw std::invalid_argument("softmax requires a non-empty final dimension");
+  if (output.shape() != x.shape())
+    throw std::invalid_argument("softmax destination has incorrect shape");
+  Op &op = impl_->record(Kind::Softmax);
+  op.t[0] = ref(x);
+  op.t[1] = ref(output);
+}
+
+namespace {
+// src/my_metal/runtime.cpp:768-841 (shared argument checks)
+void check_xent(const char *name, const Mat &logits, const IndexMat &targets) {
+  const std::string n(name);
+  if (logits.shape().size() < 2 || logits.shape().back() == 0)
+    throw std::invalid_argument(n + " requires logits with a non-empty final dimension");
+  if (targets.shape().size() + 1 != logits.shape().size())
+    throw std::invalid_argument(n + " target rank must be one less than logits rank");
+  for (size_t i = 0; i < targets.shape().size(); ++i)
+    if (targets.shape()[i] != logits.shape()[i])
+      throw std::invalid_argument(n + " target shape must match logits leading dimensions");
+}
+}  // namespace
+
+void Runtime::cross_entropy(const Mat &logits, const IndexMat &targets, Mat &output) {
+  check_xent("cross_entropy", logits, targets);
+  auto output_shape = targets.shape();
+  output_shape.push_back(1);
+  if (output.shape() != output_shape)
+    throw std::invalid_argument(
+        "cross_entropy destination must match target shape with a trailing singleton "
+        "dimension");
+  Op &op = impl_->record(Kind::Xent);
+  op.t[0] = ref(logits);
+  op.t[1] = ref(targets);
+  op.t[2] = ref(output);
+}
+
+void Runtime::cross_entropy_derivative(const Mat &logits, const IndexMat &targets, Mat &output) {
+  check_xent("cross_entropy_derivative", logits, targets);
+  if (output.shape() != logits.shape())
+    throw std::invalid_argument("cross_entropy_derivative destination must match logits shape");
+  Op &op = impl_->record(Kind::XentBwd);
+  op.t[0] = ref(logits);
+  op.t[1] = ref(targets);
+  op.t[2] = ref(output);
+}
+
+// src/my_metal/runtime.cpp:1031-1059
+void Runtime::RMS(const Mat &values, Mat &destination) {
+  auto rms_shape = values.shape();
+  if (rms_shape.empty()) throw std::invalid_argument("RMS requires a non-empty tensor");
+  rms_shape.back() = 1;
+  if (destination.shape() != rms_shape)
+    throw std::invalid_argument("RMS destination has incorrect shape");
+  if (values.shape().back() == 0) throw std::invalid_argument("RMS requires non-empty rows");
+  Op &op = impl_->record(Kind::Rms);
+  op.t[0] = ref(values);
+  op.t[1] = ref(destination);
+}
+
+// src/my_metal/runtime.cpp:1061-1072
+void Runtime::RMSNorm(const Mat &values, Mat &destination) {
+  if (destination.shape() != values.shape())
+    throw std::invalid_argument("RMSNorm destination has incorrect shape");
+  if (values.shape().empty() || values.shape().back() == 0)
+    throw std::invalid_argument("RMSNorm requires non-empty rows");
+  Op &op = impl_->record(Kind::RmsNorm);
+  op.t[0] = ref(values);
+  op.t[1] = ref(destination);
+}
+
+// ----------------------------------------------------------------- embedding
+// src/my_metal/runtime.cpp:920-944
+void Runtime::embedding_lookup(const Mat &weights, const IndexMat &ids, Mat &output) {
+  if (weights.shape().size() != 2)
+    throw std::invalid_argument("embedding weights must have rank 2");
+  auto expected = ids.shape();
+  expected.push_back(weights.shape().back());
+  if (output.shape() != expected)
+    throw std::invalid_argument("embedding output shape does not match IDs");
+  Op &op = impl_->record(Kind::Gather);
+  op.t[0] = ref(weights);
+  op.t[1] = ref(ids);
+  op.t[2] = ref(output);
+}
+
+// src/my_metal/runtime.cpp:946-950
+void Runtime::gather_rows(const Mat &values, const IndexMat &indices, Mat &output) {
+  embedding_lookup(values, indices, output);
+}
+
+namespace {
+// src/my_metal/runtime.cpp:952-981
+void check_scatter(const Mat &values, const IndexMat &ids, const Mat &destination) {
+  if (destination.shape().size() != 2)
+    throw std::invalid_argument("scatter destination must have rank 2");
+  auto expected = ids.shape();
+  expected.push_back(destination.shape().back());
+  if (values.shape() != expected)
+    throw std::invalid_argument("scatter input shape does not match IDs and embedding size");
+}
+}  // namespace
+
+// src/my_metal/runtime.cpp:983-1009
+void Runtime::scatter_add_rows(const Mat &base, const IndexMat &ids, const Mat &values,
+                               Mat &destination) {
+  if (base.shape() != destination.shape())
+    throw std::invalid_argument("scatter base and destination shapes must match");
+  check_scatter(values, ids, destination);
+  Op &op = impl_->record(Kind::Scatter);
+  op.t[0] = ref(values);
+  op.t[1] = ref(ids);
+  op.t[2] = ref(base);
+  op.t[3] = ref(destination);
+  op.workspace = tl_embedding_scatter_workspace_size(static_cast<uint32_t>(ids.numel()),
+                                                     destination.shape()[0]);
+}
+
+// src/my_metal/runtime.cpp:1011-1030
+void Runtime::scatter_index(const Mat &values, const IndexMat &ids, Mat &destination) {
+  check_scatter(values, ids, destination);
+  Op &op = impl_->record(Kind::Scatter);
+  op.t[0] = ref(values);
+  op.t[1] = ref(ids);
+  op.t[3] = ref(destination);
+  op.workspace = tl_embedding_scatter_workspace_size(static_cast<uint32_t>(ids.numel()),
+                                                     destination.shape()[0]);
+}
+
+// ----------------------------------------------------------------- optimiser
+// src/my_metal/runtime.cpp:1083-1101
+void Runtime::accumulate_gradient_squared_norm(const Mat &gradient, Mat &squared_norm) {
+  if (squared_norm.numel() != 1)
+    throw std::invalid_argument("gradient norm destination must be a scalar");
+  Op &op = impl_->record(Kind::SqNorm);
+  op.t[0] = ref(gradient);
+  op.t[1] = ref(squared_norm);
+  op.workspace = tl_grad_sqnorm_workspace_size(gradient.numel());
+}
+
+// src/my_metal/runtime.cpp:1103-1127
+void Runtime::clip_gradient(const Mat &gradient, const Mat &squared_norm, kernel_type max_norm,
+                            Mat &destination) {
+  if (squared_norm.numel() != 1) throw std::invalid_argument("gradient norm input must be a scalar");
+  if (gradient.shape() != destination.shape())
+    throw std::invalid_argument("gradient clipping input and destination shapes must match");
+  if (!(max_norm > 0.0f) || !std::isfinite(max_norm))
+    throw std::invalid_argument("maximum gradient norm must be finite and positive");
+  Op &op = impl_->record(Kind::Clip);
+  op.t[0] = ref(gradient);
+  op.t[1] = ref(squared_norm);
+  op.t[2] = ref(destination);
+  op.f0 = max_norm;
+}
+
+// src/my_metal/runtime.cpp:1129-1168
+void Runtime::adamW(const Mat &parameter, const Mat &gradient, Mat &destination, Mat &momentum1,
+                    Mat &momentum2, const Mat &beta1, const Mat &beta2, const Mat &decay,
+                    const Mat &learning_rate, kernel_type epsilon, uint32_t step) {
+  if (gradient.shape() != parameter.shape() || destination.shape() != parameter.shape() ||
+      momentum1.shape() != parameter.shape() || momentum2.shape() != parameter.shape())
+    throw std::invalid_argument("AdamW tensor shapes must match");
+  if (beta1.numel() != 1 || beta2.numel() != 1 || decay.numel() != 1 || learning_rate.numel() != 1)
+    throw std::invalid_argument("AdamW parameters must be scalars");
+  if (step == 0) throw std::invalid_argument("AdamW step must be greater than zero");
+  Op &op = impl_->record(Kind::AdamW);
+  op.t[0] = ref(parameter);
+  op.t[1] = ref(gradient);
+  op.t[2] = ref(destination);
+  op.t[3] = ref(momentum1);
+  op.t[4] = ref(momentum2);
+  op.t[5] = ref(beta1);
+  op.t[6] = ref(beta2);
+  op.t[7] = ref(decay);
+  op.t[8] = ref(learning_rate);
+  op.f0 = epsilon;
+  op.u0 = step;
+}
+
+}  // namespace cuda

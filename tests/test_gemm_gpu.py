@@ -1,0 +1,155 @@
+"""GEMM parity (tl_gemm: tcgen05 kind::tf32 tensor cores, and the exact-fp32
+CUDA-core path) with the float64 oracle on the configuration-2 sweep
+(M, N, K in {192, 384, 1536, 12288}, NN / NT / TN), the batched and
+broadcast-batch products of the attention composite, and the fused
+epilogues (bias, accumulate, GELU).
+
+Tolerance (<= 1e-3 relative for TF32 paths):
+  TF32: ||C - C_ref||_F / ||C_ref||_F <= 1e-3 and
+        max|C - C_ref| <= 4e-3 * max|C_ref|
+  FP32: |C - C_ref| <= 1e-5 * (|A| |B|) elementwise bound."""
+import itertools
+
+import numpy as np
+import pytest
+
+from oracle import ops
+from templit_b200 import capi
+from tests.helpers import Dev
+
+pytestmark = pytest.mark.gpu
+
+TF32_FRO = 1e-3
+TF32_MAX = 4e-3
+
+
+@pytest.fixture(scope="module")
+def dev():
+    return Dev()
+
+
+def check_tf32(got, want):
+    want = np.asarray(want, np.float64)
+    got = np.asarray(got, np.float64).reshape(want.shape)
+    err = got - want
+    fro = np.linalg.norm(err) / max(np.linalg.norm(want), 1e-30)
+    mx = np.abs(err).max() / max(np.abs(want).max(), 1e-30)
+    assert fro <= TF32_FRO and mx <= TF32_MAX, (fro, mx)
+
+
+def check_fp32(got, want, a, b, trans_a=False, trans_b=False):
+    x = np.swapaxes(np.abs(a), -1, -2) if trans_a else np.abs(a)
+    y = np.swapaxes(np.abs(b), -1, -2) if trans_b else np.abs(b)
+    bound = 1e-5 * np.matmul(x.astype(np.float64), y.astype(np.float64)) + 1e-30
+    assert np.all(np.abs(np.asarray(got, np.float64) - want) <= bound)
+
+
+def operands(r, m, n, k, trans_a, trans_b, batch=()):
+    a = r.standard_normal(batch + ((k, m) if trans_a else (m, k))).astype(np.float32)
+    b = r.standard_normal(batch + ((n, k) if trans_b else (k, n))).astype(np.float32)
+    return a, b
+
+
+SWEEP = [s for s in itertools.product([192, 384, 1536], repeat=3)]
+
+
+@pytest.mark.parametrize("form", ["NN", "NT", "TN"])
+@pytest.mark.parametrize("m,n,k", SWEEP)
+def test_sweep_tf32(dev, m, n, k, form):
+    r = np.random.default_rng(m * 7 + n * 3 + k)
+    ta, tb = form[0] == "T", form[1] == "T"
+    a, b = operands(r, m, n, k, ta, tb)
+    got = dev.gemm(a, b, trans_a=ta, trans_b=tb)
+    check_tf32(got, ops.gemm(a, b, ta, tb))
+
+
+@pytest.mark.parametrize("form", ["NN", "NT", "TN"])
+@pytest.mark.parametrize("m,n,k", [(12288, 384, 384), (12288, 1536, 384), (12288, 384, 1536),
+                                   (12288, 2048, 384), (384, 384, 12288), (384, 1536, 12288),
+                                   (1536, 384, 12288)])
+def test_large_tf32_sampled(dev, m, n, k, form):
+    """12288-dim cases are checked on 4096 sampled outputs in float64."""
+    r = np.random.default_rng(m + n + k)
+    ta, tb = form[0] == "T", form[1] == "T"
+    a, b = operands(r, m, n, k, ta, tb)
+    got = dev.gemm(a, b, trans_a=ta, trans_b=tb)
+    A = (a.T if ta else a).astype(np.float64)
+    B = (b.T if tb else b).astype(np.float64)
+    rows = r.integers(0, m, 4096)
+    cols = r.integers(0, n, 4096)
+    want = np.einsum("ij,ji->i", A[rows], B[:, cols])
+    check_tf32(got[rows, cols], want)
+
+
+@pytest.mark.parametrize("form", ["NN", "NT", "TN"])
+@pytest.mark.parametrize("m,n,k", [(192, 192, 192), (33, 17, 65), (2, 3, 2), (128, 64, 8),
+                                   (130, 258, 36)])
+def test_fp32_path(dev, m, n, k, form):
+    r = np.random.default_rng(m + 2 * n + 3 * k)
+    ta, tb = form[0] == "T", form[1] == "T"
+    a, b = operands(r, m, n, k, ta, tb)
+    got = dev.gemm(a, b, trans_a=ta, trans_b=tb, precision=capi.TL_GEMM_FP32)
+    check_fp32(got, ops.gemm(a, b, ta, tb), a, b, ta, tb)
+
+
+@pytest.mark.parametrize("m,n,k", [(130, 258, 36), (200, 100, 60), (129, 65, 33), (192, 256, 1000)])
+def test_ragged_tiles_tf32(dev, m, n, k):
+    """Edges of the 128 x BN x 32 tile grid (masked rows/cols, zero-filled k)."""
+    r = np.random.default_rng(17)
+    for ta, tb in ((False, False), (False, True), (True, False)):
+        a, b = operands(r, m, n, k, ta, tb)
+        check_tf32(dev.gemm(a, b, trans_a=ta, trans_b=tb), ops.gemm(a, b, ta, tb))
+
+
+def test_attention_batched_and_broadcast(dev):
+    """QK^T and PV of the attention composite (nn/multi_head.h:45-52), batch
+    [64, 6], and a broadcast batch operand."""
+    r = np.random.default_rng(3)
+    q = r.standard_normal((64, 6, 192, 64)).astype(np.float32)
+    kt = r.standard_normal((64, 6, 64, 192)).astype(np.float32)
+    check_tf32(dev.gemm(q, kt), ops.matmul(q, kt))
+    p = r.random((64, 6, 192, 192)).astype(np.float32)
+    v = r.standard_normal((64, 6, 192, 64)).astype(np.float32)
+    check_tf32(dev.gemm(p, v), ops.matmul(p, v))
+    w = r.standard_normal((384, 384)).astype(np.float32)
+    x = r.standard_normal((64, 192, 384)).astype(np.float32)
+    check_tf32(dev.gemm(x, w), ops.matmul(x, w))
+    xb = r.standard_normal((4, 1, 96, 40)).astype(np.float32)
+    yb = r.standard_normal((1, 3, 40, 72)).astype(np.float32)
+    check_tf32(dev.gemm(xb, yb), ops.matmul(xb, yb))
+    # batched transposed forms (weight gradient as one K = B*T product is the
+    # fused path; the executor's batched [64,384,192] x [64,192,N] as well)
+    xt = r.standard_normal((8, 192, 384)).astype(np.float32)
+    g = r.standard_normal((8, 192, 256)).astype(np.float32)
+    check_tf32(dev.gemm(xt, g, trans_a=True), ops.gemm(xt, g, True, False))
+
+
+def test_epilogues(dev):
+    r = np.random.default_rng(4)
+    a = r.standard_normal((512, 384)).astype(np.float32)
+    b = r.standard_normal((384, 1536)).astype(np.float32)
+    bias = r.standard_normal((1536,)).astype(np.float32)
+    c0 = r.standard_normal((512, 1536)).astype(np.float32)
+    out, g = dev.gemm(a, b, bias=bias, gelu=True)
+    want = ops.gemm(a, b, bias=bias)
+    check_tf32(out, want)
+    check_tf32(g, ops.gelu(want))
+    acc = dev.gemm(a, b, c=c0, beta=1.0)
+    check_tf32(acc, ops.gemm(a, b, c=c0, beta=1.0))
+    out32, g32 = dev.gemm(a[:64], b, bias=bias, gelu=True, precision=capi.TL_GEMM_FP32)
+    np.testing.assert_allclose(out32, ops.gemm(a[:64], b, bias=bias), rtol=1e-4, atol=1e-3)
+    np.testing.assert_allclose(g32, ops.gelu(ops.gemm(a[:64], b, bias=bias)), rtol=1e-4, atol=1e-3)
+
+
+def test_zero_and_empty(dev):
+    r = np.random.default_rng(5)
+    a = np.zeros((256, 128), np.float32)
+    b = r.standard_normal((128, 256)).astype(np.float32)
+    assert np.all(dev.gemm(a, b) == 0)
+    # identity: exact in TF32 for small integers (tests/test_metal_runtime.cpp:307-342)
+    eye = np.broadcast_to(np.eye(64, dtype=np.float32), (2, 64, 64)).copy()
+    vals = (np.arange(2 * 64 * 64) % 31 - 15).astype(np.float32).reshape(2, 64, 64)
+    np.testing.assert_array_equal(dev.gemm(eye, vals), vals)
+    big = np.broadcast_to(np.eye(256, dtype=np.float32), (3, 256, 256)).copy()
+    vb = (np.arange(3 * 256 * 256) % 31 - 15).astype(np.float32).reshape(3, 256, 256)
+    np.testing.assert_array_equal(dev.gemm(big, vb), vb)

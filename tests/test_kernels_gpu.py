@@ -1,0 +1,329 @@
+"""Parity of every kernel of the C ABI (include/templit_cuda.h) with the CPU
+oracle (oracle/ops.py) and with the reference's known answers, on seeded
+inputs, including ragged sizes and the edge cases the reference tests
+(empty inputs, out-of-range targets and ids, extreme logits).
+
+Tolerances: fp32 kernels vs the float64 oracle within rtol 1e-5 (the
+reference suite's eps 1e-5 / 1e-4 where it states them); integer and index
+results bit-exact."""
+import numpy as np
+import pytest
+
+from oracle import ops
+from tests.helpers import Dev, known_answers
+from tests.test_oracle_golden import compare
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-5
+
+
+@pytest.fixture(scope="module")
+def dev():
+    return Dev()
+
+
+def rng(seed=0):
+    return np.random.default_rng(seed)
+
+
+def close(got, want, rtol=RTOL, atol=None, scale=None):
+    want = np.asarray(want, np.float64)
+    got = np.asarray(got, np.float64).reshape(want.shape)
+    if atol is None:
+        atol = rtol * (scale if scale is not None else max(1.0, np.abs(want).max(initial=0)))
+    np.testing.assert_allclose(got, want, rtol=rtol, atol=atol)
+
+
+# ------------------------------------------------------------ known answers
+KERNEL_OPS = {"binary", "scalar", "unary", "rms", "rmsnorm", "matmul", "sum_to_shape",
+              "max_to_shape", "transpose", "softmax", "cross_entropy",
+              "cross_entropy_derivative", "argmax", "embedding_lookup", "scatter", "adamw",
+              "clip"}
+CASES = [c for c in known_answers() if c["op"] in KERNEL_OPS]
+
+
+def kernel_eval(dev, case):
+    op, i = case["op"], case["inputs"]
+    if op == "binary":
+        return dev.binary(i["kind"], np.reshape(i["a"], i["a_shape"]),
+                          np.reshape(i["b"], i["b_shape"]), i["out_shape"])
+    if op == "scalar":
+        return dev.scalar(i["kind"], i["x"], i["s"])
+    if op == "unary":
+        return dev.unary(i["kind"], i["x"])
+    if op in ("rms", "rmsnorm", "softmax"):
+        return dev.rows(op, np.reshape(i["x"], i["shape"]))
+    if op == "matmul":
+        return dev.gemm(np.reshape(i["a"], i["a_shape"]), np.reshape(i["b"], i["b_shape"]))
+    if op == "sum_to_shape":
+        return dev.reduce("sum", np.reshape(i["x"], i["shape"]), i["out_shape"])
+    if op == "max_to_shape":
+        return dev.reduce("max", np.reshape(i["x"], i["shape"]), i["out_shape"])
+    if op == "transpose":
+        return dev.transpose(np.reshape(i["x"], i["shape"]), *i["dims"])
+    if op == "cross_entropy":
+        z = np.reshape(i["logits"], i["shape"])
+        return dev.xent(z, np.reshape(i["targets"], z.shape[:-1]))
+    if op == "cross_entropy_derivative":
+        z = np.reshape(i["logits"], i["shape"])
+        return dev.xent(z, np.reshape(i["targets"], z.shape[:-1]), backward=True)
+    if op == "argmax":
+        return [dev.argmax(i["x"])]
+    if op == "embedding_lookup":
+        return dev.gather(np.reshape(i["weights"], i["w_shape"]), i["ids"])
+    if op == "scatter":
+        base = None if i["base"] is None else np.reshape(i["base"], (i["n_rows"], i["dim"]))
+        return dev.scatter(np.reshape(i["values"], (-1, i["dim"])), i["ids"], i["n_rows"], base)
+    if op == "clip":
+        import ctypes
+        grads = [dev.t(g) for g in i["grads"]]
+        sq = dev.t([0.0])
+        for g in grads:
+            nb = dev.lib.tl_grad_sqnorm_workspace_size(g.numel())
+            ws = dev.ws(nb)
+            dev.call("tl_grad_sqnorm_accumulate", dev.p(g), g.numel(), dev.p(sq), dev.p(ws), nb,
+                     dev.stream)
+        for g in grads:
+            dev.call("tl_clip_gradient", dev.p(g), dev.p(sq), ctypes.c_float(i["max_norm"]),
+                     dev.p(g), g.numel(), dev.stream)
+        return {"sqnorm": float(dev.host(sq)[0]), "clipped": [dev.host(g) for g in grads]}
+    if op == "adamw":
+        return adamw_steps(dev, i, 2)
+    raise KeyError(op)
+
+
+def adamw_steps(dev, i, steps):
+    import ctypes
+    p, g = dev.t(i["param"]), dev.t(i["grad"])
+    m1, m2 = dev.t(np.zeros(p.numel())), dev.t(np.zeros(p.numel()))
+    lr, wd = i["lr"], i["weight_decay"]
+    b1, b2 = dev.t([i["beta1"]]), dev.t([i["beta2"]])
+    decay, lrt = dev.t([np.float32(1) - np.float32(lr) * np.float32(wd)]), dev.t([lr])
+    out = []
+    for step in range(1, steps + 1):
+        dev.call("tl_adamw", dev.p(p), dev.p(g), dev.p(p), dev.p(m1), dev.p(m2), dev.p(b1),
+                 dev.p(b2), dev.p(decay), dev.p(lrt), ctypes.c_float(i["eps"]), step, p.numel(),
+                 dev.stream)
+        out.append(dev.host(p).copy())
+    return out
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_kernels_match_reference_known_answers(dev, case):
+    compare(kernel_eval(dev, case), case)
+
+
+# ------------------------------------------------------ seeded oracle parity
+@pytest.mark.parametrize("shape,bshape", [
+    ((64, 192, 384), (64, 192, 384)),   # residual add
+    ((64, 192, 384), (1, 384)),         # bias row
+    ((64, 6, 192, 192), (1, 1, 192, 192)),  # attention mask
+    ((64, 6, 192, 192), (1, 1)),        # score scaling
+    ((64, 192, 384), (64, 192, 1)),     # per-row scalar (RMSNorm)
+    ((7, 5, 3), (5, 1)),                # ragged, unaligned
+    ((3,), (1,)),
+])
+@pytest.mark.parametrize("kind", ["add", "sub", "mul", "div"])
+def test_binary_broadcast(dev, shape, bshape, kind):
+    r = rng(1)
+    a = r.standard_normal(shape).astype(np.float32)
+    b = r.standard_normal(bshape).astype(np.float32)
+    if kind == "div":
+        b = np.where(np.abs(b) < 0.1, 0.5, b).astype(np.float32)
+    got = dev.binary(kind, a, b, shape)
+    close(got, ops.broadcast_binary(kind, a, b, shape))
+    # the operand may also be the broadcast one on the left
+    if kind == "sub":
+        got = dev.binary(kind, b, a, shape)
+        close(got, ops.broadcast_binary(kind, b, a, shape))
+
+
+@pytest.mark.parametrize("n", [1, 3, 4, 1023, 1 << 20, (1 << 20) + 5])
+def test_unary_scalar(dev, n):
+    r = rng(2)
+    x = r.standard_normal(n).astype(np.float32)
+    for kind, ref in (("sigmoid", ops.sigmoid), ("exp", np.exp), ("gelu", ops.gelu),
+                      ("gelu_derivative", ops.gelu_derivative)):
+        close(dev.unary(kind, x), ref(x.astype(np.float64)), rtol=2e-6, atol=2e-6)
+    close(dev.unary("sqrt", np.abs(x)), np.sqrt(np.abs(x).astype(np.float64)), rtol=1e-6)
+    close(dev.scalar("add", x, 1e-6), ops.scalar_op("add", x, np.float32(1e-6)), rtol=1e-6)
+    close(dev.scalar("div", x, 384.0), ops.scalar_op("div", x, 384.0), rtol=1e-6)
+    close(dev.scalar("pow", np.abs(x), 3.0), ops.scalar_op("pow", np.abs(x), 3.0), rtol=2e-6)
+    g = r.standard_normal(n).astype(np.float32)
+    close(dev.gelu_backward(x, g), ops.gelu_backward(x, g), rtol=2e-6, atol=2e-6)
+
+
+@pytest.mark.parametrize("shape,out", [
+    ((12288, 384), (12288, 1)),       # RMS row sums
+    ((73728, 192), (73728, 1)),       # softmax-backward row sums
+    ((64, 192, 384), (1, 384)),       # bias gradient
+    ((64, 192, 1536), (1536,)),       # bias gradient, lower rank
+    ((64, 384, 384), (384, 384)),     # weight-gradient batch reduction
+    ((2, 3, 4), (1, 3, 1)),           # non-adjacent
+    ((5, 7, 3), (5, 1, 3)),           # middle
+    ((3, 1, 5), (1, 1, 1)),
+    ((8_000_000,), (1,)),             # full reduction, split + second pass
+    ((6, 5, 4, 3), (6, 1, 4, 1)),     # generic interleaving
+])
+def test_reduce_sum(dev, shape, out):
+    r = rng(3)
+    x = r.standard_normal(shape).astype(np.float32)
+    got = dev.reduce("sum", x, out)
+    want = ops.sum_to_shape(x, out)
+    # fp32 accumulation of n terms: bound by sum |x| (not by the result)
+    scale = ops.sum_to_shape(np.abs(x), out).max()
+    close(got, want, rtol=0, atol=1e-6 * scale + 1e-6)
+
+
+@pytest.mark.parametrize("shape,out", [((2, 3), (2, 1)), ((64, 6, 192, 192), (64, 6, 192, 1)),
+                                        ((9, 33), (1, 33)), ((4, 5, 6), (4, 1, 6))])
+def test_reduce_max(dev, shape, out):
+    x = rng(4).standard_normal(shape).astype(np.float32)
+    np.testing.assert_array_equal(dev.reduce("max", x, out),
+                                  ops.max_to_shape(x, out).astype(np.float32))
+
+
+@pytest.mark.parametrize("n,pos", [(1, 0), (5000, 4097), (1 << 22, 3_000_001), (777, 776)])
+def test_argmax_bit_exact(dev, n, pos):
+    x = rng(5).standard_normal(n).astype(np.float32)
+    x[pos] = 50.0
+    assert dev.argmax(x) == ops.argmax(x) == pos
+    # ties take the lowest index; NaN and -inf never win
+    y = np.full(n + 3, -np.inf, np.float32)
+    y[1] = np.nan
+    y[-1] = 2.0
+    y[-2] = 2.0
+    assert dev.argmax(y) == ops.argmax(y) == n + 1
+    assert dev.argmax(np.full(4, -np.inf, np.float32)) == 0
+
+
+@pytest.mark.parametrize("shape,dims", [
+    ((64, 192, 384), (-2, -1)), ((384, 2048), (-2, -1)), ((64, 192, 6, 64), (1, 2)),
+    ((64, 6, 192, 64), (1, 2)), ((64, 6, 192, 64), (-2, -1)), ((3, 5, 7, 9), (0, 2)),
+    ((33, 65), (0, 1)), ((2, 1, 3), (0, 1)),
+])
+def test_transpose_bit_exact(dev, shape, dims):
+    x = rng(6).standard_normal(shape).astype(np.float32)
+    np.testing.assert_array_equal(dev.transpose(x, *dims), np.swapaxes(x, *dims))
+
+
+@pytest.mark.parametrize("rows,cols", [(73728, 192), (12288, 2048), (3, 1), (5, 37), (2, 5000)])
+def test_softmax_and_backward(dev, rows, cols):
+    r = rng(7)
+    x = (r.standard_normal((rows, cols)) * 4).astype(np.float32)
+    close(dev.rows("softmax", x), ops.softmax_rows(x), rtol=1e-5, atol=1e-7)
+    y = ops.softmax_rows(x).astype(np.float32)
+    g = r.standard_normal((rows, cols)).astype(np.float32)
+    close(dev.rows("softmax_bwd", g, y), ops.softmax_backward(g, y), rtol=1e-5, atol=1e-6)
+
+
+def test_softmax_masked_rows(dev):
+    x = np.array([[0.0, -np.inf, -np.inf], [1000, 1001, -np.inf]], np.float32)
+    close(dev.rows("softmax", x), ops.softmax_rows(x), atol=1e-7)
+
+
+@pytest.mark.parametrize("rows,cols", [(12288, 384), (12288, 1536), (7, 5), (1, 768)])
+def test_rms_family(dev, rows, cols):
+    r = rng(8)
+    x = r.standard_normal((rows, cols)).astype(np.float32)
+    close(dev.rows("rms", x), ops.rms(x), rtol=1e-5)
+    close(dev.rows("rmsnorm", x), ops.rmsnorm(x), rtol=1e-5, atol=1e-6)
+    y = ops.rmsnorm(x).astype(np.float32)
+    g = r.standard_normal((rows, cols)).astype(np.float32)
+    close(dev.rows("rmsnorm_bwd", g, x, y), ops.rmsnorm_backward(g, x, y), rtol=1e-5, atol=2e-6)
+
+
+@pytest.mark.parametrize("rows,vocab", [(12288, 2048), (4, 3), (9, 1001)])
+def test_cross_entropy(dev, rows, vocab):
+    r = rng(9)
+    z = (r.standard_normal((rows, vocab)) * 3).astype(np.float32)
+    t = r.integers(0, vocab, rows).astype(np.uint32)
+    t[0] = vocab + 5  # out of range -> +inf row
+    close(dev.xent(z, t)[1:], ops.cross_entropy(z, t)[1:], rtol=1e-5)
+    assert np.isposinf(dev.xent(z, t)[0, 0])
+    scale = r.uniform(0.1, 2.0, rows).astype(np.float32)
+    got = dev.xent(z, t, backward=True, row_scale=scale)
+    want = ops.cross_entropy_derivative(z, t, row_scale=scale)
+    assert np.all(np.isposinf(got[0]))
+    close(got[1:], want[1:], rtol=1e-5, atol=1e-7)
+    close(dev.xent(z, t, backward=True)[1:], ops.cross_entropy_derivative(z, t)[1:],
+          rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("n_rows,dim,n_ids", [(2048, 384, 12288), (192, 384, 12288), (4, 3, 4),
+                                               (50, 7, 100)])
+def test_embedding_gather_scatter(dev, n_rows, dim, n_ids):
+    r = rng(10)
+    w = r.standard_normal((n_rows, dim)).astype(np.float32)
+    p = 1.0 / np.arange(1, n_rows + 1) ** 1.1
+    ids = r.choice(n_rows, n_ids, p=p / p.sum()).astype(np.uint32)  # Zipf-like hot rows
+    np.testing.assert_array_equal(dev.gather(w, ids), w[ids])
+    v = r.standard_normal((n_ids, dim)).astype(np.float32)
+    want = ops.scatter_add(v, ids, n_rows)
+    scale = ops.scatter_add(np.abs(v), ids, n_rows).max()
+    close(dev.scatter(v, ids, n_rows), want, rtol=0, atol=2e-6 * scale)
+    base = r.standard_normal((n_rows, dim)).astype(np.float32)
+    close(dev.scatter(v, ids, n_rows, base), ops.scatter_add(v, ids, n_rows, base), rtol=0,
+          atol=2e-6 * (scale + 4))
+    # deterministic: same bits every run
+    np.testing.assert_array_equal(dev.scatter(v, ids, n_rows), dev.scatter(v, ids, n_rows))
+
+
+def test_embedding_ids_out_of_range_flag(dev):
+    from templit_b200 import capi
+    dev.status()  # clear
+    w = np.ones((4, 8), np.float32)
+    out = dev.gather(w, np.array([1, 9, 2], np.uint32))
+    assert np.all(out[1] == 0) and np.all(out[0] == 1)
+    assert dev.status() & capi.TL_FLAG_INDEX_RANGE
+    dev.scatter(np.ones((2, 8), np.float32), np.array([0, 7], np.uint32), 4)
+    assert dev.status() & capi.TL_FLAG_INDEX_RANGE
+    assert dev.status() == 0
+
+
+def test_multi_tensor_clip_adamw_matches_per_tensor(dev):
+    """tl_multi_clip_adamw == norm + clip + AdamW per tensor (compile.h:236-258)."""
+    import ctypes
+    from templit_b200 import capi
+    r = rng(11)
+    sizes = [384 * 384, 384, 1, 8191, 8193, 2048 * 384, 5]
+    lr, b1v, b2v, eps, wd, clip = 3e-4, 0.9, 0.95, 1e-8, 0.1, 1.0
+    ps = [r.standard_normal(s).astype(np.float32) * 0.02 for s in sizes]
+    gs = [r.standard_normal(s).astype(np.float32) * 0.05 for s in sizes]
+    m1s = [r.standard_normal(s).astype(np.float32) * 1e-3 for s in sizes]
+    m2s = [np.abs(r.standard_normal(s)).astype(np.float32) * 1e-4 for s in sizes]
+    steps = [3] * len(sizes)
+    n2 = ops.grad_sqnorm(gs)
+    want = [ops.adamw(p, ops.clip(g, n2, clip), m1, m2, lr, b1v, b2v, eps, wd, st)
+            for p, g, m1, m2, st in zip(ps, gs, m1s, m2s, steps)]
+    tp = [dev.t(x) for x in ps]
+    tg = [dev.t(x) for x in gs]
+    t1 = [dev.t(x) for x in m1s]
+    t2 = [dev.t(x) for x in m2s]
+    slots = (capi.TlParamSlot * len(sizes))()
+    chunk = 0
+    for i, s in enumerate(sizes):
+        slots[i].param = tp[i].data_ptr()
+        slots[i].out = tp[i].data_ptr()
+        slots[i].grad = tg[i].data_ptr()
+        slots[i].m1 = t1[i].data_ptr()
+        slots[i].m2 = t2[i].data_ptr()
+        slots[i].count = s
+        slots[i].chunk0 = chunk
+        slots[i].step = steps[i]
+        chunk += (s + capi.TL_OPT_CHUNK - 1) // capi.TL_OPT_CHUNK
+    raw = np.frombuffer(bytes(slots), np.uint8)
+    dslots = dev.t(raw, dtype=np.uint8)
+    sq = dev.t([0.0])
+    nb = dev.lib.tl_multi_clip_adamw_workspace_size(chunk)
+    ws = dev.ws(nb)
+    scal = [dev.t([v]) for v in (b1v, b2v, np.float32(1) - np.float32(lr) * np.float32(wd), lr)]
+    dev.call("tl_multi_clip_adamw", dev.p(dslots), len(sizes), chunk, dev.p(sq), ctypes.c_float(clip),
+             *[dev.p(s) for s in scal], ctypes.c_float(eps), dev.p(ws), nb, dev.stream)
+    assert abs(float(dev.host(sq)[0]) - n2) <= 1e-5 * n2
+    for i in range(len(sizes)):
+        close(dev.host(tp[i]), want[i][0], rtol=1e-5, atol=1e-7)
+        close(dev.host(t1[i]), want[i][1], rtol=1e-5, atol=1e-9)
+        close(dev.host(t2[i]), want[i][2], rtol=1e-5, atol=1e-12)
+        close(dev.host(tg[i]), ops.clip(gs[i], n2, clip), rtol=1e-6, atol=1e-9)
