@@ -37,6 +37,7 @@ typedef struct tlg_config {
   uint32_t world;        /* data-parallel ranks sharing the global batch       */
   int32_t fusion;        /* runtime program fusion on/off                      */
   int32_t graphs;        /* CUDA-graph replay on/off                           */
+  int32_t gemm_precision; /* TL_GEMM_TF32 (0, tensor cores) or TL_GEMM_FP32 (1) */
 } tlg_config;
 
 const char *tlg_last_error(void);
@@ -62,6 +63,18 @@ int tlg_nccl_unique_id(uint8_t id[128]);
 int tlg_set_communicator(void *handle, const uint8_t id[128], int nranks, int rank);
 /* Per-op device timing of the next `steps` train steps, written as JSON. */
 int tlg_profile(void *handle, const char *path, int steps);
+
+/* Configuration 1: the MLP loss sqe(linear(sigmoid(linear(X, W1, b1)), W2, b2), Y)
+ * compiled by passes::compile with SGD(lr) and trained `steps` iterations
+ * with a constant root gradient, on cuda::Runtime.  X [batch, in],
+ * W1 [in, hidden], b1 [1, hidden], W2 [hidden, out], b2 [1, out],
+ * Y [batch, out] are host arrays; the weights are updated in place,
+ * losses[s] receives the summed loss of step s, *seconds the loop time.
+ * gemm_precision selects TL_GEMM_TF32 (0) or TL_GEMM_FP32 (1). */
+int tlg_mlp_train(const float *X, uint32_t batch, uint32_t in, uint32_t hidden, uint32_t out,
+                  float *W1, float *b1, float *W2, float *b2, const float *Y, float root,
+                  float lr, int steps, int gemm_precision, float *losses, double *seconds);
+const char *tlg_mlp_last_error(void);
 
 #ifdef __cplusplus
 }

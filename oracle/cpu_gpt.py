@@ -1,0 +1,112 @@
+"""ctypes access to the host oracle of the GPT training step
+(oracle/_build/libgpt_cpu.so, built by oracle/cpu_gpt/Makefile): the
+reference's nn::GPT and passes::Compiled on a CPU restatement of every
+runtime op.  TEST INFRASTRUCTURE ONLY: GPT-level parity tests and the
+CPU baseline of bench.py."""
+from __future__ import annotations
+
+import ctypes
+import os
+import time
+from ctypes import POINTER, c_char_p, c_float, c_int, c_uint32, c_uint64, c_void_p
+
+import numpy as np
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build", "libgpt_cpu.so")
+_lib = None
+
+
+def available() -> bool:
+    return os.path.exists(LIB_PATH)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        from templit_b200.capi import TlgConfig
+        _lib = ctypes.CDLL(LIB_PATH)
+        U32P = POINTER(c_uint32)
+        sig = {
+            "tlo_last_error": (c_char_p, []),
+            "tlo_create": (c_int, [POINTER(TlgConfig), POINTER(c_void_p)]),
+            "tlo_destroy": (c_int, [c_void_p]),
+            "tlo_set_batch": (c_int, [c_void_p, U32P, U32P]),
+            "tlo_train_step": (c_int, [c_void_p, POINTER(c_float)]),
+            "tlo_forward": (c_int, [c_void_p, POINTER(c_float)]),
+            "tlo_param_count": (c_int, [c_void_p, POINTER(c_uint64), POINTER(c_uint32)]),
+            "tlo_get_params": (c_int, [c_void_p, POINTER(c_float), c_uint64]),
+            "tlo_set_params": (c_int, [c_void_p, POINTER(c_float), c_uint64]),
+        }
+        for name, (res, args) in sig.items():
+            f = getattr(_lib, name)
+            f.restype, f.argtypes = res, args
+    return _lib
+
+
+def _check(rc):
+    if rc:
+        raise RuntimeError(lib().tlo_last_error().decode())
+
+
+class OracleGPT:
+    """The reference GPT (family 4) on the host oracle runtime."""
+
+    def __init__(self, cfg):
+        self.h = c_void_p()
+        _check(lib().tlo_create(ctypes.byref(cfg), ctypes.byref(self.h)))
+        self.n = cfg.batch * cfg.seq
+
+    def set_batch(self, x, y):
+        x = np.ascontiguousarray(x, np.uint32).ravel()
+        y = np.ascontiguousarray(y, np.uint32).ravel()
+        u = POINTER(c_uint32)
+        _check(lib().tlo_set_batch(self.h, x.ctypes.data_as(u), y.ctypes.data_as(u)))
+
+    def train_step(self):
+        v = c_float()
+        _check(lib().tlo_train_step(self.h, ctypes.byref(v)))
+        return v.value
+
+    def forward(self):
+        out = np.zeros(self.n, np.float32)
+        _check(lib().tlo_forward(self.h, out.ctypes.data_as(POINTER(c_float))))
+        return out
+
+    def params(self):
+        n, t = c_uint64(), c_uint32()
+        _check(lib().tlo_param_count(self.h, ctypes.byref(n), ctypes.byref(t)))
+        out = np.zeros(n.value, np.float32)
+        _check(lib().tlo_get_params(self.h, out.ctypes.data_as(POINTER(c_float)), n.value))
+        return out
+
+    def set_params(self, p):
+        p = np.ascontiguousarray(p, np.float32)
+        _check(lib().tlo_set_params(self.h, p.ctypes.data_as(POINTER(c_float)), p.size))
+
+    def close(self):
+        if self.h:
+            lib().tlo_destroy(self.h)
+            self.h = c_void_p()
+
+
+def train_tokens_per_s(batch, seq, steps, threads):
+    """Times `steps` GPT d384 training steps on the host oracle (all
+    `threads` OpenMP threads); returns (tokens/s, seconds)."""
+    from templit_b200.capi import TlgConfig
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    cfg = TlgConfig(family=4, batch=batch, seq=seq, seed=1234, init_std=0.02, lr=3e-4,
+                    beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, clip=1.0, world=1,
+                    fusion=0, graphs=0, gemm_precision=1)
+    rng = np.random.default_rng(7)
+    g = OracleGPT(cfg)
+    try:
+        x = rng.integers(0, 2048, (batch, seq))
+        y = rng.integers(0, 2048, (batch, seq))
+        g.set_batch(x, y)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            g.train_step()
+        secs = time.perf_counter() - t0
+    finally:
+        g.close()
+    return batch * seq * steps / secs, secs

@@ -1,0 +1,95 @@
+// TEST INFRASTRUCTURE: the GPT training step of include/templit_gpt.h on the
+// host oracle runtime (host_runtime.h): the reference's nn::GPT and
+// passes::Compiled executor with every runtime op restated on the CPU.
+// Exposed as tlo_* (oracle) so it can never be mistaken for the product.
+#include "host_runtime.h"
+
+#include "gpt_driver.h"
+
+#include <chrono>
+#include <cstring>
+#include <memory>
+#include <string>
+
+namespace {
+
+using Mat = cpu_ref::Mat;
+using GPT4 = nn::GPT<Mat, 2048, 192, 384, 6>;
+thread_local std::string g_error;
+
+struct Handle {
+  cpu_ref::Runtime runtime;
+  std::unique_ptr<templit_b200::DriverBase> driver;
+};
+
+template <typename F> int guarded(F &&f) {
+  try {
+    f();
+    return 0;
+  } catch (const std::exception &e) {
+    g_error = e.what();
+  }
+  return 1;
+}
+
+}  // namespace
+
+static_assert(passes::Runnable<Mat, cpu_ref::Runtime>);
+
+extern "C" {
+
+const char *tlo_last_error(void) { return g_error.c_str(); }
+
+int tlo_create(const tlg_config *c, void **handle) {
+  return guarded([&] {
+    if (c->family != 4) throw std::invalid_argument("oracle GPT supports family 4");
+    auto h = std::make_unique<Handle>();
+    h->driver = std::make_unique<templit_b200::GptDriver<Mat, cpu_ref::Runtime, GPT4>>(*c, h->runtime);
+    *handle = h.release();
+  });
+}
+
+int tlo_destroy(void *h) {
+  return guarded([&] { delete static_cast<Handle *>(h); });
+}
+
+int tlo_set_batch(void *h, const uint32_t *x, const uint32_t *y) {
+  return guarded([&] { static_cast<Handle *>(h)->driver->set_batch(x, y); });
+}
+
+int tlo_train_step(void *h, float *mean_loss) {
+  return guarded([&] {
+    const float l = static_cast<Handle *>(h)->driver->train_step();
+    if (mean_loss) *mean_loss = l;
+  });
+}
+
+int tlo_forward(void *h, float *losses) {
+  return guarded([&] { static_cast<Handle *>(h)->driver->forward(losses); });
+}
+
+int tlo_param_count(void *h, uint64_t *count, uint32_t *tensors) {
+  return guarded([&] {
+    std::vector<float> all;
+    uint32_t t = 0;
+    static_cast<Handle *>(h)->driver->params(all, t);
+    *count = all.size();
+    if (tensors) *tensors = t;
+  });
+}
+
+int tlo_get_params(void *h, float *out, uint64_t count) {
+  return guarded([&] {
+    std::vector<float> all;
+    uint32_t t = 0;
+    static_cast<Handle *>(h)->driver->params(all, t);
+    if (all.size() != count) throw std::invalid_argument("parameter count mismatch");
+    std::memcpy(out, all.data(), count * sizeof(float));
+  });
+}
+
+int tlo_set_params(void *h, const float *in, uint64_t count) {
+  return guarded([&] { static_cast<Handle *>(h)->driver->set_params(in, count); });
+}
+
+}  // extern "C"

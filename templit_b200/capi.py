@@ -52,7 +52,8 @@ class TlgConfig(Structure):
                 ("seed", c_uint32), ("init_std", c_float), ("lr", c_float),
                 ("beta1", c_float), ("beta2", c_float), ("eps", c_float),
                 ("weight_decay", c_float), ("clip", c_float),
-                ("world", c_uint32), ("fusion", c_int32), ("graphs", c_int32)]
+                ("world", c_uint32), ("fusion", c_int32), ("graphs", c_int32),
+                ("gemm_precision", c_int32)]
 
 
 U32P = POINTER(c_uint32)
@@ -140,6 +141,11 @@ GPT_ABI = {
     "tlg_nccl_unique_id": (c_int, [POINTER(c_uint8)]),
     "tlg_set_communicator": (c_int, [c_void_p, POINTER(c_uint8), c_int, c_int]),
     "tlg_profile": (c_int, [c_void_p, c_char_p, c_int]),
+    "tlg_mlp_train": (c_int, [POINTER(c_float), c_uint32, c_uint32, c_uint32, c_uint32,
+                              POINTER(c_float), POINTER(c_float), POINTER(c_float),
+                              POINTER(c_float), POINTER(c_float), c_float, c_float, c_int,
+                              c_int, POINTER(c_float), POINTER(ctypes.c_double)]),
+    "tlg_mlp_last_error": (c_char_p, []),
 }
 
 _libs: dict[str, ctypes.CDLL] = {}

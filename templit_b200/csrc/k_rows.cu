@@ -18,11 +18,14 @@ namespace {
 
 constexpr int kWarpsPerBlock = 8;
 
+// Adds one term to a running (max, sum of exp(x - max)).  A -inf term (a
+// masked score) contributes nothing, also while the running max is still
+// -inf; a NaN term poisons the sum as it does in the reference kernel.
 __device__ __forceinline__ void online_add(float &m, float &s, float x) {
   if (x > m) {
     s = s * expf(m - x) + 1.0f;
     m = x;
-  } else {
+  } else if (x != -INFINITY) {
     s += expf(x - m);
   }
 }

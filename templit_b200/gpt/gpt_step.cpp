@@ -69,6 +69,7 @@ int tlg_create(const tlg_config *config, void **handle) {
     h->runtime = std::make_unique<cuda::Runtime>();
     h->runtime->set_fusion(config->fusion != 0);
     h->runtime->set_graphs(config->graphs != 0);
+    h->runtime->set_gemm_precision(config->gemm_precision);
     h->driver = make_driver(*config, *h->runtime);
     *handle = h.release();
   });

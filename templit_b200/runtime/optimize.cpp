@@ -5,8 +5,12 @@
 // short op sequences.  Because the runtime records a whole window before it
 // launches anything, it can see those sequences and replace them with one
 // kernel, provided every value another op (or the host, after wait()) can
-// still observe comes out identical.  Intermediates are only skipped when
-// their storage is released inside the window and nothing else reads them.
+// still observe comes out identical.  An intermediate is only skipped when
+// its storage is released inside the window (an executor-local temporary:
+// the transposed operand and product of a mult derivative, the reduced
+// tensors of the softmax / RMSNorm derivative rules) and no op reads it in
+// between.  Buffers are identified by allocation id, never by address, so
+// memory reused after a release is never confused with the value released.
 #include "optimize.h"
 
 #include <algorithm>
@@ -15,6 +19,363 @@
 
 namespace cuda::internal {
 namespace {
+
+constexpr size_t kNone = static_cast<size_t>(-1);
+
+// Allocation ids an op reads / writes.
+struct Access {
+  uint64_t r[10];
+  int nr = 0;
+  uint64_t w[3];
+  int nw = 0;
+  void read(const TRef &t) {
+    if (t.p) r[nr++] = t.id;
+  }
+  void write(const TRef &t) {
+    if (t.p) w[nw++] = t.id;
+  }
+};
+
+Access access(const Op &op) {
+  Access a;
+  const auto &t = op.t;
+  switch (op.kind) {
+    case Kind::Binary: a.read(t[0]); a.read(t[1]); a.write(t[2]); break;
+    case Kind::Scalar: case Kind::Unary: case Kind::Copy: case Kind::Reduce: case Kind::Argmax:
+    case Kind::Transpose: case Kind::Softmax: case Kind::Rms: case Kind::RmsNorm:
+      a.read(t[0]); a.write(t[1]); break;
+    case Kind::Xent: a.read(t[0]); a.read(t[1]); a.write(t[2]); break;
+    case Kind::XentBwd: a.read(t[0]); a.read(t[1]); a.read(t[3]); a.write(t[2]); break;
+    case Kind::Gather: a.read(t[0]); a.read(t[1]); a.write(t[2]); break;
+    case Kind::Scatter: a.read(t[0]); a.read(t[1]); a.read(t[2]); a.write(t[3]); break;
+    case Kind::SqNorm: a.read(t[0]); a.read(t[1]); a.write(t[1]); break;
+    case Kind::Clip: a.read(t[0]); a.read(t[1]); a.write(t[2]); break;
+    case Kind::AdamW:
+      for (int i : {0, 1, 3, 4, 5, 6, 7, 8}) a.read(t[i]);
+      a.write(t[2]); a.write(t[3]); a.write(t[4]); break;
+    case Kind::Gemm:
+      a.read(t[0]); a.read(t[1]); a.read(t[3]);
+      if (op.gemm.beta != 0.0f) a.read(t[2]);
+      a.write(t[2]); a.write(t[4]); break;
+    case Kind::HostWrite: case Kind::Fill: a.write(t[0]); break;
+    case Kind::DevCopy: a.read(t[1]); a.write(t[0]); break;
+    case Kind::GeluBwd: a.read(t[0]); a.read(t[1]); a.write(t[2]); break;
+    case Kind::SoftmaxBwd: a.read(t[0]); a.read(t[1]); a.write(t[2]); break;
+    case Kind::RmsNormBwd: a.read(t[0]); a.read(t[1]); a.read(t[2]); a.write(t[3]); break;
+    default: break;  // Release, MultiAdamW, AllReduce: handled by their passes
+  }
+  return a;
+}
+
+bool reads(const Access &a, uint64_t id) {
+  for (int i = 0; i < a.nr; ++i)
+    if (a.r[i] == id) return true;
+  return false;
+}
+bool writes(const Access &a, uint64_t id) {
+  for (int i = 0; i < a.nw; ++i)
+    if (a.w[i] == id) return true;
+  return false;
+}
+
+// Next live op after i (skipping dead ops and releases), or kNone.
+size_t next_op(const std::vector<Op> &p, size_t i) {
+  for (size_t j = i + 1; j < p.size(); ++j)
+    if (!p[j].dead && p[j].kind != Kind::Release) return j;
+  return kNone;
+}
+
+// True when the value in allocation `id` is never read after op `after`
+// (exclusive) before the allocation is released inside the program, except
+// by the ops listed in `allowed`.  A write that fully replaces the value
+// also ends its life.
+bool dead_after(const std::vector<Op> &p, size_t after, uint64_t id,
+                std::initializer_list<size_t> allowed = {}) {
+  for (size_t j = after + 1; j < p.size(); ++j) {
+    const Op &op = p[j];
+    if (op.dead) continue;
+    if (op.kind == Kind::Release) {
+      if (op.t[0].id == id) return true;
+      continue;
+    }
+    if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce) {
+      for (const auto &s : op.multi)
+        if (s.grad.id == id || s.param.id == id || s.m1.id == id || s.m2.id == id) return false;
+      continue;
+    }
+    bool ok = false;
+    for (size_t k : allowed)
+      if (k == j) ok = true;
+    const Access a = access(op);
+    if (reads(a, id) && !ok) return false;
+    if (writes(a, id) && !reads(a, id)) return true;
+  }
+  return false;  // alive at the end of the program: observable
+}
+
+bool is_last_two(const Op &tr) {
+  const int r = tr.t[0].rank;
+  return r >= 2 && tr.i0 == r - 2 && tr.i1 == r - 1;
+}
+
+bool same(const TRef &a, const TRef &b) { return a.p && a.id == b.id; }
+
+// ------------------------------------------------------------------- GEMM
+// transpose(X -> T); mult(T, G -> P); sum_to_shape(P -> D) with T, P released:
+// the weight gradient of EXPR_MULT_RHS_DERIVATIVE (execute.h:210-232) as
+// one TN product D = X^T G with K = every batch row.  X and G must be dense
+// batched operands of the same batch shape.
+uint64_t fuse_weight_gradient(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t i = 0; i < p.size(); ++i) {
+    Op &tr = p[i];
+    if (tr.dead || tr.kind != Kind::Transpose || !is_last_two(tr)) continue;
+    const size_t j = next_op(p, i);
+    if (j == kNone) continue;
+    Op &mm = p[j];
+    if (mm.kind != Kind::Gemm || !same(mm.t[0], tr.t[1]) || mm.gemm.trans_a || mm.gemm.trans_b ||
+        mm.gemm.bias || mm.gemm.gelu_out || mm.gemm.beta != 0.0f || mm.gemm.batch_rank == 0)
+      continue;
+    const size_t k = next_op(p, j);
+    if (k == kNone) continue;
+    Op &rd = p[k];
+    if (rd.kind != Kind::Reduce || rd.code != TL_REDUCE_SUM || !same(rd.t[0], mm.t[2])) continue;
+    const tl_gemm_desc &g = mm.gemm;
+    // output must be exactly one [M, N] matrix (all batch dims summed)
+    if (rd.t[1].numel() != uint64_t(g.m) * g.n || rd.t[1].last() != g.n) continue;
+    // dense, unbroadcast batch operands
+    uint64_t batch = 1;
+    bool dense = true;
+    for (int d = static_cast<int>(g.batch_rank) - 1; d >= 0; --d) {
+      const uint64_t want_a = uint64_t(g.m) * g.k * batch, want_b = uint64_t(g.k) * g.n * batch;
+      if (g.a_batch_stride[d] != want_a || g.b_batch_stride[d] != want_b) dense = false;
+      batch *= g.batch_shape[d];
+    }
+    if (!dense || uint64_t(g.k) * batch > 0x7fffffffull) continue;
+    if (!dead_after(p, j, mm.t[0].id) || !dead_after(p, k, mm.t[2].id)) continue;
+    Op fused = mm;
+    fused.t[0] = tr.t[0];                 // X, stored [batch*K, M]
+    fused.t[2] = rd.t[1];                 // D
+    fused.gemm.a = static_cast<const float *>(tr.t[0].p);
+    fused.gemm.c = rd.t[1].f();
+    fused.gemm.trans_a = 1;
+    fused.gemm.k = static_cast<uint32_t>(g.k * batch);
+    fused.gemm.batch_rank = 0;
+    fused.workspace = 0;
+    tr.dead = true;
+    mm.dead = true;
+    rd = std::move(fused);
+    folded += 2;
+  }
+  return folded;
+}
+
+// transpose(W -> T); mult(.., T ..) with T released after the mult: the
+// operand is read in its stored order instead (EXPR_MULT_LHS/RHS_DERIVATIVE,
+// execute.h:187-232, and expression transposes feeding a product).
+uint64_t fold_transposes(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t i = 0; i < p.size(); ++i) {
+    Op &tr = p[i];
+    if (tr.dead || tr.kind != Kind::Transpose || !is_last_two(tr)) continue;
+    const size_t j = next_op(p, i);
+    if (j == kNone) continue;
+    Op &mm = p[j];
+    if (mm.kind != Kind::Gemm) continue;
+    tl_gemm_desc &g = mm.gemm;
+    const bool as_b = same(mm.t[1], tr.t[1]) && !same(mm.t[0], tr.t[1]) && !g.trans_b;
+    const bool as_a = same(mm.t[0], tr.t[1]) && !same(mm.t[1], tr.t[1]) && !g.trans_a &&
+                      mm.i1 == 0;  // a flattened product's rows are not the source's rows
+    if (!as_a && !as_b) continue;
+    if (!dead_after(p, j, tr.t[1].id)) continue;
+    if (as_b) {
+      mm.t[1] = tr.t[0];
+      g.b = static_cast<const float *>(tr.t[0].p);
+      g.trans_b = 1;
+    } else {
+      mm.t[0] = tr.t[0];
+      g.a = static_cast<const float *>(tr.t[0].p);
+      g.trans_a = 1;
+    }
+    tr.dead = true;
+    ++folded;
+  }
+  return folded;
+}
+
+// mult(X, W -> C); add(C, bias[1,N] -> C) [; GELU(C -> H)]: EXPR_LINEAR
+// (execute.h:241-252) and the FFN activation as one GEMM epilogue.
+uint64_t fuse_gemm_epilogues(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t i = 0; i < p.size(); ++i) {
+    Op &mm = p[i];
+    if (mm.dead || mm.kind != Kind::Gemm || mm.gemm.beta != 0.0f) continue;
+    size_t j = next_op(p, i);
+    if (j == kNone) continue;
+    Op &ad = p[j];
+    if (!mm.gemm.bias && ad.kind == Kind::Binary && ad.code == TL_ADD && same(ad.t[0], mm.t[2]) &&
+        same(ad.t[2], mm.t[2]) && ad.t[2].same_shape(mm.t[2]) && ad.t[1].last() == mm.gemm.n &&
+        ad.t[1].numel() == mm.gemm.n && !same(ad.t[1], mm.t[2])) {
+      mm.t[3] = ad.t[1];
+      mm.gemm.bias = ad.t[1].f();
+      ad.dead = true;
+      ++folded;
+      j = next_op(p, i);
+      if (j == kNone) continue;
+    }
+    Op &ge = p[j];
+    if (!mm.gemm.gelu_out && ge.kind == Kind::Unary && ge.code == TL_GELU &&
+        same(ge.t[0], mm.t[2]) && ge.t[1].numel() == mm.t[2].numel() && !same(ge.t[1], mm.t[2]) &&
+        mm.gemm.batch_rank == 0) {
+      mm.t[4] = ge.t[1];
+      mm.gemm.gelu_out = ge.t[1].f();
+      ge.dead = true;
+      ++folded;
+    }
+  }
+  return folded;
+}
+
+// --------------------------------------------------------- derivative rules
+// SFTMX_DERIVATIVE (execute.h:291-308):
+//   hadamard(g, y -> d); sum(d -> r); sub(g, r -> d); hadamard(y, d -> d)
+uint64_t fuse_softmax_backward(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t i = 0; i < p.size(); ++i) {
+    Op &h1 = p[i];
+    if (h1.dead || h1.kind != Kind::Binary || h1.code != TL_MUL) continue;
+    const TRef g = h1.t[0], y = h1.t[1], d = h1.t[2];
+    if (!g.same_shape(y) || !g.same_shape(d) || same(d, g) || same(d, y)) continue;
+    const size_t j = next_op(p, i);
+    if (j == kNone) continue;
+    Op &sm = p[j];
+    if (sm.kind != Kind::Reduce || sm.code != TL_REDUCE_SUM || !same(sm.t[0], d) ||
+        sm.t[1].rank != d.rank || sm.t[1].last() != 1 ||
+        sm.t[1].numel() * d.last() != d.numel())
+      continue;
+    const TRef r = sm.t[1];
+    const size_t k = next_op(p, j);
+    if (k == kNone) continue;
+    Op &sb = p[k];
+    if (sb.kind != Kind::Binary || sb.code != TL_SUB || !same(sb.t[0], g) || !same(sb.t[1], r) ||
+        !same(sb.t[2], d))
+      continue;
+    const size_t l = next_op(p, k);
+    if (l == kNone) continue;
+    Op &h2 = p[l];
+    if (h2.kind != Kind::Binary || h2.code != TL_MUL || !same(h2.t[0], y) || !same(h2.t[1], d) ||
+        !same(h2.t[2], d))
+      continue;
+    if (!dead_after(p, l, r.id)) continue;
+    Op fused;
+    fused.kind = Kind::SoftmaxBwd;
+    fused.t[0] = g;
+    fused.t[1] = y;
+    fused.t[2] = d;
+    h1.dead = sm.dead = sb.dead = true;
+    h2 = std::move(fused);
+    folded += 3;
+  }
+  return folded;
+}
+
+// RMSN_DERIVATIVE (execute.h:330-356):
+//   RMS(x -> s); hadamard(g, y -> d); sum(d -> m); divide(m, D -> m);
+//   hadamard(y, m -> d); sub(g, d -> d); divide(d, s -> d)
+uint64_t fuse_rmsnorm_backward(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t i = 0; i < p.size(); ++i) {
+    Op &rm = p[i];
+    if (rm.dead || rm.kind != Kind::Rms) continue;
+    const TRef x = rm.t[0], s = rm.t[1];
+    size_t idx[6];
+    size_t c = i;
+    bool ok = true;
+    for (int n = 0; n < 6 && ok; ++n) {
+      c = next_op(p, c);
+      ok = c != kNone;
+      idx[n] = c;
+    }
+    if (!ok) continue;
+    Op &h1 = p[idx[0]], &sm = p[idx[1]], &dv = p[idx[2]], &h2 = p[idx[3]], &sb = p[idx[4]],
+       &dd = p[idx[5]];
+    if (h1.kind != Kind::Binary || h1.code != TL_MUL) continue;
+    const TRef g = h1.t[0], y = h1.t[1], d = h1.t[2];
+    if (!g.same_shape(x) || !y.same_shape(x) || !d.same_shape(x) || same(d, g) || same(d, y) ||
+        same(d, x))
+      continue;
+    if (sm.kind != Kind::Reduce || sm.code != TL_REDUCE_SUM || !same(sm.t[0], d)) continue;
+    const TRef m = sm.t[1];
+    if (m.numel() * x.last() != x.numel() || m.last() != 1) continue;
+    if (dv.kind != Kind::Scalar || dv.code != TL_SCALAR_DIV || !same(dv.t[0], m) ||
+        !same(dv.t[1], m) || dv.f0 != static_cast<float>(x.last()))
+      continue;
+    if (h2.kind != Kind::Binary || h2.code != TL_MUL || !same(h2.t[0], y) || !same(h2.t[1], m) ||
+        !same(h2.t[2], d))
+      continue;
+    if (sb.kind != Kind::Binary || sb.code != TL_SUB || !same(sb.t[0], g) || !same(sb.t[1], d) ||
+        !same(sb.t[2], d))
+      continue;
+    if (dd.kind != Kind::Binary || dd.code != TL_DIV || !same(dd.t[0], d) || !same(dd.t[1], s) ||
+        !same(dd.t[2], d))
+      continue;
+    if (!dead_after(p, idx[5], s.id) || !dead_after(p, idx[5], m.id)) continue;
+    Op fused;
+    fused.kind = Kind::RmsNormBwd;
+    fused.t[0] = g;
+    fused.t[1] = x;
+    fused.t[2] = y;
+    fused.t[3] = d;
+    rm.dead = h1.dead = sm.dead = dv.dead = h2.dead = sb.dead = true;
+    dd = std::move(fused);
+    folded += 6;
+  }
+  return folded;
+}
+
+// cross_entropy_derivative(z, t -> D); hadamard(root[..,1], D -> out) with D
+// released: the loss root gradient applied per row inside the kernel.
+// GELU_derivative(x -> T); hadamard(T, g -> out) (or (g, T)) with T
+// released: the GELU chain rule in one pass.
+uint64_t fuse_pointwise_backward(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t i = 0; i < p.size(); ++i) {
+    Op &a = p[i];
+    if (a.dead) continue;
+    const bool xent = a.kind == Kind::XentBwd && !a.t[3].p;
+    const bool gelu = a.kind == Kind::Unary && a.code == TL_GELU_DERIVATIVE;
+    if (!xent && !gelu) continue;
+    const TRef tmp = xent ? a.t[2] : a.t[1];
+    const size_t j = next_op(p, i);
+    if (j == kNone) continue;
+    Op &h = p[j];
+    if (h.kind != Kind::Binary || h.code != TL_MUL || !h.t[2].same_shape(tmp)) continue;
+    const bool left = same(h.t[1], tmp) && !same(h.t[0], tmp);
+    const bool right = same(h.t[0], tmp) && !same(h.t[1], tmp);
+    if (!left && !right) continue;
+    const TRef other = left ? h.t[0] : h.t[1];
+    if (!dead_after(p, j, tmp.id)) continue;
+    if (xent) {
+      // root gradient [..., 1] against logits [..., V]
+      if (other.rank != tmp.rank || other.last() != 1 ||
+          other.numel() * tmp.last() != tmp.numel())
+        continue;
+      a.t[3] = other;
+      a.t[2] = h.t[2];
+    } else {
+      if (!other.same_shape(tmp)) continue;
+      Op fused;
+      fused.kind = Kind::GeluBwd;
+      fused.t[0] = a.t[0];
+      fused.t[1] = other;
+      fused.t[2] = h.t[2];
+      a = std::move(fused);
+    }
+    h.dead = true;
+    ++folded;
+  }
+  return folded;
+}
 
 bool is_opt(Kind k) {
   return k == Kind::SqNorm || k == Kind::Clip || k == Kind::AdamW;
@@ -134,6 +495,12 @@ void add_gradient_allreduce(std::vector<Op> &prog) {
 
 uint64_t optimize(std::vector<Op> &prog, void *comm) {
   uint64_t folded = 0;
+  folded += fuse_weight_gradient(prog);
+  folded += fold_transposes(prog);
+  folded += fuse_gemm_epilogues(prog);
+  folded += fuse_softmax_backward(prog);
+  folded += fuse_rmsnorm_backward(prog);
+  folded += fuse_pointwise_backward(prog);
   folded += fuse_step(prog);
   if (comm) add_gradient_allreduce(prog);
   return folded;

@@ -729,6 +729,13 @@ void Runtime::mult(const Mat &a, const Mat &b, Mat &output) {
   }
   if (bshape.size() > TL_GEMM_MAX_BATCH_RANK)
     throw std::invalid_argument("matmul batch rank exceeds the CUDA runtime limit");
+  // A batch of row-blocks against one shared B (activations x weights,
+  // e.g. [64,192,384] x [384,384]) is a single product with M * batch rows.
+  if (bshape.size() == 1 && sb[0] == 0 && sa[0] == amat && sc[0] == cmat) {
+    g.m *= bshape[0];
+    bshape.clear();
+    op.i1 = 1;  // flattened: A's rows run across the batch
+  }
   g.batch_rank = static_cast<uint32_t>(bshape.size());
   for (size_t i = 0; i < bshape.size(); ++i) {
     g.batch_shape[i] = bshape[i];
