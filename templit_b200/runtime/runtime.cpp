@@ -104,7 +104,9 @@ struct Runtime::Impl : internal::Recorder {
     uint64_t last_use = 0;
   };
   std::unordered_map<std::string, Cached> graph_cache;
-  std::string last_signature;
+  // programs seen once (forward, backward and step windows alternate, so a
+  // program recurs every few windows); captured on the second sighting
+  std::unordered_map<std::string, uint64_t> seen_once;
   uint64_t use_clock = 0;
 
   // profiling
@@ -163,7 +165,7 @@ struct Runtime::Impl : internal::Recorder {
   void release_resources() noexcept {
     for (auto &kv : graph_cache) tl_graph_destroy(kv.second.exec);
     graph_cache.clear();
-    last_signature.clear();
+    seen_once.clear();
     if (workspace.ptr) {
       detail::release(workspace);
       workspace = detail::Block{};
@@ -467,13 +469,15 @@ struct Runtime::Impl : internal::Recorder {
       stats.kernel_launches += it->second.kernels;
       return;
     }
-    if (sig != last_signature) {
+    if (seen_once.find(sig) == seen_once.end()) {
       // first sighting: run eagerly, capture if the same program comes back
-      last_signature = std::move(sig);
+      if (seen_once.size() >= 64) seen_once.clear();
+      seen_once.emplace(std::move(sig), ++use_clock);
       run_ops(s);
       stats.kernel_launches += tl_kernel_launches() - k0;
       return;
     }
+    seen_once.erase(sig);
     check(tl_graph_capture_begin(s), "graph capture");
     try {
       run_ops(s);
@@ -494,7 +498,7 @@ struct Runtime::Impl : internal::Recorder {
       tl_graph_destroy(victim->second.exec);
       graph_cache.erase(victim);
     }
-    graph_cache[last_signature] = Cached{exec, kernels, ++use_clock};
+    graph_cache[std::move(sig)] = Cached{exec, kernels, ++use_clock};
     ++stats.graph_captures;
     check(tl_graph_launch(exec, s), "graph launch");
     stats.kernel_launches += kernels;

@@ -1,0 +1,309 @@
+// CPU test of the program optimiser (templit_b200/runtime/optimize.cpp):
+// builds recorded programs by hand, in the shapes the typed executor emits
+// them (include/passes/execute.h of JTPuffer/TempLit), and checks which
+// rewrites happen - and that none happens when an intermediate is still
+// observable.  Needs no GPU: nothing is launched.
+#include "optimize.h"
+#include "program.h"
+
+#include <cstdio>
+#include <functional>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+using namespace cuda::internal;
+
+namespace {
+
+struct Failure : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+void require(bool ok, const std::string &what) {
+  if (!ok) throw Failure(what);
+}
+
+uint64_t g_id = 1;
+uintptr_t g_addr = 0x10000;
+
+TRef tensor(std::vector<uint32_t> shape) {
+  TRef t;
+  t.p = reinterpret_cast<void *>(g_addr);
+  g_addr += 0x100000;
+  t.id = g_id++;
+  t.rank = static_cast<uint8_t>(shape.size());
+  for (size_t i = 0; i < shape.size(); ++i) t.shape[i] = shape[i];
+  return t;
+}
+
+Op op(Kind k) {
+  Op o;
+  o.kind = k;
+  return o;
+}
+Op release(const TRef &t) {
+  Op o = op(Kind::Release);
+  o.t[0] = t;
+  return o;
+}
+Op binary(int code, const TRef &a, const TRef &b, const TRef &c) {
+  Op o = op(Kind::Binary);
+  o.code = code;
+  o.t[0] = a;
+  o.t[1] = b;
+  o.t[2] = c;
+  return o;
+}
+Op gemm(const TRef &a, const TRef &b, const TRef &c, uint32_t m, uint32_t n, uint32_t k,
+        uint32_t batch = 0) {
+  Op o = op(Kind::Gemm);
+  o.t[0] = a;
+  o.t[1] = b;
+  o.t[2] = c;
+  o.gemm.a = static_cast<const float *>(a.p);
+  o.gemm.b = static_cast<const float *>(b.p);
+  o.gemm.c = c.f();
+  o.gemm.m = m;
+  o.gemm.n = n;
+  o.gemm.k = k;
+  if (batch) {
+    o.gemm.batch_rank = 1;
+    o.gemm.batch_shape[0] = batch;
+    o.gemm.a_batch_stride[0] = uint64_t(m) * k;
+    o.gemm.b_batch_stride[0] = uint64_t(k) * n;
+    o.gemm.c_batch_stride[0] = uint64_t(m) * n;
+  }
+  return o;
+}
+Op transpose(const TRef &a, const TRef &out) {
+  Op o = op(Kind::Transpose);
+  o.t[0] = a;
+  o.t[1] = out;
+  o.i0 = a.rank - 2;
+  o.i1 = a.rank - 1;
+  return o;
+}
+Op reduce(const TRef &a, const TRef &out) {
+  Op o = op(Kind::Reduce);
+  o.code = TL_REDUCE_SUM;
+  o.t[0] = a;
+  o.t[1] = out;
+  return o;
+}
+std::vector<const Op *> live(const std::vector<Op> &p) {
+  std::vector<const Op *> v;
+  for (const Op &o : p)
+    if (!o.dead && o.kind != Kind::Release) v.push_back(&o);
+  return v;
+}
+
+void linear_bias_gelu() {
+  auto x = tensor({12288, 384}), w = tensor({384, 1536}), b = tensor({1, 1536});
+  auto c = tensor({12288, 1536}), h = tensor({12288, 1536});
+  std::vector<Op> p = {gemm(x, w, c, 12288, 1536, 384), binary(TL_ADD, c, b, c)};
+  Op g = op(Kind::Unary);
+  g.code = TL_GELU;
+  g.t[0] = c;
+  g.t[1] = h;
+  p.push_back(g);
+  require(optimize(p, nullptr) == 2, "two ops folded");
+  auto v = live(p);
+  require(v.size() == 1 && v[0]->gemm.bias == b.p && v[0]->gemm.gelu_out == h.p,
+          "bias and GELU in the GEMM epilogue");
+}
+
+void weight_gradient_tn() {
+  auto x = tensor({64, 192, 384}), g = tensor({64, 192, 1536});
+  auto xt = tensor({64, 384, 192}), prod = tensor({64, 384, 1536}), dw = tensor({384, 1536});
+  std::vector<Op> p = {transpose(x, xt), gemm(xt, g, prod, 384, 1536, 192, 64), reduce(prod, dw),
+                       release(prod), release(xt)};
+  require(optimize(p, nullptr) == 2, "transpose and product folded");
+  auto v = live(p);
+  require(v.size() == 1 && v[0]->kind == Kind::Gemm, "one GEMM");
+  const auto &d = v[0]->gemm;
+  require(d.trans_a == 1 && d.k == 64 * 192 && d.m == 384 && d.n == 1536 && d.batch_rank == 0 &&
+              d.a == static_cast<const float *>(x.p) && d.c == dw.f(),
+          "TN product with K = batch * T");
+}
+
+void weight_gradient_observable_product_kept() {
+  auto x = tensor({8, 16, 32}), g = tensor({8, 16, 24});
+  auto xt = tensor({8, 32, 16}), prod = tensor({8, 32, 24}), dw = tensor({32, 24});
+  // the product is never released: it is observable after the program
+  std::vector<Op> p = {transpose(x, xt), gemm(xt, g, prod, 32, 24, 16, 8), reduce(prod, dw),
+                       release(xt)};
+  optimize(p, nullptr);
+  auto v = live(p);
+  require(v.size() == 2 && v[0]->kind == Kind::Gemm && v[0]->gemm.trans_a == 1 &&
+              v[1]->kind == Kind::Reduce,
+          "only the transpose folds; product and reduction stay");
+}
+
+void transpose_into_b() {
+  auto g = tensor({12288, 2048}), w = tensor({384, 2048}), wt = tensor({2048, 384});
+  auto dx = tensor({12288, 384});
+  std::vector<Op> p = {transpose(w, wt), gemm(g, wt, dx, 12288, 384, 2048), release(wt)};
+  require(optimize(p, nullptr) == 1, "folded");
+  auto v = live(p);
+  require(v.size() == 1 && v[0]->gemm.trans_b == 1 && v[0]->gemm.b == static_cast<const float *>(w.p),
+          "NT product on the stored weight");
+}
+
+void transpose_kept_when_read_later() {
+  auto a = tensor({64, 6, 192, 64}), at = tensor({64, 6, 64, 192}), q = tensor({64, 6, 192, 64});
+  auto s = tensor({64, 6, 192, 192});
+  Op mm = gemm(q, at, s, 192, 192, 64, 384);
+  Op later = op(Kind::Copy);
+  later.t[0] = at;
+  later.t[1] = tensor({64, 6, 64, 192});
+  std::vector<Op> p = {transpose(a, at), mm, later};
+  require(optimize(p, nullptr) == 0, "K^T saved for backward: no fold");
+}
+
+void softmax_backward() {
+  auto g = tensor({64, 6, 192, 192}), y = tensor({64, 6, 192, 192}), d = tensor({64, 6, 192, 192});
+  auto r = tensor({64, 6, 192, 1});
+  std::vector<Op> p = {binary(TL_MUL, g, y, d), reduce(d, r), binary(TL_SUB, g, r, d),
+                       binary(TL_MUL, y, d, d), release(r)};
+  require(optimize(p, nullptr) == 3, "softmax derivative fused");
+  auto v = live(p);
+  require(v.size() == 1 && v[0]->kind == Kind::SoftmaxBwd && v[0]->t[2].id == d.id, "one row kernel");
+}
+
+void rmsnorm_backward() {
+  auto x = tensor({64, 192, 384}), g = tensor({64, 192, 384}), y = tensor({64, 192, 384});
+  auto d = tensor({64, 192, 384}), s = tensor({64, 192, 1}), m = tensor({64, 192, 1});
+  Op rms = op(Kind::Rms);
+  rms.t[0] = x;
+  rms.t[1] = s;
+  Op dv = op(Kind::Scalar);
+  dv.code = TL_SCALAR_DIV;
+  dv.t[0] = m;
+  dv.t[1] = m;
+  dv.f0 = 384.0f;
+  std::vector<Op> p = {rms,
+                       binary(TL_MUL, g, y, d),
+                       reduce(d, m),
+                       dv,
+                       binary(TL_MUL, y, m, d),
+                       binary(TL_SUB, g, d, d),
+                       binary(TL_DIV, d, s, d),
+                       release(m),
+                       release(s)};
+  require(optimize(p, nullptr) == 6, "RMSNorm derivative fused");
+  auto v = live(p);
+  require(v.size() == 1 && v[0]->kind == Kind::RmsNormBwd, "one row kernel");
+}
+
+void xent_and_gelu_backward() {
+  auto z = tensor({64, 192, 2048}), t = tensor({64, 192}), dz = tensor({64, 192, 2048});
+  auto root = tensor({64, 192, 1}), out = tensor({64, 192, 2048});
+  Op xb = op(Kind::XentBwd);
+  xb.t[0] = z;
+  xb.t[1] = t;
+  xb.t[2] = dz;
+  auto x = tensor({64, 192, 1536}), gd = tensor({64, 192, 1536}), g = tensor({64, 192, 1536});
+  auto o2 = tensor({64, 192, 1536});
+  Op gdo = op(Kind::Unary);
+  gdo.code = TL_GELU_DERIVATIVE;
+  gdo.t[0] = x;
+  gdo.t[1] = gd;
+  std::vector<Op> p = {xb, binary(TL_MUL, root, dz, out), release(dz),
+                       gdo, binary(TL_MUL, gd, g, o2), release(gd)};
+  require(optimize(p, nullptr) == 2, "both fused");
+  auto v = live(p);
+  require(v.size() == 2 && v[0]->kind == Kind::XentBwd && v[0]->t[3].id == root.id &&
+              v[0]->t[2].id == out.id && v[1]->kind == Kind::GeluBwd && v[1]->t[2].id == o2.id,
+          "row-scaled CE backward and GELU backward");
+}
+
+void reused_address_is_not_confused() {
+  // r is released, then a new allocation lands at the same address: the
+  // optimiser must see two different values.
+  auto g = tensor({8, 16}), y = tensor({8, 16}), d = tensor({8, 16}), r = tensor({8, 1});
+  TRef r2 = r;
+  r2.id = g_id++;  // same address, new allocation
+  Op use = op(Kind::Copy);
+  use.t[0] = r2;
+  use.t[1] = tensor({8, 1});
+  std::vector<Op> p = {binary(TL_MUL, g, y, d), reduce(d, r), binary(TL_SUB, g, r, d),
+                       binary(TL_MUL, y, d, d), release(r), use};
+  require(optimize(p, nullptr) == 3, "fused although the address is reused");
+}
+
+void fused_step() {
+  std::vector<Op> p;
+  auto sq = tensor({1});
+  auto b1 = tensor({1, 1}), b2 = tensor({1, 1}), dc = tensor({1, 1}), lr = tensor({1, 1});
+  std::vector<TRef> ps, gs;
+  for (int i = 0; i < 3; ++i) {
+    ps.push_back(tensor({384, 384}));
+    gs.push_back(tensor({384, 384}));
+  }
+  for (int i = 0; i < 3; ++i) {
+    Op n = op(Kind::SqNorm);
+    n.t[0] = gs[i];
+    n.t[1] = sq;
+    p.push_back(n);
+  }
+  for (int i = 0; i < 3; ++i) {
+    Op c = op(Kind::Clip);
+    c.t[0] = gs[i];
+    c.t[1] = sq;
+    c.t[2] = gs[i];
+    c.f0 = 1.0f;
+    p.push_back(c);
+  }
+  for (int i = 0; i < 3; ++i) {
+    Op a = op(Kind::AdamW);
+    a.t[0] = ps[i];
+    a.t[1] = gs[i];
+    a.t[2] = ps[i];
+    a.t[3] = tensor({384, 384});
+    a.t[4] = tensor({384, 384});
+    a.t[5] = b1;
+    a.t[6] = b2;
+    a.t[7] = dc;
+    a.t[8] = lr;
+    a.f0 = 1e-8f;
+    a.u0 = 7;
+    p.push_back(a);
+  }
+  require(optimize(p, nullptr) == 8, "9 optimiser ops -> 1");
+  auto v = live(p);
+  require(v.size() == 1 && v[0]->kind == Kind::MultiAdamW && v[0]->multi.size() == 3 &&
+              v[0]->f0 == 1.0f && v[0]->multi[0].step == 7,
+          "fused clip + AdamW");
+  add_gradient_allreduce(p);
+  v = live(p);
+  require(v.size() == 2 && v[0]->kind == Kind::AllReduce && v[0]->multi.size() == 3,
+          "data-parallel all-reduce ahead of the optimiser");
+}
+
+}  // namespace
+
+int main() {
+  int failures = 0;
+  const std::vector<std::pair<const char *, void (*)()>> cases = {
+      {"linear_bias_gelu", linear_bias_gelu},
+      {"weight_gradient_tn", weight_gradient_tn},
+      {"weight_gradient_observable_product_kept", weight_gradient_observable_product_kept},
+      {"transpose_into_b", transpose_into_b},
+      {"transpose_kept_when_read_later", transpose_kept_when_read_later},
+      {"softmax_backward", softmax_backward},
+      {"rmsnorm_backward", rmsnorm_backward},
+      {"xent_and_gelu_backward", xent_and_gelu_backward},
+      {"reused_address_is_not_confused", reused_address_is_not_confused},
+      {"fused_step", fused_step},
+  };
+  for (const auto &[name, fn] : cases) {
+    try {
+      fn();
+      std::printf("PASS %s\n", name);
+    } catch (const std::exception &e) {
+      std::printf("FAIL %s: %s\n", name, e.what());
+      ++failures;
+    }
+  }
+  return failures ? 1 : 0;
+}
