@@ -143,6 +143,26 @@ int tl_reduce(int op, const float *x, const uint32_t *x_shape, int x_rank,
 size_t tl_reduce_workspace_size(const uint32_t *x_shape, int x_rank,
                                 const uint32_t *out_shape, int out_rank);
 
+/*
+ * tl_reduce without a workspace argument; it allocates nothing.  No
+ * counterpart in the reference: it exists for callers that cannot allocate
+ * device memory when they reduce - code running while a CUDA stream is
+ * captured into a graph (cudaMalloc is not allowed there), hosts whose
+ * device memory is wholly owned by another allocator (a framework pool or a
+ * fixed arena), and foreign-language callers without a CUDA allocator.
+ * Partial sums go to a 4 MiB array in the library's device memory
+ * (tl_reduce_noalloc_max_workspace() bytes), held by every GPU that loads
+ * the library until the process exits.  A reduction whose
+ * tl_reduce_workspace_size() exceeds that returns TL_ERR_RANGE.  The first
+ * call on each device looks up the array's device address (make it before
+ * any stream capture).  All calls share the array: calls that can overlap
+ * on the GPU (other streams, other host threads) race on it; calls ordered
+ * on one stream do not.
+ */
+int tl_reduce_noalloc(int op, const float *x, const uint32_t *x_shape, int x_rank,
+                      float *out, const uint32_t *out_shape, int out_rank, void *stream);
+size_t tl_reduce_noalloc_max_workspace(void);
+
 /* First index of the maximum of x[0..count) (NaN ignored, 0 if none).
  * Replaces Runtime::argmax (src/my_metal/runtime.cpp:850-918; math.metal:715-777). */
 int tl_argmax(const float *x, size_t count, uint32_t *out_index,

@@ -93,6 +93,9 @@ CUDA_ABI = {
     "tl_reduce": (c_int, [c_int, c_void_p, U32P, c_int, c_void_p, U32P, c_int,
                           c_void_p, c_size_t, c_void_p]),
     "tl_reduce_workspace_size": (c_size_t, [U32P, c_int, U32P, c_int]),
+    "tl_reduce_noalloc": (c_int, [c_int, c_void_p, U32P, c_int, c_void_p, U32P, c_int,
+                                  c_void_p]),
+    "tl_reduce_noalloc_max_workspace": (c_size_t, []),
     "tl_argmax": (c_int, [c_void_p, c_size_t, c_void_p, c_void_p, c_size_t, c_void_p]),
     "tl_argmax_workspace_size": (c_size_t, [c_size_t]),
     "tl_transpose": (c_int, [c_void_p, U32P, c_int, c_int, c_int, c_void_p, c_void_p]),

@@ -439,3 +439,75 @@ int tl_argmax(const float *x, size_t count, uint32_t *out_index, void *workspace
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of tl_reduce (no counterpart in the reference).
+//
+// Some callers cannot allocate device memory at the moment they need a
+// reduction: code running while a CUDA stream is being captured into a graph
+// (where cudaMalloc is not allowed), hosts whose whole device-memory budget
+// is owned by another allocator (a framework's caching pool or a fixed
+// arena, where an extra cudaMalloc would exceed the budget or fragment it),
+// and foreign-language callers that bind this C ABI without binding the
+// CUDA allocator.  tl_reduce_noalloc takes no workspace: the split partial
+// sums live in the file-scope device array below, which every GPU that
+// loads this library holds until the process exits.
+namespace tl {
+namespace {
+
+// 4 MiB of partials: enough for every reduction of the GPT training step
+// (the largest plan, a [12288, 1536] -> [1536] bias gradient, needs 2.4 MiB).
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
+static __device__ __align__(256) unsigned char g_reduce_scratch[kNoAllocScratchBytes];
+
+// Device address of g_reduce_scratch on the current device.  In host code
+// the array's name is only a host-side stand-in, so the address is looked
+// up once per device (with that device current) and cached.
+int noalloc_scratch(void **ptr) {
+  static void *cached[64] = {};
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "tl_reduce_noalloc: cudaGetDevice");
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return fail(TL_ERR_RANGE, "tl_reduce_noalloc: device id above 63");
+  if (!cached[dev]) {
+    void *p = nullptr;
+    rc = check_cuda(cudaGetSymbolAddress(&p, g_reduce_scratch),
+                    "tl_reduce_noalloc: cudaGetSymbolAddress of the scratch array");
+    if (rc) return rc;
+    cached[dev] = p;
+  }
+  *ptr = cached[dev];
+  return TL_OK;
+}
+
+}  // namespace
+}  // namespace tl
+
+extern "C" size_t tl_reduce_noalloc_max_workspace(void) { return tl::kNoAllocScratchBytes; }
+
+extern "C" int tl_reduce_noalloc(int op, const float *x, const uint32_t *x_shape, int x_rank,
+                                 float *out, const uint32_t *out_shape, int out_rank,
+                                 void *stream) {
+  if (op != TL_REDUCE_SUM && op != TL_REDUCE_MAX)
+    return fail(TL_ERR_INVALID, "tl_reduce_noalloc: unknown op");
+  ReducePlan pl;
+  int rc = make_plan(x_shape, x_rank, out_shape, out_rank, pl);
+  if (rc) return rc;
+  if (pl.numel == 0 || pl.out_count == 0) return TL_OK;
+  if (!x || !out) return fail(TL_ERR_INVALID, "tl_reduce_noalloc: null pointer");
+  if (pl.numel > 0xffffffffull)
+    return fail(TL_ERR_RANGE, "tl_reduce_noalloc: more than 2^32-1 elements");
+  if (pl.workspace > kNoAllocScratchBytes)
+    return fail(TL_ERR_RANGE, "tl_reduce_noalloc: this reduction needs " +
+                                  std::to_string(pl.workspace) +
+                                  " bytes of partials, above the built-in 4 MiB scratch; use "
+                                  "tl_reduce with a caller workspace");
+  void *scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  // Partial planes are written in full by the first pass before the second
+  // pass reads them, so the previous call's contents need no clearing.
+  cudaStream_t s = as_stream(stream);
+  return op == TL_REDUCE_SUM ? run_plan<TL_REDUCE_SUM>(pl, x, out, scratch, s)
+                             : run_plan<TL_REDUCE_MAX>(pl, x, out, scratch, s);
+}
