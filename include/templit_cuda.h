@@ -306,8 +306,15 @@ typedef struct tl_gemm_desc {
   uint64_t a_batch_stride[TL_GEMM_MAX_BATCH_RANK];
   uint64_t b_batch_stride[TL_GEMM_MAX_BATCH_RANK];
   uint64_t c_batch_stride[TL_GEMM_MAX_BATCH_RANK];
+  /* Scratch for split-K slices (tl_gemm_workspace_size bytes).  A product
+   * with few output tiles and a long K (a weight gradient) is cut into K
+   * slices summed in order by a second kernel; with a smaller workspace it
+   * runs unsplit, with the same result. */
+  void *workspace;
+  uint64_t workspace_bytes;
 } tl_gemm_desc;
 int tl_gemm(const tl_gemm_desc *desc, void *stream);
+size_t tl_gemm_workspace_size(const tl_gemm_desc *desc);
 
 #ifdef __cplusplus
 }

@@ -44,7 +44,8 @@ class TlGemmDesc(Structure):
                 ("batch_shape", c_uint32 * TL_GEMM_MAX_BATCH_RANK),
                 ("a_batch_stride", c_uint64 * TL_GEMM_MAX_BATCH_RANK),
                 ("b_batch_stride", c_uint64 * TL_GEMM_MAX_BATCH_RANK),
-                ("c_batch_stride", c_uint64 * TL_GEMM_MAX_BATCH_RANK)]
+                ("c_batch_stride", c_uint64 * TL_GEMM_MAX_BATCH_RANK),
+                ("workspace", c_void_p), ("workspace_bytes", c_uint64)]
 
 
 class TlgConfig(Structure):
@@ -127,6 +128,7 @@ CUDA_ABI = {
                                     c_void_p, c_size_t, c_void_p]),
     "tl_multi_clip_adamw_workspace_size": (c_size_t, [c_uint32]),
     "tl_gemm": (c_int, [POINTER(TlGemmDesc), c_void_p]),
+    "tl_gemm_workspace_size": (c_size_t, [POINTER(TlGemmDesc)]),
 }
 
 GPT_ABI = {

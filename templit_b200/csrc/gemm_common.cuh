@@ -55,6 +55,9 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs &g, float *Cb,
 int launch_sgemm(const GemmArgs &g, cudaStream_t s);
 // Returns TL_ERR_UNSUPPORTED when the operands do not meet the tensor-core
 // path's alignment rules; the caller then falls back to launch_sgemm.
-int launch_tc_gemm(const GemmArgs &g, cudaStream_t s);
+// `workspace` holds split-K slices when the plan splits K (see
+// tc_gemm_workspace); with less room the product runs unsplit.
+int launch_tc_gemm(const GemmArgs &g, void *workspace, size_t workspace_bytes, cudaStream_t s);
+size_t tc_gemm_workspace(const GemmArgs &g);
 
 }  // namespace tl

@@ -21,12 +21,7 @@ bool force_fp32_from_env() {
   return v;
 }
 
-}  // namespace
-}  // namespace tl
-
-using namespace tl;
-
-extern "C" int tl_gemm(const tl_gemm_desc *d, void *stream) {
+int to_args(const tl_gemm_desc *d, GemmArgs &g) {
   if (!d) return fail(TL_ERR_INVALID, "tl_gemm: null descriptor");
   if (d->batch_rank > TL_GEMM_MAX_BATCH_RANK)
     return fail(TL_ERR_INVALID, "tl_gemm: batch rank too large");
@@ -34,7 +29,7 @@ extern "C" int tl_gemm(const tl_gemm_desc *d, void *stream) {
     return fail(TL_ERR_INVALID, "tl_gemm: beta must be 0 or 1");
   if (d->precision < TL_GEMM_TF32 || d->precision > TL_GEMM_3XTF32)
     return fail(TL_ERR_INVALID, "tl_gemm: unknown precision");
-  GemmArgs g{};
+  g = GemmArgs{};
   g.a = d->a;
   g.b = d->b;
   g.c = d->c;
@@ -55,16 +50,37 @@ extern "C" int tl_gemm(const tl_gemm_desc *d, void *stream) {
     g.sc[i] = d->c_batch_stride[i];
     g.batch_count *= d->batch_shape[i];
   }
+  return TL_OK;
+}
+
+bool wants_tc(const tl_gemm_desc *d, const GemmArgs &g) {
+  const uint64_t macs = static_cast<uint64_t>(g.m) * g.n * g.k * g.batch_count;
+  return d->precision != TL_GEMM_FP32 && !force_fp32_from_env() && macs >= kTcMinMacs &&
+         g.k > 0;
+}
+
+}  // namespace
+}  // namespace tl
+
+using namespace tl;
+
+extern "C" size_t tl_gemm_workspace_size(const tl_gemm_desc *d) {
+  GemmArgs g;
+  if (to_args(d, g) || g.m == 0 || g.n == 0 || g.batch_count == 0) return 0;
+  return wants_tc(d, g) ? tc_gemm_workspace(g) : 0;
+}
+
+extern "C" int tl_gemm(const tl_gemm_desc *d, void *stream) {
+  GemmArgs g;
+  int rc = to_args(d, g);
+  if (rc) return rc;
   if (g.m == 0 || g.n == 0 || g.batch_count == 0) return TL_OK;
   if (!g.c || (g.k && (!g.a || !g.b))) return fail(TL_ERR_INVALID, "tl_gemm: null pointer");
   cudaStream_t s = as_stream(stream);
-  const uint64_t macs = static_cast<uint64_t>(g.m) * g.n * g.k * g.batch_count;
-  const bool want_tc = d->precision != TL_GEMM_FP32 && !force_fp32_from_env() &&
-                       macs >= kTcMinMacs && g.k > 0;
-  if (want_tc) {
+  if (wants_tc(d, g)) {
     if (d->precision == TL_GEMM_3XTF32)
       return fail(TL_ERR_UNSUPPORTED, "tl_gemm: 3xTF32 is not built in this version");
-    const int rc = launch_tc_gemm(g, s);
+    rc = launch_tc_gemm(g, d->workspace, d->workspace_bytes, s);
     if (rc != TL_ERR_UNSUPPORTED) return rc;
   }
   return launch_sgemm(g, s);

@@ -39,9 +39,14 @@ constexpr uint32_t kFlagTimeout = TL_FLAG_TIMEOUT;
 struct TcArgs {
   GemmArgs g;
   uint32_t mt, nt;        // tiles along M and N
-  uint64_t num_tiles;     // batch * mt * nt
+  uint64_t num_tiles;     // batch * splits * mt * nt
   uint64_t a_mat, b_mat;  // elements per A / B matrix
   uint32_t *status;
+  // split-K: the K range is cut into `splits` slices of kb_per_split k-tiles;
+  // slice s writes its raw fp32 product to partial + s * M * N (batch 1 only)
+  // and a second kernel sums the slices in order and applies the epilogue.
+  uint32_t splits, kb_per_split;
+  float *partial;
 };
 
 template <int BN>
@@ -53,12 +58,23 @@ struct Cfg {
   static constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + 256;
 };
 
+// tile = ((z * splits + s) * nt + nb) * mt + mb: consecutive CTAs take
+// consecutive row blocks of the same column block and K slice, so they
+// share the B tiles in L2.
 __device__ __forceinline__ void decode_tile(const TcArgs &t, uint64_t tile, uint64_t &z,
-                                            uint32_t &mb, uint32_t &nb) {
+                                            uint32_t &s, uint32_t &mb, uint32_t &nb) {
   mb = static_cast<uint32_t>(tile % t.mt);
-  const uint64_t r = tile / t.mt;
+  uint64_t r = tile / t.mt;
   nb = static_cast<uint32_t>(r % t.nt);
-  z = r / t.nt;
+  r /= t.nt;
+  s = static_cast<uint32_t>(r % t.splits);
+  z = r / t.splits;
+}
+
+__device__ __forceinline__ void k_range(const TcArgs &t, uint32_t ktiles, uint32_t s,
+                                        uint32_t &kb0, uint32_t &kb1) {
+  kb0 = s * t.kb_per_split;
+  kb1 = min(ktiles, kb0 + t.kb_per_split);
 }
 
 template <int BN, bool A_MN, bool B_MN>
@@ -119,14 +135,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
       for (uint64_t tile = blockIdx.x; tile < t.num_tiles && !*abort_flag;
            tile += gridDim.x) {
         uint64_t z;
-        uint32_t mb, nb;
-        decode_tile(t, tile, z, mb, nb);
+        uint32_t s, mb, nb, kb0, kb1;
+        decode_tile(t, tile, z, s, mb, nb);
+        k_range(t, ktiles, s, kb0, kb1);
         uint64_t oa, ob, oc;
         batch_offsets(g, z, oa, ob, oc);
         const int32_t za = static_cast<int32_t>(oa / t.a_mat);
         const int32_t zb = static_cast<int32_t>(ob / t.b_mat);
         const int32_t m0 = static_cast<int32_t>(mb * BM), n0 = static_cast<int32_t>(nb * BN);
-        for (uint32_t kb = 0; kb < ktiles; ++kb) {
+        for (uint32_t kb = kb0; kb < kb1; ++kb) {
           if (!ptx::mbar_wait_bounded(&empty[stage], phase ^ 1, kWaitLimitNs)) {
             timeout();
             break;
@@ -187,7 +204,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
-        for (uint32_t kb = 0; kb < ktiles; ++kb) {
+        uint64_t z;
+        uint32_t s, mb, nb, kb0, kb1;
+        decode_tile(t, tile, z, s, mb, nb);
+        k_range(t, ktiles, s, kb0, kb1);
+        for (uint32_t kb = kb0; kb < kb1; ++kb) {
           if (!ptx::mbar_wait_bounded(&full[stage], phase, kWaitLimitNs)) {
             timeout();
             ok = false;
@@ -204,7 +225,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
             const uint64_t bd =
                 B_MN ? ptx::smem_desc(sb + kk * 1024, 4096, 512, ptx::kSwizzle128B32BAtom)
                      : ptx::smem_desc(sb + kk * 32, 16, 1024, ptx::kSwizzle128B);
-            ptx::mma_tf32(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+            ptx::mma_tf32(d_tmem, ad, bd, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
           }
           issued_any = true;
           ptx::mma_commit(&empty[stage]);  // stage reusable once these MMAs finish
@@ -240,16 +261,19 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
       if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
       ptx::tc_fence_after();
       uint64_t z;
-      uint32_t mb, nb;
-      decode_tile(t, tile, z, mb, nb);
+      uint32_t s, mb, nb;
+      decode_tile(t, tile, z, s, mb, nb);
       uint64_t oa, ob, oc;
       batch_offsets(g, z, oa, ob, oc);
-      float *Cb = g.c + oc;
+      // split-K slices store their raw partial product; the epilogue
+      // (bias, accumulate, GELU) runs once in the slice-summing kernel
+      const bool raw = t.partial != nullptr;
+      float *Cb = raw ? t.partial + static_cast<size_t>(s) * g.m * g.n : g.c + oc;
       const uint32_t m = mb * BM + q * 32 + lane;
       const uint32_t n_base = nb * BN;
       const bool row_ok = m < g.m;
-      const bool fast = (g.n % 4) == 0 && aligned16(Cb) && !g.gelu_out && !g.bias &&
-                        g.beta == 0.0f;
+      const bool fast = (g.n % 4) == 0 && aligned16(Cb) &&
+                        (raw || (!g.gelu_out && !g.bias && g.beta == 0.0f));
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -268,7 +292,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const uint32_t n = n0 + j;
-            if (n < g.n) epilogue_store(g, Cb, oc, rowoff + n, n, __uint_as_float(r[j]));
+            if (n >= g.n) continue;
+            if (raw) Cb[rowoff + n] = __uint_as_float(r[j]);
+            else epilogue_store(g, Cb, oc, rowoff + n, n, __uint_as_float(r[j]));
           }
         }
       }
@@ -330,14 +356,59 @@ uint64_t matrices_spanned(const GemmArgs &g, const uint64_t *strides, uint64_t m
   return last / mat + 1;
 }
 
+// Slice sums of a split-K product in slice order, then the epilogue.
+__global__ void __launch_bounds__(256)
+splitk_epilogue_kernel(const float *__restrict__ part, uint32_t splits, GemmArgs g) {
+  const uint64_t mn = static_cast<uint64_t>(g.m) * g.n;
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < mn;
+       i += stride) {
+    float v = part[i];
+    for (uint32_t s = 1; s < splits; ++s) v += part[s * mn + i];
+    epilogue_store(g, g.c, 0, i, static_cast<uint32_t>(i % g.n), v);
+  }
+}
+
+struct TcPlan {
+  int bn;
+  uint32_t splits, kb_per_split;
+  size_t workspace;
+};
+
+TcPlan plan_tc(const GemmArgs &g) {
+  TcPlan p{};
+  p.bn = g.n > 128 ? 256 : (g.n > 64 ? 128 : 64);
+  const uint64_t tiles = g.batch_count * ((g.m + BM - 1) / BM) * ((g.n + p.bn - 1) / p.bn);
+  const uint32_t ktiles = (g.k + BK - 1) / BK;
+  p.splits = 1;
+  p.kb_per_split = ktiles;
+  // Few output tiles but a long K (weight gradients: K = every token of the
+  // batch): cut K so the tiles times slices fill the GPU, keeping at least 8
+  // k-tiles (256 of K) per slice.
+  if (g.batch_count == 1 && tiles < static_cast<uint64_t>(kNumSMs) / 2 && ktiles >= 16) {
+    uint64_t want = (kNumSMs + tiles - 1) / tiles;
+    const uint64_t cap = ktiles / 8;
+    if (want > cap) want = cap;
+    if (want > 1) {
+      p.kb_per_split = static_cast<uint32_t>((ktiles + want - 1) / want);
+      p.splits = (ktiles + p.kb_per_split - 1) / p.kb_per_split;
+      p.workspace = static_cast<size_t>(p.splits) * g.m * g.n * sizeof(float);
+    }
+  }
+  return p;
+}
+
 template <int BN, bool A_MN, bool B_MN>
-int launch_variant(const GemmArgs &g, cudaStream_t s) {
+int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaStream_t s) {
   using C = Cfg<BN>;
   TcArgs t{};
   t.g = g;
   t.mt = (g.m + BM - 1) / BM;
   t.nt = (g.n + BN - 1) / BN;
-  t.num_tiles = g.batch_count * t.mt * t.nt;
+  t.splits = partial ? plan.splits : 1;
+  t.kb_per_split = partial ? plan.kb_per_split : (g.k + BK - 1) / BK;
+  t.partial = partial;
+  t.num_tiles = g.batch_count * t.splits * t.mt * t.nt;
   t.a_mat = static_cast<uint64_t>(g.m) * g.k;
   t.b_mat = static_cast<uint64_t>(g.k) * g.n;
   t.status = device_status_ptr();
@@ -362,32 +433,49 @@ int launch_variant(const GemmArgs &g, cudaStream_t s) {
   }
   const uint64_t grid = t.num_tiles < static_cast<uint64_t>(kNumSMs) ? t.num_tiles : kNumSMs;
   tc_gemm_kernel<BN, A_MN, B_MN><<<static_cast<unsigned>(grid), kThreads, C::SMEM, s>>>(ma, mb, t);
-  return launch_status("tl_gemm tf32");
+  int rc = launch_status("tl_gemm tf32");
+  if (rc || !partial) return rc;
+  const uint64_t mn = static_cast<uint64_t>(g.m) * g.n;
+  splitk_epilogue_kernel<<<grid_for(mn, 256), 256, 0, s>>>(partial, t.splits, g);
+  return launch_status("tl_gemm split-K sum");
 }
 
 template <int BN>
-int launch_bn(const GemmArgs &g, cudaStream_t s) {
+int launch_bn(const GemmArgs &g, const TcPlan &plan, float *partial, cudaStream_t s) {
   const bool a_mn = g.trans_a != 0, b_mn = g.trans_b == 0;
-  if (a_mn && b_mn) return launch_variant<BN, true, true>(g, s);
-  if (a_mn) return launch_variant<BN, true, false>(g, s);
-  if (b_mn) return launch_variant<BN, false, true>(g, s);
-  return launch_variant<BN, false, false>(g, s);
+  if (a_mn && b_mn) return launch_variant<BN, true, true>(g, plan, partial, s);
+  if (a_mn) return launch_variant<BN, true, false>(g, plan, partial, s);
+  if (b_mn) return launch_variant<BN, false, true>(g, plan, partial, s);
+  return launch_variant<BN, false, false>(g, plan, partial, s);
+}
+
+bool tc_supported(const GemmArgs &g) {
+  // TMA rules: 16-byte aligned bases, row strides and matrix strides.
+  const uint32_t a_inner = g.trans_a ? g.m : g.k;
+  const uint32_t b_inner = g.trans_b ? g.k : g.n;
+  if (g.k == 0 || a_inner % 4 || b_inner % 4 || !aligned16(g.a) || !aligned16(g.b)) return false;
+  for (uint32_t d = 0; d < g.batch_rank; ++d)
+    if (g.sa[d] % 4 || g.sb[d] % 4) return false;
+  return g.m <= 0x7fffffffu && g.n <= 0x7fffffffu && g.k <= 0x7fffffffu;
 }
 
 }  // namespace
 
-int launch_tc_gemm(const GemmArgs &g, cudaStream_t s) {
-  // TMA rules: 16-byte aligned bases, row strides and matrix strides.
-  const uint32_t a_inner = g.trans_a ? g.m : g.k;
-  const uint32_t b_inner = g.trans_b ? g.k : g.n;
-  if (g.k == 0 || a_inner % 4 || b_inner % 4 || !aligned16(g.a) || !aligned16(g.b))
-    return TL_ERR_UNSUPPORTED;
-  for (uint32_t d = 0; d < g.batch_rank; ++d)
-    if (g.sa[d] % 4 || g.sb[d] % 4) return TL_ERR_UNSUPPORTED;
-  if (g.m > 0x7fffffffu || g.n > 0x7fffffffu || g.k > 0x7fffffffu) return TL_ERR_UNSUPPORTED;
-  if (g.n > 128) return launch_bn<256>(g, s);
-  if (g.n > 64) return launch_bn<128>(g, s);
-  return launch_bn<64>(g, s);
+size_t tc_gemm_workspace(const GemmArgs &g) {
+  return tc_supported(g) ? plan_tc(g).workspace : 0;
+}
+
+int launch_tc_gemm(const GemmArgs &g, void *workspace, size_t workspace_bytes, cudaStream_t s) {
+  if (!tc_supported(g)) return TL_ERR_UNSUPPORTED;
+  const TcPlan plan = plan_tc(g);
+  // without room for the slices the product runs unsplit (same result)
+  float *partial = plan.splits > 1 && workspace && workspace_bytes >= plan.workspace &&
+                           aligned16(workspace)
+                       ? static_cast<float *>(workspace)
+                       : nullptr;
+  if (plan.bn == 256) return launch_bn<256>(g, plan, partial, s);
+  if (plan.bn == 128) return launch_bn<128>(g, plan, partial, s);
+  return launch_bn<64>(g, plan, partial, s);
 }
 
 }  // namespace tl

@@ -298,9 +298,13 @@ struct Runtime::Impl : internal::Recorder {
                        t[7].f(), t[8].f(), op.f0, op.u0, t[0].numel(), s),
               "adamW");
         break;
-      case Kind::Gemm:
-        check(tl_gemm(&op.gemm, s), "mult");
+      case Kind::Gemm: {
+        tl_gemm_desc d = op.gemm;
+        d.workspace = ws;
+        d.workspace_bytes = wsb;
+        check(tl_gemm(&d, s), "mult");
         break;
+      }
       case Kind::HostWrite:
         check(tl_memcpy_h2d(static_cast<char *>(t[0].p) + op.n, op.host.data(), op.host.size(), s),
               "Storage::write");
@@ -398,35 +402,57 @@ struct Runtime::Impl : internal::Recorder {
     }
   }
 
-  void run_profiled(void *s) {
-    void *e0 = nullptr, *e1 = nullptr;
-    check(tl_event_create(&e0), "profile event");
-    check(tl_event_create(&e1), "profile event");
-    size_t slot_base = 0;
-    for (const Op &op : prog) {
-      if (op.dead || op.kind == Kind::Release) continue;
-      check(tl_event_record(e0, s), "profile event");
-      execute(op, s, slot_base);
-      check(tl_event_record(e1, s), "profile event");
-      float ms = 0.0f;
-      check(tl_event_elapsed_ms(&ms, e0, e1), "profile event");
-      std::string key = internal::kind_name(op.kind);
-      if (op.kind == Kind::Gemm) {
-        key += " " + std::to_string(op.gemm.m) + "x" + std::to_string(op.gemm.n) + "x" +
-               std::to_string(op.gemm.k);
-        uint64_t batch = 1;
-        for (uint32_t i = 0; i < op.gemm.batch_rank; ++i) batch *= op.gemm.batch_shape[i];
-        if (batch > 1) key += " b" + std::to_string(batch);
-        key += op.gemm.trans_a ? " T" : " N";
-        key += op.gemm.trans_b ? "T" : "N";
+  // Per-op device time: one event between consecutive ops, all enqueued
+  // before the first is read, so the GPU runs the program back to back
+  // (an op's time can include host launch latency only when the GPU ran
+  // dry waiting for it).
+  static std::string profile_key(const Op &op) {
+    std::string key = internal::kind_name(op.kind);
+    if (op.kind == Kind::Gemm) {
+      key += " " + std::to_string(op.gemm.m) + "x" + std::to_string(op.gemm.n) + "x" +
+             std::to_string(op.gemm.k);
+      uint64_t batch = 1;
+      for (uint32_t i = 0; i < op.gemm.batch_rank; ++i) batch *= op.gemm.batch_shape[i];
+      if (batch > 1) key += " b" + std::to_string(batch);
+      key += op.gemm.trans_a ? " T" : " N";
+      key += op.gemm.trans_b ? "T" : "N";
+    } else if (op.kind != Kind::MultiAdamW && op.kind != Kind::AllReduce) {
+      // element-wise and row ops: code and the shapes that set the traffic
+      if (op.kind == Kind::Binary || op.kind == Kind::Unary || op.kind == Kind::Scalar ||
+          op.kind == Kind::Reduce)
+        key += "#" + std::to_string(op.code);
+      for (int i = 0; i < 3; ++i) {
+        const TRef &r = op.t[i];
+        if (!r.p || r.rank == 0) continue;
+        key += " [";
+        for (int d = 0; d < r.rank; ++d) key += (d ? "," : "") + std::to_string(r.shape[d]);
+        key += "]";
       }
-      Prof &p = profile[key];
+    }
+    return key;
+  }
+
+  void run_profiled(void *s) {
+    std::vector<const Op *> ops;
+    for (const Op &op : prog)
+      if (!op.dead && op.kind != Kind::Release) ops.push_back(&op);
+    std::vector<void *> ev(ops.size() + 1, nullptr);
+    for (void *&e : ev) check(tl_event_create(&e), "profile event");
+    size_t slot_base = 0;
+    for (size_t i = 0; i < ops.size(); ++i) {
+      check(tl_event_record(ev[i], s), "profile event");
+      execute(*ops[i], s, slot_base);
+      if (ops[i]->kind == Kind::MultiAdamW) slot_base += ops[i]->multi.size();
+    }
+    check(tl_event_record(ev.back(), s), "profile event");
+    for (size_t i = 0; i < ops.size(); ++i) {
+      float ms = 0.0f;
+      check(tl_event_elapsed_ms(&ms, ev[i], ev[i + 1]), "profile event");
+      Prof &p = profile[profile_key(*ops[i])];
       ++p.calls;
       p.ms += ms;
-      if (op.kind == Kind::MultiAdamW) slot_base += op.multi.size();
     }
-    tl_event_destroy(e0);
-    tl_event_destroy(e1);
+    for (void *e : ev) tl_event_destroy(e);
   }
 
   void run_program() {
@@ -435,7 +461,7 @@ struct Runtime::Impl : internal::Recorder {
     uint64_t live = 0;
     for (const Op &op : prog) {
       if (op.dead) continue;
-      ws = std::max(ws, op.workspace);
+      ws = std::max(ws, op.kind == Kind::Gemm ? tl_gemm_workspace_size(&op.gemm) : op.workspace);
       if (op.kind == Kind::MultiAdamW) slots += op.multi.size();
       if (op.kind != Kind::Release) ++live;
     }

@@ -215,5 +215,10 @@ class Dev:
             d.a_batch_stride[i] = sa[i]
             d.b_batch_stride[i] = sb[i]
             d.c_batch_stride[i] = sc[i]
+        nbytes = self.lib.tl_gemm_workspace_size(ctypes.byref(d))
+        ws = self.ws(nbytes) if nbytes else None
+        if ws is not None:
+            d.workspace = ws.data_ptr()
+            d.workspace_bytes = nbytes
         self.call("tl_gemm", ctypes.byref(d), self.stream)
         return (self.host(tc), self.host(tg)) if gelu else self.host(tc)

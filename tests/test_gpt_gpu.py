@@ -143,19 +143,26 @@ def test_deterministic_and_graph_replay_is_bit_exact():
     rng = np.random.default_rng(3)
     x, y = zipf(rng, 4, 64)
     runs = []
-    for graphs, fusion in ((1, 1), (0, 1), (0, 0)):
+    p0 = None
+    for graphs, fusion in ((1, 1), (0, 1), (0, 0), (1, 1)):
         g = CudaGPT(config(4, 64, graphs=graphs, fusion=fusion))
+        if p0 is None:
+            p0 = g.params()
         g.set_batch(x, y)
         losses = [g.train_step() for _ in range(4)]
         runs.append((losses, g.params(), g.stats()))
         g.close()
-    (l1, p1, s1), (l2, p2, s2), (l3, p3, s3) = runs
+    (l1, p1, s1), (l2, p2, s2), (l3, p3, s3), (l4, p4, _) = runs
     assert l1 == l2 and np.array_equal(p1, p2)  # replay == eager, bit for bit
+    assert l1 == l4 and np.array_equal(p1, p4)  # run to run, bit for bit
     assert s1["replays"] > 0 and s1["captures"] > 0
     assert s2["replays"] == 0
     assert s1["fused"] > 0 and s3["fused"] == 0
-    # fused optimiser vs per-tensor launches: same math, different norm order
-    np.testing.assert_allclose(p1, p3, rtol=0, atol=1e-6)
+    # fused kernels vs the unfused program: same math, different rounding
+    # order; the updates agree to 1% in norm (AdamW normalises every update)
+    d1, d3 = p1 - p0, p3 - p0
+    assert np.linalg.norm(d1 - d3) <= 1e-2 * np.linalg.norm(d3)
+    np.testing.assert_allclose(l1, l3, rtol=1e-4)
 
 
 def test_full_size_step_runs():
