@@ -18,6 +18,7 @@
 #include <map>
 #include <mutex>
 #include <unordered_map>
+#include <unordered_set>
 #include <vector>
 
 namespace cuda {
@@ -35,6 +36,9 @@ struct State {
   uint64_t next_id = 1;
   uint64_t window_counter = 0;
   internal::Recorder *recorder = nullptr;
+  // blocks whose value was read outside a recorded program (host reads,
+  // immediate device copies), until released
+  std::unordered_set<uint64_t> observed;
 };
 
 State &state() {
@@ -72,6 +76,7 @@ void ensure_init() {
 Recorder *active_recorder() { return state().recorder; }
 void set_active_recorder(Recorder *r) { state().recorder = r; }
 uint64_t next_window_id() { return ++state().window_counter; }
+bool host_observed(uint64_t id) { return state().observed.count(id) != 0; }
 
 }  // namespace internal
 
@@ -152,6 +157,7 @@ void release(const Block &block) noexcept {
   if (!block.ptr) return;
   State &s = state();
   if (s.recorder) s.recorder->record_release(block);
+  s.observed.erase(block.id);
   s.in_use -= block.bytes;
   s.free_blocks.emplace(block.bytes, block.ptr);
 }
@@ -176,6 +182,7 @@ void write(const Block &dst, size_t offset_bytes, const void *src, size_t bytes)
 
 void read(const Block &src, size_t offset_bytes, void *dst, size_t bytes) {
   if (bytes == 0) return;
+  state().observed.insert(src.id);
   internal::check(tl_memcpy_d2h(dst, static_cast<const char *>(src.ptr) + offset_bytes, bytes,
                                 state().stream),
                   "Storage::read");
@@ -197,6 +204,7 @@ void copy(const Block &dst, const Block &src, size_t bytes) {
     state().recorder->record_copy(dst, src, bytes);
     return;
   }
+  state().observed.insert(src.id);
   internal::check(tl_memcpy_d2d(dst.ptr, src.ptr, bytes, state().stream), "Storage::clone");
 }
 

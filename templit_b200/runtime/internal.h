@@ -29,6 +29,10 @@ struct Recorder {
 Recorder *active_recorder();
 void set_active_recorder(Recorder *r);
 uint64_t next_window_id();
+// True when the block's value has been read outside a recorded program
+// (Storage::read / compare on the host, or an immediate clone) since it
+// was allocated.
+bool host_observed(uint64_t id);
 
 // Throws std::runtime_error with the library's message unless status == TL_OK.
 inline void check(int status, const char *what) {

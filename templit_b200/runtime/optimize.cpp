@@ -18,23 +18,6 @@
 #include <unordered_set>
 
 namespace cuda::internal {
-namespace {
-
-constexpr size_t kNone = static_cast<size_t>(-1);
-
-// Allocation ids an op reads / writes.
-struct Access {
-  uint64_t r[10];
-  int nr = 0;
-  uint64_t w[3];
-  int nw = 0;
-  void read(const TRef &t) {
-    if (t.p) r[nr++] = t.id;
-  }
-  void write(const TRef &t) {
-    if (t.p) w[nw++] = t.id;
-  }
-};
 
 Access access(const Op &op) {
   Access a;
@@ -66,6 +49,23 @@ Access access(const Op &op) {
   }
   return a;
 }
+
+bool full_write(const Op &op) {
+  switch (op.kind) {
+    case Kind::HostWrite: return op.n == 0 && op.host.size() >= op.t[0].numel();
+    case Kind::Fill: return op.n * 4 >= op.t[0].numel();
+    case Kind::DevCopy: return op.n >= op.t[0].numel();
+    case Kind::SqNorm: return false;  // accumulates
+    default: return true;
+  }
+}
+
+namespace {
+
+constexpr size_t kNone = static_cast<size_t>(-1);
+
+// Window liveness of the program being optimised (null: none known).
+thread_local const Liveness *g_live = nullptr;
 
 bool reads(const Access &a, uint64_t id) {
   for (int i = 0; i < a.nr; ++i)
@@ -108,9 +108,10 @@ bool dead_after(const std::vector<Op> &p, size_t after, uint64_t id,
       if (k == j) ok = true;
     const Access a = access(op);
     if (reads(a, id) && !ok) return false;
-    if (writes(a, id) && !reads(a, id)) return true;
+    if (writes(a, id) && !reads(a, id) && full_write(op)) return true;
   }
-  return false;  // alive at the end of the program: observable
+  // alive at the end of the program: observable unless window-local
+  return g_live && g_live->window_local(id);
 }
 
 bool is_last_two(const Op &tr) {
@@ -377,6 +378,94 @@ uint64_t fuse_pointwise_backward(std::vector<Op> &p) {
   return folded;
 }
 
+// --------------------------------------------------------- copy forwarding
+bool elementwise(Kind k) {
+  return k == Kind::Binary || k == Kind::Scalar || k == Kind::Unary || k == Kind::Copy ||
+         k == Kind::GeluBwd;
+}
+
+// Points every read of allocation `from` in `op` at `to` (same element
+// count; the op keeps its own view of the shape).
+void retarget_reads(Op &op, const TRef &from, const TRef &to) {
+  auto swap = [&](TRef &r) {
+    if (r.p && r.id == from.id) {
+      r.p = to.p;
+      r.id = to.id;
+    }
+  };
+  auto &t = op.t;
+  switch (op.kind) {
+    case Kind::Binary: case Kind::Xent: case Kind::Gather: case Kind::GeluBwd:
+    case Kind::SoftmaxBwd:
+      swap(t[0]); swap(t[1]); break;
+    case Kind::XentBwd: swap(t[0]); swap(t[1]); swap(t[3]); break;
+    case Kind::Scatter: swap(t[0]); swap(t[1]); swap(t[2]); break;
+    case Kind::Clip: swap(t[0]); swap(t[1]); break;
+    case Kind::RmsNormBwd: swap(t[0]); swap(t[1]); swap(t[2]); break;
+    case Kind::DevCopy: swap(t[1]); break;
+    case Kind::Gemm:
+      swap(t[0]); swap(t[1]); swap(t[3]);
+      op.gemm.a = static_cast<const float *>(t[0].p);
+      op.gemm.b = static_cast<const float *>(t[1].p);
+      op.gemm.bias = t[3].p ? t[3].f() : nullptr;
+      break;
+    default: swap(t[0]); break;  // single-input kinds
+  }
+}
+
+// copy(S -> T) where T's copied value is only read by later ops of this
+// program (then released, overwritten, or window-local): the readers read S
+// instead and the copy goes.  This removes the executor's reshape copies
+// (split_last_dim / merge_last_dims, execute.h:384-401, copies in the Metal
+// runtime, runtime.cpp:571-593) and identity sum_to_shape copies
+// (runtime.cpp:692-698) that feed one consumer.
+uint64_t forward_copies(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  std::vector<size_t> readers;
+  for (size_t i = 0; i < p.size(); ++i) {
+    Op &cp = p[i];
+    if (cp.dead || cp.kind != Kind::Copy) continue;
+    const TRef S = cp.t[0], T = cp.t[1];
+    if (!S.p || !T.p || S.id == T.id || S.numel() != T.numel()) continue;
+    readers.clear();
+    bool ok = true, ended = false, s_changed = false;
+    for (size_t j = i + 1; j < p.size() && ok && !ended; ++j) {
+      const Op &op = p[j];
+      if (op.dead) continue;
+      if (op.kind == Kind::Release) {
+        if (op.t[0].id == T.id) ended = true;
+        else if (op.t[0].id == S.id) s_changed = true;
+        continue;
+      }
+      if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce) {
+        for (const auto &s : op.multi)
+          for (const TRef *r : {&s.param, &s.grad, &s.out, &s.m1, &s.m2})
+            if (r->id == T.id || r->id == S.id) ok = false;
+        continue;
+      }
+      const Access a = access(op);
+      const bool rT = reads(a, T.id), wT = writes(a, T.id), wS = writes(a, S.id);
+      if (rT) {
+        if (s_changed) ok = false;
+        if (op.kind == Kind::Gemm && op.gemm.beta != 0.0f && op.t[2].id == T.id) ok = false;
+        if (wS && !elementwise(op.kind)) ok = false;  // would read S while writing it
+        readers.push_back(j);
+      }
+      if (wT) {
+        if (!full_write(op)) ok = false;
+        ended = true;  // T's copied value ends here (readers above forwarded)
+      }
+      if (wS) s_changed = true;
+    }
+    if (!ended) ended = g_live && g_live->window_local(T.id);
+    if (!ok || !ended) continue;
+    for (size_t j : readers) retarget_reads(p[j], T, S);
+    cp.dead = true;
+    ++folded;
+  }
+  return folded;
+}
+
 bool is_opt(Kind k) {
   return k == Kind::SqNorm || k == Kind::Clip || k == Kind::AdamW;
 }
@@ -493,8 +582,10 @@ void add_gradient_allreduce(std::vector<Op> &prog) {
   prog.insert(prog.begin() + static_cast<std::ptrdiff_t>(first), std::move(ar));
 }
 
-uint64_t optimize(std::vector<Op> &prog, void *comm) {
+uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live) {
+  g_live = live;
   uint64_t folded = 0;
+  folded += forward_copies(prog);
   folded += fuse_weight_gradient(prog);
   folded += fold_transposes(prog);
   folded += fuse_gemm_epilogues(prog);
@@ -503,6 +594,7 @@ uint64_t optimize(std::vector<Op> &prog, void *comm) {
   folded += fuse_pointwise_backward(prog);
   folded += fuse_step(prog);
   if (comm) add_gradient_allreduce(prog);
+  g_live = nullptr;
   return folded;
 }
 

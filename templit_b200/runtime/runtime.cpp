@@ -21,6 +21,7 @@
 #include <numeric>
 #include <stdexcept>
 #include <unordered_map>
+#include <unordered_set>
 
 namespace cuda {
 
@@ -79,7 +80,7 @@ const char *kind_name(Kind k) { return kKindNames[static_cast<int>(k)]; }
 }  // namespace internal
 
 // ---------------------------------------------------------------------------
-struct Runtime::Impl : internal::Recorder {
+struct Runtime::Impl : internal::Recorder, internal::Liveness {
   enum class State { Idle, Recording, Submitted };
   State state = State::Idle;
   uint64_t window_id = 0;
@@ -118,7 +119,50 @@ struct Runtime::Impl : internal::Recorder {
   };
   std::map<std::string, Prof> profile;
 
+  // window liveness: per allocation, whether some recorded program read it
+  // before writing it (its value crosses windows) and how many programs
+  // opened by fully overwriting it
+  struct Life {
+    bool crossed = false;
+    uint32_t fresh_writes = 0;
+  };
+  std::unordered_map<uint64_t, Life> life;
+  uint64_t optimizer_windows = 0;
+
   ~Impl() override { release_resources(); }
+
+  // Updates `life` from a recorded (not yet optimised) program.
+  void observe(const std::vector<Op> &p) {
+    std::unordered_set<uint64_t> touched;
+    bool updates = false;
+    for (const Op &op : p) {
+      if (op.kind == Kind::Release) {
+        life.erase(op.t[0].id);
+        continue;
+      }
+      if (op.kind == Kind::AdamW) updates = true;
+      const internal::Access a = internal::access(op);
+      for (int i = 0; i < a.nr; ++i)
+        if (touched.insert(a.r[i]).second) life[a.r[i]].crossed = true;
+      for (int i = 0; i < a.nw; ++i)
+        if (touched.insert(a.w[i]).second) {
+          Life &l = life[a.w[i]];
+          if (internal::full_write(op)) ++l.fresh_writes;
+          else l.crossed = true;
+        }
+    }
+    if (updates) ++optimizer_windows;
+  }
+
+  // ---- Liveness: a buffer is window-local once two optimiser steps have
+  // run, every program so far that touched it overwrote it first (at least
+  // twice), and the host never read it.
+  bool window_local(uint64_t id) const override {
+    if (optimizer_windows < 2) return false;
+    const auto it = life.find(id);
+    return it != life.end() && !it->second.crossed && it->second.fresh_writes >= 2 &&
+           !internal::host_observed(id);
+  }
 
   // ---- Recorder
   uint64_t window() const override { return state == State::Recording ? window_id : 0; }
@@ -565,7 +609,10 @@ void Runtime::submit() {
   if (internal::active_recorder() == impl_.get()) internal::set_active_recorder(nullptr);
   const uint64_t recorded = impl_->prog.size();
   (void)recorded;
-  if (impl_->fusion) impl_->stats.fused_ops += internal::optimize(impl_->prog, impl_->comm);
+  if (impl_->fusion) {
+    impl_->observe(impl_->prog);
+    impl_->stats.fused_ops += internal::optimize(impl_->prog, impl_->comm, impl_.get());
+  }
   else if (impl_->comm) internal::add_gradient_allreduce(impl_->prog);
   impl_->state = Impl::State::Submitted;
   ++impl_->stats.windows;

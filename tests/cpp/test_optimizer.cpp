@@ -280,6 +280,63 @@ void fused_step() {
           "data-parallel all-reduce ahead of the optimiser");
 }
 
+
+Op copy(const TRef &src, const TRef &dst) {
+  Op o = op(Kind::Copy);
+  o.t[0] = src;
+  o.t[1] = dst;
+  return o;
+}
+
+struct FixedLiveness : Liveness {
+  std::vector<uint64_t> ids;
+  bool window_local(uint64_t id) const override {
+    for (uint64_t i : ids)
+      if (i == id) return true;
+    return false;
+  }
+};
+
+// reshape copy (merge_last_dims) feeding one GEMM, then released: the GEMM
+// reads the source and the copy goes
+void copy_forwarded_to_reader() {
+  auto s = tensor({64, 192, 384}), t = tensor({12288, 384}), w = tensor({384, 1536});
+  auto c = tensor({12288, 1536});
+  std::vector<Op> p = {copy(s, t), gemm(t, w, c, 12288, 1536, 384), release(t)};
+  require(optimize(p, nullptr) == 1, "copy folded");
+  auto v = live(p);
+  require(v.size() == 1 && v[0]->t[0].id == s.id && v[0]->gemm.a == s.p,
+          "GEMM reads the copy's source");
+}
+
+// the copy's destination outlives the program: kept, unless window-local
+void copy_kept_when_observable() {
+  auto s = tensor({4096}), t = tensor({4096}), u = tensor({4096});
+  std::vector<Op> p = {copy(s, t), binary(TL_MUL, t, t, u)};
+  require(optimize(p, nullptr) == 0, "observable copy kept");
+  std::vector<Op> q = {copy(s, t), binary(TL_MUL, t, t, u)};
+  FixedLiveness live_t;
+  live_t.ids = {t.id};
+  require(optimize(q, nullptr, &live_t) == 1, "window-local copy folded");
+  auto v = live(q);
+  require(v.size() == 1 && v[0]->t[0].id == s.id && v[0]->t[1].id == s.id, "both operands");
+}
+
+// the source changes before the destination is read: kept
+void copy_kept_when_source_changes() {
+  auto s = tensor({4096}), t = tensor({4096}), u = tensor({4096});
+  std::vector<Op> p = {copy(s, t), binary(TL_ADD, u, u, s), binary(TL_MUL, t, t, u), release(t)};
+  require(optimize(p, nullptr) == 0, "copy kept: source overwritten before the read");
+  // a partial Storage write of the destination does not end the copied value
+  auto a = tensor({4096}), b = tensor({4096}), c = tensor({4096});
+  Op fill = op(Kind::Fill);
+  fill.t[0] = b;
+  fill.t[0].shape[0] = 4096 * 4;  // byte view of the block
+  fill.n = 16;
+  std::vector<Op> q = {copy(a, b), fill, binary(TL_MUL, b, b, c), release(b)};
+  require(optimize(q, nullptr) == 0, "copy kept: partial overwrite");
+}
+
 }  // namespace
 
 int main() {
@@ -295,6 +352,9 @@ int main() {
       {"xent_and_gelu_backward", xent_and_gelu_backward},
       {"reused_address_is_not_confused", reused_address_is_not_confused},
       {"fused_step", fused_step},
+      {"copy_forwarded_to_reader", copy_forwarded_to_reader},
+      {"copy_kept_when_observable", copy_kept_when_observable},
+      {"copy_kept_when_source_changes", copy_kept_when_source_changes},
   };
   for (const auto &[name, fn] : cases) {
     try {
