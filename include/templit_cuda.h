@@ -219,13 +219,15 @@ int tl_embedding_gather(const float *weights, uint32_t n_rows, uint32_t dim,
  * (base NULL => zeros; base may equal dst).  Replaces
  * Runtime::scatter_add_rows (base given) and Runtime::scatter_index (base
  * NULL) (src/my_metal/runtime.cpp:952-1030; math.metal:794-820).
- * Deterministic: rows are bucketed by id (stable) and summed in input order.
+ * Deterministic: each chunk of 256 ids is summed per id in input order, and
+ * each row folds its chunk sums in chunk order.  The workspace holds one
+ * partial row per id (tl_embedding_scatter_workspace_size).
  * An id >= n_rows is skipped and sets TL_FLAG_INDEX_RANGE. */
 int tl_embedding_scatter_add(const float *values, const uint32_t *ids,
                              uint32_t n_ids, uint32_t dim, const float *base,
                              float *dst, uint32_t n_rows, void *workspace,
                              size_t workspace_bytes, void *stream);
-size_t tl_embedding_scatter_workspace_size(uint32_t n_ids, uint32_t n_rows);
+size_t tl_embedding_scatter_workspace_size(uint32_t n_ids, uint32_t n_rows, uint32_t dim);
 
 /* -------------------------------------------------------------- optimiser */
 /* sqnorm[0] += sum(grad^2).  Replaces Runtime::accumulate_gradient_squared_norm

@@ -115,7 +115,7 @@ CUDA_ABI = {
                                     c_void_p, c_void_p]),
     "tl_embedding_scatter_add": (c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_void_p,
                                          c_void_p, c_uint32, c_void_p, c_size_t, c_void_p]),
-    "tl_embedding_scatter_workspace_size": (c_size_t, [c_uint32, c_uint32]),
+    "tl_embedding_scatter_workspace_size": (c_size_t, [c_uint32, c_uint32, c_uint32]),
     "tl_grad_sqnorm_accumulate": (c_int, [c_void_p, c_size_t, c_void_p, c_void_p,
                                           c_size_t, c_void_p]),
     "tl_grad_sqnorm_workspace_size": (c_size_t, [c_size_t]),

@@ -3,12 +3,15 @@
 // src/my_metal/runtime.cpp:920-1030; math.metal:778-820).
 //
 // The reference scatters with one float atomic per element, so its result
-// depends on arrival order.  Here the scatter is a stable counting sort of
-// the ids (one CTA: histogram, scan, stable placement through warp match
-// masks) followed by a gather-sum per destination row in input order, which
-// makes every run bit-identical.  Ids outside the table never touch memory:
+// depends on arrival order.  Here the scatter runs in two deterministic
+// phases: every chunk of 256 ids is sorted in shared memory and summed per
+// distinct id (position order), then every destination row folds its chunk
+// partials in a fixed order.  Every run is bit-identical, and a hot id (a
+// frequent token) is spread over all chunks instead of one serial loop.  Ids outside the table never touch memory:
 // they raise TL_FLAG_INDEX_RANGE in the device status word instead.
 #include "tl_common.cuh"
+
+#include <type_traits>
 
 namespace tl {
 namespace {
@@ -39,119 +42,175 @@ gather_kernel(const float *__restrict__ w, uint32_t n_rows, uint32_t dim,
   }
 }
 
-constexpr int kSortThreads = 1024;
+constexpr uint32_t kChunk = 256;  // ids per chunk (one CTA, one thread per id)
+constexpr uint32_t kInvalid = 0xffffffffu;
 
-// Stable counting sort of ids into order[] (positions grouped by id, input
-// order inside a group) and offsets[r]..offsets[r+1] bounds of group r.
-// One CTA; counts/offsets live in `offsets` (n_rows + 1 words).
-__global__ void __launch_bounds__(kSortThreads)
-bucket_kernel(const uint32_t *__restrict__ ids, uint32_t n_ids, uint32_t n_rows,
-              uint32_t *offsets, uint32_t *order, uint32_t *status) {
-  // 1. histogram
-  for (uint32_t r = threadIdx.x; r <= n_rows; r += blockDim.x) offsets[r] = 0;
-  __syncthreads();
-  for (uint32_t i = threadIdx.x; i < n_ids; i += blockDim.x) {
-    const uint32_t id = ids[i];
-    if (id < n_rows) atomicAdd(&offsets[id + 1], 1u);
-    else raise_flag(status, TL_FLAG_INDEX_RANGE);
-  }
-  __syncthreads();
-  // 2. inclusive scan of offsets[1..n_rows] -> exclusive starts
-  __shared__ uint32_t carry;
-  __shared__ uint32_t warp_tot[kSortThreads / 32];
-  if (threadIdx.x == 0) carry = 0;
-  __syncthreads();
-  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (uint32_t base = 1; base <= n_rows; base += blockDim.x) {
-    const uint32_t r = base + threadIdx.x;
-    uint32_t v = r <= n_rows ? offsets[r] : 0;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t u = __shfl_up_sync(0xffffffffu, v, o);
-      if (lane >= static_cast<uint32_t>(o)) v += u;
+// Phase 1: CTA p takes ids [p * kChunk, (p + 1) * kChunk), sorts the
+// (id, position) pairs of its chunk (bitonic, in shared memory), and for each
+// distinct id u of the chunk (ascending) writes
+//   partial[p * kChunk + u, :] = sum of values[i, :] over the chunk's i with
+//                                ids[i] == id, in position order,
+//   uid[p * kChunk + u] = id, and ucount[p] = number of distinct ids.
+template <int V>
+__global__ void __launch_bounds__(kChunk)
+chunk_sum_kernel(const float *__restrict__ values, const uint32_t *__restrict__ ids,
+                 uint32_t n_ids, uint32_t dim, uint32_t n_rows, float *partial,
+                 uint32_t *uid, uint32_t *ucount, uint32_t *status) {
+  __shared__ unsigned long long key[kChunk];
+  __shared__ uint32_t gstart[kChunk + 1];
+  __shared__ uint32_t warp_heads[kChunk / 32], warp_valid[kChunk / 32];
+  const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const uint64_t first = static_cast<uint64_t>(blockIdx.x) * kChunk;
+  uint32_t id = kInvalid;
+  if (first + t < n_ids) {
+    id = ids[first + t];
+    if (id >= n_rows) {
+      raise_flag(status, TL_FLAG_INDEX_RANGE);
+      id = kInvalid;
     }
-    if (lane == 31) warp_tot[warp] = v;
-    __syncthreads();
-    if (warp == 0) {
-      uint32_t w = lane < blockDim.x / 32 ? warp_tot[lane] : 0;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t u = __shfl_up_sync(0xffffffffu, w, o);
-        if (lane >= static_cast<uint32_t>(o)) w += u;
-      }
-      warp_tot[lane] = w;  // inclusive warp prefix
-    }
-    __syncthreads();
-    const uint32_t add = carry + (warp ? warp_tot[warp - 1] : 0);
-    if (r <= n_rows) offsets[r] = v + add;
-    __syncthreads();
-    if (threadIdx.x == 0) carry += warp_tot[blockDim.x / 32 - 1];
-    __syncthreads();
   }
-  // 3. stable placement: chunks of blockDim ids in order; inside a chunk the
-  //    warps take turns so earlier positions claim earlier slots.
-  for (uint32_t base = 0; base < n_ids; base += blockDim.x) {
-    const uint32_t i = base + threadIdx.x;
-    const uint32_t id = i < n_ids ? ids[i] : 0xffffffffu;
-    const bool valid = i < n_ids && id < n_rows;
-    const uint32_t key = valid ? id : 0xffffffffu;
-    const uint32_t peers = __match_any_sync(0xffffffffu, key);
-    const uint32_t rank = __popc(peers & ((1u << lane) - 1u));
-    const bool leader = rank == 0;
-    const uint32_t group = __popc(peers);
-    for (uint32_t w = 0; w < blockDim.x / 32; ++w) {
-      if (warp == w && valid) {
-        // offsets[id] is the running insert cursor of bucket id
-        uint32_t start = 0;
-        if (leader) start = atomicAdd(&offsets[id], group);
-        const int src = __ffs(peers) - 1;
-        start = __shfl_sync(peers, start, src);
-        order[start + rank] = i;
+  key[t] = (static_cast<unsigned long long>(id) << 32) | t;
+  __syncthreads();
+  for (uint32_t k = 2; k <= kChunk; k <<= 1) {
+    for (uint32_t j = k >> 1; j > 0; j >>= 1) {
+      const uint32_t o = t ^ j;
+      if (o > t) {
+        const unsigned long long a = key[t], b = key[o];
+        if ((a > b) == ((t & k) == 0)) {
+          key[t] = b;
+          key[o] = a;
+        }
       }
       __syncthreads();
     }
   }
-  // offsets[r] now holds the end of bucket r (the insert cursor ran through it)
+  // group heads and their ranks (a block-wide exclusive count)
+  const uint32_t my = static_cast<uint32_t>(key[t] >> 32);
+  const bool valid = my != kInvalid;
+  const bool head = valid && (t == 0 || static_cast<uint32_t>(key[t - 1] >> 32) != my);
+  const uint32_t hb = __ballot_sync(0xffffffffu, head), vb = __ballot_sync(0xffffffffu, valid);
+  if (lane == 0) {
+    warp_heads[warp] = __popc(hb);
+    warp_valid[warp] = __popc(vb);
+  }
+  __syncthreads();
+  uint32_t before = 0, groups = 0, n_valid = 0;
+  for (uint32_t w = 0; w < kChunk / 32; ++w) {
+    if (w < warp) before += warp_heads[w];
+    groups += warp_heads[w];
+    n_valid += warp_valid[w];
+  }
+  const uint32_t g = before + __popc(hb & ((1u << lane) - 1u));
+  if (head) {
+    gstart[g] = t;
+    uid[first + g] = my;
+  }
+  if (t == 0) {
+    gstart[groups] = n_valid;
+    ucount[blockIdx.x] = groups;
+  }
+  __syncthreads();
+  for (uint32_t q = warp; q < groups; q += kChunk / 32) {
+    const uint32_t b = gstart[q], e = gstart[q + 1];
+    float *dst = partial + (first + q) * dim;
+    for (uint32_t d = lane * V; d < dim; d += 32 * V) {
+      if constexpr (V == 4) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (uint32_t k = b; k < e; ++k) {
+          const uint32_t pos = static_cast<uint32_t>(key[k] & 0xffffffffu);
+          const float4 v =
+              *reinterpret_cast<const float4 *>(values + (first + pos) * dim + d);
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
+        }
+        *reinterpret_cast<float4 *>(dst + d) = acc;
+      } else {
+        float acc = 0.0f;
+        for (uint32_t k = b; k < e; ++k) {
+          const uint32_t pos = static_cast<uint32_t>(key[k] & 0xffffffffu);
+          acc += values[(first + pos) * dim + d];
+        }
+        dst[d] = acc;
+      }
+    }
+  }
 }
 
-// After bucket_kernel offsets[r] = end of bucket r (the cursor ran to the end)
-// so bucket r spans [r ? offsets[r-1] : 0, offsets[r]).
+// Phase 2: CTA (r, slice) writes dst[r, slice] = base[r, slice] + the chunk
+// partials of row r.  Thread t binary-searches chunk t of each round of 256
+// chunks; warp w folds the chunks c with c % 8 == w in increasing order, and
+// warp 0 folds the 8 warp sums in warp order: a fixed summation order.
 template <int V>
-__global__ void __launch_bounds__(256)
-segment_sum_kernel(const float *__restrict__ values, const uint32_t *__restrict__ order,
-                   const uint32_t *__restrict__ ends, uint32_t dim, uint32_t n_rows,
+__global__ void __launch_bounds__(kChunk)
+row_combine_kernel(const float *__restrict__ partial, const uint32_t *__restrict__ uid,
+                   const uint32_t *__restrict__ ucount, uint32_t n_chunks, uint32_t dim,
                    const float *base, float *dst) {
-  const uint32_t per_row = dim / V;
-  const uint64_t total = static_cast<uint64_t>(n_rows) * per_row;
-  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
-  for (uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-       t < total; t += stride) {
-    const uint32_t r = static_cast<uint32_t>(t / per_row);
-    const uint32_t c = static_cast<uint32_t>(t % per_row) * V;
-    const uint32_t b = r ? ends[r - 1] : 0u, e = ends[r];
-    const size_t o = static_cast<size_t>(r) * dim + c;
-    if constexpr (V == 4) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (uint32_t k = b; k < e; ++k) {
-        const float4 v = *reinterpret_cast<const float4 *>(values + static_cast<size_t>(order[k]) * dim + c);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+  using Vec = typename std::conditional<V == 4, float4, float>::type;
+  __shared__ int slot[kChunk];
+  __shared__ Vec wsum[kChunk / 32][32];
+  const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const uint32_t r = blockIdx.x;
+  const uint32_t d = blockIdx.y * 32 * V + lane * V;
+  const bool in = d < dim;
+  float acc[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) acc[v] = 0.0f;
+  for (uint32_t round = 0; round < n_chunks; round += kChunk) {
+    const uint32_t c = round + t;
+    int found = -1;
+    if (c < n_chunks) {
+      const uint32_t *u = uid + static_cast<uint64_t>(c) * kChunk;
+      uint32_t lo = 0, hi = ucount[c];
+      while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (u[mid] < r) lo = mid + 1;
+        else hi = mid;
       }
-      if (base) {
-        const float4 bv = *reinterpret_cast<const float4 *>(base + o);
-        acc.x = bv.x + acc.x;
-        acc.y = bv.y + acc.y;
-        acc.z = bv.z + acc.z;
-        acc.w = bv.w + acc.w;
-      }
-      *reinterpret_cast<float4 *>(dst + o) = acc;
-    } else {
-      float acc = 0.0f;
-      for (uint32_t k = b; k < e; ++k) acc += values[static_cast<size_t>(order[k]) * dim + c];
-      dst[o] = base ? base[o] + acc : acc;
+      if (lo < ucount[c] && u[lo] == r) found = static_cast<int>(lo);
     }
+    slot[t] = found;
+    __syncthreads();
+    const uint32_t in_round = min(kChunk, n_chunks - round);
+    for (uint32_t q = warp; q < in_round; q += kChunk / 32) {
+      const int u = slot[q];
+      if (u < 0 || !in) continue;
+      const float *src = partial + ((static_cast<uint64_t>(round + q)) * kChunk + u) * dim + d;
+      if constexpr (V == 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(src);
+        acc[0] += v.x;
+        acc[1] += v.y;
+        acc[2] += v.z;
+        acc[3] += v.w;
+      } else {
+        acc[0] += *src;
+      }
+    }
+    __syncthreads();
+  }
+  if constexpr (V == 4) wsum[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  else wsum[warp][lane] = acc[0];
+  __syncthreads();
+  if (warp != 0 || !in) return;
+  float s[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) s[v] = 0.0f;
+  for (uint32_t w = 0; w < kChunk / 32; ++w) {
+    const float *x = reinterpret_cast<const float *>(&wsum[w][lane]);
+#pragma unroll
+    for (int v = 0; v < V; ++v) s[v] += x[v];
+  }
+  const size_t o = static_cast<size_t>(r) * dim + d;
+  if constexpr (V == 4) {
+    float4 out = make_float4(s[0], s[1], s[2], s[3]);
+    if (base) {
+      const float4 b = *reinterpret_cast<const float4 *>(base + o);
+      out = make_float4(b.x + s[0], b.y + s[1], b.z + s[2], b.w + s[3]);
+    }
+    *reinterpret_cast<float4 *>(dst + o) = out;
+  } else {
+    dst[o] = base ? base[o] + s[0] : s[0];
   }
 }
 
@@ -178,8 +237,16 @@ int tl_embedding_gather(const float *weights, uint32_t n_rows, uint32_t dim,
   return launch_status("tl_embedding_gather");
 }
 
-size_t tl_embedding_scatter_workspace_size(uint32_t n_ids, uint32_t n_rows) {
-  return (static_cast<size_t>(n_rows) + 1 + n_ids) * sizeof(uint32_t);
+namespace {
+uint32_t scatter_chunks(uint32_t n_ids) { return (n_ids + kChunk - 1) / kChunk; }
+}  // namespace
+
+size_t tl_embedding_scatter_workspace_size(uint32_t n_ids, uint32_t n_rows, uint32_t dim) {
+  (void)n_rows;
+  const size_t slots = static_cast<size_t>(scatter_chunks(n_ids)) * kChunk;
+  // partial rows, then uid per slot, then one count per chunk
+  return slots * dim * sizeof(float) + slots * sizeof(uint32_t) +
+         scatter_chunks(n_ids) * sizeof(uint32_t);
 }
 
 int tl_embedding_scatter_add(const float *values, const uint32_t *ids,
@@ -189,24 +256,34 @@ int tl_embedding_scatter_add(const float *values, const uint32_t *ids,
   if (n_rows == 0 || dim == 0) return TL_OK;
   if (!dst || (n_ids && (!values || !ids)))
     return fail(TL_ERR_INVALID, "tl_embedding_scatter_add: null pointer");
-  if (!workspace || workspace_bytes < tl_embedding_scatter_workspace_size(n_ids, n_rows))
+  if (n_ids && (!workspace ||
+                workspace_bytes < tl_embedding_scatter_workspace_size(n_ids, n_rows, dim)))
     return fail(TL_ERR_INVALID, "tl_embedding_scatter_add: workspace too small");
   uint32_t *status = device_status_ptr();
   if (!status) return fail(TL_ERR_CUDA, "tl_embedding_scatter_add: no status word");
   cudaStream_t s = as_stream(stream);
-  uint32_t *offsets = static_cast<uint32_t *>(workspace);
-  uint32_t *order = offsets + n_rows + 1;
-  bucket_kernel<<<1, kSortThreads, 0, s>>>(ids, n_ids, n_rows, offsets, order, status);
-  int rc = launch_status("tl_embedding_scatter_add bucket");
-  if (rc) return rc;
-  // the placement cursor ends each bucket at its end: bucket r = [ends[r-1], ends[r])
-  const uint64_t total = static_cast<uint64_t>(n_rows) * dim;
-  const bool vec = dim % 4 == 0 && aligned16(values) && aligned16(dst) && (!base || aligned16(base));
+  const uint32_t chunks = scatter_chunks(n_ids);
+  const size_t slots = static_cast<size_t>(chunks) * kChunk;
+  float *partial = static_cast<float *>(workspace);
+  uint32_t *uid = reinterpret_cast<uint32_t *>(partial + slots * dim);
+  uint32_t *ucount = uid + slots;
+  const bool vec = dim % 4 == 0 && aligned16(values) && aligned16(dst) &&
+                   (!base || aligned16(base)) && aligned16(workspace);
+  if (chunks) {
+    if (vec)
+      chunk_sum_kernel<4><<<chunks, kChunk, 0, s>>>(values, ids, n_ids, dim, n_rows, partial, uid, ucount, status);
+    else
+      chunk_sum_kernel<1><<<chunks, kChunk, 0, s>>>(values, ids, n_ids, dim, n_rows, partial, uid, ucount, status);
+    const int rc = launch_status("tl_embedding_scatter_add chunks");
+    if (rc) return rc;
+  }
+  const uint32_t per = 32 * (vec ? 4 : 1);
+  const dim3 grid(n_rows, (dim + per - 1) / per);
   if (vec)
-    segment_sum_kernel<4><<<grid_for(total / 4, 256), 256, 0, s>>>(values, order, offsets, dim, n_rows, base, dst);
+    row_combine_kernel<4><<<grid, kChunk, 0, s>>>(partial, uid, ucount, chunks, dim, base, dst);
   else
-    segment_sum_kernel<1><<<grid_for(total, 256), 256, 0, s>>>(values, order, offsets, dim, n_rows, base, dst);
-  return launch_status("tl_embedding_scatter_add sum");
+    row_combine_kernel<1><<<grid, kChunk, 0, s>>>(partial, uid, ucount, chunks, dim, base, dst);
+  return launch_status("tl_embedding_scatter_add rows");
 }
 
 }  // extern "C"

@@ -272,8 +272,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
       const uint32_t m = mb * BM + q * 32 + lane;
       const uint32_t n_base = nb * BN;
       const bool row_ok = m < g.m;
+      // 128-bit path: raw partials, or the full epilogue on float4 groups
+      // (bias, accumulate and GELU in the same order as epilogue_store)
       const bool fast = (g.n % 4) == 0 && aligned16(Cb) &&
-                        (raw || (!g.gelu_out && !g.bias && g.beta == 0.0f));
+                        (raw || ((!g.bias || aligned16(g.bias)) &&
+                                 (!g.gelu_out || aligned16(g.gelu_out + oc))));
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -285,9 +288,24 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
         if (fast && n0 + 32 <= g.n) {
           float4 *dst = reinterpret_cast<float4 *>(Cb + rowoff + n0);
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          for (int j = 0; j < 8; ++j) {
+            float4 v = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+            if (!raw) {
+              if (g.bias) {
+                const float4 b = *reinterpret_cast<const float4 *>(g.bias + n0 + 4 * j);
+                v = make_float4(v.x + b.x, v.y + b.y, v.z + b.z, v.w + b.w);
+              }
+              if (g.beta != 0.0f) {
+                const float4 o = dst[j];
+                v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
+              }
+            }
+            dst[j] = v;
+            if (!raw && g.gelu_out)
+              *reinterpret_cast<float4 *>(g.gelu_out + oc + rowoff + n0 + 4 * j) =
+                  make_float4(gelu_f(v.x), gelu_f(v.y), gelu_f(v.z), gelu_f(v.w));
+          }
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {

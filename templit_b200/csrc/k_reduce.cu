@@ -82,6 +82,7 @@ cols_kernel(const float *__restrict__ x, float *out, uint32_t K1, uint32_t R,
     const float *base = x + (static_cast<size_t>(k1) * R) * K2 + k2;
     if constexpr (V == 4) {
       float4 acc = make_float4(rinit<OP>(), rinit<OP>(), rinit<OP>(), rinit<OP>());
+#pragma unroll 8
       for (uint32_t r = r0; r < r1; ++r) {
         const float4 v = *reinterpret_cast<const float4 *>(base + static_cast<size_t>(r) * K2);
         acc.x = rcomb<OP>(acc.x, v.x);
@@ -99,17 +100,29 @@ cols_kernel(const float *__restrict__ x, float *out, uint32_t K1, uint32_t R,
   }
 }
 
-// Sums `splits` partial planes part[s, i] into out[i] in split order.
+// Sums `splits` partial planes part[s, i] into out[i].  A CTA owns 32
+// consecutive outputs; warp w folds splits w, w + 8, w + 16, ... in order and
+// warp 0 then folds the 8 warp results in warp order, so the summation order
+// is fixed (deterministic) while 8 warps keep loads in flight.
 template <int OP>
 __global__ void __launch_bounds__(256)
 combine_kernel(const float *__restrict__ part, float *out, uint64_t n,
                uint32_t splits) {
-  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
-  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-       i < n; i += stride) {
-    float acc = rinit<OP>();
-    for (uint32_t s = 0; s < splits; ++s) acc = rcomb<OP>(acc, part[s * n + i]);
-    out[i] = acc;
+  __shared__ float acc_w[8][33];
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint64_t i = static_cast<uint64_t>(blockIdx.x) * 32 + lane;
+  float acc = rinit<OP>();
+  if (i < n) {
+#pragma unroll 4
+    for (uint32_t s = warp; s < splits; s += 8) acc = rcomb<OP>(acc, part[s * n + i]);
+  }
+  acc_w[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && i < n) {
+    float r = acc_w[0][lane];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) r = rcomb<OP>(r, acc_w[w][lane]);
+    out[i] = r;
   }
 }
 
@@ -291,7 +304,7 @@ int run_plan(const ReducePlan &pl, const float *x, float *out, void *ws,
         cols_kernel<OP, 1><<<grid_for(work, 256, 16), 256, 0, s>>>(x, dst, pl.K1, pl.R, pl.K2, pl.splits, pl.chunk);
       int rc = launch_status("reduce cols");
       if (rc || pl.splits == 1) return rc;
-      combine_kernel<OP><<<grid_for(outs, 256), 256, 0, s>>>(dst, out, outs, pl.splits);
+      combine_kernel<OP><<<static_cast<unsigned>((outs + 31) / 32), 256, 0, s>>>(dst, out, outs, pl.splits);
       return launch_status("reduce cols combine");
     }
     default:

@@ -14,6 +14,7 @@
 #include "optimize.h"
 
 #include <algorithm>
+#include <string>
 #include <unordered_map>
 #include <unordered_set>
 
@@ -413,55 +414,171 @@ void retarget_reads(Op &op, const TRef &from, const TRef &to) {
   }
 }
 
-// copy(S -> T) where T's copied value is only read by later ops of this
-// program (then released, overwritten, or window-local): the readers read S
-// instead and the copy goes.  This removes the executor's reshape copies
-// (split_last_dim / merge_last_dims, execute.h:384-401, copies in the Metal
-// runtime, runtime.cpp:571-593) and identity sum_to_shape copies
-// (runtime.cpp:692-698) that feed one consumer.
+// Op i left in T a value equal to the current value of S.  When every later
+// read of that value can read S instead (S unchanged until the last such
+// read; T's value then ends: released, fully overwritten, or window-local),
+// retargets those reads to S and returns true; otherwise changes nothing.
+bool forward_value(std::vector<Op> &p, size_t i, const TRef &T, const TRef &S) {
+  std::vector<size_t> readers;
+  bool ended = false, s_changed = false;
+  for (size_t j = i + 1; j < p.size() && !ended; ++j) {
+    const Op &op = p[j];
+    if (op.dead) continue;
+    if (op.kind == Kind::Release) {
+      if (op.t[0].id == T.id) ended = true;
+      else if (op.t[0].id == S.id) s_changed = true;
+      continue;
+    }
+    if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce) {
+      for (const auto &sl : op.multi)
+        for (const TRef *r : {&sl.param, &sl.grad, &sl.out, &sl.m1, &sl.m2})
+          if (r->id == T.id || r->id == S.id) return false;
+      continue;
+    }
+    const Access a = access(op);
+    const bool rT = reads(a, T.id), wT = writes(a, T.id), wS = writes(a, S.id);
+    if (rT) {
+      if (s_changed) return false;
+      if (op.kind == Kind::Gemm && op.gemm.beta != 0.0f && op.t[2].id == T.id) return false;
+      if (op.kind == Kind::HostWrite || op.kind == Kind::Fill || op.kind == Kind::DevCopy)
+        return false;  // byte views of whole blocks
+      if (wS && !elementwise(op.kind)) return false;  // would read S while writing it
+      readers.push_back(j);
+    }
+    if (wT) {
+      if (!full_write(op)) return false;
+      ended = true;  // T's forwarded value ends here
+    }
+    if (wS) s_changed = true;
+  }
+  if (!ended && !(g_live && g_live->window_local(T.id))) return false;
+  for (size_t j : readers) retarget_reads(p[j], T, S);
+  return true;
+}
+
+// copy(S -> T) whose destination value can be read from S: the copy goes.
+// This removes the executor's reshape copies (split_last_dim /
+// merge_last_dims, execute.h:384-401, copies in the Metal runtime,
+// runtime.cpp:571-593) and identity sum_to_shape copies
+// (runtime.cpp:692-698).
 uint64_t forward_copies(std::vector<Op> &p) {
   uint64_t folded = 0;
-  std::vector<size_t> readers;
   for (size_t i = 0; i < p.size(); ++i) {
     Op &cp = p[i];
     if (cp.dead || cp.kind != Kind::Copy) continue;
     const TRef S = cp.t[0], T = cp.t[1];
     if (!S.p || !T.p || S.id == T.id || S.numel() != T.numel()) continue;
-    readers.clear();
-    bool ok = true, ended = false, s_changed = false;
-    for (size_t j = i + 1; j < p.size() && ok && !ended; ++j) {
-      const Op &op = p[j];
-      if (op.dead) continue;
-      if (op.kind == Kind::Release) {
-        if (op.t[0].id == T.id) ended = true;
-        else if (op.t[0].id == S.id) s_changed = true;
-        continue;
-      }
-      if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce) {
-        for (const auto &s : op.multi)
-          for (const TRef *r : {&s.param, &s.grad, &s.out, &s.m1, &s.m2})
-            if (r->id == T.id || r->id == S.id) ok = false;
-        continue;
-      }
-      const Access a = access(op);
-      const bool rT = reads(a, T.id), wT = writes(a, T.id), wS = writes(a, S.id);
-      if (rT) {
-        if (s_changed) ok = false;
-        if (op.kind == Kind::Gemm && op.gemm.beta != 0.0f && op.t[2].id == T.id) ok = false;
-        if (wS && !elementwise(op.kind)) ok = false;  // would read S while writing it
-        readers.push_back(j);
-      }
-      if (wT) {
-        if (!full_write(op)) ok = false;
-        ended = true;  // T's copied value ends here (readers above forwarded)
-      }
-      if (wS) s_changed = true;
-    }
-    if (!ended) ended = g_live && g_live->window_local(T.id);
-    if (!ok || !ended) continue;
-    for (size_t j : readers) retarget_reads(p[j], T, S);
+    if (!forward_value(p, i, T, S)) continue;
     cp.dead = true;
     ++folded;
+  }
+  return folded;
+}
+
+// Common subexpressions.  Reverse-mode rules embed the upstream gradient
+// expression in every operand's gradient (include/passes/autograd.h), so
+// the executor evaluates a shared upstream gradient once per path that
+// uses it (attention's score gradient for both dQ and dK, the output
+// projection's input gradient for each of dQ, dK, dV).  An op that repeats
+// an earlier op (same kind and parameters, same input buffers holding the
+// same values) is dropped when its result can be read from the earlier
+// op's output instead.  All kernels are deterministic, so the values read
+// are bit-identical to the recomputed ones.
+bool cse_candidate(const Op &op, const Access &a) {
+  switch (op.kind) {
+    case Kind::Binary: case Kind::Scalar: case Kind::Unary: case Kind::Copy: case Kind::Reduce:
+    case Kind::Argmax: case Kind::Transpose: case Kind::Softmax: case Kind::Rms:
+    case Kind::RmsNorm: case Kind::Xent: case Kind::XentBwd: case Kind::Gather:
+    case Kind::Scatter: case Kind::GeluBwd: case Kind::SoftmaxBwd: case Kind::RmsNormBwd:
+      break;
+    case Kind::Gemm:
+      if (op.gemm.beta != 0.0f || op.gemm.gelu_out) return false;
+      break;
+    default:
+      return false;
+  }
+  return a.nw == 1 && !reads(a, a.w[0]);
+}
+
+uint64_t eliminate_common(std::vector<Op> &p) {
+  std::unordered_map<uint64_t, uint32_t> version;
+  struct Seen {
+    size_t op;
+    TRef out;
+    uint32_t out_version;
+  };
+  std::unordered_map<std::string, Seen> table;
+  auto bump = [&](uint64_t id) { ++version[id]; };
+  auto put = [](std::string &k, const void *d, size_t n) {
+    k.append(static_cast<const char *>(d), n);
+  };
+  uint64_t folded = 0;
+  std::string key;
+  for (size_t i = 0; i < p.size(); ++i) {
+    Op &op = p[i];
+    if (op.dead) continue;
+    if (op.kind == Kind::Release) {
+      bump(op.t[0].id);
+      continue;
+    }
+    if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce) {
+      for (const auto &sl : op.multi)
+        for (const TRef *r : {&sl.param, &sl.grad, &sl.out, &sl.m1, &sl.m2}) bump(r->id);
+      continue;
+    }
+    const Access a = access(op);
+    if (!cse_candidate(op, a)) {
+      for (int w = 0; w < a.nw; ++w) bump(a.w[w]);
+      continue;
+    }
+    const uint64_t out_id = a.w[0];
+    key.clear();
+    put(key, &op.kind, sizeof(op.kind));
+    put(key, &op.code, sizeof(op.code));
+    put(key, &op.f0, sizeof(op.f0));
+    put(key, &op.f1, sizeof(op.f1));
+    put(key, &op.i0, sizeof(op.i0));
+    put(key, &op.i1, sizeof(op.i1));
+    put(key, &op.u0, sizeof(op.u0));
+    put(key, &op.n, sizeof(op.n));
+    int out_slot = -1;
+    for (int k = 0; k < 9; ++k) {
+      const TRef &r = op.t[k];
+      const uint8_t present = r.p ? 1 : 0;
+      put(key, &present, 1);
+      if (!r.p) continue;
+      put(key, &r.rank, 1);
+      put(key, r.shape, r.rank * sizeof(uint32_t));
+      if (r.id == out_id) {
+        out_slot = k;
+        continue;
+      }
+      const uint32_t v = version[r.id];
+      put(key, &r.id, sizeof(r.id));
+      put(key, &v, sizeof(v));
+    }
+    if (op.kind == Kind::Gemm) {
+      tl_gemm_desc g = op.gemm;  // pointers are covered by the operands above
+      g.a = g.b = nullptr;
+      g.c = g.gelu_out = nullptr;
+      g.bias = nullptr;
+      g.workspace = nullptr;
+      g.workspace_bytes = 0;
+      put(key, &g, sizeof(g));
+    }
+    auto it = table.find(key);
+    if (it != table.end() && version[it->second.out.id] == it->second.out_version &&
+        out_slot >= 0) {
+      const TRef &S = it->second.out;
+      const TRef &T = op.t[out_slot];
+      if (S.id == T.id || forward_value(p, i, T, S)) {
+        op.dead = true;  // T is not written: its readers now read S
+        ++folded;
+        continue;
+      }
+    }
+    bump(out_id);
+    if (out_slot >= 0) table[key] = Seen{i, op.t[out_slot], version[out_id]};
   }
   return folded;
 }
@@ -585,6 +702,7 @@ void add_gradient_allreduce(std::vector<Op> &prog) {
 uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live) {
   g_live = live;
   uint64_t folded = 0;
+  folded += eliminate_common(prog);
   folded += forward_copies(prog);
   folded += fuse_weight_gradient(prog);
   folded += fold_transposes(prog);

@@ -15,6 +15,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <map>
@@ -129,7 +130,54 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
   std::unordered_map<uint64_t, Life> life;
   uint64_t optimizer_windows = 0;
 
+  // program listings (TL_PROGRAM_DUMP=<file>): each distinct recorded
+  // program once, as recorded and as optimised
+  std::string dump_path = [] {
+    const char *e = std::getenv("TL_PROGRAM_DUMP");
+    return std::string(e ? e : "");
+  }();
+  std::unordered_set<std::string> dumped;
+
   ~Impl() override { release_resources(); }
+
+  static std::string describe(const Op &op) {
+    std::string s = internal::kind_name(op.kind);
+    if (op.kind == Kind::Binary || op.kind == Kind::Unary || op.kind == Kind::Scalar ||
+        op.kind == Kind::Reduce)
+      s += "#" + std::to_string(op.code);
+    if (op.kind == Kind::Gemm) {
+      const auto &g = op.gemm;
+      s += " " + std::to_string(g.m) + "x" + std::to_string(g.n) + "x" + std::to_string(g.k);
+      s += g.trans_a ? " T" : " N";
+      s += g.trans_b ? "T" : "N";
+      for (uint32_t i = 0; i < g.batch_rank; ++i)
+        s += (i ? "," : " b[") + std::to_string(g.batch_shape[i]) + "/" +
+             std::to_string(g.a_batch_stride[i]) + ":" + std::to_string(g.b_batch_stride[i]) +
+             ":" + std::to_string(g.c_batch_stride[i]) + (i + 1 == g.batch_rank ? "]" : "");
+      if (g.beta != 0.0f) s += " beta";
+      if (g.bias) s += " bias";
+      if (g.gelu_out) s += " gelu";
+    }
+    if (op.kind == Kind::Transpose) s += " " + std::to_string(op.i0) + "<>" + std::to_string(op.i1);
+    if (op.kind == Kind::Scalar) s += " " + std::to_string(op.f0);
+    for (int i = 0; i < 9; ++i) {
+      const TRef &r = op.t[i];
+      if (!r.p && !r.id) continue;
+      s += " t" + std::to_string(i) + "=" + std::to_string(r.id) + "[";
+      for (int d = 0; d < r.rank; ++d) s += (d ? "," : "") + std::to_string(r.shape[d]);
+      s += "]";
+    }
+    if (!op.multi.empty()) s += " slots=" + std::to_string(op.multi.size());
+    if (op.dead) s += " DEAD";
+    return s;
+  }
+
+  void dump(const char *title, bool fresh) {
+    std::ofstream out(dump_path, std::ios::app);
+    out << "== " << title << " window " << window_id << (fresh ? "" : " (again)") << " ops "
+        << prog.size() << "\n";
+    for (size_t i = 0; i < prog.size(); ++i) out << i << " " << describe(prog[i]) << "\n";
+  }
 
   // Updates `life` from a recorded (not yet optimised) program.
   void observe(const std::vector<Op> &p) {
@@ -609,10 +657,18 @@ void Runtime::submit() {
   if (internal::active_recorder() == impl_.get()) internal::set_active_recorder(nullptr);
   const uint64_t recorded = impl_->prog.size();
   (void)recorded;
+  bool dump = false;
+  if (!impl_->dump_path.empty() && impl_->dumped.size() < 64) {
+    std::string key = Impl::signature(impl_->prog);
+    key += impl_->optimizer_windows >= 2 ? 'L' : '-';  // window liveness known
+    dump = impl_->dumped.insert(std::move(key)).second;
+    if (dump) impl_->dump("recorded", true);
+  }
   if (impl_->fusion) {
     impl_->observe(impl_->prog);
     impl_->stats.fused_ops += internal::optimize(impl_->prog, impl_->comm, impl_.get());
   }
+  if (dump) impl_->dump("optimised", true);
   else if (impl_->comm) internal::add_gradient_allreduce(impl_->prog);
   impl_->state = Impl::State::Submitted;
   ++impl_->stats.windows;
@@ -1065,7 +1121,8 @@ void Runtime::scatter_add_rows(const Mat &base, const IndexMat &ids, const Mat &
   op.t[2] = ref(base);
   op.t[3] = ref(destination);
   op.workspace = tl_embedding_scatter_workspace_size(static_cast<uint32_t>(ids.numel()),
-                                                     destination.shape()[0]);
+                                                     destination.shape()[0],
+                                                     destination.shape()[1]);
 }
 
 // src/my_metal/runtime.cpp:1011-1030
@@ -1076,7 +1133,8 @@ void Runtime::scatter_index(const Mat &values, const IndexMat &ids, Mat &destina
   op.t[1] = ref(ids);
   op.t[3] = ref(destination);
   op.workspace = tl_embedding_scatter_workspace_size(static_cast<uint32_t>(ids.numel()),
-                                                     destination.shape()[0]);
+                                                     destination.shape()[0],
+                                                     destination.shape()[1]);
 }
 
 // ----------------------------------------------------------------- optimiser

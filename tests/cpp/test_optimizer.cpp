@@ -337,6 +337,42 @@ void copy_kept_when_source_changes() {
   require(optimize(q, nullptr) == 0, "copy kept: partial overwrite");
 }
 
+
+// the upstream gradient evaluated once per path (same GEMM, same inputs):
+// the second evaluation goes and its reader reads the first result
+void common_gemm_evaluated_once() {
+  auto g = tensor({12288, 384}), w = tensor({384, 384}), d1 = tensor({12288, 384});
+  auto d2 = tensor({12288, 384}), x = tensor({12288, 384}), y = tensor({12288, 384});
+  std::vector<Op> p = {gemm(g, w, d1, 12288, 384, 384), binary(TL_MUL, d1, d1, x),
+                       gemm(g, w, d2, 12288, 384, 384), binary(TL_ADD, d2, x, y),
+                       release(d2), release(d1)};
+  require(optimize(p, nullptr) == 1, "second product folded");
+  auto v = live(p);
+  require(v.size() == 3 && v[2]->kind == Kind::Binary && v[2]->t[0].id == d1.id,
+          "reader of the repeat reads the first product");
+}
+
+// an input changes between the two evaluations: both stay
+void common_kept_when_input_changes() {
+  auto g = tensor({4096}), d1 = tensor({4096}), d2 = tensor({4096}), x = tensor({4096});
+  Op u1 = op(Kind::Unary), u2 = op(Kind::Unary);
+  u1.code = u2.code = TL_EXP;
+  u1.t[0] = u2.t[0] = g;
+  u1.t[1] = d1;
+  u2.t[1] = d2;
+  std::vector<Op> p = {u1, binary(TL_ADD, d1, d1, g), u2, binary(TL_MUL, d2, d1, x),
+                       release(d2)};
+  require(optimize(p, nullptr) == 0, "input rewritten in between");
+  // same buffer rewritten with the value it still holds: the repeat goes
+  auto e = tensor({4096}), f = tensor({4096});
+  Op v1 = op(Kind::Unary), v2 = op(Kind::Unary);
+  v1.code = v2.code = TL_EXP;
+  v1.t[0] = v2.t[0] = e;
+  v1.t[1] = v2.t[1] = f;
+  std::vector<Op> q = {v1, binary(TL_MUL, f, f, x), v2, binary(TL_ADD, f, x, x)};
+  require(optimize(q, nullptr) == 1, "repeat into the same buffer folded");
+}
+
 }  // namespace
 
 int main() {
@@ -355,6 +391,8 @@ int main() {
       {"copy_forwarded_to_reader", copy_forwarded_to_reader},
       {"copy_kept_when_observable", copy_kept_when_observable},
       {"copy_kept_when_source_changes", copy_kept_when_source_changes},
+      {"common_gemm_evaluated_once", common_gemm_evaluated_once},
+      {"common_kept_when_input_changes", common_kept_when_input_changes},
   };
   for (const auto &[name, fn] : cases) {
     try {

@@ -172,7 +172,7 @@ class Dev:
         tv, ti = self.t(v), self.t(ids.view(np.int32), dtype=np.int32)
         tb = self.t(base) if base is not None else None
         out = self.empty((n_rows, dim))
-        nbytes = self.lib.tl_embedding_scatter_workspace_size(ids.size, n_rows)
+        nbytes = self.lib.tl_embedding_scatter_workspace_size(ids.size, n_rows, dim)
         ws = self.ws(nbytes)
         self.call("tl_embedding_scatter_add", self.p(tv), self.p(ti), ids.size, dim, self.p(tb),
                   self.p(out), n_rows, self.p(ws), nbytes, self.stream)
