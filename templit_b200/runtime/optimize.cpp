@@ -339,6 +339,32 @@ uint64_t fuse_rmsnorm_backward(std::vector<Op> &p) {
 // released: the loss root gradient applied per row inside the kernel.
 // GELU_derivative(x -> T); hadamard(T, g -> out) (or (g, T)) with T
 // released: the GELU chain rule in one pass.
+// True when no live op strictly between i and j writes or releases `id`.
+bool unchanged_between(const std::vector<Op> &p, size_t i, size_t j, uint64_t id) {
+  for (size_t k = i + 1; k < j; ++k) {
+    const Op &op = p[k];
+    if (op.dead) continue;
+    if (op.kind == Kind::Release) {
+      if (op.t[0].id == id) return false;
+      continue;
+    }
+    if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce) return false;
+    if (writes(access(op), id)) return false;
+  }
+  return true;
+}
+
+// First live op after i that reads `id` (kNone if none).
+size_t first_reader(const std::vector<Op> &p, size_t i, uint64_t id) {
+  for (size_t j = i + 1; j < p.size(); ++j) {
+    const Op &op = p[j];
+    if (op.dead || op.kind == Kind::Release) continue;
+    if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce) return kNone;
+    if (reads(access(op), id)) return j;
+  }
+  return kNone;
+}
+
 uint64_t fuse_pointwise_backward(std::vector<Op> &p) {
   uint64_t folded = 0;
   for (size_t i = 0; i < p.size(); ++i) {
@@ -348,7 +374,10 @@ uint64_t fuse_pointwise_backward(std::vector<Op> &p) {
     const bool gelu = a.kind == Kind::Unary && a.code == TL_GELU_DERIVATIVE;
     if (!xent && !gelu) continue;
     const TRef tmp = xent ? a.t[2] : a.t[1];
-    const size_t j = next_op(p, i);
+    // the product may come later in the program: the fused op then runs at
+    // the product's position, so its other inputs must still hold the
+    // values they had at op i
+    const size_t j = first_reader(p, i, tmp.id);
     if (j == kNone) continue;
     Op &h = p[j];
     if (h.kind != Kind::Binary || h.code != TL_MUL || !h.t[2].same_shape(tmp)) continue;
@@ -357,23 +386,26 @@ uint64_t fuse_pointwise_backward(std::vector<Op> &p) {
     if (!left && !right) continue;
     const TRef other = left ? h.t[0] : h.t[1];
     if (!dead_after(p, j, tmp.id)) continue;
+    if (!unchanged_between(p, i, j, a.t[0].id)) continue;
+    if (xent && !unchanged_between(p, i, j, a.t[1].id)) continue;
+    Op fused;
     if (xent) {
       // root gradient [..., 1] against logits [..., V]
       if (other.rank != tmp.rank || other.last() != 1 ||
           other.numel() * tmp.last() != tmp.numel())
         continue;
-      a.t[3] = other;
-      a.t[2] = h.t[2];
+      fused = a;
+      fused.t[3] = other;
+      fused.t[2] = h.t[2];
     } else {
       if (!other.same_shape(tmp)) continue;
-      Op fused;
       fused.kind = Kind::GeluBwd;
       fused.t[0] = a.t[0];
       fused.t[1] = other;
       fused.t[2] = h.t[2];
-      a = std::move(fused);
     }
-    h.dead = true;
+    h = std::move(fused);
+    a.dead = true;
     ++folded;
   }
   return folded;
@@ -702,14 +734,20 @@ void add_gradient_allreduce(std::vector<Op> &prog) {
 uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live) {
   g_live = live;
   uint64_t folded = 0;
-  folded += eliminate_common(prog);
-  folded += forward_copies(prog);
-  folded += fuse_weight_gradient(prog);
-  folded += fold_transposes(prog);
-  folded += fuse_gemm_epilogues(prog);
-  folded += fuse_softmax_backward(prog);
-  folded += fuse_rmsnorm_backward(prog);
-  folded += fuse_pointwise_backward(prog);
+  // Two rounds: fusion exposes further repeats (a repeated product whose
+  // transposed operand lived in a released temporary reads the weight itself
+  // once the transpose is folded), and removing repeats exposes fusions
+  // whose intermediate had several (repeated) readers.
+  for (int round = 0; round < 2; ++round) {
+    folded += eliminate_common(prog);
+    folded += forward_copies(prog);
+    folded += fuse_weight_gradient(prog);
+    folded += fold_transposes(prog);
+    folded += fuse_gemm_epilogues(prog);
+    folded += fuse_softmax_backward(prog);
+    folded += fuse_rmsnorm_backward(prog);
+    folded += fuse_pointwise_backward(prog);
+  }
   folded += fuse_step(prog);
   if (comm) add_gradient_allreduce(prog);
   g_live = nullptr;
