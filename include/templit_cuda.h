@@ -179,10 +179,19 @@ int tl_transpose(const float *x, const uint32_t *shape, int rank, int dim_a,
  * (src/my_metal/runtime.cpp:747-766; math.metal:857-882). */
 int tl_softmax_rows(const float *x, float *out, uint32_t rows, uint32_t cols,
                     void *stream);
-/* dx = y * (g - sum_row(g * y)): the SFTMX_DERIVATIVE rule
- * (include/passes/execute.h:291-308) in one pass. */
-int tl_softmax_backward_rows(const float *grad, const float *y, float *dx,
-                             uint32_t rows, uint32_t cols, void *stream);
+/* out = softmax(x / divisor[0] + mask[r % mask_rows, :]) (divisor and mask
+ * optional, mask of mask_rows x cols): the score chain of
+ * nn::MultiHeadAttention (include/nn/multi_head.h: divide by
+ * sqrt(HeadSize), add the causal mask, soft_max) in one pass, bit-identical
+ * to the three separate ops. */
+int tl_softmax_scaled_masked_rows(const float *x, const float *divisor, const float *mask,
+                                  uint32_t mask_rows, float *out, uint32_t rows,
+                                  uint32_t cols, void *stream);
+/* dx = y * (g - sum_row(g * y)) (then / divisor[0] when divisor is not
+ * NULL): the SFTMX_DERIVATIVE rule (include/passes/execute.h:291-308) in one
+ * pass, optionally with the derivative of the preceding score division. */
+int tl_softmax_backward_rows(const float *grad, const float *y, const float *divisor,
+                             float *dx, uint32_t rows, uint32_t cols, void *stream);
 /* rms[r] = sqrt(sum(x^2)/cols + 1e-6).  Replaces Runtime::RMS
  * (src/my_metal/runtime.cpp:1031-1059). */
 int tl_rms_rows(const float *x, float *rms, uint32_t rows, uint32_t cols,
@@ -191,10 +200,11 @@ int tl_rms_rows(const float *x, float *rms, uint32_t rows, uint32_t cols,
  * (src/my_metal/runtime.cpp:1061-1072). */
 int tl_rmsnorm_rows(const float *x, float *out, float *rms_out, uint32_t rows,
                     uint32_t cols, void *stream);
-/* dx = (g - y * mean(g * y)) / rms(x): the RMSN_DERIVATIVE rule
- * (include/passes/execute.h:330-356) in one pass. */
+/* dx = (g - y * mean(g * y)) / rms(x) (+ addend when not NULL; addend may
+ * equal dx): the RMSN_DERIVATIVE rule (include/passes/execute.h:330-356) in
+ * one pass, optionally with the residual gradient added after it. */
 int tl_rmsnorm_backward_rows(const float *grad, const float *x, const float *y,
-                             float *dx, uint32_t rows, uint32_t cols,
+                             const float *addend, float *dx, uint32_t rows, uint32_t cols,
                              void *stream);
 /* loss[r] = max + log(sum(exp(z - max))) - z[t]; +inf when t >= vocab.
  * Replaces Runtime::cross_entropy (src/my_metal/runtime.cpp:768-804; math.metal:884-910). */
@@ -291,7 +301,10 @@ enum tl_gemm_precision {
  * Runtime::mult (src/my_metal/runtime.cpp:375-505; math.metal:13-400) and,
  * through trans_a/trans_b, the executor's transpose+mult pairs of
  * EXPR_MULT_{LHS,RHS}_DERIVATIVE (include/passes/execute.h:187-232).
- * gelu_out (optional) receives GELU of the final value.
+ * gelu_out (optional) receives GELU of the final value.  addend (optional,
+ * C's layout) is added to the product: C = addend + (A*B + bias), the
+ * executor's add of a product into a gradient or residual stream folded
+ * into the epilogue; beta = 1 is the same with addend = C.
  */
 typedef struct tl_gemm_desc {
   const float *a;
@@ -314,6 +327,7 @@ typedef struct tl_gemm_desc {
    * runs unsplit, with the same result. */
   void *workspace;
   uint64_t workspace_bytes;
+  const float *addend;
 } tl_gemm_desc;
 int tl_gemm(const tl_gemm_desc *desc, void *stream);
 size_t tl_gemm_workspace_size(const tl_gemm_desc *desc);

@@ -45,7 +45,8 @@ class TlGemmDesc(Structure):
                 ("a_batch_stride", c_uint64 * TL_GEMM_MAX_BATCH_RANK),
                 ("b_batch_stride", c_uint64 * TL_GEMM_MAX_BATCH_RANK),
                 ("c_batch_stride", c_uint64 * TL_GEMM_MAX_BATCH_RANK),
-                ("workspace", c_void_p), ("workspace_bytes", c_uint64)]
+                ("workspace", c_void_p), ("workspace_bytes", c_uint64),
+                ("addend", c_void_p)]
 
 
 class TlgConfig(Structure):
@@ -101,12 +102,14 @@ CUDA_ABI = {
     "tl_argmax_workspace_size": (c_size_t, [c_size_t]),
     "tl_transpose": (c_int, [c_void_p, U32P, c_int, c_int, c_int, c_void_p, c_void_p]),
     "tl_softmax_rows": (c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_void_p]),
-    "tl_softmax_backward_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_uint32,
+    "tl_softmax_scaled_masked_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_uint32,
+                                              c_void_p, c_uint32, c_uint32, c_void_p]),
+    "tl_softmax_backward_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_uint32,
                                          c_uint32, c_void_p]),
     "tl_rms_rows": (c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_void_p]),
     "tl_rmsnorm_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_uint32,
                                 c_void_p]),
-    "tl_rmsnorm_backward_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p,
+    "tl_rmsnorm_backward_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                          c_uint32, c_uint32, c_void_p]),
     "tl_xent_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_void_p]),
     "tl_xent_backward_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_uint32,

@@ -12,6 +12,7 @@ struct GemmArgs {
   float *c;
   const float *bias;
   float *gelu_out;
+  const float *addend;  // C's layout; C itself when accumulating (beta = 1)
   uint32_t m, n, k;
   int trans_a, trans_b;
   float beta;
@@ -39,15 +40,15 @@ __device__ __forceinline__ void batch_offsets(const GemmArgs &g, uint64_t z,
   }
 }
 
-// Final value of C[idx] (idx relative to the batch's C base `Cb`, column n):
-// v = A*B (+ bias[n]) (+ C) - the reference adds the bias after the product
-// (EXPR_LINEAR: mult then add, include/passes/execute.h:241-252) and gradient
-// accumulation adds the new term to the old (context.h:74-89).
+// Final value of C[idx] (idx relative to the batch's C base, column n):
+// v = A*B (+ bias[n]) then addend + v - the reference adds the bias after
+// the product (EXPR_LINEAR: mult then add, include/passes/execute.h:241-252)
+// and gradient accumulation adds the new term to the old (context.h:74-89).
 __device__ __forceinline__ void epilogue_store(const GemmArgs &g, float *Cb,
                                                uint64_t oc, size_t idx,
                                                uint32_t n, float v) {
   if (g.bias) v = v + g.bias[n];
-  if (g.beta != 0.0f) v = Cb[idx] + v;
+  if (g.addend) v = g.addend[oc + idx] + v;
   Cb[idx] = v;
   if (g.gelu_out) g.gelu_out[oc + idx] = gelu_f(v);
 }

@@ -41,6 +41,9 @@ int to_args(const tl_gemm_desc *d, GemmArgs &g) {
   g.trans_a = d->trans_a != 0;
   g.trans_b = d->trans_b != 0;
   g.beta = d->beta;
+  if (d->addend && d->beta != 0.0f && d->addend != d->c)
+    return fail(TL_ERR_INVALID, "tl_gemm: addend with beta = 1 must be C");
+  g.addend = d->addend ? d->addend : (d->beta != 0.0f ? d->c : nullptr);
   g.batch_rank = d->batch_rank;
   g.batch_count = 1;
   for (uint32_t i = 0; i < d->batch_rank; ++i) {

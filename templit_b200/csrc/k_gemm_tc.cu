@@ -276,6 +276,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
       // (bias, accumulate and GELU in the same order as epilogue_store)
       const bool fast = (g.n % 4) == 0 && aligned16(Cb) &&
                         (raw || ((!g.bias || aligned16(g.bias)) &&
+                                 (!g.addend || aligned16(g.addend + oc)) &&
                                  (!g.gelu_out || aligned16(g.gelu_out + oc))));
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -296,8 +297,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                 const float4 b = *reinterpret_cast<const float4 *>(g.bias + n0 + 4 * j);
                 v = make_float4(v.x + b.x, v.y + b.y, v.z + b.z, v.w + b.w);
               }
-              if (g.beta != 0.0f) {
-                const float4 o = dst[j];
+              if (g.addend) {
+                const float4 o =
+                    *reinterpret_cast<const float4 *>(g.addend + oc + rowoff + n0 + 4 * j);
                 v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
               }
             }

@@ -103,10 +103,61 @@ softmax_kernel(const float *__restrict__ x, float *out, uint32_t rows,
   }
 }
 
-// dx = y * (g - sum(g*y))
+// out = softmax(x / divisor[0] + mask[row % mask_rows, :]): the attention
+// score chain of nn::MultiHeadAttention (divide by sqrt(head size), add the
+// causal mask, soft_max; include/nn/multi_head.h) in one pass.  Each element
+// is transformed exactly as the separate divide and add kernels would, in
+// the same per-lane order, so the result is bit-identical to the chain.
+__device__ __forceinline__ float score(float x, const float *dv, const float *mr, uint32_t c) {
+  if (dv) x = x / *dv;
+  if (mr) x = x + mr[c];
+  return x;
+}
+
+__global__ void __launch_bounds__(256)
+softmax_scaled_masked_kernel(const float *__restrict__ x, const float *__restrict__ divisor,
+                             const float *__restrict__ mask, uint32_t mask_rows, float *out,
+                             uint32_t rows, uint32_t cols, bool vec) {
+  ROW_LOOP {
+    const float *xr = x + static_cast<size_t>(row) * cols;
+    const float *mr = mask ? mask + static_cast<size_t>(row % mask_rows) * cols : nullptr;
+    float *yr = out + static_cast<size_t>(row) * cols;
+    float m = -INFINITY, s = 0.0f;
+    if (vec) {
+      for (uint32_t c = lane * 4; c < cols; c += 128) {
+        const float4 v = *reinterpret_cast<const float4 *>(xr + c);
+        online_add(m, s, score(v.x, divisor, mr, c));
+        online_add(m, s, score(v.y, divisor, mr, c + 1));
+        online_add(m, s, score(v.z, divisor, mr, c + 2));
+        online_add(m, s, score(v.w, divisor, mr, c + 3));
+      }
+    } else {
+      for (uint32_t c = lane; c < cols; c += 32) online_add(m, s, score(xr[c], divisor, mr, c));
+    }
+    warp_online(m, s);
+    if (vec) {
+      for (uint32_t c = lane * 4; c < cols; c += 128) {
+        float4 v = *reinterpret_cast<const float4 *>(xr + c);
+        v.x = expf(score(v.x, divisor, mr, c) - m) / s;
+        v.y = expf(score(v.y, divisor, mr, c + 1) - m) / s;
+        v.z = expf(score(v.z, divisor, mr, c + 2) - m) / s;
+        v.w = expf(score(v.w, divisor, mr, c + 3) - m) / s;
+        *reinterpret_cast<float4 *>(yr + c) = v;
+      }
+    } else {
+      for (uint32_t c = lane; c < cols; c += 32) yr[c] = expf(score(xr[c], divisor, mr, c) - m) / s;
+    }
+  }
+}
+
+// dx = y * (g - sum(g*y)) (then / divisor[0] when given: the derivative of
+// the score division that precedes the softmax, folded in)
+__device__ __forceinline__ float div_opt(float v, const float *d) { return d ? v / *d : v; }
+
 __global__ void __launch_bounds__(256)
 softmax_backward_kernel(const float *__restrict__ g, const float *__restrict__ y,
-                        float *dx, uint32_t rows, uint32_t cols, bool vec) {
+                        const float *__restrict__ divisor, float *dx, uint32_t rows,
+                        uint32_t cols, bool vec) {
   ROW_LOOP {
     const size_t off = static_cast<size_t>(row) * cols;
     const float dot = row_dot(g + off, y + off, cols, vec, lane);
@@ -115,14 +166,15 @@ softmax_backward_kernel(const float *__restrict__ g, const float *__restrict__ y
         const float4 gv = *reinterpret_cast<const float4 *>(g + off + c);
         const float4 yv = *reinterpret_cast<const float4 *>(y + off + c);
         float4 r;
-        r.x = yv.x * (gv.x - dot);
-        r.y = yv.y * (gv.y - dot);
-        r.z = yv.z * (gv.z - dot);
-        r.w = yv.w * (gv.w - dot);
+        r.x = div_opt(yv.x * (gv.x - dot), divisor);
+        r.y = div_opt(yv.y * (gv.y - dot), divisor);
+        r.z = div_opt(yv.z * (gv.z - dot), divisor);
+        r.w = div_opt(yv.w * (gv.w - dot), divisor);
         *reinterpret_cast<float4 *>(dx + off + c) = r;
       }
     } else {
-      for (uint32_t c = lane; c < cols; c += 32) dx[off + c] = y[off + c] * (g[off + c] - dot);
+      for (uint32_t c = lane; c < cols; c += 32)
+        dx[off + c] = div_opt(y[off + c] * (g[off + c] - dot), divisor);
     }
   }
 }
@@ -165,11 +217,13 @@ rmsnorm_kernel(const float *__restrict__ x, float *out, float *rms_out,
   }
 }
 
-// dx = (g - y * (sum(g*y)/D)) / rms(x)
+// dx = (g - y * (sum(g*y)/D)) / rms(x), plus addend when given (the
+// residual-stream gradient the executor adds next, folded in).  addend may
+// alias dx: each element is read before it is written by the same thread.
 __global__ void __launch_bounds__(256)
 rmsnorm_backward_kernel(const float *__restrict__ g, const float *__restrict__ x,
-                        const float *__restrict__ y, float *dx, uint32_t rows,
-                        uint32_t cols, bool vec) {
+                        const float *__restrict__ y, const float *addend, float *dx,
+                        uint32_t rows, uint32_t cols, bool vec) {
   ROW_LOOP {
     const size_t off = static_cast<size_t>(row) * cols;
     const float r = row_rms(x + off, cols, vec, lane);
@@ -183,11 +237,17 @@ rmsnorm_backward_kernel(const float *__restrict__ g, const float *__restrict__ x
         o.y = (gv.y - yv.y * mean) / r;
         o.z = (gv.z - yv.z * mean) / r;
         o.w = (gv.w - yv.w * mean) / r;
+        if (addend) {
+          const float4 a = *reinterpret_cast<const float4 *>(addend + off + c);
+          o = make_float4(a.x + o.x, a.y + o.y, a.z + o.z, a.w + o.w);
+        }
         *reinterpret_cast<float4 *>(dx + off + c) = o;
       }
     } else {
-      for (uint32_t c = lane; c < cols; c += 32)
-        dx[off + c] = (g[off + c] - y[off + c] * mean) / r;
+      for (uint32_t c = lane; c < cols; c += 32) {
+        const float o = (g[off + c] - y[off + c] * mean) / r;
+        dx[off + c] = addend ? addend[off + c] + o : o;
+      }
     }
   }
 }
@@ -274,12 +334,25 @@ int tl_softmax_rows(const float *x, float *out, uint32_t rows, uint32_t cols,
   return launch_status("tl_softmax_rows");
 }
 
-int tl_softmax_backward_rows(const float *grad, const float *y, float *dx,
-                             uint32_t rows, uint32_t cols, void *stream) {
+int tl_softmax_scaled_masked_rows(const float *x, const float *divisor, const float *mask,
+                                  uint32_t mask_rows, float *out, uint32_t rows,
+                                  uint32_t cols, void *stream) {
+  if (cols == 0) return fail(TL_ERR_INVALID, "softmax requires a non-empty final dimension");
+  if (rows == 0) return TL_OK;
+  if (!x || !out) return fail(TL_ERR_INVALID, "tl_softmax_scaled_masked_rows: null pointer");
+  if (mask && mask_rows == 0)
+    return fail(TL_ERR_INVALID, "tl_softmax_scaled_masked_rows: mask without rows");
+  softmax_scaled_masked_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
+      x, divisor, mask, mask_rows, out, rows, cols, row_vec(cols, {x, out, mask}));
+  return launch_status("tl_softmax_scaled_masked_rows");
+}
+
+int tl_softmax_backward_rows(const float *grad, const float *y, const float *divisor,
+                             float *dx, uint32_t rows, uint32_t cols, void *stream) {
   if (rows == 0 || cols == 0) return TL_OK;
   if (!grad || !y || !dx) return fail(TL_ERR_INVALID, "tl_softmax_backward_rows: null pointer");
   softmax_backward_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
-      grad, y, dx, rows, cols, row_vec(cols, {grad, y, dx}));
+      grad, y, divisor, dx, rows, cols, row_vec(cols, {grad, y, dx}));
   return launch_status("tl_softmax_backward_rows");
 }
 
@@ -304,13 +377,14 @@ int tl_rmsnorm_rows(const float *x, float *out, float *rms_out, uint32_t rows,
 }
 
 int tl_rmsnorm_backward_rows(const float *grad, const float *x, const float *y,
-                             float *dx, uint32_t rows, uint32_t cols, void *stream) {
+                             const float *addend, float *dx, uint32_t rows, uint32_t cols,
+                             void *stream) {
   if (rows == 0) return TL_OK;
   if (cols == 0) return fail(TL_ERR_INVALID, "tl_rmsnorm_backward_rows: empty rows");
   if (!grad || !x || !y || !dx)
     return fail(TL_ERR_INVALID, "tl_rmsnorm_backward_rows: null pointer");
   rmsnorm_backward_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
-      grad, x, y, dx, rows, cols, row_vec(cols, {grad, x, y, dx}));
+      grad, x, y, addend, dx, rows, cols, row_vec(cols, {grad, x, y, dx, addend}));
   return launch_status("tl_rmsnorm_backward_rows");
 }
 

@@ -26,8 +26,9 @@ Access access(const Op &op) {
   switch (op.kind) {
     case Kind::Binary: a.read(t[0]); a.read(t[1]); a.write(t[2]); break;
     case Kind::Scalar: case Kind::Unary: case Kind::Copy: case Kind::Reduce: case Kind::Argmax:
-    case Kind::Transpose: case Kind::Softmax: case Kind::Rms: case Kind::RmsNorm:
+    case Kind::Transpose: case Kind::Rms: case Kind::RmsNorm:
       a.read(t[0]); a.write(t[1]); break;
+    case Kind::Softmax: a.read(t[0]); a.read(t[2]); a.read(t[3]); a.write(t[1]); break;
     case Kind::Xent: a.read(t[0]); a.read(t[1]); a.write(t[2]); break;
     case Kind::XentBwd: a.read(t[0]); a.read(t[1]); a.read(t[3]); a.write(t[2]); break;
     case Kind::Gather: a.read(t[0]); a.read(t[1]); a.write(t[2]); break;
@@ -38,14 +39,15 @@ Access access(const Op &op) {
       for (int i : {0, 1, 3, 4, 5, 6, 7, 8}) a.read(t[i]);
       a.write(t[2]); a.write(t[3]); a.write(t[4]); break;
     case Kind::Gemm:
-      a.read(t[0]); a.read(t[1]); a.read(t[3]);
+      a.read(t[0]); a.read(t[1]); a.read(t[3]); a.read(t[5]);
       if (op.gemm.beta != 0.0f) a.read(t[2]);
       a.write(t[2]); a.write(t[4]); break;
     case Kind::HostWrite: case Kind::Fill: a.write(t[0]); break;
     case Kind::DevCopy: a.read(t[1]); a.write(t[0]); break;
     case Kind::GeluBwd: a.read(t[0]); a.read(t[1]); a.write(t[2]); break;
-    case Kind::SoftmaxBwd: a.read(t[0]); a.read(t[1]); a.write(t[2]); break;
-    case Kind::RmsNormBwd: a.read(t[0]); a.read(t[1]); a.read(t[2]); a.write(t[3]); break;
+    case Kind::SoftmaxBwd: a.read(t[0]); a.read(t[1]); a.read(t[3]); a.write(t[2]); break;
+    case Kind::RmsNormBwd:
+      a.read(t[0]); a.read(t[1]); a.read(t[2]); a.read(t[4]); a.write(t[3]); break;
     default: break;  // Release, MultiAdamW, AllReduce: handled by their passes
   }
   return a;
@@ -411,6 +413,189 @@ uint64_t fuse_pointwise_backward(std::vector<Op> &p) {
   return folded;
 }
 
+// Latest live op before j that writes `id` (kNone if none, or if the
+// allocation is released or an optimiser op intervenes first).
+size_t last_writer(const std::vector<Op> &p, size_t j, uint64_t id) {
+  for (size_t k = j; k-- > 0;) {
+    const Op &op = p[k];
+    if (op.dead) continue;
+    if (op.kind == Kind::Release) {
+      if (op.t[0].id == id) return kNone;
+      continue;
+    }
+    if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce) return kNone;
+    if (writes(access(op), id)) return k;
+  }
+  return kNone;
+}
+
+// True when no live op strictly between i and j reads, writes or releases id.
+bool untouched_between(const std::vector<Op> &p, size_t i, size_t j, uint64_t id) {
+  for (size_t k = i + 1; k < j; ++k) {
+    const Op &op = p[k];
+    if (op.dead) continue;
+    if (op.kind == Kind::Release) {
+      if (op.t[0].id == id) return false;
+      continue;
+    }
+    if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce) return false;
+    const Access a = access(op);
+    if (reads(a, id) || writes(a, id)) return false;
+  }
+  return true;
+}
+
+bool is_scalar_tensor(const TRef &t) { return t.p && t.numel() == 1; }
+
+// mult(...) -> P; add(A, P) -> O (either operand order) with the add the only
+// reader of P: the product is written to O with A added in the epilogue
+// (C = A + (A*B + bias), the add's own arithmetic).  The executor emits this
+// for every residual connection (the attention / FFN output added to the
+// stream) and for every gradient that sums contributions of several paths.
+uint64_t fuse_gemm_accumulate(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t j = 0; j < p.size(); ++j) {
+    Op &h = p[j];
+    if (h.dead || h.kind != Kind::Binary || h.code != TL_ADD) continue;
+    const TRef O = h.t[2];
+    for (int side = 0; side < 2; ++side) {
+      const TRef P = h.t[side], A = h.t[1 - side];
+      if (!P.p || !A.p || P.id == A.id || P.numel() != O.numel() || A.numel() != O.numel())
+        continue;
+      const size_t x = last_writer(p, j, P.id);
+      if (x == kNone) continue;
+      Op &mm = p[x];
+      if (mm.kind != Kind::Gemm || mm.gemm.beta != 0.0f || mm.gemm.gelu_out || mm.t[5].p ||
+          mm.t[2].id != P.id)
+        continue;
+      if (first_reader(p, x, P.id) != j || !dead_after(p, j, P.id)) continue;
+      if (!unchanged_between(p, x, j, A.id) || !untouched_between(p, x, j, O.id)) continue;
+      const Access ma = access(mm);
+      if (reads(ma, O.id)) continue;  // the product's operands must not be its output
+      mm.t[2].p = O.p;
+      mm.t[2].id = O.id;
+      mm.gemm.c = O.f();
+      if (A.id == O.id) {
+        mm.gemm.beta = 1.0f;  // accumulate in place: C = C + product
+      } else {
+        mm.t[5] = A;
+        mm.gemm.addend = A.f();
+      }
+      h.dead = true;
+      ++folded;
+      break;
+    }
+  }
+  return folded;
+}
+
+// softmax_backward(G, Y) -> T; divide(T, D[1]) -> O: the derivative of the
+// score division (divide by sqrt(head size)) folded into the row kernel.
+// rmsnorm_backward(G, X, Y) -> T; add(A, T) -> O: the residual-stream
+// gradient added in the same pass.  Both run at the second op's position.
+uint64_t fuse_row_backward_tails(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t i = 0; i < p.size(); ++i) {
+    Op &a = p[i];
+    if (a.dead) continue;
+    const bool sm = a.kind == Kind::SoftmaxBwd && !a.t[3].p;
+    const bool rn = a.kind == Kind::RmsNormBwd && !a.t[4].p;
+    if (!sm && !rn) continue;
+    const TRef T = sm ? a.t[2] : a.t[3];
+    const size_t j = first_reader(p, i, T.id);
+    if (j == kNone) continue;
+    Op &h = p[j];
+    if (h.kind != Kind::Binary || !dead_after(p, j, T.id)) continue;
+    const TRef O = h.t[2];
+    if (O.numel() != T.numel()) continue;
+    bool inputs_ok = true;
+    for (int k = 0; k < (sm ? 2 : 3); ++k)
+      if (!unchanged_between(p, i, j, a.t[k].id) || a.t[k].id == O.id) inputs_ok = false;
+    if (!inputs_ok) continue;
+    Op fused = a;
+    if (sm) {
+      if (h.code != TL_DIV || !same(h.t[0], T) || same(h.t[1], T) || !is_scalar_tensor(h.t[1]))
+        continue;
+      fused.t[2] = O;
+      fused.t[3] = h.t[1];
+    } else {
+      if (h.code != TL_ADD) continue;
+      const bool left = same(h.t[1], T) && !same(h.t[0], T);
+      const bool right = same(h.t[0], T) && !same(h.t[1], T);
+      if (!left && !right) continue;
+      const TRef A = left ? h.t[0] : h.t[1];
+      if (A.numel() != T.numel()) continue;
+      fused.t[3] = O;
+      fused.t[4] = A;
+    }
+    h = std::move(fused);
+    a.dead = true;
+    ++folded;
+  }
+  return folded;
+}
+
+// divide(S, D[1]) -> S1; add(S1, M) -> S2 (M broadcast over leading dims);
+// softmax(S2) -> P, with S1 and S2 read by nothing else: one softmax pass
+// that divides and adds the mask as it reads the scores
+// (nn::MultiHeadAttention, include/nn/multi_head.h).  Either step may be
+// absent.
+bool mask_broadcasts(const TRef &m, const TRef &s) {
+  int lead = 0;
+  while (lead < m.rank && m.shape[lead] == 1) ++lead;
+  const int tail = m.rank - lead;
+  if (tail < 1 || tail > s.rank) return false;
+  for (int d = 0; d < tail; ++d)
+    if (m.shape[lead + d] != s.shape[s.rank - tail + d]) return false;
+  return true;
+}
+
+uint64_t fuse_score_softmax(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t k = 0; k < p.size(); ++k) {
+    Op &sm = p[k];
+    if (sm.dead || sm.kind != Kind::Softmax || sm.t[2].p || sm.t[3].p) continue;
+    TRef X = sm.t[0];
+    TRef D{}, M{};
+    std::vector<size_t> gone;
+    // optional mask add
+    size_t j = last_writer(p, k, X.id);
+    if (j != kNone && p[j].kind == Kind::Binary && p[j].code == TL_ADD) {
+      const Op &ad = p[j];
+      for (int side = 0; side < 2; ++side) {
+        const TRef S1 = ad.t[side], m = ad.t[1 - side];
+        if (S1.numel() == X.numel() && m.numel() < X.numel() && m.last() == X.last() &&
+            mask_broadcasts(m, X) && first_reader(p, j, X.id) == k && dead_after(p, k, X.id) &&
+            unchanged_between(p, j, k, m.id)) {
+          M = m;
+          gone.push_back(j);
+          X = S1;
+          break;
+        }
+      }
+    }
+    // optional division by a one-element tensor
+    const size_t end = gone.empty() ? k : gone.back();
+    size_t i = last_writer(p, end, X.id);
+    if (i != kNone && p[i].kind == Kind::Binary && p[i].code == TL_DIV &&
+        is_scalar_tensor(p[i].t[1]) && !same(p[i].t[1], X) && p[i].t[0].numel() == X.numel() &&
+        first_reader(p, i, X.id) == end && dead_after(p, end, X.id) &&
+        unchanged_between(p, i, k, p[i].t[0].id) && unchanged_between(p, i, k, p[i].t[1].id)) {
+      D = p[i].t[1];
+      X = p[i].t[0];
+      gone.push_back(i);
+    }
+    if (gone.empty() || X.id == sm.t[1].id) continue;
+    if (!unchanged_between(p, gone.back(), k, X.id)) continue;
+    sm.t[0] = X;
+    sm.t[2] = D;
+    sm.t[3] = M;
+    for (size_t g : gone) p[g].dead = true;
+    folded += gone.size();
+  }
+  return folded;
+}
+
 // --------------------------------------------------------- copy forwarding
 bool elementwise(Kind k) {
   return k == Kind::Binary || k == Kind::Scalar || k == Kind::Unary || k == Kind::Copy ||
@@ -429,18 +614,20 @@ void retarget_reads(Op &op, const TRef &from, const TRef &to) {
   auto &t = op.t;
   switch (op.kind) {
     case Kind::Binary: case Kind::Xent: case Kind::Gather: case Kind::GeluBwd:
-    case Kind::SoftmaxBwd:
       swap(t[0]); swap(t[1]); break;
+    case Kind::SoftmaxBwd: swap(t[0]); swap(t[1]); swap(t[3]); break;
+    case Kind::Softmax: swap(t[0]); swap(t[2]); swap(t[3]); break;
     case Kind::XentBwd: swap(t[0]); swap(t[1]); swap(t[3]); break;
     case Kind::Scatter: swap(t[0]); swap(t[1]); swap(t[2]); break;
     case Kind::Clip: swap(t[0]); swap(t[1]); break;
-    case Kind::RmsNormBwd: swap(t[0]); swap(t[1]); swap(t[2]); break;
+    case Kind::RmsNormBwd: swap(t[0]); swap(t[1]); swap(t[2]); swap(t[4]); break;
     case Kind::DevCopy: swap(t[1]); break;
     case Kind::Gemm:
-      swap(t[0]); swap(t[1]); swap(t[3]);
+      swap(t[0]); swap(t[1]); swap(t[3]); swap(t[5]);
       op.gemm.a = static_cast<const float *>(t[0].p);
       op.gemm.b = static_cast<const float *>(t[1].p);
       op.gemm.bias = t[3].p ? t[3].f() : nullptr;
+      op.gemm.addend = t[5].p ? t[5].f() : nullptr;
       break;
     default: swap(t[0]); break;  // single-input kinds
   }
@@ -501,6 +688,66 @@ uint64_t forward_copies(std::vector<Op> &p) {
     const TRef S = cp.t[0], T = cp.t[1];
     if (!S.p || !T.p || S.id == T.id || S.numel() != T.numel()) continue;
     if (!forward_value(p, i, T, S)) continue;
+    cp.dead = true;
+    ++folded;
+  }
+  return folded;
+}
+
+// Output slot of the ops whose single result may be redirected (-1: none).
+int output_slot(const Op &op) {
+  switch (op.kind) {
+    case Kind::Scalar: case Kind::Unary: case Kind::Copy: case Kind::Reduce: case Kind::Argmax:
+    case Kind::Transpose: case Kind::Softmax: case Kind::Rms: case Kind::RmsNorm:
+      return 1;
+    case Kind::Binary: case Kind::Xent: case Kind::XentBwd: case Kind::Gather: case Kind::Clip:
+    case Kind::GeluBwd: case Kind::SoftmaxBwd: case Kind::Gemm:
+      return 2;
+    case Kind::Scatter: case Kind::RmsNormBwd:
+      return 3;
+    default:
+      return -1;
+  }
+}
+
+// copy(S -> G) where S was just produced for the copy: the producer writes G
+// itself and the copy goes.  The executor accumulates every first gradient
+// contribution by copying the freshly computed term into the gradient
+// buffer (include/passes/context.h accumulate_grad); the weight-gradient
+// product and bias-gradient sum now land in the gradient buffer directly.
+uint64_t forward_producers(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t c = 0; c < p.size(); ++c) {
+    Op &cp = p[c];
+    if (cp.dead || cp.kind != Kind::Copy) continue;
+    const TRef S = cp.t[0], G = cp.t[1];
+    if (!S.p || !G.p || S.id == G.id || S.numel() != G.numel()) continue;
+    // the producer: latest live op before the copy that touches S or G
+    size_t x = kNone;
+    for (size_t k = c; k-- > 0;) {
+      const Op &op = p[k];
+      if (op.dead) continue;
+      if (op.kind == Kind::Release) {
+        if (op.t[0].id == S.id || op.t[0].id == G.id) break;
+        continue;
+      }
+      if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce) break;
+      const Access a = access(op);
+      if (reads(a, G.id) || writes(a, G.id) || reads(a, S.id)) break;
+      if (writes(a, S.id)) {
+        x = k;
+        break;
+      }
+    }
+    if (x == kNone) continue;
+    Op &prod = p[x];
+    const int slot = output_slot(prod);
+    if (slot < 0 || prod.t[slot].id != S.id || !full_write(prod)) continue;
+    if (prod.kind == Kind::Gemm && prod.gemm.beta != 0.0f) continue;
+    if (!dead_after(p, c, S.id)) continue;
+    prod.t[slot].p = G.p;
+    prod.t[slot].id = G.id;
+    if (prod.kind == Kind::Gemm) prod.gemm.c = G.f();
     cp.dead = true;
     ++folded;
   }
@@ -741,6 +988,7 @@ uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live) {
   for (int round = 0; round < 2; ++round) {
     folded += eliminate_common(prog);
     folded += forward_copies(prog);
+    folded += forward_producers(prog);
     folded += fuse_weight_gradient(prog);
     folded += fold_transposes(prog);
     folded += fuse_gemm_epilogues(prog);
@@ -748,6 +996,11 @@ uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live) {
     folded += fuse_rmsnorm_backward(prog);
     folded += fuse_pointwise_backward(prog);
   }
+  // Folds that change an op's inputs (an added operand, a divisor) come last
+  // so they cannot hide a repeat from the common-subexpression pass.
+  folded += fuse_gemm_accumulate(prog);
+  folded += fuse_row_backward_tails(prog);
+  folded += fuse_score_softmax(prog);
   folded += fuse_step(prog);
   if (comm) add_gradient_allreduce(prog);
   g_live = nullptr;

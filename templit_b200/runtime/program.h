@@ -47,7 +47,7 @@ enum class Kind : uint8_t {
   Reduce,      // code = tl_reduce_op; t0 x, t1 out
   Argmax,      // t0 x, t1 out index
   Transpose,   // t0 x, t1 out, i0 dim_a, i1 dim_b
-  Softmax,     // t0 x, t1 out
+  Softmax,     // t0 x, t1 out (+ t2 divisor [1], t3 mask [r, cols] added per row r % rows)
   Rms,         // t0 x, t1 rms
   RmsNorm,     // t0 x, t1 out
   Xent,        // t0 logits, t1 targets, t2 loss
@@ -57,7 +57,7 @@ enum class Kind : uint8_t {
   SqNorm,      // t0 gradient, t1 sqnorm
   Clip,        // t0 gradient, t1 sqnorm, t2 out, f0 max_norm
   AdamW,       // t0 param, t1 grad, t2 out, t3 m1, t4 m2, t5 b1, t6 b2, t7 decay, t8 lr; f0 eps, u0 step
-  Gemm,        // gemm descriptor; t0 a, t1 b, t2 c (+ t3 bias, t4 gelu out)
+  Gemm,        // gemm descriptor; t0 a, t1 b, t2 c (+ t3 bias, t4 gelu out, t5 addend)
   // Storage data movement inside the window
   HostWrite,   // t0 dst (rank 1 byte view), u64 offset, host payload
   Fill,        // t0 dst, u0 pattern, n elements
@@ -65,8 +65,8 @@ enum class Kind : uint8_t {
   Release,     // t0: allocation id released here (no launch)
   // produced by the optimiser
   GeluBwd,     // t0 x, t1 grad, t2 out
-  SoftmaxBwd,  // t0 grad, t1 y, t2 out
-  RmsNormBwd,  // t0 grad, t1 x, t2 y, t3 out
+  SoftmaxBwd,  // t0 grad, t1 y, t2 out (+ t3 divisor [1])
+  RmsNormBwd,  // t0 grad, t1 x, t2 y, t3 out (+ t4 addend)
   MultiAdamW,  // slots in `multi`; t0 sqnorm (optional); f0 max_norm; f1 eps; t5..t8 scalars
   AllReduce,   // NCCL sum of the gradients in `multi`
 };

@@ -342,9 +342,16 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
               "transpose");
         break;
       case Kind::Softmax:
-        check(tl_softmax_rows(t[0].f(), t[1].f(), static_cast<uint32_t>(t[0].numel() / t[0].last()),
-                              t[0].last(), s),
-              "softmax");
+        if (t[2].p || t[3].p)
+          check(tl_softmax_scaled_masked_rows(
+                    t[0].f(), t[2].p ? t[2].f() : nullptr, t[3].p ? t[3].f() : nullptr,
+                    t[3].p ? static_cast<uint32_t>(t[3].numel() / t[0].last()) : 0u, t[1].f(),
+                    static_cast<uint32_t>(t[0].numel() / t[0].last()), t[0].last(), s),
+                "softmax");
+        else
+          check(tl_softmax_rows(t[0].f(), t[1].f(),
+                                static_cast<uint32_t>(t[0].numel() / t[0].last()), t[0].last(), s),
+                "softmax");
         break;
       case Kind::Rms:
         check(tl_rms_rows(t[0].f(), t[1].f(), static_cast<uint32_t>(t[0].numel() / t[0].last()),
@@ -413,13 +420,14 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
         check(tl_gelu_backward(t[0].f(), t[1].f(), t[2].f(), t[2].numel(), s), "GELU backward");
         break;
       case Kind::SoftmaxBwd:
-        check(tl_softmax_backward_rows(t[0].f(), t[1].f(), t[2].f(),
+        check(tl_softmax_backward_rows(t[0].f(), t[1].f(), t[3].p ? t[3].f() : nullptr, t[2].f(),
                                        static_cast<uint32_t>(t[2].numel() / t[2].last()),
                                        t[2].last(), s),
               "softmax backward");
         break;
       case Kind::RmsNormBwd:
-        check(tl_rmsnorm_backward_rows(t[0].f(), t[1].f(), t[2].f(), t[3].f(),
+        check(tl_rmsnorm_backward_rows(t[0].f(), t[1].f(), t[2].f(), t[4].p ? t[4].f() : nullptr,
+                                       t[3].f(),
                                        static_cast<uint32_t>(t[3].numel() / t[3].last()),
                                        t[3].last(), s),
               "RMSNorm backward");

@@ -373,6 +373,74 @@ void common_kept_when_input_changes() {
   require(optimize(q, nullptr) == 1, "repeat into the same buffer folded");
 }
 
+
+// residual add of a product: the add moves into the GEMM epilogue
+void residual_add_into_gemm() {
+  auto x = tensor({12288, 384}), w = tensor({384, 384}), p0 = tensor({12288, 384});
+  auto r = tensor({12288, 384}), o = tensor({12288, 384});
+  std::vector<Op> p = {gemm(x, w, p0, 12288, 384, 384), binary(TL_ADD, r, p0, o), release(p0)};
+  require(optimize(p, nullptr) == 1, "add folded");
+  auto v = live(p);
+  require(v.size() == 1 && v[0]->t[2].id == o.id && v[0]->gemm.addend == r.p &&
+              v[0]->gemm.beta == 0.0f,
+          "product written to the sum with the residual as addend");
+  // in place: acc = acc + product
+  auto acc = tensor({12288, 384}), p1 = tensor({12288, 384});
+  std::vector<Op> q = {gemm(x, w, p1, 12288, 384, 384), binary(TL_ADD, acc, p1, acc),
+                       release(p1)};
+  require(optimize(q, nullptr) == 1, "accumulate folded");
+  auto u = live(q);
+  require(u.size() == 1 && u[0]->t[2].id == acc.id && u[0]->gemm.beta == 1.0f &&
+              !u[0]->gemm.addend,
+          "accumulated in place");
+  // the product is read again: kept
+  auto p2 = tensor({12288, 384}), o2 = tensor({12288, 384}), z = tensor({12288, 384});
+  std::vector<Op> k = {gemm(x, w, p2, 12288, 384, 384), binary(TL_ADD, r, p2, o2),
+                       binary(TL_MUL, p2, p2, z), release(p2)};
+  require(optimize(k, nullptr) == 0, "product still read: kept");
+}
+
+// divide by sqrt(d), add the causal mask, softmax: one softmax op
+void attention_scores_into_softmax() {
+  auto sc = tensor({64, 6, 192, 192}), d = tensor({1, 1}), s1 = tensor({64, 6, 192, 192});
+  auto m = tensor({1, 1, 192, 192}), s2 = tensor({64, 6, 192, 192}), pr = tensor({64, 6, 192, 192});
+  Op sm = op(Kind::Softmax);
+  sm.t[0] = s2;
+  sm.t[1] = pr;
+  std::vector<Op> p = {binary(TL_DIV, sc, d, s1), binary(TL_ADD, s1, m, s2), sm, release(s2),
+                       release(s1)};
+  require(optimize(p, nullptr) == 2, "divide and mask folded");
+  auto v = live(p);
+  require(v.size() == 1 && v[0]->kind == Kind::Softmax && v[0]->t[0].id == sc.id &&
+              v[0]->t[2].id == d.id && v[0]->t[3].id == m.id,
+          "softmax reads the raw scores, divisor and mask");
+}
+
+// softmax backward then divide; RMSNorm backward then residual add
+void row_backward_tails() {
+  auto g = tensor({64, 6, 192, 192}), y = tensor({64, 6, 192, 192}), t = tensor({64, 6, 192, 192});
+  auto d = tensor({1, 1}), o = tensor({64, 6, 192, 192});
+  Op sb = op(Kind::SoftmaxBwd);
+  sb.t[0] = g;
+  sb.t[1] = y;
+  sb.t[2] = t;
+  std::vector<Op> p = {sb, binary(TL_DIV, t, d, o), release(t)};
+  require(optimize(p, nullptr) == 1, "divide folded");
+  auto v = live(p);
+  require(v.size() == 1 && v[0]->t[2].id == o.id && v[0]->t[3].id == d.id, "divisor attached");
+  auto gr = tensor({12288, 384}), x = tensor({12288, 384}), yn = tensor({12288, 384});
+  auto tr = tensor({12288, 384}), a = tensor({12288, 384});
+  Op rb = op(Kind::RmsNormBwd);
+  rb.t[0] = gr;
+  rb.t[1] = x;
+  rb.t[2] = yn;
+  rb.t[3] = tr;
+  std::vector<Op> q = {rb, binary(TL_ADD, a, tr, a), release(tr)};
+  require(optimize(q, nullptr) == 1, "residual gradient folded");
+  auto u = live(q);
+  require(u.size() == 1 && u[0]->t[3].id == a.id && u[0]->t[4].id == a.id, "added in place");
+}
+
 }  // namespace
 
 int main() {
@@ -393,6 +461,9 @@ int main() {
       {"copy_kept_when_source_changes", copy_kept_when_source_changes},
       {"common_gemm_evaluated_once", common_gemm_evaluated_once},
       {"common_kept_when_input_changes", common_kept_when_input_changes},
+      {"residual_add_into_gemm", residual_add_into_gemm},
+      {"attention_scores_into_softmax", attention_scores_into_softmax},
+      {"row_backward_tails", row_backward_tails},
   };
   for (const auto &[name, fn] : cases) {
     try {

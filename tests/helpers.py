@@ -132,12 +132,46 @@ class Dev:
             out = self.empty(x.shape[:-1] + (1,))
         else:
             out = self.empty(x.shape)
-        args = [self.p(t) for t in ts] + [self.p(out)]
+        args = [self.p(t) for t in ts]
+        if name in ("softmax_bwd", "rmsnorm_bwd"):
+            args.append(ctypes.c_void_p(0))  # no divisor / addend
+        args.append(self.p(out))
         if name == "rmsnorm":
             args.append(ctypes.c_void_p(0))
         self.call({"softmax": "tl_softmax_rows", "softmax_bwd": "tl_softmax_backward_rows",
                    "rms": "tl_rms_rows", "rmsnorm": "tl_rmsnorm_rows",
                    "rmsnorm_bwd": "tl_rmsnorm_backward_rows"}[name], *args, rows, cols, self.stream)
+        return self.host(out)
+
+    def softmax_scaled_masked(self, x, divisor=None, mask=None):
+        x = np.asarray(x, np.float32)
+        cols = x.shape[-1]
+        tx = self.t(x)
+        td = self.t(np.asarray([divisor], np.float32)) if divisor is not None else None
+        tm = self.t(np.asarray(mask, np.float32)) if mask is not None else None
+        mask_rows = (np.asarray(mask).size // cols) if mask is not None else 0
+        out = self.empty(x.shape)
+        self.call("tl_softmax_scaled_masked_rows", self.p(tx), self.p(td), self.p(tm), mask_rows,
+                  self.p(out), x.size // cols, cols, self.stream)
+        return self.host(out)
+
+    def softmax_bwd_div(self, g, y, divisor):
+        g = np.asarray(g, np.float32)
+        cols = g.shape[-1]
+        tg, ty = self.t(g), self.t(y)
+        td = self.t(np.asarray([divisor], np.float32))
+        out = self.empty(g.shape)
+        self.call("tl_softmax_backward_rows", self.p(tg), self.p(ty), self.p(td), self.p(out),
+                  g.size // cols, cols, self.stream)
+        return self.host(out)
+
+    def rmsnorm_bwd_add(self, g, x, y, addend, in_place=False):
+        g = np.asarray(g, np.float32)
+        cols = g.shape[-1]
+        tg, tx, ty, ta = self.t(g), self.t(x), self.t(y), self.t(addend)
+        out = ta if in_place else self.empty(g.shape)
+        self.call("tl_rmsnorm_backward_rows", self.p(tg), self.p(tx), self.p(ty), self.p(ta),
+                  self.p(out), g.size // cols, cols, self.stream)
         return self.host(out)
 
     def xent(self, logits, targets, backward=False, row_scale=None):
@@ -179,7 +213,7 @@ class Dev:
         return self.host(out)
 
     def gemm(self, a, b, trans_a=False, trans_b=False, bias=None, c=None, beta=0.0, gelu=False,
-             precision=capi.TL_GEMM_TF32):
+             precision=capi.TL_GEMM_TF32, addend=None):
         a = np.asarray(a, np.float32)
         b = np.asarray(b, np.float32)
         ta, tb = self.t(a), self.t(b)
@@ -192,7 +226,10 @@ class Dev:
             else self.empty(out_shape)
         tg = self.empty(out_shape) if gelu else None
         tbias = self.t(bias) if bias is not None else None
+        tadd = self.t(np.broadcast_to(np.asarray(addend, np.float32), out_shape)) \
+            if addend is not None else None
         d = capi.TlGemmDesc()
+        d.addend = tadd.data_ptr() if tadd is not None else None
         d.a, d.b, d.c = ta.data_ptr(), tb.data_ptr(), tc.data_ptr()
         d.bias = tbias.data_ptr() if tbias is not None else None
         d.gelu_out = tg.data_ptr() if tg is not None else None

@@ -136,7 +136,21 @@ def test_epilogues(dev):
     check_tf32(g, ops.gelu(want))
     acc = dev.gemm(a, b, c=c0, beta=1.0)
     check_tf32(acc, ops.gemm(a, b, c=c0, beta=1.0))
+    # addend (a residual or gradient added to the product): bit-identical to
+    # the product followed by the separate add kernel
+    prod = dev.gemm(a, b, bias=bias)
+    np.testing.assert_array_equal(dev.gemm(a, b, bias=bias, addend=c0),
+                                  dev.binary("add", c0, prod, prod.shape))
+    k_long = r.standard_normal((12288, 64)).astype(np.float32)  # split-K path
+    g_long = r.standard_normal((12288, 96)).astype(np.float32)
+    add = r.standard_normal((64, 96)).astype(np.float32)
+    prod = dev.gemm(k_long, g_long, trans_a=True)
+    np.testing.assert_array_equal(dev.gemm(k_long, g_long, trans_a=True, addend=add),
+                                  dev.binary("add", add, prod, prod.shape))
     out32, g32 = dev.gemm(a[:64], b, bias=bias, gelu=True, precision=capi.TL_GEMM_FP32)
+    np.testing.assert_array_equal(dev.gemm(a[:64], b, bias=bias, addend=c0[:64],
+                                           precision=capi.TL_GEMM_FP32),
+                                  dev.binary("add", c0[:64], out32, out32.shape))
     np.testing.assert_allclose(out32, ops.gemm(a[:64], b, bias=bias), rtol=1e-4, atol=1e-3)
     np.testing.assert_allclose(g32, ops.gelu(ops.gemm(a[:64], b, bias=bias)), rtol=1e-4, atol=1e-3)
 

@@ -218,6 +218,45 @@ def test_softmax_and_backward(dev, rows, cols):
     close(dev.rows("softmax_bwd", g, y), ops.softmax_backward(g, y), rtol=1e-5, atol=1e-6)
 
 
+@pytest.mark.parametrize("rows,cols", [(73728, 192), (40, 37), (6, 5000)])
+def test_softmax_scaled_masked_is_the_op_chain(dev, rows, cols):
+    """Fused divide + mask add + softmax equals the three separate kernels
+    bit for bit (same per-element arithmetic, same reduction order)."""
+    r = rng(17)
+    x = (r.standard_normal((rows, cols)) * 6).astype(np.float32)
+    t = 192 if rows % 192 == 0 and cols == 192 else 4
+    mask = np.triu(np.full((t, cols), -np.inf, np.float32), 1) if rows % t == 0 else None
+    d = np.float32(8.0)
+    fused = dev.softmax_scaled_masked(x, d, mask)
+    s1 = dev.binary("div", x, np.full((1, 1), d, np.float32), x.shape)
+    if mask is not None:
+        s1 = dev.binary("add", s1.reshape(rows // t, t, cols), mask.reshape(1, t, cols),
+                        (rows // t, t, cols)).reshape(rows, cols)
+    chain = dev.rows("softmax", s1)
+    np.testing.assert_array_equal(fused, chain)
+    want = ops.softmax_rows(x.astype(np.float64) / 8.0 + (np.tile(mask, (rows // t, 1)) if mask is not None else 0))
+    close(fused, want, rtol=1e-5, atol=1e-7)
+
+
+def test_softmax_backward_divisor_and_rmsnorm_backward_addend(dev):
+    r = rng(18)
+    x = (r.standard_normal((384, 192)) * 3).astype(np.float32)
+    y = ops.softmax_rows(x).astype(np.float32)
+    g = r.standard_normal((384, 192)).astype(np.float32)
+    plain = dev.rows("softmax_bwd", g, y)
+    np.testing.assert_array_equal(dev.softmax_bwd_div(g, y, 8.0),
+                                  dev.binary("div", plain, np.full((1, 1), 8.0, np.float32),
+                                             plain.shape))
+    x = r.standard_normal((96, 384)).astype(np.float32)
+    yn = ops.rmsnorm(x).astype(np.float32)
+    g = r.standard_normal((96, 384)).astype(np.float32)
+    a = r.standard_normal((96, 384)).astype(np.float32)
+    plain = dev.rows("rmsnorm_bwd", g, x, yn)
+    want = dev.binary("add", a, plain, a.shape)
+    np.testing.assert_array_equal(dev.rmsnorm_bwd_add(g, x, yn, a), want)
+    np.testing.assert_array_equal(dev.rmsnorm_bwd_add(g, x, yn, a, in_place=True), want)
+
+
 def test_softmax_masked_rows(dev):
     x = np.array([[0.0, -np.inf, -np.inf], [1000, 1001, -np.inf]], np.float32)
     close(dev.rows("softmax", x), ops.softmax_rows(x), atol=1e-7)
