@@ -284,12 +284,12 @@ def main():
             ms = float(t.item())
         return ms
 
-    stats0 = (ctypes.c_uint64 * 8)()
+    stats0 = (ctypes.c_uint64 * 11)()
     capi.check(lib.tlg_stats(h, stats0), lib, "stats")
     with ClockSampler(local) as clocks:
         ms_value = timed(with_host_io=False)
         ms_e2e = timed(with_host_io=True)
-    stats1 = (ctypes.c_uint64 * 8)()
+    stats1 = (ctypes.c_uint64 * 11)()
     capi.check(lib.tlg_stats(h, stats1), lib, "stats")
     kernels = int(stats1[3] - stats0[3]) // 2  # two timed regions of K steps each
 
@@ -336,7 +336,10 @@ def main():
         "runtime": {"windows": int(stats1[0]), "ops_recorded": int(stats1[1]),
                     "ops_launched": int(stats1[2]), "graph_replays": int(stats1[4]),
                     "graph_captures": int(stats1[5]), "fused_ops": int(stats1[6]),
-                    "peak_device_bytes": int(stats1[7])},
+                    "peak_device_bytes": int(stats1[7]),
+                    "host_ms_per_step": round((stats1[8] + stats1[9] - stats0[8] - stats0[9])
+                                              / 2e6 / args.steps, 3),
+                    "optimiser_cache_hits": int(stats1[10])},
     }
     print(json.dumps(line))
     return 0

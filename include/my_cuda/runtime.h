@@ -41,6 +41,9 @@ struct RuntimeStats {
   uint64_t graph_replays = 0;   // programs served by replaying a captured graph
   uint64_t graph_captures = 0;  // graphs captured
   uint64_t fused_ops = 0;       // recorded ops folded into fused kernels
+  uint64_t host_record_ns = 0;  // host time from start() to submit(), in total
+  uint64_t host_submit_ns = 0;  // host time inside submit() (optimise + launch), in total
+  uint64_t optimiser_cache_hits = 0;  // programs whose optimised form was reused
 };
 
 class Runtime {

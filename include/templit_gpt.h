@@ -55,8 +55,12 @@ int tlg_get_params(void *handle, float *out, uint64_t count);
 int tlg_set_params(void *handle, const float *in, uint64_t count);
 /* The backend stream (cudaStream_t) every launch of this handle uses. */
 void *tlg_stream(void *handle);
-/* Runtime counters: windows, recorded ops, launched ops, kernels, graph replays. */
-int tlg_stats(void *handle, uint64_t out[8]);
+/* Runtime counters: [0] windows, [1] recorded ops, [2] launched ops,
+ * [3] kernels, [4] graph replays, [5] graph captures, [6] fused ops,
+ * [7] peak device bytes, [8] host ns recording, [9] host ns in submit,
+ * [10] optimiser cache hits (totals since creation). */
+#define TLG_STATS 11
+int tlg_stats(void *handle, uint64_t out[TLG_STATS]);
 /* Data parallelism: NCCL unique id (128 bytes) made on rank 0 and shared
  * by the caller, then a communicator on every rank. */
 int tlg_nccl_unique_id(uint8_t id[128]);

@@ -47,15 +47,24 @@ struct TcArgs {
   // and a second kernel sums the slices in order and applies the epilogue.
   uint32_t splits, kb_per_split;
   float *partial;
+  // epilogue through shared memory and TMA stores (C, or the split-K
+  // partials, dense per matrix with rows of a multiple of 16 bytes)
+  bool tma_epi;
+  uint64_t c_mat;  // elements per C matrix
 };
 
 template <int BN>
 struct Cfg {
   static constexpr uint32_t B_BYTES = BN * BK * 4;
   static constexpr uint32_t STAGE_BYTES = kA_BYTES + B_BYTES;
-  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
-  static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
-  static constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + 256;
+  static constexpr int STAGES = BN >= 192 ? 4 : (BN == 128 ? 6 : 8);
+  // second accumulator at a power-of-two column; allocation a power of two
+  static constexpr uint32_t ACC_COLS = BN == 192 ? 256 : BN;
+  static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS < 32 ? 32 : 2 * ACC_COLS;
+  // per epilogue warp two 32 x 32 fp32 staging boxes (4 KB each, 128-byte
+  // swizzled rows) for the TMA stores
+  static constexpr uint32_t OUT_BYTES = 4 * 2 * 4096;
+  static constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + OUT_BYTES + 256;
 };
 
 // tile = ((z * splits + s) * nt + nb) * mt + mb: consecutive CTAs take
@@ -77,21 +86,31 @@ __device__ __forceinline__ void k_range(const TcArgs &t, uint32_t ktiles, uint32
   kb1 = min(ktiles, kb0 + t.kb_per_split);
 }
 
+// Byte offset of 16-byte group j of row r in a 128-byte-swizzled box.
+__device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t j) {
+  return r * 128u + ((j ^ (r & 7u)) << 4);
+}
+
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-               const __grid_constant__ CUtensorMap tmB, const TcArgs t) {
+               const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmC,
+               const __grid_constant__ CUtensorMap tmG,
+               const __grid_constant__ CUtensorMap tmD, const TcArgs t) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t *stage_base = smem;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
+  uint8_t *out_base = smem + C::STAGES * C::STAGE_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(out_base + C::OUT_BYTES);
   uint64_t *full = bars;
   uint64_t *empty = bars + C::STAGES;
   uint64_t *tfull = bars + 2 * C::STAGES;
   uint64_t *tempty = tfull + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+  uint64_t *abar = tempty + 2;  // one per epilogue warp: addend box loaded
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(abar + 4);
   volatile uint32_t *abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -106,11 +125,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
       ptx::mbar_init(&tfull[a], 1);
       ptx::mbar_init(&tempty[a], 128);
     }
+    for (int w = 0; w < 4; ++w) ptx::mbar_init(&abar[w], 1);
     *abort_flag = 0;
     ptx::fence_barrier_init();
     ptx::fence_proxy_async_smem();
     ptx::prefetch_tensormap(&tmA);
     ptx::prefetch_tensormap(&tmB);
+    if (t.tma_epi) ptx::prefetch_tensormap(&tmC);
   }
   if (warp == 1) {
     ptx::tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -202,7 +223,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * C::ACC_COLS;
         bool ok = true;
         uint64_t z;
         uint32_t s, mb, nb, kb0, kb1;
@@ -251,6 +272,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
     // ------------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     uint32_t acc = 0, acc_phase = 0;
+    uint8_t *obuf = out_base + (warp - 2) * 8192;  // this warp's two staging boxes
+    uint32_t nbuf = 0, a_phase = 0;
+    uint64_t *my_abar = &abar[warp - 2];
     for (uint64_t tile = blockIdx.x; tile < t.num_tiles; tile += gridDim.x) {
       // warp-uniform decisions: tcgen05.ld below needs all 32 lanes
       const bool got = ptx::mbar_wait_bounded(&tfull[acc], acc_phase, kWaitLimitNs);
@@ -278,10 +302,93 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         (raw || ((!g.bias || aligned16(g.bias)) &&
                                  (!g.addend || aligned16(g.addend + oc)) &&
                                  (!g.gelu_out || aligned16(g.gelu_out + oc))));
+      if (t.tma_epi) {
+        // Each chunk of 32 columns: TMEM -> registers (+ bias, + addend box
+        // loaded by TMA into the staging box) -> swizzled staging box -> TMA
+        // store of the 32 x 32 box (rows and columns past M, N are clipped).
+        // Two boxes per warp alternate so one store is always in flight.
+        const int32_t y0 = static_cast<int32_t>(mb * BM + q * 32);
+        const int32_t zc = raw ? static_cast<int32_t>(s) : static_cast<int32_t>(oc / t.c_mat);
+        const bool with_add = !raw && g.addend != nullptr;
+        const bool with_gelu = !raw && g.gelu_out != nullptr;
+        bool failed = false;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          const uint32_t n0 = n_base + c * 32;
+          if (n0 >= g.n) break;  // warp-uniform
+          uint32_t r[32];
+          ptx::tmem_load_32x32b_x32(tmem_base + acc * C::ACC_COLS + c * 32 + ((q * 32u) << 16), r);
+          uint8_t *box = obuf + (nbuf++ & 1u) * 4096;
+          if (lane == 0) ptx::bulk_wait_group_read<1>();  // box free again
+          __syncwarp();
+          if (with_add) {
+            if (lane == 0) {
+              ptx::mbar_arrive_expect_tx(my_abar, 4096);
+              ptx::tma_load_3d(box, &tmD, my_abar, static_cast<int32_t>(n0), y0, zc);
+            }
+            const bool got_add = ptx::mbar_wait_bounded(my_abar, a_phase, kWaitLimitNs);
+            a_phase ^= 1;
+            if (!__all_sync(0xffffffffu, got_add)) {
+              if (lane == 0) timeout();
+              failed = true;
+            }
+          }
+          ptx::tmem_load_wait();
+          if (failed) break;
+          float4 v[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            v[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                               __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+            if (!raw && g.bias) {
+              const uint32_t nb4 = n0 + 4 * j;
+              if (nb4 + 4 <= g.n) {
+                const float4 b = *reinterpret_cast<const float4 *>(g.bias + nb4);
+                v[j] = make_float4(v[j].x + b.x, v[j].y + b.y, v[j].z + b.z, v[j].w + b.w);
+              }
+            }
+            float4 *slot = reinterpret_cast<float4 *>(box + swz(lane, j));
+            if (with_add) {
+              const float4 a = *slot;
+              v[j] = make_float4(a.x + v[j].x, a.y + v[j].y, a.z + v[j].z, a.w + v[j].w);
+            }
+            *slot = v[j];
+          }
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            ptx::tma_store_3d(&tmC, box, static_cast<int32_t>(n0), y0, zc);
+            ptx::bulk_commit_group();
+          }
+          if (with_gelu) {
+            uint8_t *gbox = obuf + (nbuf++ & 1u) * 4096;
+            if (lane == 0) ptx::bulk_wait_group_read<1>();
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<float4 *>(gbox + swz(lane, j)) =
+                  make_float4(gelu_f(v[j].x), gelu_f(v[j].y), gelu_f(v[j].z), gelu_f(v[j].w));
+            ptx::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              ptx::tma_store_3d(&tmG, gbox, static_cast<int32_t>(n0), y0, zc);
+              ptx::bulk_commit_group();
+            }
+          }
+        }
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(&tempty[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+        if (failed) break;
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
-        ptx::tmem_load_32x32b_x32(tmem_base + acc * BN + c * 32 + ((q * 32u) << 16), r);
+        ptx::tmem_load_32x32b_x32(tmem_base + acc * C::ACC_COLS + c * 32 + ((q * 32u) << 16), r);
         ptx::tmem_load_wait();
         const uint32_t n0 = n_base + c * 32;
         if (!row_ok || n0 >= g.n) continue;
@@ -327,6 +434,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
     }
   }
 
+  // every TMA store issued by this CTA has written its box before exit
+  if (warp >= 2 && lane == 0) ptx::bulk_wait_group<0>();
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
@@ -370,6 +479,17 @@ bool make_map(CUtensorMap *map, const float *base, uint64_t inner, uint64_t oute
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// True when C's batch strides lay its matrices out one after another
+// (matrix z at z * M * N), the layout a 3-D store map can address.
+bool c_dense(const GemmArgs &g) {
+  uint64_t expect = static_cast<uint64_t>(g.m) * g.n;
+  for (int d = static_cast<int>(g.batch_rank) - 1; d >= 0; --d) {
+    if (g.batch_shape[d] > 1 && g.sc[d] != expect) return false;
+    expect *= g.batch_shape[d];
+  }
+  return true;
+}
+
 uint64_t matrices_spanned(const GemmArgs &g, const uint64_t *strides, uint64_t mat) {
   uint64_t last = 0;
   for (uint32_t d = 0; d < g.batch_rank; ++d) last += (g.batch_shape[d] - 1) * strides[d];
@@ -398,6 +518,22 @@ struct TcPlan {
 TcPlan plan_tc(const GemmArgs &g) {
   TcPlan p{};
   p.bn = g.n > 128 ? 256 : (g.n > 64 ? 128 : 64);
+  // Enough tiles for every SM: pick the tile width with the least work per
+  // SM, waves x (width + a fixed per-tile cost of ~64 columns), so N = 384
+  // runs as 3 x 128 instead of 2 x 256 with a quarter of the MMAs wasted,
+  // and the attention products (N = 192) as one 192-wide tile.
+  const uint64_t mt = (g.m + BM - 1) / BM;
+  if (g.batch_count * mt * ((g.n + 255) / 256) >= static_cast<uint64_t>(kNumSMs) / 2) {
+    uint64_t best = ~0ull;
+    for (int bn : {64, 128, 192, 256}) {
+      const uint64_t tiles = g.batch_count * mt * ((g.n + bn - 1) / bn);
+      const uint64_t cost = (tiles + kNumSMs - 1) / kNumSMs * (bn + 64);
+      if (cost < best) {
+        best = cost;
+        p.bn = bn;
+      }
+    }
+  }
   const uint64_t tiles = g.batch_count * ((g.m + BM - 1) / BM) * ((g.n + p.bn - 1) / p.bn);
   const uint32_t ktiles = (g.k + BK - 1) / BK;
   p.splits = 1;
@@ -442,6 +578,24 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
                               CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)
                    : make_map(&mb, g.b, g.k, g.n, nbm, 32, BN, CU_TENSOR_MAP_SWIZZLE_128B));
   if (!ok) return fail(TL_ERR_UNSUPPORTED, "tl_gemm: tensor map rejected");
+  // epilogue through TMA stores when every output is dense per matrix with
+  // 16-byte rows; otherwise per-thread stores
+  CUtensorMap mc{}, mg{}, md{};
+  t.c_mat = static_cast<uint64_t>(g.m) * g.n;
+  if (partial) {
+    t.tma_epi = g.n % 4 == 0 &&
+                make_map(&mc, partial, g.n, g.m, t.splits, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    const uint64_t nc = matrices_spanned(g, g.sc, t.c_mat);
+    t.tma_epi = g.n % 4 == 0 && c_dense(g) && aligned16(g.c) &&
+                (!g.bias || aligned16(g.bias)) && (!g.gelu_out || aligned16(g.gelu_out)) &&
+                (!g.addend || aligned16(g.addend)) &&
+                make_map(&mc, g.c, g.n, g.m, nc, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) &&
+                (!g.gelu_out ||
+                 make_map(&mg, g.gelu_out, g.n, g.m, nc, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B)) &&
+                (!g.addend ||
+                 make_map(&md, g.addend, g.n, g.m, nc, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
   static bool attr_set = false;
   if (!attr_set) {
     int rc = check_cuda(cudaFuncSetAttribute(tc_gemm_kernel<BN, A_MN, B_MN>,
@@ -452,7 +606,8 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
     attr_set = true;
   }
   const uint64_t grid = t.num_tiles < static_cast<uint64_t>(kNumSMs) ? t.num_tiles : kNumSMs;
-  tc_gemm_kernel<BN, A_MN, B_MN><<<static_cast<unsigned>(grid), kThreads, C::SMEM, s>>>(ma, mb, t);
+  tc_gemm_kernel<BN, A_MN, B_MN><<<static_cast<unsigned>(grid), kThreads, C::SMEM, s>>>(
+      ma, mb, mc, mg, md, t);
   int rc = launch_status("tl_gemm tf32");
   if (rc || !partial) return rc;
   const uint64_t mn = static_cast<uint64_t>(g.m) * g.n;
@@ -494,6 +649,7 @@ int launch_tc_gemm(const GemmArgs &g, void *workspace, size_t workspace_bytes, c
                        ? static_cast<float *>(workspace)
                        : nullptr;
   if (plan.bn == 256) return launch_bn<256>(g, plan, partial, s);
+  if (plan.bn == 192) return launch_bn<192>(g, plan, partial, s);
   if (plan.bn == 128) return launch_bn<128>(g, plan, partial, s);
   return launch_bn<64>(g, plan, partial, s);
 }

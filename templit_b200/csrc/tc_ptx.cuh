@@ -78,6 +78,35 @@ __device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *m
       : "memory");
 }
 
+// Tiled TMA store of a shared-memory box to global memory (no multicast;
+// elements outside the tensor are not written), tracked by bulk async-groups.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *smem_src,
+                                             int32_t c0, int32_t c1, int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_addr(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Waits until at most N committed bulk groups of this thread still read
+// their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Waits until at most N committed bulk groups of this thread are incomplete
+// (their global writes done).
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -129,7 +129,7 @@ int tlg_set_params(void *handle, const float *in, uint64_t count) {
 
 void *tlg_stream(void *) { return cuda::stream(); }
 
-int tlg_stats(void *handle, uint64_t out[8]) {
+int tlg_stats(void *handle, uint64_t out[TLG_STATS]) {
   return guarded([&] {
     const cuda::RuntimeStats &s = static_cast<Handle *>(handle)->runtime->stats();
     out[0] = s.windows;
@@ -140,6 +140,9 @@ int tlg_stats(void *handle, uint64_t out[8]) {
     out[5] = s.graph_captures;
     out[6] = s.fused_ops;
     out[7] = cuda::memory_stats().peak_in_use;
+    out[8] = s.host_record_ns;
+    out[9] = s.host_submit_ns;
+    out[10] = s.optimiser_cache_hits;
   });
 }
 

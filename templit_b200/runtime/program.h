@@ -91,6 +91,7 @@ struct Op {
   std::vector<uint8_t> host;       // HostWrite payload
   std::vector<MultiSlot> multi;    // MultiAdamW / AllReduce
   bool dead = false;               // folded away by the optimiser
+  uint32_t src = UINT32_MAX;       // index in the recorded program (optimiser cache)
 };
 
 }  // namespace cuda::internal

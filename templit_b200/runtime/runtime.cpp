@@ -138,6 +138,81 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
   }();
   std::unordered_set<std::string> dumped;
 
+  // Optimised programs by recorded-program signature.  A training loop
+  // records the same few programs every step; their optimised form is
+  // reused while every buffer the optimiser relied on as window-local still
+  // is.  Only Storage write payloads vary between recordings of one
+  // signature, and they are copied from the new recording.
+  struct Plan {
+    std::vector<Op> ops;
+    std::vector<uint64_t> local_ids;  // window_local() answers that were true
+    uint64_t folded = 0;
+    uint64_t last_use = 0;
+  };
+  std::unordered_map<std::string, Plan> plans;
+  std::chrono::steady_clock::time_point record_t0;
+
+  // Liveness view that remembers which buffers it reported window-local.
+  struct NotingLiveness : internal::Liveness {
+    const Impl *impl;
+    mutable std::vector<uint64_t> yes;
+    explicit NotingLiveness(const Impl *i) : impl(i) {}
+    bool window_local(uint64_t id) const override {
+      const bool v = impl->window_local(id);
+      if (v) yes.push_back(id);
+      return v;
+    }
+  };
+
+  void optimise_program() {
+    observe(prog);
+    std::string key = signature(prog);
+    key += optimizer_windows >= 2 ? 'L' : '-';
+    key += comm ? 'C' : '-';
+    auto it = plans.find(key);
+    if (it != plans.end()) {
+      bool valid = true;
+      for (uint64_t id : it->second.local_ids)
+        if (!window_local(id)) {
+          valid = false;
+          break;
+        }
+      if (valid) {
+        std::vector<Op> recorded = std::move(prog);
+        prog = it->second.ops;
+        for (Op &op : prog)
+          if (op.kind == Kind::HostWrite && op.src < recorded.size())
+            op.host = std::move(recorded[op.src].host);
+        stats.fused_ops += it->second.folded;
+        ++stats.optimiser_cache_hits;
+        it->second.last_use = ++use_clock;
+        return;
+      }
+      plans.erase(it);
+    }
+    for (size_t i = 0; i < prog.size(); ++i) prog[i].src = static_cast<uint32_t>(i);
+    NotingLiveness live(this);
+    Plan plan;
+    plan.folded = internal::optimize(prog, comm, &live);
+    stats.fused_ops += plan.folded;
+    // small programs re-optimise cheaply; optimiser-step programs carry the
+    // step count in their signature and never recur
+    if (prog.size() < 64) return;
+    for (const Op &op : prog)
+      if (op.kind == Kind::AdamW || op.kind == Kind::MultiAdamW) return;
+    if (plans.size() >= 16) {
+      auto victim = plans.begin();
+      for (auto p = plans.begin(); p != plans.end(); ++p)
+        if (p->second.last_use < victim->second.last_use) victim = p;
+      plans.erase(victim);
+    }
+    plan.ops = prog;
+    for (Op &op : plan.ops) op.host.clear();
+    plan.local_ids = std::move(live.yes);
+    plan.last_use = ++use_clock;
+    plans.emplace(std::move(key), std::move(plan));
+  }
+
   ~Impl() override { release_resources(); }
 
   static std::string describe(const Op &op) {
@@ -655,6 +730,7 @@ void Runtime::start() {
   impl_->prog.clear();
   impl_->window_id = internal::next_window_id();
   impl_->state = Impl::State::Recording;
+  impl_->record_t0 = std::chrono::steady_clock::now();
   internal::set_active_recorder(impl_.get());
 }
 
@@ -663,8 +739,9 @@ void Runtime::submit() {
   if (impl_->state != Impl::State::Recording)
     throw std::logic_error("CUDA runtime execution has not started");
   if (internal::active_recorder() == impl_.get()) internal::set_active_recorder(nullptr);
-  const uint64_t recorded = impl_->prog.size();
-  (void)recorded;
+  const auto t_submit = std::chrono::steady_clock::now();
+  impl_->stats.host_record_ns += static_cast<uint64_t>(
+      std::chrono::duration_cast<std::chrono::nanoseconds>(t_submit - impl_->record_t0).count());
   bool dump = false;
   if (!impl_->dump_path.empty() && impl_->dumped.size() < 64) {
     std::string key = Impl::signature(impl_->prog);
@@ -672,12 +749,9 @@ void Runtime::submit() {
     dump = impl_->dumped.insert(std::move(key)).second;
     if (dump) impl_->dump("recorded", true);
   }
-  if (impl_->fusion) {
-    impl_->observe(impl_->prog);
-    impl_->stats.fused_ops += internal::optimize(impl_->prog, impl_->comm, impl_.get());
-  }
-  if (dump) impl_->dump("optimised", true);
+  if (impl_->fusion) impl_->optimise_program();
   else if (impl_->comm) internal::add_gradient_allreduce(impl_->prog);
+  if (dump) impl_->dump("optimised", true);
   impl_->state = Impl::State::Submitted;
   ++impl_->stats.windows;
   try {
@@ -687,6 +761,10 @@ void Runtime::submit() {
     throw;
   }
   impl_->prog.clear();
+  impl_->stats.host_submit_ns += static_cast<uint64_t>(
+      std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() -
+                                                           t_submit)
+          .count());
 }
 
 // src/my_metal/runtime.cpp:310-317

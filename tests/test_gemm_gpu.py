@@ -108,6 +108,15 @@ def test_attention_batched_and_broadcast(dev):
     q = r.standard_normal((64, 6, 192, 64)).astype(np.float32)
     kt = r.standard_normal((64, 6, 64, 192)).astype(np.float32)
     check_tf32(dev.gemm(q, kt), ops.matmul(q, kt))
+    # the 192-wide tile in every operand form, with the epilogue extras
+    check_tf32(dev.gemm(q, q, trans_b=True), ops.gemm(q, q, False, True))
+    check_tf32(dev.gemm(kt, kt, trans_a=True), ops.gemm(kt, kt, True, False))
+    bias = r.standard_normal((192,)).astype(np.float32)
+    add = r.standard_normal((64, 6, 192, 192)).astype(np.float32)
+    prod = dev.gemm(q, kt, bias=bias)
+    check_tf32(prod, ops.gemm(q, kt, bias=bias))
+    np.testing.assert_array_equal(dev.gemm(q, kt, bias=bias, addend=add),
+                                  dev.binary("add", add, prod, prod.shape))
     p = r.random((64, 6, 192, 192)).astype(np.float32)
     v = r.standard_normal((64, 6, 192, 64)).astype(np.float32)
     check_tf32(dev.gemm(p, v), ops.matmul(p, v))

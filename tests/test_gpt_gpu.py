@@ -65,10 +65,10 @@ class CudaGPT:
                                            p.size), self.lib, "set_params")
 
     def stats(self):
-        s = (ctypes.c_uint64 * 8)()
+        s = (ctypes.c_uint64 * 11)()
         capi.check(self.lib.tlg_stats(self.h, s), self.lib, "stats")
         return dict(zip(["windows", "recorded", "launched", "kernels", "replays", "captures",
-                         "fused", "peak_bytes"], list(s)))
+                         "fused", "peak_bytes", "record_ns", "submit_ns", "plan_hits"], list(s)))
 
     def close(self):
         capi.check(self.lib.tlg_destroy(self.h), self.lib, "destroy")
@@ -156,6 +156,7 @@ def test_deterministic_and_graph_replay_is_bit_exact():
     assert l1 == l2 and np.array_equal(p1, p2)  # replay == eager, bit for bit
     assert l1 == l4 and np.array_equal(p1, p4)  # run to run, bit for bit
     assert s1["replays"] > 0 and s1["captures"] > 0
+    assert s1["plan_hits"] > 0 and s3["plan_hits"] == 0  # optimised programs reused
     assert s2["replays"] == 0
     assert s1["fused"] > 0 and s3["fused"] == 0
     # fused kernels vs the unfused program: same math, different rounding
