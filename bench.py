@@ -224,7 +224,7 @@ def main():
     cfg = capi.TlgConfig(family=4, batch=args.batch, seq=SEQ, seed=1234, init_std=0.02,
                          lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, clip=1.0,
                          world=world, fusion=0 if args.no_fusion else 1,
-                         graphs=0 if args.no_graphs else 1)
+                         graphs=0 if args.no_graphs else 1, deferred_wait=1)
     h = ctypes.c_void_p()
     capi.check(lib.tlg_create(ctypes.byref(cfg), ctypes.byref(h)), lib, "tlg_create")
     if world > 1:

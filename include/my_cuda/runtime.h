@@ -120,6 +120,11 @@ public:
   // sum-reduces every gradient it reads across the communicator's ranks, so
   // all ranks clip and step with the same global gradient.
   void set_communicator(void *nccl_comm);
+  // Deferred wait (off by default): wait() returns without synchronising,
+  // so the host records the next window while the GPU runs this one.
+  // Storage reads still synchronise; a device error (embedding id out of
+  // range, kernel timeout) is raised by a later wait() instead of this one.
+  void set_deferred_wait(bool enabled);
   const RuntimeStats &stats() const;
 
   struct Impl;

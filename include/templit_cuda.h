@@ -53,6 +53,10 @@ const char *tl_last_error(void);
 int tl_device_init(int device);
 /* Synchronise `stream`, then read and clear the device status word. */
 int tl_device_status(uint32_t *flags, void *stream);
+/* Without synchronising: enqueue on `stream` a move of the status word into
+ * *host_flags (pinned host memory, valid once the stream reaches this point)
+ * and clear it.  Backs cuda::Runtime's deferred wait(). */
+int tl_device_status_enqueue(uint32_t *host_flags, void *stream);
 
 /* ------------------------------------------- memory (Storage<Metal,T> ops) */
 /* Device allocation; replaces MTL::Device::newBuffer (include/my_metal/storage.h:13-16). */
@@ -79,6 +83,8 @@ int tl_event_destroy(void *event);
 int tl_event_record(void *event, void *stream);
 /* Milliseconds between two recorded events (waits for `end`). */
 int tl_event_elapsed_ms(float *ms, void *start, void *end);
+/* *done = 1 when all work before the event's record has completed. */
+int tl_event_query(void *event, int *done);
 /* Stream capture into a replayable graph: the counterpart of encoding a
  * command buffer once and committing it again (src/my_metal/runtime.cpp:290-317). */
 int tl_graph_capture_begin(void *stream);
@@ -328,6 +334,11 @@ typedef struct tl_gemm_desc {
   void *workspace;
   uint64_t workspace_bytes;
   const float *addend;
+  /* Row strides (elements) of the stored A, B and C matrices; 0 = dense
+   * (the stored row length: K or M for A, N or K for B, N for C).  C,
+   * gelu_out and addend share ldc.  With the batch strides they address
+   * strided views, e.g. one attention head of a [B, T, H, D] tensor. */
+  uint64_t lda, ldb, ldc;
 } tl_gemm_desc;
 int tl_gemm(const tl_gemm_desc *desc, void *stream);
 size_t tl_gemm_workspace_size(const tl_gemm_desc *desc);

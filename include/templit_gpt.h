@@ -38,6 +38,8 @@ typedef struct tlg_config {
   int32_t fusion;        /* runtime program fusion on/off                      */
   int32_t graphs;        /* CUDA-graph replay on/off                           */
   int32_t gemm_precision; /* TL_GEMM_TF32 (0, tensor cores) or TL_GEMM_FP32 (1) */
+  int32_t deferred_wait; /* cuda::Runtime::set_deferred_wait: the host records the
+                            next window while the GPU runs the current one     */
 } tlg_config;
 
 const char *tlg_last_error(void);

@@ -55,7 +55,7 @@ class TlgConfig(Structure):
                 ("beta1", c_float), ("beta2", c_float), ("eps", c_float),
                 ("weight_decay", c_float), ("clip", c_float),
                 ("world", c_uint32), ("fusion", c_int32), ("graphs", c_int32),
-                ("gemm_precision", c_int32)]
+                ("gemm_precision", c_int32), ("deferred_wait", c_int32)]
 
 
 U32P = POINTER(c_uint32)
@@ -66,6 +66,7 @@ CUDA_ABI = {
     "tl_last_error": (c_char_p, []),
     "tl_device_init": (c_int, [c_int]),
     "tl_device_status": (c_int, [U32P, c_void_p]),
+    "tl_device_status_enqueue": (c_int, [U32P, c_void_p]),
     "tl_malloc": (c_int, [POINTER(c_void_p), c_size_t]),
     "tl_free": (c_int, [c_void_p]),
     "tl_host_alloc": (c_int, [POINTER(c_void_p), c_size_t]),
@@ -81,6 +82,7 @@ CUDA_ABI = {
     "tl_event_destroy": (c_int, [c_void_p]),
     "tl_event_record": (c_int, [c_void_p, c_void_p]),
     "tl_event_elapsed_ms": (c_int, [POINTER(c_float), c_void_p, c_void_p]),
+    "tl_event_query": (c_int, [c_void_p, POINTER(c_int)]),
     "tl_graph_capture_begin": (c_int, [c_void_p]),
     "tl_graph_capture_end": (c_int, [c_void_p, POINTER(c_void_p)]),
     "tl_graph_launch": (c_int, [c_void_p, c_void_p]),

@@ -14,6 +14,7 @@ struct GemmArgs {
   float *gelu_out;
   const float *addend;  // C's layout; C itself when accumulating (beta = 1)
   uint32_t m, n, k;
+  uint64_t lda, ldb, ldc;  // row strides of the stored matrices (elements)
   int trans_a, trans_b;
   float beta;
   uint32_t batch_rank;

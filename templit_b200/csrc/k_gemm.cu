@@ -44,14 +44,36 @@ int to_args(const tl_gemm_desc *d, GemmArgs &g) {
   if (d->addend && d->beta != 0.0f && d->addend != d->c)
     return fail(TL_ERR_INVALID, "tl_gemm: addend with beta = 1 must be C");
   g.addend = d->addend ? d->addend : (d->beta != 0.0f ? d->c : nullptr);
-  g.batch_rank = d->batch_rank;
+  g.lda = d->lda ? d->lda : (g.trans_a ? g.m : g.k);
+  g.ldb = d->ldb ? d->ldb : (g.trans_b ? g.k : g.n);
+  g.ldc = d->ldc ? d->ldc : g.n;
+  if (g.lda < (g.trans_a ? g.m : g.k) || g.ldb < (g.trans_b ? g.k : g.n) || g.ldc < g.n)
+    return fail(TL_ERR_INVALID, "tl_gemm: row stride shorter than the row");
+  // batch dims, merging neighbours that every operand walks as one (the
+  // outer stride is the inner stride times the inner extent)
+  g.batch_rank = 0;
   g.batch_count = 1;
   for (uint32_t i = 0; i < d->batch_rank; ++i) {
-    g.batch_shape[i] = d->batch_shape[i];
-    g.sa[i] = d->a_batch_stride[i];
-    g.sb[i] = d->b_batch_stride[i];
-    g.sc[i] = d->c_batch_stride[i];
-    g.batch_count *= d->batch_shape[i];
+    const uint32_t n = d->batch_shape[i];
+    g.batch_count *= n;
+    if (n == 1) continue;
+    const uint64_t sa = d->a_batch_stride[i], sb = d->b_batch_stride[i],
+                   sc = d->c_batch_stride[i];
+    if (g.batch_rank > 0) {
+      const uint32_t j = g.batch_rank - 1;
+      if (g.sa[j] == sa * n && g.sb[j] == sb * n && g.sc[j] == sc * n) {
+        g.batch_shape[j] *= n;
+        g.sa[j] = sa;
+        g.sb[j] = sb;
+        g.sc[j] = sc;
+        continue;
+      }
+    }
+    g.batch_shape[g.batch_rank] = n;
+    g.sa[g.batch_rank] = sa;
+    g.sb[g.batch_rank] = sb;
+    g.sc[g.batch_rank] = sc;
+    ++g.batch_rank;
   }
   return TL_OK;
 }

@@ -1,6 +1,7 @@
 // CUDA-core fp32 GEMM: the exact-fp32 path of tl_gemm (TL_GEMM_FP32) and the
 // path for operands the tensor-core kernel cannot take (rows whose byte
-// length is not a multiple of 16, which TMA cannot address).
+// length is not a multiple of 16, which TMA cannot address).  Operands and
+// C are addressed through their row strides (lda, ldb, ldc).
 //
 // 128x128x8 CTA tile, 256 threads, 8x8 outputs per thread, operands staged
 // through shared memory in k-major order so every thread reads its 8 rows
@@ -43,7 +44,7 @@ sgemm_kernel(GemmArgs g) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const uint32_t k = k0 + kc + q;
-        As[buf][kc + q][r] = (m < M && k < K) ? A[static_cast<size_t>(m) * K + k] : 0.0f;
+        As[buf][kc + q][r] = (m < M && k < K) ? A[static_cast<size_t>(m) * g.lda + k] : 0.0f;
       }
     } else {  // A stored [K][M]: thread -> (k row tid/32, 4 consecutive m)
       const uint32_t kr = tid / 32, mc = (tid % 32) * 4;
@@ -51,7 +52,7 @@ sgemm_kernel(GemmArgs g) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const uint32_t m = m0 + mc + q;
-        As[buf][kr][mc + q] = (m < M && k < K) ? A[static_cast<size_t>(k) * M + m] : 0.0f;
+        As[buf][kr][mc + q] = (m < M && k < K) ? A[static_cast<size_t>(k) * g.lda + m] : 0.0f;
       }
     }
     if (!g.trans_b) {  // B[k][n] at B[k*N + n]
@@ -60,7 +61,7 @@ sgemm_kernel(GemmArgs g) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const uint32_t n = n0 + nc + q;
-        Bs[buf][kr][nc + q] = (n < N && k < K) ? B[static_cast<size_t>(k) * N + n] : 0.0f;
+        Bs[buf][kr][nc + q] = (n < N && k < K) ? B[static_cast<size_t>(k) * g.ldb + n] : 0.0f;
       }
     } else {  // B stored [N][K]
       const uint32_t r = tid / 2, kc = (tid % 2) * 4;
@@ -68,7 +69,7 @@ sgemm_kernel(GemmArgs g) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const uint32_t k = k0 + kc + q;
-        Bs[buf][kc + q][r] = (n < N && k < K) ? B[static_cast<size_t>(n) * K + k] : 0.0f;
+        Bs[buf][kc + q][r] = (n < N && k < K) ? B[static_cast<size_t>(n) * g.ldb + k] : 0.0f;
       }
     }
   };
@@ -107,7 +108,7 @@ sgemm_kernel(GemmArgs g) {
     for (int j = 0; j < TN; ++j) {
       const uint32_t n = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
       if (n >= N) continue;
-      const size_t idx = static_cast<size_t>(m) * N + n;
+      const size_t idx = static_cast<size_t>(m) * g.ldc + n;
       epilogue_store(g, C, oc, idx, n, acc[i][j]);
     }
   }

@@ -36,11 +36,18 @@ constexpr uint32_t kA_BYTES = BM * BK * 4;  // 16 KB
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kFlagTimeout = TL_FLAG_TIMEOUT;
 
+struct OpMap {
+  int32_t nb;      // batch dims in the map (0..3)
+  int32_t dim[3];  // product batch dim of map dim 2 + i
+};
+
 struct TcArgs {
   GemmArgs g;
   uint32_t mt, nt;        // tiles along M and N
   uint64_t num_tiles;     // batch * splits * mt * nt
-  uint64_t a_mat, b_mat;  // elements per A / B matrix
+  // batch dims each operand's tensor map walks (those with a nonzero
+  // stride), as indices into the product's batch dims
+  OpMap ma, mb, mc;
   uint32_t *status;
   // split-K: the K range is cut into `splits` slices of kb_per_split k-tiles;
   // slice s writes its raw fp32 product to partial + s * M * N (batch 1 only)
@@ -50,7 +57,6 @@ struct TcArgs {
   // epilogue through shared memory and TMA stores (C, or the split-K
   // partials, dense per matrix with rows of a multiple of 16 bytes)
   bool tma_epi;
-  uint64_t c_mat;  // elements per C matrix
 };
 
 template <int BN>
@@ -84,6 +90,21 @@ __device__ __forceinline__ void k_range(const TcArgs &t, uint32_t ktiles, uint32
                                         uint32_t &kb0, uint32_t &kb1) {
   kb0 = s * t.kb_per_split;
   kb1 = min(ktiles, kb0 + t.kb_per_split);
+}
+
+// Coordinates of flattened batch index z in the product's batch dims.
+__device__ __forceinline__ void batch_coords(const GemmArgs &g, uint64_t z,
+                                             int32_t (&cz)[TL_GEMM_MAX_BATCH_RANK]) {
+  for (int d = static_cast<int>(g.batch_rank) - 1; d >= 0; --d) {
+    cz[d] = static_cast<int32_t>(z % g.batch_shape[d]);
+    z /= g.batch_shape[d];
+  }
+}
+
+__device__ __forceinline__ void map_coords(const OpMap &m, const int32_t (&cz)[TL_GEMM_MAX_BATCH_RANK],
+                                           int32_t (&out)[3]) {
+#pragma unroll
+  for (int i = 0; i < 3; ++i) out[i] = i < m.nb ? cz[m.dim[i]] : 0;
 }
 
 // Byte offset of 16-byte group j of row r in a 128-byte-swizzled box.
@@ -159,10 +180,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
         uint32_t s, mb, nb, kb0, kb1;
         decode_tile(t, tile, z, s, mb, nb);
         k_range(t, ktiles, s, kb0, kb1);
-        uint64_t oa, ob, oc;
-        batch_offsets(g, z, oa, ob, oc);
-        const int32_t za = static_cast<int32_t>(oa / t.a_mat);
-        const int32_t zb = static_cast<int32_t>(ob / t.b_mat);
+        int32_t cz[TL_GEMM_MAX_BATCH_RANK], za[3], zb[3];
+        batch_coords(g, z, cz);
+        map_coords(t.ma, cz, za);
+        map_coords(t.mb, cz, zb);
         const int32_t m0 = static_cast<int32_t>(mb * BM), n0 = static_cast<int32_t>(nb * BN);
         for (uint32_t kb = kb0; kb < kb1; ++kb) {
           if (!ptx::mbar_wait_bounded(&empty[stage], phase ^ 1, kWaitLimitNs)) {
@@ -174,18 +195,18 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
           ptx::mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
           const int32_t k0 = static_cast<int32_t>(kb * BK);
           if (!A_MN) {
-            ptx::tma_load_3d(sa, &tmA, &full[stage], k0, m0, za);
+            ptx::tma_load_nd(sa, &tmA, &full[stage], k0, m0, t.ma.nb, za);
           } else {
 #pragma unroll
             for (int j = 0; j < BM / 32; ++j)
-              ptx::tma_load_3d(sa + j * 4096, &tmA, &full[stage], m0 + 32 * j, k0, za);
+              ptx::tma_load_nd(sa + j * 4096, &tmA, &full[stage], m0 + 32 * j, k0, t.ma.nb, za);
           }
           if (!B_MN) {
-            ptx::tma_load_3d(sb, &tmB, &full[stage], k0, n0, zb);
+            ptx::tma_load_nd(sb, &tmB, &full[stage], k0, n0, t.mb.nb, zb);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 32; ++j)
-              ptx::tma_load_3d(sb + j * 4096, &tmB, &full[stage], n0 + 32 * j, k0, zb);
+              ptx::tma_load_nd(sb + j * 4096, &tmB, &full[stage], n0 + 32 * j, k0, t.mb.nb, zb);
           }
           ++issued;
           if (++stage == C::STAGES) {
@@ -298,7 +319,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
       const bool row_ok = m < g.m;
       // 128-bit path: raw partials, or the full epilogue on float4 groups
       // (bias, accumulate and GELU in the same order as epilogue_store)
-      const bool fast = (g.n % 4) == 0 && aligned16(Cb) &&
+      const uint64_t ldo = raw ? g.n : g.ldc;  // split-K slices are dense
+      const bool fast = (g.n % 4) == 0 && (ldo % 4) == 0 && aligned16(Cb) &&
                         (raw || ((!g.bias || aligned16(g.bias)) &&
                                  (!g.addend || aligned16(g.addend + oc)) &&
                                  (!g.gelu_out || aligned16(g.gelu_out + oc))));
@@ -308,7 +330,18 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
         // store of the 32 x 32 box (rows and columns past M, N are clipped).
         // Two boxes per warp alternate so one store is always in flight.
         const int32_t y0 = static_cast<int32_t>(mb * BM + q * 32);
-        const int32_t zc = raw ? static_cast<int32_t>(s) : static_cast<int32_t>(oc / t.c_mat);
+        int32_t zc[3];
+        int ncz;
+        if (raw) {  // split-K slices: [splits][M][N]
+          zc[0] = static_cast<int32_t>(s);
+          zc[1] = zc[2] = 0;
+          ncz = 1;
+        } else {
+          int32_t cz[TL_GEMM_MAX_BATCH_RANK];
+          batch_coords(g, z, cz);
+          map_coords(t.mc, cz, zc);
+          ncz = t.mc.nb;
+        }
         const bool with_add = !raw && g.addend != nullptr;
         const bool with_gelu = !raw && g.gelu_out != nullptr;
         bool failed = false;
@@ -324,7 +357,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
           if (with_add) {
             if (lane == 0) {
               ptx::mbar_arrive_expect_tx(my_abar, 4096);
-              ptx::tma_load_3d(box, &tmD, my_abar, static_cast<int32_t>(n0), y0, zc);
+              ptx::tma_load_nd(box, &tmD, my_abar, static_cast<int32_t>(n0), y0, ncz, zc);
             }
             const bool got_add = ptx::mbar_wait_bounded(my_abar, a_phase, kWaitLimitNs);
             a_phase ^= 1;
@@ -357,7 +390,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
           ptx::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            ptx::tma_store_3d(&tmC, box, static_cast<int32_t>(n0), y0, zc);
+            ptx::tma_store_nd(&tmC, box, static_cast<int32_t>(n0), y0, ncz, zc);
             ptx::bulk_commit_group();
           }
           if (with_gelu) {
@@ -371,7 +404,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
             ptx::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              ptx::tma_store_3d(&tmG, gbox, static_cast<int32_t>(n0), y0, zc);
+              ptx::tma_store_nd(&tmG, gbox, static_cast<int32_t>(n0), y0, ncz, zc);
               ptx::bulk_commit_group();
             }
           }
@@ -392,7 +425,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
         ptx::tmem_load_wait();
         const uint32_t n0 = n_base + c * 32;
         if (!row_ok || n0 >= g.n) continue;
-        const size_t rowoff = static_cast<size_t>(m) * g.n;
+        const size_t rowoff = static_cast<size_t>(m) * ldo;
         if (fast && n0 + 32 <= g.n) {
           float4 *dst = reinterpret_cast<float4 *>(Cb + rowoff + n0);
 #pragma unroll
@@ -463,37 +496,33 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 3-D map over `nmat` matrices of [outer][inner] fp32 with a box of
-// box_inner x box_outer x 1.
-bool make_map(CUtensorMap *map, const float *base, uint64_t inner, uint64_t outer,
-              uint64_t nmat, uint32_t box_inner, uint32_t box_outer,
-              CUtensorMapSwizzle swz) {
+// Map of a stored matrix [outer][inner] (row stride ld elements) and the
+// batch dims of `strides` that are not broadcast (stride 0), box
+// box_inner x box_outer.  Fills `om` with those dims; false when TMA cannot
+// describe the operand (more than three such dims, or encoding refused).
+bool make_operand_map(CUtensorMap *map, const float *base, uint64_t inner, uint64_t outer,
+                      uint64_t ld, const GemmArgs &g, const uint64_t *strides,
+                      uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz,
+                      OpMap &om) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
-  const cuuint64_t dims[3] = {inner, outer, nmat};
-  const cuuint64_t strides[2] = {inner * 4, inner * outer * 4};
-  const cuuint32_t box[3] = {box_inner, box_outer, 1};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides,
+  cuuint64_t dims[5] = {inner, outer, 1, 1, 1};
+  cuuint64_t st[4] = {ld * 4, 0, 0, 0};
+  om = OpMap{};
+  int rank = 2;
+  for (uint32_t d = 0; d < g.batch_rank; ++d) {
+    if (strides[d] == 0) continue;
+    if (om.nb == 3) return false;
+    dims[rank] = g.batch_shape[d];
+    st[rank - 1] = strides[d] * 4;
+    om.dim[om.nb++] = static_cast<int32_t>(d);
+    ++rank;
+  }
+  const cuuint32_t box[5] = {box_inner, box_outer, 1, 1, 1};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<float *>(base), dims, st,
              box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// True when C's batch strides lay its matrices out one after another
-// (matrix z at z * M * N), the layout a 3-D store map can address.
-bool c_dense(const GemmArgs &g) {
-  uint64_t expect = static_cast<uint64_t>(g.m) * g.n;
-  for (int d = static_cast<int>(g.batch_rank) - 1; d >= 0; --d) {
-    if (g.batch_shape[d] > 1 && g.sc[d] != expect) return false;
-    expect *= g.batch_shape[d];
-  }
-  return true;
-}
-
-uint64_t matrices_spanned(const GemmArgs &g, const uint64_t *strides, uint64_t mat) {
-  uint64_t last = 0;
-  for (uint32_t d = 0; d < g.batch_rank; ++d) last += (g.batch_shape[d] - 1) * strides[d];
-  return last / mat + 1;
 }
 
 // Slice sums of a split-K product in slice order, then the epilogue.
@@ -505,7 +534,8 @@ splitk_epilogue_kernel(const float *__restrict__ part, uint32_t splits, GemmArgs
        i += stride) {
     float v = part[i];
     for (uint32_t s = 1; s < splits; ++s) v += part[s * mn + i];
-    epilogue_store(g, g.c, 0, i, static_cast<uint32_t>(i % g.n), v);
+    const uint32_t n = static_cast<uint32_t>(i % g.n);
+    epilogue_store(g, g.c, 0, (i / g.n) * g.ldc + n, n, v);
   }
 }
 
@@ -565,36 +595,43 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
   t.kb_per_split = partial ? plan.kb_per_split : (g.k + BK - 1) / BK;
   t.partial = partial;
   t.num_tiles = g.batch_count * t.splits * t.mt * t.nt;
-  t.a_mat = static_cast<uint64_t>(g.m) * g.k;
-  t.b_mat = static_cast<uint64_t>(g.k) * g.n;
   t.status = device_status_ptr();
   if (!t.status) return fail(TL_ERR_CUDA, "tl_gemm: no status word");
   CUtensorMap ma, mb;
-  const uint64_t na = matrices_spanned(g, g.sa, t.a_mat);
-  const uint64_t nbm = matrices_spanned(g, g.sb, t.b_mat);
-  bool ok = A_MN ? make_map(&ma, g.a, g.m, g.k, na, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)
-                 : make_map(&ma, g.a, g.k, g.m, na, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B);
-  ok = ok && (B_MN ? make_map(&mb, g.b, g.n, g.k, nbm, 32, 32,
-                              CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)
-                   : make_map(&mb, g.b, g.k, g.n, nbm, 32, BN, CU_TENSOR_MAP_SWIZZLE_128B));
+  bool ok = A_MN ? make_operand_map(&ma, g.a, g.m, g.k, g.lda, g, g.sa, 32, 32,
+                                    CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, t.ma)
+                 : make_operand_map(&ma, g.a, g.k, g.m, g.lda, g, g.sa, 32, BM,
+                                    CU_TENSOR_MAP_SWIZZLE_128B, t.ma);
+  ok = ok && (B_MN ? make_operand_map(&mb, g.b, g.n, g.k, g.ldb, g, g.sb, 32, 32,
+                                      CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, t.mb)
+                   : make_operand_map(&mb, g.b, g.k, g.n, g.ldb, g, g.sb, 32, BN,
+                                      CU_TENSOR_MAP_SWIZZLE_128B, t.mb));
   if (!ok) return fail(TL_ERR_UNSUPPORTED, "tl_gemm: tensor map rejected");
-  // epilogue through TMA stores when every output is dense per matrix with
-  // 16-byte rows; otherwise per-thread stores
+  // epilogue through TMA stores when C (and gelu_out, addend: same layout)
+  // have 16-byte rows; otherwise per-thread stores
   CUtensorMap mc{}, mg{}, md{};
-  t.c_mat = static_cast<uint64_t>(g.m) * g.n;
   if (partial) {
+    GemmArgs slices = g;  // [splits][M][N], dense
+    slices.batch_rank = 1;
+    slices.batch_shape[0] = t.splits;
+    const uint64_t mn = static_cast<uint64_t>(g.m) * g.n;
+    OpMap unused;
     t.tma_epi = g.n % 4 == 0 &&
-                make_map(&mc, partial, g.n, g.m, t.splits, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+                make_operand_map(&mc, partial, g.n, g.m, g.n, slices, &mn, 32, 32,
+                                 CU_TENSOR_MAP_SWIZZLE_128B, unused);
   } else {
-    const uint64_t nc = matrices_spanned(g, g.sc, t.c_mat);
-    t.tma_epi = g.n % 4 == 0 && c_dense(g) && aligned16(g.c) &&
+    bool strides_ok = g.ldc % 4 == 0;
+    for (uint32_t d = 0; d < g.batch_rank; ++d) strides_ok = strides_ok && g.sc[d] % 4 == 0;
+    OpMap og{}, od{};
+    t.tma_epi = g.n % 4 == 0 && strides_ok && aligned16(g.c) &&
                 (!g.bias || aligned16(g.bias)) && (!g.gelu_out || aligned16(g.gelu_out)) &&
                 (!g.addend || aligned16(g.addend)) &&
-                make_map(&mc, g.c, g.n, g.m, nc, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) &&
-                (!g.gelu_out ||
-                 make_map(&mg, g.gelu_out, g.n, g.m, nc, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B)) &&
-                (!g.addend ||
-                 make_map(&md, g.addend, g.n, g.m, nc, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B));
+                make_operand_map(&mc, g.c, g.n, g.m, g.ldc, g, g.sc, 32, 32,
+                                 CU_TENSOR_MAP_SWIZZLE_128B, t.mc) &&
+                (!g.gelu_out || make_operand_map(&mg, g.gelu_out, g.n, g.m, g.ldc, g, g.sc, 32,
+                                                 32, CU_TENSOR_MAP_SWIZZLE_128B, og)) &&
+                (!g.addend || make_operand_map(&md, g.addend, g.n, g.m, g.ldc, g, g.sc, 32, 32,
+                                               CU_TENSOR_MAP_SWIZZLE_128B, od));
   }
   static bool attr_set = false;
   if (!attr_set) {
@@ -625,13 +662,17 @@ int launch_bn(const GemmArgs &g, const TcPlan &plan, float *partial, cudaStream_
 }
 
 bool tc_supported(const GemmArgs &g) {
-  // TMA rules: 16-byte aligned bases, row strides and matrix strides.
-  const uint32_t a_inner = g.trans_a ? g.m : g.k;
-  const uint32_t b_inner = g.trans_b ? g.k : g.n;
-  if (g.k == 0 || a_inner % 4 || b_inner % 4 || !aligned16(g.a) || !aligned16(g.b)) return false;
-  for (uint32_t d = 0; d < g.batch_rank; ++d)
+  // TMA rules: 16-byte aligned bases, row strides and batch strides; at
+  // most three walked batch dims per operand.
+  if (g.k == 0 || g.lda % 4 || g.ldb % 4 || !aligned16(g.a) || !aligned16(g.b)) return false;
+  int na = 0, nb = 0;
+  for (uint32_t d = 0; d < g.batch_rank; ++d) {
     if (g.sa[d] % 4 || g.sb[d] % 4) return false;
-  return g.m <= 0x7fffffffu && g.n <= 0x7fffffffu && g.k <= 0x7fffffffu;
+    na += g.sa[d] != 0;
+    nb += g.sb[d] != 0;
+  }
+  return na <= 3 && nb <= 3 && g.m <= 0x7fffffffu && g.n <= 0x7fffffffu &&
+         g.k <= 0x7fffffffu;
 }
 
 }  // namespace

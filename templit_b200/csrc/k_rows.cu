@@ -306,6 +306,170 @@ xent_backward_kernel(const float *__restrict__ z, const uint32_t *__restrict__ t
   }
 }
 
+// ---- register-resident rows (cols <= 128 * NV, 128-bit rows) ----------
+// One warp per row keeps the whole row in registers (NV float4 per lane,
+// lane l holding columns 4l + 128i): one pass over memory, the same
+// per-lane order of operations as the looping kernels above, so the
+// results are bit-identical to them.
+template <int NV>
+__global__ void __launch_bounds__(256)
+softmax_regs_kernel(const float *__restrict__ x, const float *__restrict__ divisor,
+                    const float *__restrict__ mask, uint32_t mask_rows, float *out,
+                    uint32_t rows, uint32_t cols) {
+  ROW_LOOP {
+    const float *xr = x + static_cast<size_t>(row) * cols;
+    const float *mr = mask ? mask + static_cast<size_t>(row % mask_rows) * cols : nullptr;
+    float4 v[NV];
+    float m = -INFINITY, s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint32_t c = (i * 32 + lane) * 4;
+      if (c < cols) {
+        v[i] = *reinterpret_cast<const float4 *>(xr + c);
+        v[i].x = score(v[i].x, divisor, mr, c);
+        v[i].y = score(v[i].y, divisor, mr, c + 1);
+        v[i].z = score(v[i].z, divisor, mr, c + 2);
+        v[i].w = score(v[i].w, divisor, mr, c + 3);
+        online_add(m, s, v[i].x);
+        online_add(m, s, v[i].y);
+        online_add(m, s, v[i].z);
+        online_add(m, s, v[i].w);
+      }
+    }
+    warp_online(m, s);
+    float *yr = out + static_cast<size_t>(row) * cols;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint32_t c = (i * 32 + lane) * 4;
+      if (c < cols)
+        *reinterpret_cast<float4 *>(yr + c) =
+            make_float4(expf(v[i].x - m) / s, expf(v[i].y - m) / s, expf(v[i].z - m) / s,
+                        expf(v[i].w - m) / s);
+    }
+  }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(256)
+softmax_backward_regs_kernel(const float *__restrict__ g, const float *__restrict__ y,
+                             const float *__restrict__ divisor, float *dx, uint32_t rows,
+                             uint32_t cols) {
+  ROW_LOOP {
+    const size_t off = static_cast<size_t>(row) * cols;
+    float4 gv[NV], yv[NV];
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint32_t c = (i * 32 + lane) * 4;
+      if (c < cols) {
+        gv[i] = *reinterpret_cast<const float4 *>(g + off + c);
+        yv[i] = *reinterpret_cast<const float4 *>(y + off + c);
+        acc += gv[i].x * yv[i].x + gv[i].y * yv[i].y + gv[i].z * yv[i].z + gv[i].w * yv[i].w;
+      }
+    }
+    const float dot = warp_sum(acc);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint32_t c = (i * 32 + lane) * 4;
+      if (c < cols)
+        *reinterpret_cast<float4 *>(dx + off + c) =
+            make_float4(div_opt(yv[i].x * (gv[i].x - dot), divisor),
+                        div_opt(yv[i].y * (gv[i].y - dot), divisor),
+                        div_opt(yv[i].z * (gv[i].z - dot), divisor),
+                        div_opt(yv[i].w * (gv[i].w - dot), divisor));
+    }
+  }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(256)
+rmsnorm_regs_kernel(const float *__restrict__ x, float *out, float *rms_out, uint32_t rows,
+                    uint32_t cols) {
+  ROW_LOOP {
+    const float *xr = x + static_cast<size_t>(row) * cols;
+    float4 v[NV];
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint32_t c = (i * 32 + lane) * 4;
+      if (c < cols) {
+        v[i] = *reinterpret_cast<const float4 *>(xr + c);
+        acc += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+      }
+    }
+    const float r = sqrtf(warp_sum(acc) / static_cast<float>(cols) + 1e-6f);
+    if (rms_out && lane == 0) rms_out[row] = r;
+    float *yr = out + static_cast<size_t>(row) * cols;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint32_t c = (i * 32 + lane) * 4;
+      if (c < cols)
+        *reinterpret_cast<float4 *>(yr + c) =
+            make_float4(v[i].x / r, v[i].y / r, v[i].z / r, v[i].w / r);
+    }
+  }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(256)
+rmsnorm_backward_regs_kernel(const float *__restrict__ g, const float *__restrict__ x,
+                             const float *__restrict__ y, const float *addend, float *dx,
+                             uint32_t rows, uint32_t cols) {
+  ROW_LOOP {
+    const size_t off = static_cast<size_t>(row) * cols;
+    float4 gv[NV], yv[NV];
+    float ss = 0.0f, gy = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint32_t c = (i * 32 + lane) * 4;
+      if (c < cols) {
+        const float4 xv = *reinterpret_cast<const float4 *>(x + off + c);
+        ss += xv.x * xv.x + xv.y * xv.y + xv.z * xv.z + xv.w * xv.w;
+        gv[i] = *reinterpret_cast<const float4 *>(g + off + c);
+        yv[i] = *reinterpret_cast<const float4 *>(y + off + c);
+        gy += gv[i].x * yv[i].x + gv[i].y * yv[i].y + gv[i].z * yv[i].z + gv[i].w * yv[i].w;
+      }
+    }
+    const float r = sqrtf(warp_sum(ss) / static_cast<float>(cols) + 1e-6f);
+    const float mean = warp_sum(gy) / static_cast<float>(cols);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint32_t c = (i * 32 + lane) * 4;
+      if (c < cols) {
+        float4 o = make_float4((gv[i].x - yv[i].x * mean) / r, (gv[i].y - yv[i].y * mean) / r,
+                               (gv[i].z - yv[i].z * mean) / r, (gv[i].w - yv[i].w * mean) / r);
+        if (addend) {
+          const float4 a = *reinterpret_cast<const float4 *>(addend + off + c);
+          o = make_float4(a.x + o.x, a.y + o.y, a.z + o.z, a.w + o.w);
+        }
+        *reinterpret_cast<float4 *>(dx + off + c) = o;
+      }
+    }
+  }
+}
+
+// Float4s per lane that hold a row of `cols` (0: too long, use the loops).
+int regs_for(uint32_t cols) {
+  const uint32_t nv = (cols + 127) / 128;
+  if (nv <= 1) return 1;
+  if (nv <= 2) return 2;
+  if (nv <= 3) return 3;
+  if (nv <= 4) return 4;
+  if (nv <= 6) return 6;
+  if (nv <= 8) return 8;
+  return 0;
+}
+
+#define TL_ROWS_DISPATCH(NVVAR, LAUNCH) \
+  switch (NVVAR) {                      \
+    case 1: LAUNCH(1); break;           \
+    case 2: LAUNCH(2); break;           \
+    case 3: LAUNCH(3); break;           \
+    case 4: LAUNCH(4); break;           \
+    case 6: LAUNCH(6); break;           \
+    default: LAUNCH(8); break;          \
+  }
+
 unsigned row_grid(uint32_t rows) {
   return grid_for(rows, kWarpsPerBlock, 16);
 }
@@ -329,8 +493,16 @@ int tl_softmax_rows(const float *x, float *out, uint32_t rows, uint32_t cols,
   if (cols == 0) return fail(TL_ERR_INVALID, "softmax requires a non-empty final dimension");
   if (rows == 0) return TL_OK;
   if (!x || !out) return fail(TL_ERR_INVALID, "tl_softmax_rows: null pointer");
-  softmax_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(x, out, rows, cols,
-                                                                row_vec(cols, {x, out}));
+  const int nv = row_vec(cols, {x, out}) ? regs_for(cols) : 0;
+  if (nv) {
+#define L(NV) softmax_regs_kernel<NV><<<row_grid(rows), 256, 0, as_stream(stream)>>>( \
+    x, nullptr, nullptr, 0, out, rows, cols)
+    TL_ROWS_DISPATCH(nv, L)
+#undef L
+  } else {
+    softmax_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(x, out, rows, cols,
+                                                                  row_vec(cols, {x, out}));
+  }
   return launch_status("tl_softmax_rows");
 }
 
@@ -342,8 +514,16 @@ int tl_softmax_scaled_masked_rows(const float *x, const float *divisor, const fl
   if (!x || !out) return fail(TL_ERR_INVALID, "tl_softmax_scaled_masked_rows: null pointer");
   if (mask && mask_rows == 0)
     return fail(TL_ERR_INVALID, "tl_softmax_scaled_masked_rows: mask without rows");
-  softmax_scaled_masked_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
-      x, divisor, mask, mask_rows, out, rows, cols, row_vec(cols, {x, out, mask}));
+  const int nv = row_vec(cols, {x, out, mask}) ? regs_for(cols) : 0;
+  if (nv) {
+#define L(NV) softmax_regs_kernel<NV><<<row_grid(rows), 256, 0, as_stream(stream)>>>( \
+    x, divisor, mask, mask_rows, out, rows, cols)
+    TL_ROWS_DISPATCH(nv, L)
+#undef L
+  } else {
+    softmax_scaled_masked_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
+        x, divisor, mask, mask_rows, out, rows, cols, row_vec(cols, {x, out, mask}));
+  }
   return launch_status("tl_softmax_scaled_masked_rows");
 }
 
@@ -351,8 +531,16 @@ int tl_softmax_backward_rows(const float *grad, const float *y, const float *div
                              float *dx, uint32_t rows, uint32_t cols, void *stream) {
   if (rows == 0 || cols == 0) return TL_OK;
   if (!grad || !y || !dx) return fail(TL_ERR_INVALID, "tl_softmax_backward_rows: null pointer");
-  softmax_backward_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
-      grad, y, divisor, dx, rows, cols, row_vec(cols, {grad, y, dx}));
+  const int nv = row_vec(cols, {grad, y, dx}) ? regs_for(cols) : 0;
+  if (nv) {
+#define L(NV) softmax_backward_regs_kernel<NV><<<row_grid(rows), 256, 0, as_stream(stream)>>>( \
+    grad, y, divisor, dx, rows, cols)
+    TL_ROWS_DISPATCH(nv, L)
+#undef L
+  } else {
+    softmax_backward_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
+        grad, y, divisor, dx, rows, cols, row_vec(cols, {grad, y, dx}));
+  }
   return launch_status("tl_softmax_backward_rows");
 }
 
@@ -371,8 +559,16 @@ int tl_rmsnorm_rows(const float *x, float *out, float *rms_out, uint32_t rows,
   if (rows == 0) return TL_OK;
   if (cols == 0) return fail(TL_ERR_INVALID, "tl_rmsnorm_rows: empty rows");
   if (!x || !out) return fail(TL_ERR_INVALID, "tl_rmsnorm_rows: null pointer");
-  rmsnorm_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
-      x, out, rms_out, rows, cols, row_vec(cols, {x, out}));
+  const int nv = row_vec(cols, {x, out}) ? regs_for(cols) : 0;
+  if (nv) {
+#define L(NV) rmsnorm_regs_kernel<NV><<<row_grid(rows), 256, 0, as_stream(stream)>>>( \
+    x, out, rms_out, rows, cols)
+    TL_ROWS_DISPATCH(nv, L)
+#undef L
+  } else {
+    rmsnorm_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
+        x, out, rms_out, rows, cols, row_vec(cols, {x, out}));
+  }
   return launch_status("tl_rmsnorm_rows");
 }
 
@@ -383,8 +579,16 @@ int tl_rmsnorm_backward_rows(const float *grad, const float *x, const float *y,
   if (cols == 0) return fail(TL_ERR_INVALID, "tl_rmsnorm_backward_rows: empty rows");
   if (!grad || !x || !y || !dx)
     return fail(TL_ERR_INVALID, "tl_rmsnorm_backward_rows: null pointer");
-  rmsnorm_backward_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
-      grad, x, y, addend, dx, rows, cols, row_vec(cols, {grad, x, y, dx, addend}));
+  const int nv = row_vec(cols, {grad, x, y, dx, addend}) ? regs_for(cols) : 0;
+  if (nv) {
+#define L(NV) rmsnorm_backward_regs_kernel<NV><<<row_grid(rows), 256, 0, as_stream(stream)>>>( \
+    grad, x, y, addend, dx, rows, cols)
+    TL_ROWS_DISPATCH(nv, L)
+#undef L
+  } else {
+    rmsnorm_backward_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
+        grad, x, y, addend, dx, rows, cols, row_vec(cols, {grad, x, y, dx, addend}));
+  }
   return launch_status("tl_rmsnorm_backward_rows");
 }
 

@@ -78,6 +78,80 @@ __device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *m
       : "memory");
 }
 
+// Tiled TMA load of a box of a rank-(2 + nb) map (nb = 0..3 batch
+// coordinates in zc), completing on `bar`; no multicast.
+__device__ __forceinline__ void tma_load_nd(void *smem_dst, const CUtensorMap *map,
+                                            uint64_t *bar, int32_t c0, int32_t c1, int nb,
+                                            const int32_t *zc) {
+  const uint64_t m = reinterpret_cast<uint64_t>(map);
+  const uint32_t d = smem_addr(smem_dst), b = smem_addr(bar);
+  switch (nb) {
+    case 0:
+      asm volatile(
+          "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+          " [%0], [%1, {%2, %3}], [%4];" ::"r"(d),
+          "l"(m), "r"(c0), "r"(c1), "r"(b)
+          : "memory");
+      break;
+    case 1:
+      asm volatile(
+          "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+          " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(d),
+          "l"(m), "r"(c0), "r"(c1), "r"(zc[0]), "r"(b)
+          : "memory");
+      break;
+    case 2:
+      asm volatile(
+          "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+          " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(d),
+          "l"(m), "r"(c0), "r"(c1), "r"(zc[0]), "r"(zc[1]), "r"(b)
+          : "memory");
+      break;
+    default:
+      asm volatile(
+          "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+          " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(d),
+          "l"(m), "r"(c0), "r"(c1), "r"(zc[0]), "r"(zc[1]), "r"(zc[2]), "r"(b)
+          : "memory");
+      break;
+  }
+}
+
+// Tiled TMA store of a box to a rank-(2 + nb) map (bulk async-group).
+__device__ __forceinline__ void tma_store_nd(const CUtensorMap *map, const void *smem_src,
+                                             int32_t c0, int32_t c1, int nb, const int32_t *zc) {
+  const uint64_t m = reinterpret_cast<uint64_t>(map);
+  const uint32_t s = smem_addr(smem_src);
+  switch (nb) {
+    case 0:
+      asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                   ::"l"(m), "r"(s), "r"(c0), "r"(c1)
+                   : "memory");
+      break;
+    case 1:
+      asm volatile(
+          "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+              m),
+          "r"(s), "r"(c0), "r"(c1), "r"(zc[0])
+          : "memory");
+      break;
+    case 2:
+      asm volatile(
+          "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::
+              "l"(m),
+          "r"(s), "r"(c0), "r"(c1), "r"(zc[0]), "r"(zc[1])
+          : "memory");
+      break;
+    default:
+      asm volatile(
+          "cp.async.bulk.tensor.5d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5, %6}], "
+          "[%1];" ::"l"(m),
+          "r"(s), "r"(c0), "r"(c1), "r"(zc[0]), "r"(zc[1]), "r"(zc[2])
+          : "memory");
+      break;
+  }
+}
+
 // Tiled TMA store of a shared-memory box to global memory (no multicast;
 // elements outside the tensor are not written), tracked by bulk async-groups.
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *smem_src,

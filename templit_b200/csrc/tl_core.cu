@@ -41,6 +41,14 @@ uint32_t *device_status_ptr() {
   return cached[dev];
 }
 
+// Moves the status word into a mailbox and clears it, in stream order.
+__global__ void status_take_kernel(uint32_t *status, uint32_t *mailbox) {
+  *mailbox = *status;
+  *status = 0;
+}
+
+__device__ uint32_t g_status_mailbox;
+
 }  // namespace tl
 
 using namespace tl;
@@ -70,6 +78,23 @@ int tl_device_status(uint32_t *flags, void *stream) {
                     "clear status");
   }
   return rc;
+}
+
+int tl_device_status_enqueue(uint32_t *host_flags, void *stream) {
+  if (!host_flags) return fail(TL_ERR_INVALID, "tl_device_status_enqueue: null flags");
+  uint32_t *status = device_status_ptr();
+  uint32_t *mailbox = nullptr;
+  int rc = check_cuda(cudaGetSymbolAddress(reinterpret_cast<void **>(&mailbox), g_status_mailbox),
+                      "status mailbox");
+  if (rc) return rc;
+  if (!status) return fail(TL_ERR_CUDA, "tl_device_status_enqueue: no status word");
+  cudaStream_t s = as_stream(stream);
+  status_take_kernel<<<1, 1, 0, s>>>(status, mailbox);
+  rc = launch_status("tl_device_status_enqueue");
+  if (rc) return rc;
+  return check_cuda(cudaMemcpyAsync(host_flags, mailbox, sizeof(uint32_t),
+                                    cudaMemcpyDeviceToHost, s),
+                    "status copy");
 }
 
 int tl_malloc(void **ptr, size_t bytes) {
@@ -156,6 +181,17 @@ int tl_event_elapsed_ms(float *ms, void *start, void *end) {
   return check_cuda(cudaEventElapsedTime(ms, static_cast<cudaEvent_t>(start),
                                          static_cast<cudaEvent_t>(end)),
                     "cudaEventElapsedTime");
+}
+
+int tl_event_query(void *event, int *done) {
+  if (!event || !done) return fail(TL_ERR_INVALID, "tl_event_query: null pointer");
+  const cudaError_t e = cudaEventQuery(static_cast<cudaEvent_t>(event));
+  if (e == cudaErrorNotReady) {
+    *done = 0;
+    return TL_OK;
+  }
+  *done = 1;
+  return check_cuda(e, "cudaEventQuery");
 }
 
 int tl_graph_capture_begin(void *stream) {

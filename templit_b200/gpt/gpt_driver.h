@@ -131,15 +131,20 @@ public:
     targets_.get_value().set(std::span<const uint32_t>(targets, n));
   }
 
+  // The reference loop body (src/train.cpp:120-157): zero_grad, forward,
+  // read the losses, backward, step.  The losses are read after the
+  // backward and optimiser windows are queued (nothing in them writes the
+  // loss tensor), so with a deferred wait the host records those windows
+  // while the GPU still runs the forward pass.
   float train_step() override {
     compiled_->zero_grad();
     const Mat loss = compiled_->forward();
-    loss.read(losses_);
-    double acc = 0.0;
-    for (float v : losses_) acc += v;
     compiled_->backward(root_grad_);
     if (cfg_.clip > 0.0f) compiled_->step(cfg_.clip);
     else compiled_->step();
+    loss.read(losses_);
+    double acc = 0.0;
+    for (float v : losses_) acc += v;
     return static_cast<float>(acc / static_cast<double>(losses_.size()));
   }
 

@@ -70,6 +70,7 @@ int tlg_create(const tlg_config *config, void **handle) {
     h->runtime->set_fusion(config->fusion != 0);
     h->runtime->set_graphs(config->graphs != 0);
     h->runtime->set_gemm_precision(config->gemm_precision);
+    h->runtime->set_deferred_wait(config->deferred_wait != 0);
     h->driver = make_driver(*config, *h->runtime);
     *handle = h.release();
   });

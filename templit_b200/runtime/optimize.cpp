@@ -596,6 +596,193 @@ uint64_t fuse_score_softmax(std::vector<Op> &p) {
   return folded;
 }
 
+// ---------------------------------------------- head transposes as strides
+// Dense row-major strides of a shape.
+void dense_strides(const TRef &t, uint64_t (&st)[kMaxRank]) {
+  uint64_t acc = 1;
+  for (int d = t.rank; d-- > 0;) {
+    st[d] = acc;
+    acc *= t.shape[d];
+  }
+}
+
+// Strides, in X's memory, of the dims of Y = transpose(X, a, b).
+void transposed_view(const Op &tr, uint64_t (&st)[kMaxRank]) {
+  uint64_t xs[kMaxRank];
+  dense_strides(tr.t[0], xs);
+  for (int d = 0; d < tr.t[0].rank; ++d) st[d] = xs[d];
+  std::swap(st[tr.i0], st[tr.i1]);
+}
+
+// Re-expresses the product's flattened batch over the `lead` leading dims
+// of shape `dims`: operand X walks them with strides xs (from its view),
+// the other operands densely (their flattened stride split over the dims).
+// False unless the product's batch is exactly those dims, flattened densely
+// for this operand (stride `mat`).
+bool expand_batch(tl_gemm_desc &g, int which, const uint32_t *dims, int lead,
+                  const uint64_t *xs, uint64_t mat) {
+  if (lead > TL_GEMM_MAX_BATCH_RANK) return false;
+  uint64_t *out[3] = {g.a_batch_stride, g.b_batch_stride, g.c_batch_stride};
+  uint64_t count = 1;
+  for (int d = 0; d < lead; ++d) count *= dims[d];
+  if (g.batch_rank == static_cast<uint32_t>(lead) && lead > 1) {
+    // already walked per dim (an earlier fold): this operand must be dense
+    uint64_t inner = mat;
+    for (int d = lead; d-- > 0;) {
+      if (g.batch_shape[d] != dims[d] || out[which][d] != inner) return false;
+      inner *= dims[d];
+    }
+    for (int d = 0; d < lead; ++d) out[which][d] = xs[d];
+    return true;
+  }
+  uint64_t flat[3] = {0, 0, 0};
+  if (g.batch_rank == 0) {
+    if (count != 1) return false;
+  } else {
+    if (g.batch_rank != 1 || g.batch_shape[0] != count) return false;
+    for (int o = 0; o < 3; ++o) flat[o] = out[o][0];
+    if (flat[which] != mat) return false;
+  }
+  uint64_t inner = 1;  // product of dims after d
+  for (int d = lead; d-- > 0;) {
+    g.batch_shape[d] = dims[d];
+    for (int o = 0; o < 3; ++o) out[o][d] = o == which ? xs[d] : flat[o] * inner;
+    inner *= dims[d];
+  }
+  g.batch_rank = static_cast<uint32_t>(lead);
+  return true;
+}
+
+// transpose(X -> Y) swapping dims of a [..., T, H, D]-style tensor, with Y
+// read only as a GEMM operand: the GEMMs read X through strides (the batch
+// walks the view's leading dims, the row stride is the view's) and the
+// transpose goes.  GEMM(...) -> O; transpose(O -> Z): the GEMM writes Z
+// through strides.  Attention's head split / merge
+// (expr::transpose<1, 2> of nn::MultiHeadAttention, include/nn/multi_head.h)
+// in both directions.
+uint64_t fold_head_transposes(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t i = 0; i < p.size(); ++i) {
+    Op &tr = p[i];
+    if (tr.dead || tr.kind != Kind::Transpose) continue;
+    const TRef X = tr.t[0], Y = tr.t[1];
+    const int r = X.rank;
+    if (r < 3 || Y.rank != r) continue;
+    uint64_t ys[kMaxRank];
+    transposed_view(tr, ys);
+
+    // ---- input side: every reader of Y is a GEMM operand
+    std::vector<size_t> readers;
+    bool ok = true;
+    size_t j = i;
+    while (ok) {
+      j = first_reader(p, j, Y.id);
+      if (j == kNone) break;
+      const Op &mm = p[j];
+      if (mm.kind != Kind::Gemm || mm.gemm.beta != 0.0f || same(mm.t[2], Y) ||
+          same(mm.t[3], Y) || same(mm.t[5], Y) || (same(mm.t[0], Y) && same(mm.t[1], Y)))
+        ok = false;
+      else
+        readers.push_back(j);
+    }
+    if (ok && !readers.empty() && dead_after(p, readers.back(), Y.id) &&
+        unchanged_between(p, i, readers.back(), X.id)) {
+      std::vector<Op> trial;
+      for (size_t k : readers) {
+        Op mm = p[k];
+        tl_gemm_desc &g = mm.gemm;
+        const int which = same(mm.t[0], Y) ? 0 : 1;
+        const bool trans = which == 0 ? g.trans_a : g.trans_b;
+        // the operand as stored by the GEMM: [rows][cols] = Y's last two dims
+        const uint32_t rows = which == 0 ? (trans ? g.k : g.m) : (trans ? g.n : g.k);
+        const uint32_t cols = which == 0 ? (trans ? g.m : g.k) : (trans ? g.k : g.n);
+        if (Y.shape[r - 2] != rows || Y.shape[r - 1] != cols || mm.i1 != 0) {
+          ok = false;
+          break;
+        }
+        uint64_t ld;
+        bool flip;
+        if (ys[r - 1] == 1) {
+          ld = ys[r - 2];
+          flip = false;
+        } else if (ys[r - 2] == 1) {
+          ld = ys[r - 1];
+          flip = true;
+        } else {
+          ok = false;
+          break;
+        }
+        if (!expand_batch(g, which, Y.shape, r - 2, ys, static_cast<uint64_t>(rows) * cols)) {
+          ok = false;
+          break;
+        }
+        if (which == 0) {
+          mm.t[0] = X;
+          g.a = static_cast<const float *>(X.p);
+          g.lda = ld;
+          if (flip) g.trans_a = !g.trans_a;
+        } else {
+          mm.t[1] = X;
+          g.b = static_cast<const float *>(X.p);
+          g.ldb = ld;
+          if (flip) g.trans_b = !g.trans_b;
+        }
+        trial.push_back(std::move(mm));
+      }
+      if (ok) {
+        for (size_t k = 0; k < readers.size(); ++k) p[readers[k]] = std::move(trial[k]);
+        tr.dead = true;
+        ++folded;
+        continue;
+      }
+    }
+
+    // ---- output side: a GEMM produced X for this transpose only
+    const size_t x = last_writer(p, i, X.id);
+    if (x == kNone) continue;
+    Op &mm = p[x];
+    if (mm.kind != Kind::Gemm || mm.gemm.beta != 0.0f || mm.gemm.gelu_out || mm.t[5].p ||
+        mm.t[2].id != X.id || mm.i1 != 0)
+      continue;
+    if (first_reader(p, x, X.id) != i || !dead_after(p, i, X.id) ||
+        !untouched_between(p, x, i, Y.id) || reads(access(mm), Y.id))
+      continue;
+    tl_gemm_desc g = mm.gemm;
+    if (X.shape[r - 2] != g.m || X.shape[r - 1] != g.n || (g.ldc != 0 && g.ldc != g.n)) continue;
+    // strides of X's dims inside Y (Y dense)
+    uint64_t yd[kMaxRank], xs[kMaxRank];
+    dense_strides(Y, yd);
+    for (int d = 0; d < r; ++d) xs[d] = yd[d];
+    std::swap(xs[tr.i0], xs[tr.i1]);
+    uint64_t ldc;
+    if (xs[r - 1] == 1) {
+      ldc = xs[r - 2];
+    } else if (xs[r - 2] == 1 && !g.bias) {
+      // C^T = B^T A^T: the product's rows become the stored columns
+      std::swap(g.a, g.b);
+      std::swap(g.m, g.n);
+      std::swap(g.lda, g.ldb);
+      const int32_t ta = g.trans_a;
+      g.trans_a = !g.trans_b;
+      g.trans_b = !ta;
+      for (uint32_t d = 0; d < g.batch_rank; ++d) std::swap(g.a_batch_stride[d], g.b_batch_stride[d]);
+      std::swap(mm.t[0], mm.t[1]);
+      ldc = xs[r - 1];
+    } else {
+      continue;
+    }
+    if (!expand_batch(g, 2, X.shape, r - 2, xs, static_cast<uint64_t>(g.m) * g.n)) continue;
+    g.ldc = ldc;
+    g.c = static_cast<float *>(Y.p);
+    mm.gemm = g;
+    mm.t[2].p = Y.p;
+    mm.t[2].id = Y.id;
+    tr.dead = true;
+    ++folded;
+  }
+  return folded;
+}
+
 // --------------------------------------------------------- copy forwarding
 bool elementwise(Kind k) {
   return k == Kind::Binary || k == Kind::Scalar || k == Kind::Unary || k == Kind::Copy ||
@@ -996,8 +1183,11 @@ uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live) {
     folded += fuse_rmsnorm_backward(prog);
     folded += fuse_pointwise_backward(prog);
   }
-  // Folds that change an op's inputs (an added operand, a divisor) come last
-  // so they cannot hide a repeat from the common-subexpression pass.
+  // Folds that change an op's inputs (an added operand, a divisor, strided
+  // operands) come last so they cannot hide a repeat from the
+  // common-subexpression pass.
+  folded += fold_head_transposes(prog);
+  folded += fold_head_transposes(prog);  // a second transpose of the same product
   folded += fuse_gemm_accumulate(prog);
   folded += fuse_row_backward_tails(prog);
   folded += fuse_score_softmax(prog);

@@ -150,6 +150,13 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
     uint64_t last_use = 0;
   };
   std::unordered_map<std::string, Plan> plans;
+
+  // deferred wait: this window's status word is moved to pinned memory in
+  // stream order and read by a later wait() once its event has passed
+  bool deferred_wait = false;
+  uint32_t *status_host = nullptr;
+  void *status_event = nullptr;
+  bool status_pending = false;
   std::chrono::steady_clock::time_point record_t0;
 
   // Liveness view that remembers which buffers it reported window-local.
@@ -329,8 +336,43 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
     return push(k);
   }
 
+  uint32_t deferred_status() {
+    uint32_t flags = 0;
+    if (!status_host) {
+      void *p = nullptr;
+      check(tl_host_alloc(&p, sizeof(uint32_t)), "status staging");
+      status_host = static_cast<uint32_t *>(p);
+      check(tl_event_create(&status_event), "status event");
+    }
+    if (status_pending) {
+      int done = 0;
+      check(tl_event_query(status_event, &done), "status event");
+      if (done) {
+        flags = *status_host;
+        status_pending = false;
+      }
+    }
+    if (!status_pending) {
+      // flags raised since the last move stay in the device word until then
+      check(tl_device_status_enqueue(status_host, cuda::stream()), "status");
+      check(tl_event_record(status_event, cuda::stream()), "status event");
+      status_pending = true;
+    }
+    return flags;
+  }
+
   void release_resources() noexcept {
     for (auto &kv : graph_cache) tl_graph_destroy(kv.second.exec);
+    if (status_host) {
+      if (cuda::initialised()) {
+        tl_stream_sync(cuda::stream());
+        tl_host_free(status_host);
+        tl_event_destroy(status_event);
+      }
+      status_host = nullptr;
+      status_event = nullptr;
+      status_pending = false;
+    }
     graph_cache.clear();
     seen_once.clear();
     if (workspace.ptr) {
@@ -773,7 +815,8 @@ void Runtime::wait() {
     throw std::logic_error("CUDA runtime execution has not been submitted");
   impl_->state = Impl::State::Idle;
   uint32_t flags = 0;
-  check(tl_device_status(&flags, cuda::stream()), "CUDA runtime wait");
+  if (impl_->deferred_wait) flags = impl_->deferred_status();
+  else check(tl_device_status(&flags, cuda::stream()), "CUDA runtime wait");
   if (flags & TL_FLAG_INDEX_RANGE)
     throw std::out_of_range("embedding index out of range of the embedding table");
   if (flags & TL_FLAG_TIMEOUT)
@@ -815,6 +858,7 @@ void Runtime::end_profile() {
 }
 
 void Runtime::set_fusion(bool enabled) { impl_->fusion = enabled; }
+void Runtime::set_deferred_wait(bool enabled) { impl_->deferred_wait = enabled; }
 void Runtime::set_graphs(bool enabled) { impl_->graphs = enabled; }
 void Runtime::set_gemm_precision(int precision) {
   if (precision != TL_GEMM_TF32 && precision != TL_GEMM_FP32)

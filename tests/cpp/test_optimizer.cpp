@@ -441,6 +441,36 @@ void row_backward_tails() {
   require(u.size() == 1 && u[0]->t[3].id == a.id && u[0]->t[4].id == a.id, "added in place");
 }
 
+
+// attention head split / merge: the GEMMs address the [B, T, H, D] tensors
+// through strides and both transposes go
+void head_transposes_become_strides() {
+  auto q = tensor({4, 192, 6, 64}), qh = tensor({4, 6, 192, 64}), kt = tensor({4, 6, 64, 192});
+  auto s1 = tensor({4, 6, 192, 192}), pv = tensor({4, 6, 192, 64}), o = tensor({4, 192, 6, 64});
+  auto v = tensor({4, 6, 192, 64});
+  Op split = transpose(q, qh);
+  split.i0 = 1;
+  split.i1 = 2;
+  Op merge = transpose(pv, o);
+  merge.i0 = 1;
+  merge.i1 = 2;
+  std::vector<Op> p = {split, gemm(qh, kt, s1, 192, 192, 64, 24), release(qh),
+                       gemm(s1, v, pv, 192, 64, 192, 24), merge, release(pv)};
+  require(optimize(p, nullptr) == 2, "both transposes folded");
+  auto l = live(p);
+  require(l.size() == 2, "two products left");
+  const tl_gemm_desc &g0 = l[0]->gemm;
+  require(l[0]->t[0].id == q.id && g0.lda == 384 && g0.batch_rank == 2 &&
+              g0.batch_shape[0] == 4 && g0.batch_shape[1] == 6 &&
+              g0.a_batch_stride[0] == 192 * 384 && g0.a_batch_stride[1] == 64 &&
+              g0.b_batch_stride[0] == 6 * 64 * 192 && g0.b_batch_stride[1] == 64 * 192,
+          "scores read the heads of Q in place");
+  const tl_gemm_desc &g1 = l[1]->gemm;
+  require(l[1]->t[2].id == o.id && g1.ldc == 384 && g1.batch_rank == 2 &&
+              g1.c_batch_stride[0] == 192 * 384 && g1.c_batch_stride[1] == 64,
+          "the output lands in [B, T, H, D] directly");
+}
+
 }  // namespace
 
 int main() {
@@ -464,6 +494,7 @@ int main() {
       {"residual_add_into_gemm", residual_add_into_gemm},
       {"attention_scores_into_softmax", attention_scores_into_softmax},
       {"row_backward_tails", row_backward_tails},
+      {"head_transposes_become_strides", head_transposes_become_strides},
   };
   for (const auto &[name, fn] : cases) {
     try {

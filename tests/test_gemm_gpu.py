@@ -8,6 +8,7 @@ Tolerance (<= 1e-3 relative for TF32 paths):
   TF32: ||C - C_ref||_F / ||C_ref||_F <= 1e-3 and
         max|C - C_ref| <= 4e-3 * max|C_ref|
   FP32: |C - C_ref| <= 1e-5 * (|A| |B|) elementwise bound."""
+import ctypes
 import itertools
 
 import numpy as np
@@ -176,3 +177,57 @@ def test_zero_and_empty(dev):
     big = np.broadcast_to(np.eye(256, dtype=np.float32), (3, 256, 256)).copy()
     vb = (np.arange(3 * 256 * 256) % 31 - 15).astype(np.float32).reshape(3, 256, 256)
     np.testing.assert_array_equal(dev.gemm(big, vb), vb)
+
+
+def _strided_gemm(dev, a, b, c_shape, m, n, k, trans_a, trans_b, batch, sa, sb, sc,
+                  lda, ldb, ldc, precision):
+    """tl_gemm on raw buffers with explicit strides; returns C's buffer."""
+    ta, tb = dev.t(a), dev.t(b)
+    tc = dev.empty(c_shape)
+    d = capi.TlGemmDesc()
+    d.a, d.b, d.c = ta.data_ptr(), tb.data_ptr(), tc.data_ptr()
+    d.m, d.n, d.k = m, n, k
+    d.trans_a, d.trans_b = int(trans_a), int(trans_b)
+    d.precision = precision
+    d.batch_rank = len(batch)
+    for i, s in enumerate(batch):
+        d.batch_shape[i] = s
+        d.a_batch_stride[i], d.b_batch_stride[i], d.c_batch_stride[i] = sa[i], sb[i], sc[i]
+    d.lda, d.ldb, d.ldc = lda, ldb, ldc
+    nbytes = dev.lib.tl_gemm_workspace_size(ctypes.byref(d))
+    ws = dev.ws(nbytes) if nbytes else None
+    if ws is not None:
+        d.workspace, d.workspace_bytes = ws.data_ptr(), nbytes
+    dev.call("tl_gemm", ctypes.byref(d), dev.stream)
+    return dev.host(tc)
+
+
+@pytest.mark.parametrize("precision", [capi.TL_GEMM_TF32, capi.TL_GEMM_FP32])
+def test_head_strided_operands(dev, precision):
+    """Attention heads read and written in place in [B, T, H, D] tensors:
+    batch dims (B, H) with strides (T*H*D, D), row stride H*D."""
+    r = np.random.default_rng(21)
+    B, T, H, D = 8, 192, 6, 64
+    q = r.standard_normal((B, T, H, D)).astype(np.float32)
+    kk = r.standard_normal((B, T, H, D)).astype(np.float32)
+    v = r.standard_normal((B, T, H, D)).astype(np.float32)
+    qh, kh, vh = (np.swapaxes(x, 1, 2) for x in (q, kk, v))  # [B, H, T, D] views
+    hs = (T * H * D, D)
+    # S = Qh Kh^T (NT): C dense [B, H, T, T]
+    s = _strided_gemm(dev, q, kk, (B, H, T, T), T, T, D, False, True, (B, H), hs, hs,
+                      (H * T * T, T * T), H * D, H * D, 0, precision)
+    want = np.matmul(qh.astype(np.float64), np.swapaxes(kh, -1, -2).astype(np.float64))
+    check = check_tf32 if precision == capi.TL_GEMM_TF32 else (
+        lambda g, w: np.testing.assert_allclose(g, w, rtol=1e-4, atol=1e-3))
+    check(s, want)
+    # O = P Vh written straight into [B, T, H, D] (C row stride H*D)
+    p = r.random((B, H, T, T)).astype(np.float32)
+    o = _strided_gemm(dev, p, v, (B, T, H, D), T, D, T, False, False, (B, H),
+                      (H * T * T, T * T), hs, hs, 0, H * D, H * D, precision)
+    want = np.swapaxes(np.matmul(p.astype(np.float64), vh.astype(np.float64)), 1, 2)
+    check(o, want)
+    # dK^T-style TN product from a head view: Qh^T P (A stored [K=T, M=D], lda = H*D)
+    g = _strided_gemm(dev, q, p, (B, H, D, T), D, T, T, True, False, (B, H), hs,
+                      (H * T * T, T * T), (H * D * T, D * T), H * D, 0, 0, precision)
+    want = np.matmul(np.swapaxes(qh, -1, -2).astype(np.float64), p.astype(np.float64))
+    check(g, want)

@@ -20,10 +20,11 @@ from templit_b200 import capi
 pytestmark = pytest.mark.gpu
 
 
-def config(batch, seq, precision=capi.TL_GEMM_TF32, fusion=1, graphs=1, seed=11):
+def config(batch, seq, precision=capi.TL_GEMM_TF32, fusion=1, graphs=1, seed=11, deferred=1):
     return capi.TlgConfig(family=4, batch=batch, seq=seq, seed=seed, init_std=0.02, lr=3e-4,
                           beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, clip=1.0, world=1,
-                          fusion=fusion, graphs=graphs, gemm_precision=precision)
+                          fusion=fusion, graphs=graphs, gemm_precision=precision,
+                          deferred_wait=deferred)
 
 
 class CudaGPT:
@@ -144,8 +145,8 @@ def test_deterministic_and_graph_replay_is_bit_exact():
     x, y = zipf(rng, 4, 64)
     runs = []
     p0 = None
-    for graphs, fusion in ((1, 1), (0, 1), (0, 0), (1, 1)):
-        g = CudaGPT(config(4, 64, graphs=graphs, fusion=fusion))
+    for graphs, fusion, deferred in ((1, 1, 1), (0, 1, 1), (0, 0, 1), (1, 1, 0)):
+        g = CudaGPT(config(4, 64, graphs=graphs, fusion=fusion, deferred=deferred))
         if p0 is None:
             p0 = g.params()
         g.set_batch(x, y)
@@ -154,7 +155,7 @@ def test_deterministic_and_graph_replay_is_bit_exact():
         g.close()
     (l1, p1, s1), (l2, p2, s2), (l3, p3, s3), (l4, p4, _) = runs
     assert l1 == l2 and np.array_equal(p1, p2)  # replay == eager, bit for bit
-    assert l1 == l4 and np.array_equal(p1, p4)  # run to run, bit for bit
+    assert l1 == l4 and np.array_equal(p1, p4)  # run to run (and deferred wait), bit for bit
     assert s1["replays"] > 0 and s1["captures"] > 0
     assert s1["plan_hits"] > 0 and s3["plan_hits"] == 0  # optimised programs reused
     assert s2["replays"] == 0
