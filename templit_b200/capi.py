@@ -46,7 +46,7 @@ class TlGemmDesc(Structure):
                 ("b_batch_stride", c_uint64 * TL_GEMM_MAX_BATCH_RANK),
                 ("c_batch_stride", c_uint64 * TL_GEMM_MAX_BATCH_RANK),
                 ("workspace", c_void_p), ("workspace_bytes", c_uint64),
-                ("addend", c_void_p)]
+                ("addend", c_void_p), ("lda", c_uint64), ("ldb", c_uint64), ("ldc", c_uint64)]
 
 
 class TlgConfig(Structure):

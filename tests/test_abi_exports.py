@@ -65,3 +65,30 @@ def test_errors_without_gpu_are_reported_not_raised():
     assert lib.tl_argmax(None, 0, None, None, 0, None) == capi.TL_ERR_INVALID
     assert lib.tl_adamw(None, None, None, None, None, None, None, None, None, 1e-8, 0, 4,
                         None) == capi.TL_ERR_INVALID
+
+
+def test_struct_layouts_match_the_headers(tmp_path):
+    """The ctypes mirrors of the C structs have the C compiler's size and
+    field offsets (a missing field would let the library read past the
+    caller's struct)."""
+    structs = {"tl_gemm_desc": capi.TlGemmDesc, "tl_param_slot": capi.TlParamSlot,
+               "tlg_config": capi.TlgConfig}
+    lines = ['#include <stddef.h>', '#include <stdio.h>', '#include "templit_cuda.h"',
+             '#include "templit_gpt.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for field, _ in py._fields_:
+            lines.append(f'  printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines.append("  return 0;\n}")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    cuda_inc = "/usr/local/cuda/include"
+    rc = os.system(f"gcc -I{ROOT}/include -I{cuda_inc} {src} -o {exe} 2> {tmp_path}/err.txt")
+    if rc != 0:
+        pytest.skip("no C compiler for the layout check: " + open(f"{tmp_path}/err.txt").read())
+    got = dict(line.rsplit(" ", 1) for line in os.popen(str(exe)).read().splitlines())
+    for cname, py in structs.items():
+        assert int(got[f"{cname} size"]) == ctypes.sizeof(py), cname
+        for field, _ in py._fields_:
+            assert int(got[f"{cname} {field}"]) == getattr(py, field).offset, (cname, field)
