@@ -4,7 +4,7 @@
 //
 // The reference scatters with one float atomic per element, so its result
 // depends on arrival order.  Here the scatter runs in two deterministic
-// phases: every chunk of 256 ids is sorted in shared memory and summed per
+// phases: every chunk of 64 ids is sorted in shared memory and summed per
 // distinct id (position order), then every destination row folds its chunk
 // partials in a fixed order.  Every run is bit-identical, and a hot id (a
 // frequent token) is spread over all chunks instead of one serial loop.  Ids outside the table never touch memory:
@@ -42,7 +42,8 @@ gather_kernel(const float *__restrict__ w, uint32_t n_rows, uint32_t dim,
   }
 }
 
-constexpr uint32_t kChunk = 256;  // ids per chunk (one CTA, one thread per id)
+constexpr uint32_t kChunk = 64;      // ids per chunk (phase 1 CTA)
+constexpr uint32_t kThreads = 256;   // threads per CTA, both phases
 constexpr uint32_t kInvalid = 0xffffffffu;
 
 // Phase 1: CTA p takes ids [p * kChunk, (p + 1) * kChunk), sorts the
@@ -51,30 +52,35 @@ constexpr uint32_t kInvalid = 0xffffffffu;
 //   partial[p * kChunk + u, :] = sum of values[i, :] over the chunk's i with
 //                                ids[i] == id, in position order,
 //   uid[p * kChunk + u] = id, and ucount[p] = number of distinct ids.
+// The sums spread (distinct id, column group) items over all threads, four
+// items at a time so their first loads are in flight together.
 template <int V>
-__global__ void __launch_bounds__(kChunk)
+__global__ void __launch_bounds__(kThreads)
 chunk_sum_kernel(const float *__restrict__ values, const uint32_t *__restrict__ ids,
                  uint32_t n_ids, uint32_t dim, uint32_t n_rows, float *partial,
                  uint32_t *uid, uint32_t *ucount, uint32_t *status) {
   __shared__ unsigned long long key[kChunk];
   __shared__ uint32_t gstart[kChunk + 1];
   __shared__ uint32_t warp_heads[kChunk / 32], warp_valid[kChunk / 32];
+  __shared__ uint32_t n_groups;
   const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const uint64_t first = static_cast<uint64_t>(blockIdx.x) * kChunk;
-  uint32_t id = kInvalid;
-  if (first + t < n_ids) {
-    id = ids[first + t];
-    if (id >= n_rows) {
-      raise_flag(status, TL_FLAG_INDEX_RANGE);
-      id = kInvalid;
+  if (t < kChunk) {
+    uint32_t id = kInvalid;
+    if (first + t < n_ids) {
+      id = ids[first + t];
+      if (id >= n_rows) {
+        raise_flag(status, TL_FLAG_INDEX_RANGE);
+        id = kInvalid;
+      }
     }
+    key[t] = (static_cast<unsigned long long>(id) << 32) | t;
   }
-  key[t] = (static_cast<unsigned long long>(id) << 32) | t;
   __syncthreads();
   for (uint32_t k = 2; k <= kChunk; k <<= 1) {
     for (uint32_t j = k >> 1; j > 0; j >>= 1) {
       const uint32_t o = t ^ j;
-      if (o > t) {
+      if (t < kChunk && o > t) {
         const unsigned long long a = key[t], b = key[o];
         if ((a > b) == ((t & k) == 0)) {
           key[t] = b;
@@ -84,56 +90,82 @@ chunk_sum_kernel(const float *__restrict__ values, const uint32_t *__restrict__ 
       __syncthreads();
     }
   }
-  // group heads and their ranks (a block-wide exclusive count)
-  const uint32_t my = static_cast<uint32_t>(key[t] >> 32);
-  const bool valid = my != kInvalid;
-  const bool head = valid && (t == 0 || static_cast<uint32_t>(key[t - 1] >> 32) != my);
-  const uint32_t hb = __ballot_sync(0xffffffffu, head), vb = __ballot_sync(0xffffffffu, valid);
-  if (lane == 0) {
-    warp_heads[warp] = __popc(hb);
-    warp_valid[warp] = __popc(vb);
+  // group heads and their ranks (warps covering the chunk)
+  if (t < kChunk) {
+    const uint32_t my = static_cast<uint32_t>(key[t] >> 32);
+    const bool valid = my != kInvalid;
+    const bool head = valid && (t == 0 || static_cast<uint32_t>(key[t - 1] >> 32) != my);
+    const uint32_t hb = __ballot_sync(0xffffffffu, head), vb = __ballot_sync(0xffffffffu, valid);
+    if (lane == 0) {
+      warp_heads[warp] = __popc(hb);
+      warp_valid[warp] = __popc(vb);
+    }
   }
   __syncthreads();
-  uint32_t before = 0, groups = 0, n_valid = 0;
-  for (uint32_t w = 0; w < kChunk / 32; ++w) {
-    if (w < warp) before += warp_heads[w];
-    groups += warp_heads[w];
-    n_valid += warp_valid[w];
-  }
-  const uint32_t g = before + __popc(hb & ((1u << lane) - 1u));
-  if (head) {
-    gstart[g] = t;
-    uid[first + g] = my;
-  }
-  if (t == 0) {
-    gstart[groups] = n_valid;
-    ucount[blockIdx.x] = groups;
+  if (t < kChunk) {
+    const uint32_t my = static_cast<uint32_t>(key[t] >> 32);
+    const bool valid = my != kInvalid;
+    const bool head = valid && (t == 0 || static_cast<uint32_t>(key[t - 1] >> 32) != my);
+    const uint32_t hb = __ballot_sync(0xffffffffu, head);
+    uint32_t before = 0, groups = 0, n_valid = 0;
+    for (uint32_t w = 0; w < kChunk / 32; ++w) {
+      if (w < warp) before += warp_heads[w];
+      groups += warp_heads[w];
+      n_valid += warp_valid[w];
+    }
+    const uint32_t g = before + __popc(hb & ((1u << lane) - 1u));
+    if (head) {
+      gstart[g] = t;
+      uid[first + g] = my;
+    }
+    if (t == 0) {
+      gstart[groups] = n_valid;
+      ucount[blockIdx.x] = groups;
+      n_groups = groups;
+    }
   }
   __syncthreads();
-  for (uint32_t q = warp; q < groups; q += kChunk / 32) {
-    const uint32_t b = gstart[q], e = gstart[q + 1];
-    float *dst = partial + (first + q) * dim;
-    for (uint32_t d = lane * V; d < dim; d += 32 * V) {
-      if constexpr (V == 4) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (uint32_t k = b; k < e; ++k) {
-          const uint32_t pos = static_cast<uint32_t>(key[k] & 0xffffffffu);
-          const float4 v =
-              *reinterpret_cast<const float4 *>(values + (first + pos) * dim + d);
-          acc.x += v.x;
-          acc.y += v.y;
-          acc.z += v.z;
-          acc.w += v.w;
-        }
-        *reinterpret_cast<float4 *>(dst + d) = acc;
-      } else {
-        float acc = 0.0f;
-        for (uint32_t k = b; k < e; ++k) {
-          const uint32_t pos = static_cast<uint32_t>(key[k] & 0xffffffffu);
-          acc += values[(first + pos) * dim + d];
-        }
-        dst[d] = acc;
+  const uint32_t cols = dim / V, total = n_groups * cols;
+  for (uint32_t base = t; base < total; base += 4 * kThreads) {
+    float acc[4][V];
+    uint32_t q[4], col[4], b[4], e[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t item = base + u * kThreads;
+      q[u] = item / cols;
+      col[u] = (item % cols) * V;
+      b[u] = e[u] = 0;
+#pragma unroll
+      for (int v = 0; v < V; ++v) acc[u][v] = 0.0f;
+      if (item < total) {
+        b[u] = gstart[q[u]];
+        e[u] = gstart[q[u] + 1];
       }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      for (uint32_t k = b[u]; k < e[u]; ++k) {
+        const uint32_t pos = static_cast<uint32_t>(key[k] & 0xffffffffu);
+        const float *src = values + (first + pos) * dim + col[u];
+        if constexpr (V == 4) {
+          const float4 x = *reinterpret_cast<const float4 *>(src);
+          acc[u][0] += x.x;
+          acc[u][1] += x.y;
+          acc[u][2] += x.z;
+          acc[u][3] += x.w;
+        } else {
+          acc[u][0] += *src;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (b[u] == e[u]) continue;
+      float *dst = partial + (first + q[u]) * dim + col[u];
+      if constexpr (V == 4)
+        *reinterpret_cast<float4 *>(dst) = make_float4(acc[u][0], acc[u][1], acc[u][2], acc[u][3]);
+      else
+        *dst = acc[u][0];
     }
   }
 }
@@ -143,13 +175,13 @@ chunk_sum_kernel(const float *__restrict__ values, const uint32_t *__restrict__ 
 // chunks; warp w folds the chunks c with c % 8 == w in increasing order, and
 // warp 0 folds the 8 warp sums in warp order: a fixed summation order.
 template <int V>
-__global__ void __launch_bounds__(kChunk)
+__global__ void __launch_bounds__(kThreads)
 row_combine_kernel(const float *__restrict__ partial, const uint32_t *__restrict__ uid,
                    const uint32_t *__restrict__ ucount, uint32_t n_chunks, uint32_t dim,
                    const float *base, float *dst) {
   using Vec = typename std::conditional<V == 4, float4, float>::type;
-  __shared__ int slot[kChunk];
-  __shared__ Vec wsum[kChunk / 32][32];
+  __shared__ int slot[kThreads];
+  __shared__ Vec wsum[kThreads / 32][32];
   const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const uint32_t r = blockIdx.x;
   const uint32_t d = blockIdx.y * 32 * V + lane * V;
@@ -157,7 +189,7 @@ row_combine_kernel(const float *__restrict__ partial, const uint32_t *__restrict
   float acc[V];
 #pragma unroll
   for (int v = 0; v < V; ++v) acc[v] = 0.0f;
-  for (uint32_t round = 0; round < n_chunks; round += kChunk) {
+  for (uint32_t round = 0; round < n_chunks; round += kThreads) {
     const uint32_t c = round + t;
     int found = -1;
     if (c < n_chunks) {
@@ -172,8 +204,8 @@ row_combine_kernel(const float *__restrict__ partial, const uint32_t *__restrict
     }
     slot[t] = found;
     __syncthreads();
-    const uint32_t in_round = min(kChunk, n_chunks - round);
-    for (uint32_t q = warp; q < in_round; q += kChunk / 32) {
+    const uint32_t in_round = min(kThreads, n_chunks - round);
+    for (uint32_t q = warp; q < in_round; q += kThreads / 32) {
       const int u = slot[q];
       if (u < 0 || !in) continue;
       const float *src = partial + ((static_cast<uint64_t>(round + q)) * kChunk + u) * dim + d;
@@ -196,7 +228,7 @@ row_combine_kernel(const float *__restrict__ partial, const uint32_t *__restrict
   float s[V];
 #pragma unroll
   for (int v = 0; v < V; ++v) s[v] = 0.0f;
-  for (uint32_t w = 0; w < kChunk / 32; ++w) {
+  for (uint32_t w = 0; w < kThreads / 32; ++w) {
     const float *x = reinterpret_cast<const float *>(&wsum[w][lane]);
 #pragma unroll
     for (int v = 0; v < V; ++v) s[v] += x[v];
@@ -271,18 +303,18 @@ int tl_embedding_scatter_add(const float *values, const uint32_t *ids,
                    (!base || aligned16(base)) && aligned16(workspace);
   if (chunks) {
     if (vec)
-      chunk_sum_kernel<4><<<chunks, kChunk, 0, s>>>(values, ids, n_ids, dim, n_rows, partial, uid, ucount, status);
+      chunk_sum_kernel<4><<<chunks, kThreads, 0, s>>>(values, ids, n_ids, dim, n_rows, partial, uid, ucount, status);
     else
-      chunk_sum_kernel<1><<<chunks, kChunk, 0, s>>>(values, ids, n_ids, dim, n_rows, partial, uid, ucount, status);
+      chunk_sum_kernel<1><<<chunks, kThreads, 0, s>>>(values, ids, n_ids, dim, n_rows, partial, uid, ucount, status);
     const int rc = launch_status("tl_embedding_scatter_add chunks");
     if (rc) return rc;
   }
   const uint32_t per = 32 * (vec ? 4 : 1);
   const dim3 grid(n_rows, (dim + per - 1) / per);
   if (vec)
-    row_combine_kernel<4><<<grid, kChunk, 0, s>>>(partial, uid, ucount, chunks, dim, base, dst);
+    row_combine_kernel<4><<<grid, kThreads, 0, s>>>(partial, uid, ucount, chunks, dim, base, dst);
   else
-    row_combine_kernel<1><<<grid, kChunk, 0, s>>>(partial, uid, ucount, chunks, dim, base, dst);
+    row_combine_kernel<1><<<grid, kThreads, 0, s>>>(partial, uid, ucount, chunks, dim, base, dst);
   return launch_status("tl_embedding_scatter_add rows");
 }
 

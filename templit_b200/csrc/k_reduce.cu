@@ -100,6 +100,48 @@ cols_kernel(const float *__restrict__ x, float *out, uint32_t K1, uint32_t R,
   }
 }
 
+// [K1, R, K2] column reduction by blocks: CTA (c, k1, cb) folds rows
+// [c * rchunk, (c + 1) * rchunk) of columns [128 cb, 128 cb + 128): warp w
+// takes rows w, w + 8, ... (float4 per lane, 128-byte rows per warp) and the
+// 8 warp results are folded in warp order, so each split costs one pass over
+// its rows with all 8 warps' loads in flight and the order is fixed.
+template <int OP>
+__global__ void __launch_bounds__(256)
+cols_block_kernel(const float *__restrict__ x, float *out, uint32_t K1, uint32_t R,
+                  uint32_t K2, uint32_t rchunk) {
+  __shared__ float4 part[8][32];
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t c = blockIdx.x, k1 = blockIdx.y;
+  const uint32_t col = blockIdx.z * 128 + lane * 4;
+  const uint32_t r0 = c * rchunk, r1 = min(R, r0 + rchunk);
+  float4 acc = make_float4(rinit<OP>(), rinit<OP>(), rinit<OP>(), rinit<OP>());
+  if (col < K2) {
+    const float *base = x + static_cast<size_t>(k1) * R * K2 + col;
+#pragma unroll 4
+    for (uint32_t r = r0 + warp; r < r1; r += 8) {
+      const float4 v = *reinterpret_cast<const float4 *>(base + static_cast<size_t>(r) * K2);
+      acc.x = rcomb<OP>(acc.x, v.x);
+      acc.y = rcomb<OP>(acc.y, v.y);
+      acc.z = rcomb<OP>(acc.z, v.z);
+      acc.w = rcomb<OP>(acc.w, v.w);
+    }
+  }
+  part[warp][lane] = acc;
+  __syncthreads();
+  if (warp != 0 || col >= K2) return;
+  float4 r = part[0][lane];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) {
+    const float4 v = part[w][lane];
+    r.x = rcomb<OP>(r.x, v.x);
+    r.y = rcomb<OP>(r.y, v.y);
+    r.z = rcomb<OP>(r.z, v.z);
+    r.w = rcomb<OP>(r.w, v.w);
+  }
+  *reinterpret_cast<float4 *>(out + static_cast<size_t>(c) * K1 * K2 +
+                              static_cast<size_t>(k1) * K2 + col) = r;
+}
+
 // Sums `splits` partial planes part[s, i] into out[i].  A CTA owns 32
 // consecutive outputs; warp w folds splits w, w + 8, w + 16, ... in order and
 // warp 0 then folds the 8 warp results in warp order, so the summation order
@@ -173,6 +215,7 @@ struct ReducePlan {
   // rows: rows x cols; cols: K1 x R x K2
   uint32_t rows, cols, K1, R, K2;
   uint32_t splits, chunk;
+  bool block = false;  // kCols by cols_block_kernel
   size_t workspace;   // bytes
   GenericParams gp;
 };
@@ -240,6 +283,21 @@ int make_plan(const uint32_t *x_shape, int x_rank, const uint32_t *out_shape,
     pl.R = g == 2 ? gs[0] : gs[1];
     pl.K2 = g == 2 ? gs[1] : gs[2];
     const uint64_t outs = static_cast<uint64_t>(pl.K1) * pl.K2;
+    if (pl.K2 % 4 == 0 && pl.K1 <= 65535 && pl.K2 / 128 < 65535) {
+      // blocks of 8 warps x 128 columns: about four CTAs per SM, >= 64 rows
+      const uint64_t colblocks = (pl.K2 + 127) / 128;
+      uint64_t want = (4ull * kNumSMs + pl.K1 * colblocks - 1) / (pl.K1 * colblocks);
+      const uint64_t max_splits = (pl.R + 63) / 64;
+      if (want > max_splits) want = max_splits;
+      if (want < 1) want = 1;
+      uint32_t chunk = static_cast<uint32_t>((pl.R + want - 1) / want);
+      chunk = (chunk + 7) & ~7u;
+      pl.splits = (pl.R + chunk - 1) / chunk;
+      pl.chunk = chunk;
+      pl.block = true;
+      pl.workspace = pl.splits > 1 ? outs * pl.splits * sizeof(float) : 0;
+      return TL_OK;
+    }
     const uint64_t lanes = pl.K2 % 4 == 0 ? outs / 4 : outs;
     uint32_t splits = 1;
     if (lanes < target_threads) {
@@ -298,7 +356,10 @@ int run_plan(const ReducePlan &pl, const float *x, float *out, void *ws,
       float *dst = pl.splits > 1 ? static_cast<float *>(ws) : out;
       const uint64_t outs = static_cast<uint64_t>(pl.K1) * pl.K2;
       const uint64_t work = (vec ? outs / 4 : outs) * pl.splits;
-      if (vec)
+      if (pl.block && vec)
+        cols_block_kernel<OP><<<dim3(pl.splits, pl.K1, (pl.K2 + 127) / 128), 256, 0, s>>>(
+            x, dst, pl.K1, pl.R, pl.K2, pl.chunk);
+      else if (vec)
         cols_kernel<OP, 4><<<grid_for(work, 256, 16), 256, 0, s>>>(x, dst, pl.K1, pl.R, pl.K2, pl.splits, pl.chunk);
       else
         cols_kernel<OP, 1><<<grid_for(work, 256, 16), 256, 0, s>>>(x, dst, pl.K1, pl.R, pl.K2, pl.splits, pl.chunk);

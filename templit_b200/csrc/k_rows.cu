@@ -308,9 +308,13 @@ xent_backward_kernel(const float *__restrict__ z, const uint32_t *__restrict__ t
 
 // ---- register-resident rows (cols <= 128 * NV, 128-bit rows) ----------
 // One warp per row keeps the whole row in registers (NV float4 per lane,
-// lane l holding columns 4l + 128i): one pass over memory, the same
-// per-lane order of operations as the looping kernels above, so the
-// results are bit-identical to them.
+// lane l holding columns 4l + 128i): one pass over memory.  The backward
+// and RMSNorm kernels keep the looping kernels' per-lane order of
+// operations (bit-identical results); the softmax is the three-pass form.
+// Register-resident softmax: the row's maximum, then the sum of
+// exp(x - max), then exp(x - max) / sum - the reference kernel's three
+// passes (math.metal:857-882) over registers, without the online
+// rescaling's data-dependent branches (half of a causal score row is -inf).
 template <int NV>
 __global__ void __launch_bounds__(256)
 softmax_regs_kernel(const float *__restrict__ x, const float *__restrict__ divisor,
@@ -320,7 +324,7 @@ softmax_regs_kernel(const float *__restrict__ x, const float *__restrict__ divis
     const float *xr = x + static_cast<size_t>(row) * cols;
     const float *mr = mask ? mask + static_cast<size_t>(row % mask_rows) * cols : nullptr;
     float4 v[NV];
-    float m = -INFINITY, s = 0.0f;
+    float m = -INFINITY;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const uint32_t c = (i * 32 + lane) * 4;
@@ -330,21 +334,28 @@ softmax_regs_kernel(const float *__restrict__ x, const float *__restrict__ divis
         v[i].y = score(v[i].y, divisor, mr, c + 1);
         v[i].z = score(v[i].z, divisor, mr, c + 2);
         v[i].w = score(v[i].w, divisor, mr, c + 3);
-        online_add(m, s, v[i].x);
-        online_add(m, s, v[i].y);
-        online_add(m, s, v[i].z);
-        online_add(m, s, v[i].w);
+        m = fmaxf(m, fmaxf(fmaxf(v[i].x, v[i].y), fmaxf(v[i].z, v[i].w)));
       }
     }
-    warp_online(m, s);
+    m = warp_max(m);
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint32_t c = (i * 32 + lane) * 4;
+      if (c < cols) {
+        v[i] = make_float4(expf(v[i].x - m), expf(v[i].y - m), expf(v[i].z - m),
+                           expf(v[i].w - m));
+        s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+      }
+    }
+    s = warp_sum(s);
     float *yr = out + static_cast<size_t>(row) * cols;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const uint32_t c = (i * 32 + lane) * 4;
       if (c < cols)
         *reinterpret_cast<float4 *>(yr + c) =
-            make_float4(expf(v[i].x - m) / s, expf(v[i].y - m) / s, expf(v[i].z - m) / s,
-                        expf(v[i].w - m) / s);
+            make_float4(v[i].x / s, v[i].y / s, v[i].z / s, v[i].w / s);
     }
   }
 }
