@@ -37,8 +37,10 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kFlagTimeout = TL_FLAG_TIMEOUT;
 
 struct OpMap {
-  int32_t nb;      // batch dims in the map (0..3)
-  int32_t dim[3];  // product batch dim of map dim 2 + i
+  int32_t nb;       // batch dims in the map (0..3)
+  int32_t dim[3];   // product batch dim of its batch map dim i
+  int32_t chunked;  // MN-major: one load of `chunked` 32-wide chunks (map
+                    // dims 32 x K x MN/32 [x batch]), 0: one load per chunk
 };
 
 struct TcArgs {
@@ -196,6 +198,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
           const int32_t k0 = static_cast<int32_t>(kb * BK);
           if (!A_MN) {
             ptx::tma_load_nd(sa, &tmA, &full[stage], k0, m0, t.ma.nb, za);
+          } else if (t.ma.chunked) {
+            const int32_t c[5] = {0, k0, m0 / 32, za[0], za[1]};
+            ptx::tma_load_rank(sa, &tmA, &full[stage], 3 + t.ma.nb, c);
           } else {
 #pragma unroll
             for (int j = 0; j < BM / 32; ++j)
@@ -203,6 +208,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
           }
           if (!B_MN) {
             ptx::tma_load_nd(sb, &tmB, &full[stage], k0, n0, t.mb.nb, zb);
+          } else if (t.mb.chunked) {
+            const int32_t c[5] = {0, k0, n0 / 32, zb[0], zb[1]};
+            ptx::tma_load_rank(sb, &tmB, &full[stage], 3 + t.mb.nb, c);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 32; ++j)
@@ -503,23 +511,46 @@ EncodeTiledFn encode_fn() {
 bool make_operand_map(CUtensorMap *map, const float *base, uint64_t inner, uint64_t outer,
                       uint64_t ld, const GemmArgs &g, const uint64_t *strides,
                       uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz,
-                      OpMap &om) {
+                      OpMap &om, uint32_t chunks = 0) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
+  om = OpMap{};
+  int nb = 0;
+  for (uint32_t d = 0; d < g.batch_rank; ++d)
+    if (strides[d] != 0) {
+      if (nb == 3) return false;
+      om.dim[nb++] = static_cast<int32_t>(d);
+    }
+  om.nb = nb;
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  if (chunks && inner % 32 == 0 && nb <= 2) {
+    // [MN/32 chunks][K][32]: one load brings `chunks` 32 x 32 boxes, laid
+    // out one after another exactly as `chunks` separate loads would
+    cuuint64_t dims[5] = {32, outer, inner / 32, 1, 1};
+    cuuint64_t st[4] = {ld * 4, 128, 0, 0};
+    int rank = 3;
+    for (int i = 0; i < nb; ++i) {
+      dims[rank] = g.batch_shape[om.dim[i]];
+      st[rank - 1] = strides[om.dim[i]] * 4;
+      ++rank;
+    }
+    const cuuint32_t box[5] = {32, box_outer, chunks, 1, 1};
+    if (enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<float *>(base), dims, st, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+      om.chunked = static_cast<int32_t>(chunks);
+      return true;
+    }
+  }
   cuuint64_t dims[5] = {inner, outer, 1, 1, 1};
   cuuint64_t st[4] = {ld * 4, 0, 0, 0};
-  om = OpMap{};
   int rank = 2;
-  for (uint32_t d = 0; d < g.batch_rank; ++d) {
-    if (strides[d] == 0) continue;
-    if (om.nb == 3) return false;
-    dims[rank] = g.batch_shape[d];
-    st[rank - 1] = strides[d] * 4;
-    om.dim[om.nb++] = static_cast<int32_t>(d);
+  for (int i = 0; i < nb; ++i) {
+    dims[rank] = g.batch_shape[om.dim[i]];
+    st[rank - 1] = strides[om.dim[i]] * 4;
     ++rank;
   }
   const cuuint32_t box[5] = {box_inner, box_outer, 1, 1, 1};
-  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<float *>(base), dims, st,
              box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
@@ -599,11 +630,11 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
   if (!t.status) return fail(TL_ERR_CUDA, "tl_gemm: no status word");
   CUtensorMap ma, mb;
   bool ok = A_MN ? make_operand_map(&ma, g.a, g.m, g.k, g.lda, g, g.sa, 32, 32,
-                                    CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, t.ma)
+                                    CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, t.ma, BM / 32)
                  : make_operand_map(&ma, g.a, g.k, g.m, g.lda, g, g.sa, 32, BM,
                                     CU_TENSOR_MAP_SWIZZLE_128B, t.ma);
   ok = ok && (B_MN ? make_operand_map(&mb, g.b, g.n, g.k, g.ldb, g, g.sb, 32, 32,
-                                      CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, t.mb)
+                                      CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, t.mb, BN / 32)
                    : make_operand_map(&mb, g.b, g.k, g.n, g.ldb, g, g.sb, 32, BN,
                                       CU_TENSOR_MAP_SWIZZLE_128B, t.mb));
   if (!ok) return fail(TL_ERR_UNSUPPORTED, "tl_gemm: tensor map rejected");

@@ -117,6 +117,36 @@ __device__ __forceinline__ void tma_load_nd(void *smem_dst, const CUtensorMap *m
   }
 }
 
+// Tiled TMA load of a box of a rank-`rank` map (3..5) at coordinates c.
+__device__ __forceinline__ void tma_load_rank(void *smem_dst, const CUtensorMap *map,
+                                              uint64_t *bar, int rank, const int32_t *c) {
+  const uint64_t m = reinterpret_cast<uint64_t>(map);
+  const uint32_t d = smem_addr(smem_dst), b = smem_addr(bar);
+  switch (rank) {
+    case 3:
+      asm volatile(
+          "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+          " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(d),
+          "l"(m), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(b)
+          : "memory");
+      break;
+    case 4:
+      asm volatile(
+          "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+          " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(d),
+          "l"(m), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]), "r"(b)
+          : "memory");
+      break;
+    default:
+      asm volatile(
+          "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+          " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(d),
+          "l"(m), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]), "r"(c[4]), "r"(b)
+          : "memory");
+      break;
+  }
+}
+
 // Tiled TMA store of a box to a rank-(2 + nb) map (bulk async-group).
 __device__ __forceinline__ void tma_store_nd(const CUtensorMap *map, const void *smem_src,
                                              int32_t c0, int32_t c1, int nb, const int32_t *zc) {

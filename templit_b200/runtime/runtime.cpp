@@ -138,6 +138,27 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
   }();
   std::unordered_set<std::string> dumped;
 
+  // host timing per window (TL_HOST_TRACE=<file>): recorded ops, host ns
+  // recording, optimising, launching; written when the runtime is destroyed
+  std::string trace_path = [] {
+    const char *e = std::getenv("TL_HOST_TRACE");
+    return std::string(e ? e : "");
+  }();
+  struct WindowTime {
+    uint64_t ops, record_ns, optimise_ns, launch_ns;
+  };
+  std::vector<WindowTime> trace;
+
+  void write_trace() {
+    if (trace_path.empty() || trace.empty()) return;
+    std::ofstream out(trace_path);
+    out << "ops,record_us,optimise_us,launch_us\n";
+    for (const auto &w : trace)
+      out << w.ops << "," << w.record_ns / 1000.0 << "," << w.optimise_ns / 1000.0 << ","
+          << w.launch_ns / 1000.0 << "\n";
+    trace.clear();
+  }
+
   // Optimised programs by recorded-program signature.  A training loop
   // records the same few programs every step; their optimised form is
   // reused while every buffer the optimiser relied on as window-local still
@@ -220,7 +241,10 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
     plans.emplace(std::move(key), std::move(plan));
   }
 
-  ~Impl() override { release_resources(); }
+  ~Impl() override {
+    write_trace();
+    release_resources();
+  }
 
   static std::string describe(const Op &op) {
     std::string s = internal::kind_name(op.kind);
@@ -791,9 +815,11 @@ void Runtime::submit() {
     dump = impl_->dumped.insert(std::move(key)).second;
     if (dump) impl_->dump("recorded", true);
   }
+  const uint64_t recorded_ops = impl_->prog.size();
   if (impl_->fusion) impl_->optimise_program();
   else if (impl_->comm) internal::add_gradient_allreduce(impl_->prog);
   if (dump) impl_->dump("optimised", true);
+  const auto t_optimised = std::chrono::steady_clock::now();
   impl_->state = Impl::State::Submitted;
   ++impl_->stats.windows;
   try {
@@ -803,6 +829,14 @@ void Runtime::submit() {
     throw;
   }
   impl_->prog.clear();
+  if (!impl_->trace_path.empty()) {
+    const auto now = std::chrono::steady_clock::now();
+    auto ns = [](auto d) {
+      return static_cast<uint64_t>(std::chrono::duration_cast<std::chrono::nanoseconds>(d).count());
+    };
+    impl_->trace.push_back({recorded_ops, ns(t_submit - impl_->record_t0),
+                            ns(t_optimised - t_submit), ns(now - t_optimised)});
+  }
   impl_->stats.host_submit_ns += static_cast<uint64_t>(
       std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() -
                                                            t_submit)

@@ -118,12 +118,20 @@ def test_forward_and_three_steps_match_host_oracle_fp32():
     cpu.close()
 
 
-def test_loss_curve_100_steps_tf32_tracks_oracle():
+@pytest.mark.parametrize("precision,rtol", [
+    # exact fp32 products: the runtime's rewrites (common subexpressions,
+    # window liveness, fused kernels) must keep the whole 100-step
+    # trajectory on the oracle's
+    (capi.TL_GEMM_FP32, 2e-3),
+    # TF32 products (10-bit mantissas) drift further as the model fits the
+    # repeated batches: the curve must still track within 5%
+    (capi.TL_GEMM_TF32, 5e-2)])
+def test_loss_curve_100_steps_tracks_oracle(precision, rtol):
     cg = oracle()
     rng = np.random.default_rng(9)
     B, T = 2, 32
     batches = [zipf(rng, B, T) for _ in range(10)]
-    gpu = CudaGPT(config(B, T))
+    gpu = CudaGPT(config(B, T, precision=precision))
     cpu = cg.OracleGPT(config(B, T, precision=capi.TL_GEMM_FP32))
     cpu.set_params(gpu.params())
     lg, lc = [], []
@@ -135,7 +143,7 @@ def test_loss_curve_100_steps_tf32_tracks_oracle():
         lc.append(cpu.train_step())
     lg, lc = np.array(lg), np.array(lc)
     assert lc[-1] < lc[0] - 1.0  # the model learns on repeated batches
-    np.testing.assert_allclose(lg, lc, rtol=2e-2)
+    np.testing.assert_allclose(lg, lc, rtol=rtol)
     gpu.close()
     cpu.close()
 
