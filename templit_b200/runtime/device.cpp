@@ -15,6 +15,7 @@
 
 #include <cstdlib>
 #include <cstring>
+#include <iterator>
 #include <map>
 #include <mutex>
 #include <unordered_map>
@@ -132,6 +133,10 @@ Block allocate(size_t bytes) {
   b.bytes = want;
   auto it = s.free_blocks.lower_bound(want);
   if (it != s.free_blocks.end() && it->first <= 2 * want) {
+    // the most recently released block of the best size (last-in,
+    // first-out): a window that allocates and releases the same sequence
+    // every step then gets the same addresses every step
+    it = std::prev(s.free_blocks.upper_bound(it->first));
     b.ptr = it->second;
     b.bytes = it->first;
     s.free_blocks.erase(it);

@@ -169,7 +169,9 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
     std::vector<uint64_t> local_ids;  // window_local() answers that were true
     uint64_t folded = 0;
     uint64_t last_use = 0;
+    std::string graph_sig;  // signature of the optimised program
   };
+  const std::string *planned_sig = nullptr;  // this submit's, when cached
   std::unordered_map<std::string, Plan> plans;
 
   // deferred wait: this window's status word is moved to pinned memory in
@@ -214,6 +216,7 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
         stats.fused_ops += it->second.folded;
         ++stats.optimiser_cache_hits;
         it->second.last_use = ++use_clock;
+        planned_sig = &it->second.graph_sig;
         return;
       }
       plans.erase(it);
@@ -238,7 +241,8 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
     for (Op &op : plan.ops) op.host.clear();
     plan.local_ids = std::move(live.yes);
     plan.last_use = ++use_clock;
-    plans.emplace(std::move(key), std::move(plan));
+    plan.graph_sig = signature(prog);
+    planned_sig = &plans.emplace(std::move(key), std::move(plan)).first->second.graph_sig;
   }
 
   ~Impl() override {
@@ -720,7 +724,7 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
       stats.kernel_launches += tl_kernel_launches() - k0;
       return;
     }
-    std::string sig = signature(prog);
+    std::string sig = planned_sig ? *planned_sig : signature(prog);
     auto it = graph_cache.find(sig);
     if (it != graph_cache.end()) {
       // slot tables are re-read from pinned memory by the graph's copies
@@ -816,6 +820,7 @@ void Runtime::submit() {
     if (dump) impl_->dump("recorded", true);
   }
   const uint64_t recorded_ops = impl_->prog.size();
+  impl_->planned_sig = nullptr;
   if (impl_->fusion) impl_->optimise_program();
   else if (impl_->comm) internal::add_gradient_allreduce(impl_->prog);
   if (dump) impl_->dump("optimised", true);
