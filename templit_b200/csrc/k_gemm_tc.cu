@@ -1,11 +1,12 @@
 // Tensor-core GEMM for sm_100a: tcgen05.mma kind::tf32 with fp32
 // accumulation in TMEM, operands staged by TMA (no multicast).
 //
-// Persistent, warp-specialised CTA of 192 threads (one CTA per SM):
+// Persistent, warp-specialised CTA of 320 threads (one CTA per SM):
 //   warp 0      TMA producer: STAGES-deep ring of (A, B) k-tiles in smem
 //   warp 1      TMEM owner + MMA issuer (one thread issues tcgen05.mma)
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator, bias / accumulate /
-//               GELU, 128-bit stores to C
+//   warps 2..9  epilogue, two warps per TMEM lane quadrant on alternate
+//               32-column chunks: tcgen05.ld of the accumulator, bias /
+//               addend / GELU, swizzled smem boxes, TMA stores to C
 // Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
 // the MMAs of tile i+1.  CTA tile 128 x BN x 32 (32 fp32 = one 128-byte
 // swizzle row).  Operand majorness follows the stored layout:
@@ -30,7 +31,8 @@
 namespace tl {
 namespace {
 
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two warps per TMEM lane quadrant
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int BM = 128, BK = 32;
 constexpr uint32_t kA_BYTES = BM * BK * 4;  // 16 KB
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
@@ -65,13 +67,15 @@ template <int BN>
 struct Cfg {
   static constexpr uint32_t B_BYTES = BN * BK * 4;
   static constexpr uint32_t STAGE_BYTES = kA_BYTES + B_BYTES;
-  static constexpr int STAGES = BN >= 192 ? 4 : (BN == 128 ? 6 : 8);
+  // staging boxes for the TMA stores: per epilogue warp two 32 x 32 fp32
+  // boxes (4 KB each, 128-byte swizzled rows), one for the widest tile
+  static constexpr int BOXES = BN == 256 ? 1 : 2;
+  static constexpr uint32_t OUT_BYTES = kEpiWarps * BOXES * 4096;
+  static constexpr int STAGES_FIT = static_cast<int>((232448u - 1280u - OUT_BYTES) / STAGE_BYTES);
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   // second accumulator at a power-of-two column; allocation a power of two
   static constexpr uint32_t ACC_COLS = BN == 192 ? 256 : BN;
   static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS < 32 ? 32 : 2 * ACC_COLS;
-  // per epilogue warp two 32 x 32 fp32 staging boxes (4 KB each, 128-byte
-  // swizzled rows) for the TMA stores
-  static constexpr uint32_t OUT_BYTES = 4 * 2 * 4096;
   static constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + OUT_BYTES + 256;
 };
 
@@ -80,11 +84,13 @@ struct Cfg {
 // share the B tiles in L2.
 __device__ __forceinline__ void decode_tile(const TcArgs &t, uint64_t tile, uint64_t &z,
                                             uint32_t &s, uint32_t &mb, uint32_t &nb) {
-  mb = static_cast<uint32_t>(tile % t.mt);
-  uint64_t r = tile / t.mt;
-  nb = static_cast<uint32_t>(r % t.nt);
+  // fewer than 2^32 tiles (checked at launch): 32-bit divisions
+  const uint32_t tl = static_cast<uint32_t>(tile);
+  mb = tl % t.mt;
+  uint32_t r = tl / t.mt;
+  nb = r % t.nt;
   r /= t.nt;
-  s = static_cast<uint32_t>(r % t.splits);
+  s = r % t.splits;
   z = r / t.splits;
 }
 
@@ -97,9 +103,10 @@ __device__ __forceinline__ void k_range(const TcArgs &t, uint32_t ktiles, uint32
 // Coordinates of flattened batch index z in the product's batch dims.
 __device__ __forceinline__ void batch_coords(const GemmArgs &g, uint64_t z,
                                              int32_t (&cz)[TL_GEMM_MAX_BATCH_RANK]) {
+  uint32_t r = static_cast<uint32_t>(z);
   for (int d = static_cast<int>(g.batch_rank) - 1; d >= 0; --d) {
-    cz[d] = static_cast<int32_t>(z % g.batch_shape[d]);
-    z /= g.batch_shape[d];
+    cz[d] = static_cast<int32_t>(r % g.batch_shape[d]);
+    r /= g.batch_shape[d];
   }
 }
 
@@ -133,7 +140,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
   uint64_t *tfull = bars + 2 * C::STAGES;
   uint64_t *tempty = tfull + 2;
   uint64_t *abar = tempty + 2;  // one per epilogue warp: addend box loaded
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(abar + 4);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(abar + kEpiWarps);
   volatile uint32_t *abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -146,9 +153,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&tfull[a], 1);
-      ptx::mbar_init(&tempty[a], 128);
+      ptx::mbar_init(&tempty[a], 32 * kEpiWarps);
     }
-    for (int w = 0; w < 4; ++w) ptx::mbar_init(&abar[w], 1);
+    for (int w = 0; w < kEpiWarps; ++w) ptx::mbar_init(&abar[w], 1);
     *abort_flag = 0;
     ptx::fence_barrier_init();
     ptx::fence_proxy_async_smem();
@@ -299,11 +306,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
     }
   } else {
     // ------------------------------------------------------------- epilogue
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    // Warps 2..9: quadrant q = warp % 4 (the TMEM lanes a warp may read),
+    // two warps per quadrant taking alternate 32-column chunks.
+    const int q = warp & 3;
+    const int e = warp - 2;
+    const int c0 = e >> 2;
     uint32_t acc = 0, acc_phase = 0;
-    uint8_t *obuf = out_base + (warp - 2) * 8192;  // this warp's two staging boxes
+    uint8_t *obuf = out_base + e * C::BOXES * 4096;  // this warp's staging boxes
     uint32_t nbuf = 0, a_phase = 0;
-    uint64_t *my_abar = &abar[warp - 2];
+    uint64_t *my_abar = &abar[e];
     for (uint64_t tile = blockIdx.x; tile < t.num_tiles; tile += gridDim.x) {
       // warp-uniform decisions: tcgen05.ld below needs all 32 lanes
       const bool got = ptx::mbar_wait_bounded(&tfull[acc], acc_phase, kWaitLimitNs);
@@ -336,7 +347,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
         // Each chunk of 32 columns: TMEM -> registers (+ bias, + addend box
         // loaded by TMA into the staging box) -> swizzled staging box -> TMA
         // store of the 32 x 32 box (rows and columns past M, N are clipped).
-        // Two boxes per warp alternate so one store is always in flight.
+        // A warp's boxes alternate (two per warp; one for 256-wide tiles) so
+        // a store is in flight while the next box is filled.
         const int32_t y0 = static_cast<int32_t>(mb * BM + q * 32);
         int32_t zc[3];
         int ncz;
@@ -354,13 +366,16 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
         const bool with_gelu = !raw && g.gelu_out != nullptr;
         bool failed = false;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = c0; c < BN / 32; c += 2) {
           const uint32_t n0 = n_base + c * 32;
           if (n0 >= g.n) break;  // warp-uniform
           uint32_t r[32];
           ptx::tmem_load_32x32b_x32(tmem_base + acc * C::ACC_COLS + c * 32 + ((q * 32u) << 16), r);
-          uint8_t *box = obuf + (nbuf++ & 1u) * 4096;
-          if (lane == 0) ptx::bulk_wait_group_read<1>();  // box free again
+          uint8_t *box = obuf + (C::BOXES == 2 ? (nbuf++ & 1u) * 4096 : 0);
+          if (lane == 0) {  // the box's previous store has read it
+            if constexpr (C::BOXES == 2) ptx::bulk_wait_group_read<1>();
+            else ptx::bulk_wait_group_read<0>();
+          }
           __syncwarp();
           if (with_add) {
             if (lane == 0) {
@@ -402,8 +417,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
             ptx::bulk_commit_group();
           }
           if (with_gelu) {
-            uint8_t *gbox = obuf + (nbuf++ & 1u) * 4096;
-            if (lane == 0) ptx::bulk_wait_group_read<1>();
+            uint8_t *gbox = obuf + (C::BOXES == 2 ? (nbuf++ & 1u) * 4096 : 0);
+            if (lane == 0) {
+              if constexpr (C::BOXES == 2) ptx::bulk_wait_group_read<1>();
+              else ptx::bulk_wait_group_read<0>();
+            }
             __syncwarp();
 #pragma unroll
             for (int j = 0; j < 8; ++j)
@@ -427,7 +445,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
         continue;
       }
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = c0; c < BN / 32; c += 2) {
         uint32_t r[32];
         ptx::tmem_load_32x32b_x32(tmem_base + acc * C::ACC_COLS + c * 32 + ((q * 32u) << 16), r);
         ptx::tmem_load_wait();
@@ -626,6 +644,7 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
   t.kb_per_split = partial ? plan.kb_per_split : (g.k + BK - 1) / BK;
   t.partial = partial;
   t.num_tiles = g.batch_count * t.splits * t.mt * t.nt;
+  if (t.num_tiles >= (1ull << 32)) return fail(TL_ERR_UNSUPPORTED, "tl_gemm: too many tiles");
   t.status = device_status_ptr();
   if (!t.status) return fail(TL_ERR_CUDA, "tl_gemm: no status word");
   CUtensorMap ma, mb;
