@@ -35,6 +35,7 @@ template <int OP, int VEC>
 __global__ void __launch_bounds__(256)
 binary_kernel(const float *__restrict__ a, const float *__restrict__ b,
               float *out, NdParams p, uint32_t n_vec) {
+  pdl_enter();
   const int r = p.rank;
   for (uint32_t v = blockIdx.x * blockDim.x + threadIdx.x; v < n_vec;
        v += gridDim.x * blockDim.x) {
@@ -86,6 +87,7 @@ __device__ __forceinline__ float apply_unary(float x) {
 template <typename F>
 __global__ void __launch_bounds__(256)
 map1_kernel(const float *__restrict__ x, float *out, size_t n, F f) {
+  pdl_enter();
   const size_t n4 = n / 4;
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -103,6 +105,7 @@ map1_kernel(const float *__restrict__ x, float *out, size_t n, F f) {
 template <typename F>
 __global__ void __launch_bounds__(256)
 map1_scalar_kernel(const float *__restrict__ x, float *out, size_t n, F f) {
+  pdl_enter();
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
        i < n; i += stride)
@@ -113,6 +116,7 @@ template <typename F>
 __global__ void __launch_bounds__(256)
 map2_kernel(const float *__restrict__ x, const float *__restrict__ y,
             float *out, size_t n, F f) {
+  pdl_enter();
   const size_t n4 = n / 4;
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -132,6 +136,7 @@ template <typename F>
 __global__ void __launch_bounds__(256)
 map2_scalar_kernel(const float *__restrict__ x, const float *__restrict__ y,
                    float *out, size_t n, F f) {
+  pdl_enter();
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
        i < n; i += stride)
@@ -143,9 +148,9 @@ int launch_map1(const float *x, float *out, size_t n, cudaStream_t s, F f,
                 const char *what) {
   if (n == 0) return TL_OK;
   if (aligned16(x) && aligned16(out))
-    map1_kernel<<<grid_for((n + 3) / 4, 256), 256, 0, s>>>(x, out, n, f);
+    launch_pdl(map1_kernel<F>, grid_for((n + 3) / 4, 256), 256, 0, s, x, out, n, f);
   else
-    map1_scalar_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, out, n, f);
+    launch_pdl(map1_scalar_kernel<F>, grid_for(n, 256), 256, 0, s, x, out, n, f);
   return launch_status(what);
 }
 
@@ -154,9 +159,9 @@ int launch_map2(const float *x, const float *y, float *out, size_t n,
                 cudaStream_t s, F f, const char *what) {
   if (n == 0) return TL_OK;
   if (aligned16(x) && aligned16(y) && aligned16(out))
-    map2_kernel<<<grid_for((n + 3) / 4, 256), 256, 0, s>>>(x, y, out, n, f);
+    launch_pdl(map2_kernel<F>, grid_for((n + 3) / 4, 256), 256, 0, s, x, y, out, n, f);
   else
-    map2_scalar_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, y, out, n, f);
+    launch_pdl(map2_scalar_kernel<F>, grid_for(n, 256), 256, 0, s, x, y, out, n, f);
   return launch_status(what);
 }
 
@@ -172,6 +177,7 @@ struct GeluBackwardFn {
 };
 
 __global__ void fill_u32_kernel(uint32_t *dst, uint32_t v, size_t n) {
+  pdl_enter();
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
        i < n; i += stride)
@@ -252,9 +258,9 @@ void launch_binary(const float *a, const float *b, float *out, const NdParams &p
                    (p.sb[r - 1] == 0 || aligned16(b));
   if (vec) {
     const uint32_t nv = static_cast<uint32_t>(n / 4);
-    binary_kernel<OP, 4><<<grid_for(nv, 256), 256, 0, s>>>(a, b, out, p, nv);
+    launch_pdl(binary_kernel<OP, 4>, grid_for(nv, 256), 256, 0, s, a, b, out, p, nv);
   } else {
-    binary_kernel<OP, 1><<<grid_for(n, 256), 256, 0, s>>>(
+    launch_pdl(binary_kernel<OP, 1>, grid_for(n, 256), 256, 0, s, 
         a, b, out, p, static_cast<uint32_t>(n));
   }
 }
@@ -337,7 +343,7 @@ int tl_fill_u32(void *dst, uint32_t pattern, size_t count, void *stream) {
   cudaStream_t s = as_stream(stream);
   if (pattern == 0)
     return check_cuda(cudaMemsetAsync(dst, 0, count * 4, s), "tl_fill_u32 memset");
-  fill_u32_kernel<<<grid_for(count, 256), 256, 0, s>>>(static_cast<uint32_t *>(dst),
+  launch_pdl(fill_u32_kernel, grid_for(count, 256), 256, 0, s, static_cast<uint32_t *>(dst),
                                                        pattern, count);
   return launch_status("tl_fill_u32");
 }

@@ -21,6 +21,7 @@ __global__ void __launch_bounds__(256)
 gather_kernel(const float *__restrict__ w, uint32_t n_rows, uint32_t dim,
               const uint32_t *__restrict__ ids, uint32_t n_ids, float *out,
               uint32_t *status) {
+  pdl_enter();
   const uint32_t per_row = dim / V;
   const uint64_t total = static_cast<uint64_t>(n_ids) * per_row;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
@@ -59,6 +60,7 @@ __global__ void __launch_bounds__(kThreads)
 chunk_sum_kernel(const float *__restrict__ values, const uint32_t *__restrict__ ids,
                  uint32_t n_ids, uint32_t dim, uint32_t n_rows, float *partial,
                  uint32_t *uid, uint32_t *ucount, uint32_t *status) {
+  pdl_enter();
   __shared__ unsigned long long key[kChunk];
   __shared__ uint32_t gstart[kChunk + 1];
   __shared__ uint32_t warp_heads[kChunk / 32], warp_valid[kChunk / 32];
@@ -179,6 +181,7 @@ __global__ void __launch_bounds__(kThreads)
 row_combine_kernel(const float *__restrict__ partial, const uint32_t *__restrict__ uid,
                    const uint32_t *__restrict__ ucount, uint32_t n_chunks, uint32_t dim,
                    const float *base, float *dst) {
+  pdl_enter();
   using Vec = typename std::conditional<V == 4, float4, float>::type;
   __shared__ int slot[kThreads];
   __shared__ Vec wsum[kThreads / 32][32];
@@ -263,9 +266,9 @@ int tl_embedding_gather(const float *weights, uint32_t n_rows, uint32_t dim,
   cudaStream_t s = as_stream(stream);
   const uint64_t total = static_cast<uint64_t>(n_ids) * dim;
   if (dim % 4 == 0 && aligned16(weights) && aligned16(out))
-    gather_kernel<4><<<grid_for(total / 4, 256), 256, 0, s>>>(weights, n_rows, dim, ids, n_ids, out, status);
+    launch_pdl(gather_kernel<4>, grid_for(total / 4, 256), 256, 0, s, weights, n_rows, dim, ids, n_ids, out, status);
   else
-    gather_kernel<1><<<grid_for(total, 256), 256, 0, s>>>(weights, n_rows, dim, ids, n_ids, out, status);
+    launch_pdl(gather_kernel<1>, grid_for(total, 256), 256, 0, s, weights, n_rows, dim, ids, n_ids, out, status);
   return launch_status("tl_embedding_gather");
 }
 
@@ -303,18 +306,18 @@ int tl_embedding_scatter_add(const float *values, const uint32_t *ids,
                    (!base || aligned16(base)) && aligned16(workspace);
   if (chunks) {
     if (vec)
-      chunk_sum_kernel<4><<<chunks, kThreads, 0, s>>>(values, ids, n_ids, dim, n_rows, partial, uid, ucount, status);
+      launch_pdl(chunk_sum_kernel<4>, chunks, kThreads, 0, s, values, ids, n_ids, dim, n_rows, partial, uid, ucount, status);
     else
-      chunk_sum_kernel<1><<<chunks, kThreads, 0, s>>>(values, ids, n_ids, dim, n_rows, partial, uid, ucount, status);
+      launch_pdl(chunk_sum_kernel<1>, chunks, kThreads, 0, s, values, ids, n_ids, dim, n_rows, partial, uid, ucount, status);
     const int rc = launch_status("tl_embedding_scatter_add chunks");
     if (rc) return rc;
   }
   const uint32_t per = 32 * (vec ? 4 : 1);
   const dim3 grid(n_rows, (dim + per - 1) / per);
   if (vec)
-    row_combine_kernel<4><<<grid, kThreads, 0, s>>>(partial, uid, ucount, chunks, dim, base, dst);
+    launch_pdl(row_combine_kernel<4>, grid, kThreads, 0, s, partial, uid, ucount, chunks, dim, base, dst);
   else
-    row_combine_kernel<1><<<grid, kThreads, 0, s>>>(partial, uid, ucount, chunks, dim, base, dst);
+    launch_pdl(row_combine_kernel<1>, grid, kThreads, 0, s, partial, uid, ucount, chunks, dim, base, dst);
   return launch_status("tl_embedding_scatter_add rows");
 }
 

@@ -17,6 +17,7 @@ constexpr int BM = 128, BN = 128, BK = 8, TM = 8, TN = 8;
 
 __global__ void __launch_bounds__(256)
 sgemm_kernel(GemmArgs g) {
+  pdl_enter();
   __shared__ __align__(16) float As[2][BK][BM];
   __shared__ __align__(16) float Bs[2][BK][BN];
   const uint32_t batch = blockIdx.z;
@@ -122,7 +123,7 @@ int launch_sgemm(const GemmArgs &g, cudaStream_t s) {
     GemmArgs gb = g;
     gb.batch_base = b0;
     grid.z = static_cast<unsigned>(g.batch_count - b0 < 65535 ? g.batch_count - b0 : 65535);
-    sgemm_kernel<<<grid, 256, 0, s>>>(gb);
+    launch_pdl(sgemm_kernel, grid, 256, 0, s, gb);
     int rc = launch_status("tl_gemm fp32");
     if (rc) return rc;
   }

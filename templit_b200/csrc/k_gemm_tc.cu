@@ -172,6 +172,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t ktiles = (g.k + BK - 1) / BK;
+  // the setup above overlaps the previous kernel's tail
+  pdl_enter();
 
   auto timeout = [&]() {
     *abort_flag = 1;
@@ -577,6 +579,7 @@ bool make_operand_map(CUtensorMap *map, const float *base, uint64_t inner, uint6
 // Slice sums of a split-K product in slice order, then the epilogue.
 __global__ void __launch_bounds__(256)
 splitk_epilogue_kernel(const float *__restrict__ part, uint32_t splits, GemmArgs g) {
+  pdl_enter();
   const uint64_t mn = static_cast<uint64_t>(g.m) * g.n;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
   for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < mn;
@@ -693,12 +696,12 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
     attr_set = true;
   }
   const uint64_t grid = t.num_tiles < static_cast<uint64_t>(kNumSMs) ? t.num_tiles : kNumSMs;
-  tc_gemm_kernel<BN, A_MN, B_MN><<<static_cast<unsigned>(grid), kThreads, C::SMEM, s>>>(
+  launch_pdl(tc_gemm_kernel<BN, A_MN, B_MN>, static_cast<unsigned>(grid), kThreads, C::SMEM, s, 
       ma, mb, mc, mg, md, t);
   int rc = launch_status("tl_gemm tf32");
   if (rc || !partial) return rc;
   const uint64_t mn = static_cast<uint64_t>(g.m) * g.n;
-  splitk_epilogue_kernel<<<grid_for(mn, 256), 256, 0, s>>>(partial, t.splits, g);
+  launch_pdl(splitk_epilogue_kernel, grid_for(mn, 256), 256, 0, s, partial, t.splits, g);
   return launch_status("tl_gemm split-K sum");
 }
 

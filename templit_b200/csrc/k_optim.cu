@@ -34,6 +34,7 @@ __device__ __forceinline__ float block_sum(float v) {
 __global__ void __launch_bounds__(kNormThreads)
 sqnorm_partial_kernel(const float *__restrict__ g, size_t n, float *partial,
                       float *sqnorm) {
+  pdl_enter();
   float acc = 0.0f;
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -57,6 +58,7 @@ sqnorm_partial_kernel(const float *__restrict__ g, size_t n, float *partial,
 __global__ void __launch_bounds__(kNormThreads)
 sqnorm_combine_kernel(const float *__restrict__ partial, uint32_t count,
                       float *sqnorm) {
+  pdl_enter();
   float acc = 0.0f;
   // fixed assignment of partials to threads, then a fixed-shape tree
   for (uint32_t i = threadIdx.x; i < count; i += blockDim.x) acc += partial[i];
@@ -71,6 +73,7 @@ __device__ __forceinline__ float clip_scale(float n2, float max_norm) {
 __global__ void __launch_bounds__(256)
 clip_kernel(const float *__restrict__ g, const float *__restrict__ sqnorm,
             float max_norm, float *out, size_t n) {
+  pdl_enter();
   const float sc = clip_scale(*sqnorm, max_norm);
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
@@ -107,6 +110,7 @@ adamw_kernel(const float *param, const float *__restrict__ grad, float *out,
              float *m1, float *m2, const float *beta1, const float *beta2,
              const float *decay, const float *lr, float eps, uint32_t step,
              size_t n) {
+  pdl_enter();
   const AdamScalars a = load_adam(beta1, beta2, decay, lr, step);
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
@@ -134,6 +138,7 @@ __device__ __forceinline__ uint32_t find_slot(const tl_param_slot *slots,
 __global__ void __launch_bounds__(kNormThreads)
 multi_sqnorm_kernel(const tl_param_slot *__restrict__ slots, uint32_t n_slots,
                     uint32_t n_chunks, float *partial) {
+  pdl_enter();
   float acc = 0.0f;
   for (uint32_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
     const tl_param_slot &sl = slots[find_slot(slots, n_slots, c)];
@@ -160,6 +165,7 @@ multi_clip_adamw_kernel(const tl_param_slot *__restrict__ slots, uint32_t n_slot
                         uint32_t n_chunks, const float *__restrict__ sqnorm,
                         float max_norm, const float *beta1, const float *beta2,
                         const float *decay, const float *lr, float eps) {
+  pdl_enter();
   const bool clip = max_norm > 0.0f;
   const float sc = clip ? clip_scale(*sqnorm, max_norm) : 1.0f;
   const float b1 = *beta1, b2 = *beta2, dc = *decay, lrv = *lr;
@@ -243,16 +249,16 @@ int tl_grad_sqnorm_accumulate(const float *grad, size_t count, float *sqnorm,
   const uint32_t blocks = norm_blocks(count);
   cudaStream_t s = as_stream(stream);
   if (blocks == 1) {
-    sqnorm_partial_kernel<<<1, kNormThreads, 0, s>>>(grad, count, nullptr, sqnorm);
+    launch_pdl(sqnorm_partial_kernel, 1, kNormThreads, 0, s, grad, count, nullptr, sqnorm);
     return launch_status("tl_grad_sqnorm_accumulate");
   }
   if (!workspace || workspace_bytes < blocks * sizeof(float))
     return fail(TL_ERR_INVALID, "tl_grad_sqnorm_accumulate: workspace too small");
   float *partial = static_cast<float *>(workspace);
-  sqnorm_partial_kernel<<<blocks, kNormThreads, 0, s>>>(grad, count, partial, sqnorm);
+  launch_pdl(sqnorm_partial_kernel, blocks, kNormThreads, 0, s, grad, count, partial, sqnorm);
   int rc = launch_status("tl_grad_sqnorm_accumulate partial");
   if (rc) return rc;
-  sqnorm_combine_kernel<<<1, kNormThreads, 0, s>>>(partial, blocks, sqnorm);
+  launch_pdl(sqnorm_combine_kernel, 1, kNormThreads, 0, s, partial, blocks, sqnorm);
   return launch_status("tl_grad_sqnorm_accumulate combine");
 }
 
@@ -262,7 +268,7 @@ int tl_clip_gradient(const float *grad, const float *sqnorm, float max_norm,
     return fail(TL_ERR_INVALID, "maximum gradient norm must be finite and positive");
   if (count == 0) return TL_OK;
   if (!grad || !sqnorm || !out) return fail(TL_ERR_INVALID, "tl_clip_gradient: null pointer");
-  clip_kernel<<<grid_for(count, 256), 256, 0, as_stream(stream)>>>(grad, sqnorm, max_norm,
+  launch_pdl(clip_kernel, grid_for(count, 256), 256, 0, as_stream(stream), grad, sqnorm, max_norm,
                                                                    out, count);
   return launch_status("tl_clip_gradient");
 }
@@ -275,7 +281,7 @@ int tl_adamw(const float *param, const float *grad, float *out, float *m1, float
   if (count == 0) return TL_OK;
   if (!param || !grad || !out || !m1 || !m2 || !beta1 || !beta2 || !decay || !lr)
     return fail(TL_ERR_INVALID, "tl_adamw: null pointer");
-  adamw_kernel<<<grid_for(count, 256), 256, 0, as_stream(stream)>>>(
+  launch_pdl(adamw_kernel, grid_for(count, 256), 256, 0, as_stream(stream), 
       param, grad, out, m1, m2, beta1, beta2, decay, lr, epsilon, step, count);
   return launch_status("tl_adamw");
 }
@@ -301,14 +307,14 @@ int tl_multi_clip_adamw(const tl_param_slot *slots, uint32_t n_slots, uint32_t n
     if (!workspace || workspace_bytes < blocks * sizeof(float))
       return fail(TL_ERR_INVALID, "tl_multi_clip_adamw: workspace too small");
     float *partial = static_cast<float *>(workspace);
-    multi_sqnorm_kernel<<<blocks, kNormThreads, 0, s>>>(slots, n_slots, n_chunks, partial);
+    launch_pdl(multi_sqnorm_kernel, blocks, kNormThreads, 0, s, slots, n_slots, n_chunks, partial);
     int rc = launch_status("tl_multi_clip_adamw norm");
     if (rc) return rc;
-    sqnorm_combine_kernel<<<1, kNormThreads, 0, s>>>(partial, blocks, sqnorm);
+    launch_pdl(sqnorm_combine_kernel, 1, kNormThreads, 0, s, partial, blocks, sqnorm);
     rc = launch_status("tl_multi_clip_adamw combine");
     if (rc) return rc;
   }
-  multi_clip_adamw_kernel<<<blocks, 256, 0, s>>>(slots, n_slots, n_chunks, sqnorm, max_norm,
+  launch_pdl(multi_clip_adamw_kernel, blocks, 256, 0, s, slots, n_slots, n_chunks, sqnorm, max_norm,
                                                  beta1, beta2, decay, lr, epsilon);
   return launch_status("tl_multi_clip_adamw update");
 }

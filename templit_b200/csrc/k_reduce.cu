@@ -37,6 +37,7 @@ template <int OP>
 __global__ void __launch_bounds__(256)
 rows_kernel(const float *__restrict__ x, float *out, uint32_t rows,
             uint32_t cols, uint32_t splits, uint32_t chunk, bool vec) {
+  pdl_enter();
   const uint32_t warps = (blockDim.x / 32) * gridDim.x;
   const uint32_t lane = threadIdx.x & 31;
   const uint64_t total = static_cast<uint64_t>(rows) * splits;
@@ -67,6 +68,7 @@ template <int OP, int V>
 __global__ void __launch_bounds__(256)
 cols_kernel(const float *__restrict__ x, float *out, uint32_t K1, uint32_t R,
             uint32_t K2, uint32_t splits, uint32_t rchunk) {
+  pdl_enter();
   const uint32_t k2v = K2 / V;
   const uint64_t per_split = static_cast<uint64_t>(K1) * k2v;
   const uint64_t total = per_split * splits;
@@ -109,6 +111,7 @@ template <int OP>
 __global__ void __launch_bounds__(256)
 cols_block_kernel(const float *__restrict__ x, float *out, uint32_t K1, uint32_t R,
                   uint32_t K2, uint32_t rchunk) {
+  pdl_enter();
   __shared__ float4 part[8][32];
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t c = blockIdx.x, k1 = blockIdx.y;
@@ -150,6 +153,7 @@ template <int OP>
 __global__ void __launch_bounds__(256)
 combine_kernel(const float *__restrict__ part, float *out, uint64_t n,
                uint32_t splits) {
+  pdl_enter();
   __shared__ float acc_w[8][33];
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint64_t i = static_cast<uint64_t>(blockIdx.x) * 32 + lane;
@@ -181,6 +185,7 @@ struct GenericParams {
 template <int OP>
 __global__ void generic_kernel(const float *__restrict__ x, float *out,
                                GenericParams p) {
+  pdl_enter();
   for (uint32_t o = blockIdx.x * blockDim.x + threadIdx.x; o < p.out_count;
        o += gridDim.x * blockDim.x) {
     // decode o over kept dims (row-major over kept dims)
@@ -342,12 +347,12 @@ int run_plan(const ReducePlan &pl, const float *x, float *out, void *ws,
       const bool vec = pl.cols % 4 == 0 && aligned16(x);
       float *dst = pl.splits > 1 ? static_cast<float *>(ws) : out;
       const uint64_t warps = static_cast<uint64_t>(pl.rows) * pl.splits;
-      rows_kernel<OP><<<grid_for(warps * 32, 256, 16), 256, 0, s>>>(
+      launch_pdl(rows_kernel<OP>, grid_for(warps * 32, 256, 16), 256, 0, s, 
           x, dst, pl.rows, pl.cols, pl.splits, pl.chunk, vec);
       int rc = launch_status("reduce rows");
       if (rc || pl.splits == 1) return rc;
       // dst is [rows, splits]: a second row pass over the partials
-      rows_kernel<OP><<<grid_for(static_cast<uint64_t>(pl.rows) * 32, 256, 16), 256, 0, s>>>(
+      launch_pdl(rows_kernel<OP>, grid_for(static_cast<uint64_t>(pl.rows) * 32, 256, 16), 256, 0, s, 
           dst, out, pl.rows, pl.splits, 1, pl.splits, false);
       return launch_status("reduce rows combine");
     }
@@ -357,19 +362,19 @@ int run_plan(const ReducePlan &pl, const float *x, float *out, void *ws,
       const uint64_t outs = static_cast<uint64_t>(pl.K1) * pl.K2;
       const uint64_t work = (vec ? outs / 4 : outs) * pl.splits;
       if (pl.block && vec)
-        cols_block_kernel<OP><<<dim3(pl.splits, pl.K1, (pl.K2 + 127) / 128), 256, 0, s>>>(
+        launch_pdl(cols_block_kernel<OP>, dim3(pl.splits, pl.K1, (pl.K2 + 127) / 128), 256, 0, s, 
             x, dst, pl.K1, pl.R, pl.K2, pl.chunk);
       else if (vec)
-        cols_kernel<OP, 4><<<grid_for(work, 256, 16), 256, 0, s>>>(x, dst, pl.K1, pl.R, pl.K2, pl.splits, pl.chunk);
+        launch_pdl(cols_kernel<OP, 4>, grid_for(work, 256, 16), 256, 0, s, x, dst, pl.K1, pl.R, pl.K2, pl.splits, pl.chunk);
       else
-        cols_kernel<OP, 1><<<grid_for(work, 256, 16), 256, 0, s>>>(x, dst, pl.K1, pl.R, pl.K2, pl.splits, pl.chunk);
+        launch_pdl(cols_kernel<OP, 1>, grid_for(work, 256, 16), 256, 0, s, x, dst, pl.K1, pl.R, pl.K2, pl.splits, pl.chunk);
       int rc = launch_status("reduce cols");
       if (rc || pl.splits == 1) return rc;
-      combine_kernel<OP><<<static_cast<unsigned>((outs + 31) / 32), 256, 0, s>>>(dst, out, outs, pl.splits);
+      launch_pdl(combine_kernel<OP>, static_cast<unsigned>((outs + 31) / 32), 256, 0, s, dst, out, outs, pl.splits);
       return launch_status("reduce cols combine");
     }
     default:
-      generic_kernel<OP><<<grid_for(pl.out_count, 128), 128, 0, s>>>(x, out, pl.gp);
+      launch_pdl(generic_kernel<OP>, grid_for(pl.out_count, 128), 128, 0, s, x, out, pl.gp);
       return launch_status("reduce generic");
   }
 }
@@ -400,6 +405,7 @@ __device__ __forceinline__ void arg_warp(float &v, uint32_t &i) {
 __global__ void __launch_bounds__(256)
 argmax_partial_kernel(const float *__restrict__ x, uint64_t n, ArgBest *part,
                       uint32_t *out_index, bool final_pass) {
+  pdl_enter();
   float v = -INFINITY;
   uint32_t idx = 0xffffffffu;
   for (uint64_t j = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; j < n;
@@ -429,6 +435,7 @@ argmax_partial_kernel(const float *__restrict__ x, uint64_t n, ArgBest *part,
 
 __global__ void __launch_bounds__(256)
 argmax_final_kernel(const ArgBest *part, uint32_t count, uint32_t *out_index) {
+  pdl_enter();
   float v = -INFINITY;
   uint32_t idx = 0xffffffffu;
   for (uint32_t j = threadIdx.x; j < count; j += blockDim.x)
@@ -499,16 +506,16 @@ int tl_argmax(const float *x, size_t count, uint32_t *out_index, void *workspace
   const uint32_t blocks = argmax_blocks(count);
   cudaStream_t s = as_stream(stream);
   if (blocks == 1) {
-    argmax_partial_kernel<<<1, 256, 0, s>>>(x, count, nullptr, out_index, true);
+    launch_pdl(argmax_partial_kernel, 1, 256, 0, s, x, count, nullptr, out_index, true);
     return launch_status("tl_argmax");
   }
   if (!workspace || workspace_bytes < blocks * sizeof(ArgBest))
     return fail(TL_ERR_INVALID, "tl_argmax: workspace too small");
   ArgBest *part = static_cast<ArgBest *>(workspace);
-  argmax_partial_kernel<<<blocks, 256, 0, s>>>(x, count, part, nullptr, false);
+  launch_pdl(argmax_partial_kernel, blocks, 256, 0, s, x, count, part, nullptr, false);
   int rc = launch_status("tl_argmax partial");
   if (rc) return rc;
-  argmax_final_kernel<<<1, 256, 0, s>>>(part, blocks, out_index);
+  launch_pdl(argmax_final_kernel, 1, 256, 0, s, part, blocks, out_index);
   return launch_status("tl_argmax final");
 }
 

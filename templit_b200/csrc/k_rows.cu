@@ -83,6 +83,7 @@ __device__ __forceinline__ float row_dot(const float *a, const float *b,
 __global__ void __launch_bounds__(256)
 softmax_kernel(const float *__restrict__ x, float *out, uint32_t rows,
                uint32_t cols, bool vec) {
+  pdl_enter();
   ROW_LOOP {
     const float *xr = x + static_cast<size_t>(row) * cols;
     float *yr = out + static_cast<size_t>(row) * cols;
@@ -118,6 +119,7 @@ __global__ void __launch_bounds__(256)
 softmax_scaled_masked_kernel(const float *__restrict__ x, const float *__restrict__ divisor,
                              const float *__restrict__ mask, uint32_t mask_rows, float *out,
                              uint32_t rows, uint32_t cols, bool vec) {
+  pdl_enter();
   ROW_LOOP {
     const float *xr = x + static_cast<size_t>(row) * cols;
     const float *mr = mask ? mask + static_cast<size_t>(row % mask_rows) * cols : nullptr;
@@ -158,6 +160,7 @@ __global__ void __launch_bounds__(256)
 softmax_backward_kernel(const float *__restrict__ g, const float *__restrict__ y,
                         const float *__restrict__ divisor, float *dx, uint32_t rows,
                         uint32_t cols, bool vec) {
+  pdl_enter();
   ROW_LOOP {
     const size_t off = static_cast<size_t>(row) * cols;
     const float dot = row_dot(g + off, y + off, cols, vec, lane);
@@ -188,6 +191,7 @@ __device__ __forceinline__ float row_rms(const float *xr, uint32_t cols, bool ve
 __global__ void __launch_bounds__(256)
 rms_kernel(const float *__restrict__ x, float *rms, uint32_t rows, uint32_t cols,
            bool vec) {
+  pdl_enter();
   ROW_LOOP {
     const float r = row_rms(x + static_cast<size_t>(row) * cols, cols, vec, lane);
     if (lane == 0) rms[row] = r;
@@ -197,6 +201,7 @@ rms_kernel(const float *__restrict__ x, float *rms, uint32_t rows, uint32_t cols
 __global__ void __launch_bounds__(256)
 rmsnorm_kernel(const float *__restrict__ x, float *out, float *rms_out,
                uint32_t rows, uint32_t cols, bool vec) {
+  pdl_enter();
   ROW_LOOP {
     const float *xr = x + static_cast<size_t>(row) * cols;
     float *yr = out + static_cast<size_t>(row) * cols;
@@ -224,6 +229,7 @@ __global__ void __launch_bounds__(256)
 rmsnorm_backward_kernel(const float *__restrict__ g, const float *__restrict__ x,
                         const float *__restrict__ y, const float *addend, float *dx,
                         uint32_t rows, uint32_t cols, bool vec) {
+  pdl_enter();
   ROW_LOOP {
     const size_t off = static_cast<size_t>(row) * cols;
     const float r = row_rms(x + off, cols, vec, lane);
@@ -255,6 +261,7 @@ rmsnorm_backward_kernel(const float *__restrict__ g, const float *__restrict__ x
 __global__ void __launch_bounds__(256)
 xent_kernel(const float *__restrict__ z, const uint32_t *__restrict__ t,
             float *loss, uint32_t rows, uint32_t vocab, bool vec) {
+  pdl_enter();
   ROW_LOOP {
     const uint32_t target = t[row];
     if (target >= vocab) {
@@ -272,6 +279,7 @@ __global__ void __launch_bounds__(256)
 xent_backward_kernel(const float *__restrict__ z, const uint32_t *__restrict__ t,
                      const float *__restrict__ scale, float *dz, uint32_t rows,
                      uint32_t vocab, bool vec) {
+  pdl_enter();
   ROW_LOOP {
     const uint32_t target = t[row];
     const float *zr = z + static_cast<size_t>(row) * vocab;
@@ -320,6 +328,7 @@ __global__ void __launch_bounds__(256)
 softmax_regs_kernel(const float *__restrict__ x, const float *__restrict__ divisor,
                     const float *__restrict__ mask, uint32_t mask_rows, float *out,
                     uint32_t rows, uint32_t cols) {
+  pdl_enter();
   ROW_LOOP {
     const float *xr = x + static_cast<size_t>(row) * cols;
     const float *mr = mask ? mask + static_cast<size_t>(row % mask_rows) * cols : nullptr;
@@ -365,6 +374,7 @@ __global__ void __launch_bounds__(256)
 softmax_backward_regs_kernel(const float *__restrict__ g, const float *__restrict__ y,
                              const float *__restrict__ divisor, float *dx, uint32_t rows,
                              uint32_t cols) {
+  pdl_enter();
   ROW_LOOP {
     const size_t off = static_cast<size_t>(row) * cols;
     float4 gv[NV], yv[NV];
@@ -396,6 +406,7 @@ template <int NV>
 __global__ void __launch_bounds__(256)
 rmsnorm_regs_kernel(const float *__restrict__ x, float *out, float *rms_out, uint32_t rows,
                     uint32_t cols) {
+  pdl_enter();
   ROW_LOOP {
     const float *xr = x + static_cast<size_t>(row) * cols;
     float4 v[NV];
@@ -426,6 +437,7 @@ __global__ void __launch_bounds__(256)
 rmsnorm_backward_regs_kernel(const float *__restrict__ g, const float *__restrict__ x,
                              const float *__restrict__ y, const float *addend, float *dx,
                              uint32_t rows, uint32_t cols) {
+  pdl_enter();
   ROW_LOOP {
     const size_t off = static_cast<size_t>(row) * cols;
     float4 gv[NV], yv[NV];
@@ -458,6 +470,114 @@ rmsnorm_backward_regs_kernel(const float *__restrict__ g, const float *__restric
     }
   }
 }
+
+// ---- rows of 64 * NP columns (attention scores: T = 192) ---------------
+// Lane l holds columns 2l + 64i (a float2 each), so every lane does the same
+// work and loads stay coalesced (256 bytes per warp instruction).  A
+// divisor that is a power of two (sqrt of a power-of-four head size) is
+// applied as a multiplication, which is exact; the final normalisation
+// multiplies by one reciprocal of the row sum.
+__device__ __forceinline__ bool pow2f(float d) {
+  const uint32_t b = __float_as_uint(d);
+  const uint32_t e = (b >> 23) & 0xffu;
+  return (b & 0x7fffffu) == 0 && e != 0 && e != 0xffu;
+}
+
+template <int NP>
+__global__ void __launch_bounds__(256)
+softmax_pairs_kernel(const float *__restrict__ x, const float *__restrict__ divisor,
+                     const float *__restrict__ mask, uint32_t mask_rows, float *out,
+                     uint32_t rows, uint32_t cols) {
+  pdl_enter();
+  const float dv = divisor ? *divisor : 1.0f;
+  const bool exact_scale = divisor && pow2f(dv);
+  const float rdv = 1.0f / dv;
+  ROW_LOOP {
+    const float *xr = x + static_cast<size_t>(row) * cols;
+    const float *mr = mask ? mask + static_cast<size_t>(row % mask_rows) * cols : nullptr;
+    float2 v[NP];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      const uint32_t c = 2 * lane + 64 * i;
+      v[i] = *reinterpret_cast<const float2 *>(xr + c);
+      if (divisor) {
+        if (exact_scale) v[i] = make_float2(v[i].x * rdv, v[i].y * rdv);
+        else v[i] = make_float2(v[i].x / dv, v[i].y / dv);
+      }
+      if (mr) {
+        const float2 k = *reinterpret_cast<const float2 *>(mr + c);
+        v[i] = make_float2(v[i].x + k.x, v[i].y + k.y);
+      }
+      m = fmaxf(m, fmaxf(v[i].x, v[i].y));
+    }
+    m = warp_max(m);
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      v[i] = make_float2(expf(v[i].x - m), expf(v[i].y - m));
+      s += v[i].x + v[i].y;
+    }
+    const float inv = 1.0f / warp_sum(s);
+    float *yr = out + static_cast<size_t>(row) * cols;
+#pragma unroll
+    for (int i = 0; i < NP; ++i)
+      *reinterpret_cast<float2 *>(yr + 2 * lane + 64 * i) = make_float2(v[i].x * inv, v[i].y * inv);
+  }
+}
+
+template <int NP>
+__global__ void __launch_bounds__(256)
+softmax_backward_pairs_kernel(const float *__restrict__ g, const float *__restrict__ y,
+                              const float *__restrict__ divisor, float *dx, uint32_t rows,
+                              uint32_t cols) {
+  pdl_enter();
+  const float dv = divisor ? *divisor : 1.0f;
+  const bool exact_scale = divisor && pow2f(dv);
+  const float rdv = 1.0f / dv;
+  ROW_LOOP {
+    const size_t off = static_cast<size_t>(row) * cols;
+    float2 gv[NP], yv[NP];
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      const uint32_t c = 2 * lane + 64 * i;
+      gv[i] = *reinterpret_cast<const float2 *>(g + off + c);
+      yv[i] = *reinterpret_cast<const float2 *>(y + off + c);
+      acc += gv[i].x * yv[i].x + gv[i].y * yv[i].y;
+    }
+    const float dot = warp_sum(acc);
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      float2 r = make_float2(yv[i].x * (gv[i].x - dot), yv[i].y * (gv[i].y - dot));
+      if (divisor) {
+        if (exact_scale) r = make_float2(r.x * rdv, r.y * rdv);
+        else r = make_float2(r.x / dv, r.y / dv);
+      }
+      *reinterpret_cast<float2 *>(dx + off + 2 * lane + 64 * i) = r;
+    }
+  }
+}
+
+// float2 pairs per lane for rows of exactly 64 * NP columns (0: other rows)
+int pairs_for(uint32_t cols, std::initializer_list<const void *> ptrs) {
+  if (cols % 64 || cols > 512) return 0;
+  for (const void *p : ptrs)
+    if (p && (reinterpret_cast<uintptr_t>(p) & 7u)) return 0;
+  return static_cast<int>(cols / 64);
+}
+
+#define TL_PAIRS_DISPATCH(NPVAR, LAUNCH) \
+  switch (NPVAR) {                       \
+    case 1: LAUNCH(1); break;            \
+    case 2: LAUNCH(2); break;            \
+    case 3: LAUNCH(3); break;            \
+    case 4: LAUNCH(4); break;            \
+    case 5: LAUNCH(5); break;            \
+    case 6: LAUNCH(6); break;            \
+    case 7: LAUNCH(7); break;            \
+    default: LAUNCH(8); break;           \
+  }
 
 // Float4s per lane that hold a row of `cols` (0: too long, use the loops).
 int regs_for(uint32_t cols) {
@@ -504,14 +624,20 @@ int tl_softmax_rows(const float *x, float *out, uint32_t rows, uint32_t cols,
   if (cols == 0) return fail(TL_ERR_INVALID, "softmax requires a non-empty final dimension");
   if (rows == 0) return TL_OK;
   if (!x || !out) return fail(TL_ERR_INVALID, "tl_softmax_rows: null pointer");
+  const int np = pairs_for(cols, {x, out});
   const int nv = row_vec(cols, {x, out}) ? regs_for(cols) : 0;
-  if (nv) {
-#define L(NV) softmax_regs_kernel<NV><<<row_grid(rows), 256, 0, as_stream(stream)>>>( \
+  if (np) {
+#define L(NP) launch_pdl(softmax_pairs_kernel<NP>, row_grid(rows), 256, 0, as_stream(stream),  \
+    x, nullptr, nullptr, 0, out, rows, cols)
+    TL_PAIRS_DISPATCH(np, L)
+#undef L
+  } else if (nv) {
+#define L(NV) launch_pdl(softmax_regs_kernel<NV>, row_grid(rows), 256, 0, as_stream(stream),  \
     x, nullptr, nullptr, 0, out, rows, cols)
     TL_ROWS_DISPATCH(nv, L)
 #undef L
   } else {
-    softmax_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(x, out, rows, cols,
+    launch_pdl(softmax_kernel, row_grid(rows), 256, 0, as_stream(stream), x, out, rows, cols,
                                                                   row_vec(cols, {x, out}));
   }
   return launch_status("tl_softmax_rows");
@@ -525,14 +651,20 @@ int tl_softmax_scaled_masked_rows(const float *x, const float *divisor, const fl
   if (!x || !out) return fail(TL_ERR_INVALID, "tl_softmax_scaled_masked_rows: null pointer");
   if (mask && mask_rows == 0)
     return fail(TL_ERR_INVALID, "tl_softmax_scaled_masked_rows: mask without rows");
+  const int np = pairs_for(cols, {x, out, mask});
   const int nv = row_vec(cols, {x, out, mask}) ? regs_for(cols) : 0;
-  if (nv) {
-#define L(NV) softmax_regs_kernel<NV><<<row_grid(rows), 256, 0, as_stream(stream)>>>( \
+  if (np) {
+#define L(NP) launch_pdl(softmax_pairs_kernel<NP>, row_grid(rows), 256, 0, as_stream(stream),  \
+    x, divisor, mask, mask_rows, out, rows, cols)
+    TL_PAIRS_DISPATCH(np, L)
+#undef L
+  } else if (nv) {
+#define L(NV) launch_pdl(softmax_regs_kernel<NV>, row_grid(rows), 256, 0, as_stream(stream),  \
     x, divisor, mask, mask_rows, out, rows, cols)
     TL_ROWS_DISPATCH(nv, L)
 #undef L
   } else {
-    softmax_scaled_masked_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
+    launch_pdl(softmax_scaled_masked_kernel, row_grid(rows), 256, 0, as_stream(stream), 
         x, divisor, mask, mask_rows, out, rows, cols, row_vec(cols, {x, out, mask}));
   }
   return launch_status("tl_softmax_scaled_masked_rows");
@@ -542,14 +674,20 @@ int tl_softmax_backward_rows(const float *grad, const float *y, const float *div
                              float *dx, uint32_t rows, uint32_t cols, void *stream) {
   if (rows == 0 || cols == 0) return TL_OK;
   if (!grad || !y || !dx) return fail(TL_ERR_INVALID, "tl_softmax_backward_rows: null pointer");
+  const int np = pairs_for(cols, {grad, y, dx});
   const int nv = row_vec(cols, {grad, y, dx}) ? regs_for(cols) : 0;
-  if (nv) {
-#define L(NV) softmax_backward_regs_kernel<NV><<<row_grid(rows), 256, 0, as_stream(stream)>>>( \
+  if (np) {
+#define L(NP) launch_pdl(softmax_backward_pairs_kernel<NP>, row_grid(rows), 256, 0, as_stream(stream),  \
+    grad, y, divisor, dx, rows, cols)
+    TL_PAIRS_DISPATCH(np, L)
+#undef L
+  } else if (nv) {
+#define L(NV) launch_pdl(softmax_backward_regs_kernel<NV>, row_grid(rows), 256, 0, as_stream(stream),  \
     grad, y, divisor, dx, rows, cols)
     TL_ROWS_DISPATCH(nv, L)
 #undef L
   } else {
-    softmax_backward_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
+    launch_pdl(softmax_backward_kernel, row_grid(rows), 256, 0, as_stream(stream), 
         grad, y, divisor, dx, rows, cols, row_vec(cols, {grad, y, dx}));
   }
   return launch_status("tl_softmax_backward_rows");
@@ -560,7 +698,7 @@ int tl_rms_rows(const float *x, float *rms, uint32_t rows, uint32_t cols,
   if (rows == 0) return TL_OK;
   if (cols == 0) return fail(TL_ERR_INVALID, "tl_rms_rows: empty rows");
   if (!x || !rms) return fail(TL_ERR_INVALID, "tl_rms_rows: null pointer");
-  rms_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(x, rms, rows, cols,
+  launch_pdl(rms_kernel, row_grid(rows), 256, 0, as_stream(stream), x, rms, rows, cols,
                                                             row_vec(cols, {x}));
   return launch_status("tl_rms_rows");
 }
@@ -572,12 +710,12 @@ int tl_rmsnorm_rows(const float *x, float *out, float *rms_out, uint32_t rows,
   if (!x || !out) return fail(TL_ERR_INVALID, "tl_rmsnorm_rows: null pointer");
   const int nv = row_vec(cols, {x, out}) ? regs_for(cols) : 0;
   if (nv) {
-#define L(NV) rmsnorm_regs_kernel<NV><<<row_grid(rows), 256, 0, as_stream(stream)>>>( \
+#define L(NV) launch_pdl(rmsnorm_regs_kernel<NV>, row_grid(rows), 256, 0, as_stream(stream),  \
     x, out, rms_out, rows, cols)
     TL_ROWS_DISPATCH(nv, L)
 #undef L
   } else {
-    rmsnorm_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
+    launch_pdl(rmsnorm_kernel, row_grid(rows), 256, 0, as_stream(stream), 
         x, out, rms_out, rows, cols, row_vec(cols, {x, out}));
   }
   return launch_status("tl_rmsnorm_rows");
@@ -592,12 +730,12 @@ int tl_rmsnorm_backward_rows(const float *grad, const float *x, const float *y,
     return fail(TL_ERR_INVALID, "tl_rmsnorm_backward_rows: null pointer");
   const int nv = row_vec(cols, {grad, x, y, dx, addend}) ? regs_for(cols) : 0;
   if (nv) {
-#define L(NV) rmsnorm_backward_regs_kernel<NV><<<row_grid(rows), 256, 0, as_stream(stream)>>>( \
+#define L(NV) launch_pdl(rmsnorm_backward_regs_kernel<NV>, row_grid(rows), 256, 0, as_stream(stream),  \
     grad, x, y, addend, dx, rows, cols)
     TL_ROWS_DISPATCH(nv, L)
 #undef L
   } else {
-    rmsnorm_backward_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
+    launch_pdl(rmsnorm_backward_kernel, row_grid(rows), 256, 0, as_stream(stream), 
         grad, x, y, addend, dx, rows, cols, row_vec(cols, {grad, x, y, dx, addend}));
   }
   return launch_status("tl_rmsnorm_backward_rows");
@@ -609,7 +747,7 @@ int tl_xent_rows(const float *logits, const uint32_t *targets, float *loss,
     return fail(TL_ERR_INVALID, "cross_entropy requires logits with a non-empty final dimension");
   if (rows == 0) return TL_OK;
   if (!logits || !targets || !loss) return fail(TL_ERR_INVALID, "tl_xent_rows: null pointer");
-  xent_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
+  launch_pdl(xent_kernel, row_grid(rows), 256, 0, as_stream(stream), 
       logits, targets, loss, rows, vocab, row_vec(vocab, {logits}));
   return launch_status("tl_xent_rows");
 }
@@ -623,7 +761,7 @@ int tl_xent_backward_rows(const float *logits, const uint32_t *targets,
   if (rows == 0) return TL_OK;
   if (!logits || !targets || !dlogits)
     return fail(TL_ERR_INVALID, "tl_xent_backward_rows: null pointer");
-  xent_backward_kernel<<<row_grid(rows), 256, 0, as_stream(stream)>>>(
+  launch_pdl(xent_backward_kernel, row_grid(rows), 256, 0, as_stream(stream), 
       logits, targets, row_scale, dlogits, rows, vocab, row_vec(vocab, {logits, dlogits}));
   return launch_status("tl_xent_backward_rows");
 }

@@ -23,6 +23,7 @@ template <int V>
 __global__ void __launch_bounds__(256)
 transpose_rows_kernel(const float *__restrict__ x, float *__restrict__ out,
                       RowParams p, uint64_t n_rows) {
+  pdl_enter();
   const uint32_t per_row = p.row_len / V;
   const uint64_t total = n_rows * per_row;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
@@ -47,6 +48,7 @@ transpose_rows_kernel(const float *__restrict__ x, float *__restrict__ out,
 __global__ void __launch_bounds__(256)
 transpose_tile_kernel(const float *__restrict__ x, float *__restrict__ out,
                       uint32_t A, uint32_t Q, uint32_t B) {
+  pdl_enter();
   __shared__ float tile[32][33];
   const uint32_t pq = blockIdx.z;
   const uint32_t p = pq / Q, q = pq % Q;
@@ -117,9 +119,9 @@ extern "C" int tl_transpose(const float *x, const uint32_t *shape, int rank,
     const uint64_t rows = n / L;
     const bool vec = L % 4 == 0 && aligned16(x) && aligned16(out);
     if (vec)
-      transpose_rows_kernel<4><<<grid_for(n / 4, 256), 256, 0, s>>>(x, out, p, rows);
+      launch_pdl(transpose_rows_kernel<4>, grid_for(n / 4, 256), 256, 0, s, x, out, p, rows);
     else
-      transpose_rows_kernel<1><<<grid_for(n, 256), 256, 0, s>>>(x, out, p, rows);
+      launch_pdl(transpose_rows_kernel<1>, grid_for(n, 256), 256, 0, s, x, out, p, rows);
     return launch_status("tl_transpose rows");
   }
   uint32_t P = 1, Q = 1;
@@ -130,6 +132,6 @@ extern "C" int tl_transpose(const float *x, const uint32_t *shape, int rank,
     return fail(TL_ERR_RANGE, "tl_transpose: too many tiles");
   dim3 grid((B + 31) / 32, (A + 31) / 32, P * Q);
   if (grid.z > 65535u) return fail(TL_ERR_RANGE, "tl_transpose: batch too large");
-  transpose_tile_kernel<<<grid, 256, 0, s>>>(x, out, A, Q, B);
+  launch_pdl(transpose_tile_kernel, grid, 256, 0, s, x, out, A, Q, B);
   return launch_status("tl_transpose tiles");
 }

@@ -9,6 +9,7 @@
 
 #include <cmath>
 #include <string>
+#include <utility>
 
 namespace tl {
 
@@ -24,6 +25,34 @@ int check_cuda(cudaError_t e, const char *what);
 int launch_status(const char *what);
 
 inline cudaStream_t as_stream(void *s) { return static_cast<cudaStream_t>(s); }
+
+// Programmatic dependent launch: every kernel of the library is launched
+// with programmatic stream serialisation and waits for the previous
+// kernel's completion and memory (griddepcontrol.wait) before it touches
+// global memory, so its launch is staged while the previous kernel still
+// runs.  TL_PDL=0 in the environment turns it off.
+bool pdl_enabled();
+
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args &&...args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // failures are reported by launch_status (cudaGetLastError)
+  (void)cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Grid for a grid-stride loop over `work` items with `threads` per CTA,
 // capped at `per_sm` CTAs per SM.

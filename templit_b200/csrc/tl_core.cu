@@ -2,6 +2,9 @@
 // points of the C ABI (include/templit_cuda.h).
 #include "tl_common.cuh"
 
+#include <cstdlib>
+#include <cstring>
+
 #include <cstdio>
 #include <cstring>
 
@@ -43,11 +46,20 @@ uint32_t *device_status_ptr() {
 
 // Moves the status word into a mailbox and clears it, in stream order.
 __global__ void status_take_kernel(uint32_t *status, uint32_t *mailbox) {
+  pdl_enter();
   *mailbox = *status;
   *status = 0;
 }
 
 __device__ uint32_t g_status_mailbox;
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *e = std::getenv("TL_PDL");
+    return !(e && std::strcmp(e, "0") == 0);
+  }();
+  return on;
+}
 
 }  // namespace tl
 
@@ -89,7 +101,7 @@ int tl_device_status_enqueue(uint32_t *host_flags, void *stream) {
   if (rc) return rc;
   if (!status) return fail(TL_ERR_CUDA, "tl_device_status_enqueue: no status word");
   cudaStream_t s = as_stream(stream);
-  status_take_kernel<<<1, 1, 0, s>>>(status, mailbox);
+  launch_pdl(status_take_kernel, 1, 1, 0, s, status, mailbox);
   rc = launch_status("tl_device_status_enqueue");
   if (rc) return rc;
   return check_cuda(cudaMemcpyAsync(host_flags, mailbox, sizeof(uint32_t),
