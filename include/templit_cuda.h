@@ -299,6 +299,12 @@ enum tl_gemm_precision {
   TL_GEMM_3XTF32 = 2  /* tcgen05 with split big/small tf32 operands        */
 };
 #define TL_GEMM_MAX_BATCH_RANK 6
+#define TL_GEMM_MAX_GROUPS 4
+enum tl_gemm_group_mode {
+  TL_GEMM_GROUP_NONE = 0,
+  TL_GEMM_GROUP_N = 1,  /* C_g = op(A) op(B_g) (+ bias_g), A shared           */
+  TL_GEMM_GROUP_K = 2   /* C = sum_g op(A_g) op(B_g) (+ bias) (+ addend / C)   */
+};
 /*
  * C[b] = op(A[b]) * op(B[b]) (+ bias) (+ beta * C[b]) for every batch index
  * b of batch_shape, with per-operand batch strides in elements (0 =
@@ -339,6 +345,20 @@ typedef struct tl_gemm_desc {
    * gelu_out and addend share ldc.  With the batch strides they address
    * strided views, e.g. one attention head of a [B, T, H, D] tensor. */
   uint64_t lda, ldb, ldc;
+  /* Grouped products (group_mode != TL_GEMM_GROUP_NONE, 2 <= groups <=
+   * TL_GEMM_MAX_GROUPS) sharing every other field: the Q, K and V
+   * projections of one input (GROUP_N: b_group[g], c_group[g],
+   * bias_group[g] per product, `a` shared, c_group[0] == c; no GELU,
+   * addend or beta), or a sum of products into one output over their
+   * concatenated K (GROUP_K: a_group[g], b_group[g], each product of depth
+   * k; bias, addend and beta apply once; no GELU).  One launch instead of
+   * `groups`. */
+  int32_t group_mode;
+  uint32_t groups;
+  const float *a_group[TL_GEMM_MAX_GROUPS];
+  const float *b_group[TL_GEMM_MAX_GROUPS];
+  float *c_group[TL_GEMM_MAX_GROUPS];
+  const float *bias_group[TL_GEMM_MAX_GROUPS];
 } tl_gemm_desc;
 int tl_gemm(const tl_gemm_desc *desc, void *stream);
 size_t tl_gemm_workspace_size(const tl_gemm_desc *desc);

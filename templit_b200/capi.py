@@ -15,6 +15,8 @@ from ctypes import (POINTER, Structure, c_char_p, c_float, c_int, c_int32,
 BUILD_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build")
 
 TL_MAX_RANK = 8
+TL_GEMM_MAX_GROUPS = 4
+TL_GEMM_GROUP_NONE, TL_GEMM_GROUP_N, TL_GEMM_GROUP_K = 0, 1, 2
 TL_GEMM_MAX_BATCH_RANK = 6
 TL_OPT_CHUNK = 8192
 
@@ -46,7 +48,11 @@ class TlGemmDesc(Structure):
                 ("b_batch_stride", c_uint64 * TL_GEMM_MAX_BATCH_RANK),
                 ("c_batch_stride", c_uint64 * TL_GEMM_MAX_BATCH_RANK),
                 ("workspace", c_void_p), ("workspace_bytes", c_uint64),
-                ("addend", c_void_p), ("lda", c_uint64), ("ldb", c_uint64), ("ldc", c_uint64)]
+                ("addend", c_void_p), ("lda", c_uint64), ("ldb", c_uint64), ("ldc", c_uint64),
+                ("group_mode", c_int32), ("groups", c_uint32),
+                ("a_group", c_void_p * TL_GEMM_MAX_GROUPS), ("b_group", c_void_p * TL_GEMM_MAX_GROUPS),
+                ("c_group", c_void_p * TL_GEMM_MAX_GROUPS),
+                ("bias_group", c_void_p * TL_GEMM_MAX_GROUPS)]
 
 
 class TlgConfig(Structure):

@@ -24,6 +24,13 @@ struct GemmArgs {
   uint64_t sc[TL_GEMM_MAX_BATCH_RANK];
   uint64_t batch_count;
   uint64_t batch_base;  // first batch index of this launch
+  // grouped products (tl_gemm_desc.group_mode): groups == 1 when none
+  int group_mode;
+  uint32_t groups;
+  const float *ag[TL_GEMM_MAX_GROUPS];
+  const float *bg[TL_GEMM_MAX_GROUPS];
+  float *cg[TL_GEMM_MAX_GROUPS];
+  const float *biasg[TL_GEMM_MAX_GROUPS];
 };
 
 // Element offsets of batch `z` (relative to batch_base) in A, B and C.

@@ -44,6 +44,31 @@ int to_args(const tl_gemm_desc *d, GemmArgs &g) {
   if (d->addend && d->beta != 0.0f && d->addend != d->c)
     return fail(TL_ERR_INVALID, "tl_gemm: addend with beta = 1 must be C");
   g.addend = d->addend ? d->addend : (d->beta != 0.0f ? d->c : nullptr);
+  g.group_mode = d->group_mode;
+  g.groups = 1;
+  if (d->group_mode != TL_GEMM_GROUP_NONE) {
+    if (d->group_mode != TL_GEMM_GROUP_N && d->group_mode != TL_GEMM_GROUP_K)
+      return fail(TL_ERR_INVALID, "tl_gemm: unknown group mode");
+    if (d->groups < 2 || d->groups > TL_GEMM_MAX_GROUPS)
+      return fail(TL_ERR_INVALID, "tl_gemm: group count out of range");
+    g.groups = d->groups;
+    for (uint32_t i = 0; i < g.groups; ++i) {
+      g.ag[i] = d->group_mode == TL_GEMM_GROUP_K ? d->a_group[i] : d->a;
+      g.bg[i] = d->b_group[i];
+      g.cg[i] = d->group_mode == TL_GEMM_GROUP_N ? d->c_group[i] : d->c;
+      g.biasg[i] = d->group_mode == TL_GEMM_GROUP_N ? d->bias_group[i] : d->bias;
+      if (!g.ag[i] || !g.bg[i] || !g.cg[i])
+        return fail(TL_ERR_INVALID, "tl_gemm: null group operand");
+    }
+    if (d->group_mode == TL_GEMM_GROUP_N && (d->gelu_out || d->addend || d->beta != 0.0f))
+      return fail(TL_ERR_INVALID, "tl_gemm: N-grouped products take no GELU, addend or beta");
+    if (d->group_mode == TL_GEMM_GROUP_K && d->gelu_out)
+      return fail(TL_ERR_INVALID, "tl_gemm: K-grouped products take no GELU");
+    if (d->group_mode == TL_GEMM_GROUP_N && d->c_group[0] != d->c)
+      return fail(TL_ERR_INVALID, "tl_gemm: c_group[0] must be c");
+    g.a = g.ag[0];
+    g.b = g.bg[0];
+  }
   g.lda = d->lda ? d->lda : (g.trans_a ? g.m : g.k);
   g.ldb = d->ldb ? d->ldb : (g.trans_b ? g.k : g.n);
   g.ldc = d->ldc ? d->ldc : g.n;
@@ -92,7 +117,18 @@ using namespace tl;
 extern "C" size_t tl_gemm_workspace_size(const tl_gemm_desc *d) {
   GemmArgs g;
   if (to_args(d, g) || g.m == 0 || g.n == 0 || g.batch_count == 0) return 0;
-  return wants_tc(d, g) ? tc_gemm_workspace(g) : 0;
+  if (!wants_tc(d, g)) return 0;
+  size_t ws = tc_gemm_workspace(g);
+  if (g.groups > 1) {  // split fallback: each product's own plan
+    for (uint32_t i = 0; i < g.groups; ++i) {
+      tl_gemm_desc one = *d;
+      one.group_mode = TL_GEMM_GROUP_NONE;
+      one.groups = 0;
+      const size_t w = tl_gemm_workspace_size(&one);
+      if (w > ws) ws = w;
+    }
+  }
+  return ws;
 }
 
 extern "C" int tl_gemm(const tl_gemm_desc *d, void *stream) {
@@ -107,6 +143,31 @@ extern "C" int tl_gemm(const tl_gemm_desc *d, void *stream) {
       return fail(TL_ERR_UNSUPPORTED, "tl_gemm: 3xTF32 is not built in this version");
     rc = launch_tc_gemm(g, d->workspace, d->workspace_bytes, s);
     if (rc != TL_ERR_UNSUPPORTED) return rc;
+  }
+  if (g.groups > 1) {
+    // one product per group: N groups independently; K groups as a chain
+    // accumulating into C (bias and addend with the first)
+    for (uint32_t i = 0; i < g.groups; ++i) {
+      tl_gemm_desc one = *d;
+      one.group_mode = TL_GEMM_GROUP_NONE;
+      one.groups = 0;
+      one.a = g.ag[i];
+      one.b = g.bg[i];
+      one.c = g.cg[i];
+      if (d->group_mode == TL_GEMM_GROUP_N) {
+        one.bias = g.biasg[i];
+      } else if (i > 0) {
+        one.bias = nullptr;
+        one.addend = nullptr;
+        one.beta = 1.0f;
+        one.gelu_out = nullptr;
+      } else {
+        one.gelu_out = nullptr;
+      }
+      rc = tl_gemm(&one, stream);
+      if (rc) return rc;
+    }
+    return TL_OK;
   }
   return launch_sgemm(g, s);
 }

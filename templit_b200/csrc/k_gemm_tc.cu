@@ -45,10 +45,23 @@ struct OpMap {
                     // dims 32 x K x MN/32 [x batch]), 0: one load per chunk
 };
 
+// Tensor maps of one launch: per group the A, B and C maps (N groups share
+// A; K groups share C), plus GELU output and addend (C's layout).
+struct TcMaps {
+  CUtensorMap a[TL_GEMM_MAX_GROUPS];
+  CUtensorMap b[TL_GEMM_MAX_GROUPS];
+  CUtensorMap c[TL_GEMM_MAX_GROUPS];
+  CUtensorMap gelu;
+  CUtensorMap addend;
+};
+
 struct TcArgs {
   GemmArgs g;
   uint32_t mt, nt;        // tiles along M and N
-  uint64_t num_tiles;     // batch * splits * mt * nt
+  uint64_t num_tiles;     // groups (N) * batch * splits * mt * nt
+  uint32_t tiles_per_group;  // batch * splits * mt * nt
+  bool kgroups;              // K-grouped: k-tiles run through the groups
+  uint32_t kb_per_group;     // k-tiles of one group
   // batch dims each operand's tensor map walks (those with a nonzero
   // stride), as indices into the product's batch dims
   OpMap ma, mb, mc;
@@ -83,9 +96,12 @@ struct Cfg {
 // consecutive row blocks of the same column block and K slice, so they
 // share the B tiles in L2.
 __device__ __forceinline__ void decode_tile(const TcArgs &t, uint64_t tile, uint64_t &z,
-                                            uint32_t &s, uint32_t &mb, uint32_t &nb) {
+                                            uint32_t &s, uint32_t &mb, uint32_t &nb,
+                                            uint32_t &grp) {
   // fewer than 2^32 tiles (checked at launch): 32-bit divisions
-  const uint32_t tl = static_cast<uint32_t>(tile);
+  uint32_t tl = static_cast<uint32_t>(tile);
+  grp = tl / t.tiles_per_group;  // N groups: group-major
+  tl -= grp * t.tiles_per_group;
   mb = tl % t.mt;
   uint32_t r = tl / t.mt;
   nb = r % t.nt;
@@ -123,11 +139,7 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t j) {
 
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
-tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-               const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmC,
-               const __grid_constant__ CUtensorMap tmG,
-               const __grid_constant__ CUtensorMap tmD, const TcArgs t) {
+tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -159,9 +171,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
     *abort_flag = 0;
     ptx::fence_barrier_init();
     ptx::fence_proxy_async_smem();
-    ptx::prefetch_tensormap(&tmA);
-    ptx::prefetch_tensormap(&tmB);
-    if (t.tma_epi) ptx::prefetch_tensormap(&tmC);
+    for (uint32_t i = 0; i < t.g.groups; ++i) {
+      if (i == 0 || t.kgroups) ptx::prefetch_tensormap(&maps.a[i]);
+      ptx::prefetch_tensormap(&maps.b[i]);
+      if (t.tma_epi && (i == 0 || !t.kgroups)) ptx::prefetch_tensormap(&maps.c[i]);
+    }
   }
   if (warp == 1) {
     ptx::tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -171,7 +185,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t ktiles = (g.k + BK - 1) / BK;
+  const uint32_t ktiles = t.kgroups ? t.g.groups * t.kb_per_group : (g.k + BK - 1) / BK;
   // the setup above overlaps the previous kernel's tail
   pdl_enter();
 
@@ -188,8 +202,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
       for (uint64_t tile = blockIdx.x; tile < t.num_tiles && !*abort_flag;
            tile += gridDim.x) {
         uint64_t z;
-        uint32_t s, mb, nb, kb0, kb1;
-        decode_tile(t, tile, z, s, mb, nb);
+        uint32_t s, mb, nb, kb0, kb1, grp;
+        decode_tile(t, tile, z, s, mb, nb, grp);
         k_range(t, ktiles, s, kb0, kb1);
         int32_t cz[TL_GEMM_MAX_BATCH_RANK], za[3], zb[3];
         batch_coords(g, z, cz);
@@ -204,26 +218,34 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
           uint8_t *sa = stage_base + stage * C::STAGE_BYTES;
           uint8_t *sb = sa + kA_BYTES;
           ptx::mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-          const int32_t k0 = static_cast<int32_t>(kb * BK);
+          // K groups walk group after group; N groups use their own B
+          uint32_t kg = 0, kl = kb;
+          if (t.kgroups) {
+            kg = kb / t.kb_per_group;
+            kl = kb - kg * t.kb_per_group;
+          }
+          const CUtensorMap *tmA = &maps.a[kg];
+          const CUtensorMap *tmB = &maps.b[t.kgroups ? kg : grp];
+          const int32_t k0 = static_cast<int32_t>(kl * BK);
           if (!A_MN) {
-            ptx::tma_load_nd(sa, &tmA, &full[stage], k0, m0, t.ma.nb, za);
+            ptx::tma_load_nd(sa, tmA, &full[stage], k0, m0, t.ma.nb, za);
           } else if (t.ma.chunked) {
             const int32_t c[5] = {0, k0, m0 / 32, za[0], za[1]};
-            ptx::tma_load_rank(sa, &tmA, &full[stage], 3 + t.ma.nb, c);
+            ptx::tma_load_rank(sa, tmA, &full[stage], 3 + t.ma.nb, c);
           } else {
 #pragma unroll
             for (int j = 0; j < BM / 32; ++j)
-              ptx::tma_load_nd(sa + j * 4096, &tmA, &full[stage], m0 + 32 * j, k0, t.ma.nb, za);
+              ptx::tma_load_nd(sa + j * 4096, tmA, &full[stage], m0 + 32 * j, k0, t.ma.nb, za);
           }
           if (!B_MN) {
-            ptx::tma_load_nd(sb, &tmB, &full[stage], k0, n0, t.mb.nb, zb);
+            ptx::tma_load_nd(sb, tmB, &full[stage], k0, n0, t.mb.nb, zb);
           } else if (t.mb.chunked) {
             const int32_t c[5] = {0, k0, n0 / 32, zb[0], zb[1]};
-            ptx::tma_load_rank(sb, &tmB, &full[stage], 3 + t.mb.nb, c);
+            ptx::tma_load_rank(sb, tmB, &full[stage], 3 + t.mb.nb, c);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 32; ++j)
-              ptx::tma_load_nd(sb + j * 4096, &tmB, &full[stage], n0 + 32 * j, k0, t.mb.nb, zb);
+              ptx::tma_load_nd(sb + j * 4096, tmB, &full[stage], n0 + 32 * j, k0, t.mb.nb, zb);
           }
           ++issued;
           if (++stage == C::STAGES) {
@@ -264,8 +286,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
         const uint32_t d_tmem = tmem_base + acc * C::ACC_COLS;
         bool ok = true;
         uint64_t z;
-        uint32_t s, mb, nb, kb0, kb1;
-        decode_tile(t, tile, z, s, mb, nb);
+        uint32_t s, mb, nb, kb0, kb1, grp;
+        decode_tile(t, tile, z, s, mb, nb, grp);
         k_range(t, ktiles, s, kb0, kb1);
         for (uint32_t kb = kb0; kb < kb1; ++kb) {
           if (!ptx::mbar_wait_bounded(&full[stage], phase, kWaitLimitNs)) {
@@ -327,14 +349,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
       if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
       ptx::tc_fence_after();
       uint64_t z;
-      uint32_t s, mb, nb;
-      decode_tile(t, tile, z, s, mb, nb);
+      uint32_t s, mb, nb, grp;
+      decode_tile(t, tile, z, s, mb, nb, grp);
       uint64_t oa, ob, oc;
       batch_offsets(g, z, oa, ob, oc);
       // split-K slices store their raw partial product; the epilogue
       // (bias, accumulate, GELU) runs once in the slice-summing kernel
       const bool raw = t.partial != nullptr;
-      float *Cb = raw ? t.partial + static_cast<size_t>(s) * g.m * g.n : g.c + oc;
+      const uint32_t slice = grp * t.splits + s;  // [groups][splits][M][N]
+      float *Cb = raw ? t.partial + static_cast<size_t>(slice) * g.m * g.n : g.c + oc;
+      // N groups: this tile's product has its own output and bias
+      const float *bias = t.g.groups > 1 && !t.kgroups ? t.g.biasg[grp] : g.bias;
       const uint32_t m = mb * BM + q * 32 + lane;
       const uint32_t n_base = nb * BN;
       const bool row_ok = m < g.m;
@@ -354,8 +379,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
         const int32_t y0 = static_cast<int32_t>(mb * BM + q * 32);
         int32_t zc[3];
         int ncz;
-        if (raw) {  // split-K slices: [splits][M][N]
-          zc[0] = static_cast<int32_t>(s);
+        if (raw) {  // split-K slices: [groups x splits][M][N]
+          zc[0] = static_cast<int32_t>(slice);
           zc[1] = zc[2] = 0;
           ncz = 1;
         } else {
@@ -382,7 +407,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
           if (with_add) {
             if (lane == 0) {
               ptx::mbar_arrive_expect_tx(my_abar, 4096);
-              ptx::tma_load_nd(box, &tmD, my_abar, static_cast<int32_t>(n0), y0, ncz, zc);
+              ptx::tma_load_nd(box, &maps.addend, my_abar, static_cast<int32_t>(n0), y0, ncz, zc);
             }
             const bool got_add = ptx::mbar_wait_bounded(my_abar, a_phase, kWaitLimitNs);
             a_phase ^= 1;
@@ -398,10 +423,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
           for (int j = 0; j < 8; ++j) {
             v[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
                                __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-            if (!raw && g.bias) {
+            if (!raw && bias) {
               const uint32_t nb4 = n0 + 4 * j;
               if (nb4 + 4 <= g.n) {
-                const float4 b = *reinterpret_cast<const float4 *>(g.bias + nb4);
+                const float4 b = *reinterpret_cast<const float4 *>(bias + nb4);
                 v[j] = make_float4(v[j].x + b.x, v[j].y + b.y, v[j].z + b.z, v[j].w + b.w);
               }
             }
@@ -415,7 +440,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
           ptx::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            ptx::tma_store_nd(&tmC, box, static_cast<int32_t>(n0), y0, ncz, zc);
+            ptx::tma_store_nd(&maps.c[raw ? 0 : grp], box, static_cast<int32_t>(n0), y0, ncz, zc);
             ptx::bulk_commit_group();
           }
           if (with_gelu) {
@@ -432,7 +457,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
             ptx::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              ptx::tma_store_nd(&tmG, gbox, static_cast<int32_t>(n0), y0, ncz, zc);
+              ptx::tma_store_nd(&maps.gelu, gbox, static_cast<int32_t>(n0), y0, ncz, zc);
               ptx::bulk_commit_group();
             }
           }
@@ -605,10 +630,12 @@ TcPlan plan_tc(const GemmArgs &g) {
   // runs as 3 x 128 instead of 2 x 256 with a quarter of the MMAs wasted,
   // and the attention products (N = 192) as one 192-wide tile.
   const uint64_t mt = (g.m + BM - 1) / BM;
-  if (g.batch_count * mt * ((g.n + 255) / 256) >= static_cast<uint64_t>(kNumSMs) / 2) {
+  const bool kgroups = g.groups > 1 && g.group_mode == TL_GEMM_GROUP_K;
+  const uint64_t outs = g.batch_count * (g.groups > 1 && !kgroups ? g.groups : 1);
+  if (outs * mt * ((g.n + 255) / 256) >= static_cast<uint64_t>(kNumSMs) / 2) {
     uint64_t best = ~0ull;
     for (int bn : {64, 128, 192, 256}) {
-      const uint64_t tiles = g.batch_count * mt * ((g.n + bn - 1) / bn);
+      const uint64_t tiles = outs * mt * ((g.n + bn - 1) / bn);
       const uint64_t cost = (tiles + kNumSMs - 1) / kNumSMs * (bn + 64);
       if (cost < best) {
         best = cost;
@@ -616,8 +643,8 @@ TcPlan plan_tc(const GemmArgs &g) {
       }
     }
   }
-  const uint64_t tiles = g.batch_count * ((g.m + BM - 1) / BM) * ((g.n + p.bn - 1) / p.bn);
-  const uint32_t ktiles = (g.k + BK - 1) / BK;
+  const uint64_t tiles = outs * ((g.m + BM - 1) / BM) * ((g.n + p.bn - 1) / p.bn);
+  const uint32_t ktiles = (g.k + BK - 1) / BK * (kgroups ? g.groups : 1);
   p.splits = 1;
   p.kb_per_split = ktiles;
   // Few output tiles but a long K (weight gradients: K = every token of the
@@ -630,7 +657,8 @@ TcPlan plan_tc(const GemmArgs &g) {
     if (want > 1) {
       p.kb_per_split = static_cast<uint32_t>((ktiles + want - 1) / want);
       p.splits = (ktiles + p.kb_per_split - 1) / p.kb_per_split;
-      p.workspace = static_cast<size_t>(p.splits) * g.m * g.n * sizeof(float);
+      p.workspace = static_cast<size_t>(p.splits) * (outs / g.batch_count) * g.m * g.n *
+                    sizeof(float);
     }
   }
   return p;
@@ -643,34 +671,45 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
   t.g = g;
   t.mt = (g.m + BM - 1) / BM;
   t.nt = (g.n + BN - 1) / BN;
+  t.kgroups = g.groups > 1 && g.group_mode == TL_GEMM_GROUP_K;
+  t.kb_per_group = (g.k + BK - 1) / BK;
+  const uint32_t ktiles = t.kgroups ? g.groups * t.kb_per_group : t.kb_per_group;
+  if (t.kgroups && g.k % BK) return fail(TL_ERR_UNSUPPORTED, "tl_gemm: K groups need k % 32 == 0");
   t.splits = partial ? plan.splits : 1;
-  t.kb_per_split = partial ? plan.kb_per_split : (g.k + BK - 1) / BK;
+  t.kb_per_split = partial ? plan.kb_per_split : ktiles;
   t.partial = partial;
-  t.num_tiles = g.batch_count * t.splits * t.mt * t.nt;
+  const uint64_t per_group = g.batch_count * t.splits * t.mt * t.nt;
+  const uint32_t ngroups = g.groups > 1 && !t.kgroups ? g.groups : 1;
+  t.num_tiles = per_group * ngroups;
   if (t.num_tiles >= (1ull << 32)) return fail(TL_ERR_UNSUPPORTED, "tl_gemm: too many tiles");
+  t.tiles_per_group = static_cast<uint32_t>(per_group);
   t.status = device_status_ptr();
   if (!t.status) return fail(TL_ERR_CUDA, "tl_gemm: no status word");
-  CUtensorMap ma, mb;
-  bool ok = A_MN ? make_operand_map(&ma, g.a, g.m, g.k, g.lda, g, g.sa, 32, 32,
-                                    CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, t.ma, BM / 32)
-                 : make_operand_map(&ma, g.a, g.k, g.m, g.lda, g, g.sa, 32, BM,
-                                    CU_TENSOR_MAP_SWIZZLE_128B, t.ma);
-  ok = ok && (B_MN ? make_operand_map(&mb, g.b, g.n, g.k, g.ldb, g, g.sb, 32, 32,
-                                      CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, t.mb, BN / 32)
-                   : make_operand_map(&mb, g.b, g.k, g.n, g.ldb, g, g.sb, 32, BN,
-                                      CU_TENSOR_MAP_SWIZZLE_128B, t.mb));
+  TcMaps maps{};
+  bool ok = true;
+  for (uint32_t i = 0; i < g.groups && ok; ++i) {
+    if (i == 0 || t.kgroups)
+      ok = A_MN ? make_operand_map(&maps.a[i], g.ag[i] ? g.ag[i] : g.a, g.m, g.k, g.lda, g, g.sa,
+                                   32, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, t.ma, BM / 32)
+                : make_operand_map(&maps.a[i], g.ag[i] ? g.ag[i] : g.a, g.k, g.m, g.lda, g, g.sa,
+                                   32, BM, CU_TENSOR_MAP_SWIZZLE_128B, t.ma);
+    ok = ok && (B_MN ? make_operand_map(&maps.b[i], g.bg[i] ? g.bg[i] : g.b, g.n, g.k, g.ldb, g,
+                                        g.sb, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, t.mb,
+                                        BN / 32)
+                     : make_operand_map(&maps.b[i], g.bg[i] ? g.bg[i] : g.b, g.k, g.n, g.ldb, g,
+                                        g.sb, 32, BN, CU_TENSOR_MAP_SWIZZLE_128B, t.mb));
+  }
   if (!ok) return fail(TL_ERR_UNSUPPORTED, "tl_gemm: tensor map rejected");
   // epilogue through TMA stores when C (and gelu_out, addend: same layout)
   // have 16-byte rows; otherwise per-thread stores
-  CUtensorMap mc{}, mg{}, md{};
   if (partial) {
-    GemmArgs slices = g;  // [splits][M][N], dense
+    GemmArgs slices = g;  // [groups x splits][M][N], dense
     slices.batch_rank = 1;
-    slices.batch_shape[0] = t.splits;
+    slices.batch_shape[0] = t.splits * ngroups;
     const uint64_t mn = static_cast<uint64_t>(g.m) * g.n;
     OpMap unused;
     t.tma_epi = g.n % 4 == 0 &&
-                make_operand_map(&mc, partial, g.n, g.m, g.n, slices, &mn, 32, 32,
+                make_operand_map(&maps.c[0], partial, g.n, g.m, g.n, slices, &mn, 32, 32,
                                  CU_TENSOR_MAP_SWIZZLE_128B, unused);
   } else {
     bool strides_ok = g.ldc % 4 == 0;
@@ -679,13 +718,21 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
     t.tma_epi = g.n % 4 == 0 && strides_ok && aligned16(g.c) &&
                 (!g.bias || aligned16(g.bias)) && (!g.gelu_out || aligned16(g.gelu_out)) &&
                 (!g.addend || aligned16(g.addend)) &&
-                make_operand_map(&mc, g.c, g.n, g.m, g.ldc, g, g.sc, 32, 32,
-                                 CU_TENSOR_MAP_SWIZZLE_128B, t.mc) &&
-                (!g.gelu_out || make_operand_map(&mg, g.gelu_out, g.n, g.m, g.ldc, g, g.sc, 32,
-                                                 32, CU_TENSOR_MAP_SWIZZLE_128B, og)) &&
-                (!g.addend || make_operand_map(&md, g.addend, g.n, g.m, g.ldc, g, g.sc, 32, 32,
-                                               CU_TENSOR_MAP_SWIZZLE_128B, od));
+                (!g.gelu_out || make_operand_map(&maps.gelu, g.gelu_out, g.n, g.m, g.ldc, g,
+                                                 g.sc, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, og)) &&
+                (!g.addend || make_operand_map(&maps.addend, g.addend, g.n, g.m, g.ldc, g, g.sc,
+                                               32, 32, CU_TENSOR_MAP_SWIZZLE_128B, od));
+    for (uint32_t i = 0; i < ngroups && t.tma_epi; ++i) {
+      float *ci = g.cg[i] ? g.cg[i] : g.c;
+      const float *bi = g.groups > 1 ? g.biasg[i] : g.bias;
+      t.tma_epi = aligned16(ci) && (!bi || aligned16(bi)) &&
+                  make_operand_map(&maps.c[i], ci, g.n, g.m, g.ldc, g, g.sc, 32, 32,
+                                   CU_TENSOR_MAP_SWIZZLE_128B, t.mc);
+    }
   }
+  // grouped outputs leave only through the TMA epilogue
+  if (ngroups > 1 && !t.tma_epi)
+    return fail(TL_ERR_UNSUPPORTED, "tl_gemm: grouped outputs need 16-byte rows");
   static bool attr_set = false;
   if (!attr_set) {
     int rc = check_cuda(cudaFuncSetAttribute(tc_gemm_kernel<BN, A_MN, B_MN>,
@@ -696,13 +743,23 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
     attr_set = true;
   }
   const uint64_t grid = t.num_tiles < static_cast<uint64_t>(kNumSMs) ? t.num_tiles : kNumSMs;
-  launch_pdl(tc_gemm_kernel<BN, A_MN, B_MN>, static_cast<unsigned>(grid), kThreads, C::SMEM, s, 
-      ma, mb, mc, mg, md, t);
+  launch_pdl(tc_gemm_kernel<BN, A_MN, B_MN>, static_cast<unsigned>(grid), kThreads, C::SMEM, s,
+             maps, t);
   int rc = launch_status("tl_gemm tf32");
   if (rc || !partial) return rc;
   const uint64_t mn = static_cast<uint64_t>(g.m) * g.n;
-  launch_pdl(splitk_epilogue_kernel, grid_for(mn, 256), 256, 0, s, partial, t.splits, g);
-  return launch_status("tl_gemm split-K sum");
+  for (uint32_t i = 0; i < ngroups; ++i) {
+    GemmArgs gi = g;
+    if (ngroups > 1) {
+      gi.c = gi.cg[i];
+      gi.bias = gi.biasg[i];
+    }
+    launch_pdl(splitk_epilogue_kernel, grid_for(mn, 256), 256, 0, s,
+               partial + static_cast<size_t>(i) * t.splits * mn, t.splits, gi);
+    rc = launch_status("tl_gemm split-K sum");
+    if (rc) return rc;
+  }
+  return TL_OK;
 }
 
 template <int BN>
@@ -718,6 +775,8 @@ bool tc_supported(const GemmArgs &g) {
   // TMA rules: 16-byte aligned bases, row strides and batch strides; at
   // most three walked batch dims per operand.
   if (g.k == 0 || g.lda % 4 || g.ldb % 4 || !aligned16(g.a) || !aligned16(g.b)) return false;
+  for (uint32_t i = 0; i < g.groups; ++i)
+    if ((g.ag[i] && !aligned16(g.ag[i])) || (g.bg[i] && !aligned16(g.bg[i]))) return false;
   int na = 0, nb = 0;
   for (uint32_t d = 0; d < g.batch_rank; ++d) {
     if (g.sa[d] % 4 || g.sb[d] % 4) return false;

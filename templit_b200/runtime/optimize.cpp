@@ -41,7 +41,17 @@ Access access(const Op &op) {
     case Kind::Gemm:
       a.read(t[0]); a.read(t[1]); a.read(t[3]); a.read(t[5]);
       if (op.gemm.beta != 0.0f) a.read(t[2]);
-      a.write(t[2]); a.write(t[4]); break;
+      a.write(t[2]); a.write(t[4]);
+      if (op.gemm.group_mode == TL_GEMM_GROUP_N) {
+        for (size_t i = 0; i + 2 < op.group_refs.size(); i += 3) {
+          a.read(op.group_refs[i]);
+          a.write(op.group_refs[i + 1]);
+          a.read(op.group_refs[i + 2]);
+        }
+      } else if (op.gemm.group_mode == TL_GEMM_GROUP_K) {
+        for (const TRef &r : op.group_refs) a.read(r);
+      }
+      break;
     case Kind::HostWrite: case Kind::Fill: a.write(t[0]); break;
     case Kind::DevCopy: a.read(t[1]); a.write(t[0]); break;
     case Kind::GeluBwd: a.read(t[0]); a.read(t[1]); a.write(t[2]); break;
@@ -783,6 +793,173 @@ uint64_t fold_head_transposes(std::vector<Op> &p) {
   return folded;
 }
 
+// ------------------------------------------------------- grouped products
+bool groupable(const Op &op) {
+  return !op.dead && op.kind == Kind::Gemm && op.gemm.group_mode == TL_GEMM_GROUP_NONE &&
+         !op.gemm.gelu_out && op.i1 == 0;
+}
+
+// Same product shape and layout (everything but the operand addresses).
+bool same_product(const tl_gemm_desc &a, const tl_gemm_desc &b) {
+  if (a.m != b.m || a.n != b.n || a.k != b.k || a.trans_a != b.trans_a ||
+      a.trans_b != b.trans_b || a.precision != b.precision || a.lda != b.lda ||
+      a.ldb != b.ldb || a.ldc != b.ldc || a.batch_rank != b.batch_rank)
+    return false;
+  for (uint32_t d = 0; d < a.batch_rank; ++d)
+    if (a.batch_shape[d] != b.batch_shape[d] || a.a_batch_stride[d] != b.a_batch_stride[d] ||
+        a.b_batch_stride[d] != b.b_batch_stride[d] || a.c_batch_stride[d] != b.c_batch_stride[d])
+      return false;
+  return true;
+}
+
+// Products of one input by several weights (nn::MultiHeadAttention's
+// w_q, w_k, w_v applied to one tensor, include/nn/multi_head.h; their weight
+// gradients X^T dQ, X^T dK, X^T dV) run as one N-grouped launch, either at
+// the first product's position (later weights and biases unchanged since
+// then, later outputs untouched) or at the last one's (earlier operands
+// unchanged until then, earlier outputs not read before it).
+uint64_t group_shared_input(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  auto clash = [&](const std::vector<size_t> &members, const Op &y) {
+    for (size_t k : members) {
+      const Op &z = p[k];
+      for (uint64_t id : {z.t[0].id, z.t[1].id, z.t[2].id, z.t[3].id})
+        if (id && id == y.t[2].id) return true;
+      if (y.t[1].id == z.t[2].id || (y.t[3].p && y.t[3].id == z.t[2].id)) return true;
+    }
+    return false;
+  };
+  for (size_t i = 0; i < p.size(); ++i) {
+    Op &x = p[i];
+    if (!groupable(x) || x.gemm.beta != 0.0f || x.t[5].p) continue;
+    std::vector<size_t> cand;
+    for (size_t j = i + 1; j < p.size() && j < i + 256; ++j) {
+      const Op &y = p[j];
+      if (groupable(y) && y.gemm.beta == 0.0f && !y.t[5].p && same(y.t[0], x.t[0]) &&
+          same_product(x.gemm, y.gemm))
+        cand.push_back(j);
+    }
+    if (cand.empty()) continue;
+    // hoist to i
+    std::vector<size_t> members{i};
+    for (size_t j : cand) {
+      if (members.size() == TL_GEMM_MAX_GROUPS) break;
+      const Op &y = p[j];
+      if (!unchanged_between(p, i, j, x.t[0].id) || !unchanged_between(p, i, j, y.t[1].id) ||
+          (y.t[3].p && !unchanged_between(p, i, j, y.t[3].id)) ||
+          !untouched_between(p, i, j, y.t[2].id) || clash(members, y))
+        continue;
+      members.push_back(j);
+    }
+    size_t at = i;
+    if (members.size() < 2) {
+      // sink to the last candidate that keeps every earlier member valid
+      members.assign(1, i);
+      for (size_t j : cand) {
+        if (members.size() == TL_GEMM_MAX_GROUPS) break;
+        const Op &y = p[j];
+        if (clash(members, y) || !unchanged_between(p, i, j, x.t[0].id)) continue;
+        bool ok = true;
+        for (size_t k : members) {
+          const Op &z = p[k];
+          for (const TRef *r : {&z.t[1], &z.t[3]})
+            if (r->p && !unchanged_between(p, k, j, r->id)) ok = false;
+          if (!untouched_between(p, k, j, z.t[2].id)) ok = false;
+        }
+        if (ok) members.push_back(j);
+      }
+      if (members.size() < 2) continue;
+      at = members.back();
+    }
+    Op grouped = p[members.front()];
+    tl_gemm_desc &g = grouped.gemm;
+    g.group_mode = TL_GEMM_GROUP_N;
+    g.groups = static_cast<uint32_t>(members.size());
+    grouped.group_refs.clear();
+    for (size_t k = 0; k < members.size(); ++k) {
+      const Op &y = p[members[k]];
+      g.b_group[k] = y.gemm.b;
+      g.c_group[k] = y.gemm.c;
+      g.bias_group[k] = y.gemm.bias;
+      if (k > 0) {
+        grouped.group_refs.push_back(y.t[1]);
+        grouped.group_refs.push_back(y.t[2]);
+        grouped.group_refs.push_back(y.t[3]);
+      }
+    }
+    for (size_t k : members) p[k].dead = true;
+    p[at] = std::move(grouped);
+    folded += members.size() - 1;
+  }
+  return folded;
+}
+
+// The input gradient of a tensor used by several products, summed by the
+// executor one product at a time (dX = dQ Wq^T, + dK Wk^T, + dV Wv^T after
+// the accumulate folds: a product, one with it as addend, one accumulating
+// in place): one K-grouped product over the concatenated K at the last
+// product's position.
+uint64_t group_summed_products(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t i = 0; i < p.size(); ++i) {
+    if (!groupable(p[i]) || p[i].gemm.beta != 0.0f) continue;
+    std::vector<size_t> chain{i};
+    size_t cur = i;
+    while (chain.size() < TL_GEMM_MAX_GROUPS) {
+      const TRef out = p[cur].t[2];
+      const size_t j = first_reader(p, cur, out.id);
+      if (j == kNone) break;
+      const Op &y = p[j];
+      if (!groupable(y) || y.t[3].p || !same_product(p[i].gemm, y.gemm)) break;
+      const bool as_addend = y.gemm.beta == 0.0f && same(y.t[5], out) && !same(y.t[0], out) &&
+                             !same(y.t[1], out);
+      const bool in_place = y.gemm.beta != 0.0f && !y.t[5].p && same(y.t[2], out) &&
+                            !same(y.t[0], out) && !same(y.t[1], out);
+      if (!as_addend && !in_place) break;
+      if (as_addend && !dead_after(p, j, out.id)) break;
+      chain.push_back(j);
+      cur = j;
+    }
+    if (chain.size() < 2) continue;
+    const size_t last = chain.back();
+    bool ok = true;
+    for (size_t k = 0; k + 1 < chain.size() && ok; ++k) {
+      const Op &y = p[chain[k]];
+      for (const TRef *r : {&y.t[0], &y.t[1], &y.t[3], &y.t[5]})
+        if (r->p && !unchanged_between(p, chain[k], last, r->id)) ok = false;
+    }
+    if (!ok) continue;
+    Op merged = p[last];
+    const Op &first = p[chain.front()];
+    tl_gemm_desc &g = merged.gemm;
+    g.group_mode = TL_GEMM_GROUP_K;
+    g.groups = static_cast<uint32_t>(chain.size());
+    g.beta = 0.0f;
+    g.bias = first.gemm.bias;
+    g.addend = first.gemm.addend;
+    merged.t[3] = first.t[3];
+    merged.t[5] = first.t[5];
+    merged.t[0] = first.t[0];
+    merged.t[1] = first.t[1];
+    g.a = first.gemm.a;
+    g.b = first.gemm.b;
+    merged.group_refs.clear();
+    for (size_t k = 0; k < chain.size(); ++k) {
+      const Op &y = p[chain[k]];
+      g.a_group[k] = y.gemm.a;
+      g.b_group[k] = y.gemm.b;
+      if (k > 0) {
+        merged.group_refs.push_back(y.t[0]);
+        merged.group_refs.push_back(y.t[1]);
+      }
+    }
+    for (size_t k = 0; k + 1 < chain.size(); ++k) p[chain[k]].dead = true;
+    p[last] = std::move(merged);
+    folded += chain.size() - 1;
+  }
+  return folded;
+}
+
 // --------------------------------------------------------- copy forwarding
 bool elementwise(Kind k) {
   return k == Kind::Binary || k == Kind::Scalar || k == Kind::Unary || k == Kind::Copy ||
@@ -1191,6 +1368,8 @@ uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live) {
   folded += fuse_gemm_accumulate(prog);
   folded += fuse_row_backward_tails(prog);
   folded += fuse_score_softmax(prog);
+  folded += group_summed_products(prog);
+  folded += group_shared_input(prog);
   folded += fuse_step(prog);
   if (comm) add_gradient_allreduce(prog);
   g_live = nullptr;

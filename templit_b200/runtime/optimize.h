@@ -10,9 +10,9 @@ namespace cuda::internal {
 
 // Allocation ids an op reads / writes.
 struct Access {
-  uint64_t r[10];
+  uint64_t r[16];
   int nr = 0;
-  uint64_t w[3];
+  uint64_t w[6];
   int nw = 0;
   void read(const TRef &t) {
     if (t.p) r[nr++] = t.id;

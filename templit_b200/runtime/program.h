@@ -90,6 +90,9 @@ struct Op {
   tl_gemm_desc gemm{};
   std::vector<uint8_t> host;       // HostWrite payload
   std::vector<MultiSlot> multi;    // MultiAdamW / AllReduce
+  // grouped GEMM operands beyond group 0 (gemm.group_mode): N groups
+  // (B, C, bias) per group, K groups (A, B) per group, from group 1 on
+  std::vector<TRef> group_refs;
   bool dead = false;               // folded away by the optimiser
   uint32_t src = UINT32_MAX;       // index in the recorded program (optimiser cache)
 };

@@ -471,6 +471,37 @@ void head_transposes_become_strides() {
           "the output lands in [B, T, H, D] directly");
 }
 
+
+// Q, K, V projections of one input: one N-grouped product; the summed input
+// gradient dX = dQ Wq^T + dK Wk^T + dV Wv^T: one K-grouped product
+void projections_grouped() {
+  auto x = tensor({12288, 384}), wq = tensor({384, 384}), wk = tensor({384, 384});
+  auto wv = tensor({384, 384}), q = tensor({12288, 384}), k = tensor({12288, 384});
+  auto v = tensor({12288, 384});
+  std::vector<Op> p = {gemm(x, wq, q, 12288, 384, 384), gemm(x, wk, k, 12288, 384, 384),
+                       gemm(x, wv, v, 12288, 384, 384)};
+  require(optimize(p, nullptr) == 2, "three projections grouped");
+  auto l = live(p);
+  require(l.size() == 1 && l[0]->gemm.group_mode == TL_GEMM_GROUP_N && l[0]->gemm.groups == 3 &&
+              l[0]->gemm.b_group[2] == wv.p && l[0]->gemm.c_group[1] == k.p,
+          "one launch, per-group weights and outputs");
+  auto dq = tensor({12288, 384}), dk = tensor({12288, 384}), dv = tensor({12288, 384});
+  auto pq = tensor({12288, 384}), dx = tensor({12288, 384});
+  Op g1 = gemm(dq, wq, pq, 12288, 384, 384), g2 = gemm(dk, wk, dx, 12288, 384, 384),
+     g3 = gemm(dv, wv, dx, 12288, 384, 384);
+  g1.gemm.trans_b = g2.gemm.trans_b = g3.gemm.trans_b = 1;
+  g2.t[5] = pq;
+  g2.gemm.addend = pq.f();
+  g3.gemm.beta = 1.0f;
+  std::vector<Op> q2 = {g1, g2, g3, release(pq)};
+  require(optimize(q2, nullptr) == 2, "three summed products grouped");
+  auto m = live(q2);
+  require(m.size() == 1 && m[0]->gemm.group_mode == TL_GEMM_GROUP_K && m[0]->gemm.groups == 3 &&
+              m[0]->gemm.a_group[0] == dq.p && m[0]->gemm.b_group[2] == wv.p &&
+              m[0]->t[2].id == dx.id && m[0]->gemm.beta == 0.0f && !m[0]->gemm.addend,
+          "one K-grouped product into dX");
+}
+
 }  // namespace
 
 int main() {
@@ -495,6 +526,7 @@ int main() {
       {"attention_scores_into_softmax", attention_scores_into_softmax},
       {"row_backward_tails", row_backward_tails},
       {"head_transposes_become_strides", head_transposes_become_strides},
+      {"projections_grouped", projections_grouped},
   };
   for (const auto &[name, fn] : cases) {
     try {

@@ -231,3 +231,62 @@ def test_head_strided_operands(dev, precision):
                       (H * T * T, T * T), (H * D * T, D * T), H * D, 0, 0, precision)
     want = np.matmul(np.swapaxes(qh, -1, -2).astype(np.float64), p.astype(np.float64))
     check(g, want)
+
+
+def _grouped(dev, mode, a_list, b_list, m, n, k, trans_a, trans_b, bias_list=None,
+             precision=capi.TL_GEMM_TF32):
+    """tl_gemm with group_mode; returns the output(s)."""
+    ta = [dev.t(a) for a in a_list]
+    tb = [dev.t(b) for b in b_list]
+    groups = len(b_list)
+    outs = [dev.empty((m, n)) for _ in range(groups if mode == capi.TL_GEMM_GROUP_N else 1)]
+    tbias = [dev.t(b) for b in bias_list] if bias_list else None
+    d = capi.TlGemmDesc()
+    d.a, d.b, d.c = ta[0].data_ptr(), tb[0].data_ptr(), outs[0].data_ptr()
+    d.m, d.n, d.k = m, n, k
+    d.trans_a, d.trans_b = int(trans_a), int(trans_b)
+    d.precision = precision
+    d.group_mode, d.groups = mode, groups
+    for i in range(groups):
+        d.a_group[i] = ta[min(i, len(ta) - 1)].data_ptr()
+        d.b_group[i] = tb[i].data_ptr()
+        if mode == capi.TL_GEMM_GROUP_N:
+            d.c_group[i] = outs[i].data_ptr()
+            if tbias:
+                d.bias_group[i] = tbias[i].data_ptr()
+    nbytes = dev.lib.tl_gemm_workspace_size(ctypes.byref(d))
+    ws = dev.ws(nbytes) if nbytes else None
+    if ws is not None:
+        d.workspace, d.workspace_bytes = ws.data_ptr(), nbytes
+    dev.call("tl_gemm", ctypes.byref(d), dev.stream)
+    return [dev.host(o) for o in outs]
+
+
+@pytest.mark.parametrize("precision", [capi.TL_GEMM_TF32, capi.TL_GEMM_FP32])
+def test_grouped_products(dev, precision):
+    """One launch for the Q, K and V projections of one input (N groups),
+    for their weight gradients (N groups, split K), and for the input
+    gradient summed over the three (K groups)."""
+    r = np.random.default_rng(23)
+    check = check_tf32 if precision == capi.TL_GEMM_TF32 else (
+        lambda g, w: np.testing.assert_allclose(g, w, rtol=1e-4, atol=1e-3))
+    x = r.standard_normal((2048, 384)).astype(np.float32)
+    ws = [r.standard_normal((384, 384)).astype(np.float32) for _ in range(3)]
+    bs = [r.standard_normal((384,)).astype(np.float32) for _ in range(3)]
+    outs = _grouped(dev, capi.TL_GEMM_GROUP_N, [x], ws, 2048, 384, 384, False, False, bs,
+                    precision)
+    for o, w, b in zip(outs, ws, bs):
+        check(o, ops.gemm(x, w, bias=b))
+    # weight gradients: X^T dY_g, K = 12288 (split-K slices per group)
+    xl = r.standard_normal((12288, 384)).astype(np.float32)
+    dys = [r.standard_normal((12288, 384)).astype(np.float32) for _ in range(3)]
+    outs = _grouped(dev, capi.TL_GEMM_GROUP_N, [xl], dys, 384, 384, 12288, True, False,
+                    precision=precision)
+    for o, dy in zip(outs, dys):
+        check(o, ops.gemm(xl, dy, True, False))
+    # input gradient: sum_g dY_g W_g^T over the concatenated K
+    gs = [r.standard_normal((2048, 384)).astype(np.float32) for _ in range(3)]
+    (out,) = _grouped(dev, capi.TL_GEMM_GROUP_K, gs, ws, 2048, 384, 384, False, True,
+                      precision=precision)
+    want = sum(ops.gemm(g, w, False, True) for g, w in zip(gs, ws))
+    check(out, want)
