@@ -36,6 +36,7 @@ def lib():
             "tlo_param_count": (c_int, [c_void_p, POINTER(c_uint64), POINTER(c_uint32)]),
             "tlo_get_params": (c_int, [c_void_p, POINTER(c_float), c_uint64]),
             "tlo_set_params": (c_int, [c_void_p, POINTER(c_float), c_uint64]),
+            "tlo_set_allreduce": (c_int, [c_void_p, ALLREDUCE_FN, c_void_p]),
         }
         for name, (res, args) in sig.items():
             f = getattr(_lib, name)
@@ -46,6 +47,10 @@ def lib():
 def _check(rc):
     if rc:
         raise RuntimeError(lib().tlo_last_error().decode())
+
+
+# void (*)(float *data, uint64_t count, void *ctx): sums a gradient across ranks
+ALLREDUCE_FN = ctypes.CFUNCTYPE(None, POINTER(c_float), c_uint64, c_void_p)
 
 
 class OracleGPT:
@@ -78,6 +83,14 @@ class OracleGPT:
         out = np.zeros(n.value, np.float32)
         _check(lib().tlo_get_params(self.h, out.ctypes.data_as(POINTER(c_float)), n.value))
         return out
+
+    def set_allreduce(self, fn):
+        """fn(array) sums a float32 gradient (numpy view) across ranks in
+        place; called once per gradient before the optimiser reads it."""
+        def cb(data, count, ctx):
+            fn(np.ctypeslib.as_array(data, shape=(count,)))
+        self._cb = ALLREDUCE_FN(cb)  # kept alive with the handle
+        _check(lib().tlo_set_allreduce(self.h, self._cb, None))
 
     def set_params(self, p):
         p = np.ascontiguousarray(p, np.float32)

@@ -88,6 +88,14 @@ int tlo_get_params(void *h, float *out, uint64_t count) {
   });
 }
 
+int tlo_set_allreduce(void *h, cpu_ref::Runtime::AllReduceFn fn, void *ctx) {
+  return guarded([&] {
+    auto *hd = static_cast<Handle *>(h);
+    hd->runtime.allreduce = fn;
+    hd->runtime.allreduce_ctx = ctx;
+  });
+}
+
 int tlo_set_params(void *h, const float *in, uint64_t count) {
   return guarded([&] { static_cast<Handle *>(h)->driver->set_params(in, count); });
 }

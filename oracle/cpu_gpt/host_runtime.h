@@ -91,9 +91,26 @@ inline std::vector<size_t> bstrides(const std::vector<uint32_t> &shape,
 
 class Runtime {
 public:
-  void start() {}
+  // Data parallelism, as the CUDA runtime's optimiser windows do it: every
+  // gradient an optimiser op reads is first summed across ranks, once per
+  // window (the callback performs the sum in place).
+  using AllReduceFn = void (*)(float *data, uint64_t count, void *ctx);
+  AllReduceFn allreduce = nullptr;
+  void *allreduce_ctx = nullptr;
+  std::vector<const void *> reduced;  // gradients summed in this window
+
+  void start() { reduced.clear(); }
   void submit() {}
   void wait() {}
+
+  void reduce_once(const Mat &g) {
+    if (!allreduce) return;
+    const void *key = g.get_storage()->data();
+    for (const void *k : reduced)
+      if (k == key) return;
+    reduced.push_back(key);
+    allreduce(const_cast<float *>(P(g)), g.numel(), allreduce_ctx);
+  }
   void abort() noexcept {}
   void cleanup() noexcept {}
 
@@ -439,11 +456,13 @@ public:
   }
   void scatter_index(const Mat &values, const IMat &ids, Mat &dst) { scatter(values, ids, dst, nullptr); }
   void accumulate_gradient_squared_norm(const Mat &g, Mat &sq) {
+    reduce_once(g);
     double s = 0;
     for (size_t i = 0; i < g.numel(); ++i) s += double(P(g)[i]) * P(g)[i];
     P(sq)[0] = static_cast<float>(double(P(sq)[0]) + s);
   }
   void clip_gradient(const Mat &g, const Mat &sq, float max_norm, Mat &o) {
+    reduce_once(g);
     const double n2 = std::max(double(P(sq)[0]), 1e-12);
     const double sc = std::min(1.0, double(max_norm) / std::sqrt(n2));
     for (size_t i = 0; i < g.numel(); ++i) P(o)[i] = static_cast<float>(P(g)[i] * sc);
@@ -451,6 +470,7 @@ public:
   void adamW(const Mat &p, const Mat &g, Mat &o, Mat &m1, Mat &m2, const Mat &b1, const Mat &b2,
              const Mat &decay, const Mat &lr, float eps, uint32_t step) {
     if (step == 0) throw std::invalid_argument("AdamW step must be greater than zero");
+    reduce_once(g);
     const double B1 = P(b1)[0], B2 = P(b2)[0], D = P(decay)[0], L = P(lr)[0];
     const double c1 = 1.0 - std::pow(B1, double(step)), c2 = 1.0 - std::pow(B2, double(step));
     const size_t n = p.numel();
