@@ -363,6 +363,33 @@ typedef struct tl_gemm_desc {
 int tl_gemm(const tl_gemm_desc *desc, void *stream);
 size_t tl_gemm_workspace_size(const tl_gemm_desc *desc);
 
+/* -------------------------------------------------------------- attention */
+/* The attention core of nn::MultiHeadAttention (include/nn/multi_head.h:
+ * 45-52) after the projections, for every batch b and head h:
+ *   S = Q_bh K_bh^T / divisor[0] + mask        (mask optional, [T, T])
+ *   P = softmax_rows(S)   -> p [B, H, T, T]    (kept for the backward)
+ *   O_bh = P V_bh         -> o (q's layout)
+ * q, k, v, o and the gradients share one layout: [B, H, T, D] (the tensors
+ * the reference's head split produces) or [B, T, H, D] (the projections
+ * before the split; each head is then read and written in place).  divisor
+ * is a device scalar (sqrt(D) in the reference), mask is added after the
+ * divide (causal_mask, include/nn/attention.h:10-22: -inf above the
+ * diagonal).  Products in `precision` (tl_gemm_precision), softmax fp32. */
+enum tl_attention_layout { TL_ATTN_BHTD = 0, TL_ATTN_BTHD = 1 };
+int tl_attention_fwd(const float *q, const float *k, const float *v, const float *divisor,
+                     const float *mask, float *p, float *o, uint32_t B, uint32_t T, uint32_t H,
+                     uint32_t D, int32_t layout, int32_t precision, void *workspace,
+                     size_t workspace_bytes, void *stream);
+/* Its backward (the product rules and SFTMX_DERIVATIVE, include/passes/
+ * execute.h:187-232,291-308): dq, dk, dv from d_o and the forward's p. */
+int tl_attention_bwd(const float *q, const float *k, const float *v, const float *p,
+                     const float *divisor, const float *d_o, float *dq, float *dk, float *dv,
+                     uint32_t B, uint32_t T, uint32_t H, uint32_t D, int32_t layout,
+                     int32_t precision, void *workspace, size_t workspace_bytes, void *stream);
+/* Scratch of either call: the scores (forward), their gradient and the
+ * softmax gradient (backward). */
+size_t tl_attention_workspace_size(uint32_t B, uint32_t T, uint32_t H, uint32_t D);
+
 #ifdef __cplusplus
 }
 #endif

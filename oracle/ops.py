@@ -266,3 +266,32 @@ def gemm(a, b, trans_a=False, trans_b=False, bias=None, c=None, beta=0.0):
     if beta:
         r = _f(c) + r
     return r
+
+
+# -------------------------------------------------------------- attention
+def causal_mask(t):
+    """[T, T] mask, -inf above the diagonal, 0 elsewhere (nn::causal_mask,
+    include/nn/attention.h:10-22)."""
+    return np.triu(np.full((t, t), -np.inf), 1)
+
+
+def attention_forward(q, k, v, divisor, mask=None):
+    """Attention core of MultiHeadAttention on head-split [B, H, T, D]
+    operands (include/nn/multi_head.h:45-52): P = softmax(Q K^T / divisor +
+    mask), O = P V.  Returns (P, O)."""
+    s = np.matmul(_f(q), np.swapaxes(_f(k), -1, -2)) / F64(divisor)
+    if mask is not None:
+        s = s + _f(mask)
+    p = softmax_rows(s)
+    return p, np.matmul(p, _f(v))
+
+
+def attention_backward(q, k, v, p, divisor, d_o):
+    """Gradients of attention_forward by the executor's rules: the product
+    rule of mult (execute.h:187-232), SFTMX_DERIVATIVE (execute.h:291-308)
+    and the divide by a constant.  Returns (dQ, dK, dV)."""
+    q, k, v, p, d_o = _f(q), _f(k), _f(v), _f(p), _f(d_o)
+    dp = np.matmul(d_o, np.swapaxes(v, -1, -2))
+    ds = softmax_backward(dp, p) / F64(divisor)
+    return (np.matmul(ds, k), np.matmul(np.swapaxes(ds, -1, -2), q),
+            np.matmul(np.swapaxes(p, -1, -2), d_o))

@@ -16,6 +16,8 @@ BUILD_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build")
 
 TL_MAX_RANK = 8
 TL_GEMM_MAX_GROUPS = 4
+TL_ATTN_BHTD = 0
+TL_ATTN_BTHD = 1
 TL_GEMM_GROUP_NONE, TL_GEMM_GROUP_N, TL_GEMM_GROUP_K = 0, 1, 2
 TL_GEMM_MAX_BATCH_RANK = 6
 TL_OPT_CHUNK = 8192
@@ -89,6 +91,13 @@ CUDA_ABI = {
     "tl_event_record": (c_int, [c_void_p, c_void_p]),
     "tl_event_elapsed_ms": (c_int, [POINTER(c_float), c_void_p, c_void_p]),
     "tl_event_query": (c_int, [c_void_p, POINTER(c_int)]),
+    "tl_attention_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                 c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_int32,
+                                 c_int32, c_void_p, c_size_t, c_void_p]),
+    "tl_attention_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                 c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_uint32,
+                                 c_uint32, c_int32, c_int32, c_void_p, c_size_t, c_void_p]),
+    "tl_attention_workspace_size": (c_size_t, [c_uint32, c_uint32, c_uint32, c_uint32]),
     "tl_graph_capture_begin": (c_int, [c_void_p]),
     "tl_graph_capture_end": (c_int, [c_void_p, POINTER(c_void_p)]),
     "tl_graph_launch": (c_int, [c_void_p, c_void_p]),

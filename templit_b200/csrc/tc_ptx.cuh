@@ -7,6 +7,16 @@
 #include <stdint.h>
 
 namespace tl {
+
+// cuTensorMapEncodeTiled, fetched from the driver once (nullptr when the
+// driver does not offer it).
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+EncodeTiledFn tensor_map_encoder();
+
 namespace ptx {
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
@@ -273,6 +283,11 @@ __device__ __forceinline__ void tmem_load_32x32b_x32(uint32_t taddr, uint32_t (&
         "=r"(r[31])
       : "r"(taddr)
       : "memory");
+}
+
+// Named barrier `id` (1..15) over `count` threads (a multiple of 32).
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 __device__ __forceinline__ void tmem_load_wait() {

@@ -155,6 +155,32 @@ class Dev:
                   self.p(out), x.size // cols, cols, self.stream)
         return self.host(out)
 
+    def attention(self, q, k, v, divisor, mask=None, d_o=None, layout=capi.TL_ATTN_BHTD,
+                  precision=capi.TL_GEMM_TF32):
+        """tl_attention_fwd (and tl_attention_bwd when d_o is given) on
+        operands in `layout`; returns (p, o) or (p, o, dq, dk, dv)."""
+        q, k, v = (np.asarray(x, np.float32) for x in (q, k, v))
+        if layout == capi.TL_ATTN_BHTD:
+            B, H, T, D = q.shape
+        else:
+            B, T, H, D = q.shape
+        tq, tk, tv = self.t(q), self.t(k), self.t(v)
+        td = self.t(np.asarray([divisor], np.float32))
+        tm = self.t(np.asarray(mask, np.float32)) if mask is not None else None
+        ws = self.ws(self.lib.tl_attention_workspace_size(B, T, H, D))
+        p, o = self.empty((B, H, T, T)), self.empty(q.shape)
+        self.call("tl_attention_fwd", self.p(tq), self.p(tk), self.p(tv), self.p(td), self.p(tm),
+                  self.p(p), self.p(o), B, T, H, D, layout, precision, self.p(ws), ws.numel(),
+                  self.stream)
+        if d_o is None:
+            return self.host(p), self.host(o)
+        tg = self.t(d_o)
+        dq, dk, dv = self.empty(q.shape), self.empty(q.shape), self.empty(q.shape)
+        self.call("tl_attention_bwd", self.p(tq), self.p(tk), self.p(tv), self.p(p), self.p(td),
+                  self.p(tg), self.p(dq), self.p(dk), self.p(dv), B, T, H, D, layout, precision,
+                  self.p(ws), ws.numel(), self.stream)
+        return tuple(self.host(x) for x in (p, o, dq, dk, dv))
+
     def softmax_bwd_div(self, g, y, divisor):
         g = np.asarray(g, np.float32)
         cols = g.shape[-1]

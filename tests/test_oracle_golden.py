@@ -168,3 +168,33 @@ def test_oracle_matches_reference_cpu_runtime():
         else:
             raise KeyError(op)
         np.testing.assert_allclose(got, want, atol=tol, rtol=1e-6, err_msg=name)
+
+
+def test_oracle_attention_gradients_match_finite_differences():
+    """The attention backward of the oracle (product rules + softmax
+    derivative) agrees with central differences of its forward, so the
+    GPU attention parity tests check against the right gradients."""
+    rng = np.random.default_rng(5)
+    B, H, T, D = 1, 2, 5, 3
+    q, k, v, d_o = (rng.standard_normal((B, H, T, D)) for _ in range(4))
+    mask = ops.causal_mask(T)
+    div = np.sqrt(D)
+    p, _ = ops.attention_forward(q, k, v, div, mask)
+    grads = ops.attention_backward(q, k, v, p, div, d_o)
+
+    def loss(qq, kk, vv):
+        return float((ops.attention_forward(qq, kk, vv, div, mask)[1] * d_o).sum())
+
+    h = 1e-6
+    for which, g in enumerate(grads):
+        args = [q, k, v]
+        num = np.zeros_like(args[which])
+        for idx in np.ndindex(num.shape):
+            plus = [a.copy() for a in args]
+            minus = [a.copy() for a in args]
+            plus[which][idx] += h
+            minus[which][idx] -= h
+            num[idx] = (loss(*plus) - loss(*minus)) / (2 * h)
+        np.testing.assert_allclose(g, num, rtol=1e-6, atol=1e-8)
+    # the mask zeroes every weight above the diagonal
+    assert not np.triu(p, 1).any()
