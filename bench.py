@@ -170,6 +170,19 @@ def gemm_roofline(profile_path, peak_tflops, peak_source):
         launches += o["calls"]
     if ms == 0:
         return None, prof
+    # fused attention ops (tcgen05 kernels of their own): dense-count FLOPs
+    # per pass, 4 B H T^2 D (scores + values, or dP + dQ) and 2 B H T^2 D
+    # for the key-side product
+    a_flops = a_ms = 0.0
+    a_launches = 0
+    for o in prof:
+        if not o["op"].startswith("attention#"):
+            continue
+        code, dims = o["op"][len("attention#"):].split()
+        b, h, t, d = (int(v) for v in dims.split("x"))
+        a_flops += (2.0 if code == "2" else 4.0) * b * h * t * t * d * o["calls"]
+        a_ms += o["ms"]
+        a_launches += o["calls"]
     achieved = flops / (ms * 1e-3) / 1e12
     return {"bound": "tensor", "kernel": "tc_gemm_kernel (tcgen05 kind::tf32)",
             "achieved": round(achieved, 1), "peak": peak_tflops, "unit": "TFLOP/s",
@@ -177,7 +190,14 @@ def gemm_roofline(profile_path, peak_tflops, peak_source):
             "peak_source": peak_source, "traffic": None,
             "flops_per_step": flops, "gemm_ms_per_step": round(ms, 4),
             "gemm_launches_per_step": launches,
-            "gemm_share_of_step": round(ms / total_ms, 3) if total_ms else None}, prof
+            "gemm_share_of_step": round(ms / total_ms, 3) if total_ms else None,
+            "attention": {"kernel": "attn_fwd / attn_bwd_q / attn_bwd_kv (tcgen05 kind::tf32)",
+                          "flops_per_step": a_flops, "ms_per_step": round(a_ms, 4),
+                          "launches_per_step": a_launches,
+                          "achieved_tflops": round(a_flops / (a_ms * 1e-3) / 1e12, 1)
+                          if a_ms else None,
+                          "frac": round(a_flops / (a_ms * 1e-3) / 1e12 / peak_tflops, 4)
+                          if a_ms and peak_tflops else None}}, prof
 
 
 def measure_tf32_peak(torch):

@@ -390,6 +390,42 @@ int tl_attention_bwd(const float *q, const float *k, const float *v, const float
  * softmax gradient (backward). */
 size_t tl_attention_workspace_size(uint32_t B, uint32_t T, uint32_t H, uint32_t D);
 
+/* Fused passes of the same attention for T <= 192 and D == 64 on operands
+ * with their own strides (the runtime's fused attention ops).  A view is
+ * one [T, D] block per (batch b, head h): element (t, d) of block (b, h) at
+ * p + b * batch_stride + h * head_stride + t * row_stride + d, or, when
+ * `transposed`, at p + b * batch_stride + h * head_stride + d * row_stride
+ * + t (only k may be transposed).  p and ds are dense [B, H, T, T].
+ *   TL_ATTN_FORWARD      q, k, v, divisor, mask (optional) -> p, o
+ *   TL_ATTN_BACKWARD_Q   d_o, v, k, p, divisor -> ds = P * (dP - rowsum(dP
+ *                        * P)) / divisor with dP = dO V^T, dq = ds K
+ *   TL_ATTN_PRODUCT_TN   dk = ds^T q: one [T, T]^T x [T, D] product per
+ *                        block (dK = dS^T Q, dV = P^T dO) */
+enum tl_attn_pass { TL_ATTN_FORWARD = 0, TL_ATTN_BACKWARD_Q = 1, TL_ATTN_PRODUCT_TN = 2 };
+typedef struct tl_attn_view {
+  const float *p;
+  uint64_t batch_stride, head_stride, row_stride; /* elements */
+  int32_t transposed;
+  int32_t reserved;
+} tl_attn_view;
+typedef struct tl_attn_desc {
+  int32_t pass; /* tl_attn_pass */
+  uint32_t B, T, H, D;
+  tl_attn_view q, k, v, o, d_o, dq, dk;
+  const float *divisor, *mask;
+  float *p, *ds;
+  /* forward scratch (>= 16 bytes, optional): a word recording whether the
+   * mask is the causal one (-inf above the diagonal, 0 elsewhere), which
+   * the kernel then applies without reading it and skips the fully masked
+   * key blocks */
+  void *workspace;
+  uint64_t workspace_bytes;
+} tl_attn_desc;
+/* 1 when the fused kernels take this descriptor, 0 when not (no launch). */
+int tl_attention_fused_supported(const tl_attn_desc *d);
+/* TL_ERR_UNSUPPORTED when they do not. */
+int tl_attention_fused(const tl_attn_desc *d, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -18,6 +18,7 @@ TL_MAX_RANK = 8
 TL_GEMM_MAX_GROUPS = 4
 TL_ATTN_BHTD = 0
 TL_ATTN_BTHD = 1
+TL_ATTN_FORWARD, TL_ATTN_BACKWARD_Q, TL_ATTN_PRODUCT_TN = range(3)
 TL_GEMM_GROUP_NONE, TL_GEMM_GROUP_N, TL_GEMM_GROUP_K = 0, 1, 2
 TL_GEMM_MAX_BATCH_RANK = 6
 TL_OPT_CHUNK = 8192
@@ -55,6 +56,19 @@ class TlGemmDesc(Structure):
                 ("a_group", c_void_p * TL_GEMM_MAX_GROUPS), ("b_group", c_void_p * TL_GEMM_MAX_GROUPS),
                 ("c_group", c_void_p * TL_GEMM_MAX_GROUPS),
                 ("bias_group", c_void_p * TL_GEMM_MAX_GROUPS)]
+
+
+class TlAttnView(Structure):
+    _fields_ = [("p", c_void_p), ("batch_stride", c_uint64), ("head_stride", c_uint64),
+                ("row_stride", c_uint64), ("transposed", c_int32), ("reserved", c_int32)]
+
+
+class TlAttnDesc(Structure):
+    _fields_ = [("pass", c_int32), ("B", c_uint32), ("T", c_uint32), ("H", c_uint32),
+                ("D", c_uint32), ("q", TlAttnView), ("k", TlAttnView), ("v", TlAttnView),
+                ("o", TlAttnView), ("d_o", TlAttnView), ("dq", TlAttnView), ("dk", TlAttnView),
+                ("divisor", c_void_p), ("mask", c_void_p), ("p", c_void_p), ("ds", c_void_p),
+                ("workspace", c_void_p), ("workspace_bytes", c_uint64)]
 
 
 class TlgConfig(Structure):
@@ -98,6 +112,8 @@ CUDA_ABI = {
                                  c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_uint32,
                                  c_uint32, c_int32, c_int32, c_void_p, c_size_t, c_void_p]),
     "tl_attention_workspace_size": (c_size_t, [c_uint32, c_uint32, c_uint32, c_uint32]),
+    "tl_attention_fused_supported": (c_int, [c_void_p]),
+    "tl_attention_fused": (c_int, [c_void_p, c_void_p]),
     "tl_graph_capture_begin": (c_int, [c_void_p]),
     "tl_graph_capture_end": (c_int, [c_void_p, POINTER(c_void_p)]),
     "tl_graph_launch": (c_int, [c_void_p, c_void_p]),

@@ -1,5 +1,5 @@
 // Fused tensor-core attention kernels (k_attention_tc.cu) behind
-// tl_attention_fwd / tl_attention_bwd.
+// tl_attention_fwd / tl_attention_bwd and the runtime's fused attention ops.
 #pragma once
 
 #include "tl_common.cuh"
@@ -7,24 +7,41 @@
 namespace tl {
 
 constexpr uint32_t kMaxFusedKeys = 192;  // longest sequence of the fused kernels
+constexpr uint32_t kFusedHeadDim = 64;   // head width of the fused kernels
 
-// Shape and element strides of the head-strided q, k, v, o (and gradients).
-struct FusedAttnShape {
-  uint32_t B, T, H, D;
+// One [T, D] block per (batch, head) of a strided tensor: element (b, h, t, d)
+// at p + b * sb + h * sh + t * ld + d, or, when `trans`, the block is stored
+// transposed ([D, T]: element (t, d) at t + d * ld).
+struct HeadView {
+  const float *p;
   uint64_t sb, sh, ld;
+  bool trans;
 };
 
-// True when the fused kernels take this shape: D == 64, T <= 192, T % 4 == 0,
-// strides and pointers 16-byte aligned.
-bool fused_attention_supported(const FusedAttnShape &sh, const void *const *ptrs, int n);
+struct AttnDims {
+  uint32_t B, T, H;
+};
 
-int launch_attention_fwd_tc(const float *q, const float *k, const float *v, const float *divisor,
-                            const float *mask, float *p, float *o, const FusedAttnShape &sh,
-                            cudaStream_t s);
+// True when the fused kernels take these operands: T <= 192 with T % 4 == 0,
+// 16-byte aligned pointers and strides, and only K stored transposed
+// (`k_may_trans` marks which views may be).
+bool fused_attention_fits(const AttnDims &d, const HeadView *views, const bool *may_trans,
+                          int n);
 
-// dq, dk, dv from the forward's p; ds ([B, H, T, T]) receives dS.
-int launch_attention_bwd_tc(const float *q, const float *k, const float *v, const float *p,
-                            const float *divisor, const float *d_o, float *dq, float *dk,
-                            float *dv, float *ds, const FusedAttnShape &sh, cudaStream_t s);
+// P = softmax(Q K^T / divisor + mask) ([B, H, T, T], dense), O = P V.
+// mask_flag (optional device word): first set to whether the mask is the
+// causal one, which the kernel then applies arithmetically.
+int launch_attention_fwd_tc(const AttnDims &d, const HeadView &q, const HeadView &k,
+                            const HeadView &v, const float *divisor, const float *mask, float *p,
+                            const HeadView &o, uint32_t *mask_flag, cudaStream_t s);
+// dS = P * (dP - rowsum(dP * P)) / divisor with dP = dO V^T (written to ds,
+// dense [B, H, T, T]); dQ = dS K.
+int launch_attention_bwd_q_tc(const AttnDims &d, const HeadView &d_o, const HeadView &v,
+                              const HeadView &k, const float *p, const float *divisor, float *ds,
+                              const HeadView &dq, cudaStream_t s);
+// dK = dS^T Q (when dk.p) and dV = P^T dO (when dv.p), one launch.
+int launch_attention_bwd_kv_tc(const AttnDims &d, const float *ds, const HeadView &q,
+                               const HeadView &dk, const float *p, const HeadView &d_o,
+                               const HeadView &dv, cudaStream_t s);
 
 }  // namespace tl

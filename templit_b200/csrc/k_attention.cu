@@ -102,11 +102,16 @@ int tl_attention_fwd(const float *q, const float *k, const float *v, const float
   if (rc) return rc;
   cudaStream_t s = as_stream(stream);
   const uint64_t hs = hl.sb, hh = hl.sh, ld = hl.ld;
-  if (precision == TL_GEMM_TF32) {
-    const FusedAttnShape shape{B, T, H, D, hs, hh, ld};
-    const void *fp[] = {q, k, v, p, o};
-    if (fused_attention_supported(shape, fp, 5)) {
-      rc = launch_attention_fwd_tc(q, k, v, divisor, mask, p, o, shape, s);
+  if (precision == TL_GEMM_TF32 && D == kFusedHeadDim && aligned16(p) &&
+      (!mask || aligned16(mask))) {
+    const AttnDims dims{B, T, H};
+    auto view = [&](const float *x) { return HeadView{x, hs, hh, ld, false}; };
+    const HeadView views[] = {view(q), view(k), view(v), view(o)};
+    const bool may_trans[] = {false, false, false, false};
+    if (fused_attention_fits(dims, views, may_trans, 4)) {
+      uint32_t *flag = aligned16(workspace) ? static_cast<uint32_t *>(workspace) : nullptr;
+      rc = launch_attention_fwd_tc(dims, views[0], views[1], views[2], divisor, mask, p, views[3],
+                                   flag, s);
       if (rc != TL_ERR_UNSUPPORTED) return rc;
     }
   }
@@ -137,12 +142,17 @@ int tl_attention_bwd(const float *q, const float *k, const float *v, const float
   if (rc) return rc;
   cudaStream_t s = as_stream(stream);
   const uint64_t hs = hl.sb, hh = hl.sh, ld = hl.ld;
-  if (precision == TL_GEMM_TF32) {
-    const FusedAttnShape shape{B, T, H, D, hs, hh, ld};
-    const void *fp[] = {q, k, v, p, d_o, dq, dk, dv, workspace};
-    if (fused_attention_supported(shape, fp, 9)) {
-      rc = launch_attention_bwd_tc(q, k, v, p, divisor, d_o, dq, dk, dv,
-                                   static_cast<float *>(workspace), shape, s);
+  if (precision == TL_GEMM_TF32 && D == kFusedHeadDim && aligned16(p) && aligned16(workspace)) {
+    const AttnDims dims{B, T, H};
+    auto view = [&](const float *x) { return HeadView{x, hs, hh, ld, false}; };
+    const HeadView views[] = {view(q), view(k), view(v), view(d_o), view(dq), view(dk), view(dv)};
+    const bool may_trans[7] = {};
+    if (fused_attention_fits(dims, views, may_trans, 7)) {
+      float *ds = static_cast<float *>(workspace);
+      rc = launch_attention_bwd_q_tc(dims, views[3], views[2], views[1], p, divisor, ds, views[4],
+                                     s);
+      if (rc == TL_OK)
+        rc = launch_attention_bwd_kv_tc(dims, ds, views[0], views[5], p, views[3], views[6], s);
       if (rc != TL_ERR_UNSUPPORTED) return rc;
     }
   }
@@ -167,6 +177,71 @@ int tl_attention_bwd(const float *q, const float *k, const float *v, const float
   if (rc) return rc;
   return product({p, H * ts, ts, T}, true, {d_o, hs, hh, ld}, false, dv, hs, hh, ld, T, D, T, B, H,
                  precision, s);
+}
+
+namespace {
+
+tl::HeadView hv(const tl_attn_view &v) {
+  return tl::HeadView{v.p, v.batch_stride, v.head_stride, v.row_stride, v.transposed != 0};
+}
+
+bool fused_fits(const tl_attn_desc &d) {
+  if (d.D != tl::kFusedHeadDim) return false;
+  const tl::AttnDims dims{d.B, d.T, d.H};
+  switch (d.pass) {
+    case TL_ATTN_FORWARD: {
+      if (!d.divisor || !d.p || !d.q.p || !d.k.p || !d.v.p || !d.o.p || !tl::aligned16(d.p) ||
+          (d.mask && !tl::aligned16(d.mask)))
+        return false;
+      const tl::HeadView v[] = {hv(d.q), hv(d.k), hv(d.v), hv(d.o)};
+      const bool t[] = {false, true, false, false};
+      return tl::fused_attention_fits(dims, v, t, 4);
+    }
+    case TL_ATTN_BACKWARD_Q: {
+      if (!d.divisor || !d.p || !d.ds || !d.d_o.p || !d.v.p || !d.k.p || !d.dq.p ||
+          !tl::aligned16(d.p) || !tl::aligned16(d.ds))
+        return false;
+      const tl::HeadView v[] = {hv(d.d_o), hv(d.v), hv(d.k), hv(d.dq)};
+      const bool t[] = {false, false, true, false};
+      return tl::fused_attention_fits(dims, v, t, 4);
+    }
+    case TL_ATTN_PRODUCT_TN: {
+      if (!d.ds || !d.q.p || !d.dk.p || !tl::aligned16(d.ds)) return false;
+      const tl::HeadView v[] = {hv(d.q), hv(d.dk)};
+      const bool t[] = {false, false};
+      return tl::fused_attention_fits(dims, v, t, 2);
+    }
+    default:
+      return false;
+  }
+}
+
+}  // namespace
+
+int tl_attention_fused_supported(const tl_attn_desc *d) { return d && fused_fits(*d) ? 1 : 0; }
+
+int tl_attention_fused(const tl_attn_desc *d, void *stream) {
+  if (!d) return fail(TL_ERR_INVALID, "tl_attention_fused: null descriptor");
+  if (!fused_fits(*d)) return fail(TL_ERR_UNSUPPORTED, "tl_attention_fused: shape not supported");
+  const tl::AttnDims dims{d->B, d->T, d->H};
+  cudaStream_t s = as_stream(stream);
+  switch (d->pass) {
+    case TL_ATTN_FORWARD: {
+      uint32_t *flag = d->workspace && d->workspace_bytes >= 16 && tl::aligned16(d->workspace)
+                           ? static_cast<uint32_t *>(d->workspace)
+                           : nullptr;
+      return tl::launch_attention_fwd_tc(dims, hv(d->q), hv(d->k), hv(d->v), d->divisor, d->mask,
+                                         d->p, hv(d->o), flag, s);
+    }
+    case TL_ATTN_BACKWARD_Q:
+      return tl::launch_attention_bwd_q_tc(dims, hv(d->d_o), hv(d->v), hv(d->k), d->p,
+                                           d->divisor, d->ds, hv(d->dq), s);
+    default: {
+      const tl::HeadView none{nullptr, 0, 0, 0, false};
+      return tl::launch_attention_bwd_kv_tc(dims, d->ds, hv(d->q), hv(d->dk), nullptr, none,
+                                            none, s);
+    }
+  }
 }
 
 }  // extern "C"

@@ -1,18 +1,30 @@
 // Fused attention on the tensor cores for short sequences (T <= 192) and
 // 64-wide heads: the executor's attention composite (include/nn/
-// multi_head.h:45-52) without its T x T score tensor in HBM.
+// multi_head.h:45-52; softmax derivative include/passes/execute.h:291-308)
+// without its T x T score and score-gradient tensors in HBM.
 //
-// Forward, one CTA per (batch, head, 128 query rows), 320 threads:
-//   warp 0      TMA: the Q tile, all of K (K-major) and V (MN-major)
-//   warp 1      TMEM owner, MMA issuer: S = Q K^T into TMEM (128 x nk fp32),
-//               then O = P V block by block as the softmax hands over P
-//   warps 2..9  softmax, two warps per TMEM lane quadrant on alternate
-//               32-key blocks: pass 1 an online (max, sum) of S / divisor +
-//               mask, merged across the pair through shared memory; pass 2
-//               writes P = exp(x - max) / sum into shared memory in the
-//               MMA's K-major layout (also the TMA box of the P store);
-//               finally O from TMEM to global.
+// Forward, one CTA per (batch, head, 128 query rows), 576 threads:
+//   warp 0       TMA: the Q tile, all of K, all of V
+//   warp 1       TMEM owner, MMA issuer: S = Q K^T into TMEM (128 x nk fp32),
+//                then O = P V block by block as the softmax hands over P
+//   warps 2..17  softmax, four warps per TMEM lane quadrant on interleaved
+//                16-key pieces: the row max of S / divisor + mask, then the
+//                sum of exponentials (both merged across the four warps
+//                through shared memory), then P = exp(x - max) / sum written
+//                into shared memory in the MMA's K-major layout (also the
+//                TMA box of the P store); finally O from TMEM to global.
 // P leaves through TMA stores (the backward reads it); S never leaves TMEM.
+//
+// Backward, query side (same CTA shape): dP = dO V^T into TMEM; the softmax
+// derivative dS = P * (dP - rowsum(dP * P)) / divisor overwrites this tile's
+// P in shared memory and leaves through TMA stores; dQ = dS K.  Key side,
+// one CTA per (batch, head, 128 keys): dK = dS^T Q and dV = P^T dO over
+// 32-query blocks of a TMA ring, all four operands MN-major.
+//
+// Operand layouts follow storage, as in the GEMM: a [T, D] row block is
+// K-major for a product over D and MN-major (TMA 32-byte-atom swizzle) for a
+// product over T; K may also come stored transposed ([D, T], the executor's
+// K^T), which swaps its two roles.
 //
 // Every wait is bounded (2 s): on timeout the CTA raises TL_FLAG_TIMEOUT,
 // lets what it issued finish and returns.
@@ -24,11 +36,123 @@
 namespace tl {
 namespace {
 
-constexpr int kSoftWarps = 8;
+constexpr int kSoftWarps = 16;  // four per TMEM lane quadrant
 constexpr int kThreads = 64 + 32 * kSoftWarps;
 constexpr uint32_t BMQ = 128;  // query rows of a CTA
-constexpr uint32_t HD = 64;    // head width
+constexpr uint32_t HD = kFusedHeadDim;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Element strides of a head-strided output written from registers.
+struct Out {
+  float *p;
+  uint64_t sb, sh, ld;
+};
+
+Out out_of(const HeadView &v) { return Out{const_cast<float *>(v.p), v.sb, v.sh, v.ld}; }
+
+// Shared memory of the query-side kernels (offsets from a 1024-aligned
+// base): a 128-row tile of D = 64 (two 16 KB K-major blocks), two operands
+// of nk rows (48 KB each at most), the P / dS tile (nk / 32 blocks of
+// 128 x 32), barriers.
+constexpr uint32_t kTile = 0;
+constexpr uint32_t kOp1 = kTile + 2 * BMQ * 128;
+constexpr uint32_t kOp2 = kOp1 + 2 * kMaxFusedKeys * 128;
+constexpr uint32_t kScores = kOp2 + 2 * kMaxFusedKeys * 128;
+constexpr uint32_t kBars = kScores + (kMaxFusedKeys / 32) * BMQ * 128;
+constexpr size_t kQuerySmem = 1024 + kBars + 256;
+static_assert(kQuerySmem <= 232448, "query tile exceeds shared memory");
+
+__device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t j) {
+  return r * 128u + ((j ^ (r & 7u)) << 4);
+}
+
+__device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
+  return reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(p) + 1023) &
+                                     ~static_cast<uintptr_t>(1023));
+}
+
+// Row `row` of a 128 x 64 fp32 TMEM accumulator half (32 columns at col0)
+// to out[row] columns col0.. (float4 stores).
+__device__ __forceinline__ void store_row32(uint32_t taddr, const Out &o, int32_t b, int32_t h,
+                                            uint32_t t, uint32_t col0, bool ok) {
+  uint32_t r[32];
+  ptx::tmem_load_32x32b_x32(taddr, r);
+  ptx::tmem_load_wait();
+  if (!ok) return;
+  float4 *dst =
+      reinterpret_cast<float4 *>(o.p + b * o.sb + h * o.sh + static_cast<uint64_t>(t) * o.ld + col0);
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                         __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+}
+
+// 16 columns of row `row` of a TMEM accumulator to out[t] columns col0..
+__device__ __forceinline__ void store_row16(uint32_t taddr, const Out &o, int32_t b, int32_t h,
+                                            uint32_t t, uint32_t col0, bool ok) {
+  uint32_t r[16];
+  ptx::tmem_load_32x32b_x16(taddr, r);
+  ptx::tmem_load_wait();
+  if (!ok) return;
+  float4 *dst =
+      reinterpret_cast<float4 *>(o.p + b * o.sb + h * o.sh + static_cast<uint64_t>(t) * o.ld + col0);
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                         __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+}
+
+// Scores of 16 columns of one row: s / divisor (as s * (1 / divisor)) +
+// mask (a mask row, when given); columns from `lim` on (past T, or past the
+// row under a causal mask) are -inf.
+__device__ __forceinline__ void score16(const uint32_t (&r)[16], float inv, const float *mrow,
+                                        uint32_t col0, uint32_t T, uint32_t lim,
+                                        float (&x)[16]) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    float4 mk = make_float4(0.f, 0.f, 0.f, 0.f);
+    const uint32_t c = col0 + 4 * g;
+    if (mrow && c + 4 <= T) mk = *reinterpret_cast<const float4 *>(mrow + c);
+    const float mv[4] = {mk.x, mk.y, mk.z, mk.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t col = c + i;
+      float v = __uint_as_float(r[4 * g + i]) * inv;
+      if (mrow) v = v + (c + 4 <= T ? mv[i] : (col < T ? mrow[col] : 0.0f));
+      x[4 * g + i] = col < lim ? v : -INFINITY;
+    }
+  }
+}
+
+// Loads of the nk-row operands.  A [T, D] block as a K-major operand of a
+// product over D: two boxes of 32 columns x nk rows.  As an MN-major operand
+// of a product over T: one box of (32 columns, nk rows, 2 chunks).  A
+// transposed ([D, T]) block: nk / 32 boxes of 32 keys x 64 rows, K-major for
+// a product over T (128-byte swizzle) or MN-major for one over D (32-byte
+// atoms).
+__device__ __forceinline__ void load_rows_kmajor(uint8_t *dst, const CUtensorMap *m, uint64_t *bar,
+                                                 uint32_t nk, int32_t h, int32_t b) {
+  for (int kb = 0; kb < 2; ++kb) {
+    const int32_t c[4] = {32 * kb, 0, h, b};
+    ptx::tma_load_rank(dst + kb * nk * 128, m, bar, 4, c);
+  }
+}
+
+__device__ __forceinline__ void load_rows_mnmajor(uint8_t *dst, const CUtensorMap *m,
+                                                  uint64_t *bar, int32_t h, int32_t b) {
+  const int32_t c[5] = {0, 0, 0, h, b};
+  ptx::tma_load_rank(dst, m, bar, 5, c);
+}
+
+__device__ __forceinline__ void load_trans_blocks(uint8_t *dst, const CUtensorMap *m,
+                                                  uint64_t *bar, uint32_t nk, int32_t h,
+                                                  int32_t b) {
+  for (uint32_t c = 0; c < nk / 32; ++c) {
+    const int32_t cc[4] = {static_cast<int32_t>(32 * c), 0, h, b};
+    ptx::tma_load_rank(dst + c * HD * 128, m, bar, 4, cc);
+  }
+}
 
 struct FwdMaps {
   CUtensorMap q, k, v, p;
@@ -37,47 +161,39 @@ struct FwdMaps {
 struct FwdArgs {
   uint32_t T, H, nk, qtiles;
   const float *divisor, *mask;
-  float *o;
-  uint64_t sb, sh, ld;  // element strides of q, k, v, o: batch, head, row
+  const uint32_t *mask_flag;  // nonzero: the mask is the causal one
+  Out o;
   uint32_t *status;
 };
 
-// Shared memory (offsets from a 1024-aligned base): Q 2 x [128 x 32],
-// K 2 x [nk x 32] (K-major, 128-byte swizzle), V 2 x [nk x 32] (MN-major,
-// 32-byte-atom swizzle), P (nk / 32) x [128 x 32] (K-major), barriers.
-constexpr uint32_t kQ = 0;
-constexpr uint32_t kK = kQ + 2 * BMQ * 128;
-constexpr uint32_t kV = kK + 2 * kMaxFusedKeys * 128;
-constexpr uint32_t kP = kV + 2 * kMaxFusedKeys * 128;
-constexpr uint32_t kBars = kP + (kMaxFusedKeys / 32) * BMQ * 128;
-constexpr size_t kFwdSmem = 1024 + kBars + 256;
-static_assert(kFwdSmem <= 232448, "forward tile exceeds shared memory");
-
-__device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t j) {
-  return r * 128u + ((j ^ (r & 7u)) << 4);
-}
-
-__device__ __forceinline__ void online_add(float &m, float &s, float x) {
-  if (x > m) {
-    s = s * expf(m - x) + 1.0f;
-    m = x;
-  } else if (x != -INFINITY) {
-    s += expf(x - m);
+// Whether `mask` ([T, T], T % 4 == 0) is the causal mask of nn::causal_mask
+// (include/nn/attention.h:10-22: -inf above the diagonal, 0 elsewhere).
+__global__ void __launch_bounds__(1024)
+mask_causal_kernel(const float *__restrict__ mask, uint32_t T, uint32_t *flag) {
+  pdl_enter();
+  bool ok = true;
+  const uint32_t n4 = T * T / 4;  // T <= 192
+  for (uint32_t i = threadIdx.x; i < n4; i += blockDim.x) {
+    const float4 m = reinterpret_cast<const float4 *>(mask)[i];
+    const uint32_t r = (4 * i) / T, c = 4 * i - r * T;
+    ok = ok && m.x == (c > r ? -INFINITY : 0.0f) && m.y == (c + 1 > r ? -INFINITY : 0.0f) &&
+         m.z == (c + 2 > r ? -INFINITY : 0.0f) && m.w == (c + 3 > r ? -INFINITY : 0.0f);
   }
+  ok = __syncthreads_and(ok);
+  if (threadIdx.x == 0) *flag = ok ? 1u : 0u;
 }
 
+template <bool KT>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *smem = align1024(smem_raw);
+  uint8_t *s_q = smem + kTile, *s_k = smem + kOp1, *s_v = smem + kOp2, *s_p = smem + kScores;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBars);
   uint64_t *bar_qk = bars, *bar_v = bars + 1, *bar_s = bars + 2, *bar_o = bars + 3;
   uint64_t *bar_p = bars + 4;  // one per 32-key block
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar_p + kMaxFusedKeys / 32);
   volatile uint32_t *abort_flag = tmem_slot + 1;
-  // (max, sum) of each row half, exchanged after pass 1 (Q is dead by then)
-  float2 *red = reinterpret_cast<float2 *>(smem + kQ);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const uint32_t nkb = a.nk / 32;
@@ -87,11 +203,9 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
   const int32_t q0 = static_cast<int32_t>(qt * BMQ);
 
   if (threadIdx.x == 0) {
-    ptx::mbar_init(bar_qk, 1);
-    ptx::mbar_init(bar_v, 1);
-    ptx::mbar_init(bar_s, 1);
-    ptx::mbar_init(bar_o, 1);
-    for (uint32_t c = 0; c < nkb; ++c) ptx::mbar_init(&bar_p[c], 4 * 32);
+    for (int i = 0; i < 4; ++i) ptx::mbar_init(&bars[i], 1);
+    // a 32-key block of P: two 16-column pieces, each from four warps
+    for (uint32_t c = 0; c < nkb; ++c) ptx::mbar_init(&bar_p[c], 2 * 4 * 32);
     *abort_flag = 0;
     ptx::fence_barrier_init();
     ptx::prefetch_tensormap(&maps.q);
@@ -109,6 +223,11 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmem_s = tmem, tmem_o = tmem + 256;
   pdl_enter();
+  // causal mask: applied arithmetically; key blocks past the tile's last
+  // row are all masked (P = 0 there), so S and P V stop at nk_eff
+  const bool causal = a.mask && a.mask_flag && *a.mask_flag != 0;
+  const uint32_t nk_eff =
+      causal ? min(a.nk, (min(a.T, static_cast<uint32_t>(q0) + BMQ) + 31) / 32 * 32) : a.nk;
 
   auto timeout = [&]() {
     *abort_flag = 1;
@@ -117,18 +236,19 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint32_t kbytes = a.nk * 128;
-      ptx::mbar_arrive_expect_tx(bar_qk, 2 * BMQ * 128 + 2 * kbytes);
+      const uint32_t kbytes = a.nk * HD * 4;
+      ptx::mbar_arrive_expect_tx(bar_qk, 2 * BMQ * 128 + kbytes);
       for (int kb = 0; kb < 2; ++kb) {
         const int32_t cq[4] = {32 * kb, q0, hh, bb};
-        ptx::tma_load_rank(smem + kQ + kb * BMQ * 128, &maps.q, bar_qk, 4, cq);
-        const int32_t ck[4] = {32 * kb, 0, hh, bb};
-        ptx::tma_load_rank(smem + kK + kb * kbytes, &maps.k, bar_qk, 4, ck);
+        ptx::tma_load_rank(s_q + kb * BMQ * 128, &maps.q, bar_qk, 4, cq);
       }
-      ptx::mbar_arrive_expect_tx(bar_v, 2 * kbytes);
-      const int32_t cv[5] = {0, 0, 0, hh, bb};
-      ptx::tma_load_rank(smem + kV, &maps.v, bar_v, 5, cv);
-      // the loads must land before the CTA may exit
+      if (KT)
+        load_trans_blocks(s_k, &maps.k, bar_qk, a.nk, hh, bb);
+      else
+        load_rows_kmajor(s_k, &maps.k, bar_qk, a.nk, hh, bb);
+      ptx::mbar_arrive_expect_tx(bar_v, kbytes);
+      load_rows_mnmajor(s_v, &maps.v, bar_v, hh, bb);
+      // the loads land before the CTA may exit
       if (!ptx::mbar_wait_bounded(bar_qk, 0, kWaitLimitNs) ||
           !ptx::mbar_wait_bounded(bar_v, 0, kWaitLimitNs))
         timeout();
@@ -136,26 +256,29 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
   } else if (warp == 1) {
     if (lane == 0) {
       bool issued = false;
-      const uint32_t sq = ptx::smem_addr(smem + kQ), sk = ptx::smem_addr(smem + kK);
-      const uint32_t sv = ptx::smem_addr(smem + kV), sp = ptx::smem_addr(smem + kP);
+      const uint32_t sq = ptx::smem_addr(s_q), sk = ptx::smem_addr(s_k);
+      const uint32_t sv = ptx::smem_addr(s_v), sp = ptx::smem_addr(s_p);
       if (ptx::mbar_wait_bounded(bar_qk, 0, kWaitLimitNs)) {
         ptx::tc_fence_after();
-        const uint32_t idesc_s = ptx::idesc_tf32(BMQ, a.nk, false, false);
+        const uint32_t idesc_s = ptx::idesc_tf32(BMQ, nk_eff, false, KT);
 #pragma unroll
         for (uint32_t kb = 0; kb < 2; ++kb)
 #pragma unroll
-          for (uint32_t kk = 0; kk < 4; ++kk)
+          for (uint32_t kk = 0; kk < 4; ++kk) {
+            const uint64_t bd =
+                KT ? ptx::smem_desc(sk + (kb * 32 + kk * 8) * 128, HD * 128, 512,
+                                    ptx::kSwizzle128B32BAtom)
+                   : ptx::smem_desc(sk + kb * a.nk * 128 + kk * 32, 16, 1024, ptx::kSwizzle128B);
             ptx::mma_tf32(tmem_s,
                           ptx::smem_desc(sq + kb * BMQ * 128 + kk * 32, 16, 1024,
                                          ptx::kSwizzle128B),
-                          ptx::smem_desc(sk + kb * a.nk * 128 + kk * 32, 16, 1024,
-                                         ptx::kSwizzle128B),
-                          idesc_s, (kb | kk) ? 1u : 0u);
+                          bd, idesc_s, (kb | kk) ? 1u : 0u);
+          }
         issued = true;
         ptx::mma_commit(bar_s);
         bool ok = ptx::mbar_wait_bounded(bar_v, 0, kWaitLimitNs);
         const uint32_t idesc_o = ptx::idesc_tf32(BMQ, HD, false, true);
-        for (uint32_t c = 0; c < nkb && ok; ++c) {
+        for (uint32_t c = 0; c < nk_eff / 32 && ok; ++c) {
           if (!ptx::mbar_wait_bounded(&bar_p[c], 0, kWaitLimitNs)) {
             ok = false;
             break;
@@ -179,87 +302,105 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
       if (issued) ptx::mbar_wait_bounded(bar_o, 0, kWaitLimitNs);
     }
   } else {
-    // ------------------------------------------------------------ softmax
+    // Warps 2..17: quadrant q = warp % 4 (the TMEM lanes a warp may read);
+    // the four warps of a quadrant take 16-column pieces quarter, quarter +
+    // 4, ...  Three passes over S: max, sum of exponentials, P.
     const int e = warp - 2;
-    const uint32_t q = warp & 3, half = e >> 2;
+    const uint32_t q = warp & 3, quarter = static_cast<uint32_t>(e) >> 2;
     const uint32_t row = q * 32 + lane;
     const uint32_t grow = qt * BMQ + row;
     const bool row_ok = grow < a.T;
-    const float dv = *a.divisor;
-    const float *mrow = (a.mask && row_ok) ? a.mask + static_cast<size_t>(grow) * a.T : nullptr;
+    const float inv = 1.0f / *a.divisor;
+    const float *mrow =
+        (a.mask && !causal && row_ok) ? a.mask + static_cast<size_t>(grow) * a.T : nullptr;
+    // keys past `lim` are masked: past T, or (causal) past this row
+    const uint32_t lim = causal ? min(a.T, grow + 1) : a.T;
     const uint32_t lane_base = (q * 32u) << 16;
+    const uint32_t npieces = nk_eff / 16;
+    float *red_m = reinterpret_cast<float *>(s_q);  // [4][128], Q is dead by then
+    float *red_s = red_m + 4 * BMQ;
     bool ok = ptx::mbar_wait_bounded(bar_s, 0, kWaitLimitNs);
     if (!__all_sync(0xffffffffu, ok)) {
       if (lane == 0) timeout();
       ok = false;
     }
-    float m = -INFINITY, s = 0.0f;
+    float m = -INFINITY;
     if (ok) {
       ptx::tc_fence_after();
-      for (uint32_t c = half; c < nkb; c += 2) {
-        uint32_t r[32];
-        ptx::tmem_load_32x32b_x32(tmem_s + lane_base + c * 32, r);
+      for (uint32_t c = quarter; c < npieces; c += 4) {
+        uint32_t r[16];
+        ptx::tmem_load_32x32b_x16(tmem_s + lane_base + c * 16, r);
         ptx::tmem_load_wait();
+        float x[16];
+        score16(r, inv, mrow, c * 16, a.T, lim, x);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const uint32_t col = c * 32 + j;
-          if (col < a.T) {
-            float x = __uint_as_float(r[j]) / dv;
-            if (mrow) x = x + mrow[col];
-            online_add(m, s, x);
-          }
-        }
+        for (int j = 0; j < 16; ++j) m = fmaxf(m, x[j]);
       }
-      red[half * BMQ + row] = make_float2(m, s);
+      red_m[quarter * BMQ + row] = m;
+    }
+    ptx::named_bar_sync(1, 32 * kSoftWarps);
+    float sum = 0.0f;
+    if (ok) {
+      m = fmaxf(fmaxf(red_m[row], red_m[BMQ + row]), fmaxf(red_m[2 * BMQ + row], red_m[3 * BMQ + row]));
+      const float ml = m * kLog2e;
+      for (uint32_t c = quarter; c < npieces; c += 4) {
+        uint32_t r[16];
+        ptx::tmem_load_32x32b_x16(tmem_s + lane_base + c * 16, r);
+        ptx::tmem_load_wait();
+        float x[16];
+        score16(r, inv, mrow, c * 16, a.T, lim, x);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) sum += ptx::ex2_approx(fmaf(x[j], kLog2e, -ml));
+      }
+      red_s[quarter * BMQ + row] = sum;
     }
     ptx::named_bar_sync(1, 32 * kSoftWarps);
     if (ok) {
-      const float2 o2 = red[(half ^ 1) * BMQ + row];
-      online_merge(m, s, o2.x, o2.y);
-      for (uint32_t c = half; c < nkb; c += 2) {
-        uint32_t r[32];
-        ptx::tmem_load_32x32b_x32(tmem_s + lane_base + c * 32, r);
-        ptx::tmem_load_wait();
-        uint8_t *blk = smem + kP + c * BMQ * 128;
+      // every warp adds the four partial sums in the same order
+      sum = ((red_s[row] + red_s[BMQ + row]) + red_s[2 * BMQ + row]) + red_s[3 * BMQ + row];
+      const float inv_sum = 1.0f / sum;
+      const float ml = m * kLog2e;
+      // every piece of P: those past nk_eff are zeros (stored, not multiplied)
+      for (uint32_t c = quarter; c < a.nk / 16; c += 4) {
+        uint8_t *blk = s_p + (c >> 1) * BMQ * 128;
+        if (c < npieces) {
+          uint32_t r[16];
+          ptx::tmem_load_32x32b_x16(tmem_s + lane_base + c * 16, r);
+          ptx::tmem_load_wait();
+          float x[16];
+          score16(r, inv, mrow, c * 16, a.T, lim, x);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float p4[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint32_t col = c * 32 + 4 * j + i;
-            float x = __uint_as_float(r[4 * j + i]) / dv;
-            if (mrow && col < a.T) x = x + mrow[col];
-            p4[i] = col < a.T ? expf(x - m) / s : 0.0f;
+          for (int g = 0; g < 4; ++g) {
+            float4 v;
+            v.x = ptx::ex2_approx(fmaf(x[4 * g], kLog2e, -ml)) * inv_sum;
+            v.y = ptx::ex2_approx(fmaf(x[4 * g + 1], kLog2e, -ml)) * inv_sum;
+            v.z = ptx::ex2_approx(fmaf(x[4 * g + 2], kLog2e, -ml)) * inv_sum;
+            v.w = ptx::ex2_approx(fmaf(x[4 * g + 3], kLog2e, -ml)) * inv_sum;
+            *reinterpret_cast<float4 *>(blk + swz(row, (c & 1) * 4 + g)) = v;
           }
-          *reinterpret_cast<float4 *>(blk + swz(row, j)) = make_float4(p4[0], p4[1], p4[2], p4[3]);
+        } else {
+#pragma unroll
+          for (int g = 0; g < 4; ++g)
+            *reinterpret_cast<float4 *>(blk + swz(row, (c & 1) * 4 + g)) =
+                make_float4(0.f, 0.f, 0.f, 0.f);
         }
         ptx::fence_proxy_async_smem();
-        ptx::mbar_arrive(&bar_p[c]);
+        ptx::mbar_arrive(&bar_p[c >> 1]);
       }
     }
     // P to global: every block is complete once all softmax warps are here
     ptx::named_bar_sync(1, 32 * kSoftWarps);
     if (ok && e == 0 && lane == 0) {
-      for (uint32_t c = 0; c < nkb; ++c)
-        ptx::tma_store_3d(&maps.p, smem + kP + c * BMQ * 128, static_cast<int32_t>(c * 32), q0,
+      for (uint32_t c = 0; c < a.nk / 32; ++c)
+        ptx::tma_store_3d(&maps.p, s_p + c * BMQ * 128, static_cast<int32_t>(c * 32), q0,
                           static_cast<int32_t>(bh));
       ptx::bulk_commit_group();
     }
-    // O = P V: TMEM -> global, each warp of a pair 32 of the 64 columns
+    // O: TMEM -> global, each warp of a quadrant 16 of the 64 columns
     ok = ok && ptx::mbar_wait_bounded(bar_o, 0, kWaitLimitNs);
     if (__all_sync(0xffffffffu, ok) && !*abort_flag) {
       ptx::tc_fence_after();
-      uint32_t r[32];
-      ptx::tmem_load_32x32b_x32(tmem_o + lane_base + half * 32, r);
-      ptx::tmem_load_wait();
-      if (row_ok) {
-        float4 *dst = reinterpret_cast<float4 *>(a.o + bb * a.sb + hh * a.sh +
-                                                 static_cast<uint64_t>(grow) * a.ld + half * 32);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                               __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-      }
+      store_row16(tmem_o + lane_base + quarter * 16, a.o, bb, hh, grow, quarter * 16, row_ok);
     } else if (lane == 0 && !ok) {
       timeout();
     }
@@ -272,16 +413,7 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
   if (warp == 1) ptx::tmem_dealloc(tmem, 512);
 }
 
-// ------------------------------------------------------------------ backward
-// Query side, one CTA per (batch, head, 128 query rows), 320 threads:
-//   warp 0      TMA: dO and V (K-major), this tile's rows of P (K-major,
-//               as the forward stored them), K (MN-major)
-//   warp 1      dP = dO V^T into TMEM, then dQ = dS K block by block
-//   warps 2..9  softmax derivative (include/passes/execute.h:291-308):
-//               pass 1 rowsum(dP * P), merged across the warp pair; pass 2
-//               dS = P * (dP - rowsum) / divisor written over P in shared
-//               memory (the dQ MMA's A operand and the TMA box of the dS
-//               store); then dQ from TMEM to global.
+// ------------------------------------------------------ backward, query side
 struct BwdQMaps {
   CUtensorMap d_o, v, k, p, ds;
 };
@@ -289,27 +421,25 @@ struct BwdQMaps {
 struct BwdQArgs {
   uint32_t T, H, nk, qtiles;
   const float *divisor;
-  float *dq;
-  uint64_t sb, sh, ld;
+  Out dq;
   uint32_t *status;
 };
 
+template <bool KT>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  // same footprint as the forward: dO in Q's place, V in K's, K in V's,
-  // P / dS in P's
-  uint8_t *s_do = smem + kQ, *s_v = smem + kK, *s_k = smem + kV, *s_p = smem + kP;
+  uint8_t *smem = align1024(smem_raw);
+  uint8_t *s_do = smem + kTile, *s_v = smem + kOp1, *s_k = smem + kOp2, *s_p = smem + kScores;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBars);
   uint64_t *bar_a = bars, *bar_k = bars + 1, *bar_pl = bars + 2, *bar_dp = bars + 3,
            *bar_dq = bars + 4;
   uint64_t *bar_ds = bars + 5;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar_ds + kMaxFusedKeys / 32);
   volatile uint32_t *abort_flag = tmem_slot + 1;
-  // row sums of each half, exchanged after pass 1 (dO is dead by then)
-  float2 *red_sm = reinterpret_cast<float2 *>(s_do);
+  // partial row sums of the four warps of a quadrant ([4][128]), exchanged
+  // after pass 1 (dO is dead by then)
+  float *red = reinterpret_cast<float *>(s_do);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const uint32_t nkb = a.nk / 32;
@@ -320,7 +450,7 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 5; ++i) ptx::mbar_init(&bars[i], 1);
-    for (uint32_t c = 0; c < nkb; ++c) ptx::mbar_init(&bar_ds[c], 4 * 32);
+    for (uint32_t c = 0; c < nkb; ++c) ptx::mbar_init(&bar_ds[c], 2 * 4 * 32);
     *abort_flag = 0;
     ptx::fence_barrier_init();
     ptx::prefetch_tensormap(&maps.d_o);
@@ -347,21 +477,22 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint32_t kbytes = a.nk * 128;
-      ptx::mbar_arrive_expect_tx(bar_a, 2 * BMQ * 128 + 2 * kbytes);
+      const uint32_t kbytes = a.nk * HD * 4;
+      ptx::mbar_arrive_expect_tx(bar_a, 2 * BMQ * 128 + kbytes);
       for (int kb = 0; kb < 2; ++kb) {
         const int32_t cd[4] = {32 * kb, q0, hh, bb};
         ptx::tma_load_rank(s_do + kb * BMQ * 128, &maps.d_o, bar_a, 4, cd);
-        const int32_t cv[4] = {32 * kb, 0, hh, bb};
-        ptx::tma_load_rank(s_v + kb * kbytes, &maps.v, bar_a, 4, cv);
       }
+      load_rows_kmajor(s_v, &maps.v, bar_a, a.nk, hh, bb);
       ptx::mbar_arrive_expect_tx(bar_pl, nkb * BMQ * 128);
       for (uint32_t c = 0; c < nkb; ++c)
         ptx::tma_load_3d(s_p + c * BMQ * 128, &maps.p, bar_pl, static_cast<int32_t>(c * 32), q0,
                          static_cast<int32_t>(bh));
-      ptx::mbar_arrive_expect_tx(bar_k, 2 * kbytes);
-      const int32_t ck[5] = {0, 0, 0, hh, bb};
-      ptx::tma_load_rank(s_k, &maps.k, bar_k, 5, ck);
+      ptx::mbar_arrive_expect_tx(bar_k, kbytes);
+      if (KT)
+        load_trans_blocks(s_k, &maps.k, bar_k, a.nk, hh, bb);
+      else
+        load_rows_mnmajor(s_k, &maps.k, bar_k, hh, bb);
       if (!ptx::mbar_wait_bounded(bar_a, 0, kWaitLimitNs) ||
           !ptx::mbar_wait_bounded(bar_pl, 0, kWaitLimitNs) ||
           !ptx::mbar_wait_bounded(bar_k, 0, kWaitLimitNs))
@@ -388,7 +519,7 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
         issued = true;
         ptx::mma_commit(bar_dp);
         bool ok = ptx::mbar_wait_bounded(bar_k, 0, kWaitLimitNs);
-        const uint32_t idesc_q = ptx::idesc_tf32(BMQ, HD, false, true);
+        const uint32_t idesc_q = ptx::idesc_tf32(BMQ, HD, false, !KT);
         for (uint32_t c = 0; c < nkb && ok; ++c) {
           if (!ptx::mbar_wait_bounded(&bar_ds[c], 0, kWaitLimitNs)) {
             ok = false;
@@ -396,13 +527,16 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
           }
           ptx::tc_fence_after();
 #pragma unroll
-          for (uint32_t kk = 0; kk < 4; ++kk)
+          for (uint32_t kk = 0; kk < 4; ++kk) {
+            const uint64_t bd =
+                KT ? ptx::smem_desc(sk + c * HD * 128 + kk * 32, 16, 1024, ptx::kSwizzle128B)
+                   : ptx::smem_desc(sk + (c * 32 + kk * 8) * 128, a.nk * 128, 512,
+                                    ptx::kSwizzle128B32BAtom);
             ptx::mma_tf32(tmem_dq,
                           ptx::smem_desc(sp + c * BMQ * 128 + kk * 32, 16, 1024,
                                          ptx::kSwizzle128B),
-                          ptx::smem_desc(sk + (c * 32 + kk * 8) * 128, a.nk * 128, 512,
-                                         ptx::kSwizzle128B32BAtom),
-                          idesc_q, (c | kk) ? 1u : 0u);
+                          bd, idesc_q, (c | kk) ? 1u : 0u);
+          }
         }
         if (!ok) timeout();
         ptx::mma_commit(bar_dq);
@@ -413,11 +547,12 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
     }
   } else {
     const int e = warp - 2;
-    const uint32_t q = warp & 3, half = e >> 2;
+    const uint32_t q = warp & 3, quarter = static_cast<uint32_t>(e) >> 2;
     const uint32_t row = q * 32 + lane;
     const uint32_t grow = qt * BMQ + row;
-    const float dv = *a.divisor;
+    const float inv = 1.0f / *a.divisor;
     const uint32_t lane_base = (q * 32u) << 16;
+    const uint32_t npieces = a.nk / 16;
     bool ok = ptx::mbar_wait_bounded(bar_dp, 0, kWaitLimitNs) &&
               ptx::mbar_wait_bounded(bar_pl, 0, kWaitLimitNs);
     if (!__all_sync(0xffffffffu, ok)) {
@@ -427,48 +562,47 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
     float sum = 0.0f;
     if (ok) {
       ptx::tc_fence_after();
-      for (uint32_t c = half; c < nkb; c += 2) {
-        uint32_t r[32];
-        ptx::tmem_load_32x32b_x32(tmem_dp + lane_base + c * 32, r);
+      for (uint32_t c = quarter; c < npieces; c += 4) {
+        uint32_t r[16];
+        ptx::tmem_load_32x32b_x16(tmem_dp + lane_base + c * 16, r);
         ptx::tmem_load_wait();
-        const uint8_t *blk = s_p + c * BMQ * 128;
+        const uint8_t *blk = s_p + (c >> 1) * BMQ * 128;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 p4 = *reinterpret_cast<const float4 *>(blk + swz(row, j));
-          sum += __uint_as_float(r[4 * j]) * p4.x;
-          sum += __uint_as_float(r[4 * j + 1]) * p4.y;
-          sum += __uint_as_float(r[4 * j + 2]) * p4.z;
-          sum += __uint_as_float(r[4 * j + 3]) * p4.w;
+        for (int g = 0; g < 4; ++g) {
+          const float4 p4 = *reinterpret_cast<const float4 *>(blk + swz(row, (c & 1) * 4 + g));
+          sum = fmaf(__uint_as_float(r[4 * g]), p4.x, sum);
+          sum = fmaf(__uint_as_float(r[4 * g + 1]), p4.y, sum);
+          sum = fmaf(__uint_as_float(r[4 * g + 2]), p4.z, sum);
+          sum = fmaf(__uint_as_float(r[4 * g + 3]), p4.w, sum);
         }
       }
-      red_sm[half * BMQ + row] = make_float2(sum, 0.0f);
+      red[quarter * BMQ + row] = sum;
     }
     ptx::named_bar_sync(1, 32 * kSoftWarps);
     if (ok) {
-      // both halves add in the same order: low columns first
-      const float lo = red_sm[row].x, hi = red_sm[BMQ + row].x;
-      sum = lo + hi;
-      for (uint32_t c = half; c < nkb; c += 2) {
-        uint32_t r[32];
-        ptx::tmem_load_32x32b_x32(tmem_dp + lane_base + c * 32, r);
+      // every warp adds the four partial sums in the same order
+      sum = ((red[row] + red[BMQ + row]) + red[2 * BMQ + row]) + red[3 * BMQ + row];
+      for (uint32_t c = quarter; c < npieces; c += 4) {
+        uint32_t r[16];
+        ptx::tmem_load_32x32b_x16(tmem_dp + lane_base + c * 16, r);
         ptx::tmem_load_wait();
-        uint8_t *blk = s_p + c * BMQ * 128;
+        uint8_t *blk = s_p + (c >> 1) * BMQ * 128;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float4 *slot = reinterpret_cast<float4 *>(blk + swz(row, j));
+        for (int g = 0; g < 4; ++g) {
+          float4 *slot = reinterpret_cast<float4 *>(blk + swz(row, (c & 1) * 4 + g));
           const float4 p4 = *slot;
-          *slot = make_float4(p4.x * (__uint_as_float(r[4 * j]) - sum) / dv,
-                              p4.y * (__uint_as_float(r[4 * j + 1]) - sum) / dv,
-                              p4.z * (__uint_as_float(r[4 * j + 2]) - sum) / dv,
-                              p4.w * (__uint_as_float(r[4 * j + 3]) - sum) / dv);
+          *slot = make_float4(p4.x * (__uint_as_float(r[4 * g]) - sum) * inv,
+                              p4.y * (__uint_as_float(r[4 * g + 1]) - sum) * inv,
+                              p4.z * (__uint_as_float(r[4 * g + 2]) - sum) * inv,
+                              p4.w * (__uint_as_float(r[4 * g + 3]) - sum) * inv);
         }
         ptx::fence_proxy_async_smem();
-        ptx::mbar_arrive(&bar_ds[c]);
+        ptx::mbar_arrive(&bar_ds[c >> 1]);
       }
     }
     ptx::named_bar_sync(1, 32 * kSoftWarps);
     if (ok && e == 0 && lane == 0) {
-      for (uint32_t c = 0; c < nkb; ++c)
+      for (uint32_t c = 0; c < a.nk / 32; ++c)
         ptx::tma_store_3d(&maps.ds, s_p + c * BMQ * 128, static_cast<int32_t>(c * 32), q0,
                           static_cast<int32_t>(bh));
       ptx::bulk_commit_group();
@@ -476,17 +610,8 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
     ok = ok && ptx::mbar_wait_bounded(bar_dq, 0, kWaitLimitNs);
     if (__all_sync(0xffffffffu, ok) && !*abort_flag) {
       ptx::tc_fence_after();
-      uint32_t r[32];
-      ptx::tmem_load_32x32b_x32(tmem_dq + lane_base + half * 32, r);
-      ptx::tmem_load_wait();
-      if (grow < a.T) {
-        float4 *dst = reinterpret_cast<float4 *>(a.dq + bb * a.sb + hh * a.sh +
-                                                 static_cast<uint64_t>(grow) * a.ld + half * 32);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                               __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-      }
+      store_row16(tmem_dq + lane_base + quarter * 16, a.dq, bb, hh, grow, quarter * 16,
+                  grow < a.T);
     } else if (lane == 0 && !ok) {
       timeout();
     }
@@ -499,17 +624,13 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
   if (warp == 1) ptx::tmem_dealloc(tmem, 512);
 }
 
-// Key side, one CTA per (batch, head, 128 keys), 192 threads:
-//   warp 0      TMA ring over 32-query blocks: dS^T and P^T (MN-major, from
-//               the [T, T] matrices), Q and dO (MN-major)
-//   warp 1      dK += dS^T Q and dV += P^T dO into TMEM (64 columns each)
-//   warps 2..5  dK, dV from TMEM to global
+// -------------------------------------------------------- backward, key side
 constexpr int kKvThreads = 64 + 128;
 constexpr int kKvStages = 4;
 constexpr uint32_t kKvA = 128 * 32 * 4;  // 128 keys x 32 queries
 constexpr uint32_t kKvB = 32 * HD * 4;   // 32 queries x 64
-constexpr uint32_t kKvStage = 2 * kKvA + 2 * kKvB;
-constexpr size_t kKvSmem = 1024 + kKvStages * kKvStage + 256;
+constexpr uint32_t kKvPart = kKvA + kKvB;  // one product's share of a stage
+constexpr size_t kv_smem(uint32_t products) { return 1024 + kKvStages * products * kKvPart + 256; }
 
 struct BwdKvMaps {
   CUtensorMap ds, p, q, d_o;
@@ -517,17 +638,17 @@ struct BwdKvMaps {
 
 struct BwdKvArgs {
   uint32_t T, H, ktiles, qblocks;
-  float *dk, *dv;
-  uint64_t sb, sh, ld;
+  bool with_dk, with_dv;
+  uint32_t stage_bytes, dv_off;  // products x kKvPart; dV's part in a stage
+  Out dk, dv;
   uint32_t *status;
 };
 
-__global__ void __launch_bounds__(kKvThreads, 1)
+__global__ void __launch_bounds__(kKvThreads, 2)
 attn_bwd_kv_kernel(const __grid_constant__ BwdKvMaps maps, const BwdKvArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kKvStages * kKvStage);
+  uint8_t *smem = align1024(smem_raw);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kKvStages * a.stage_bytes);
   uint64_t *empty = full + kKvStages;
   uint64_t *done = empty + kKvStages;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
@@ -547,10 +668,14 @@ attn_bwd_kv_kernel(const __grid_constant__ BwdKvMaps maps, const BwdKvArgs a) {
     ptx::mbar_init(done, 1);
     *abort_flag = 0;
     ptx::fence_barrier_init();
-    ptx::prefetch_tensormap(&maps.ds);
-    ptx::prefetch_tensormap(&maps.p);
-    ptx::prefetch_tensormap(&maps.q);
-    ptx::prefetch_tensormap(&maps.d_o);
+    if (a.with_dk) {
+      ptx::prefetch_tensormap(&maps.ds);
+      ptx::prefetch_tensormap(&maps.q);
+    }
+    if (a.with_dv) {
+      ptx::prefetch_tensormap(&maps.p);
+      ptx::prefetch_tensormap(&maps.d_o);
+    }
   }
   if (warp == 1) {
     ptx::tmem_alloc(tmem_slot, 128);
@@ -569,27 +694,29 @@ attn_bwd_kv_kernel(const __grid_constant__ BwdKvMaps maps, const BwdKvArgs a) {
 
   if (warp == 0) {
     if (lane == 0) {
+      const uint32_t bytes = a.stage_bytes;
       uint32_t stage = 0, phase = 0, issued = 0;
       for (uint32_t qb = 0; qb < a.qblocks; ++qb) {
         if (!ptx::mbar_wait_bounded(&empty[stage], phase ^ 1, kWaitLimitNs)) {
           timeout();
           break;
         }
-        uint8_t *st = smem + stage * kKvStage;
-        ptx::mbar_arrive_expect_tx(&full[stage], kKvStage);
+        uint8_t *st = smem + stage * a.stage_bytes;
+        ptx::mbar_arrive_expect_tx(&full[stage], bytes);
         const int32_t y = static_cast<int32_t>(qb * 32);
-#pragma unroll
         for (int j = 0; j < 4; ++j) {
-          ptx::tma_load_3d(st + j * 4096, &maps.ds, &full[stage], k0 + 32 * j, y,
-                           static_cast<int32_t>(bh));
-          ptx::tma_load_3d(st + kKvA + j * 4096, &maps.p, &full[stage], k0 + 32 * j, y,
-                           static_cast<int32_t>(bh));
+          if (a.with_dk)
+            ptx::tma_load_3d(st + j * 4096, &maps.ds, &full[stage], k0 + 32 * j, y,
+                             static_cast<int32_t>(bh));
+          if (a.with_dv)
+            ptx::tma_load_3d(st + a.dv_off + j * 4096, &maps.p, &full[stage], k0 + 32 * j, y,
+                             static_cast<int32_t>(bh));
         }
-#pragma unroll
         for (int j = 0; j < 2; ++j) {
           const int32_t c[4] = {32 * j, y, hh, bb};
-          ptx::tma_load_rank(st + 2 * kKvA + j * 4096, &maps.q, &full[stage], 4, c);
-          ptx::tma_load_rank(st + 2 * kKvA + kKvB + j * 4096, &maps.d_o, &full[stage], 4, c);
+          if (a.with_dk) ptx::tma_load_rank(st + kKvA + j * 4096, &maps.q, &full[stage], 4, c);
+          if (a.with_dv)
+            ptx::tma_load_rank(st + a.dv_off + kKvA + j * 4096, &maps.d_o, &full[stage], 4, c);
         }
         ++issued;
         if (++stage == kKvStages) {
@@ -598,7 +725,7 @@ attn_bwd_kv_kernel(const __grid_constant__ BwdKvMaps maps, const BwdKvArgs a) {
         }
       }
       // every issued stage has landed before the CTA may exit
-      uint32_t back = issued < kKvStages ? issued : kKvStages;
+      const uint32_t back = issued < kKvStages ? issued : kKvStages;
       uint32_t s = stage, p = phase;
       for (uint32_t i = 0; i < back; ++i) {
         if (s == 0) {
@@ -624,21 +751,23 @@ attn_bwd_kv_kernel(const __grid_constant__ BwdKvMaps maps, const BwdKvArgs a) {
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t st = ptx::smem_addr(smem + stage * kKvStage);
+        const uint32_t st = ptx::smem_addr(smem + stage * a.stage_bytes);
 #pragma unroll
         for (uint32_t kk = 0; kk < 4; ++kk) {
           const uint32_t acc = (qb | kk) ? 1u : 0u;
-          ptx::mma_tf32(tmem,
-                        ptx::smem_desc(st + kk * 1024, 4096, 512, ptx::kSwizzle128B32BAtom),
-                        ptx::smem_desc(st + 2 * kKvA + kk * 1024, 4096, 512,
-                                       ptx::kSwizzle128B32BAtom),
-                        idesc, acc);
-          ptx::mma_tf32(tmem + HD,
-                        ptx::smem_desc(st + kKvA + kk * 1024, 4096, 512,
-                                       ptx::kSwizzle128B32BAtom),
-                        ptx::smem_desc(st + 2 * kKvA + kKvB + kk * 1024, 4096, 512,
-                                       ptx::kSwizzle128B32BAtom),
-                        idesc, acc);
+          if (a.with_dk)
+            ptx::mma_tf32(tmem,
+                          ptx::smem_desc(st + kk * 1024, 4096, 512, ptx::kSwizzle128B32BAtom),
+                          ptx::smem_desc(st + kKvA + kk * 1024, 4096, 512,
+                                         ptx::kSwizzle128B32BAtom),
+                          idesc, acc);
+          if (a.with_dv)
+            ptx::mma_tf32(tmem + HD,
+                          ptx::smem_desc(st + a.dv_off + kk * 1024, 4096, 512,
+                                         ptx::kSwizzle128B32BAtom),
+                          ptx::smem_desc(st + a.dv_off + kKvA + kk * 1024, 4096, 512,
+                                         ptx::kSwizzle128B32BAtom),
+                          idesc, acc);
         }
         issued = true;
         ptx::mma_commit(&empty[stage]);
@@ -651,7 +780,7 @@ attn_bwd_kv_kernel(const __grid_constant__ BwdKvMaps maps, const BwdKvArgs a) {
         ptx::mma_commit(done);
         if (!ptx::mbar_wait_bounded(done, 0, kWaitLimitNs)) timeout();
       } else {
-        ptx::mbar_arrive(done);  // nothing to wait for: release the epilogue
+        ptx::mbar_arrive(done);  // nothing issued: release the epilogue
       }
     }
   } else {
@@ -661,21 +790,12 @@ attn_bwd_kv_kernel(const __grid_constant__ BwdKvMaps maps, const BwdKvArgs a) {
     if (__all_sync(0xffffffffu, ok) && !*abort_flag) {
       ptx::tc_fence_after();
       const uint32_t lane_base = (q * 32u) << 16;
-      const uint64_t off = bb * a.sb + hh * a.sh + static_cast<uint64_t>(key) * a.ld;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        ptx::tmem_load_32x32b_x32(tmem + lane_base + c * 32, r);
-        ptx::tmem_load_wait();
-        if (key < a.T) {
-          float *base = (c < 2 ? a.dk : a.dv) + off + (c & 1) * 32;
-          float4 *dst = reinterpret_cast<float4 *>(base);
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-        }
-      }
+      if (a.with_dk)
+        for (uint32_t c = 0; c < 2; ++c)
+          store_row32(tmem + lane_base + c * 32, a.dk, bb, hh, key, c * 32, key < a.T);
+      if (a.with_dv)
+        for (uint32_t c = 0; c < 2; ++c)
+          store_row32(tmem + lane_base + HD + c * 32, a.dv, bb, hh, key, c * 32, key < a.T);
     } else if (lane == 0 && !ok) {
       timeout();
     }
@@ -687,6 +807,7 @@ attn_bwd_kv_kernel(const __grid_constant__ BwdKvMaps maps, const BwdKvArgs a) {
   if (warp == 1) ptx::tmem_dealloc(tmem, 128);
 }
 
+// ---------------------------------------------------------------- host side
 bool encode(CUtensorMap *map, const float *base, int rank, const cuuint64_t *dims,
             const cuuint64_t *strides_bytes, const cuuint32_t *box, CUtensorMapSwizzle swz) {
   EncodeTiledFn enc = tensor_map_encoder();
@@ -698,40 +819,40 @@ bool encode(CUtensorMap *map, const float *base, int rank, const cuuint64_t *dim
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// [D, T, H, B] view of a head-strided operand, box 32 x rows.
-bool head_map(CUtensorMap *map, const float *base, const FusedAttnShape &sh, uint32_t rows) {
-  const cuuint64_t dims[4] = {HD, sh.T, sh.H, sh.B};
-  const cuuint64_t st[3] = {sh.ld * 4, sh.sh * 4, sh.sb * 4};
+// A [T, D] head block as [D, T, H, B], box 32 columns x `rows`.
+bool rows_map(CUtensorMap *map, const HeadView &v, const AttnDims &d, uint32_t rows,
+              CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+  const cuuint64_t dims[4] = {HD, d.T, d.H, d.B};
+  const cuuint64_t st[3] = {v.ld * 4, v.sh * 4, v.sb * 4};
   const cuuint32_t box[4] = {32, rows, 1, 1};
-  return encode(map, base, 4, dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  return encode(map, v.p, 4, dims, st, box, swz);
 }
 
-// [32, T, D / 32, H, B] view (the MN-major operand layout: 32-wide column
-// chunks of rows), box 32 x rows x D / 32.
-bool head_map_mn(CUtensorMap *map, const float *base, const FusedAttnShape &sh, uint32_t rows) {
-  const cuuint64_t dims[5] = {32, sh.T, HD / 32, sh.H, sh.B};
-  const cuuint64_t st[4] = {sh.ld * 4, 128, sh.sh * 4, sh.sb * 4};
+// A [T, D] head block as [32, T, D / 32, H, B] (32-wide column chunks of
+// rows, the MN-major operand layout), box 32 x rows x D / 32.
+bool rows_map_mn(CUtensorMap *map, const HeadView &v, const AttnDims &d, uint32_t rows) {
+  const cuuint64_t dims[5] = {32, d.T, HD / 32, d.H, d.B};
+  const cuuint64_t st[4] = {v.ld * 4, 128, v.sh * 4, v.sb * 4};
   const cuuint32_t box[5] = {32, rows, HD / 32, 1, 1};
-  return encode(map, base, 5, dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+  return encode(map, v.p, 5, dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
 }
 
-// [T, T, B * H] view of P (or dS), box 32 x rows: K-major rows of 128
-// queries, or (32-byte-atom swizzle) MN-major 32 x 32 blocks.
-bool scores_map(CUtensorMap *map, const float *base, const FusedAttnShape &sh,
-                uint32_t rows = BMQ, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
-  const cuuint64_t dims[3] = {sh.T, sh.T, static_cast<cuuint64_t>(sh.B) * sh.H};
-  const cuuint64_t st[2] = {static_cast<cuuint64_t>(sh.T) * 4,
-                            static_cast<cuuint64_t>(sh.T) * sh.T * 4};
+// A transposed [D, T] head block as [T, D, H, B], box 32 keys x D rows.
+bool trans_map(CUtensorMap *map, const HeadView &v, const AttnDims &d, CUtensorMapSwizzle swz) {
+  const cuuint64_t dims[4] = {d.T, HD, d.H, d.B};
+  const cuuint64_t st[3] = {v.ld * 4, v.sh * 4, v.sb * 4};
+  const cuuint32_t box[4] = {32, HD, 1, 1};
+  return encode(map, v.p, 4, dims, st, box, swz);
+}
+
+// Dense [B, H, T, T] scores as [T, T, B * H], box 32 x rows.
+bool scores_map(CUtensorMap *map, const float *base, const AttnDims &d, uint32_t rows,
+                CUtensorMapSwizzle swz) {
+  const cuuint64_t dims[3] = {d.T, d.T, static_cast<cuuint64_t>(d.B) * d.H};
+  const cuuint64_t st[2] = {static_cast<cuuint64_t>(d.T) * 4,
+                            static_cast<cuuint64_t>(d.T) * d.T * 4};
   const cuuint32_t box[3] = {32, rows, 1};
   return encode(map, base, 3, dims, st, box, swz);
-}
-
-// [D, T, H, B] view with 32 x 32 boxes in the MN-major layout.
-bool head_map_mn32(CUtensorMap *map, const float *base, const FusedAttnShape &sh) {
-  const cuuint64_t dims[4] = {HD, sh.T, sh.H, sh.B};
-  const cuuint64_t st[3] = {sh.ld * 4, sh.sh * 4, sh.sb * 4};
-  const cuuint32_t box[4] = {32, 32, 1, 1};
-  return encode(map, base, 4, dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
 }
 
 template <typename K>
@@ -744,95 +865,129 @@ int set_smem(K kernel, size_t bytes, bool &done, const char *what) {
   return rc;
 }
 
+uint32_t keys_of(const AttnDims &d) { return (d.T + 31) / 32 * 32; }
+
 }  // namespace
 
-bool fused_attention_supported(const FusedAttnShape &sh, const void *const *ptrs, int n) {
-  if (sh.D != HD || sh.T == 0 || sh.T > kMaxFusedKeys || sh.T % 4 != 0) return false;
-  if (sh.ld % 4 || sh.sh % 4 || sh.sb % 4) return false;
-  if (static_cast<uint64_t>(sh.B) * sh.H * ((sh.T + BMQ - 1) / BMQ) > 0x7fffffffu) return false;
-  for (int i = 0; i < n; ++i)
-    if (ptrs[i] && !aligned16(ptrs[i])) return false;
-  return tensor_map_encoder() != nullptr;
+bool fused_attention_fits(const AttnDims &d, const HeadView *views, const bool *may_trans,
+                          int n) {
+  if (d.T == 0 || d.T > kMaxFusedKeys || d.T % 4 != 0 || d.B == 0 || d.H == 0) return false;
+  if (static_cast<uint64_t>(d.B) * d.H * ((d.T + BMQ - 1) / BMQ) > 0x7fffffffu) return false;
+  for (int i = 0; i < n; ++i) {
+    const HeadView &v = views[i];
+    if (!v.p) continue;
+    if (!aligned16(v.p) || v.ld % 4 || v.sh % 4 || v.sb % 4) return false;
+    if (v.trans && !may_trans[i]) return false;
+  }
+  return true;
 }
 
-int launch_attention_fwd_tc(const float *q, const float *k, const float *v, const float *divisor,
-                            const float *mask, float *p, float *o, const FusedAttnShape &sh,
-                            cudaStream_t s) {
+int launch_attention_fwd_tc(const AttnDims &d, const HeadView &q, const HeadView &k,
+                            const HeadView &v, const float *divisor, const float *mask, float *p,
+                            const HeadView &o, uint32_t *mask_flag, cudaStream_t s) {
   FwdMaps maps{};
   FwdArgs a{};
-  a.T = sh.T;
-  a.H = sh.H;
-  a.nk = (sh.T + 31) / 32 * 32;
-  a.qtiles = (sh.T + BMQ - 1) / BMQ;
+  if (mask && !aligned16(mask))  // rows of the mask are read as float4
+    return fail(TL_ERR_UNSUPPORTED, "attention forward: mask not 16-byte aligned");
+  a.mask_flag = mask ? mask_flag : nullptr;
+  a.T = d.T;
+  a.H = d.H;
+  a.nk = keys_of(d);
+  a.qtiles = (d.T + BMQ - 1) / BMQ;
   a.divisor = divisor;
   a.mask = mask;
-  a.o = o;
-  a.sb = sh.sb;
-  a.sh = sh.sh;
-  a.ld = sh.ld;
+  a.o = out_of(o);
   a.status = device_status_ptr();
-  if (!a.status) return fail(TL_ERR_CUDA, "tl_attention_fwd: no status word");
-  if (!head_map(&maps.q, q, sh, BMQ) || !head_map(&maps.k, k, sh, a.nk) ||
-      !head_map_mn(&maps.v, v, sh, a.nk) || !scores_map(&maps.p, p, sh))
-    return fail(TL_ERR_UNSUPPORTED, "tl_attention_fwd: tensor maps refused");
-  static bool attr = false;
-  int rc = set_smem(attn_fwd_kernel, kFwdSmem, attr, "tl_attention_fwd: shared memory");
+  if (!a.status) return fail(TL_ERR_CUDA, "attention forward: no status word");
+  const bool kt = k.trans;
+  const bool maps_ok =
+      rows_map(&maps.q, q, d, BMQ) &&
+      (kt ? trans_map(&maps.k, k, d, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)
+          : rows_map(&maps.k, k, d, a.nk)) &&
+      rows_map_mn(&maps.v, v, d, a.nk) &&
+      scores_map(&maps.p, p, d, BMQ, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!maps_ok) return fail(TL_ERR_UNSUPPORTED, "attention forward: tensor maps refused");
+  static bool attr[2] = {false, false};
+  int rc = kt ? set_smem(attn_fwd_kernel<true>, kQuerySmem, attr[1], "attention forward: smem")
+              : set_smem(attn_fwd_kernel<false>, kQuerySmem, attr[0], "attention forward: smem");
   if (rc) return rc;
-  const unsigned grid = static_cast<unsigned>(static_cast<uint64_t>(sh.B) * sh.H * a.qtiles);
-  launch_pdl(attn_fwd_kernel, grid, kThreads, kFwdSmem, s, maps, a);
-  return launch_status("tl_attention_fwd");
+  if (a.mask_flag) {
+    launch_pdl(mask_causal_kernel, 1, 1024, 0, s, mask, d.T, mask_flag);
+    rc = launch_status("attention forward (mask check)");
+    if (rc) return rc;
+  }
+  const unsigned grid = static_cast<unsigned>(static_cast<uint64_t>(d.B) * d.H * a.qtiles);
+  if (kt)
+    launch_pdl(attn_fwd_kernel<true>, grid, kThreads, kQuerySmem, s, maps, a);
+  else
+    launch_pdl(attn_fwd_kernel<false>, grid, kThreads, kQuerySmem, s, maps, a);
+  return launch_status("attention forward");
 }
 
-int launch_attention_bwd_tc(const float *q, const float *k, const float *v, const float *p,
-                            const float *divisor, const float *d_o, float *dq, float *dk,
-                            float *dv, float *ds, const FusedAttnShape &sh, cudaStream_t s) {
-  uint32_t *status = device_status_ptr();
-  if (!status) return fail(TL_ERR_CUDA, "tl_attention_bwd: no status word");
-  const uint32_t nk = (sh.T + 31) / 32 * 32;
-  BwdQMaps qm{};
-  BwdQArgs qa{};
-  qa.T = sh.T;
-  qa.H = sh.H;
-  qa.nk = nk;
-  qa.qtiles = (sh.T + BMQ - 1) / BMQ;
-  qa.divisor = divisor;
-  qa.dq = dq;
-  qa.sb = sh.sb;
-  qa.sh = sh.sh;
-  qa.ld = sh.ld;
-  qa.status = status;
-  BwdKvMaps km{};
-  BwdKvArgs ka{};
-  ka.T = sh.T;
-  ka.H = sh.H;
-  ka.ktiles = (sh.T + 127) / 128;
-  ka.qblocks = (sh.T + 31) / 32;
-  ka.dk = dk;
-  ka.dv = dv;
-  ka.sb = sh.sb;
-  ka.sh = sh.sh;
-  ka.ld = sh.ld;
-  ka.status = status;
-  if (!head_map(&qm.d_o, d_o, sh, BMQ) || !head_map(&qm.v, v, sh, nk) ||
-      !head_map_mn(&qm.k, k, sh, nk) || !scores_map(&qm.p, p, sh) ||
-      !scores_map(&qm.ds, ds, sh) ||
-      !scores_map(&km.ds, ds, sh, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
-      !scores_map(&km.p, p, sh, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
-      !head_map_mn32(&km.q, q, sh) || !head_map_mn32(&km.d_o, d_o, sh))
-    return fail(TL_ERR_UNSUPPORTED, "tl_attention_bwd: tensor maps refused");
-  static bool attr_q = false, attr_kv = false;
-  int rc = set_smem(attn_bwd_q_kernel, kFwdSmem, attr_q, "tl_attention_bwd: shared memory");
-  if (rc == TL_OK)
-    rc = set_smem(attn_bwd_kv_kernel, kKvSmem, attr_kv, "tl_attention_bwd: shared memory");
+int launch_attention_bwd_q_tc(const AttnDims &d, const HeadView &d_o, const HeadView &v,
+                              const HeadView &k, const float *p, const float *divisor, float *ds,
+                              const HeadView &dq, cudaStream_t s) {
+  BwdQMaps maps{};
+  BwdQArgs a{};
+  a.T = d.T;
+  a.H = d.H;
+  a.nk = keys_of(d);
+  a.qtiles = (d.T + BMQ - 1) / BMQ;
+  a.divisor = divisor;
+  a.dq = out_of(dq);
+  a.status = device_status_ptr();
+  if (!a.status) return fail(TL_ERR_CUDA, "attention backward: no status word");
+  const bool kt = k.trans;
+  const bool maps_ok = rows_map(&maps.d_o, d_o, d, BMQ) && rows_map(&maps.v, v, d, a.nk) &&
+                       (kt ? trans_map(&maps.k, k, d, CU_TENSOR_MAP_SWIZZLE_128B)
+                           : rows_map_mn(&maps.k, k, d, a.nk)) &&
+                       scores_map(&maps.p, p, d, BMQ, CU_TENSOR_MAP_SWIZZLE_128B) &&
+                       scores_map(&maps.ds, ds, d, BMQ, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!maps_ok) return fail(TL_ERR_UNSUPPORTED, "attention backward: tensor maps refused");
+  static bool attr[2] = {false, false};
+  int rc = kt ? set_smem(attn_bwd_q_kernel<true>, kQuerySmem, attr[1], "attention backward: smem")
+              : set_smem(attn_bwd_q_kernel<false>, kQuerySmem, attr[0], "attention backward: smem");
   if (rc) return rc;
-  const uint64_t bhn = static_cast<uint64_t>(sh.B) * sh.H;
-  launch_pdl(attn_bwd_q_kernel, static_cast<unsigned>(bhn * qa.qtiles), kThreads, kFwdSmem, s,
-             qm, qa);
-  rc = launch_status("tl_attention_bwd (dQ)");
+  const unsigned grid = static_cast<unsigned>(static_cast<uint64_t>(d.B) * d.H * a.qtiles);
+  if (kt)
+    launch_pdl(attn_bwd_q_kernel<true>, grid, kThreads, kQuerySmem, s, maps, a);
+  else
+    launch_pdl(attn_bwd_q_kernel<false>, grid, kThreads, kQuerySmem, s, maps, a);
+  return launch_status("attention backward (dQ)");
+}
+
+int launch_attention_bwd_kv_tc(const AttnDims &d, const float *ds, const HeadView &q,
+                               const HeadView &dk, const float *p, const HeadView &d_o,
+                               const HeadView &dv, cudaStream_t s) {
+  BwdKvMaps maps{};
+  BwdKvArgs a{};
+  a.T = d.T;
+  a.H = d.H;
+  a.ktiles = (d.T + 127) / 128;
+  a.qblocks = (d.T + 31) / 32;
+  a.with_dk = dk.p != nullptr;
+  a.with_dv = dv.p != nullptr;
+  a.dk = out_of(dk);
+  a.dv = out_of(dv);
+  a.status = device_status_ptr();
+  if (!a.status) return fail(TL_ERR_CUDA, "attention backward: no status word");
+  if (!a.with_dk && !a.with_dv) return TL_OK;
+  constexpr CUtensorMapSwizzle mn = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+  bool maps_ok = true;
+  if (a.with_dk)
+    maps_ok = scores_map(&maps.ds, ds, d, 32, mn) && rows_map(&maps.q, q, d, 32, mn);
+  if (a.with_dv)
+    maps_ok = maps_ok && scores_map(&maps.p, p, d, 32, mn) && rows_map(&maps.d_o, d_o, d, 32, mn);
+  if (!maps_ok) return fail(TL_ERR_UNSUPPORTED, "attention backward: tensor maps refused");
+  a.stage_bytes = ((a.with_dk ? 1u : 0u) + (a.with_dv ? 1u : 0u)) * kKvPart;
+  a.dv_off = a.with_dk ? kKvPart : 0;
+  const size_t smem = kv_smem(a.stage_bytes / kKvPart);
+  static bool attr = false;
+  int rc = set_smem(attn_bwd_kv_kernel, kv_smem(2), attr, "attention backward: smem");
   if (rc) return rc;
-  launch_pdl(attn_bwd_kv_kernel, static_cast<unsigned>(bhn * ka.ktiles), kKvThreads, kKvSmem, s,
-             km, ka);
-  return launch_status("tl_attention_bwd (dK, dV)");
+  const unsigned grid = static_cast<unsigned>(static_cast<uint64_t>(d.B) * d.H * a.ktiles);
+  launch_pdl(attn_bwd_kv_kernel, grid, kKvThreads, smem, s, maps, a);
+  return launch_status("attention backward (dK, dV)");
 }
 
 }  // namespace tl

@@ -58,6 +58,14 @@ Access access(const Op &op) {
     case Kind::SoftmaxBwd: a.read(t[0]); a.read(t[1]); a.read(t[3]); a.write(t[2]); break;
     case Kind::RmsNormBwd:
       a.read(t[0]); a.read(t[1]); a.read(t[2]); a.read(t[4]); a.write(t[3]); break;
+    case Kind::Attention:
+      if (op.code == TL_ATTN_PRODUCT_TN) {
+        a.read(t[0]); a.read(t[1]); a.write(t[2]);
+      } else {
+        for (int i = 0; i < 5; ++i) a.read(t[i]);
+        a.write(t[5]); a.write(t[6]);
+      }
+      break;
     default: break;  // Release, MultiAdamW, AllReduce: handled by their passes
   }
   return a;
@@ -76,6 +84,7 @@ bool full_write(const Op &op) {
 namespace {
 
 constexpr size_t kNone = static_cast<size_t>(-1);
+constexpr uint32_t kFusedHeadDimHost = 64;  // head width of tl_attention_fused
 
 // Window liveness of the program being optimised (null: none known).
 thread_local const Liveness *g_live = nullptr;
@@ -793,6 +802,211 @@ uint64_t fold_head_transposes(std::vector<Op> &p) {
   return folded;
 }
 
+// -------------------------------------------------------- fused attention
+// A plain product: no epilogue, no groups, TF32 (the fused kernels' type).
+bool plain_product(const Op &op) {
+  const tl_gemm_desc &g = op.gemm;
+  return !op.dead && op.kind == Kind::Gemm && g.beta == 0.0f && !g.bias && !g.gelu_out &&
+         !g.addend && !op.t[5].p && g.group_mode == TL_GEMM_GROUP_NONE &&
+         g.precision == TL_GEMM_TF32 && op.i1 == 0;
+}
+
+// Operand `which` (0 A, 1 B, 2 C) of a product batched over B x H (one
+// flattened dim or the two dims) as per-(batch, head) blocks whose stored
+// rows hold `cols` elements when dense.
+bool head_view(const tl_gemm_desc &g, int which, uint32_t B, uint32_t H, uint32_t cols,
+               bool transposed, tl_attn_view &v) {
+  const uint64_t *st = which == 0 ? g.a_batch_stride
+                       : which == 1 ? g.b_batch_stride
+                                    : g.c_batch_stride;
+  const uint64_t ld = which == 0 ? g.lda : which == 1 ? g.ldb : g.ldc;
+  v = tl_attn_view{};
+  v.p = which == 0 ? g.a : which == 1 ? g.b : g.c;
+  v.row_stride = ld ? ld : cols;
+  v.transposed = transposed ? 1 : 0;
+  if (g.batch_rank == 1 && g.batch_shape[0] == static_cast<uint64_t>(B) * H) {
+    v.head_stride = st[0];
+    v.batch_stride = st[0] * H;
+  } else if (g.batch_rank == 2 && g.batch_shape[0] == B && g.batch_shape[1] == H) {
+    v.batch_stride = st[0];
+    v.head_stride = st[1];
+  } else {
+    return false;
+  }
+  return true;
+}
+
+bool dense_scores(const tl_attn_view &v, uint32_t H, uint32_t T) {
+  const uint64_t tt = static_cast<uint64_t>(T) * T;
+  return v.row_stride == T && v.head_stride == tt && v.batch_stride == tt * H && !v.transposed;
+}
+
+// [B, H, T, T] tensor: its B, H, T.
+bool score_dims(const TRef &t, uint32_t &B, uint32_t &H, uint32_t &T) {
+  if (t.rank != 4 || t.shape[2] != t.shape[3]) return false;
+  B = t.shape[0];
+  H = t.shape[1];
+  T = t.shape[2];
+  return true;
+}
+
+// The executor's attention composite (include/nn/multi_head.h:45-52 and its
+// gradients) on the fused tensor-core kernels:
+//   forward   S = Q K^T (product), softmax(S / divisor + mask) -> P, O = P V
+//             -> one op at O's product (S never written)
+//   backward  dP = dO V^T, softmax derivative(dP, P) / divisor -> dS,
+//             dQ = dS K -> one op at dQ's product (dP never written)
+//   dK = dS^T Q and dV = P^T dO (square [T, T] left operands) -> the
+//             key-side kernel in place of the product
+// Each only when the fused kernels take the operands' strides and the
+// values read at the fused op's position are those the originals read.
+uint64_t fuse_attention(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t k = 0; k < p.size(); ++k) {
+    Op &sm = p[k];
+    if (sm.dead) continue;
+    if (sm.kind == Kind::Softmax && sm.t[2].p) {
+      const TRef X = sm.t[0], Y = sm.t[1], div = sm.t[2], mask = sm.t[3];
+      uint32_t B, H, T;
+      if (!score_dims(Y, B, H, T) || !is_scalar_tensor(div)) continue;
+      if (mask.p && mask.numel() != static_cast<uint64_t>(T) * T) continue;
+      const size_t i = last_writer(p, k, X.id);
+      if (i == kNone || !plain_product(p[i]) || first_reader(p, i, X.id) != k ||
+          !dead_after(p, k, X.id))
+        continue;
+      const size_t j = first_reader(p, k, Y.id);
+      if (j == kNone || !plain_product(p[j]) || !same(p[j].t[0], Y) || same(p[j].t[1], Y))
+        continue;
+      const tl_gemm_desc &g1 = p[i].gemm, &g2 = p[j].gemm;
+      if (g1.m != T || g1.n != T || g1.k != kFusedHeadDimHost || g1.trans_a || g2.m != T ||
+          g2.k != T || g2.n != kFusedHeadDimHost || g2.trans_a || g2.trans_b)
+        continue;
+      tl_attn_desc d{};
+      d.pass = TL_ATTN_FORWARD;
+      d.B = B;
+      d.H = H;
+      d.T = T;
+      d.D = kFusedHeadDimHost;
+      tl_attn_view sv, pv;
+      if (!head_view(g1, 0, B, H, g1.k, false, d.q) ||
+          !head_view(g1, 1, B, H, g1.trans_b ? g1.k : g1.n, !g1.trans_b, d.k) ||
+          !head_view(g1, 2, B, H, T, false, sv) || !dense_scores(sv, H, T) ||
+          !head_view(g2, 0, B, H, T, false, pv) || !dense_scores(pv, H, T) ||
+          !head_view(g2, 1, B, H, g2.n, false, d.v) || !head_view(g2, 2, B, H, g2.n, false, d.o))
+        continue;
+      d.divisor = div.f();
+      d.mask = mask.p ? mask.f() : nullptr;
+      d.p = Y.f();
+      const TRef Q = p[i].t[0], K = p[i].t[1];
+      if (!unchanged_between(p, i, j, Q.id) || !unchanged_between(p, i, j, K.id) ||
+          !unchanged_between(p, k, j, div.id) || (mask.p && !unchanged_between(p, k, j, mask.id)) ||
+          !untouched_between(p, k, j, Y.id) || tl_attention_fused_supported(&d) != 1)
+        continue;
+      Op fused{};
+      fused.kind = Kind::Attention;
+      fused.code = TL_ATTN_FORWARD;
+      fused.attn = d;
+      fused.workspace = 256;  // the causal-mask word
+      fused.t[0] = Q;
+      fused.t[1] = K;
+      fused.t[2] = p[j].t[1];
+      fused.t[3] = div;
+      fused.t[4] = mask;
+      fused.t[5] = Y;
+      fused.t[6] = p[j].t[2];
+      fused.src = p[j].src;
+      p[i].dead = true;
+      sm.dead = true;
+      p[j] = std::move(fused);
+      folded += 2;
+    } else if (sm.kind == Kind::SoftmaxBwd && sm.t[3].p) {
+      const TRef dP = sm.t[0], P = sm.t[1], dS = sm.t[2], div = sm.t[3];
+      uint32_t B, H, T;
+      if (!score_dims(P, B, H, T) || !dS.same_shape(P) || !is_scalar_tensor(div)) continue;
+      const size_t i = last_writer(p, k, dP.id);
+      if (i == kNone || !plain_product(p[i]) || first_reader(p, i, dP.id) != k ||
+          !dead_after(p, k, dP.id))
+        continue;
+      const size_t j = first_reader(p, k, dS.id);
+      if (j == kNone || !plain_product(p[j]) || !same(p[j].t[0], dS) || same(p[j].t[1], dS))
+        continue;
+      const tl_gemm_desc &g1 = p[i].gemm, &g2 = p[j].gemm;
+      if (g1.m != T || g1.n != T || g1.k != kFusedHeadDimHost || g1.trans_a || !g1.trans_b ||
+          g2.m != T || g2.k != T || g2.n != kFusedHeadDimHost || g2.trans_a)
+        continue;
+      tl_attn_desc d{};
+      d.pass = TL_ATTN_BACKWARD_Q;
+      d.B = B;
+      d.H = H;
+      d.T = T;
+      d.D = kFusedHeadDimHost;
+      tl_attn_view pv, sv;
+      if (!head_view(g1, 0, B, H, g1.k, false, d.d_o) ||
+          !head_view(g1, 1, B, H, g1.k, false, d.v) || !head_view(g1, 2, B, H, T, false, pv) ||
+          !dense_scores(pv, H, T) || !head_view(g2, 0, B, H, T, false, sv) ||
+          !dense_scores(sv, H, T) ||
+          !head_view(g2, 1, B, H, g2.trans_b ? g2.k : g2.n, g2.trans_b, d.k) ||
+          !head_view(g2, 2, B, H, g2.n, false, d.dq))
+        continue;
+      d.divisor = div.f();
+      d.p = P.f();
+      d.ds = dS.f();
+      const TRef dO = p[i].t[0], V = p[i].t[1];
+      if (!unchanged_between(p, i, j, dO.id) || !unchanged_between(p, i, j, V.id) ||
+          !unchanged_between(p, k, j, P.id) || !unchanged_between(p, k, j, div.id) ||
+          !untouched_between(p, k, j, dS.id) || tl_attention_fused_supported(&d) != 1)
+        continue;
+      Op fused{};
+      fused.kind = Kind::Attention;
+      fused.code = TL_ATTN_BACKWARD_Q;
+      fused.attn = d;
+      fused.t[0] = dO;
+      fused.t[1] = V;
+      fused.t[2] = p[j].t[1];
+      fused.t[3] = P;
+      fused.t[4] = div;
+      fused.t[5] = dS;
+      fused.t[6] = p[j].t[2];
+      fused.src = p[j].src;
+      p[i].dead = true;
+      sm.dead = true;
+      p[j] = std::move(fused);
+      folded += 2;
+    }
+  }
+  // dK = dS^T Q, dV = P^T dO: square left operand, transposed
+  for (Op &op : p) {
+    if (!plain_product(op)) continue;
+    const tl_gemm_desc &g = op.gemm;
+    uint32_t B, H, T;
+    if (!g.trans_a || g.trans_b || !score_dims(op.t[0], B, H, T) || g.m != T || g.k != T ||
+        g.n != kFusedHeadDimHost)
+      continue;
+    tl_attn_desc d{};
+    d.pass = TL_ATTN_PRODUCT_TN;
+    d.B = B;
+    d.H = H;
+    d.T = T;
+    d.D = kFusedHeadDimHost;
+    tl_attn_view av;
+    if (!head_view(g, 0, B, H, T, false, av) || !dense_scores(av, H, T) ||
+        !head_view(g, 1, B, H, g.n, false, d.q) || !head_view(g, 2, B, H, g.n, false, d.dk))
+      continue;
+    d.ds = op.t[0].f();
+    if (tl_attention_fused_supported(&d) != 1) continue;
+    Op fused{};
+    fused.kind = Kind::Attention;
+    fused.code = TL_ATTN_PRODUCT_TN;
+    fused.attn = d;
+    fused.t[0] = op.t[0];
+    fused.t[1] = op.t[1];
+    fused.t[2] = op.t[2];
+    fused.src = op.src;
+    op = std::move(fused);
+  }
+  return folded;
+}
+
 // ------------------------------------------------------- grouped products
 bool groupable(const Op &op) {
   return !op.dead && op.kind == Kind::Gemm && op.gemm.group_mode == TL_GEMM_GROUP_NONE &&
@@ -1368,6 +1582,7 @@ uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live) {
   folded += fuse_gemm_accumulate(prog);
   folded += fuse_row_backward_tails(prog);
   folded += fuse_score_softmax(prog);
+  folded += fuse_attention(prog);
   folded += group_summed_products(prog);
   folded += group_shared_input(prog);
   folded += fuse_step(prog);

@@ -69,6 +69,11 @@ enum class Kind : uint8_t {
   RmsNormBwd,  // t0 grad, t1 x, t2 y, t3 out (+ t4 addend)
   MultiAdamW,  // slots in `multi`; t0 sqnorm (optional); f0 max_norm; f1 eps; t5..t8 scalars
   AllReduce,   // NCCL sum of the gradients in `multi`
+  // fused attention (tl_attention_fused with `attn`), code = tl_attn_pass:
+  //   forward       t0 q, t1 k, t2 v, t3 divisor, t4 mask (optional), t5 p, t6 o
+  //   backward Q    t0 dO, t1 v, t2 k, t3 p, t4 divisor, t5 ds, t6 dq
+  //   product TN    t0 ds (or p), t1 q (or dO), t2 dk (or dv)
+  Attention,
 };
 
 const char *kind_name(Kind k);
@@ -88,6 +93,7 @@ struct Op {
   uint64_t n = 0;          // element / byte counts for data movement
   size_t workspace = 0;    // device scratch bytes this op needs
   tl_gemm_desc gemm{};
+  tl_attn_desc attn{};             // Attention
   std::vector<uint8_t> host;       // HostWrite payload
   std::vector<MultiSlot> multi;    // MultiAdamW / AllReduce
   // grouped GEMM operands beyond group 0 (gemm.group_mode): N groups

@@ -72,7 +72,8 @@ const char *const kKindNames[] = {
     "binary",  "scalar",    "unary",      "copy",       "reduce",    "argmax",   "transpose",
     "softmax", "rms",       "rmsnorm",    "xent",       "xent_bwd",  "gather",   "scatter",
     "sqnorm",  "clip",      "adamw",      "gemm",       "host_write", "fill",    "dev_copy",
-    "release", "gelu_bwd",  "softmax_bwd", "rmsnorm_bwd", "multi_adamw", "allreduce"};
+    "release", "gelu_bwd",  "softmax_bwd", "rmsnorm_bwd", "multi_adamw", "allreduce",
+    "attention"};
 
 }  // namespace
 
@@ -592,6 +593,13 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
       case Kind::AllReduce:
         internal::all_reduce_gradients(op, comm, s);
         break;
+      case Kind::Attention: {
+        tl_attn_desc d = op.attn;
+        d.workspace = ws;
+        d.workspace_bytes = wsb;
+        check(tl_attention_fused(&d, s), "attention");
+        break;
+      }
     }
   }
 
@@ -619,6 +627,7 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
       if (op.kind == Kind::AdamW) put(&op.u0, sizeof(op.u0));
       if (op.kind == Kind::Fill) put(&op.u0, sizeof(op.u0));
       if (op.kind == Kind::Gemm) put(&op.gemm, sizeof(op.gemm));
+      if (op.kind == Kind::Attention) put(&op.attn, sizeof(op.attn));
       if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce) {
         for (const auto &s : op.multi) {
           put(&s.param.p, sizeof(void *));
@@ -661,6 +670,10 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
       if (batch > 1) key += " b" + std::to_string(batch);
       key += op.gemm.trans_a ? " T" : " N";
       key += op.gemm.trans_b ? "T" : "N";
+    } else if (op.kind == Kind::Attention) {
+      key += "#" + std::to_string(op.code) + " " + std::to_string(op.attn.B) + "x" +
+             std::to_string(op.attn.H) + "x" + std::to_string(op.attn.T) + "x" +
+             std::to_string(op.attn.D);
     } else if (op.kind != Kind::MultiAdamW && op.kind != Kind::AllReduce) {
       // element-wise and row ops: code and the shapes that set the traffic
       if (op.kind == Kind::Binary || op.kind == Kind::Unary || op.kind == Kind::Scalar ||

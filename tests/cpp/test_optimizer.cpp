@@ -502,6 +502,83 @@ void projections_grouped() {
           "one K-grouped product into dX");
 }
 
+
+Op softmax_op(const TRef &x, const TRef &y, const TRef &div, const TRef &mask) {
+  Op o = op(Kind::Softmax);
+  o.t[0] = x;
+  o.t[1] = y;
+  o.t[2] = div;
+  o.t[3] = mask;
+  return o;
+}
+
+// attention forward: scores product, scaled masked softmax, P V -> one
+// fused op at the P V product, with K read through its transposed copy
+void attention_forward_fused() {
+  const uint32_t B = 4, H = 6, T = 192, D = 64;
+  auto q = tensor({B, H, T, D}), kt = tensor({B, H, D, T}), v = tensor({B, H, T, D});
+  auto s1 = tensor({B, H, T, T}), pr = tensor({B, H, T, T}), o = tensor({B, H, T, D});
+  auto div = tensor({1, 1}), mask = tensor({1, 1, T, T});
+  std::vector<Op> p = {gemm(q, kt, s1, T, T, D, B * H), softmax_op(s1, pr, div, mask),
+                       release(s1), gemm(pr, v, o, T, D, T, B * H)};
+  require(optimize(p, nullptr) == 2, "two ops folded into the fused op");
+  auto l = live(p);
+  require(l.size() == 1 && l[0]->kind == Kind::Attention && l[0]->code == TL_ATTN_FORWARD,
+          "one fused attention op");
+  const tl_attn_desc &d = l[0]->attn;
+  require(d.B == B && d.H == H && d.T == T && d.D == D && d.k.transposed == 1 &&
+              d.k.row_stride == T && d.k.head_stride == D * T && d.q.transposed == 0 &&
+              d.q.row_stride == D && d.q.batch_stride == H * T * D && d.p == pr.p &&
+              d.mask == mask.p && d.divisor == div.p && d.o.p == o.p,
+          "views of Q, K^T, V, O and the score tensors");
+  // P read by another op before the P V product: kept unfused
+  auto other = tensor({B, H, T, T});
+  std::vector<Op> p2 = {gemm(q, kt, s1, T, T, D, B * H), softmax_op(s1, pr, div, mask),
+                        release(s1), binary(TL_ADD, pr, pr, other),
+                        gemm(pr, v, o, T, D, T, B * H)};
+  optimize(p2, nullptr);
+  for (const Op *x : live(p2)) require(x->kind != Kind::Attention, "P observed: not fused");
+  // Q rewritten between the products: kept unfused
+  std::vector<Op> p3 = {gemm(q, kt, s1, T, T, D, B * H), softmax_op(s1, pr, div, mask),
+                        release(s1), binary(TL_ADD, v, v, q), gemm(pr, v, o, T, D, T, B * H)};
+  optimize(p3, nullptr);
+  for (const Op *x : live(p3)) require(x->kind != Kind::Attention, "Q changed: not fused");
+}
+
+// attention backward: dP = dO V^T, softmax derivative with the divisor,
+// dQ = dS K -> one fused op; dK = dS^T Q and dV = P^T dO -> key-side ops
+void attention_backward_fused() {
+  const uint32_t B = 4, H = 6, T = 192, D = 64;
+  auto d_o = tensor({B, H, T, D}), v = tensor({B, H, T, D}), pr = tensor({B, H, T, T});
+  auto dp = tensor({B, H, T, T}), ds = tensor({B, H, T, T}), kt = tensor({B, H, D, T});
+  auto dq = tensor({B, H, T, D}), q = tensor({B, H, T, D}), dk = tensor({B, H, T, D});
+  auto dv = tensor({B, H, T, D}), div = tensor({1, 1});
+  Op g1 = gemm(d_o, v, dp, T, T, D, B * H);
+  g1.gemm.trans_b = 1;
+  Op sb = op(Kind::SoftmaxBwd);
+  sb.t[0] = dp;
+  sb.t[1] = pr;
+  sb.t[2] = ds;
+  sb.t[3] = div;
+  Op g2 = gemm(ds, kt, dq, T, D, T, B * H);
+  g2.gemm.trans_b = 1;
+  Op g3 = gemm(ds, q, dk, T, D, T, B * H);
+  g3.gemm.trans_a = 1;
+  Op g4 = gemm(pr, d_o, dv, T, D, T, B * H);
+  g4.gemm.trans_a = 1;
+  std::vector<Op> p = {g1, sb, release(dp), g2, g3, release(ds), g4};
+  require(optimize(p, nullptr) == 2, "dP product and derivative folded");
+  auto l = live(p);
+  require(l.size() == 3 && l[0]->kind == Kind::Attention &&
+              l[0]->code == TL_ATTN_BACKWARD_Q && l[0]->attn.k.transposed == 1 &&
+              l[0]->attn.ds == ds.p && l[0]->attn.dq.p == dq.p,
+          "query side fused, dS still written");
+  require(l[1]->kind == Kind::Attention && l[1]->code == TL_ATTN_PRODUCT_TN &&
+              l[1]->attn.ds == ds.p && l[1]->attn.q.p == q.p && l[1]->attn.dk.p == dk.p &&
+              l[2]->kind == Kind::Attention && l[2]->attn.ds == pr.p && l[2]->attn.dk.p == dv.p,
+          "dK and dV on the key-side kernel");
+}
+
 }  // namespace
 
 int main() {
@@ -527,6 +604,8 @@ int main() {
       {"row_backward_tails", row_backward_tails},
       {"head_transposes_become_strides", head_transposes_become_strides},
       {"projections_grouped", projections_grouped},
+      {"attention_forward_fused", attention_forward_fused},
+      {"attention_backward_fused", attention_backward_fused},
   };
   for (const auto &[name, fn] : cases) {
     try {

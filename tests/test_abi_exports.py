@@ -72,7 +72,8 @@ def test_struct_layouts_match_the_headers(tmp_path):
     field offsets (a missing field would let the library read past the
     caller's struct)."""
     structs = {"tl_gemm_desc": capi.TlGemmDesc, "tl_param_slot": capi.TlParamSlot,
-               "tlg_config": capi.TlgConfig}
+               "tlg_config": capi.TlgConfig, "tl_attn_view": capi.TlAttnView,
+               "tl_attn_desc": capi.TlAttnDesc}
     lines = ['#include <stddef.h>', '#include <stdio.h>', '#include "templit_cuda.h"',
              '#include "templit_gpt.h"', "int main(void) {"]
     for cname, py in structs.items():

@@ -42,9 +42,10 @@ def inputs(B, H, T, D, seed):
     return [rng.standard_normal((B, H, T, D)).astype(np.float32) for _ in range(4)]
 
 
-def run_case(dev, B, H, T, D, masked, layout, precision, seed=0):
+def run_case(dev, B, H, T, D, masked, layout, precision, seed=0, mask=None):
     q, k, v, d_o = inputs(B, H, T, D, seed)
-    mask = ops.causal_mask(T) if masked else None
+    if mask is None and masked:
+        mask = ops.causal_mask(T)
     divisor = float(np.sqrt(np.float32(D)))
     p, o = ops.attention_forward(q, k, v, divisor, mask)
     dq, dk, dv = ops.attention_backward(q, k, v, p, divisor, d_o)
@@ -59,7 +60,7 @@ def run_case(dev, B, H, T, D, masked, layout, precision, seed=0):
     for n, e in errs.items():
         bound = 1e-5 if precision == capi.TL_GEMM_FP32 else 1e-3 * CHAIN[n]
         assert e <= bound, (n, e, bound, errs)
-    if masked:  # exactly zero above the diagonal
+    if masked and np.isneginf(np.triu(mask, 1)).all():  # exactly zero above the diagonal
         assert not np.triu(got[0], 1).any()
     return errs
 
@@ -77,6 +78,20 @@ def test_config3_causal(dev, precision):
 ])
 def test_ragged(dev, B, H, T, D, masked):
     run_case(dev, B, H, T, D, masked, capi.TL_ATTN_BHTD, capi.TL_GEMM_TF32, seed=T)
+
+
+@pytest.mark.parametrize("kind", ["additive", "causal_but_one"])
+def test_general_masks(dev, kind):
+    """A mask that is not the causal one is read element by element: an
+    arbitrary additive mask, and the causal mask with one entry changed."""
+    T = 192
+    rng = np.random.default_rng(11)
+    if kind == "additive":
+        mask = (0.5 * rng.standard_normal((T, T))).astype(np.float32)
+    else:
+        mask = ops.causal_mask(T).astype(np.float32)
+        mask[100, 7] = -3.0
+    run_case(dev, 2, 3, T, 64, True, capi.TL_ATTN_BHTD, capi.TL_GEMM_TF32, seed=4, mask=mask)
 
 
 def test_heads_in_place_layout(dev):
