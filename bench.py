@@ -164,8 +164,13 @@ def gemm_roofline(profile_path, peak_tflops, peak_source):
             continue
         parts = o["op"].split()
         m, n, k = (int(v) for v in parts[1].split("x"))
-        batch = int(parts[2][1:]) if len(parts) > 2 and parts[2].startswith("b") else 1
-        flops += 2.0 * m * n * k * batch * o["calls"]
+        batch = groups = 1
+        for tok in parts[2:]:
+            if tok.startswith("b"):
+                batch = int(tok[1:])
+            elif tok.startswith("g"):  # grouped launch: `groups` products
+                groups = int(tok[1:])
+        flops += 2.0 * m * n * k * batch * groups * o["calls"]
         ms += o["ms"]
         launches += o["calls"]
     if ms == 0:

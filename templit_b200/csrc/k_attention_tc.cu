@@ -36,7 +36,7 @@
 namespace tl {
 namespace {
 
-constexpr int kSoftWarps = 16;  // four per TMEM lane quadrant
+constexpr int kSoftWarps = 8;  // two per TMEM lane quadrant
 constexpr int kThreads = 64 + 32 * kSoftWarps;
 constexpr uint32_t BMQ = 128;  // query rows of a CTA
 constexpr uint32_t HD = kFusedHeadDim;
@@ -52,16 +52,22 @@ struct Out {
 Out out_of(const HeadView &v) { return Out{const_cast<float *>(v.p), v.sb, v.sh, v.ld}; }
 
 // Shared memory of the query-side kernels (offsets from a 1024-aligned
-// base): a 128-row tile of D = 64 (two 16 KB K-major blocks), two operands
-// of nk rows (48 KB each at most), the P / dS tile (nk / 32 blocks of
-// 128 x 32), barriers.
-constexpr uint32_t kTile = 0;
-constexpr uint32_t kOp1 = kTile + 2 * BMQ * 128;
-constexpr uint32_t kOp2 = kOp1 + 2 * kMaxFusedKeys * 128;
-constexpr uint32_t kScores = kOp2 + 2 * kMaxFusedKeys * 128;
-constexpr uint32_t kBars = kScores + (kMaxFusedKeys / 32) * BMQ * 128;
+// base), small enough for two CTAs per SM.  Region A holds the operands of
+// the first product (a 128-row tile of D = 64 in two 16 KB K-major blocks,
+// then an nk-row operand, 48 KB at most), and, once that product is done,
+// the second product's nk-row operand (48 KB) and a ring of two 128 x 32
+// score blocks (P or dS) that the softmax warps fill, the MMA warp
+// multiplies and warp 0 stores.  Then the row reductions and barriers.
+constexpr uint32_t kBlock = BMQ * 128;                         // 16 KB
+constexpr uint32_t kRegQ = 2 * kBlock;                         // 32 KB
+constexpr uint32_t kRingOff = 2 * kMaxFusedKeys * 128;         // 48 KB
+constexpr uint32_t kRegion = kRegQ + 2 * kMaxFusedKeys * 128;  // 80 KB
+static_assert(kRingOff + 2 * kBlock <= kRegion, "ring exceeds region A");
+constexpr uint32_t kRed = kRegion;
+constexpr uint32_t kBars = kRed + 4 * BMQ * 4;
 constexpr size_t kQuerySmem = 1024 + kBars + 256;
-static_assert(kQuerySmem <= 232448, "query tile exceeds shared memory");
+constexpr uint32_t kTmemCols = 256;  // scores (<= 192 columns) + a 64-column product
+static_assert(kMaxFusedKeys + HD <= kTmemCols, "TMEM budget");
 
 __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t j) {
   return r * 128u + ((j ^ (r & 7u)) << 4);
@@ -184,15 +190,18 @@ mask_causal_kernel(const float *__restrict__ mask, uint32_t T, uint32_t *flag) {
 }
 
 template <bool KT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
 attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
-  uint8_t *s_q = smem + kTile, *s_k = smem + kOp1, *s_v = smem + kOp2, *s_p = smem + kScores;
+  // region A: Q and K for S, then V and the P ring for P V
+  uint8_t *s_q = smem, *s_k = smem + kRegQ, *s_v = smem, *s_ring = smem + kRingOff;
+  float *red_m = reinterpret_cast<float *>(smem + kRed);  // [2][128] row maxima
+  float *red_s = red_m + 2 * BMQ;                          // [2][128] row sums
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBars);
   uint64_t *bar_qk = bars, *bar_v = bars + 1, *bar_s = bars + 2, *bar_o = bars + 3;
-  uint64_t *bar_p = bars + 4;  // one per 32-key block
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar_p + kMaxFusedKeys / 32);
+  uint64_t *full = bars + 4, *mma_done = bars + 6, *store_done = bars + 8;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 10);
   volatile uint32_t *abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -204,8 +213,11 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 4; ++i) ptx::mbar_init(&bars[i], 1);
-    // a 32-key block of P: two 16-column pieces, each from four warps
-    for (uint32_t c = 0; c < nkb; ++c) ptx::mbar_init(&bar_p[c], 2 * 4 * 32);
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(&full[i], kSoftWarps * 32);  // a block: every softmax thread
+      ptx::mbar_init(&mma_done[i], 1);
+      ptx::mbar_init(&store_done[i], 1);
+    }
     *abort_flag = 0;
     ptx::fence_barrier_init();
     ptx::prefetch_tensormap(&maps.q);
@@ -214,14 +226,14 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
     ptx::prefetch_tensormap(&maps.p);
   }
   if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, 512);
+    ptx::tmem_alloc(tmem_slot, kTmemCols);
     ptx::tmem_relinquish();
   }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_s = tmem, tmem_o = tmem + 256;
+  const uint32_t tmem_s = tmem, tmem_o = tmem + kMaxFusedKeys;
   pdl_enter();
   // causal mask: applied arithmetically; key blocks past the tile's last
   // row are all masked (P = 0 there), so S and P V stop at nk_eff
@@ -235,8 +247,10 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
   };
 
   if (warp == 0) {
+    // ------------------------------------------------ loads and P stores
     if (lane == 0) {
       const uint32_t kbytes = a.nk * HD * 4;
+      bool ok = true;
       ptx::mbar_arrive_expect_tx(bar_qk, 2 * BMQ * 128 + kbytes);
       for (int kb = 0; kb < 2; ++kb) {
         const int32_t cq[4] = {32 * kb, q0, hh, bb};
@@ -246,19 +260,38 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
         load_trans_blocks(s_k, &maps.k, bar_qk, a.nk, hh, bb);
       else
         load_rows_kmajor(s_k, &maps.k, bar_qk, a.nk, hh, bb);
-      ptx::mbar_arrive_expect_tx(bar_v, kbytes);
-      load_rows_mnmajor(s_v, &maps.v, bar_v, hh, bb);
-      // the loads land before the CTA may exit
-      if (!ptx::mbar_wait_bounded(bar_qk, 0, kWaitLimitNs) ||
-          !ptx::mbar_wait_bounded(bar_v, 0, kWaitLimitNs))
-        timeout();
+      // V replaces Q and K once S is computed
+      ok = ptx::mbar_wait_bounded(bar_s, 0, kWaitLimitNs);
+      if (ok) {
+        ptx::mbar_arrive_expect_tx(bar_v, kbytes);
+        load_rows_mnmajor(s_v, &maps.v, bar_v, hh, bb);
+      }
+      // each P block leaves by TMA store once written; its ring slot is
+      // free again when the store has read it and its MMAs are done
+      for (uint32_t c = 0; c < nkb && ok; ++c) {
+        const uint32_t slot = c & 1, use = c >> 1;
+        if (!ptx::mbar_wait_bounded(&full[slot], use & 1, kWaitLimitNs)) {
+          ok = false;
+          break;
+        }
+        ptx::tma_store_3d(&maps.p, s_ring + slot * kBlock, static_cast<int32_t>(c * 32), q0,
+                          static_cast<int32_t>(bh));
+        ptx::bulk_commit_group();
+        ptx::bulk_wait_group_read<0>();
+        ptx::mbar_arrive(&store_done[slot]);
+      }
+      if (ok) ok = ptx::mbar_wait_bounded(bar_v, 0, kWaitLimitNs);
+      if (!ok) timeout();
+      ptx::bulk_wait_group<0>();
     }
   } else if (warp == 1) {
+    // ------------------------------------------------------------ MMAs
     if (lane == 0) {
       bool issued = false;
       const uint32_t sq = ptx::smem_addr(s_q), sk = ptx::smem_addr(s_k);
-      const uint32_t sv = ptx::smem_addr(s_v), sp = ptx::smem_addr(s_p);
-      if (ptx::mbar_wait_bounded(bar_qk, 0, kWaitLimitNs)) {
+      const uint32_t sv = ptx::smem_addr(s_v), sr = ptx::smem_addr(s_ring);
+      bool ok = ptx::mbar_wait_bounded(bar_qk, 0, kWaitLimitNs);
+      if (ok) {
         ptx::tc_fence_after();
         const uint32_t idesc_s = ptx::idesc_tf32(BMQ, nk_eff, false, KT);
 #pragma unroll
@@ -276,49 +309,53 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
           }
         issued = true;
         ptx::mma_commit(bar_s);
-        bool ok = ptx::mbar_wait_bounded(bar_v, 0, kWaitLimitNs);
-        const uint32_t idesc_o = ptx::idesc_tf32(BMQ, HD, false, true);
-        for (uint32_t c = 0; c < nk_eff / 32 && ok; ++c) {
-          if (!ptx::mbar_wait_bounded(&bar_p[c], 0, kWaitLimitNs)) {
-            ok = false;
-            break;
-          }
-          ptx::tc_fence_after();
+        ok = ptx::mbar_wait_bounded(bar_v, 0, kWaitLimitNs);
+      }
+      const uint32_t idesc_o = ptx::idesc_tf32(BMQ, HD, false, true);
+      for (uint32_t c = 0; c < nkb && ok; ++c) {
+        const uint32_t slot = c & 1, use = c >> 1;
+        if (!ptx::mbar_wait_bounded(&full[slot], use & 1, kWaitLimitNs)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        if (c < nk_eff / 32) {
 #pragma unroll
           for (uint32_t kk = 0; kk < 4; ++kk)
             ptx::mma_tf32(tmem_o,
-                          ptx::smem_desc(sp + c * BMQ * 128 + kk * 32, 16, 1024,
+                          ptx::smem_desc(sr + slot * kBlock + kk * 32, 16, 1024,
                                          ptx::kSwizzle128B),
                           ptx::smem_desc(sv + (c * 32 + kk * 8) * 128, a.nk * 128, 512,
                                          ptx::kSwizzle128B32BAtom),
                           idesc_o, (c | kk) ? 1u : 0u);
         }
-        if (!ok) timeout();
-        ptx::mma_commit(bar_o);
-      } else {
-        timeout();
+        ptx::mma_commit(&mma_done[slot]);  // (blocks of zeros: nothing to wait for)
       }
-      // what was issued has finished before TMEM is released
-      if (issued) ptx::mbar_wait_bounded(bar_o, 0, kWaitLimitNs);
+      if (!ok) timeout();
+      if (issued) {
+        ptx::mma_commit(bar_o);
+        ptx::mbar_wait_bounded(bar_o, 0, kWaitLimitNs);  // before TMEM is released
+      } else {
+        ptx::mbar_arrive(bar_o);
+      }
     }
   } else {
-    // Warps 2..17: quadrant q = warp % 4 (the TMEM lanes a warp may read);
-    // the four warps of a quadrant take 16-column pieces quarter, quarter +
-    // 4, ...  Three passes over S: max, sum of exponentials, P.
+    // --------------------------------------------------------- softmax
+    // Warps 2..9: quadrant q = warp % 4 (the TMEM lanes a warp may read),
+    // the two warps of a quadrant on alternate 16-key pieces.  Three passes
+    // over S: max, sum of exponentials, P (through the ring).
     const int e = warp - 2;
-    const uint32_t q = warp & 3, quarter = static_cast<uint32_t>(e) >> 2;
+    const uint32_t q = warp & 3, half = static_cast<uint32_t>(e) >> 2;
     const uint32_t row = q * 32 + lane;
     const uint32_t grow = qt * BMQ + row;
     const bool row_ok = grow < a.T;
     const float inv = 1.0f / *a.divisor;
     const float *mrow =
         (a.mask && !causal && row_ok) ? a.mask + static_cast<size_t>(grow) * a.T : nullptr;
-    // keys past `lim` are masked: past T, or (causal) past this row
+    // keys from `lim` on are masked: past T, or (causal) past this row
     const uint32_t lim = causal ? min(a.T, grow + 1) : a.T;
     const uint32_t lane_base = (q * 32u) << 16;
     const uint32_t npieces = nk_eff / 16;
-    float *red_m = reinterpret_cast<float *>(s_q);  // [4][128], Q is dead by then
-    float *red_s = red_m + 4 * BMQ;
     bool ok = ptx::mbar_wait_bounded(bar_s, 0, kWaitLimitNs);
     if (!__all_sync(0xffffffffu, ok)) {
       if (lane == 0) timeout();
@@ -327,7 +364,7 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
     float m = -INFINITY;
     if (ok) {
       ptx::tc_fence_after();
-      for (uint32_t c = quarter; c < npieces; c += 4) {
+      for (uint32_t c = half; c < npieces; c += 2) {
         uint32_t r[16];
         ptx::tmem_load_32x32b_x16(tmem_s + lane_base + c * 16, r);
         ptx::tmem_load_wait();
@@ -336,14 +373,14 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) m = fmaxf(m, x[j]);
       }
-      red_m[quarter * BMQ + row] = m;
+      red_m[half * BMQ + row] = m;
     }
     ptx::named_bar_sync(1, 32 * kSoftWarps);
     float sum = 0.0f;
     if (ok) {
-      m = fmaxf(fmaxf(red_m[row], red_m[BMQ + row]), fmaxf(red_m[2 * BMQ + row], red_m[3 * BMQ + row]));
+      m = fmaxf(red_m[row], red_m[BMQ + row]);
       const float ml = m * kLog2e;
-      for (uint32_t c = quarter; c < npieces; c += 4) {
+      for (uint32_t c = half; c < npieces; c += 2) {
         uint32_t r[16];
         ptx::tmem_load_32x32b_x16(tmem_s + lane_base + c * 16, r);
         ptx::tmem_load_wait();
@@ -352,94 +389,91 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) sum += ptx::ex2_approx(fmaf(x[j], kLog2e, -ml));
       }
-      red_s[quarter * BMQ + row] = sum;
+      red_s[half * BMQ + row] = sum;
     }
     ptx::named_bar_sync(1, 32 * kSoftWarps);
     if (ok) {
-      // every warp adds the four partial sums in the same order
-      sum = ((red_s[row] + red_s[BMQ + row]) + red_s[2 * BMQ + row]) + red_s[3 * BMQ + row];
+      sum = red_s[row] + red_s[BMQ + row];  // same order in both halves
       const float inv_sum = 1.0f / sum;
       const float ml = m * kLog2e;
-      // every piece of P: those past nk_eff are zeros (stored, not multiplied)
-      for (uint32_t c = quarter; c < a.nk / 16; c += 4) {
-        uint8_t *blk = s_p + (c >> 1) * BMQ * 128;
-        if (c < npieces) {
+      for (uint32_t c = 0; c < nkb; ++c) {
+        const uint32_t slot = c & 1, use = c >> 1;
+        const uint32_t piece = 2 * c + half;
+        float4 v[4];
+        if (piece < npieces) {
           uint32_t r[16];
-          ptx::tmem_load_32x32b_x16(tmem_s + lane_base + c * 16, r);
+          ptx::tmem_load_32x32b_x16(tmem_s + lane_base + piece * 16, r);
           ptx::tmem_load_wait();
           float x[16];
-          score16(r, inv, mrow, c * 16, a.T, lim, x);
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            float4 v;
-            v.x = ptx::ex2_approx(fmaf(x[4 * g], kLog2e, -ml)) * inv_sum;
-            v.y = ptx::ex2_approx(fmaf(x[4 * g + 1], kLog2e, -ml)) * inv_sum;
-            v.z = ptx::ex2_approx(fmaf(x[4 * g + 2], kLog2e, -ml)) * inv_sum;
-            v.w = ptx::ex2_approx(fmaf(x[4 * g + 3], kLog2e, -ml)) * inv_sum;
-            *reinterpret_cast<float4 *>(blk + swz(row, (c & 1) * 4 + g)) = v;
-          }
-        } else {
+          score16(r, inv, mrow, piece * 16, a.T, lim, x);
 #pragma unroll
           for (int g = 0; g < 4; ++g)
-            *reinterpret_cast<float4 *>(blk + swz(row, (c & 1) * 4 + g)) =
-                make_float4(0.f, 0.f, 0.f, 0.f);
+            v[g] = make_float4(ptx::ex2_approx(fmaf(x[4 * g], kLog2e, -ml)) * inv_sum,
+                               ptx::ex2_approx(fmaf(x[4 * g + 1], kLog2e, -ml)) * inv_sum,
+                               ptx::ex2_approx(fmaf(x[4 * g + 2], kLog2e, -ml)) * inv_sum,
+                               ptx::ex2_approx(fmaf(x[4 * g + 3], kLog2e, -ml)) * inv_sum);
+        } else {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) v[g] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
+        if (use > 0) {  // the slot's previous block is stored and multiplied
+          const bool freed = ptx::mbar_wait_bounded(&mma_done[slot], (use - 1) & 1, kWaitLimitNs) &&
+                             ptx::mbar_wait_bounded(&store_done[slot], (use - 1) & 1, kWaitLimitNs);
+          if (!__all_sync(0xffffffffu, freed)) {
+            if (lane == 0) timeout();
+            ok = false;
+            break;
+          }
+        }
+        uint8_t *blk = s_ring + slot * kBlock;
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+          *reinterpret_cast<float4 *>(blk + swz(row, half * 4 + g)) = v[g];
         ptx::fence_proxy_async_smem();
-        ptx::mbar_arrive(&bar_p[c >> 1]);
+        ptx::mbar_arrive(&full[slot]);
       }
     }
-    // P to global: every block is complete once all softmax warps are here
-    ptx::named_bar_sync(1, 32 * kSoftWarps);
-    if (ok && e == 0 && lane == 0) {
-      for (uint32_t c = 0; c < a.nk / 32; ++c)
-        ptx::tma_store_3d(&maps.p, s_p + c * BMQ * 128, static_cast<int32_t>(c * 32), q0,
-                          static_cast<int32_t>(bh));
-      ptx::bulk_commit_group();
-    }
-    // O: TMEM -> global, each warp of a quadrant 16 of the 64 columns
+    // O: TMEM -> global, each warp of a quadrant 32 of the 64 columns
     ok = ok && ptx::mbar_wait_bounded(bar_o, 0, kWaitLimitNs);
     if (__all_sync(0xffffffffu, ok) && !*abort_flag) {
       ptx::tc_fence_after();
-      store_row16(tmem_o + lane_base + quarter * 16, a.o, bb, hh, grow, quarter * 16, row_ok);
+      store_row32(tmem_o + lane_base + half * 32, a.o, bb, hh, grow, half * 32, row_ok);
     } else if (lane == 0 && !ok) {
       timeout();
     }
-    if (e == 0 && lane == 0) ptx::bulk_wait_group<0>();
   }
 
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
-  if (warp == 1) ptx::tmem_dealloc(tmem, 512);
+  if (warp == 1) ptx::tmem_dealloc(tmem, kTmemCols);
 }
 
 // ------------------------------------------------------ backward, query side
 struct BwdQMaps {
-  CUtensorMap d_o, v, k, p, ds;
+  CUtensorMap d_o, v, k, ds;
 };
 
 struct BwdQArgs {
   uint32_t T, H, nk, qtiles;
-  const float *divisor;
+  const float *divisor, *p;
   Out dq;
   uint32_t *status;
 };
 
 template <bool KT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
 attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
-  uint8_t *s_do = smem + kTile, *s_v = smem + kOp1, *s_k = smem + kOp2, *s_p = smem + kScores;
+  // region A: dO and V for dP, then K and the dS ring for dQ
+  uint8_t *s_do = smem, *s_v = smem + kRegQ, *s_k = smem, *s_ring = smem + kRingOff;
+  float *red = reinterpret_cast<float *>(smem + kRed);  // [2][128] partial row sums
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBars);
-  uint64_t *bar_a = bars, *bar_k = bars + 1, *bar_pl = bars + 2, *bar_dp = bars + 3,
-           *bar_dq = bars + 4;
-  uint64_t *bar_ds = bars + 5;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar_ds + kMaxFusedKeys / 32);
+  uint64_t *bar_a = bars, *bar_k = bars + 1, *bar_dp = bars + 2, *bar_dq = bars + 3;
+  uint64_t *full = bars + 4, *mma_done = bars + 6, *store_done = bars + 8;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 10);
   volatile uint32_t *abort_flag = tmem_slot + 1;
-  // partial row sums of the four warps of a quadrant ([4][128]), exchanged
-  // after pass 1 (dO is dead by then)
-  float *red = reinterpret_cast<float *>(s_do);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const uint32_t nkb = a.nk / 32;
@@ -449,25 +483,28 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
   const int32_t q0 = static_cast<int32_t>(qt * BMQ);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 5; ++i) ptx::mbar_init(&bars[i], 1);
-    for (uint32_t c = 0; c < nkb; ++c) ptx::mbar_init(&bar_ds[c], 2 * 4 * 32);
+    for (int i = 0; i < 4; ++i) ptx::mbar_init(&bars[i], 1);
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(&full[i], kSoftWarps * 32);
+      ptx::mbar_init(&mma_done[i], 1);
+      ptx::mbar_init(&store_done[i], 1);
+    }
     *abort_flag = 0;
     ptx::fence_barrier_init();
     ptx::prefetch_tensormap(&maps.d_o);
     ptx::prefetch_tensormap(&maps.v);
     ptx::prefetch_tensormap(&maps.k);
-    ptx::prefetch_tensormap(&maps.p);
     ptx::prefetch_tensormap(&maps.ds);
   }
   if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, 512);
+    ptx::tmem_alloc(tmem_slot, kTmemCols);
     ptx::tmem_relinquish();
   }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_dp = tmem, tmem_dq = tmem + 256;
+  const uint32_t tmem_dp = tmem, tmem_dq = tmem + kMaxFusedKeys;
   pdl_enter();
 
   auto timeout = [&]() {
@@ -478,32 +515,44 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
   if (warp == 0) {
     if (lane == 0) {
       const uint32_t kbytes = a.nk * HD * 4;
+      bool ok = true;
       ptx::mbar_arrive_expect_tx(bar_a, 2 * BMQ * 128 + kbytes);
       for (int kb = 0; kb < 2; ++kb) {
         const int32_t cd[4] = {32 * kb, q0, hh, bb};
         ptx::tma_load_rank(s_do + kb * BMQ * 128, &maps.d_o, bar_a, 4, cd);
       }
       load_rows_kmajor(s_v, &maps.v, bar_a, a.nk, hh, bb);
-      ptx::mbar_arrive_expect_tx(bar_pl, nkb * BMQ * 128);
-      for (uint32_t c = 0; c < nkb; ++c)
-        ptx::tma_load_3d(s_p + c * BMQ * 128, &maps.p, bar_pl, static_cast<int32_t>(c * 32), q0,
-                         static_cast<int32_t>(bh));
-      ptx::mbar_arrive_expect_tx(bar_k, kbytes);
-      if (KT)
-        load_trans_blocks(s_k, &maps.k, bar_k, a.nk, hh, bb);
-      else
-        load_rows_mnmajor(s_k, &maps.k, bar_k, hh, bb);
-      if (!ptx::mbar_wait_bounded(bar_a, 0, kWaitLimitNs) ||
-          !ptx::mbar_wait_bounded(bar_pl, 0, kWaitLimitNs) ||
-          !ptx::mbar_wait_bounded(bar_k, 0, kWaitLimitNs))
-        timeout();
+      ok = ptx::mbar_wait_bounded(bar_dp, 0, kWaitLimitNs);  // dO, V consumed
+      if (ok) {
+        ptx::mbar_arrive_expect_tx(bar_k, kbytes);
+        if (KT)
+          load_trans_blocks(s_k, &maps.k, bar_k, a.nk, hh, bb);
+        else
+          load_rows_mnmajor(s_k, &maps.k, bar_k, hh, bb);
+      }
+      for (uint32_t c = 0; c < nkb && ok; ++c) {
+        const uint32_t slot = c & 1, use = c >> 1;
+        if (!ptx::mbar_wait_bounded(&full[slot], use & 1, kWaitLimitNs)) {
+          ok = false;
+          break;
+        }
+        ptx::tma_store_3d(&maps.ds, s_ring + slot * kBlock, static_cast<int32_t>(c * 32), q0,
+                          static_cast<int32_t>(bh));
+        ptx::bulk_commit_group();
+        ptx::bulk_wait_group_read<0>();
+        ptx::mbar_arrive(&store_done[slot]);
+      }
+      if (ok) ok = ptx::mbar_wait_bounded(bar_k, 0, kWaitLimitNs);
+      if (!ok) timeout();
+      ptx::bulk_wait_group<0>();
     }
   } else if (warp == 1) {
     if (lane == 0) {
       bool issued = false;
       const uint32_t sdo = ptx::smem_addr(s_do), sv = ptx::smem_addr(s_v);
-      const uint32_t sk = ptx::smem_addr(s_k), sp = ptx::smem_addr(s_p);
-      if (ptx::mbar_wait_bounded(bar_a, 0, kWaitLimitNs)) {
+      const uint32_t sk = ptx::smem_addr(s_k), sr = ptx::smem_addr(s_ring);
+      bool ok = ptx::mbar_wait_bounded(bar_a, 0, kWaitLimitNs);
+      if (ok) {
         ptx::tc_fence_after();
         const uint32_t idesc_p = ptx::idesc_tf32(BMQ, a.nk, false, false);
 #pragma unroll
@@ -518,43 +567,57 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
                           idesc_p, (kb | kk) ? 1u : 0u);
         issued = true;
         ptx::mma_commit(bar_dp);
-        bool ok = ptx::mbar_wait_bounded(bar_k, 0, kWaitLimitNs);
-        const uint32_t idesc_q = ptx::idesc_tf32(BMQ, HD, false, !KT);
-        for (uint32_t c = 0; c < nkb && ok; ++c) {
-          if (!ptx::mbar_wait_bounded(&bar_ds[c], 0, kWaitLimitNs)) {
-            ok = false;
-            break;
-          }
-          ptx::tc_fence_after();
-#pragma unroll
-          for (uint32_t kk = 0; kk < 4; ++kk) {
-            const uint64_t bd =
-                KT ? ptx::smem_desc(sk + c * HD * 128 + kk * 32, 16, 1024, ptx::kSwizzle128B)
-                   : ptx::smem_desc(sk + (c * 32 + kk * 8) * 128, a.nk * 128, 512,
-                                    ptx::kSwizzle128B32BAtom);
-            ptx::mma_tf32(tmem_dq,
-                          ptx::smem_desc(sp + c * BMQ * 128 + kk * 32, 16, 1024,
-                                         ptx::kSwizzle128B),
-                          bd, idesc_q, (c | kk) ? 1u : 0u);
-          }
-        }
-        if (!ok) timeout();
-        ptx::mma_commit(bar_dq);
-      } else {
-        timeout();
+        ok = ptx::mbar_wait_bounded(bar_k, 0, kWaitLimitNs);
       }
-      if (issued) ptx::mbar_wait_bounded(bar_dq, 0, kWaitLimitNs);
+      const uint32_t idesc_q = ptx::idesc_tf32(BMQ, HD, false, !KT);
+      for (uint32_t c = 0; c < nkb && ok; ++c) {
+        const uint32_t slot = c & 1, use = c >> 1;
+        if (!ptx::mbar_wait_bounded(&full[slot], use & 1, kWaitLimitNs)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+#pragma unroll
+        for (uint32_t kk = 0; kk < 4; ++kk) {
+          const uint64_t bd =
+              KT ? ptx::smem_desc(sk + c * HD * 128 + kk * 32, 16, 1024, ptx::kSwizzle128B)
+                 : ptx::smem_desc(sk + (c * 32 + kk * 8) * 128, a.nk * 128, 512,
+                                  ptx::kSwizzle128B32BAtom);
+          ptx::mma_tf32(tmem_dq,
+                        ptx::smem_desc(sr + slot * kBlock + kk * 32, 16, 1024, ptx::kSwizzle128B),
+                        bd, idesc_q, (c | kk) ? 1u : 0u);
+        }
+        ptx::mma_commit(&mma_done[slot]);
+      }
+      if (!ok) timeout();
+      if (issued) {
+        ptx::mma_commit(bar_dq);
+        ptx::mbar_wait_bounded(bar_dq, 0, kWaitLimitNs);
+      } else {
+        ptx::mbar_arrive(bar_dq);
+      }
     }
   } else {
+    // ----------------------------------------------- softmax derivative
     const int e = warp - 2;
-    const uint32_t q = warp & 3, quarter = static_cast<uint32_t>(e) >> 2;
+    const uint32_t q = warp & 3, half = static_cast<uint32_t>(e) >> 2;
     const uint32_t row = q * 32 + lane;
     const uint32_t grow = qt * BMQ + row;
+    const bool row_ok = grow < a.T;
     const float inv = 1.0f / *a.divisor;
     const uint32_t lane_base = (q * 32u) << 16;
     const uint32_t npieces = a.nk / 16;
-    bool ok = ptx::mbar_wait_bounded(bar_dp, 0, kWaitLimitNs) &&
-              ptx::mbar_wait_bounded(bar_pl, 0, kWaitLimitNs);
+    // this row of P (rows past T read as zeros)
+    const float *prow = a.p + (static_cast<size_t>(bh) * a.T + (row_ok ? grow : 0)) * a.T;
+    auto p16 = [&](uint32_t piece, float4 (&pv)[4]) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const uint32_t c = piece * 16 + 4 * g;
+        pv[g] = row_ok && c < a.T ? *reinterpret_cast<const float4 *>(prow + c)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    };
+    bool ok = ptx::mbar_wait_bounded(bar_dp, 0, kWaitLimitNs);
     if (!__all_sync(0xffffffffu, ok)) {
       if (lane == 0) timeout();
       ok = false;
@@ -562,66 +625,70 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
     float sum = 0.0f;
     if (ok) {
       ptx::tc_fence_after();
-      for (uint32_t c = quarter; c < npieces; c += 4) {
+      for (uint32_t c = half; c < npieces; c += 2) {
+        float4 pv[4];
+        p16(c, pv);
         uint32_t r[16];
         ptx::tmem_load_32x32b_x16(tmem_dp + lane_base + c * 16, r);
         ptx::tmem_load_wait();
-        const uint8_t *blk = s_p + (c >> 1) * BMQ * 128;
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          const float4 p4 = *reinterpret_cast<const float4 *>(blk + swz(row, (c & 1) * 4 + g));
-          sum = fmaf(__uint_as_float(r[4 * g]), p4.x, sum);
-          sum = fmaf(__uint_as_float(r[4 * g + 1]), p4.y, sum);
-          sum = fmaf(__uint_as_float(r[4 * g + 2]), p4.z, sum);
-          sum = fmaf(__uint_as_float(r[4 * g + 3]), p4.w, sum);
+          sum = fmaf(__uint_as_float(r[4 * g]), pv[g].x, sum);
+          sum = fmaf(__uint_as_float(r[4 * g + 1]), pv[g].y, sum);
+          sum = fmaf(__uint_as_float(r[4 * g + 2]), pv[g].z, sum);
+          sum = fmaf(__uint_as_float(r[4 * g + 3]), pv[g].w, sum);
         }
       }
-      red[quarter * BMQ + row] = sum;
+      red[half * BMQ + row] = sum;
     }
     ptx::named_bar_sync(1, 32 * kSoftWarps);
     if (ok) {
-      // every warp adds the four partial sums in the same order
-      sum = ((red[row] + red[BMQ + row]) + red[2 * BMQ + row]) + red[3 * BMQ + row];
-      for (uint32_t c = quarter; c < npieces; c += 4) {
+      sum = red[row] + red[BMQ + row];  // same order in both halves
+      for (uint32_t c = 0; c < nkb; ++c) {
+        const uint32_t slot = c & 1, use = c >> 1;
+        const uint32_t piece = 2 * c + half;
+        float4 pv[4];
+        p16(piece, pv);
         uint32_t r[16];
-        ptx::tmem_load_32x32b_x16(tmem_dp + lane_base + c * 16, r);
+        ptx::tmem_load_32x32b_x16(tmem_dp + lane_base + piece * 16, r);
         ptx::tmem_load_wait();
-        uint8_t *blk = s_p + (c >> 1) * BMQ * 128;
+        float4 v[4];
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          float4 *slot = reinterpret_cast<float4 *>(blk + swz(row, (c & 1) * 4 + g));
-          const float4 p4 = *slot;
-          *slot = make_float4(p4.x * (__uint_as_float(r[4 * g]) - sum) * inv,
-                              p4.y * (__uint_as_float(r[4 * g + 1]) - sum) * inv,
-                              p4.z * (__uint_as_float(r[4 * g + 2]) - sum) * inv,
-                              p4.w * (__uint_as_float(r[4 * g + 3]) - sum) * inv);
+        for (int g = 0; g < 4; ++g)
+          v[g] = make_float4(pv[g].x * (__uint_as_float(r[4 * g]) - sum) * inv,
+                             pv[g].y * (__uint_as_float(r[4 * g + 1]) - sum) * inv,
+                             pv[g].z * (__uint_as_float(r[4 * g + 2]) - sum) * inv,
+                             pv[g].w * (__uint_as_float(r[4 * g + 3]) - sum) * inv);
+        if (use > 0) {
+          const bool freed = ptx::mbar_wait_bounded(&mma_done[slot], (use - 1) & 1, kWaitLimitNs) &&
+                             ptx::mbar_wait_bounded(&store_done[slot], (use - 1) & 1, kWaitLimitNs);
+          if (!__all_sync(0xffffffffu, freed)) {
+            if (lane == 0) timeout();
+            ok = false;
+            break;
+          }
         }
+        uint8_t *blk = s_ring + slot * kBlock;
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+          *reinterpret_cast<float4 *>(blk + swz(row, half * 4 + g)) = v[g];
         ptx::fence_proxy_async_smem();
-        ptx::mbar_arrive(&bar_ds[c >> 1]);
+        ptx::mbar_arrive(&full[slot]);
       }
-    }
-    ptx::named_bar_sync(1, 32 * kSoftWarps);
-    if (ok && e == 0 && lane == 0) {
-      for (uint32_t c = 0; c < a.nk / 32; ++c)
-        ptx::tma_store_3d(&maps.ds, s_p + c * BMQ * 128, static_cast<int32_t>(c * 32), q0,
-                          static_cast<int32_t>(bh));
-      ptx::bulk_commit_group();
     }
     ok = ok && ptx::mbar_wait_bounded(bar_dq, 0, kWaitLimitNs);
     if (__all_sync(0xffffffffu, ok) && !*abort_flag) {
       ptx::tc_fence_after();
-      store_row16(tmem_dq + lane_base + quarter * 16, a.dq, bb, hh, grow, quarter * 16,
-                  grow < a.T);
+      store_row32(tmem_dq + lane_base + half * 32, a.dq, bb, hh, grow, half * 32, row_ok);
     } else if (lane == 0 && !ok) {
       timeout();
     }
-    if (e == 0 && lane == 0) ptx::bulk_wait_group<0>();
   }
 
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
-  if (warp == 1) ptx::tmem_dealloc(tmem, 512);
+  if (warp == 1) ptx::tmem_dealloc(tmem, kTmemCols);
 }
 
 // -------------------------------------------------------- backward, key side
@@ -938,10 +1005,10 @@ int launch_attention_bwd_q_tc(const AttnDims &d, const HeadView &d_o, const Head
   a.status = device_status_ptr();
   if (!a.status) return fail(TL_ERR_CUDA, "attention backward: no status word");
   const bool kt = k.trans;
+  a.p = p;
   const bool maps_ok = rows_map(&maps.d_o, d_o, d, BMQ) && rows_map(&maps.v, v, d, a.nk) &&
                        (kt ? trans_map(&maps.k, k, d, CU_TENSOR_MAP_SWIZZLE_128B)
                            : rows_map_mn(&maps.k, k, d, a.nk)) &&
-                       scores_map(&maps.p, p, d, BMQ, CU_TENSOR_MAP_SWIZZLE_128B) &&
                        scores_map(&maps.ds, ds, d, BMQ, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!maps_ok) return fail(TL_ERR_UNSUPPORTED, "attention backward: tensor maps refused");
   static bool attr[2] = {false, false};
