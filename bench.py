@@ -47,6 +47,10 @@ def parse_args():
     p.add_argument("--no-fusion", action="store_true")
     p.add_argument("--no-graphs", action="store_true")
     p.add_argument("--profile", default="", help="write the per-op profile JSON here")
+    p.add_argument("--kernel", choices=["gemm", "attention"], default="",
+                   help="time one kernel case instead of the training step (profiling "
+                        "driver): a tl_gemm shape, or configuration 3's attention")
+    p.add_argument("--shape", default="12288x384x384:NN", help="--kernel gemm: MxNxK:form")
     return p.parse_args()
 
 
@@ -229,10 +233,82 @@ def measure_tf32_peak(torch):
 
 
 # ----------------------------------------------------------------- main arm
+def run_kernel_case(args):
+    """One kernel case on cuda:0, --warmup untimed then --steps timed launches
+    (CUDA events, L2 flushed between launches); one JSON line.  gemm: tl_gemm
+    on the --shape operands (N(0,1), TF32).  attention: configuration 3
+    (B 64, H 6, T 192, D 64, causal, divisor 8) through tl_attention_fwd and
+    tl_attention_bwd."""
+    import torch
+    from templit_b200 import capi
+    lib = capi.cuda_lib()
+    dev = torch.device("cuda", 0)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def timed(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        ts = []
+        for _ in range(args.steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b) * 1e3)
+        return float(np.median(ts))
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    if args.kernel == "gemm":
+        dims, form = args.shape.split(":")
+        m, n, k = (int(v) for v in dims.split("x"))
+        ta, tb = form[0] == "T", form[1] == "T"
+        a = torch.randn((k, m) if ta else (m, k), device=dev, generator=g)
+        b = torch.randn((n, k) if tb else (k, n), device=dev, generator=g)
+        c = torch.zeros((m, n), device=dev)
+        d = capi.TlGemmDesc(a=a.data_ptr(), b=b.data_ptr(), c=c.data_ptr(), m=m, n=n, k=k,
+                            trans_a=int(ta), trans_b=int(tb), precision=capi.TL_GEMM_TF32)
+        wsb = lib.tl_gemm_workspace_size(ctypes.byref(d))
+        ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
+        d.workspace, d.workspace_bytes = ws.data_ptr(), wsb
+        us = timed(lambda: capi.check(lib.tl_gemm(ctypes.byref(d), stream), lib, "tl_gemm"))
+        line = {"kernel": "tl_gemm", "shape": args.shape, "us_per_launch": round(us, 2),
+                "tflops": round(2.0 * m * n * k / us / 1e6, 1)}
+    else:
+        B, H, T, D = 64, 6, 192, 64
+        q, k, v, d_o = (torch.randn(B, H, T, D, device=dev, generator=g) for _ in range(4))
+        mask = torch.triu(torch.full((T, T), float("-inf"), device=dev), 1)
+        div = torch.tensor([8.0], device=dev)
+        p = torch.empty(B, H, T, T, device=dev)
+        o, dq, dk, dv = (torch.empty_like(q) for _ in range(4))
+        ws = torch.empty(lib.tl_attention_workspace_size(B, T, H, D), dtype=torch.uint8,
+                         device=dev)
+        P = lambda t: ctypes.c_void_p(t.data_ptr())
+        fwd = lambda: capi.check(lib.tl_attention_fwd(
+            P(q), P(k), P(v), P(div), P(mask), P(p), P(o), B, T, H, D, capi.TL_ATTN_BHTD,
+            capi.TL_GEMM_TF32, P(ws), ws.numel(), stream), lib, "tl_attention_fwd")
+        bwd = lambda: capi.check(lib.tl_attention_bwd(
+            P(q), P(k), P(v), P(p), P(div), P(d_o), P(dq), P(dk), P(dv), B, T, H, D,
+            capi.TL_ATTN_BHTD, capi.TL_GEMM_TF32, P(ws), ws.numel(), stream), lib,
+            "tl_attention_bwd")
+        fwd()
+        us_f, us_b = timed(fwd), timed(bwd)
+        flops = 4.0 * B * H * T * T * D  # dense count
+        line = {"kernel": "tl_attention (configuration 3, causal)", "fwd_us": round(us_f, 2),
+                "bwd_us": round(us_b, 2), "fwd_tflops_dense": round(flops / us_f / 1e6, 1),
+                "bwd_tflops_dense": round(2 * flops / us_b / 1e6, 1)}
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.kernel:
+        return run_kernel_case(args)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -111,10 +111,16 @@ __device__ __forceinline__ void store_row16(uint32_t taddr, const Out &o, int32_
 
 // Scores of 16 columns of one row: s / divisor (as s * (1 / divisor)) +
 // mask (a mask row, when given); columns from `lim` on (past T, or past the
-// row under a causal mask) are -inf.
+// row under a causal mask) are -inf.  `open`: no mask row and every column
+// below `lim` (warp-uniform), so neither is looked at.
 __device__ __forceinline__ void score16(const uint32_t (&r)[16], float inv, const float *mrow,
-                                        uint32_t col0, uint32_t T, uint32_t lim,
+                                        uint32_t col0, uint32_t T, uint32_t lim, bool open,
                                         float (&x)[16]) {
+  if (open) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[j] = __uint_as_float(r[j]) * inv;
+    return;
+  }
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
     float4 mk = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -361,7 +367,13 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
       if (lane == 0) timeout();
       ok = false;
     }
-    float m = -INFINITY;
+    // the row of lane 0 has the warp's smallest `lim`: pieces wholly below
+    // it need no masking
+    const uint32_t lim_lo = __shfl_sync(0xffffffffu, lim, 0);
+    auto open = [&](uint32_t piece) { return !mrow && (piece + 1) * 16 <= lim_lo; };
+    // one pass over S: an online (max, sum of 2^((x - max) log2 e)) per row,
+    // rescaled once per 16-key piece
+    float m = -INFINITY, sum = 0.0f;
     if (ok) {
       ptx::tc_fence_after();
       for (uint32_t c = half; c < npieces; c += 2) {
@@ -369,31 +381,33 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
         ptx::tmem_load_32x32b_x16(tmem_s + lane_base + c * 16, r);
         ptx::tmem_load_wait();
         float x[16];
-        score16(r, inv, mrow, c * 16, a.T, lim, x);
+        score16(r, inv, mrow, c * 16, a.T, lim, open(c), x);
+        float pm = x[0];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) m = fmaxf(m, x[j]);
+        for (int j = 1; j < 16; ++j) pm = fmaxf(pm, x[j]);
+        const float mn = fmaxf(m, pm);
+        if (mn != -INFINITY) {
+          const float ml = mn * kLog2e;
+          float ps = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) ps += ptx::ex2_approx(fmaf(x[j], kLog2e, -ml));
+          sum = fmaf(sum, ptx::ex2_approx(fmaf(m, kLog2e, -ml)), ps);
+          m = mn;
+        }
       }
       red_m[half * BMQ + row] = m;
-    }
-    ptx::named_bar_sync(1, 32 * kSoftWarps);
-    float sum = 0.0f;
-    if (ok) {
-      m = fmaxf(red_m[row], red_m[BMQ + row]);
-      const float ml = m * kLog2e;
-      for (uint32_t c = half; c < npieces; c += 2) {
-        uint32_t r[16];
-        ptx::tmem_load_32x32b_x16(tmem_s + lane_base + c * 16, r);
-        ptx::tmem_load_wait();
-        float x[16];
-        score16(r, inv, mrow, c * 16, a.T, lim, x);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) sum += ptx::ex2_approx(fmaf(x[j], kLog2e, -ml));
-      }
       red_s[half * BMQ + row] = sum;
     }
     ptx::named_bar_sync(1, 32 * kSoftWarps);
     if (ok) {
-      sum = red_s[row] + red_s[BMQ + row];  // same order in both halves
+      // both halves merge in the same order, so they agree on (max, sum)
+      const float m0 = red_m[row], m1 = red_m[BMQ + row];
+      const float s0 = red_s[row], s1 = red_s[BMQ + row];
+      m = fmaxf(m0, m1);
+      const float ml0 = m * kLog2e;
+      sum = m == -INFINITY ? 0.0f
+                           : s0 * ptx::ex2_approx(fmaf(m0, kLog2e, -ml0)) +
+                                 s1 * ptx::ex2_approx(fmaf(m1, kLog2e, -ml0));
       const float inv_sum = 1.0f / sum;
       const float ml = m * kLog2e;
       for (uint32_t c = 0; c < nkb; ++c) {
@@ -405,7 +419,7 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
           ptx::tmem_load_32x32b_x16(tmem_s + lane_base + piece * 16, r);
           ptx::tmem_load_wait();
           float x[16];
-          score16(r, inv, mrow, piece * 16, a.T, lim, x);
+          score16(r, inv, mrow, piece * 16, a.T, lim, open(piece), x);
 #pragma unroll
           for (int g = 0; g < 4; ++g)
             v[g] = make_float4(ptx::ex2_approx(fmaf(x[4 * g], kLog2e, -ml)) * inv_sum,
@@ -451,28 +465,33 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
 
 // ------------------------------------------------------ backward, query side
 struct BwdQMaps {
-  CUtensorMap d_o, v, k, ds;
+  CUtensorMap d_o, v, k, p, ds;
 };
 
 struct BwdQArgs {
   uint32_t T, H, nk, qtiles;
-  const float *divisor, *p;
+  const float *divisor;
   Out dq;
   uint32_t *status;
 };
 
+// Rows of P stream through the two-slot ring twice: once for rowsum(dP * P),
+// once to turn each block into dS in place (then multiplied by K for dQ and
+// TMA-stored).  Use i of the ring (i = 0 .. 2 nkb - 1) loads P block
+// i % nkb into slot i % 2; pass-2 block c is use nkb + c.
 template <bool KT>
 __global__ void __launch_bounds__(kThreads, 2)
 attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
+  constexpr uint32_t S = 2;  // ring slots
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
-  // region A: dO and V for dP, then K and the dS ring for dQ
+  // region A: dO and V for dP, then K and the ring for dQ
   uint8_t *s_do = smem, *s_v = smem + kRegQ, *s_k = smem, *s_ring = smem + kRingOff;
   float *red = reinterpret_cast<float *>(smem + kRed);  // [2][128] partial row sums
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBars);
   uint64_t *bar_a = bars, *bar_k = bars + 1, *bar_dp = bars + 2, *bar_dq = bars + 3;
-  uint64_t *full = bars + 4, *mma_done = bars + 6, *store_done = bars + 8;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 10);
+  uint64_t *loaded = bars + 4, *consumed = bars + 6, *full = bars + 8, *mma_done = bars + 10;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
   volatile uint32_t *abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -484,16 +503,18 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 4; ++i) ptx::mbar_init(&bars[i], 1);
-    for (int i = 0; i < 2; ++i) {
+    for (uint32_t i = 0; i < S; ++i) {
+      ptx::mbar_init(&loaded[i], 1);
+      ptx::mbar_init(&consumed[i], kSoftWarps * 32);
       ptx::mbar_init(&full[i], kSoftWarps * 32);
       ptx::mbar_init(&mma_done[i], 1);
-      ptx::mbar_init(&store_done[i], 1);
     }
     *abort_flag = 0;
     ptx::fence_barrier_init();
     ptx::prefetch_tensormap(&maps.d_o);
     ptx::prefetch_tensormap(&maps.v);
     ptx::prefetch_tensormap(&maps.k);
+    ptx::prefetch_tensormap(&maps.p);
     ptx::prefetch_tensormap(&maps.ds);
   }
   if (warp == 1) {
@@ -513,16 +534,16 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
   };
 
   if (warp == 0) {
+    // ------------------------------ loads, the P stream and the dS stores
     if (lane == 0) {
       const uint32_t kbytes = a.nk * HD * 4;
-      bool ok = true;
       ptx::mbar_arrive_expect_tx(bar_a, 2 * BMQ * 128 + kbytes);
       for (int kb = 0; kb < 2; ++kb) {
         const int32_t cd[4] = {32 * kb, q0, hh, bb};
         ptx::tma_load_rank(s_do + kb * BMQ * 128, &maps.d_o, bar_a, 4, cd);
       }
       load_rows_kmajor(s_v, &maps.v, bar_a, a.nk, hh, bb);
-      ok = ptx::mbar_wait_bounded(bar_dp, 0, kWaitLimitNs);  // dO, V consumed
+      bool ok = ptx::mbar_wait_bounded(bar_dp, 0, kWaitLimitNs);  // dO, V consumed
       if (ok) {
         ptx::mbar_arrive_expect_tx(bar_k, kbytes);
         if (KT)
@@ -530,18 +551,37 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
         else
           load_rows_mnmajor(s_k, &maps.k, bar_k, hh, bb);
       }
-      for (uint32_t c = 0; c < nkb && ok; ++c) {
-        const uint32_t slot = c & 1, use = c >> 1;
-        if (!ptx::mbar_wait_bounded(&full[slot], use & 1, kWaitLimitNs)) {
-          ok = false;
-          break;
-        }
+      uint32_t stored = 0;  // pass-2 blocks stored so far
+      auto store = [&](uint32_t c) -> bool {
+        const uint32_t slot = (nkb + c) % S;
+        if (!ptx::mbar_wait_bounded(&full[slot], (c / S) & 1, kWaitLimitNs)) return false;
         ptx::tma_store_3d(&maps.ds, s_ring + slot * kBlock, static_cast<int32_t>(c * 32), q0,
                           static_cast<int32_t>(bh));
         ptx::bulk_commit_group();
-        ptx::bulk_wait_group_read<0>();
-        ptx::mbar_arrive(&store_done[slot]);
+        ++stored;
+        return true;
+      };
+      for (uint32_t i = 0; i < 2 * nkb && ok; ++i) {
+        const uint32_t slot = i % S;
+        if (i >= S) {  // the slot's previous use is over
+          const uint32_t ip = i - S;
+          if (ip < nkb) {
+            ok = ptx::mbar_wait_bounded(&consumed[slot], (ip / S) & 1, kWaitLimitNs);
+          } else {
+            const uint32_t cp = ip - nkb;
+            ok = store(cp);
+            if (ok) {
+              ptx::bulk_wait_group_read<0>();
+              ok = ptx::mbar_wait_bounded(&mma_done[slot], (cp / S) & 1, kWaitLimitNs);
+            }
+          }
+          if (!ok) break;
+        }
+        ptx::mbar_arrive_expect_tx(&loaded[slot], kBlock);
+        ptx::tma_load_3d(s_ring + slot * kBlock, &maps.p, &loaded[slot],
+                         static_cast<int32_t>((i % nkb) * 32), q0, static_cast<int32_t>(bh));
       }
+      while (ok && stored < nkb) ok = store(stored);
       if (ok) ok = ptx::mbar_wait_bounded(bar_k, 0, kWaitLimitNs);
       if (!ok) timeout();
       ptx::bulk_wait_group<0>();
@@ -571,8 +611,8 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
       }
       const uint32_t idesc_q = ptx::idesc_tf32(BMQ, HD, false, !KT);
       for (uint32_t c = 0; c < nkb && ok; ++c) {
-        const uint32_t slot = c & 1, use = c >> 1;
-        if (!ptx::mbar_wait_bounded(&full[slot], use & 1, kWaitLimitNs)) {
+        const uint32_t slot = (nkb + c) % S;
+        if (!ptx::mbar_wait_bounded(&full[slot], (c / S) & 1, kWaitLimitNs)) {
           ok = false;
           break;
         }
@@ -603,20 +643,8 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
     const uint32_t q = warp & 3, half = static_cast<uint32_t>(e) >> 2;
     const uint32_t row = q * 32 + lane;
     const uint32_t grow = qt * BMQ + row;
-    const bool row_ok = grow < a.T;
     const float inv = 1.0f / *a.divisor;
     const uint32_t lane_base = (q * 32u) << 16;
-    const uint32_t npieces = a.nk / 16;
-    // this row of P (rows past T read as zeros)
-    const float *prow = a.p + (static_cast<size_t>(bh) * a.T + (row_ok ? grow : 0)) * a.T;
-    auto p16 = [&](uint32_t piece, float4 (&pv)[4]) {
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const uint32_t c = piece * 16 + 4 * g;
-        pv[g] = row_ok && c < a.T ? *reinterpret_cast<const float4 *>(prow + c)
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    };
     bool ok = ptx::mbar_wait_bounded(bar_dp, 0, kWaitLimitNs);
     if (!__all_sync(0xffffffffu, ok)) {
       if (lane == 0) timeout();
@@ -625,19 +653,27 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
     float sum = 0.0f;
     if (ok) {
       ptx::tc_fence_after();
-      for (uint32_t c = half; c < npieces; c += 2) {
-        float4 pv[4];
-        p16(c, pv);
+      for (uint32_t c = 0; c < nkb; ++c) {
+        const uint32_t slot = c % S, piece = 2 * c + half;
         uint32_t r[16];
-        ptx::tmem_load_32x32b_x16(tmem_dp + lane_base + c * 16, r);
+        ptx::tmem_load_32x32b_x16(tmem_dp + lane_base + piece * 16, r);
+        const bool got = ptx::mbar_wait_bounded(&loaded[slot], (c / S) & 1, kWaitLimitNs);
         ptx::tmem_load_wait();
+        if (!__all_sync(0xffffffffu, got)) {
+          if (lane == 0) timeout();
+          ok = false;
+          break;
+        }
+        const uint8_t *blk = s_ring + slot * kBlock;
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          sum = fmaf(__uint_as_float(r[4 * g]), pv[g].x, sum);
-          sum = fmaf(__uint_as_float(r[4 * g + 1]), pv[g].y, sum);
-          sum = fmaf(__uint_as_float(r[4 * g + 2]), pv[g].z, sum);
-          sum = fmaf(__uint_as_float(r[4 * g + 3]), pv[g].w, sum);
+          const float4 p4 = *reinterpret_cast<const float4 *>(blk + swz(row, half * 4 + g));
+          sum = fmaf(__uint_as_float(r[4 * g]), p4.x, sum);
+          sum = fmaf(__uint_as_float(r[4 * g + 1]), p4.y, sum);
+          sum = fmaf(__uint_as_float(r[4 * g + 2]), p4.z, sum);
+          sum = fmaf(__uint_as_float(r[4 * g + 3]), p4.w, sum);
         }
+        ptx::mbar_arrive(&consumed[slot]);
       }
       red[half * BMQ + row] = sum;
     }
@@ -645,33 +681,26 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
     if (ok) {
       sum = red[row] + red[BMQ + row];  // same order in both halves
       for (uint32_t c = 0; c < nkb; ++c) {
-        const uint32_t slot = c & 1, use = c >> 1;
-        const uint32_t piece = 2 * c + half;
-        float4 pv[4];
-        p16(piece, pv);
+        const uint32_t i = nkb + c, slot = i % S, piece = 2 * c + half;
         uint32_t r[16];
         ptx::tmem_load_32x32b_x16(tmem_dp + lane_base + piece * 16, r);
+        const bool got = ptx::mbar_wait_bounded(&loaded[slot], (i / S) & 1, kWaitLimitNs);
         ptx::tmem_load_wait();
-        float4 v[4];
-#pragma unroll
-        for (int g = 0; g < 4; ++g)
-          v[g] = make_float4(pv[g].x * (__uint_as_float(r[4 * g]) - sum) * inv,
-                             pv[g].y * (__uint_as_float(r[4 * g + 1]) - sum) * inv,
-                             pv[g].z * (__uint_as_float(r[4 * g + 2]) - sum) * inv,
-                             pv[g].w * (__uint_as_float(r[4 * g + 3]) - sum) * inv);
-        if (use > 0) {
-          const bool freed = ptx::mbar_wait_bounded(&mma_done[slot], (use - 1) & 1, kWaitLimitNs) &&
-                             ptx::mbar_wait_bounded(&store_done[slot], (use - 1) & 1, kWaitLimitNs);
-          if (!__all_sync(0xffffffffu, freed)) {
-            if (lane == 0) timeout();
-            ok = false;
-            break;
-          }
+        if (!__all_sync(0xffffffffu, got)) {
+          if (lane == 0) timeout();
+          ok = false;
+          break;
         }
         uint8_t *blk = s_ring + slot * kBlock;
 #pragma unroll
-        for (int g = 0; g < 4; ++g)
-          *reinterpret_cast<float4 *>(blk + swz(row, half * 4 + g)) = v[g];
+        for (int g = 0; g < 4; ++g) {
+          float4 *slot4 = reinterpret_cast<float4 *>(blk + swz(row, half * 4 + g));
+          const float4 p4 = *slot4;
+          *slot4 = make_float4(p4.x * (__uint_as_float(r[4 * g]) - sum) * inv,
+                               p4.y * (__uint_as_float(r[4 * g + 1]) - sum) * inv,
+                               p4.z * (__uint_as_float(r[4 * g + 2]) - sum) * inv,
+                               p4.w * (__uint_as_float(r[4 * g + 3]) - sum) * inv);
+        }
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(&full[slot]);
       }
@@ -679,7 +708,7 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
     ok = ok && ptx::mbar_wait_bounded(bar_dq, 0, kWaitLimitNs);
     if (__all_sync(0xffffffffu, ok) && !*abort_flag) {
       ptx::tc_fence_after();
-      store_row32(tmem_dq + lane_base + half * 32, a.dq, bb, hh, grow, half * 32, row_ok);
+      store_row32(tmem_dq + lane_base + half * 32, a.dq, bb, hh, grow, half * 32, grow < a.T);
     } else if (lane == 0 && !ok) {
       timeout();
     }
@@ -1005,10 +1034,10 @@ int launch_attention_bwd_q_tc(const AttnDims &d, const HeadView &d_o, const Head
   a.status = device_status_ptr();
   if (!a.status) return fail(TL_ERR_CUDA, "attention backward: no status word");
   const bool kt = k.trans;
-  a.p = p;
   const bool maps_ok = rows_map(&maps.d_o, d_o, d, BMQ) && rows_map(&maps.v, v, d, a.nk) &&
                        (kt ? trans_map(&maps.k, k, d, CU_TENSOR_MAP_SWIZZLE_128B)
                            : rows_map_mn(&maps.k, k, d, a.nk)) &&
+                       scores_map(&maps.p, p, d, BMQ, CU_TENSOR_MAP_SWIZZLE_128B) &&
                        scores_map(&maps.ds, ds, d, BMQ, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!maps_ok) return fail(TL_ERR_UNSUPPORTED, "attention backward: tensor maps refused");
   static bool attr[2] = {false, false};
