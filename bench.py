@@ -47,7 +47,7 @@ def parse_args():
     p.add_argument("--no-fusion", action="store_true")
     p.add_argument("--no-graphs", action="store_true")
     p.add_argument("--profile", default="", help="write the per-op profile JSON here")
-    p.add_argument("--kernel", choices=["gemm", "attention"], default="",
+    p.add_argument("--kernel", choices=["gemm", "attention", "infer"], default="",
                    help="time one kernel case instead of the training step (profiling "
                         "driver): a tl_gemm shape, or configuration 3's attention")
     p.add_argument("--shape", default="12288x384x384:NN", help="--kernel gemm: MxNxK:form")
@@ -261,6 +261,8 @@ def run_kernel_case(args):
         return float(np.median(ts))
 
     g = torch.Generator(device=dev).manual_seed(0)
+    if args.kernel == "infer":
+        return run_inference_case(args)
     if args.kernel == "gemm":
         dims, form = args.shape.split(":")
         m, n, k = (int(v) for v in dims.split("x"))
@@ -299,6 +301,54 @@ def run_kernel_case(args):
         line = {"kernel": "tl_attention (configuration 3, causal)", "fwd_us": round(us_f, 2),
                 "bwd_us": round(us_b, 2), "fwd_tflops_dense": round(flops / us_f / 1e6, 1),
                 "bwd_tflops_dense": round(2 * flops / us_b / 1e6, 1)}
+    print(json.dumps(line))
+    return 0
+
+
+def run_inference_case(args):
+    """Forward-only generation (src/generate.cpp's set-up: batch 1, T 192,
+    top-k 40, temperature 0.6, minimum length 64) through tlg_infer_generate:
+    the reference's inference::autoregression recomputes the whole context
+    per token and samples on the host.  Wall-clock tokens/s over --steps
+    generations, beside the host oracle on a bounded sample."""
+    from templit_b200 import capi
+    lib = capi.gpt_lib()
+    cfg = capi.TlgConfig(family=4, batch=1, seq=SEQ, seed=1234, init_std=0.02, lr=3e-4,
+                         beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, clip=1.0, world=1,
+                         fusion=1, graphs=1, gemm_precision=capi.TL_GEMM_TF32, deferred_wait=0)
+    h = ctypes.c_void_p()
+    capi.check(lib.tlg_infer_create(ctypes.byref(cfg), ctypes.byref(h)), lib, "infer create")
+    prompt = np.random.default_rng(3).integers(1, VOCAB, 16).astype(np.uint32)
+    out = np.zeros(4096, np.uint32)
+    n = ctypes.c_uint32()
+    U = ctypes.POINTER(ctypes.c_uint32)
+
+    def gen(seed):
+        capi.check(lib.tlg_infer_generate(h, prompt.ctypes.data_as(U), prompt.size, 0, seed, 40,
+                                          0.6, 64, out.ctypes.data_as(U), out.size,
+                                          ctypes.byref(n)), lib, "generate")
+        return n.value
+
+    for i in range(max(1, args.warmup)):
+        gen(100 + i)
+    tokens, t0 = 0, time.perf_counter()
+    for i in range(args.steps):
+        tokens += gen(i)
+    dt = time.perf_counter() - t0
+    capi.check(lib.tlg_infer_destroy(h), lib, "infer destroy")
+    line = {"kernel": "inference (generate.cpp set-up: B 1, T 192, top-k 40)",
+            "tokens": tokens, "tokens_per_s": round(tokens / dt, 1),
+            "ms_per_token": round(1e3 * dt / max(tokens, 1), 3)}
+    try:
+        from oracle import cpu_gpt
+        if cpu_gpt.available():
+            ref = cpu_gpt.OracleGPTInference(cfg)
+            t0 = time.perf_counter()
+            ref.logits(np.zeros(SEQ, np.uint32))  # one forward = one generated token
+            line["oracle_ms_per_token"] = round(1e3 * (time.perf_counter() - t0), 1)
+            ref.close()
+    except Exception as exc:  # the line still prints
+        line["oracle_error"] = str(exc)
     print(json.dumps(line))
     return 0
 

@@ -58,6 +58,8 @@ void read(const Block &src, size_t offset_bytes, void *dst, size_t bytes);
 void fill32(const Block &dst, uint32_t pattern, size_t count);
 void copy(const Block &dst, const Block &src, size_t bytes);
 bool equal(const Block &a, const Block &b, size_t bytes);
+// Invalidates host copies of device data (called before device work runs).
+void device_changed();
 
 }  // namespace detail
 }  // namespace cuda

@@ -77,6 +77,25 @@ int tlg_profile(void *handle, const char *path, int steps);
  * Y [batch, out] are host arrays; the weights are updated in place,
  * losses[s] receives the summed loss of step s, *seconds the loop time.
  * gemm_precision selects TL_GEMM_TF32 (0) or TL_GEMM_FP32 (1). */
+/* Forward-only inference as src/generate.cpp sets it up: a batch-1 model of
+ * config->seq tokens (family 4; init_std/seed as for training) whose logits
+ * graph is compiled on its own, driven by the reference's
+ * inference::autoregression (include/inference.h:45-97).  Parameters in the
+ * order of tlg_get_params. */
+int tlg_infer_create(const tlg_config *config, void **handle);
+int tlg_infer_destroy(void *handle);
+int tlg_infer_param_count(void *handle, uint64_t *count);
+int tlg_infer_get_params(void *handle, float *out, uint64_t count);
+int tlg_infer_set_params(void *handle, const float *in, uint64_t count);
+/* logits [seq, 2048] of one window of seq tokens */
+int tlg_infer_logits(void *handle, const uint32_t *tokens, float *logits);
+/* tokens emitted by inference::autoregression for this prompt (top-k
+ * sampling with std::mt19937(seed)); *n_out = how many were emitted, of
+ * which the first max_out are stored */
+int tlg_infer_generate(void *handle, const uint32_t *prompt, uint32_t n_prompt, uint32_t eos,
+                       uint32_t seed, uint32_t top_k, float temperature, uint32_t min_length,
+                       uint32_t *out, uint32_t max_out, uint32_t *n_out);
+
 int tlg_mlp_train(const float *X, uint32_t batch, uint32_t in, uint32_t hidden, uint32_t out,
                   float *W1, float *b1, float *W2, float *b2, const float *Y, float root,
                   float lr, int steps, int gemm_precision, float *losses, double *seconds);

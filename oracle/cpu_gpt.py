@@ -37,6 +37,12 @@ def lib():
             "tlo_get_params": (c_int, [c_void_p, POINTER(c_float), c_uint64]),
             "tlo_set_params": (c_int, [c_void_p, POINTER(c_float), c_uint64]),
             "tlo_set_allreduce": (c_int, [c_void_p, ALLREDUCE_FN, c_void_p]),
+            "tlo_infer_create": (c_int, [POINTER(TlgConfig), POINTER(c_void_p)]),
+            "tlo_infer_destroy": (c_int, [c_void_p]),
+            "tlo_infer_set_params": (c_int, [c_void_p, POINTER(c_float), c_uint64]),
+            "tlo_infer_logits": (c_int, [c_void_p, U32P, POINTER(c_float)]),
+            "tlo_infer_generate": (c_int, [c_void_p, U32P, c_uint32, c_uint32, c_uint32, c_uint32,
+                                           c_float, c_uint32, U32P, c_uint32, U32P]),
         }
         for name, (res, args) in sig.items():
             f = getattr(_lib, name)
@@ -123,3 +129,40 @@ def train_tokens_per_s(batch, seq, steps, threads):
     finally:
         g.close()
     return batch * seq * steps / secs, secs
+
+
+class OracleGPTInference:
+    """Forward-only inference of the reference GPT (family 4, batch 1) on the
+    host oracle runtime: the model of src/generate.cpp driven by the
+    reference's inference::autoregression."""
+
+    def __init__(self, cfg):
+        self.h = c_void_p()
+        _check(lib().tlo_infer_create(ctypes.byref(cfg), ctypes.byref(self.h)))
+        self.seq = cfg.seq
+
+    def set_params(self, p):
+        p = np.ascontiguousarray(p, np.float32)
+        _check(lib().tlo_infer_set_params(self.h, p.ctypes.data_as(POINTER(c_float)), p.size))
+
+    def logits(self, tokens):
+        t = np.ascontiguousarray(tokens, np.uint32).ravel()
+        out = np.zeros((self.seq, 2048), np.float32)
+        _check(lib().tlo_infer_logits(self.h, t.ctypes.data_as(POINTER(c_uint32)),
+                                      out.ctypes.data_as(POINTER(c_float))))
+        return out
+
+    def generate(self, prompt, eos, seed, top_k, temperature, min_length, max_out=4096):
+        pr = np.ascontiguousarray(prompt, np.uint32)
+        out = np.zeros(max_out, np.uint32)
+        n = c_uint32()
+        u = POINTER(c_uint32)
+        _check(lib().tlo_infer_generate(self.h, pr.ctypes.data_as(u), pr.size, eos, seed, top_k,
+                                        temperature, min_length, out.ctypes.data_as(u), max_out,
+                                        ctypes.byref(n)))
+        return out[:min(n.value, max_out)].tolist()
+
+    def close(self):
+        if self.h:
+            lib().tlo_infer_destroy(self.h)
+            self.h = c_void_p()

@@ -5,6 +5,7 @@
 #include "host_runtime.h"
 
 #include "gpt_driver.h"
+#include "gpt_infer.h"
 
 #include <chrono>
 #include <cstring>
@@ -20,6 +21,11 @@ thread_local std::string g_error;
 struct Handle {
   cpu_ref::Runtime runtime;
   std::unique_ptr<templit_b200::DriverBase> driver;
+};
+
+struct InferHandle {
+  cpu_ref::Runtime runtime;
+  std::unique_ptr<templit_b200::InferBase> driver;
 };
 
 template <typename F> int guarded(F &&f) {
@@ -98,6 +104,39 @@ int tlo_set_allreduce(void *h, cpu_ref::Runtime::AllReduceFn fn, void *ctx) {
 
 int tlo_set_params(void *h, const float *in, uint64_t count) {
   return guarded([&] { static_cast<Handle *>(h)->driver->set_params(in, count); });
+}
+
+// ---------------------------------------------------------------- inference
+int tlo_infer_create(const tlg_config *c, void **handle) {
+  return guarded([&] {
+    if (c->family != 4) throw std::invalid_argument("oracle GPT supports family 4");
+    auto h = std::make_unique<InferHandle>();
+    h->driver =
+        std::make_unique<templit_b200::InferDriver<Mat, cpu_ref::Runtime, GPT4>>(*c, h->runtime);
+    *handle = h.release();
+  });
+}
+
+int tlo_infer_destroy(void *h) {
+  return guarded([&] { delete static_cast<InferHandle *>(h); });
+}
+
+int tlo_infer_set_params(void *h, const float *in, uint64_t count) {
+  return guarded([&] { static_cast<InferHandle *>(h)->driver->set_params(in, count); });
+}
+
+int tlo_infer_logits(void *h, const uint32_t *tokens, float *logits) {
+  return guarded([&] { static_cast<InferHandle *>(h)->driver->logits(tokens, logits); });
+}
+
+int tlo_infer_generate(void *h, const uint32_t *prompt, uint32_t n_prompt, uint32_t eos,
+                       uint32_t seed, uint32_t top_k, float temperature, uint32_t min_length,
+                       uint32_t *out, uint32_t max_out, uint32_t *n_out) {
+  return guarded([&] {
+    const uint32_t n = static_cast<InferHandle *>(h)->driver->generate(
+        prompt, n_prompt, eos, seed, top_k, temperature, min_length, out, max_out);
+    if (n_out) *n_out = n;
+  });
 }
 
 }  // extern "C"

@@ -182,6 +182,14 @@ GPT_ABI = {
     "tlg_nccl_unique_id": (c_int, [POINTER(c_uint8)]),
     "tlg_set_communicator": (c_int, [c_void_p, POINTER(c_uint8), c_int, c_int]),
     "tlg_profile": (c_int, [c_void_p, c_char_p, c_int]),
+    "tlg_infer_create": (c_int, [POINTER(TlgConfig), POINTER(c_void_p)]),
+    "tlg_infer_destroy": (c_int, [c_void_p]),
+    "tlg_infer_param_count": (c_int, [c_void_p, POINTER(c_uint64)]),
+    "tlg_infer_get_params": (c_int, [c_void_p, POINTER(c_float), c_uint64]),
+    "tlg_infer_set_params": (c_int, [c_void_p, POINTER(c_float), c_uint64]),
+    "tlg_infer_logits": (c_int, [c_void_p, U32P, POINTER(c_float)]),
+    "tlg_infer_generate": (c_int, [c_void_p, U32P, c_uint32, c_uint32, c_uint32, c_uint32,
+                                   c_float, c_uint32, U32P, c_uint32, U32P]),
     "tlg_mlp_train": (c_int, [POINTER(c_float), c_uint32, c_uint32, c_uint32, c_uint32,
                               POINTER(c_float), POINTER(c_float), POINTER(c_float),
                               POINTER(c_float), POINTER(c_float), c_float, c_float, c_int,

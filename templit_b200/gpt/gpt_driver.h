@@ -45,6 +45,71 @@ public:
   FlatArchive scope(const std::string &name) const { return FlatArchive(store_, prefix_ + name + "/"); }
 };
 
+// Every parameter of a compiled network (Compiled::save order) as one flat
+// float array; `tensors` = how many parameter tensors.
+template <typename C>
+void compiled_params(C &compiled, std::vector<float> &out, uint32_t &tensors) {
+  std::map<std::string, std::vector<std::byte>> store;
+  FlatArchive ar(&store);
+  compiled.save(ar);
+  out.clear();
+  tensors = 0;
+  for (;; ++tensors) {
+    auto it = store.find("parameters/" + std::to_string(tensors) + "/data");
+    if (it == store.end()) break;
+    const size_t n = it->second.size() / sizeof(float);
+    const size_t o = out.size();
+    out.resize(o + n);
+    std::memcpy(out.data() + o, it->second.data(), it->second.size());
+  }
+}
+
+template <typename C>
+void set_compiled_params(C &compiled, const float *in, uint64_t count) {
+  std::map<std::string, std::vector<std::byte>> store;
+  FlatArchive ar(&store);
+  compiled.save(ar);
+  uint64_t off = 0;
+  for (uint32_t i = 0;; ++i) {
+    auto it = store.find("parameters/" + std::to_string(i) + "/data");
+    if (it == store.end()) break;
+    const size_t n = it->second.size() / sizeof(float);
+    if (off + n > count) throw std::invalid_argument("too few parameter values");
+    std::memcpy(it->second.data(), in + off, n * sizeof(float));
+    off += n;
+  }
+  if (off != count) throw std::invalid_argument("parameter count mismatch");
+  compiled.load(ar);
+}
+
+// Re-draws every weight N(0, std) (std::mt19937(seed + 7919)) and zeroes
+// every bias ([1, n] tensors): the synthetic initialisation of the
+// benchmark configurations.
+template <typename C>
+void redraw_compiled(C &compiled, uint32_t seed, float std) {
+  std::vector<float> all;
+  uint32_t tensors = 0;
+  compiled_params(compiled, all, tensors);
+  std::map<std::string, std::vector<std::byte>> store;
+  FlatArchive ar(&store);
+  compiled.save(ar);
+  std::normal_distribution<float> dist(0.0f, std);
+  std::mt19937 g(seed + 7919u);
+  size_t off = 0;
+  for (uint32_t i = 0; i < tensors; ++i) {
+    const std::string key = "parameters/" + std::to_string(i) + "/";
+    const auto &size = store[key + "size"];
+    std::vector<uint32_t> shape(size.size() / 4);
+    std::memcpy(shape.data(), size.data(), size.size());
+    size_t n = 1;
+    for (uint32_t d : shape) n *= d;
+    const bool bias = shape.size() == 2 && shape[0] == 1;
+    for (size_t j = 0; j < n; ++j) all[off + j] = bias ? 0.0f : dist(g);
+    off += n;
+  }
+  set_compiled_params(compiled, all.data(), all.size());
+}
+
 struct DriverBase {
   virtual ~DriverBase() = default;
   virtual void set_batch(const uint32_t *tokens, const uint32_t *targets) = 0;
@@ -99,31 +164,7 @@ public:
     if (c.init_std > 0.0f) redraw(c.init_std);
   }
 
-  // Re-draws every weight N(0, std) and zeroes every bias (the synthetic
-  // initialisation of the benchmark configurations).
-  void redraw(float std) {
-    std::vector<float> all;
-    uint32_t tensors = 0;
-    params(all, tensors);
-    std::map<std::string, std::vector<std::byte>> store;
-    FlatArchive ar(&store);
-    compiled_->save(ar);
-    std::normal_distribution<float> dist(0.0f, std);
-    std::mt19937 g(cfg_.seed + 7919u);
-    size_t off = 0;
-    for (uint32_t i = 0; i < tensors; ++i) {
-      const std::string key = "parameters/" + std::to_string(i) + "/";
-      const auto &size = store[key + "size"];
-      std::vector<uint32_t> shape(size.size() / 4);
-      std::memcpy(shape.data(), size.data(), size.size());
-      size_t n = 1;
-      for (uint32_t d : shape) n *= d;
-      const bool bias = shape.size() == 2 && shape[0] == 1;
-      for (size_t j = 0; j < n; ++j) all[off + j] = bias ? 0.0f : dist(g);
-      off += n;
-    }
-    set_params(all.data(), all.size());
-  }
+  void redraw(float std) { redraw_compiled(*compiled_, cfg_.seed, std); }
 
   void set_batch(const uint32_t *tokens, const uint32_t *targets) override {
     const size_t n = losses_.size();
@@ -154,36 +195,11 @@ public:
   }
 
   void params(std::vector<float> &out, uint32_t &tensors) override {
-    std::map<std::string, std::vector<std::byte>> store;
-    FlatArchive ar(&store);
-    compiled_->save(ar);
-    out.clear();
-    tensors = 0;
-    for (;; ++tensors) {
-      auto it = store.find("parameters/" + std::to_string(tensors) + "/data");
-      if (it == store.end()) break;
-      const size_t n = it->second.size() / sizeof(float);
-      const size_t o = out.size();
-      out.resize(o + n);
-      std::memcpy(out.data() + o, it->second.data(), it->second.size());
-    }
+    compiled_params(*compiled_, out, tensors);
   }
 
   void set_params(const float *in, uint64_t count) override {
-    std::map<std::string, std::vector<std::byte>> store;
-    FlatArchive ar(&store);
-    compiled_->save(ar);
-    uint64_t off = 0;
-    for (uint32_t i = 0;; ++i) {
-      auto it = store.find("parameters/" + std::to_string(i) + "/data");
-      if (it == store.end()) break;
-      const size_t n = it->second.size() / sizeof(float);
-      if (off + n > count) throw std::invalid_argument("too few parameter values");
-      std::memcpy(it->second.data(), in + off, n * sizeof(float));
-      off += n;
-    }
-    if (off != count) throw std::invalid_argument("parameter count mismatch");
-    compiled_->load(ar);
+    set_compiled_params(*compiled_, in, count);
   }
 };
 

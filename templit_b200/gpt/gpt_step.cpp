@@ -7,6 +7,7 @@
 
 #include "deep_gpt.h"
 #include "gpt_driver.h"
+#include "gpt_infer.h"
 #include "my_cuda/runtime.h"
 #include "my_cuda/storage.h"
 
@@ -29,6 +30,11 @@ struct Handle {
   std::unique_ptr<templit_b200::DriverBase> driver;
   ncclComm_t comm = nullptr;
   int profile_steps = 0;
+};
+
+struct InferHandle {
+  std::unique_ptr<cuda::Runtime> runtime;
+  std::unique_ptr<templit_b200::InferBase> driver;
 };
 
 template <typename F> int guarded(F &&f) {
@@ -174,6 +180,73 @@ int tlg_profile(void *handle, const char *path, int steps) {
     Handle *h = static_cast<Handle *>(handle);
     h->runtime->start_profile(path);
     h->profile_steps = steps;
+  });
+}
+
+// ---------------------------------------------------------------- inference
+int tlg_infer_create(const tlg_config *config, void **handle) {
+  return guarded([&] {
+    if (!config || !handle) throw std::invalid_argument("null argument");
+    *handle = nullptr;
+    if (config->family != 4) throw std::invalid_argument("inference supports family 4");
+    if (config->seq == 0 || config->seq > 192)
+      throw std::invalid_argument("family 4 takes seq in [1, 192]");
+    cuda::init();
+    auto h = std::make_unique<InferHandle>();
+    h->runtime = std::make_unique<cuda::Runtime>();
+    h->runtime->set_fusion(config->fusion != 0);
+    h->runtime->set_graphs(config->graphs != 0);
+    h->runtime->set_gemm_precision(config->gemm_precision);
+    h->driver =
+        std::make_unique<templit_b200::InferDriver<Mat, cuda::Runtime, GPT4>>(*config, *h->runtime);
+    *handle = h.release();
+  });
+}
+
+int tlg_infer_destroy(void *handle) {
+  return guarded([&] {
+    InferHandle *h = static_cast<InferHandle *>(handle);
+    if (!h) return;
+    h->driver.reset();
+    h->runtime.reset();
+    delete h;
+  });
+}
+
+int tlg_infer_param_count(void *handle, uint64_t *count) {
+  return guarded([&] {
+    std::vector<float> all;
+    uint32_t t = 0;
+    static_cast<InferHandle *>(handle)->driver->params(all, t);
+    if (count) *count = all.size();
+  });
+}
+
+int tlg_infer_get_params(void *handle, float *out, uint64_t count) {
+  return guarded([&] {
+    std::vector<float> all;
+    uint32_t t = 0;
+    static_cast<InferHandle *>(handle)->driver->params(all, t);
+    if (count != all.size()) throw std::invalid_argument("parameter count mismatch");
+    std::memcpy(out, all.data(), all.size() * sizeof(float));
+  });
+}
+
+int tlg_infer_set_params(void *handle, const float *in, uint64_t count) {
+  return guarded([&] { static_cast<InferHandle *>(handle)->driver->set_params(in, count); });
+}
+
+int tlg_infer_logits(void *handle, const uint32_t *tokens, float *logits) {
+  return guarded([&] { static_cast<InferHandle *>(handle)->driver->logits(tokens, logits); });
+}
+
+int tlg_infer_generate(void *handle, const uint32_t *prompt, uint32_t n_prompt, uint32_t eos,
+                       uint32_t seed, uint32_t top_k, float temperature, uint32_t min_length,
+                       uint32_t *out, uint32_t max_out, uint32_t *n_out) {
+  return guarded([&] {
+    const uint32_t n = static_cast<InferHandle *>(handle)->driver->generate(
+        prompt, n_prompt, eos, seed, top_k, temperature, min_length, out, max_out);
+    if (n_out) *n_out = n;
   });
 }
 

@@ -40,6 +40,14 @@ struct State {
   // blocks whose value was read outside a recorded program (host reads,
   // immediate device copies), until released
   std::unordered_set<uint64_t> observed;
+  // Host mirror of the last block read in pieces (element-wise RTensor::get
+  // reads of logits): valid while no device write or launch has happened
+  // since it was taken (`epoch` and the library's launch counter).
+  uint64_t epoch = 0;
+  struct Mirror {
+    uint64_t id = 0, epoch = 0, launches = 0;
+    std::vector<unsigned char> bytes;
+  } mirror;
 };
 
 State &state() {
@@ -174,8 +182,11 @@ bool recorded_here(const Block &b) {
 }
 }  // namespace
 
+void device_changed() { ++state().epoch; }
+
 void write(const Block &dst, size_t offset_bytes, const void *src, size_t bytes) {
   if (bytes == 0) return;
+  device_changed();
   if (recorded_here(dst)) {
     state().recorder->record_write(dst, offset_bytes, src, bytes);
     return;
@@ -187,15 +198,36 @@ void write(const Block &dst, size_t offset_bytes, const void *src, size_t bytes)
 
 void read(const Block &src, size_t offset_bytes, void *dst, size_t bytes) {
   if (bytes == 0) return;
-  state().observed.insert(src.id);
+  State &s = state();
+  s.observed.insert(src.id);
+  State::Mirror &m = s.mirror;
+  const bool fresh = m.id == src.id && m.epoch == s.epoch && m.launches == tl_kernel_launches();
+  if (fresh && offset_bytes + bytes <= m.bytes.size()) {
+    std::memcpy(dst, m.bytes.data() + offset_bytes, bytes);
+    return;
+  }
+  // a piece of a block up to 16 MB: bring the whole block over once, so the
+  // next element reads are host copies
+  constexpr size_t kMirrorMax = size_t(16) << 20;
+  if (bytes < src.bytes && src.bytes <= kMirrorMax) {
+    m.bytes.resize(src.bytes);
+    internal::check(tl_memcpy_d2h(m.bytes.data(), src.ptr, src.bytes, s.stream), "Storage::read");
+    internal::check(tl_stream_sync(s.stream), "Storage::read sync");
+    m.id = src.id;
+    m.epoch = s.epoch;
+    m.launches = tl_kernel_launches();
+    std::memcpy(dst, m.bytes.data() + offset_bytes, bytes);
+    return;
+  }
   internal::check(tl_memcpy_d2h(dst, static_cast<const char *>(src.ptr) + offset_bytes, bytes,
-                                state().stream),
+                                s.stream),
                   "Storage::read");
-  internal::check(tl_stream_sync(state().stream), "Storage::read sync");
+  internal::check(tl_stream_sync(s.stream), "Storage::read sync");
 }
 
 void fill32(const Block &dst, uint32_t pattern, size_t count) {
   if (count == 0) return;
+  device_changed();
   if (recorded_here(dst)) {
     state().recorder->record_fill(dst, pattern, count);
     return;
@@ -205,6 +237,7 @@ void fill32(const Block &dst, uint32_t pattern, size_t count) {
 
 void copy(const Block &dst, const Block &src, size_t bytes) {
   if (bytes == 0) return;
+  device_changed();
   if (recorded_here(dst) || recorded_here(src)) {
     state().recorder->record_copy(dst, src, bytes);
     return;

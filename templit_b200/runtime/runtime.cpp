@@ -823,6 +823,7 @@ void Runtime::submit() {
   if (impl_->state != Impl::State::Recording)
     throw std::logic_error("CUDA runtime execution has not started");
   if (internal::active_recorder() == impl_.get()) internal::set_active_recorder(nullptr);
+  cuda::detail::device_changed();  // this window's launches may write anything
   const auto t_submit = std::chrono::steady_clock::now();
   impl_->stats.host_record_ns += static_cast<uint64_t>(
       std::chrono::duration_cast<std::chrono::nanoseconds>(t_submit - impl_->record_t0).count());

@@ -1,0 +1,128 @@
+"""Forward-only inference (the SURVEY's next row 2): the reference's own
+src/generate.cpp set-up and inference::autoregression (include/
+inference.h:45-97) on the CUDA runtime, against the same code on the host
+oracle runtime, with the same parameters.
+
+Tolerances: FP32 products - logits within 1e-4 of the largest logit,
+generated token sequences (greedy and top-k sampled) identical; TF32
+products - logits ||.||_F within 1e-2 relative."""
+import ctypes
+from ctypes import POINTER, c_float, c_uint32, c_uint64, c_void_p
+
+import numpy as np
+import pytest
+
+from oracle import cpu_gpt
+from templit_b200 import capi
+
+pytestmark = pytest.mark.gpu
+
+SEQ = 48
+
+
+def config(precision, seed=5, std=0.1):
+    return capi.TlgConfig(family=4, batch=1, seq=SEQ, seed=seed, init_std=std, lr=3e-4,
+                          beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, clip=1.0, world=1,
+                          fusion=1, graphs=1, gemm_precision=precision, deferred_wait=0)
+
+
+class CudaInference:
+    def __init__(self, cfg):
+        self.lib = capi.gpt_lib()
+        self.h = c_void_p()
+        capi.check(self.lib.tlg_infer_create(ctypes.byref(cfg), ctypes.byref(self.h)), self.lib,
+                   "tlg_infer_create")
+
+    def params(self):
+        n = c_uint64()
+        capi.check(self.lib.tlg_infer_param_count(self.h, ctypes.byref(n)), self.lib, "count")
+        out = np.zeros(n.value, np.float32)
+        capi.check(self.lib.tlg_infer_get_params(self.h, out.ctypes.data_as(POINTER(c_float)),
+                                                 n.value), self.lib, "params")
+        return out
+
+    def logits(self, tokens):
+        t = np.ascontiguousarray(tokens, np.uint32)
+        out = np.zeros((SEQ, 2048), np.float32)
+        capi.check(self.lib.tlg_infer_logits(self.h, t.ctypes.data_as(POINTER(c_uint32)),
+                                             out.ctypes.data_as(POINTER(c_float))), self.lib,
+                   "logits")
+        return out
+
+    def generate(self, prompt, eos, seed, top_k, temperature, min_length, max_out=4096):
+        pr = np.ascontiguousarray(prompt, np.uint32)
+        out = np.zeros(max_out, np.uint32)
+        n = c_uint32()
+        u = POINTER(c_uint32)
+        capi.check(self.lib.tlg_infer_generate(self.h, pr.ctypes.data_as(u), pr.size, eos, seed,
+                                               top_k, temperature, min_length,
+                                               out.ctypes.data_as(u), max_out, ctypes.byref(n)),
+                   self.lib, "generate")
+        return out[:min(n.value, max_out)].tolist()
+
+    def close(self):
+        self.lib.tlg_infer_destroy(self.h)
+
+
+@pytest.fixture(scope="module")
+def pair_fp32():
+    cfg = config(capi.TL_GEMM_FP32)
+    dev = CudaInference(cfg)
+    ref = cpu_gpt.OracleGPTInference(cfg)
+    ref.set_params(dev.params())
+    yield dev, ref
+    dev.close()
+    ref.close()
+
+
+def window(seed):
+    return np.random.default_rng(seed).integers(0, 2048, SEQ).astype(np.uint32)
+
+
+def test_logits_match_oracle_fp32(pair_fp32):
+    dev, ref = pair_fp32
+    for seed in (0, 1):
+        t = window(seed)
+        got, want = dev.logits(t), ref.logits(t)
+        err = np.abs(got - want).max() / np.abs(want).max()
+        assert err <= 1e-4, err
+        # the predicted token of every position whose top two logits are
+        # not within the tolerance of each other
+        top2 = np.sort(want, -1)[:, -2:]
+        clear = top2[:, 1] - top2[:, 0] > 2e-4 * np.abs(want).max()
+        np.testing.assert_array_equal(got.argmax(-1)[clear], want.argmax(-1)[clear])
+
+
+def test_logits_tf32_within_tolerance():
+    cfg = config(capi.TL_GEMM_TF32)
+    dev = CudaInference(cfg)
+    ref = cpu_gpt.OracleGPTInference(cfg)
+    try:
+        ref.set_params(dev.params())
+        t = window(2)
+        got, want = dev.logits(t), ref.logits(t)
+        rel = np.linalg.norm(got - want) / np.linalg.norm(want)
+        assert rel <= 1e-2, rel
+    finally:
+        dev.close()
+        ref.close()
+
+
+@pytest.mark.parametrize("top_k,temperature,seed", [(1, 1.0, 1), (40, 0.6, 3)])
+def test_generation_matches_oracle(pair_fp32, top_k, temperature, seed):
+    """Greedy (top_k 1) and sampled (top_k 40, temperature 0.6) continuations
+    of the same prompt: the same tokens from the same std::mt19937 seed."""
+    dev, ref = pair_fp32
+    prompt = window(7)[:8]
+    got = dev.generate(prompt, 0, seed, top_k, temperature, 0)
+    want = ref.generate(prompt, 0, seed, top_k, temperature, 0)
+    assert len(want) > 0
+    assert got == want
+
+
+def test_generation_rejects_what_the_reference_rejects(pair_fp32):
+    dev, _ = pair_fp32
+    with pytest.raises(RuntimeError, match="invalid prompt length"):
+        dev.generate(np.zeros(0, np.uint32), 0, 1, 1, 1.0, 0)
+    with pytest.raises(RuntimeError, match="invalid prompt length"):
+        dev.generate(np.zeros(SEQ + 1, np.uint32), 0, 1, 1, 1.0, 0)

@@ -201,7 +201,8 @@ def test_argmax_bit_exact(dev, n, pos):
 @pytest.mark.parametrize("shape,dims", [
     ((64, 192, 384), (-2, -1)), ((384, 2048), (-2, -1)), ((64, 192, 6, 64), (1, 2)),
     ((64, 6, 192, 64), (1, 2)), ((64, 6, 192, 64), (-2, -1)), ((3, 5, 7, 9), (0, 2)),
-    ((33, 65), (0, 1)), ((2, 1, 3), (0, 1)),
+    ((33, 65), (0, 1)), ((2, 1, 3), (0, 1)), ((2, 8, 3, 12), (1, 3)), ((3, 4, 5, 8), (0, 2)),
+    ((70, 130), (0, 1)),
 ])
 def test_transpose_bit_exact(dev, shape, dims):
     x = rng(6).standard_normal(shape).astype(np.float32)
