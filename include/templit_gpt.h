@@ -77,6 +77,24 @@ int tlg_profile(void *handle, const char *path, int steps);
  * Y [batch, out] are host arrays; the weights are updated in place,
  * losses[s] receives the summed loss of step s, *seconds the loop time.
  * gemm_precision selects TL_GEMM_TF32 (0) or TL_GEMM_FP32 (1). */
+/* Checkpoints in the reference's archive format (src/model_utils/
+ * archive.cpp:33-73, Compiled::save / load, include/passes/compile.h:
+ * 259-298): the parameters and, with `optimiser`, the AdamW moments and
+ * step count (saving those needs at least one step). */
+int tlg_save(void *handle, const char *path, int optimiser);
+int tlg_load(void *handle, const char *path, int optimiser);
+
+/* Training input pipeline (src/train.cpp:75-77,142-144): a raw uint32 token
+ * file split as the reference's Dataset (training part, or with
+ * `validation` the rest) and sampled as its Loader::get_batch with
+ * std::mt19937(seed); a background thread draws the next batch into pinned
+ * memory.  tlg_loader_next hands out [batch, seq] inputs and targets, valid
+ * until the next call - pass them to tlg_set_batch. */
+int tlg_loader_create(const char *path, double training_fraction, int validation,
+                      uint32_t batch, uint32_t seq, uint32_t seed, void **handle);
+int tlg_loader_next(void *handle, const uint32_t **inputs, const uint32_t **targets);
+int tlg_loader_destroy(void *handle);
+
 /* Forward-only inference as src/generate.cpp sets it up: a batch-1 model of
  * config->seq tokens (family 4; init_std/seed as for training) whose logits
  * graph is compiled on its own, driven by the reference's

@@ -37,6 +37,10 @@ def lib():
             "tlo_get_params": (c_int, [c_void_p, POINTER(c_float), c_uint64]),
             "tlo_set_params": (c_int, [c_void_p, POINTER(c_float), c_uint64]),
             "tlo_set_allreduce": (c_int, [c_void_p, ALLREDUCE_FN, c_void_p]),
+            "tlo_loader_batches": (c_int, [c_char_p, ctypes.c_double, c_int, c_uint32, c_uint32,
+                                           c_uint32, c_uint32, U32P, U32P]),
+            "tlo_save": (c_int, [c_void_p, c_char_p, c_int]),
+            "tlo_load": (c_int, [c_void_p, c_char_p, c_int]),
             "tlo_infer_create": (c_int, [POINTER(TlgConfig), POINTER(c_void_p)]),
             "tlo_infer_destroy": (c_int, [c_void_p]),
             "tlo_infer_set_params": (c_int, [c_void_p, POINTER(c_float), c_uint64]),
@@ -102,6 +106,13 @@ class OracleGPT:
         p = np.ascontiguousarray(p, np.float32)
         _check(lib().tlo_set_params(self.h, p.ctypes.data_as(POINTER(c_float)), p.size))
 
+    def save(self, path, optimiser=True):
+        """Checkpoint through the reference's Archive (commit)."""
+        _check(lib().tlo_save(self.h, str(path).encode(), int(optimiser)))
+
+    def load(self, path, optimiser=True):
+        _check(lib().tlo_load(self.h, str(path).encode(), int(optimiser)))
+
     def close(self):
         if self.h:
             lib().tlo_destroy(self.h)
@@ -166,3 +177,13 @@ class OracleGPTInference:
         if self.h:
             lib().tlo_infer_destroy(self.h)
             self.h = c_void_p()
+
+
+def loader_batches(path, training_fraction, validation, batch, seq, seed, n):
+    """n batches from the reference's own Dataset::load_tokens + Loader."""
+    x = np.zeros((n, batch, seq), np.uint32)
+    y = np.zeros((n, batch, seq), np.uint32)
+    u = POINTER(c_uint32)
+    _check(lib().tlo_loader_batches(str(path).encode(), training_fraction, int(validation), batch,
+                                    seq, seed, n, x.ctypes.data_as(u), y.ctypes.data_as(u)))
+    return x, y

@@ -6,6 +6,11 @@
 
 #include "gpt_driver.h"
 #include "gpt_infer.h"
+#include "model_utils/Dataset.h"
+#include "model_utils/archive.h"
+#include "model_utils/loader.h"
+
+#include <fstream>
 
 #include <chrono>
 #include <cstring>
@@ -104,6 +109,53 @@ int tlo_set_allreduce(void *h, cpu_ref::Runtime::AllReduceFn fn, void *ctx) {
 
 int tlo_set_params(void *h, const float *in, uint64_t count) {
   return guarded([&] { static_cast<Handle *>(h)->driver->set_params(in, count); });
+}
+
+// Checkpoints through the reference's own Archive (src/model_utils/
+// archive.cpp, compiled into this library): the format the CUDA library's
+// tlg_save / tlg_load must match.
+int tlo_save(void *h, const char *path, int optimiser) {
+  return guarded([&] {
+    auto *d = dynamic_cast<templit_b200::GptDriver<Mat, cpu_ref::Runtime, GPT4> *>(
+        static_cast<Handle *>(h)->driver.get());
+    if (!d) throw std::invalid_argument("not a family-4 model");
+    Archive archive;
+    d->save_archive(archive, optimiser != 0);
+    std::ofstream out(path, std::ios::binary);
+    archive.commit(out);
+    if (!out) throw std::runtime_error("checkpoint write failed");
+  });
+}
+
+int tlo_load(void *h, const char *path, int optimiser) {
+  return guarded([&] {
+    auto *d = dynamic_cast<templit_b200::GptDriver<Mat, cpu_ref::Runtime, GPT4> *>(
+        static_cast<Handle *>(h)->driver.get());
+    if (!d) throw std::invalid_argument("not a family-4 model");
+    std::ifstream in(path, std::ios::binary);
+    if (!in) throw std::runtime_error(std::string("cannot open ") + path);
+    Archive archive;
+    archive.restore(in);
+    d->load_archive(archive, optimiser != 0);
+  });
+}
+
+// The reference's own Dataset::load_tokens + Loader::get_batch (compiled
+// into this library): n batches of [batch, seq] inputs and targets.
+int tlo_loader_batches(const char *path, double training_fraction, int validation,
+                       uint32_t batch, uint32_t seq, uint32_t seed, uint32_t n,
+                       uint32_t *inputs, uint32_t *targets) {
+  return guarded([&] {
+    std::ifstream in(path, std::ios::binary);
+    Dataset dataset = Dataset::load_tokens(in, training_fraction);
+    Loader loader(validation ? dataset.validation_split() : dataset.training_split(), seed);
+    const size_t per = static_cast<size_t>(batch) * seq;
+    for (uint32_t i = 0; i < n; ++i) {
+      const auto &b = loader.get_batch(batch, seq);
+      std::memcpy(inputs + i * per, b.inputs.data(), per * sizeof(uint32_t));
+      std::memcpy(targets + i * per, b.targets.data(), per * sizeof(uint32_t));
+    }
+  });
 }
 
 // ---------------------------------------------------------------- inference

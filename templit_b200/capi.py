@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import (POINTER, Structure, c_char_p, c_float, c_int, c_int32,
+from ctypes import (POINTER, Structure, c_char_p, c_double, c_float, c_int, c_int32,
                     c_size_t, c_uint8, c_uint32, c_uint64, c_void_p)
 
 BUILD_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build")
@@ -182,6 +182,12 @@ GPT_ABI = {
     "tlg_nccl_unique_id": (c_int, [POINTER(c_uint8)]),
     "tlg_set_communicator": (c_int, [c_void_p, POINTER(c_uint8), c_int, c_int]),
     "tlg_profile": (c_int, [c_void_p, c_char_p, c_int]),
+    "tlg_loader_create": (c_int, [c_char_p, c_double, c_int, c_uint32, c_uint32, c_uint32,
+                                  POINTER(c_void_p)]),
+    "tlg_loader_next": (c_int, [c_void_p, POINTER(U32P), POINTER(U32P)]),
+    "tlg_loader_destroy": (c_int, [c_void_p]),
+    "tlg_save": (c_int, [c_void_p, c_char_p, c_int]),
+    "tlg_load": (c_int, [c_void_p, c_char_p, c_int]),
     "tlg_infer_create": (c_int, [POINTER(TlgConfig), POINTER(c_void_p)]),
     "tlg_infer_destroy": (c_int, [c_void_p]),
     "tlg_infer_param_count": (c_int, [c_void_p, POINTER(c_uint64)]),

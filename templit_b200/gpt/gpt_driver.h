@@ -14,6 +14,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <fstream>
 #include <map>
 #include <memory>
 #include <random>
@@ -25,16 +26,51 @@
 namespace templit_b200 {
 
 // Flat in-memory archive (WritableArchive + ReadableArchive with scopes) used
-// to move parameters in and out through Compiled::save / Compiled::load.
+// to move parameters in and out through Compiled::save / Compiled::load, and
+// checkpoints in the file layout of the reference's Archive
+// (src/model_utils/archive.cpp:33-73): entries `scope/.../name`, each as
+// u32 name length, name bytes, u32 blob length, blob (host byte order).
 class FlatArchive {
   std::map<std::string, std::vector<std::byte>> *store_;
   std::string prefix_;
 
 public:
+  using Store = std::map<std::string, std::vector<std::byte>>;
   explicit FlatArchive(std::map<std::string, std::vector<std::byte>> *s, std::string p = "")
       : store_(s), prefix_(std::move(p)) {}
   void write(const std::string &name, std::span<const std::byte> v) {
     (*store_)[prefix_ + name].assign(v.begin(), v.end());
+  }
+
+  // Writes every entry (any order is valid: the reference restores by name).
+  static void commit(const Store &store, std::ostream &out) {
+    for (const auto &[name, blob] : store) {
+      const uint32_t name_len = static_cast<uint32_t>(name.size());
+      const uint32_t blob_len = static_cast<uint32_t>(blob.size());
+      if (name_len != name.size() || blob_len != blob.size())
+        throw std::runtime_error("archive entry too large: " + name);
+      out.write(reinterpret_cast<const char *>(&name_len), sizeof(name_len));
+      out.write(name.data(), static_cast<std::streamsize>(name.size()));
+      out.write(reinterpret_cast<const char *>(&blob_len), sizeof(blob_len));
+      out.write(reinterpret_cast<const char *>(blob.data()),
+                static_cast<std::streamsize>(blob.size()));
+    }
+    if (!out) throw std::runtime_error("checkpoint write failed");
+  }
+
+  // Reads entries until the stream ends (a truncated last entry is dropped,
+  // as the reference's Archive::restore does).
+  static void restore(Store &store, std::istream &in) {
+    for (;;) {
+      uint32_t name_len = 0, blob_len = 0;
+      if (!in.read(reinterpret_cast<char *>(&name_len), sizeof(name_len))) break;
+      std::string name(name_len, '\0');
+      if (!in.read(name.data(), name_len)) break;
+      if (!in.read(reinterpret_cast<char *>(&blob_len), sizeof(blob_len))) break;
+      std::vector<std::byte> blob(blob_len);
+      if (!in.read(reinterpret_cast<char *>(blob.data()), blob_len)) break;
+      store[name] = std::move(blob);
+    }
   }
   void read(const std::string &name, std::span<std::byte> v) const {
     auto it = store_->find(prefix_ + name);
@@ -117,6 +153,10 @@ struct DriverBase {
   virtual void forward(float *losses) = 0;
   virtual void params(std::vector<float> &out, uint32_t &tensors) = 0;
   virtual void set_params(const float *in, uint64_t count) = 0;
+  // Checkpoint of the parameters (and the AdamW state) in the reference's
+  // archive format, through Compiled::save / save_optimisers.
+  virtual void save(const std::string &path, bool optimiser) = 0;
+  virtual void load(const std::string &path, bool optimiser) = 0;
 };
 
 template <typename Mat, typename Run, typename Model>
@@ -200,6 +240,34 @@ public:
 
   void set_params(const float *in, uint64_t count) override {
     set_compiled_params(*compiled_, in, count);
+  }
+
+  // Any archive type of the reference (include/model_utils/archive_concepts.h).
+  template <typename A> void save_archive(A &ar, bool optimiser) {
+    compiled_->save(ar);
+    if (optimiser) compiled_->save_optimisers(ar);
+  }
+  template <typename A> void load_archive(A &ar, bool optimiser) {
+    compiled_->load(ar);
+    if (optimiser) compiled_->load_optimisers(ar);
+  }
+
+  void save(const std::string &path, bool optimiser) override {
+    FlatArchive::Store store;
+    FlatArchive ar(&store);
+    save_archive(ar, optimiser);
+    std::ofstream out(path, std::ios::binary);
+    if (!out) throw std::runtime_error("cannot open " + path);
+    FlatArchive::commit(store, out);
+  }
+
+  void load(const std::string &path, bool optimiser) override {
+    std::ifstream in(path, std::ios::binary);
+    if (!in) throw std::runtime_error("cannot open " + path);
+    FlatArchive::Store store;
+    FlatArchive::restore(store, in);
+    FlatArchive ar(&store);
+    load_archive(ar, optimiser);
   }
 };
 

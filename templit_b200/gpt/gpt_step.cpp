@@ -8,6 +8,7 @@
 #include "deep_gpt.h"
 #include "gpt_driver.h"
 #include "gpt_infer.h"
+#include "input_pipeline.h"
 #include "my_cuda/runtime.h"
 #include "my_cuda/storage.h"
 
@@ -181,6 +182,43 @@ int tlg_profile(void *handle, const char *path, int steps) {
     h->runtime->start_profile(path);
     h->profile_steps = steps;
   });
+}
+
+int tlg_save(void *handle, const char *path, int optimiser) {
+  return guarded([&] {
+    if (!path) throw std::invalid_argument("null path");
+    static_cast<Handle *>(handle)->driver->save(path, optimiser != 0);
+  });
+}
+
+int tlg_load(void *handle, const char *path, int optimiser) {
+  return guarded([&] {
+    if (!path) throw std::invalid_argument("null path");
+    static_cast<Handle *>(handle)->driver->load(path, optimiser != 0);
+  });
+}
+
+// ----------------------------------------------------------- input pipeline
+int tlg_loader_create(const char *path, double training_fraction, int validation,
+                      uint32_t batch, uint32_t seq, uint32_t seed, void **handle) {
+  return guarded([&] {
+    if (!path || !handle) throw std::invalid_argument("null argument");
+    *handle = nullptr;
+    cuda::init();  // pinned memory needs the device
+    *handle = new templit_b200::TokenPipeline(path, training_fraction, validation != 0, batch,
+                                              seq, seed);
+  });
+}
+
+int tlg_loader_next(void *handle, const uint32_t **inputs, const uint32_t **targets) {
+  return guarded([&] {
+    if (!handle || !inputs || !targets) throw std::invalid_argument("null argument");
+    static_cast<templit_b200::TokenPipeline *>(handle)->next(inputs, targets);
+  });
+}
+
+int tlg_loader_destroy(void *handle) {
+  return guarded([&] { delete static_cast<templit_b200::TokenPipeline *>(handle); });
 }
 
 // ---------------------------------------------------------------- inference

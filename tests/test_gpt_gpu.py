@@ -71,6 +71,12 @@ class CudaGPT:
         return dict(zip(["windows", "recorded", "launched", "kernels", "replays", "captures",
                          "fused", "peak_bytes", "record_ns", "submit_ns", "plan_hits"], list(s)))
 
+    def save(self, path, optimiser=True):
+        capi.check(self.lib.tlg_save(self.h, str(path).encode(), int(optimiser)), self.lib, "save")
+
+    def load(self, path, optimiser=True):
+        capi.check(self.lib.tlg_load(self.h, str(path).encode(), int(optimiser)), self.lib, "load")
+
     def close(self):
         capi.check(self.lib.tlg_destroy(self.h), self.lib, "destroy")
 
