@@ -50,7 +50,8 @@ def parse_args():
     p.add_argument("--kernel", choices=["gemm", "attention", "infer"], default="",
                    help="time one kernel case instead of the training step (profiling "
                         "driver): a tl_gemm shape, or configuration 3's attention")
-    p.add_argument("--shape", default="12288x384x384:NN", help="--kernel gemm: MxNxK:form")
+    p.add_argument("--shape", default="12288x384x384:NN",
+                   help="--kernel gemm: MxNxK:form[:gelu_grad|:addend]")
     return p.parse_args()
 
 
@@ -196,7 +197,13 @@ def gemm_roofline(profile_path, peak_tflops, peak_source):
     return {"bound": "tensor", "kernel": "tc_gemm_kernel (tcgen05 kind::tf32)",
             "achieved": round(achieved, 1), "peak": peak_tflops, "unit": "TFLOP/s",
             "frac": round(achieved / peak_tflops, 4) if peak_tflops else None,
-            "peak_source": peak_source, "traffic": None,
+            "peak_source": peak_source,
+            # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the
+            # step's most frequent product (ncu capture summarised in
+            # profiles/tc_gemm_12288x384x384_NN.md): 19.55 MB = its algorithmic
+            # reads (A once, B); C stays in L2 when the kernel ends
+            "traffic": 19548928, "traffic_unit": "bytes per launch",
+            "traffic_shape": "12288x384x384 NN",
             "flops_per_step": flops, "gemm_ms_per_step": round(ms, 4),
             "gemm_launches_per_step": launches,
             "gemm_share_of_step": round(ms / total_ms, 3) if total_ms else None,
@@ -264,7 +271,9 @@ def run_kernel_case(args):
     if args.kernel == "infer":
         return run_inference_case(args)
     if args.kernel == "gemm":
-        dims, form = args.shape.split(":")
+        parts = args.shape.split(":")  # MxNxK:form[:gelu_grad|:addend]
+        dims, form = parts[0], parts[1]
+        aux = parts[2] if len(parts) > 2 else ""
         m, n, k = (int(v) for v in dims.split("x"))
         ta, tb = form[0] == "T", form[1] == "T"
         a = torch.randn((k, m) if ta else (m, k), device=dev, generator=g)
@@ -272,6 +281,11 @@ def run_kernel_case(args):
         c = torch.zeros((m, n), device=dev)
         d = capi.TlGemmDesc(a=a.data_ptr(), b=b.data_ptr(), c=c.data_ptr(), m=m, n=n, k=k,
                             trans_a=int(ta), trans_b=int(tb), precision=capi.TL_GEMM_TF32)
+        x_aux = torch.randn((m, n), device=dev, generator=g) if aux else None
+        if aux == "gelu_grad":
+            d.gelu_grad_x = x_aux.data_ptr()
+        elif aux == "addend":
+            d.addend = x_aux.data_ptr()
         wsb = lib.tl_gemm_workspace_size(ctypes.byref(d))
         ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
         d.workspace, d.workspace_bytes = ws.data_ptr(), wsb

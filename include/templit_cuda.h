@@ -359,6 +359,11 @@ typedef struct tl_gemm_desc {
   const float *b_group[TL_GEMM_MAX_GROUPS];
   float *c_group[TL_GEMM_MAX_GROUPS];
   const float *bias_group[TL_GEMM_MAX_GROUPS];
+  /* Optional, C's layout: C = GELU'(gelu_grad_x) * (A*B (+ bias)), the GELU
+   * backward (GELU_derivative(x) hadamard the incoming gradient,
+   * include/passes/execute.h) folded into the epilogue of the product that
+   * makes the gradient.  Not with addend, beta, gelu_out or groups. */
+  const float *gelu_grad_x;
 } tl_gemm_desc;
 int tl_gemm(const tl_gemm_desc *desc, void *stream);
 size_t tl_gemm_workspace_size(const tl_gemm_desc *desc);

@@ -13,6 +13,7 @@ struct GemmArgs {
   const float *bias;
   float *gelu_out;
   const float *addend;  // C's layout; C itself when accumulating (beta = 1)
+  const float *gelu_grad_x;  // C's layout: C = GELU'(x) * product
   uint32_t m, n, k;
   uint64_t lda, ldb, ldc;  // row strides of the stored matrices (elements)
   int trans_a, trans_b;
@@ -49,7 +50,8 @@ __device__ __forceinline__ void batch_offsets(const GemmArgs &g, uint64_t z,
 }
 
 // Final value of C[idx] (idx relative to the batch's C base, column n):
-// v = A*B (+ bias[n]) then addend + v - the reference adds the bias after
+// v = A*B (+ bias[n]) then addend + v (or GELU'(x) * v for a folded GELU
+// backward, in the order of the reference's hadamard) - the reference adds the bias after
 // the product (EXPR_LINEAR: mult then add, include/passes/execute.h:241-252)
 // and gradient accumulation adds the new term to the old (context.h:74-89).
 __device__ __forceinline__ void epilogue_store(const GemmArgs &g, float *Cb,
@@ -57,6 +59,7 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs &g, float *Cb,
                                                uint32_t n, float v) {
   if (g.bias) v = v + g.bias[n];
   if (g.addend) v = g.addend[oc + idx] + v;
+  if (g.gelu_grad_x) v = gelu_deriv_f(g.gelu_grad_x[oc + idx]) * v;
   Cb[idx] = v;
   if (g.gelu_out) g.gelu_out[oc + idx] = gelu_f(v);
 }

@@ -44,6 +44,9 @@ int to_args(const tl_gemm_desc *d, GemmArgs &g) {
   if (d->addend && d->beta != 0.0f && d->addend != d->c)
     return fail(TL_ERR_INVALID, "tl_gemm: addend with beta = 1 must be C");
   g.addend = d->addend ? d->addend : (d->beta != 0.0f ? d->c : nullptr);
+  g.gelu_grad_x = d->gelu_grad_x;
+  if (g.gelu_grad_x && (g.addend || d->gelu_out || d->group_mode != TL_GEMM_GROUP_NONE))
+    return fail(TL_ERR_INVALID, "tl_gemm: gelu_grad_x takes no addend, beta, gelu_out or groups");
   g.group_mode = d->group_mode;
   g.groups = 1;
   if (d->group_mode != TL_GEMM_GROUP_NONE) {

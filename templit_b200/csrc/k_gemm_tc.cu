@@ -89,6 +89,9 @@ struct TcArgs {
   // epilogue through shared memory and TMA stores (C, or the split-K
   // partials, dense per matrix with rows of a multiple of 16 bytes)
   bool tma_epi;
+  // the TMA epilogue reads an addend / GELU-input box per chunk: the
+  // producer prefetches each tile's boxes into L2 when it starts the tile
+  bool aux_prefetch;
 };
 
 template <int BN>
@@ -225,6 +228,15 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
         map_coords(t.ma, cz, za);
         map_coords(t.mb, cz, zb);
         const int32_t m0 = static_cast<int32_t>(mb * BM), n0 = static_cast<int32_t>(nb * BN);
+        if (t.aux_prefetch) {
+          // the epilogue's addend / GELU-input boxes of this tile: into L2
+          // while the mainloop runs, so its per-chunk loads hit L2
+          int32_t zc[3];
+          map_coords(t.mc, cz, zc);
+          for (int c = 0; c < BN / 32; ++c)
+            for (int q = 0; q < BM / 32; ++q)
+              ptx::tma_prefetch_nd(&maps.addend, n0 + 32 * c, m0 + 32 * q, t.mc.nb, zc);
+        }
         for (uint32_t kb = kb0; kb < kb1; ++kb) {
           if (!ptx::mbar_wait_bounded(&empty[stage], phase ^ 1, kWaitLimitNs)) {
             timeout();
@@ -384,6 +396,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
       const bool fast = (g.n % 4) == 0 && (ldo % 4) == 0 && aligned16(Cb) &&
                         (raw || ((!g.bias || aligned16(g.bias)) &&
                                  (!g.addend || aligned16(g.addend + oc)) &&
+                                 (!g.gelu_grad_x || aligned16(g.gelu_grad_x + oc)) &&
                                  (!g.gelu_out || aligned16(g.gelu_out + oc))));
       if (t.tma_epi) {
         // Each chunk of 32 columns: TMEM -> registers (+ bias, + addend box
@@ -404,7 +417,11 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
           map_coords(t.mc, cz, zc);
           ncz = t.mc.nb;
         }
-        const bool with_add = !raw && g.addend != nullptr;
+        // the addend box, or the GELU-backward input box (same map slot),
+        // loaded by TMA into the staging box (L2 hits: the producer
+        // prefetched the tile's boxes)
+        const bool with_add = !raw && (g.addend != nullptr || g.gelu_grad_x != nullptr);
+        const bool gelu_grad = !raw && g.gelu_grad_x != nullptr;
         const bool with_gelu = !raw && g.gelu_out != nullptr;
         bool failed = false;
 #pragma unroll 1
@@ -446,7 +463,11 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
               }
             }
             float4 *slot = reinterpret_cast<float4 *>(box + swz(lane, j));
-            if (with_add) {
+            if (gelu_grad) {
+              const float4 a = *slot;
+              v[j] = make_float4(gelu_deriv_f(a.x) * v[j].x, gelu_deriv_f(a.y) * v[j].y,
+                                 gelu_deriv_f(a.z) * v[j].z, gelu_deriv_f(a.w) * v[j].w);
+            } else if (with_add) {
               const float4 a = *slot;
               v[j] = make_float4(a.x + v[j].x, a.y + v[j].y, a.z + v[j].z, a.w + v[j].w);
             }
@@ -509,6 +530,12 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
                 const float4 o =
                     *reinterpret_cast<const float4 *>(g.addend + oc + rowoff + n0 + 4 * j);
                 v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
+              }
+              if (g.gelu_grad_x) {
+                const float4 x =
+                    *reinterpret_cast<const float4 *>(g.gelu_grad_x + oc + rowoff + n0 + 4 * j);
+                v = make_float4(gelu_deriv_f(x.x) * v.x, gelu_deriv_f(x.y) * v.y,
+                                gelu_deriv_f(x.z) * v.z, gelu_deriv_f(x.w) * v.w);
               }
             }
             dst[j] = v;
@@ -711,14 +738,16 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
   } else {
     bool strides_ok = g.ldc % 4 == 0;
     for (uint32_t d = 0; d < g.batch_rank; ++d) strides_ok = strides_ok && g.sc[d] % 4 == 0;
+    const float *aux = g.addend ? g.addend : g.gelu_grad_x;  // one epilogue input box
     OpMap og{}, od{};
     t.tma_epi = g.n % 4 == 0 && strides_ok && aligned16(g.c) &&
                 (!g.bias || aligned16(g.bias)) && (!g.gelu_out || aligned16(g.gelu_out)) &&
                 (!g.addend || aligned16(g.addend)) &&
+                (!g.gelu_grad_x || aligned16(g.gelu_grad_x)) &&
                 (!g.gelu_out || make_operand_map(&maps.gelu, g.gelu_out, g.n, g.m, g.ldc, g,
                                                  g.sc, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, og)) &&
-                (!g.addend || make_operand_map(&maps.addend, g.addend, g.n, g.m, g.ldc, g, g.sc,
-                                               32, 32, CU_TENSOR_MAP_SWIZZLE_128B, od));
+                (!aux || make_operand_map(&maps.addend, aux, g.n, g.m, g.ldc, g, g.sc, 32, 32,
+                                          CU_TENSOR_MAP_SWIZZLE_128B, od));
     for (uint32_t i = 0; i < ngroups && t.tma_epi; ++i) {
       float *ci = g.cg[i] ? g.cg[i] : g.c;
       const float *bi = g.groups > 1 ? g.biasg[i] : g.bias;
@@ -727,6 +756,7 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
                                    CU_TENSOR_MAP_SWIZZLE_128B, t.mc);
     }
   }
+  t.aux_prefetch = t.tma_epi && !partial && (g.addend || g.gelu_grad_x);
   // grouped outputs leave only through the TMA epilogue
   if (ngroups > 1 && !t.tma_epi)
     return fail(TL_ERR_UNSUPPORTED, "tl_gemm: grouped outputs need 16-byte rows");

@@ -130,6 +130,37 @@ __device__ __forceinline__ void tma_load_nd(void *smem_dst, const CUtensorMap *m
   }
 }
 
+// Prefetch of a box of a rank-(2 + nb) map into L2 (no shared memory, no
+// barrier): the data a later tiled load of the same box will find in L2.
+__device__ __forceinline__ void tma_prefetch_nd(const CUtensorMap *map, int32_t c0, int32_t c1,
+                                                int nb, const int32_t *zc) {
+  const uint64_t m = reinterpret_cast<uint64_t>(map);
+  switch (nb) {
+    case 0:
+      asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(m),
+                   "r"(c0), "r"(c1)
+                   : "memory");
+      break;
+    case 1:
+      asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(m),
+                   "r"(c0), "r"(c1), "r"(zc[0])
+                   : "memory");
+      break;
+    case 2:
+      asm volatile(
+          "cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(m),
+          "r"(c0), "r"(c1), "r"(zc[0]), "r"(zc[1])
+          : "memory");
+      break;
+    default:
+      asm volatile(
+          "cp.async.bulk.prefetch.tensor.5d.L2.global.tile [%0, {%1, %2, %3, %4, %5}];" ::"l"(m),
+          "r"(c0), "r"(c1), "r"(zc[0]), "r"(zc[1]), "r"(zc[2])
+          : "memory");
+      break;
+  }
+}
+
 // Tiled TMA load of a box of a rank-`rank` map (3..5) at coordinates c.
 __device__ __forceinline__ void tma_load_rank(void *smem_dst, const CUtensorMap *map,
                                               uint64_t *bar, int rank, const int32_t *c) {

@@ -39,7 +39,7 @@ Access access(const Op &op) {
       for (int i : {0, 1, 3, 4, 5, 6, 7, 8}) a.read(t[i]);
       a.write(t[2]); a.write(t[3]); a.write(t[4]); break;
     case Kind::Gemm:
-      a.read(t[0]); a.read(t[1]); a.read(t[3]); a.read(t[5]);
+      a.read(t[0]); a.read(t[1]); a.read(t[3]); a.read(t[5]); a.read(t[6]);
       if (op.gemm.beta != 0.0f) a.read(t[2]);
       a.write(t[2]); a.write(t[4]);
       if (op.gemm.group_mode == TL_GEMM_GROUP_N) {
@@ -802,12 +802,55 @@ uint64_t fold_head_transposes(std::vector<Op> &p) {
   return folded;
 }
 
+// ------------------------------------------------ GELU backward epilogue
+// mult(...) -> G; GELU backward(x, G) -> D (GELU_derivative(x) hadamard G,
+// folded by fuse_pointwise_backward) with G read by nothing else: the
+// product writes D = GELU'(x) * (its value) in its epilogue (the FFN's
+// gradient through the activation, include/nn/decoder_block.h).
+uint64_t fuse_gemm_gelu_backward(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t k = 0; k < p.size(); ++k) {
+    Op &gb = p[k];
+    if (gb.dead || gb.kind != Kind::GeluBwd) continue;
+    const TRef X = gb.t[0], G = gb.t[1], D = gb.t[2];
+    const size_t j = last_writer(p, k, G.id);
+    if (j == kNone) continue;
+    Op &mm = p[j];
+    const tl_gemm_desc &g = mm.gemm;
+    if (mm.kind != Kind::Gemm || !same(mm.t[2], G) || g.beta != 0.0f || g.addend ||
+        mm.t[5].p || g.gelu_out || g.gelu_grad_x || g.group_mode != TL_GEMM_GROUP_NONE)
+      continue;
+    // C dense, X and D the same dense shape
+    uint64_t batch = 1;
+    for (uint32_t d = 0; d < g.batch_rank; ++d) batch *= g.batch_shape[d];
+    const uint64_t mn = static_cast<uint64_t>(g.m) * g.n;
+    bool dense = (g.ldc == 0 || g.ldc == g.n) && batch * mn == G.numel() &&
+                 X.numel() == G.numel() && D.numel() == G.numel();
+    uint64_t inner = mn;
+    for (uint32_t d = g.batch_rank; d-- > 0;) {
+      dense = dense && g.c_batch_stride[d] == inner;
+      inner *= g.batch_shape[d];
+    }
+    if (!dense || same(X, G) || same(D, G) || reads(access(mm), D.id) ||
+        first_reader(p, j, G.id) != k || !dead_after(p, k, G.id) ||
+        !unchanged_between(p, j, k, X.id) || !untouched_between(p, j, k, D.id))
+      continue;
+    mm.gemm.c = D.f();
+    mm.gemm.gelu_grad_x = X.f();
+    mm.t[2] = D;
+    mm.t[6] = X;
+    gb.dead = true;
+    ++folded;
+  }
+  return folded;
+}
+
 // -------------------------------------------------------- fused attention
 // A plain product: no epilogue, no groups, TF32 (the fused kernels' type).
 bool plain_product(const Op &op) {
   const tl_gemm_desc &g = op.gemm;
   return !op.dead && op.kind == Kind::Gemm && g.beta == 0.0f && !g.bias && !g.gelu_out &&
-         !g.addend && !op.t[5].p && g.group_mode == TL_GEMM_GROUP_NONE &&
+         !g.addend && !g.gelu_grad_x && !op.t[5].p && g.group_mode == TL_GEMM_GROUP_NONE &&
          g.precision == TL_GEMM_TF32 && op.i1 == 0;
 }
 
@@ -1008,9 +1051,10 @@ uint64_t fuse_attention(std::vector<Op> &p) {
 }
 
 // ------------------------------------------------------- grouped products
+// (flattened products, op.i1 = 1, are ordinary M x N x K products here)
 bool groupable(const Op &op) {
   return !op.dead && op.kind == Kind::Gemm && op.gemm.group_mode == TL_GEMM_GROUP_NONE &&
-         !op.gemm.gelu_out && op.i1 == 0;
+         !op.gemm.gelu_out && !op.gemm.gelu_grad_x;
 }
 
 // Same product shape and layout (everything but the operand addresses).
@@ -1581,6 +1625,7 @@ uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live) {
   folded += fold_head_transposes(prog);  // a second transpose of the same product
   folded += fuse_gemm_accumulate(prog);
   folded += fuse_row_backward_tails(prog);
+  folded += fuse_gemm_gelu_backward(prog);
   folded += fuse_score_softmax(prog);
   folded += fuse_attention(prog);
   folded += group_summed_products(prog);

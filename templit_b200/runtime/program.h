@@ -57,7 +57,8 @@ enum class Kind : uint8_t {
   SqNorm,      // t0 gradient, t1 sqnorm
   Clip,        // t0 gradient, t1 sqnorm, t2 out, f0 max_norm
   AdamW,       // t0 param, t1 grad, t2 out, t3 m1, t4 m2, t5 b1, t6 b2, t7 decay, t8 lr; f0 eps, u0 step
-  Gemm,        // gemm descriptor; t0 a, t1 b, t2 c (+ t3 bias, t4 gelu out, t5 addend)
+  Gemm,        // gemm descriptor; t0 a, t1 b, t2 c (+ t3 bias, t4 gelu out, t5 addend,
+               //   t6 GELU-backward input)
   // Storage data movement inside the window
   HostWrite,   // t0 dst (rank 1 byte view), u64 offset, host payload
   Fill,        // t0 dst, u0 pattern, n elements

@@ -251,7 +251,9 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
     release_resources();
   }
 
-  static std::string describe(const Op &op) {
+  // One line per op; with `marks`, each tensor carries its liveness as the
+  // optimiser saw it: '*' window-local, '^' read by the host.
+  std::string describe(const Op &op, bool marks = false) const {
     std::string s = internal::kind_name(op.kind);
     if (op.kind == Kind::Binary || op.kind == Kind::Unary || op.kind == Kind::Scalar ||
         op.kind == Kind::Reduce)
@@ -277,6 +279,10 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
       s += " t" + std::to_string(i) + "=" + std::to_string(r.id) + "[";
       for (int d = 0; d < r.rank; ++d) s += (d ? "," : "") + std::to_string(r.shape[d]);
       s += "]";
+      if (marks && r.id) {
+        if (window_local(r.id)) s += "*";
+        if (internal::host_observed(r.id)) s += "^";
+      }
     }
     if (!op.multi.empty()) s += " slots=" + std::to_string(op.multi.size());
     if (op.dead) s += " DEAD";
@@ -287,7 +293,7 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
     std::ofstream out(dump_path, std::ios::app);
     out << "== " << title << " window " << window_id << (fresh ? "" : " (again)") << " ops "
         << prog.size() << "\n";
-    for (size_t i = 0; i < prog.size(); ++i) out << i << " " << describe(prog[i]) << "\n";
+    for (size_t i = 0; i < prog.size(); ++i) out << i << " " << describe(prog[i], true) << "\n";
   }
 
   // Updates `life` from a recorded (not yet optimised) program.

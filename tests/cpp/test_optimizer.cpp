@@ -480,6 +480,7 @@ void projections_grouped() {
   auto v = tensor({12288, 384});
   std::vector<Op> p = {gemm(x, wq, q, 12288, 384, 384), gemm(x, wk, k, 12288, 384, 384),
                        gemm(x, wv, v, 12288, 384, 384)};
+  for (Op &o : p) o.i1 = 1;  // flattened [64, 192, 384] x [384, 384] products
   require(optimize(p, nullptr) == 2, "three projections grouped");
   auto l = live(p);
   require(l.size() == 1 && l[0]->gemm.group_mode == TL_GEMM_GROUP_N && l[0]->gemm.groups == 3 &&
@@ -579,6 +580,33 @@ void attention_backward_fused() {
           "dK and dV on the key-side kernel");
 }
 
+
+
+// dH = dY W2^T; GELU backward(x, dH) -> dX: the product's epilogue applies
+// GELU'(x); kept apart when dH is read again
+void gelu_backward_into_gemm() {
+  auto dy = tensor({12288, 384}), w = tensor({1536, 384}), dh = tensor({12288, 1536});
+  auto x = tensor({12288, 1536}), dx = tensor({12288, 1536}), other = tensor({12288, 1536});
+  Op g = gemm(dy, w, dh, 12288, 1536, 384);
+  g.gemm.trans_b = 1;
+  g.i1 = 1;  // recorded as a batch of row blocks flattened into M
+  Op gb = op(Kind::GeluBwd);
+  gb.t[0] = x;
+  gb.t[1] = dh;
+  gb.t[2] = dx;
+  std::vector<Op> p = {g, gb, release(dh)};
+  require(optimize(p, nullptr) == 1, "GELU backward folded");
+  auto l = live(p);
+  require(l.size() == 1 && l[0]->kind == Kind::Gemm && l[0]->t[2].id == dx.id &&
+              l[0]->gemm.gelu_grad_x == x.p && l[0]->gemm.c == dx.p && l[0]->t[6].id == x.id,
+          "the product writes dX through GELU'(x)");
+  std::vector<Op> q = {g, gb, binary(TL_ADD, dh, dh, other), release(dh)};
+  optimize(q, nullptr);
+  bool kept = false;
+  for (const Op *o : live(q)) kept = kept || o->kind == Kind::GeluBwd;
+  require(kept, "dH read again: not folded");
+}
+
 }  // namespace
 
 int main() {
@@ -606,6 +634,7 @@ int main() {
       {"projections_grouped", projections_grouped},
       {"attention_forward_fused", attention_forward_fused},
       {"attention_backward_fused", attention_backward_fused},
+      {"gelu_backward_into_gemm", gelu_backward_into_gemm},
   };
   for (const auto &[name, fn] : cases) {
     try {

@@ -239,7 +239,7 @@ class Dev:
         return self.host(out)
 
     def gemm(self, a, b, trans_a=False, trans_b=False, bias=None, c=None, beta=0.0, gelu=False,
-             precision=capi.TL_GEMM_TF32, addend=None):
+             precision=capi.TL_GEMM_TF32, addend=None, gelu_grad_x=None):
         a = np.asarray(a, np.float32)
         b = np.asarray(b, np.float32)
         ta, tb = self.t(a), self.t(b)
@@ -254,8 +254,11 @@ class Dev:
         tbias = self.t(bias) if bias is not None else None
         tadd = self.t(np.broadcast_to(np.asarray(addend, np.float32), out_shape)) \
             if addend is not None else None
+        tgx = self.t(np.broadcast_to(np.asarray(gelu_grad_x, np.float32), out_shape)) \
+            if gelu_grad_x is not None else None
         d = capi.TlGemmDesc()
         d.addend = tadd.data_ptr() if tadd is not None else None
+        d.gelu_grad_x = tgx.data_ptr() if tgx is not None else None
         d.a, d.b, d.c = ta.data_ptr(), tb.data_ptr(), tc.data_ptr()
         d.bias = tbias.data_ptr() if tbias is not None else None
         d.gelu_out = tg.data_ptr() if tg is not None else None

@@ -290,3 +290,23 @@ def test_grouped_products(dev, precision):
                       precision=precision)
     want = sum(ops.gemm(g, w, False, True) for g, w in zip(gs, ws))
     check(out, want)
+
+
+@pytest.mark.parametrize("m,n,k,form,precision", [
+    (12288, 1536, 384, "NT", capi.TL_GEMM_TF32),   # the FFN's dH = dY W2^T
+    (384, 384, 12288, "TN", capi.TL_GEMM_TF32),    # split-K: the slice-sum kernel's epilogue
+    (100, 70, 40, "NN", capi.TL_GEMM_TF32),        # ragged: per-thread stores
+    (257, 96, 64, "NT", capi.TL_GEMM_FP32),        # CUDA-core path
+])
+def test_gelu_backward_epilogue(dev, m, n, k, form, precision):
+    """C = GELU'(x) * (A B): bit-identical to the product followed by the GELU
+    backward kernel (the executor's GELU_derivative then hadamard)."""
+    rng = np.random.default_rng(m + n)
+    ta, tb = form[0] == "T", form[1] == "T"
+    a = rng.standard_normal((k, m) if ta else (m, k)).astype(np.float32)
+    b = rng.standard_normal((n, k) if tb else (k, n)).astype(np.float32) / 8
+    x = rng.standard_normal((m, n)).astype(np.float32)
+    prod = dev.gemm(a, b, trans_a=ta, trans_b=tb, precision=precision)
+    want = dev.gelu_backward(x, prod)
+    got = dev.gemm(a, b, trans_a=ta, trans_b=tb, precision=precision, gelu_grad_x=x)
+    np.testing.assert_array_equal(got, want)
