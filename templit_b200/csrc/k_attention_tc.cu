@@ -94,21 +94,6 @@ __device__ __forceinline__ void store_row32(uint32_t taddr, const Out &o, int32_
                          __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
 }
 
-// 16 columns of row `row` of a TMEM accumulator to out[t] columns col0..
-__device__ __forceinline__ void store_row16(uint32_t taddr, const Out &o, int32_t b, int32_t h,
-                                            uint32_t t, uint32_t col0, bool ok) {
-  uint32_t r[16];
-  ptx::tmem_load_32x32b_x16(taddr, r);
-  ptx::tmem_load_wait();
-  if (!ok) return;
-  float4 *dst =
-      reinterpret_cast<float4 *>(o.p + b * o.sb + h * o.sh + static_cast<uint64_t>(t) * o.ld + col0);
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-    dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                         __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-}
-
 // Scores of 16 columns of one row: s / divisor (as s * (1 / divisor)) +
 // mask (a mask row, when given); columns from `lim` on (past T, or past the
 // row under a causal mask) are -inf.  `open`: no mask row and every column
