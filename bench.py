@@ -51,7 +51,7 @@ def parse_args():
                    help="time one kernel case instead of the training step (profiling "
                         "driver): a tl_gemm shape, or configuration 3's attention")
     p.add_argument("--shape", default="12288x384x384:NN",
-                   help="--kernel gemm: MxNxK:form[:gelu_grad|:addend]")
+                   help="--kernel gemm: MxNxK:form[:gelu_grad|:addend|:bias_gelu]")
     return p.parse_args()
 
 
@@ -271,7 +271,7 @@ def run_kernel_case(args):
     if args.kernel == "infer":
         return run_inference_case(args)
     if args.kernel == "gemm":
-        parts = args.shape.split(":")  # MxNxK:form[:gelu_grad|:addend]
+        parts = args.shape.split(":")  # MxNxK:form[:gelu_grad|:addend|:bias_gelu]
         dims, form = parts[0], parts[1]
         aux = parts[2] if len(parts) > 2 else ""
         m, n, k = (int(v) for v in dims.split("x"))
@@ -282,10 +282,13 @@ def run_kernel_case(args):
         d = capi.TlGemmDesc(a=a.data_ptr(), b=b.data_ptr(), c=c.data_ptr(), m=m, n=n, k=k,
                             trans_a=int(ta), trans_b=int(tb), precision=capi.TL_GEMM_TF32)
         x_aux = torch.randn((m, n), device=dev, generator=g) if aux else None
+        bias = torch.randn(n, device=dev, generator=g)
         if aux == "gelu_grad":
             d.gelu_grad_x = x_aux.data_ptr()
         elif aux == "addend":
             d.addend = x_aux.data_ptr()
+        elif aux == "bias_gelu":  # the FFN's first product: C = A B + bias, GELU(C)
+            d.bias, d.gelu_out = bias.data_ptr(), x_aux.data_ptr()
         wsb = lib.tl_gemm_workspace_size(ctypes.byref(d))
         ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
         d.workspace, d.workspace_bytes = ws.data_ptr(), wsb

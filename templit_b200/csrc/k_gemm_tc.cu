@@ -366,18 +366,57 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
     uint8_t *obuf = out_base + e * C::BOXES * 4096;  // this warp's staging boxes
     uint32_t nbuf = 0, a_phase = 0;
     uint64_t *my_abar = &abar[e];
+    // Tiles of at most 128 columns give a warp at most two chunks, one per
+    // staging box, so the addend / GELU-backward boxes of the whole tile
+    // are loaded before its accumulator is ready.
+    constexpr bool kBoxPerChunk = C::BOXES == 2 && BN <= 128;
+    const bool early_aux = kBoxPerChunk && t.tma_epi && t.partial == nullptr &&
+                           (g.addend != nullptr || g.gelu_grad_x != nullptr) &&
+                           g.gelu_out == nullptr;
     for (uint64_t tile = blockIdx.x; tile < t.num_tiles; tile += gridDim.x) {
+      uint64_t z;
+      uint32_t s, mb, nb, grp;
+      decode_tile(t, tile, z, s, mb, nb, grp);
+      int32_t zc[3];
+      int ncz;
+      {
+        int32_t cz[TL_GEMM_MAX_BATCH_RANK];
+        batch_coords(g, z, cz);
+        map_coords(t.mc, cz, zc);
+        ncz = t.mc.nb;
+      }
+      uint32_t early_chunks = 0;
+      if (early_aux) {
+        for (int c = c0; c < BN / 32; c += 2) early_chunks += nb * BN + c * 32 < g.n;
+        if (lane == 0 && early_chunks) {
+          ptx::bulk_wait_group_read<0>();  // both boxes' stores have read them
+          ptx::mbar_arrive_expect_tx(my_abar, early_chunks * 4096);
+          for (uint32_t i = 0; i < early_chunks; ++i)
+            ptx::tma_load_nd(obuf + i * 4096, &maps.addend, my_abar,
+                             static_cast<int32_t>(nb * BN + (c0 + 2 * i) * 32),
+                             static_cast<int32_t>(mb * BM + q * 32), ncz, zc);
+        }
+        __syncwarp();
+      }
       // warp-uniform decisions: tcgen05.ld below needs all 32 lanes
       const bool got = ptx::mbar_wait_bounded(&tfull[acc], acc_phase, kWaitLimitNs);
+      const bool aborting = !__all_sync(0xffffffffu, got) ||
+                            __any_sync(0xffffffffu, *abort_flag != 0);
+      if (early_chunks) {
+        // the boxes are needed now, and must not be in flight at exit
+        const bool got_add = ptx::mbar_wait_bounded(my_abar, a_phase, kWaitLimitNs);
+        a_phase ^= 1;
+        if (!__all_sync(0xffffffffu, got_add)) {
+          if (lane == 0) timeout();
+          break;
+        }
+      }
       if (!__all_sync(0xffffffffu, got)) {
         if (lane == 0) timeout();
         break;
       }
-      if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+      if (aborting) break;
       ptx::tc_fence_after();
-      uint64_t z;
-      uint32_t s, mb, nb, grp;
-      decode_tile(t, tile, z, s, mb, nb, grp);
       uint64_t oa, ob, oc;
       batch_offsets(g, z, oa, ob, oc);
       // split-K slices store their raw partial product; the epilogue
@@ -405,17 +444,10 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
         // A warp's boxes alternate (two per warp; one for 256-wide tiles) so
         // a store is in flight while the next box is filled.
         const int32_t y0 = static_cast<int32_t>(mb * BM + q * 32);
-        int32_t zc[3];
-        int ncz;
         if (raw) {  // split-K slices: [groups x splits][M][N]
           zc[0] = static_cast<int32_t>(slice);
           zc[1] = zc[2] = 0;
           ncz = 1;
-        } else {
-          int32_t cz[TL_GEMM_MAX_BATCH_RANK];
-          batch_coords(g, z, cz);
-          map_coords(t.mc, cz, zc);
-          ncz = t.mc.nb;
         }
         // the addend box, or the GELU-backward input box (same map slot),
         // loaded by TMA into the staging box (L2 hits: the producer
@@ -430,13 +462,18 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
           if (n0 >= g.n) break;  // warp-uniform
           uint32_t r[32];
           ptx::tmem_load_32x32b_x32(tmem_base + acc * C::ACC_COLS + c * 32 + ((q * 32u) << 16), r);
-          uint8_t *box = obuf + (C::BOXES == 2 ? (nbuf++ & 1u) * 4096 : 0);
-          if (lane == 0) {  // the box's previous store has read it
-            if constexpr (C::BOXES == 2) ptx::bulk_wait_group_read<1>();
-            else ptx::bulk_wait_group_read<0>();
+          uint8_t *box;
+          if (early_aux) {
+            box = obuf + ((c - c0) >> 1) * 4096;  // loaded before the tile began
+          } else {
+            box = obuf + (C::BOXES == 2 ? (nbuf++ & 1u) * 4096 : 0);
+            if (lane == 0) {  // the box's previous store has read it
+              if constexpr (C::BOXES == 2) ptx::bulk_wait_group_read<1>();
+              else ptx::bulk_wait_group_read<0>();
+            }
+            __syncwarp();
           }
-          __syncwarp();
-          if (with_add) {
+          if (with_add && !early_aux) {
             if (lane == 0) {
               ptx::mbar_arrive_expect_tx(my_abar, 4096);
               ptx::tma_load_nd(box, &maps.addend, my_abar, static_cast<int32_t>(n0), y0, ncz, zc);
@@ -480,6 +517,11 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
             ptx::bulk_commit_group();
           }
           if (with_gelu) {
+            // the activations are computed while the store above reads
+            // the box (the only one of a 256-wide tile's warp)
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              v[j] = make_float4(gelu_f(v[j].x), gelu_f(v[j].y), gelu_f(v[j].z), gelu_f(v[j].w));
             uint8_t *gbox = obuf + (C::BOXES == 2 ? (nbuf++ & 1u) * 4096 : 0);
             if (lane == 0) {
               if constexpr (C::BOXES == 2) ptx::bulk_wait_group_read<1>();
@@ -487,9 +529,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
             }
             __syncwarp();
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              *reinterpret_cast<float4 *>(gbox + swz(lane, j)) =
-                  make_float4(gelu_f(v[j].x), gelu_f(v[j].y), gelu_f(v[j].z), gelu_f(v[j].w));
+            for (int j = 0; j < 8; ++j) *reinterpret_cast<float4 *>(gbox + swz(lane, j)) = v[j];
             ptx::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
@@ -646,9 +686,9 @@ struct TcPlan {
   size_t workspace;
 };
 
-TcPlan plan_tc(const GemmArgs &g) {
+TcPlan plan_width(const GemmArgs &g, int max_bn) {
   TcPlan p{};
-  p.bn = g.n > 128 ? 256 : (g.n > 64 ? 128 : 64);
+  p.bn = g.n > 128 ? max_bn : (g.n > 64 ? 128 : 64);
   // Enough tiles for every SM: pick the tile width with the least work per
   // SM, waves x (width + a fixed per-tile cost of ~64 columns), so N = 384
   // runs as 3 x 128 instead of 2 x 256 with a quarter of the MMAs wasted,
@@ -659,6 +699,7 @@ TcPlan plan_tc(const GemmArgs &g) {
   if (outs * mt * ((g.n + 255) / 256) >= static_cast<uint64_t>(kNumSMs) / 2) {
     uint64_t best = ~0ull;
     for (int bn : {64, 128, 192, 256}) {
+      if (bn > max_bn) continue;
       const uint64_t tiles = outs * mt * ((g.n + bn - 1) / bn);
       const uint64_t cost = (tiles + kNumSMs - 1) / kNumSMs * (bn + 64);
       if (cost < best) {
@@ -684,6 +725,20 @@ TcPlan plan_tc(const GemmArgs &g) {
       p.workspace = static_cast<size_t>(p.splits) * (outs / g.batch_count) * g.m * g.n *
                     sizeof(float);
     }
+  }
+  return p;
+}
+
+TcPlan plan_tc(const GemmArgs &g) {
+  const TcPlan p = plan_width(g, 256);
+  // An epilogue that loads a box per chunk (addend, GELU-backward input)
+  // loads all of a tile's boxes while the tile's MMAs run when it has a
+  // staging box per chunk, which only tiles up to 128 wide have.  Only
+  // unsplit products narrow their tiles: the K slicing, and so the
+  // summation order, stays the one the same product has without epilogue.
+  if (p.splits == 1 && (g.addend || g.gelu_grad_x) && !g.gelu_out) {
+    const TcPlan q = plan_width(g, 128);
+    if (q.splits == 1) return q;
   }
   return p;
 }

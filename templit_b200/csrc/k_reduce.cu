@@ -145,29 +145,30 @@ cols_block_kernel(const float *__restrict__ x, float *out, uint32_t K1, uint32_t
                               static_cast<size_t>(k1) * K2 + col) = r;
 }
 
-// Sums `splits` partial planes part[s, i] into out[i].  A CTA owns 32
-// consecutive outputs; warp w folds splits w, w + 8, w + 16, ... in order and
-// warp 0 then folds the 8 warp results in warp order, so the summation order
-// is fixed (deterministic) while 8 warps keep loads in flight.
-template <int OP>
-__global__ void __launch_bounds__(256)
+// Sums `splits` partial planes part[s, i] into out[i].  A CTA of W warps
+// owns 32 consecutive outputs; warp w folds splits w, w + W, w + 2W, ... in
+// order and warp 0 then folds the W warp results in warp order, so the
+// summation order is fixed (deterministic).  Many splits take W = 32, so
+// each thread has only a few loads in its dependent chain.
+template <int OP, int W>
+__global__ void __launch_bounds__(W * 32)
 combine_kernel(const float *__restrict__ part, float *out, uint64_t n,
                uint32_t splits) {
   pdl_enter();
-  __shared__ float acc_w[8][33];
+  __shared__ float acc_w[W][33];
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint64_t i = static_cast<uint64_t>(blockIdx.x) * 32 + lane;
   float acc = rinit<OP>();
   if (i < n) {
 #pragma unroll 4
-    for (uint32_t s = warp; s < splits; s += 8) acc = rcomb<OP>(acc, part[s * n + i]);
+    for (uint32_t s = warp; s < splits; s += W) acc = rcomb<OP>(acc, part[s * n + i]);
   }
   acc_w[warp][lane] = acc;
   __syncthreads();
   if (warp == 0 && i < n) {
     float r = acc_w[0][lane];
 #pragma unroll
-    for (int w = 1; w < 8; ++w) r = rcomb<OP>(r, acc_w[w][lane]);
+    for (int w = 1; w < W; ++w) r = rcomb<OP>(r, acc_w[w][lane]);
     out[i] = r;
   }
 }
@@ -370,7 +371,12 @@ int run_plan(const ReducePlan &pl, const float *x, float *out, void *ws,
         launch_pdl(cols_kernel<OP, 1>, grid_for(work, 256, 16), 256, 0, s, x, dst, pl.K1, pl.R, pl.K2, pl.splits, pl.chunk);
       int rc = launch_status("reduce cols");
       if (rc || pl.splits == 1) return rc;
-      launch_pdl(combine_kernel<OP>, static_cast<unsigned>((outs + 31) / 32), 256, 0, s, dst, out, outs, pl.splits);
+      if (pl.splits >= 64)
+        launch_pdl(combine_kernel<OP, 32>, static_cast<unsigned>((outs + 31) / 32), 1024, 0, s,
+                   dst, out, outs, pl.splits);
+      else
+        launch_pdl(combine_kernel<OP, 8>, static_cast<unsigned>((outs + 31) / 32), 256, 0, s,
+                   dst, out, outs, pl.splits);
       return launch_status("reduce cols combine");
     }
     default:
