@@ -160,6 +160,8 @@ def test_unary_scalar(dev, n):
     ((64, 192, 384), (1, 384)),       # bias gradient
     ((64, 192, 1536), (1536,)),       # bias gradient, lower rank
     ((64, 384, 384), (384, 384)),     # weight-gradient batch reduction
+    ((3000, 100), (1, 100)),          # ragged 128-column block
+    ((1029, 36), (36,)),              # rows not a multiple of the split
     ((2, 3, 4), (1, 3, 1)),           # non-adjacent
     ((5, 7, 3), (5, 1, 3)),           # middle
     ((3, 1, 5), (1, 1, 1)),
@@ -177,7 +179,8 @@ def test_reduce_sum(dev, shape, out):
 
 
 @pytest.mark.parametrize("shape,out", [((2, 3), (2, 1)), ((64, 6, 192, 192), (64, 6, 192, 1)),
-                                        ((9, 33), (1, 33)), ((4, 5, 6), (4, 1, 6))])
+                                        ((9, 33), (1, 33)), ((4, 5, 6), (4, 1, 6)),
+                                        ((5000, 68), (1, 68))])
 def test_reduce_max(dev, shape, out):
     x = rng(4).standard_normal(shape).astype(np.float32)
     np.testing.assert_array_equal(dev.reduce("max", x, out),
