@@ -440,8 +440,17 @@ rmsnorm_backward_regs_kernel(const float *__restrict__ g, const float *__restric
   pdl_enter();
   ROW_LOOP {
     const size_t off = static_cast<size_t>(row) * cols;
-    float4 gv[NV], yv[NV];
+    float4 gv[NV], yv[NV], av[NV];
     float ss = 0.0f, gy = 0.0f;
+    // the addend is loaded with the row's other inputs, before the two
+    // warp reductions, so its latency is not paid after them
+    if (addend) {
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const uint32_t c = (i * 32 + lane) * 4;
+        if (c < cols) av[i] = *reinterpret_cast<const float4 *>(addend + off + c);
+      }
+    }
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const uint32_t c = (i * 32 + lane) * 4;
@@ -461,10 +470,7 @@ rmsnorm_backward_regs_kernel(const float *__restrict__ g, const float *__restric
       if (c < cols) {
         float4 o = make_float4((gv[i].x - yv[i].x * mean) / r, (gv[i].y - yv[i].y * mean) / r,
                                (gv[i].z - yv[i].z * mean) / r, (gv[i].w - yv[i].w * mean) / r);
-        if (addend) {
-          const float4 a = *reinterpret_cast<const float4 *>(addend + off + c);
-          o = make_float4(a.x + o.x, a.y + o.y, a.z + o.z, a.w + o.w);
-        }
+        if (addend) o = make_float4(av[i].x + o.x, av[i].y + o.y, av[i].z + o.z, av[i].w + o.w);
         *reinterpret_cast<float4 *>(dx + off + c) = o;
       }
     }
