@@ -364,6 +364,16 @@ typedef struct tl_gemm_desc {
    * include/passes/execute.h) folded into the epilogue of the product that
    * makes the gradient.  Not with addend, beta, gelu_out or groups. */
   const float *gelu_grad_x;
+  /* Optional head-split store (c_heads > 0): the [M, N] result is written
+   * as [M / R, H, R, N / H] with H = c_heads, R = c_head_rows, i.e. the
+   * transpose(split_last_dim(mult(x, w)), 1, 2) of nn::MultiHeadAttention's
+   * query / key / value projections (include/nn/multi_head.h) done by the
+   * product's store: element (m, n) at c[((m / R) * H + n / Dh) * R * Dh +
+   * (m % R) * Dh + n % Dh], Dh = N / H.  Unbatched, TF32 / 3xTF32, dense C
+   * (ldc 0 or N), no addend, beta, GELU or GELU backward; N % H == 0,
+   * M % R == 0, Dh and R multiples of 32, every C 16-byte aligned.  Groups
+   * (GROUP_N) share the layout. */
+  uint32_t c_heads, c_head_rows;
 } tl_gemm_desc;
 int tl_gemm(const tl_gemm_desc *desc, void *stream);
 size_t tl_gemm_workspace_size(const tl_gemm_desc *desc);

@@ -55,7 +55,8 @@ class TlGemmDesc(Structure):
                 ("group_mode", c_int32), ("groups", c_uint32),
                 ("a_group", c_void_p * TL_GEMM_MAX_GROUPS), ("b_group", c_void_p * TL_GEMM_MAX_GROUPS),
                 ("c_group", c_void_p * TL_GEMM_MAX_GROUPS),
-                ("bias_group", c_void_p * TL_GEMM_MAX_GROUPS), ("gelu_grad_x", c_void_p)]
+                ("bias_group", c_void_p * TL_GEMM_MAX_GROUPS), ("gelu_grad_x", c_void_p),
+                ("c_heads", c_uint32), ("c_head_rows", c_uint32)]
 
 
 class TlAttnView(Structure):

@@ -14,6 +14,7 @@ struct GemmArgs {
   float *gelu_out;
   const float *addend;  // C's layout; C itself when accumulating (beta = 1)
   const float *gelu_grad_x;  // C's layout: C = GELU'(x) * product
+  uint32_t c_heads, c_head_rows;  // head-split store (tl_gemm_desc), 0: none
   uint32_t m, n, k;
   uint64_t lda, ldb, ldc;  // row strides of the stored matrices (elements)
   int trans_a, trans_b;

@@ -47,6 +47,19 @@ int to_args(const tl_gemm_desc *d, GemmArgs &g) {
   g.gelu_grad_x = d->gelu_grad_x;
   if (g.gelu_grad_x && (g.addend || d->gelu_out || d->group_mode != TL_GEMM_GROUP_NONE))
     return fail(TL_ERR_INVALID, "tl_gemm: gelu_grad_x takes no addend, beta, gelu_out or groups");
+  g.c_heads = d->c_heads;
+  g.c_head_rows = d->c_heads ? d->c_head_rows : 0;
+  if (d->c_heads) {
+    const uint32_t H = d->c_heads, R = d->c_head_rows;
+    if (g.addend || d->gelu_out || g.gelu_grad_x || d->batch_rank ||
+        d->group_mode == TL_GEMM_GROUP_K || (d->ldc && d->ldc != d->n) ||
+        d->precision == TL_GEMM_FP32)
+      return fail(TL_ERR_INVALID, "tl_gemm: a head-split store takes an unbatched TF32 product "
+                                  "with dense C and no addend, beta or GELU");
+    if (R == 0 || d->n % H || d->m % R || (d->n / H) % 32 || R % 32)
+      return fail(TL_ERR_INVALID, "tl_gemm: head-split store needs N % heads == 0, "
+                                  "M % rows == 0 and head width and rows multiples of 32");
+  }
   g.group_mode = d->group_mode;
   g.groups = 1;
   if (d->group_mode != TL_GEMM_GROUP_NONE) {
@@ -147,6 +160,10 @@ extern "C" int tl_gemm(const tl_gemm_desc *d, void *stream) {
     rc = launch_tc_gemm(g, d->workspace, d->workspace_bytes, s);
     if (rc != TL_ERR_UNSUPPORTED) return rc;
   }
+  if (g.c_heads)
+    return fail(TL_ERR_UNSUPPORTED,
+                "tl_gemm: a head-split store runs on the tensor-core path only (16-byte "
+                "aligned operands and rows)");
   if (g.groups > 1) {
     // one product per group: N groups independently; K groups as a chain
     // accumulating into C (bias and addend with the first)

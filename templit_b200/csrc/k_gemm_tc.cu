@@ -513,7 +513,16 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
           ptx::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            ptx::tma_store_nd(&maps.c[raw ? 0 : grp], box, static_cast<int32_t>(n0), y0, ncz, zc);
+            if (t.g.c_heads) {  // (head column, row in the head, head, row block)
+              const uint32_t dh = g.n / g.c_heads, yr = static_cast<uint32_t>(y0);
+              const int32_t hz[2] = {static_cast<int32_t>(n0 / dh),
+                                     static_cast<int32_t>(yr / g.c_head_rows)};
+              ptx::tma_store_nd(&maps.c[grp], box, static_cast<int32_t>(n0 % dh),
+                                static_cast<int32_t>(yr % g.c_head_rows), 2, hz);
+            } else {
+              ptx::tma_store_nd(&maps.c[raw ? 0 : grp], box, static_cast<int32_t>(n0), y0, ncz,
+                                zc);
+            }
             ptx::bulk_commit_group();
           }
           if (with_gelu) {
@@ -715,7 +724,8 @@ TcPlan plan_width(const GemmArgs &g, int max_bn) {
   // Few output tiles but a long K (weight gradients: K = every token of the
   // batch): cut K so the tiles times slices fill the GPU, keeping at least 8
   // k-tiles (256 of K) per slice.
-  if (g.batch_count == 1 && tiles < static_cast<uint64_t>(kNumSMs) / 2 && ktiles >= 16) {
+  if (g.batch_count == 1 && tiles < static_cast<uint64_t>(kNumSMs) / 2 && ktiles >= 16 &&
+      !g.c_heads) {
     uint64_t want = (kNumSMs + tiles - 1) / tiles;
     const uint64_t cap = ktiles / 8;
     if (want > cap) want = cap;
@@ -727,6 +737,22 @@ TcPlan plan_width(const GemmArgs &g, int max_bn) {
     }
   }
   return p;
+}
+
+// Map of a head-split C ([M / R, H, R, Dh], tl_gemm_desc.c_heads) as the
+// 4-D tensor (Dh, R, H, M / R), boxes of 32 x 32 (head columns x rows).
+bool make_head_map(CUtensorMap *map, float *base, const GemmArgs &g) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  const uint64_t H = g.c_heads, R = g.c_head_rows, Dh = g.n / g.c_heads;
+  const cuuint64_t dims[4] = {Dh, R, H, g.m / R};
+  const cuuint64_t st[3] = {Dh * 4, R * Dh * 4, H * R * Dh * 4};
+  const cuuint32_t box[4] = {32, 32, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, st, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
 }
 
 TcPlan plan_tc(const GemmArgs &g) {
@@ -807,10 +833,13 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
       float *ci = g.cg[i] ? g.cg[i] : g.c;
       const float *bi = g.groups > 1 ? g.biasg[i] : g.bias;
       t.tma_epi = aligned16(ci) && (!bi || aligned16(bi)) &&
-                  make_operand_map(&maps.c[i], ci, g.n, g.m, g.ldc, g, g.sc, 32, 32,
-                                   CU_TENSOR_MAP_SWIZZLE_128B, t.mc);
+                  (g.c_heads ? make_head_map(&maps.c[i], ci, g)
+                             : make_operand_map(&maps.c[i], ci, g.n, g.m, g.ldc, g, g.sc, 32,
+                                                32, CU_TENSOR_MAP_SWIZZLE_128B, t.mc));
     }
   }
+  if (g.c_heads && !t.tma_epi)
+    return fail(TL_ERR_UNSUPPORTED, "tl_gemm: head-split store needs the TMA epilogue");
   t.aux_prefetch = t.tma_epi && !partial && (g.addend || g.gelu_grad_x);
   // grouped outputs leave only through the TMA epilogue
   if (ngroups > 1 && !t.tma_epi)

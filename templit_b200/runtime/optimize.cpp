@@ -1052,6 +1052,49 @@ uint64_t fuse_attention(std::vector<Op> &p) {
 
 // ------------------------------------------------------- grouped products
 // (flattened products, op.i1 = 1, are ordinary M x N x K products here)
+// mult(X, W -> C) [+ bias]; transpose(C viewed as [B, T, H, D], 1, 2 -> Y)
+// with C read by nothing else: the split_heads of nn::MultiHeadAttention's
+// query, key and value projections (include/nn/multi_head.h) done by the
+// product's store, which writes Y's [B, H, T, D] layout directly
+// (tl_gemm_desc.c_heads), so C is never written and the transpose never runs.
+uint64_t fuse_head_split_store(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t i = 0; i < p.size(); ++i) {
+    Op &g = p[i];
+    if (g.dead || g.kind != Kind::Gemm || !g.t[2].p) continue;
+    const tl_gemm_desc &d = g.gemm;
+    if (d.group_mode != TL_GEMM_GROUP_NONE || d.batch_rank || d.beta != 0.0f || d.addend ||
+        d.gelu_out || d.gelu_grad_x || d.c_heads || (d.ldc && d.ldc != d.n) ||
+        d.precision == TL_GEMM_FP32)
+      continue;
+    const size_t j = first_reader(p, i, g.t[2].id);
+    if (j == kNone) continue;
+    const Op &tr = p[j];
+    if (tr.kind != Kind::Transpose || tr.t[0].rank != 4 || tr.i0 != 1 || tr.i1 != 2 ||
+        tr.t[0].p != g.t[2].p)
+      continue;
+    const TRef &src = tr.t[0], &dst = tr.t[1];
+    const uint32_t B = src.shape[0], T = src.shape[1], H = src.shape[2], D = src.shape[3];
+    if (static_cast<uint64_t>(B) * T != d.m || static_cast<uint64_t>(H) * D != d.n ||
+        D % 32 || T % 32 || dst.rank != 4 || dst.shape[0] != B || dst.shape[1] != H ||
+        dst.shape[2] != T || dst.shape[3] != D || (reinterpret_cast<uintptr_t>(dst.p) & 15u))
+      continue;
+    bool operand = false;  // Y must not be one of the product's inputs
+    for (int k : {0, 1, 3})
+      if (g.t[k].p && g.t[k].id == dst.id) operand = true;
+    if (operand || !unchanged_between(p, i, j, g.t[2].id) ||
+        !untouched_between(p, i, j, dst.id) || !dead_after(p, j, g.t[2].id))
+      continue;
+    g.gemm.c = dst.f();
+    g.gemm.c_heads = H;
+    g.gemm.c_head_rows = T;
+    g.t[2] = dst;
+    p[j].dead = true;
+    ++folded;
+  }
+  return folded;
+}
+
 bool groupable(const Op &op) {
   return !op.dead && op.kind == Kind::Gemm && op.gemm.group_mode == TL_GEMM_GROUP_NONE &&
          !op.gemm.gelu_out && !op.gemm.gelu_grad_x;
@@ -1061,7 +1104,8 @@ bool groupable(const Op &op) {
 bool same_product(const tl_gemm_desc &a, const tl_gemm_desc &b) {
   if (a.m != b.m || a.n != b.n || a.k != b.k || a.trans_a != b.trans_a ||
       a.trans_b != b.trans_b || a.precision != b.precision || a.lda != b.lda ||
-      a.ldb != b.ldb || a.ldc != b.ldc || a.batch_rank != b.batch_rank)
+      a.ldb != b.ldb || a.ldc != b.ldc || a.batch_rank != b.batch_rank ||
+      a.c_heads != b.c_heads || a.c_head_rows != b.c_head_rows)
     return false;
   for (uint32_t d = 0; d < a.batch_rank; ++d)
     if (a.batch_shape[d] != b.batch_shape[d] || a.a_batch_stride[d] != b.a_batch_stride[d] ||
@@ -1628,6 +1672,7 @@ uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live) {
   folded += fuse_gemm_gelu_backward(prog);
   folded += fuse_score_softmax(prog);
   folded += fuse_attention(prog);
+  folded += fuse_head_split_store(prog);
   folded += group_summed_products(prog);
   folded += group_shared_input(prog);
   folded += fuse_step(prog);

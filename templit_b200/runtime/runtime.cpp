@@ -677,6 +677,7 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
       key += op.gemm.trans_a ? " T" : " N";
       key += op.gemm.trans_b ? "T" : "N";
       if (op.gemm.groups > 1) key += " g" + std::to_string(op.gemm.groups);
+      if (op.gemm.c_heads) key += " heads";
     } else if (op.kind == Kind::Attention) {
       key += "#" + std::to_string(op.code) + " " + std::to_string(op.attn.B) + "x" +
              std::to_string(op.attn.H) + "x" + std::to_string(op.attn.T) + "x" +

@@ -442,6 +442,38 @@ void row_backward_tails() {
 }
 
 
+// a projection then split_heads (transpose(1, 2) of its [B, T, H, D] view):
+// the product stores the [B, H, T, D] layout itself and the transpose goes;
+// kept when the projection is read again later
+void head_split_store() {
+  auto x = tensor({4, 192, 384}), w = tensor({384, 384}), c = tensor({4, 192, 384});
+  auto y = tensor({4, 6, 192, 64});
+  auto view = [](TRef t) {
+    t.rank = 4;
+    t.shape[0] = 4;
+    t.shape[1] = 192;
+    t.shape[2] = 6;
+    t.shape[3] = 64;
+    return t;
+  };
+  Op split = transpose(view(c), y);
+  split.i0 = 1;
+  split.i1 = 2;
+  std::vector<Op> p = {gemm(x, w, c, 768, 384, 384), split, release(c)};
+  require(optimize(p, nullptr) == 1, "transpose folded into the store");
+  auto l = live(p);
+  require(l.size() == 1 && l[0]->t[2].id == y.id && l[0]->gemm.c == y.f() &&
+              l[0]->gemm.c_heads == 6 && l[0]->gemm.c_head_rows == 192,
+          "head-split store of the product");
+  auto c2 = tensor({4, 192, 384}), y2 = tensor({4, 6, 192, 64}), r = tensor({1, 384});
+  Op split2 = transpose(view(c2), y2);
+  split2.i0 = 1;
+  split2.i1 = 2;
+  std::vector<Op> q = {gemm(x, w, c2, 768, 384, 384), split2, reduce(c2, r), release(c2)};
+  require(optimize(q, nullptr) == 0, "projection read again: kept");
+  require(live(q).size() == 3 && !live(q)[0]->gemm.c_heads, "plain store kept");
+}
+
 // attention head split / merge: the GEMMs address the [B, T, H, D] tensors
 // through strides and both transposes go
 void head_transposes_become_strides() {
@@ -616,6 +648,7 @@ int main() {
       {"weight_gradient_tn", weight_gradient_tn},
       {"weight_gradient_observable_product_kept", weight_gradient_observable_product_kept},
       {"transpose_into_b", transpose_into_b},
+      {"head_split_store", head_split_store},
       {"transpose_kept_when_read_later", transpose_kept_when_read_later},
       {"softmax_backward", softmax_backward},
       {"rmsnorm_backward", rmsnorm_backward},

@@ -310,3 +310,34 @@ def test_gelu_backward_epilogue(dev, m, n, k, form, precision):
     want = dev.gelu_backward(x, prod)
     got = dev.gemm(a, b, trans_a=ta, trans_b=tb, precision=precision, gelu_grad_x=x)
     np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("groups", [1, 3])
+def test_head_split_store(dev, groups):
+    """C stored as [B, H, T, D] (tl_gemm_desc.c_heads): the query / key /
+    value projections of nn::MultiHeadAttention with split_heads folded into
+    the store.  Bit-identical to the [M, N] product transposed afterwards."""
+    B, T, H, D, K = 4, 64, 6, 64, 128
+    M, N = B * T, H * D
+    r = np.random.default_rng(11)
+    x = r.standard_normal((M, K)).astype(np.float32)
+    ws = [r.standard_normal((K, N)).astype(np.float32) / 8 for _ in range(groups)]
+    bs = [r.standard_normal(N).astype(np.float32) for _ in range(groups)]
+    plain = [dev.gemm(x, w, bias=b) for w, b in zip(ws, bs)]
+    tx = dev.t(x)
+    tw, tb = [dev.t(w) for w in ws], [dev.t(b) for b in bs]
+    outs = [dev.empty((B, H, T, D)) for _ in range(groups)]
+    d = capi.TlGemmDesc(a=tx.data_ptr(), b=tw[0].data_ptr(), c=outs[0].data_ptr(),
+                        bias=tb[0].data_ptr(), m=M, n=N, k=K, precision=capi.TL_GEMM_TF32)
+    d.c_heads, d.c_head_rows = H, T
+    if groups > 1:
+        d.group_mode, d.groups = capi.TL_GEMM_GROUP_N, groups
+        for i in range(groups):
+            d.b_group[i], d.c_group[i] = tw[i].data_ptr(), outs[i].data_ptr()
+            d.bias_group[i] = tb[i].data_ptr()
+    lib = capi.cuda_lib()
+    capi.check(lib.tl_gemm(ctypes.byref(d), dev.stream), lib, "tl_gemm heads")
+    for o, p_ in zip(outs, plain):
+        np.testing.assert_array_equal(dev.host(o), p_.reshape(B, T, H, D).transpose(0, 2, 1, 3))
+    d.c_head_rows = 48  # rows of a head not a multiple of 32: refused
+    assert lib.tl_gemm(ctypes.byref(d), dev.stream) == capi.TL_ERR_INVALID
