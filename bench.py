@@ -40,8 +40,8 @@ WORKLOAD = ("configs[3] GPT train step: vocab 2048, T=192, d=384, 4 pre-RMSNorm 
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
-    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     p.add_argument("--batch", type=int, default=64, help="sequences per GPU")
     p.add_argument("--no-fusion", action="store_true")
@@ -156,9 +156,10 @@ def run_reference(args):
 
 
 # ----------------------------------------------------------------- roofline
-def gemm_roofline(profile_path, peak_tflops, peak_source):
-    """Dominant kernel: the tcgen05 GEMM.  Achieved = executed GEMM FLOPs of
-    one profiled step / the GEMM launches' CUDA-event time."""
+def gemm_roofline(profile_path, peak_tflops, peak_source, timed_ms_per_step=None):
+    """Dominant kernel: the tcgen05 GEMM.  The profiled step (an event pair
+    around every op) gives the GEMMs' share of the step; achieved = executed
+    GEMM FLOPs per step / (that share x the timed steps' ms per step)."""
     with open(profile_path) as f:
         prof = json.load(f)["ops"]
     flops = ms = 0.0
@@ -193,7 +194,9 @@ def gemm_roofline(profile_path, peak_tflops, peak_source):
         a_flops += (2.0 if code == "2" else 4.0) * b * h * t * t * d * o["calls"]
         a_ms += o["ms"]
         a_launches += o["calls"]
-    achieved = flops / (ms * 1e-3) / 1e12
+    share = ms / total_ms if total_ms else 1.0
+    gemm_ms = share * timed_ms_per_step if timed_ms_per_step else ms
+    achieved = flops / (gemm_ms * 1e-3) / 1e12
     return {"bound": "tensor", "kernel": "tc_gemm_kernel (tcgen05 kind::tf32)",
             "achieved": round(achieved, 1), "peak": peak_tflops, "unit": "TFLOP/s",
             "frac": round(achieved / peak_tflops, 4) if peak_tflops else None,
@@ -204,7 +207,9 @@ def gemm_roofline(profile_path, peak_tflops, peak_source):
             # reads (A once, B); C stays in L2 when the kernel ends
             "traffic": 19548928, "traffic_unit": "bytes per launch",
             "traffic_shape": "12288x384x384 NN",
-            "flops_per_step": flops, "gemm_ms_per_step": round(ms, 4),
+            "flops_per_step": flops, "gemm_ms_per_step": round(gemm_ms, 4),
+            "gemm_ms_profiled_step": round(ms, 4),
+            "timing": "GEMM share of the profiled step x the timed steps' ms per step",
             "gemm_launches_per_step": launches,
             "gemm_share_of_step": round(ms / total_ms, 3) if total_ms else None,
             "attention": {"kernel": "attn_fwd / attn_bwd_q / attn_bwd_kv (tcgen05 kind::tf32)",
@@ -452,29 +457,31 @@ def main():
         torch.cuda.synchronize()
 
     def timed(with_host_io):
+        """K steps between two events on the backend stream (max over
+        ranks), plus an event after every step for the per-step median."""
         barrier()
-        ev0 = torch.cuda.Event(enable_timing=True)
-        ev1 = torch.cuda.Event(enable_timing=True)
-        ev0.record(stream)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        evs[0].record(stream)
         for i in range(args.steps):
             if with_host_io:
                 load_next()
             losses.append(step())
-        ev1.record(stream)
-        ev1.synchronize()
+            evs[i + 1].record(stream)
+        evs[-1].synchronize()
         barrier()
-        ms = ev0.elapsed_time(ev1)
+        ms = evs[0].elapsed_time(evs[-1])
+        per = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
         if world > 1:
             t = torch.tensor([ms], device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t.item())
-        return ms
+        return ms, per
 
     stats0 = (ctypes.c_uint64 * 11)()
     capi.check(lib.tlg_stats(h, stats0), lib, "stats")
     with ClockSampler(local) as clocks:
-        ms_value = timed(with_host_io=False)
-        ms_e2e = timed(with_host_io=True)
+        ms_value, per_value = timed(with_host_io=False)
+        ms_e2e, per_e2e = timed(with_host_io=True)
     stats1 = (ctypes.c_uint64 * 11)()
     capi.check(lib.tlg_stats(h, stats1), lib, "stats")
     kernels = int(stats1[3] - stats0[3]) // 2  # two timed regions of K steps each
@@ -484,7 +491,8 @@ def main():
     e2e = total_tokens / (ms_e2e * 1e-3)
 
     roof = None
-    prof_path = args.profile or os.path.join(ROOT, "gpurun_out", f"gpt_profile_rank{rank}.json")
+    prof_path = args.profile or os.path.join(tempfile.gettempdir(),
+                                             f"templit_gpt_profile_{os.getpid()}_rank{rank}.json")
     try:
         os.makedirs(os.path.dirname(prof_path), exist_ok=True)
         capi.check(lib.tlg_profile(h, prof_path.encode(), 1), lib, "profile")
@@ -492,9 +500,16 @@ def main():
         if rank == 0:
             peak = measure_tf32_peak(torch)
             roof, _ = gemm_roofline(prof_path, round(peak, 1),
-                                    "cuBLAS TF32 8192^3 measured in this run (burst)")
+                                    "cuBLAS TF32 8192^3 measured in this run (burst)",
+                                    ms_value / args.steps)
     except Exception as exc:  # the bench line still prints
         roof = {"error": str(exc)}
+    # GEMM launches by path over the whole run (eager windows and captures;
+    # replays re-launch what was captured): a product the tensor-core path
+    # refused would run on the CUDA cores
+    g_tc, g_simt, g_refused = (ctypes.c_uint64() for _ in range(3))
+    capi.cuda_lib().tl_gemm_counters(ctypes.byref(g_tc), ctypes.byref(g_simt),
+                                     ctypes.byref(g_refused))
 
     if world > 1:
         dist.barrier()
@@ -503,13 +518,21 @@ def main():
     capi.check(lib.tlg_destroy(h), lib, "destroy")
     if world > 1:
         dist.destroy_process_group()
+    if g_simt.value:
+        print(f"bench: {g_simt.value} GEMM launches ran on the CUDA cores "
+              f"({g_refused.value} refused by the tensor-core path)", file=sys.stderr)
+        return 1
     if rank != 0:
         return 0
     cpu = cpu_baseline_gpt(steps=1, batch=2) if world == 1 else None
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": max(3, args.warmup),
-        "ms_per_step": round(ms_value / args.steps, 4), "higher_is_better": True,
+        "ms_per_step": round(ms_value / args.steps, 4),
+        "ms_per_step_median": round(statistics.median(per_value), 4),
+        "ms_per_step_p10_p90": [round(float(np.percentile(per_value, 10)), 4),
+                                round(float(np.percentile(per_value, 90)), 4)],
+        "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (Zipf(1.1) token windows; e2e draws them with the token pipeline "
                 "from a Zipf(1.1) token file; N(0,0.02) weights, zero biases)",
@@ -518,7 +541,9 @@ def main():
                    "gemm_operands": "tf32 tensor cores, fp32 accumulate",
                    "l2": "per-step activations (GBs) exceed the 126 MB L2"},
         "e2e": {"value": round(e2e, 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": 2 * n_tok * 4, "d2h_bytes_per_step": n_tok * 4},
+                "h2d_bytes_per_step": 2 * n_tok * 4, "d2h_bytes_per_step": n_tok * 4,
+                "ms_per_step_median": round(statistics.median(per_e2e), 4)},
+        "gemm_launches_by_path": {"tensor_core": g_tc.value, "cuda_core": g_simt.value},
         "gpu_launches": kernels,
         "roofline": roof, "cpu_baseline": cpu, "clocks": clocks.summary(),
         "loss_first_last": [round(losses[0], 4), round(losses[-1], 4)],

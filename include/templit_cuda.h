@@ -161,9 +161,11 @@ size_t tl_reduce_workspace_size(const uint32_t *x_shape, int x_rank,
  * the library until the process exits.  A reduction whose
  * tl_reduce_workspace_size() exceeds that returns TL_ERR_RANGE.  The first
  * call on each device looks up the array's device address (make it before
- * any stream capture).  All calls share the array: calls that can overlap
- * on the GPU (other streams, other host threads) race on it; calls ordered
- * on one stream do not.
+ * any stream capture); first calls from several host threads at once are
+ * safe.  The address stays cached for the process, so do not call this
+ * again on a device after cudaDeviceReset.  All calls share the array:
+ * calls that can overlap on the GPU (other streams, other host threads)
+ * race on it; calls ordered on one stream do not.
  */
 int tl_reduce_noalloc(int op, const float *x, const uint32_t *x_shape, int x_rank,
                       float *out, const uint32_t *out_shape, int out_rank, void *stream);
@@ -296,7 +298,9 @@ size_t tl_multi_clip_adamw_workspace_size(uint32_t n_chunks);
 enum tl_gemm_precision {
   TL_GEMM_TF32 = 0,   /* tcgen05 kind::tf32 tensor cores, fp32 accumulate */
   TL_GEMM_FP32 = 1,   /* CUDA-core fp32 FMA (exact fp32 products)         */
-  TL_GEMM_3XTF32 = 2  /* tcgen05 with split big/small tf32 operands        */
+  TL_GEMM_3XTF32 = 2  /* tcgen05 with split big/small tf32 operands: each
+                         product is big*big + big*small + small*big of the
+                         operands' tf32 halves, about fp32's accuracy   */
 };
 #define TL_GEMM_MAX_BATCH_RANK 6
 #define TL_GEMM_MAX_GROUPS 4
@@ -377,6 +381,18 @@ typedef struct tl_gemm_desc {
 } tl_gemm_desc;
 int tl_gemm(const tl_gemm_desc *desc, void *stream);
 size_t tl_gemm_workspace_size(const tl_gemm_desc *desc);
+/* 1 when tl_gemm runs this descriptor on the tcgen05 tensor-core kernel, 0
+ * when it would take the CUDA-core kernel (TL_GEMM_FP32, fewer than 2^20
+ * multiply-adds, operands TMA cannot address) or the descriptor is invalid.
+ * Products that only the tensor-core path accepts (a head-split store) are
+ * formed only when this holds.  No counterpart in the reference (its mult
+ * has one Metal kernel, src/my_metal/runtime.cpp:375-505). */
+int tl_gemm_on_tensor_cores(const tl_gemm_desc *desc);
+/* Launch counts of tl_gemm since the library loaded: on the tensor cores,
+ * on the CUDA cores, and the CUDA-core launches of products that asked for
+ * tensor cores but whose operands that path refused (a layout regression
+ * shows here instead of only as a slowdown).  NULL pointers are skipped. */
+void tl_gemm_counters(uint64_t *tensor_core, uint64_t *cuda_core, uint64_t *cuda_core_refused);
 
 /* -------------------------------------------------------------- attention */
 /* The attention core of nn::MultiHeadAttention (include/nn/multi_head.h:

@@ -166,6 +166,8 @@ CUDA_ABI = {
     "tl_multi_clip_adamw_workspace_size": (c_size_t, [c_uint32]),
     "tl_gemm": (c_int, [POINTER(TlGemmDesc), c_void_p]),
     "tl_gemm_workspace_size": (c_size_t, [POINTER(TlGemmDesc)]),
+    "tl_gemm_on_tensor_cores": (c_int, [POINTER(TlGemmDesc)]),
+    "tl_gemm_counters": (None, [POINTER(c_uint64), POINTER(c_uint64), POINTER(c_uint64)]),
 }
 
 GPT_ABI = {

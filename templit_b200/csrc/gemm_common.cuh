@@ -15,6 +15,7 @@ struct GemmArgs {
   const float *addend;  // C's layout; C itself when accumulating (beta = 1)
   const float *gelu_grad_x;  // C's layout: C = GELU'(x) * product
   uint32_t c_heads, c_head_rows;  // head-split store (tl_gemm_desc), 0: none
+  int split_tf32;  // TL_GEMM_3XTF32: big and small tf32 halves of each operand
   uint32_t m, n, k;
   uint64_t lda, ldb, ldc;  // row strides of the stored matrices (elements)
   int trans_a, trans_b;
@@ -72,5 +73,8 @@ int launch_sgemm(const GemmArgs &g, cudaStream_t s);
 // tc_gemm_workspace); with less room the product runs unsplit.
 int launch_tc_gemm(const GemmArgs &g, void *workspace, size_t workspace_bytes, cudaStream_t s);
 size_t tc_gemm_workspace(const GemmArgs &g);
+// The tensor-core path's operand rules (TMA: 16-byte aligned bases, row and
+// batch strides; at most three walked batch dims per operand).
+bool tc_gemm_supported(const GemmArgs &g);
 
 }  // namespace tl

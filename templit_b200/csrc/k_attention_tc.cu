@@ -3,16 +3,18 @@
 // multi_head.h:45-52; softmax derivative include/passes/execute.h:291-308)
 // without its T x T score and score-gradient tensors in HBM.
 //
-// Forward, one CTA per (batch, head, 128 query rows), 576 threads:
-//   warp 0       TMA: the Q tile, all of K, all of V
+// Forward, one CTA per (batch, head, 128 query rows), 320 threads, two
+// CTAs per SM:
+//   warp 0       TMA: the Q tile, all of K, all of V; TMA stores of P
 //   warp 1       TMEM owner, MMA issuer: S = Q K^T into TMEM (128 x nk fp32),
 //                then O = P V block by block as the softmax hands over P
-//   warps 2..17  softmax, four warps per TMEM lane quadrant on interleaved
-//                16-key pieces: the row max of S / divisor + mask, then the
-//                sum of exponentials (both merged across the four warps
-//                through shared memory), then P = exp(x - max) / sum written
-//                into shared memory in the MMA's K-major layout (also the
-//                TMA box of the P store); finally O from TMEM to global.
+//   warps 2..9   softmax, two warps per TMEM lane quadrant on alternate
+//                key pieces: one pass for the row max and the sum of
+//                exponentials of S / divisor + mask (merged across the two
+//                warps through shared memory), then P = exp(x - max) / sum
+//                written in 32-key blocks into a two-slot shared-memory ring
+//                in the MMA's K-major layout (also the TMA box of the P
+//                store); finally O from TMEM to global.
 // P leaves through TMA stores (the backward reads it); S never leaves TMEM.
 //
 // Backward, query side (same CTA shape): dP = dO V^T into TMEM; the softmax

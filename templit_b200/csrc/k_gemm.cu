@@ -1,8 +1,9 @@
 // tl_gemm: validates the descriptor and routes to the tcgen05 tensor-core
-// kernel (TL_GEMM_TF32) or the CUDA-core fp32 kernel (TL_GEMM_FP32, tiny
-// problems, and operands TMA cannot address).
+// kernel (TL_GEMM_TF32, TL_GEMM_3XTF32) or the CUDA-core fp32 kernel
+// (TL_GEMM_FP32, tiny problems, and operands TMA cannot address).
 #include "gemm_common.cuh"
 
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 
@@ -40,6 +41,7 @@ int to_args(const tl_gemm_desc *d, GemmArgs &g) {
   g.k = d->k;
   g.trans_a = d->trans_a != 0;
   g.trans_b = d->trans_b != 0;
+  g.split_tf32 = d->precision == TL_GEMM_3XTF32;
   g.beta = d->beta;
   if (d->addend && d->beta != 0.0f && d->addend != d->c)
     return fail(TL_ERR_INVALID, "tl_gemm: addend with beta = 1 must be C");
@@ -125,6 +127,11 @@ bool wants_tc(const tl_gemm_desc *d, const GemmArgs &g) {
          g.k > 0;
 }
 
+// Launch counters by path (tl_gemm_counters): tensor-core launches, CUDA-core
+// launches, and the CUDA-core launches of products that asked for tensor
+// cores but whose operands the tensor-core path refused.
+std::atomic<uint64_t> g_tc_launches{0}, g_simt_launches{0}, g_simt_refused{0};
+
 }  // namespace
 }  // namespace tl
 
@@ -147,6 +154,19 @@ extern "C" size_t tl_gemm_workspace_size(const tl_gemm_desc *d) {
   return ws;
 }
 
+extern "C" int tl_gemm_on_tensor_cores(const tl_gemm_desc *d) {
+  GemmArgs g;
+  if (to_args(d, g) || g.m == 0 || g.n == 0 || g.batch_count == 0) return 0;
+  return wants_tc(d, g) && tc_gemm_supported(g) ? 1 : 0;
+}
+
+extern "C" void tl_gemm_counters(uint64_t *tensor_core, uint64_t *cuda_core,
+                                 uint64_t *cuda_core_refused) {
+  if (tensor_core) *tensor_core = g_tc_launches.load();
+  if (cuda_core) *cuda_core = g_simt_launches.load();
+  if (cuda_core_refused) *cuda_core_refused = g_simt_refused.load();
+}
+
 extern "C" int tl_gemm(const tl_gemm_desc *d, void *stream) {
   GemmArgs g;
   int rc = to_args(d, g);
@@ -154,11 +174,13 @@ extern "C" int tl_gemm(const tl_gemm_desc *d, void *stream) {
   if (g.m == 0 || g.n == 0 || g.batch_count == 0) return TL_OK;
   if (!g.c || (g.k && (!g.a || !g.b))) return fail(TL_ERR_INVALID, "tl_gemm: null pointer");
   cudaStream_t s = as_stream(stream);
-  if (wants_tc(d, g)) {
-    if (d->precision == TL_GEMM_3XTF32)
-      return fail(TL_ERR_UNSUPPORTED, "tl_gemm: 3xTF32 is not built in this version");
+  const bool tc = wants_tc(d, g);
+  if (tc) {
     rc = launch_tc_gemm(g, d->workspace, d->workspace_bytes, s);
-    if (rc != TL_ERR_UNSUPPORTED) return rc;
+    if (rc != TL_ERR_UNSUPPORTED) {
+      if (rc == TL_OK) ++g_tc_launches;
+      return rc;
+    }
   }
   if (g.c_heads)
     return fail(TL_ERR_UNSUPPORTED,
@@ -189,5 +211,7 @@ extern "C" int tl_gemm(const tl_gemm_desc *d, void *stream) {
     }
     return TL_OK;
   }
+  ++g_simt_launches;
+  if (tc) ++g_simt_refused;
   return launch_sgemm(g, s);
 }

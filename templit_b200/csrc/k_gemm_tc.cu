@@ -18,6 +18,12 @@
 // need no transpose pass.  Batched operands use a 3-D tensor map whose third
 // dimension walks whole matrices, so a k-tile never reads a neighbour's rows.
 //
+// 3xTF32 (TL_GEMM_3XTF32, SPLIT): four more warps split every landed k-tile
+// in shared memory into its tf32-rounded big part (written in place) and the
+// tf32-rounded remainder (written to a second half of the stage), and the
+// MMA warp accumulates big*small + small*big + big*big per k-step, which
+// keeps about 21 of fp32's 24 significand bits of every product.
+//
 // Every mbarrier wait is bounded (2 s): on timeout the CTA raises
 // TL_FLAG_TIMEOUT in the device status word, drains what it issued and
 // returns instead of hanging the GPU.
@@ -47,7 +53,7 @@ EncodeTiledFn tensor_map_encoder() {
 namespace {
 
 constexpr int kEpiWarps = 8;  // two warps per TMEM lane quadrant
-constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kConvWarps = 4;  // 3xTF32 operand splitters
 constexpr int BM = 128, BK = 32;
 constexpr uint32_t kA_BYTES = BM * BK * 4;  // 16 KB
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
@@ -94,20 +100,30 @@ struct TcArgs {
   bool aux_prefetch;
 };
 
-template <int BN>
+template <int BN, bool SPLIT>
 struct Cfg {
+  static constexpr int THREADS = 64 + 32 * kEpiWarps + (SPLIT ? 32 * kConvWarps : 0);
   static constexpr uint32_t B_BYTES = BN * BK * 4;
-  static constexpr uint32_t STAGE_BYTES = kA_BYTES + B_BYTES;
+  // bytes TMA brings per stage (A then B); a 3xTF32 stage holds their
+  // small parts after them in the same layout
+  static constexpr uint32_t LOAD_BYTES = kA_BYTES + B_BYTES;
+  static constexpr uint32_t STAGE_BYTES = SPLIT ? 2 * LOAD_BYTES : LOAD_BYTES;
   // staging boxes for the TMA stores: per epilogue warp two 32 x 32 fp32
-  // boxes (4 KB each, 128-byte swizzled rows), one for the widest tile
-  static constexpr int BOXES = BN == 256 ? 1 : 2;
+  // boxes (4 KB each, 128-byte swizzled rows), one for the widest tile and
+  // for 3xTF32 (whose stages are twice as large)
+  static constexpr int BOXES = (BN == 256 || SPLIT) ? 1 : 2;
   static constexpr uint32_t OUT_BYTES = kEpiWarps * BOXES * 4096;
-  static constexpr int STAGES_FIT = static_cast<int>((232448u - 1280u - OUT_BYTES) / STAGE_BYTES);
+  static constexpr uint32_t BAR_BYTES = 384;
+  static constexpr int STAGES_FIT =
+      static_cast<int>((232448u - 1024u - BAR_BYTES - OUT_BYTES) / STAGE_BYTES);
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   // second accumulator at a power-of-two column; allocation a power of two
   static constexpr uint32_t ACC_COLS = BN == 192 ? 256 : BN;
   static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS < 32 ? 32 : 2 * ACC_COLS;
-  static constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + OUT_BYTES + 256;
+  static constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + OUT_BYTES + BAR_BYTES;
+  // barriers: full, empty, conv (STAGES each), tfull, tempty (2 each),
+  // abar (per epilogue warp), then the TMEM slot and the abort word
+  static_assert((3 * STAGES + 4 + kEpiWarps) * 8 + 8 <= BAR_BYTES, "barrier area");
 };
 
 // tile = ((z * splits + s) * nt + nb) * mt + mb: consecutive CTAs take
@@ -155,10 +171,10 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t j) {
   return r * 128u + ((j ^ (r & 7u)) << 4);
 }
 
-template <int BN, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, bool A_MN, bool B_MN, bool SPLIT>
+__global__ void __launch_bounds__(Cfg<BN, SPLIT>::THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, SPLIT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -170,7 +186,8 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
   uint64_t *tfull = bars + 2 * C::STAGES;
   uint64_t *tempty = tfull + 2;
   uint64_t *abar = tempty + 2;  // one per epilogue warp: addend box loaded
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(abar + kEpiWarps);
+  uint64_t *conv = abar + kEpiWarps;  // 3xTF32: stage split into big / small parts
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(conv + C::STAGES);
   volatile uint32_t *abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -180,6 +197,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
     for (int s = 0; s < C::STAGES; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
+      if (SPLIT) ptx::mbar_init(&conv[s], kConvWarps);
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&tfull[a], 1);
@@ -244,7 +262,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
           }
           uint8_t *sa = stage_base + stage * C::STAGE_BYTES;
           uint8_t *sb = sa + kA_BYTES;
-          ptx::mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          ptx::mbar_arrive_expect_tx(&full[stage], C::LOAD_BYTES);
           // K groups walk group after group; N groups use their own B
           uint32_t kg = 0, kl = kb;
           if (t.kgroups) {
@@ -317,7 +335,8 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
         decode_tile(t, tile, z, s, mb, nb, grp);
         k_range(t, ktiles, s, kb0, kb1);
         for (uint32_t kb = kb0; kb < kb1; ++kb) {
-          if (!ptx::mbar_wait_bounded(&full[stage], phase, kWaitLimitNs)) {
+          if (!ptx::mbar_wait_bounded(SPLIT ? &conv[stage] : &full[stage], phase,
+                                      kWaitLimitNs)) {
             timeout();
             ok = false;
             break;
@@ -325,15 +344,26 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
           ptx::tc_fence_after();
           const uint32_t sa = ptx::smem_addr(stage_base + stage * C::STAGE_BYTES);
           const uint32_t sb = sa + kA_BYTES;
+          auto a_desc = [&](uint32_t base, int kk) {
+            return A_MN ? ptx::smem_desc(base + kk * 1024, 4096, 512, ptx::kSwizzle128B32BAtom)
+                        : ptx::smem_desc(base + kk * 32, 16, 1024, ptx::kSwizzle128B);
+          };
+          auto b_desc = [&](uint32_t base, int kk) {
+            return B_MN ? ptx::smem_desc(base + kk * 1024, 4096, 512, ptx::kSwizzle128B32BAtom)
+                        : ptx::smem_desc(base + kk * 32, 16, 1024, ptx::kSwizzle128B);
+          };
 #pragma unroll
           for (int kk = 0; kk < BK / 8; ++kk) {
-            const uint64_t ad =
-                A_MN ? ptx::smem_desc(sa + kk * 1024, 4096, 512, ptx::kSwizzle128B32BAtom)
-                     : ptx::smem_desc(sa + kk * 32, 16, 1024, ptx::kSwizzle128B);
-            const uint64_t bd =
-                B_MN ? ptx::smem_desc(sb + kk * 1024, 4096, 512, ptx::kSwizzle128B32BAtom)
-                     : ptx::smem_desc(sb + kk * 32, 16, 1024, ptx::kSwizzle128B);
-            ptx::mma_tf32(d_tmem, ad, bd, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+            const uint64_t ad = a_desc(sa, kk), bd = b_desc(sb, kk);
+            const uint32_t acc_in = (kb != kb0 || kk != 0) ? 1u : 0u;
+            if constexpr (SPLIT) {
+              // small terms first, then the big product
+              ptx::mma_tf32(d_tmem, ad, b_desc(sb + C::LOAD_BYTES, kk), idesc, acc_in);
+              ptx::mma_tf32(d_tmem, a_desc(sa + C::LOAD_BYTES, kk), bd, idesc, 1u);
+              ptx::mma_tf32(d_tmem, ad, bd, idesc, 1u);
+            } else {
+              ptx::mma_tf32(d_tmem, ad, bd, idesc, acc_in);
+            }
           }
           issued_any = true;
           ptx::mma_commit(&empty[stage]);  // stage reusable once these MMAs finish
@@ -353,6 +383,47 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
         // let in-flight MMAs finish before TMEM is released
         ptx::mma_commit(&tfull[acc]);
         ptx::mbar_wait_bounded(&tfull[acc], acc_phase, kWaitLimitNs);
+      }
+    }
+  } else if (SPLIT && warp >= 2 + kEpiWarps) {
+    // ------------------------------------------------ 3xTF32 operand split
+    // Each landed stage: x -> big = tf32(x) in place, small = tf32(x - big)
+    // at the same offset in the stage's second half (x - big is exact).
+    const uint32_t ct = threadIdx.x - (64 + 32 * kEpiWarps);
+    uint32_t stage = 0, phase = 0;
+    bool stop = false;
+    for (uint64_t tile = blockIdx.x; tile < t.num_tiles && !stop && !*abort_flag;
+         tile += gridDim.x) {
+      uint64_t z;
+      uint32_t s, mb, nb, kb0, kb1, grp;
+      decode_tile(t, tile, z, s, mb, nb, grp);
+      k_range(t, ktiles, s, kb0, kb1);
+      for (uint32_t kb = kb0; kb < kb1; ++kb) {
+        const bool got = ptx::mbar_wait_bounded(&full[stage], phase, kWaitLimitNs);
+        if (!__all_sync(0xffffffffu, got)) {
+          if (lane == 0) timeout();
+          stop = true;
+          break;
+        }
+        float4 *big = reinterpret_cast<float4 *>(stage_base + stage * C::STAGE_BYTES);
+        float4 *small = big + C::LOAD_BYTES / 16;
+#pragma unroll 4
+        for (uint32_t i = ct; i < C::LOAD_BYTES / 16; i += 32 * kConvWarps) {
+          const float4 x = big[i];
+          const float4 h = make_float4(ptx::round_tf32(x.x), ptx::round_tf32(x.y),
+                                       ptx::round_tf32(x.z), ptx::round_tf32(x.w));
+          big[i] = h;
+          small[i] = make_float4(ptx::round_tf32(x.x - h.x), ptx::round_tf32(x.y - h.y),
+                                 ptx::round_tf32(x.z - h.z), ptx::round_tf32(x.w - h.w));
+        }
+        // generic-proxy writes, read next by the tensor cores (async proxy)
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&conv[stage]);
+        if (++stage == C::STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
       }
     }
   } else {
@@ -756,7 +827,8 @@ bool make_head_map(CUtensorMap *map, float *base, const GemmArgs &g) {
 }
 
 TcPlan plan_tc(const GemmArgs &g) {
-  const TcPlan p = plan_width(g, 256);
+  // 3xTF32 stages are twice as large: tiles of at most 128 columns
+  const TcPlan p = plan_width(g, g.split_tf32 ? 128 : 256);
   // An epilogue that loads a box per chunk (addend, GELU-backward input)
   // loads all of a tile's boxes while the tile's MMAs run when it has a
   // staging box per chunk, which only tiles up to 128 wide have.  Only
@@ -769,9 +841,9 @@ TcPlan plan_tc(const GemmArgs &g) {
   return p;
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, bool SPLIT>
 int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaStream_t s) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, SPLIT>;
   TcArgs t{};
   t.g = g;
   t.mt = (g.m + BM - 1) / BM;
@@ -846,7 +918,7 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
     return fail(TL_ERR_UNSUPPORTED, "tl_gemm: grouped outputs need 16-byte rows");
   static bool attr_set = false;
   if (!attr_set) {
-    int rc = check_cuda(cudaFuncSetAttribute(tc_gemm_kernel<BN, A_MN, B_MN>,
+    int rc = check_cuda(cudaFuncSetAttribute(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(C::SMEM)),
                         "tl_gemm smem attribute");
@@ -854,8 +926,8 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
     attr_set = true;
   }
   const uint64_t grid = t.num_tiles < static_cast<uint64_t>(kNumSMs) ? t.num_tiles : kNumSMs;
-  launch_pdl(tc_gemm_kernel<BN, A_MN, B_MN>, static_cast<unsigned>(grid), kThreads, C::SMEM, s,
-             maps, t);
+  launch_pdl(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT>, static_cast<unsigned>(grid), C::THREADS,
+             C::SMEM, s, maps, t);
   int rc = launch_status("tl_gemm tf32");
   if (rc || !partial) return rc;
   const uint64_t mn = static_cast<uint64_t>(g.m) * g.n;
@@ -873,16 +945,18 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
   return TL_OK;
 }
 
-template <int BN>
+template <int BN, bool SPLIT = false>
 int launch_bn(const GemmArgs &g, const TcPlan &plan, float *partial, cudaStream_t s) {
   const bool a_mn = g.trans_a != 0, b_mn = g.trans_b == 0;
-  if (a_mn && b_mn) return launch_variant<BN, true, true>(g, plan, partial, s);
-  if (a_mn) return launch_variant<BN, true, false>(g, plan, partial, s);
-  if (b_mn) return launch_variant<BN, false, true>(g, plan, partial, s);
-  return launch_variant<BN, false, false>(g, plan, partial, s);
+  if (a_mn && b_mn) return launch_variant<BN, true, true, SPLIT>(g, plan, partial, s);
+  if (a_mn) return launch_variant<BN, true, false, SPLIT>(g, plan, partial, s);
+  if (b_mn) return launch_variant<BN, false, true, SPLIT>(g, plan, partial, s);
+  return launch_variant<BN, false, false, SPLIT>(g, plan, partial, s);
 }
 
-bool tc_supported(const GemmArgs &g) {
+}  // namespace
+
+bool tc_gemm_supported(const GemmArgs &g) {
   // TMA rules: 16-byte aligned bases, row strides and batch strides; at
   // most three walked batch dims per operand.
   if (g.k == 0 || g.lda % 4 || g.ldb % 4 || !aligned16(g.a) || !aligned16(g.b)) return false;
@@ -898,20 +972,21 @@ bool tc_supported(const GemmArgs &g) {
          g.k <= 0x7fffffffu;
 }
 
-}  // namespace
-
 size_t tc_gemm_workspace(const GemmArgs &g) {
-  return tc_supported(g) ? plan_tc(g).workspace : 0;
+  return tc_gemm_supported(g) ? plan_tc(g).workspace : 0;
 }
 
 int launch_tc_gemm(const GemmArgs &g, void *workspace, size_t workspace_bytes, cudaStream_t s) {
-  if (!tc_supported(g)) return TL_ERR_UNSUPPORTED;
+  if (!tc_gemm_supported(g)) return TL_ERR_UNSUPPORTED;
   const TcPlan plan = plan_tc(g);
   // without room for the slices the product runs unsplit (same result)
   float *partial = plan.splits > 1 && workspace && workspace_bytes >= plan.workspace &&
                            aligned16(workspace)
                        ? static_cast<float *>(workspace)
                        : nullptr;
+  if (g.split_tf32)
+    return plan.bn == 128 ? launch_bn<128, true>(g, plan, partial, s)
+                          : launch_bn<64, true>(g, plan, partial, s);
   if (plan.bn == 256) return launch_bn<256>(g, plan, partial, s);
   if (plan.bn == 192) return launch_bn<192>(g, plan, partial, s);
   if (plan.bn == 128) return launch_bn<128>(g, plan, partial, s);

@@ -13,6 +13,9 @@
 // combined in a fixed order.
 #include "tl_common.cuh"
 
+#include <atomic>
+#include <mutex>
+
 #include <cfloat>
 
 namespace tl {
@@ -542,28 +545,38 @@ int tl_argmax(const float *x, size_t count, uint32_t *out_index, void *workspace
 namespace tl {
 namespace {
 
-// 4 MiB of partials: enough for every reduction of the GPT training step
-// (the largest plan, a [12288, 1536] -> [1536] bias gradient, needs 2.4 MiB).
+// 4 MiB of partials.  The planner's largest workspace is about 3.1 MB
+// (3 x 2^18 floats: a column plan over more than 65535 column groups, whose
+// lanes are split at most three ways); the GPT step's largest, a
+// [12288, 1536] -> [1536] bias gradient, uses about 0.3 MB.
 constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
 static __device__ __align__(256) unsigned char g_reduce_scratch[kNoAllocScratchBytes];
 
 // Device address of g_reduce_scratch on the current device.  In host code
 // the array's name is only a host-side stand-in, so the address is looked
-// up once per device (with that device current) and cached.
+// up once per device (with that device current) and cached.  The cache is
+// safe for concurrent first calls from several host threads; after
+// cudaDeviceReset the cached address is stale, so the process must not
+// call this entry point again on a device it has reset.
 int noalloc_scratch(void **ptr) {
-  static void *cached[64] = {};
+  static std::atomic<void *> cached[64];
+  static std::mutex lookup;
   int dev = 0;
   int rc = check_cuda(cudaGetDevice(&dev), "tl_reduce_noalloc: cudaGetDevice");
   if (rc) return rc;
   if (dev < 0 || dev >= 64) return fail(TL_ERR_RANGE, "tl_reduce_noalloc: device id above 63");
-  if (!cached[dev]) {
-    void *p = nullptr;
-    rc = check_cuda(cudaGetSymbolAddress(&p, g_reduce_scratch),
-                    "tl_reduce_noalloc: cudaGetSymbolAddress of the scratch array");
-    if (rc) return rc;
-    cached[dev] = p;
+  void *p = cached[dev].load(std::memory_order_acquire);
+  if (!p) {
+    std::lock_guard<std::mutex> hold(lookup);
+    p = cached[dev].load(std::memory_order_relaxed);
+    if (!p) {
+      rc = check_cuda(cudaGetSymbolAddress(&p, g_reduce_scratch),
+                      "tl_reduce_noalloc: cudaGetSymbolAddress of the scratch array");
+      if (rc) return rc;
+      cached[dev].store(p, std::memory_order_release);
+    }
   }
-  *ptr = cached[dev];
+  *ptr = p;
   return TL_OK;
 }
 

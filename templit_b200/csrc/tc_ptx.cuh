@@ -315,6 +315,14 @@ __device__ __forceinline__ void tmem_load_32x32b_x16(uint32_t taddr, uint32_t (&
       : "memory");
 }
 
+// x rounded to the nearest tf32 value (ties away from zero), as an fp32
+// bit pattern whose low 13 mantissa bits are zero (cvt.rna.tf32.f32).
+__device__ __forceinline__ float round_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
 // 2^x by the ex2.approx instruction (flush-to-zero; relative error about
 // 2^-22), for softmax exponentials written as 2^((x - max) * log2(e)).
 __device__ __forceinline__ float ex2_approx(float x) {

@@ -1057,6 +1057,21 @@ uint64_t fuse_attention(std::vector<Op> &p) {
 // query, key and value projections (include/nn/multi_head.h) done by the
 // product's store, which writes Y's [B, H, T, D] layout directly
 // (tl_gemm_desc.c_heads), so C is never written and the transpose never runs.
+// Moving a write of `dst` from op j up to op i is safe only if no block
+// released between them overlaps dst's addresses: the pool hands released
+// blocks out again, so dst (allocated after such a release) may sit where a
+// block that ops between i and j still read used to be.
+bool no_reuse_between(const std::vector<Op> &p, size_t i, size_t j, const TRef &dst) {
+  const uintptr_t d0 = reinterpret_cast<uintptr_t>(dst.p), d1 = d0 + dst.numel() * 4;
+  for (size_t k = i + 1; k < j; ++k) {
+    const Op &op = p[k];
+    if (op.kind != Kind::Release) continue;
+    const uintptr_t r0 = reinterpret_cast<uintptr_t>(op.t[0].p), r1 = r0 + op.n;
+    if (r0 < d1 && d0 < r1) return false;
+  }
+  return true;
+}
+
 uint64_t fuse_head_split_store(std::vector<Op> &p) {
   uint64_t folded = 0;
   for (size_t i = 0; i < p.size(); ++i) {
@@ -1083,8 +1098,16 @@ uint64_t fuse_head_split_store(std::vector<Op> &p) {
     for (int k : {0, 1, 3})
       if (g.t[k].p && g.t[k].id == dst.id) operand = true;
     if (operand || !unchanged_between(p, i, j, g.t[2].id) ||
-        !untouched_between(p, i, j, dst.id) || !dead_after(p, j, g.t[2].id))
+        !untouched_between(p, i, j, dst.id) || !dead_after(p, j, g.t[2].id) ||
+        !no_reuse_between(p, i, j, dst))
       continue;
+    // only the tensor-core kernel stores the head layout: fold only products
+    // that take it (tl_gemm refuses a head-split store anywhere else)
+    tl_gemm_desc folded_desc = g.gemm;
+    folded_desc.c = dst.f();
+    folded_desc.c_heads = H;
+    folded_desc.c_head_rows = T;
+    if (tl_gemm_on_tensor_cores(&folded_desc) != 1) continue;
     g.gemm.c = dst.f();
     g.gemm.c_heads = H;
     g.gemm.c_head_rows = T;

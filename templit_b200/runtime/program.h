@@ -63,7 +63,7 @@ enum class Kind : uint8_t {
   HostWrite,   // t0 dst (rank 1 byte view), u64 offset, host payload
   Fill,        // t0 dst, u0 pattern, n elements
   DevCopy,     // t0 dst, t1 src, n bytes
-  Release,     // t0: allocation id released here (no launch)
+  Release,     // t0: allocation id (and address) released here, n bytes (no launch)
   // produced by the optimiser
   GeluBwd,     // t0 x, t1 grad, t2 out
   SoftmaxBwd,  // t0 grad, t1 y, t2 out (+ t3 divisor [1])

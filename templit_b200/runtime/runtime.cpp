@@ -355,6 +355,7 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
     Op &op = push(Kind::Release);
     op.t[0].id = b.id;
     op.t[0].p = b.ptr;
+    op.n = b.bytes;  // the address range the pool may hand out again
   }
 
   Op &push(Kind k) {
@@ -922,7 +923,7 @@ void Runtime::set_fusion(bool enabled) { impl_->fusion = enabled; }
 void Runtime::set_deferred_wait(bool enabled) { impl_->deferred_wait = enabled; }
 void Runtime::set_graphs(bool enabled) { impl_->graphs = enabled; }
 void Runtime::set_gemm_precision(int precision) {
-  if (precision != TL_GEMM_TF32 && precision != TL_GEMM_FP32)
+  if (precision != TL_GEMM_TF32 && precision != TL_GEMM_FP32 && precision != TL_GEMM_3XTF32)
     throw std::invalid_argument("unsupported GEMM precision");
   impl_->gemm_precision = precision;
 }

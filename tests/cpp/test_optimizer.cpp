@@ -44,6 +44,7 @@ Op op(Kind k) {
 Op release(const TRef &t) {
   Op o = op(Kind::Release);
   o.t[0] = t;
+  o.n = t.numel() * 4;  // the block's bytes, as the runtime records them
   return o;
 }
 Op binary(int code, const TRef &a, const TRef &b, const TRef &c) {
@@ -474,6 +475,59 @@ void head_split_store() {
   require(live(q).size() == 3 && !live(q)[0]->gemm.c_heads, "plain store kept");
 }
 
+// a product too small for the tensor cores (d 64, 2 heads, T 32, batch 1:
+// 131k multiply-adds) runs on the CUDA-core kernel, which has no head-split
+// store: the transpose stays
+void head_split_store_small_product_kept() {
+  auto x = tensor({1, 32, 64}), w = tensor({64, 64}), c = tensor({1, 32, 64});
+  auto y = tensor({1, 2, 32, 32});
+  TRef cv = c;
+  cv.rank = 4;
+  cv.shape[0] = 1;
+  cv.shape[1] = 32;
+  cv.shape[2] = 2;
+  cv.shape[3] = 32;
+  Op split = transpose(cv, y);
+  split.i0 = 1;
+  split.i1 = 2;
+  std::vector<Op> p = {gemm(x, w, c, 32, 64, 64), split, release(c)};
+  require(optimize(p, nullptr) == 0, "small product: no head-split store");
+  auto l = live(p);
+  require(l.size() == 2 && !l[0]->gemm.c_heads && l[1]->kind == Kind::Transpose,
+          "product and transpose kept");
+}
+
+// the split's output reuses the address of a temporary that is read and
+// released between the projection and the split (the pool's last-in
+// first-out reuse): storing the head layout at the projection would
+// overwrite the temporary before its reader runs, so the transpose stays
+void head_split_store_reused_address_kept() {
+  auto x = tensor({4, 192, 384}), w = tensor({384, 384}), c = tensor({4, 192, 384});
+  auto z = tensor({4, 192, 384}), s = tensor({4, 192, 384});
+  TRef y = z;  // same block address, new allocation
+  y.id = g_id++;
+  y.rank = 4;
+  y.shape[0] = 4;
+  y.shape[1] = 6;
+  y.shape[2] = 192;
+  y.shape[3] = 64;
+  TRef cv = c;
+  cv.rank = 4;
+  cv.shape[0] = 4;
+  cv.shape[1] = 192;
+  cv.shape[2] = 6;
+  cv.shape[3] = 64;
+  Op split = transpose(cv, y);
+  split.i0 = 1;
+  split.i1 = 2;
+  std::vector<Op> p = {gemm(x, w, c, 768, 384, 384), binary(TL_ADD, z, x, s), release(z), split,
+                       release(c), reduce(s, tensor({1, 384}))};
+  optimize(p, nullptr);
+  bool kept = false;
+  for (const Op *o : live(p)) kept = kept || o->kind == Kind::Transpose;
+  require(kept, "released address reused by the split's output: transpose kept");
+}
+
 // attention head split / merge: the GEMMs address the [B, T, H, D] tensors
 // through strides and both transposes go
 void head_transposes_become_strides() {
@@ -649,6 +703,8 @@ int main() {
       {"weight_gradient_observable_product_kept", weight_gradient_observable_product_kept},
       {"transpose_into_b", transpose_into_b},
       {"head_split_store", head_split_store},
+      {"head_split_store_small_product_kept", head_split_store_small_product_kept},
+      {"head_split_store_reused_address_kept", head_split_store_reused_address_kept},
       {"transpose_kept_when_read_later", transpose_kept_when_read_later},
       {"softmax_backward", softmax_backward},
       {"rmsnorm_backward", rmsnorm_backward},

@@ -1,4 +1,4 @@
-"""Checkpoint I/O of device tensors (the SURVEY's next row 4): the
+"""Checkpoint I/O of device tensors: the
 parameters and the AdamW state of the GPT step saved from the CUDA runtime
 in the reference's archive format (src/model_utils/archive.cpp:33-73, via
 Compiled::save / save_optimisers) and restored.

@@ -7,7 +7,8 @@ epilogues (bias, accumulate, GELU).
 Tolerance (<= 1e-3 relative for TF32 paths):
   TF32: ||C - C_ref||_F / ||C_ref||_F <= 1e-3 and
         max|C - C_ref| <= 4e-3 * max|C_ref|
-  FP32: |C - C_ref| <= 1e-5 * (|A| |B|) elementwise bound."""
+  FP32 and 3xTF32 (split tf32 operands on the tensor cores):
+        |C - C_ref| <= 1e-5 * (|A| |B|) elementwise bound."""
 import ctypes
 import itertools
 
@@ -91,6 +92,70 @@ def test_fp32_path(dev, m, n, k, form):
     a, b = operands(r, m, n, k, ta, tb)
     got = dev.gemm(a, b, trans_a=ta, trans_b=tb, precision=capi.TL_GEMM_FP32)
     check_fp32(got, ops.gemm(a, b, ta, tb), a, b, ta, tb)
+
+
+@pytest.mark.parametrize("form", ["NN", "NT", "TN"])
+@pytest.mark.parametrize("m,n,k", [(192, 192, 192), (384, 1536, 384), (1536, 384, 1536),
+                                   (130, 258, 36), (200, 100, 600)])
+def test_3xtf32_path(dev, m, n, k, form):
+    """Big / small tf32 halves of both operands (three tensor-core products
+    per k-step) reach the exact-fp32 bound, ragged tiles included."""
+    r = np.random.default_rng(m + 5 * n + 7 * k)
+    ta, tb = form[0] == "T", form[1] == "T"
+    a, b = operands(r, m, n, k, ta, tb)
+    d = capi.TlGemmDesc(m=m, n=n, k=k, trans_a=int(ta), trans_b=int(tb),
+                        precision=capi.TL_GEMM_3XTF32)
+    assert dev.lib.tl_gemm_on_tensor_cores(ctypes.byref(d)) == (m * n * k >= 1 << 20)
+    got = dev.gemm(a, b, trans_a=ta, trans_b=tb, precision=capi.TL_GEMM_3XTF32)
+    check_fp32(got, ops.gemm(a, b, ta, tb), a, b, ta, tb)
+
+
+@pytest.mark.parametrize("m,n,k,form", [(12288, 384, 384, "NN"), (384, 384, 12288, "TN"),
+                                        (12288, 2048, 384, "NT")])
+def test_3xtf32_large_sampled(dev, m, n, k, form):
+    """Configuration-4 shapes, split-K weight gradient included, on 4096
+    sampled outputs in float64 against the exact-fp32 bound."""
+    r = np.random.default_rng(m + n + k + 1)
+    ta, tb = form[0] == "T", form[1] == "T"
+    a, b = operands(r, m, n, k, ta, tb)
+    bias = r.standard_normal(n).astype(np.float32)
+    got = dev.gemm(a, b, trans_a=ta, trans_b=tb, bias=bias, precision=capi.TL_GEMM_3XTF32)
+    A = (a.T if ta else a).astype(np.float64)
+    B = (b.T if tb else b).astype(np.float64)
+    rows = r.integers(0, m, 4096)
+    cols = r.integers(0, n, 4096)
+    want = np.einsum("ij,ji->i", A[rows], B[:, cols]) + bias[cols]
+    bound = 1e-5 * (np.einsum("ij,ji->i", np.abs(A[rows]), np.abs(B[:, cols])) + np.abs(bias[cols]))
+    assert np.all(np.abs(got[rows, cols] - want) <= bound)
+
+
+def test_gemm_counters(dev):
+    """Launch counts by path: a product below the tensor-core threshold runs
+    on the CUDA cores, one that asks for tensor cores but has a 4-byte-aligned
+    operand is refused by that path and counted."""
+    def counts():
+        c = [ctypes.c_uint64() for _ in range(3)]
+        dev.lib.tl_gemm_counters(*[ctypes.byref(x) for x in c])
+        return [x.value for x in c]
+    r = np.random.default_rng(1)
+    a = r.standard_normal((256, 384)).astype(np.float32)
+    b = r.standard_normal((384, 256)).astype(np.float32)
+    t0 = counts()
+    dev.gemm(a, b)
+    t1 = counts()
+    assert t1[0] == t0[0] + 1 and t1[1] == t0[1]
+    dev.gemm(a[:8, :8], b[:8, :8])
+    t2 = counts()
+    assert t2[1] == t1[1] + 1 and t2[2] == t1[2]
+    ta, tb = dev.t(np.concatenate([[0.0], a.ravel()]).astype(np.float32)), dev.t(b)
+    tc = dev.empty((256, 256))
+    d = capi.TlGemmDesc(a=ta.data_ptr() + 4, b=tb.data_ptr(), c=tc.data_ptr(), m=256, n=256,
+                        k=384)
+    assert dev.lib.tl_gemm_on_tensor_cores(ctypes.byref(d)) == 0
+    dev.call("tl_gemm", ctypes.byref(d), dev.stream)
+    t3 = counts()
+    assert t3[1] == t2[1] + 1 and t3[2] == t2[2] + 1
+    np.testing.assert_allclose(dev.host(tc), ops.gemm(a, b), rtol=1e-4, atol=1e-3)
 
 
 @pytest.mark.parametrize("m,n,k", [(130, 258, 36), (200, 100, 60), (129, 65, 33), (192, 256, 1000)])
@@ -202,7 +267,8 @@ def _strided_gemm(dev, a, b, c_shape, m, n, k, trans_a, trans_b, batch, sa, sb, 
     return dev.host(tc)
 
 
-@pytest.mark.parametrize("precision", [capi.TL_GEMM_TF32, capi.TL_GEMM_FP32])
+@pytest.mark.parametrize("precision", [capi.TL_GEMM_TF32, capi.TL_GEMM_FP32,
+                                       capi.TL_GEMM_3XTF32])
 def test_head_strided_operands(dev, precision):
     """Attention heads read and written in place in [B, T, H, D] tensors:
     batch dims (B, H) with strides (T*H*D, D), row stride H*D."""
@@ -262,7 +328,8 @@ def _grouped(dev, mode, a_list, b_list, m, n, k, trans_a, trans_b, bias_list=Non
     return [dev.host(o) for o in outs]
 
 
-@pytest.mark.parametrize("precision", [capi.TL_GEMM_TF32, capi.TL_GEMM_FP32])
+@pytest.mark.parametrize("precision", [capi.TL_GEMM_TF32, capi.TL_GEMM_FP32,
+                                       capi.TL_GEMM_3XTF32])
 def test_grouped_products(dev, precision):
     """One launch for the Q, K and V projections of one input (N groups),
     for their weight gradients (N groups, split K), and for the input
@@ -297,6 +364,7 @@ def test_grouped_products(dev, precision):
     (384, 384, 12288, "TN", capi.TL_GEMM_TF32),    # split-K: the slice-sum kernel's epilogue
     (100, 70, 40, "NN", capi.TL_GEMM_TF32),        # ragged: per-thread stores
     (257, 96, 64, "NT", capi.TL_GEMM_FP32),        # CUDA-core path
+    (12288, 1536, 384, "NT", capi.TL_GEMM_3XTF32),
 ])
 def test_gelu_backward_epilogue(dev, m, n, k, form, precision):
     """C = GELU'(x) * (A B): bit-identical to the product followed by the GELU
@@ -312,8 +380,9 @@ def test_gelu_backward_epilogue(dev, m, n, k, form, precision):
     np.testing.assert_array_equal(got, want)
 
 
+@pytest.mark.parametrize("precision", [capi.TL_GEMM_TF32, capi.TL_GEMM_3XTF32])
 @pytest.mark.parametrize("groups", [1, 3])
-def test_head_split_store(dev, groups):
+def test_head_split_store(dev, groups, precision):
     """C stored as [B, H, T, D] (tl_gemm_desc.c_heads): the query / key /
     value projections of nn::MultiHeadAttention with split_heads folded into
     the store.  Bit-identical to the [M, N] product transposed afterwards."""
@@ -323,12 +392,12 @@ def test_head_split_store(dev, groups):
     x = r.standard_normal((M, K)).astype(np.float32)
     ws = [r.standard_normal((K, N)).astype(np.float32) / 8 for _ in range(groups)]
     bs = [r.standard_normal(N).astype(np.float32) for _ in range(groups)]
-    plain = [dev.gemm(x, w, bias=b) for w, b in zip(ws, bs)]
+    plain = [dev.gemm(x, w, bias=b, precision=precision) for w, b in zip(ws, bs)]
     tx = dev.t(x)
     tw, tb = [dev.t(w) for w in ws], [dev.t(b) for b in bs]
     outs = [dev.empty((B, H, T, D)) for _ in range(groups)]
     d = capi.TlGemmDesc(a=tx.data_ptr(), b=tw[0].data_ptr(), c=outs[0].data_ptr(),
-                        bias=tb[0].data_ptr(), m=M, n=N, k=K, precision=capi.TL_GEMM_TF32)
+                        bias=tb[0].data_ptr(), m=M, n=N, k=K, precision=precision)
     d.c_heads, d.c_head_rows = H, T
     if groups > 1:
         d.group_mode, d.groups = capi.TL_GEMM_GROUP_N, groups

@@ -1,16 +1,26 @@
 """The GPT training step (the reference's nn::GPT + passes::Compiled on
 cuda::Runtime, include/templit_gpt.h) against the host oracle of the same
-step (oracle/cpu_gpt: the reference executor on a CPU restatement of the
-runtime ops), plus determinism and the program-replay machinery.
+step (oracle/cpu_gpt: the reference executor on a double-accumulating CPU
+restatement of the runtime ops), plus determinism and the program-replay
+machinery.
 
-Tolerances:
-  * FP32 GEMMs: per-token forward losses within 1e-5 relative; after three
-    AdamW steps the parameter updates agree to 1% in norm (AdamW divides by
-    sqrt(v), so single elements with gradients at rounding level may flip).
-  * TF32 GEMMs (the benchmark path): the 100-step loss curve within 2e-2
-    relative of the oracle's at every step (north star: loss curves within
-    the TF32 tolerance)."""
+Tolerances (relative, stated per test below):
+  * Configuration 4 itself (batch 64, T 192): per-token forward losses,
+    the two clipped AdamW steps' mean losses and the per-token losses after
+    them within 1e-5 for FP32 and 3xTF32 products and 1e-3 for TF32.  After
+    the two steps every parameter tensor agrees within 1e-5 relative per
+    element (FP32, 3xTF32), except at most 1 element in 10^5 of the model:
+    AdamW's first steps move every element by about lr * sign(gradient),
+    so an element whose gradient is zero to within rounding may step the
+    other way.
+  * The 100-step loss curve at batch 4, T 192 (the oracle's curve is a
+    committed fixture, tests/golden/make_gpt_curve_fixture.py): within
+    1e-3 of the oracle at every step for FP32 and 3xTF32 products; plain
+    TF32 products (10-bit significands) drift further as the model fits
+    the repeated batches, and that drift is bounded at 5e-2."""
 import ctypes
+import hashlib
+import os
 
 import numpy as np
 import pytest
@@ -124,34 +134,118 @@ def test_forward_and_three_steps_match_host_oracle_fp32():
     cpu.close()
 
 
+CURVE_FIXTURE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden",
+                             "gpt_curve_b4_t192.npz")
+
+
 @pytest.mark.parametrize("precision,rtol", [
-    # exact fp32 products: the runtime's rewrites (common subexpressions,
-    # window liveness, fused kernels) must keep the whole 100-step
-    # trajectory on the oracle's
-    (capi.TL_GEMM_FP32, 2e-3),
-    # TF32 products (10-bit mantissas) drift further as the model fits the
-    # repeated batches: the curve must still track within 5%
-    (capi.TL_GEMM_TF32, 5e-2)])
+    (capi.TL_GEMM_FP32, 1e-3),    # exact fp32 products (CUDA cores)
+    (capi.TL_GEMM_3XTF32, 1e-3),  # split tf32 operands on the tensor cores
+    (capi.TL_GEMM_TF32, 5e-2)])   # plain TF32: the benchmark path's drift
 def test_loss_curve_100_steps_tracks_oracle(precision, rtol):
-    cg = oracle()
-    rng = np.random.default_rng(9)
-    B, T = 2, 32
-    batches = [zipf(rng, B, T) for _ in range(10)]
-    gpu = CudaGPT(config(B, T, precision=precision))
-    cpu = cg.OracleGPT(config(B, T, precision=capi.TL_GEMM_FP32))
-    cpu.set_params(gpu.params())
-    lg, lc = [], []
-    for s in range(100):
-        x, y = batches[s % len(batches)]
-        gpu.set_batch(x, y)
-        cpu.set_batch(x, y)
-        lg.append(gpu.train_step())
-        lc.append(cpu.train_step())
-    lg, lc = np.array(lg), np.array(lc)
-    assert lc[-1] < lc[0] - 1.0  # the model learns on repeated batches
-    np.testing.assert_allclose(lg, lc, rtol=rtol)
+    fx = np.load(CURVE_FIXTURE)
+    B, T = int(fx["batch"]), int(fx["seq"])
+    gpu = CudaGPT(config(B, T, precision=precision, seed=int(fx["seed"])))
+    # both sides draw the initial weights from the same seed
+    assert hashlib.sha256(gpu.params().tobytes()).digest() == fx["params0_sha256"].tobytes()
+    want = fx["losses"].astype(np.float64)
+    got = []
+    for s in range(want.size):
+        i = s % fx["x"].shape[0]
+        gpu.set_batch(fx["x"][i], fx["y"][i])
+        got.append(gpu.train_step())
     gpu.close()
+    got = np.array(got, np.float64)
+    dev = np.abs(got - want) / np.abs(want)
+    print(f"precision {precision}: max relative deviation {dev.max():.3e} "
+          f"(step {int(dev.argmax())}), final loss {got[-1]:.5f} vs {want[-1]:.5f}")
+    assert want[-1] < want[0] - 1.0  # the model learns on repeated batches
+    assert dev.max() <= rtol
+
+
+@pytest.fixture(scope="module")
+def config4_oracle():
+    """The oracle at configuration 4: per-token losses, two clipped AdamW
+    steps, per-token losses again, and the parameters after the steps."""
+    cg = oracle()
+    rng = np.random.default_rng(21)
+    x, y = zipf(rng, 64, 192)
+    cpu = cg.OracleGPT(config(64, 192, precision=capi.TL_GEMM_FP32))
+    out = {"x": x, "y": y, "p0": cpu.params()}
+    cpu.set_batch(x, y)
+    out["f0"] = cpu.forward()
+    out["steps"] = np.array([cpu.train_step() for _ in range(2)], np.float64)
+    out["f2"] = cpu.forward()
+    out["p2"] = cpu.params()
     cpu.close()
+    return out
+
+
+def param_sizes(g, tmp_path):
+    """Element counts of the parameter tensors, in tlg_get_params order, from
+    a checkpoint (the reference archive layout: u32 name length, name, u32
+    blob length, blob; entries parameters/<i>/size hold the shapes)."""
+    path = tmp_path / "sizes.bin"
+    g.save(path, optimiser=False)
+    raw = path.read_bytes()
+    shapes, off = {}, 0
+    while off < len(raw):
+        n = int.from_bytes(raw[off:off + 4], "little")
+        name = raw[off + 4:off + 4 + n].decode()
+        off += 4 + n
+        m = int.from_bytes(raw[off:off + 4], "little")
+        blob = raw[off + 4:off + 4 + m]
+        off += 4 + m
+        parts = name.split("/")
+        if parts[0] == "parameters" and parts[2] == "size":
+            shapes[int(parts[1])] = np.frombuffer(blob, np.uint32)
+    return [int(np.prod(shapes[i])) for i in range(len(shapes))]
+
+
+@pytest.mark.parametrize("precision,rtol", [
+    (capi.TL_GEMM_FP32, 1e-5),
+    (capi.TL_GEMM_3XTF32, 1e-5),
+    (capi.TL_GEMM_TF32, 1e-3)])
+def test_config4_step_matches_oracle(config4_oracle, precision, rtol, tmp_path):
+    o = config4_oracle
+    gpu = CudaGPT(config(64, 192, precision=precision))
+    p0 = gpu.params()
+    assert np.array_equal(p0, o["p0"])  # same seed, same initial weights
+    gpu.set_batch(o["x"], o["y"])
+    f0 = gpu.forward()
+    steps = np.array([gpu.train_step() for _ in range(2)], np.float64)
+    f2 = gpu.forward()
+    p2 = gpu.params()
+    sizes = param_sizes(gpu, tmp_path)
+    gpu.close()
+    assert sum(sizes) == p2.size == 8_740_352
+
+    def rel(a, b):
+        return float(np.max(np.abs(a.astype(np.float64) - b) / np.abs(b.astype(np.float64))))
+    r0, rs, r2 = rel(f0, o["f0"]), rel(steps, o["steps"]), rel(f2, o["f2"])
+    print(f"precision {precision}: per-token losses {r0:.2e}, step losses {rs:.2e}, "
+          f"after two steps {r2:.2e}")
+    assert r0 <= rtol and rs <= rtol and r2 <= rtol
+    d_g, d_c = p2.astype(np.float64) - p0, o["p2"].astype(np.float64) - p0
+    if precision == capi.TL_GEMM_TF32:
+        # TF32 gradients differ from the exact ones at 1e-3: AdamW's
+        # sign-like first steps then flip more elements; bound the update
+        # difference in norm instead
+        upd = np.linalg.norm(d_g - d_c) / np.linalg.norm(d_c)
+        print(f"TF32 update difference {upd:.3e}")
+        assert upd <= 0.1
+        return
+    flipped, worst, off = 0, 0.0, 0
+    for n in sizes:
+        g, c = p2[off:off + n].astype(np.float64), o["p2"][off:off + n].astype(np.float64)
+        off += n
+        bad = np.abs(g - c) > rtol * np.abs(c)
+        flipped += int(bad.sum())
+        ok = ~bad
+        if ok.any():
+            worst = max(worst, float(np.max(np.abs(g[ok] - c[ok]) / np.abs(c[ok]).clip(1e-30))))
+    print(f"elements outside {rtol:g}: {flipped} of {p2.size}; worst other {worst:.2e}")
+    assert flipped <= p2.size // 100_000
 
 
 def test_deterministic_and_graph_replay_is_bit_exact():

@@ -1,4 +1,4 @@
-"""Forward-only inference (the SURVEY's next row 2): the reference's own
+"""Forward-only inference: the reference's own
 src/generate.cpp set-up and inference::autoregression (include/
 inference.h:45-97) on the CUDA runtime, against the same code on the host
 oracle runtime, with the same parameters.

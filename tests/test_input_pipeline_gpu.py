@@ -1,4 +1,4 @@
-"""Training input pipeline (the SURVEY's next row 3): tlg_loader_* draws the
+"""Training input pipeline: tlg_loader_* draws the
 same batches as the reference's own Dataset::load_tokens + Loader::get_batch
 (src/model_utils/dataset.cpp, loader.cpp, compiled into the host oracle)
 from the same token file and seed - bit-exact - into pinned memory, and a
