@@ -105,7 +105,9 @@ def test_3xtf32_path(dev, m, n, k, form):
     a, b = operands(r, m, n, k, ta, tb)
     d = capi.TlGemmDesc(m=m, n=n, k=k, trans_a=int(ta), trans_b=int(tb),
                         precision=capi.TL_GEMM_3XTF32)
-    assert dev.lib.tl_gemm_on_tensor_cores(ctypes.byref(d)) == (m * n * k >= 1 << 20)
+    lda, ldb = (m if ta else k), (k if tb else n)  # TMA wants 16-byte row strides
+    tc = m * n * k >= 1 << 20 and lda % 4 == 0 and ldb % 4 == 0
+    assert dev.lib.tl_gemm_on_tensor_cores(ctypes.byref(d)) == int(tc)
     got = dev.gemm(a, b, trans_a=ta, trans_b=tb, precision=capi.TL_GEMM_3XTF32)
     check_fp32(got, ops.gemm(a, b, ta, tb), a, b, ta, tb)
 
