@@ -457,6 +457,41 @@ int tl_attention_fused_supported(const tl_attn_desc *d);
 /* TL_ERR_UNSUPPORTED when they do not. */
 int tl_attention_fused(const tl_attn_desc *d, void *stream);
 
+/* Flash attention for any T and 64-wide heads: the same attention as
+ * tl_attention_fused (the executor's composite of include/nn/multi_head.h:
+ * 45-52 and its backward through SFTMX_DERIVATIVE, include/passes/
+ * execute.h:187-232,291-308) without a [T, T] tensor in HBM.  The forward
+ * leaves O and the row log-sum-exp lse[b, h, t] = ln sum_k e^{S[t, k]} of
+ * the scores S = Q K^T / divisor + mask; the backward recomputes P = e^(S -
+ * lse) on the tensor cores and uses delta[b, h, t] = sum_d dO * O (scratch)
+ * for the softmax derivative's row sum.  Views as in tl_attn_desc (only k
+ * may be stored transposed).  mask is optional ([T, T], added after the
+ * divide); mask_flag (optional device word, tl_attention_mask_check) marks
+ * it as the causal mask, which the kernels then apply by position and whose
+ * zero blocks they skip.  TF32 products, fp32 softmax; deterministic. */
+typedef struct tl_flash_desc {
+  uint32_t B, T, H, D; /* D must be 64 */
+  tl_attn_view q, k, v, o, d_o, dq, dk, dv;
+  const float *divisor;       /* device scalar (sqrt(D) in the reference)  */
+  const float *mask;          /* optional [T, T]                            */
+  const uint32_t *mask_flag;  /* optional: nonzero = mask is causal         */
+  float *lse;                 /* [B, H, T]                                  */
+  float *delta;               /* [B, H, T] backward scratch                 */
+} tl_flash_desc;
+/* 1 when the flash kernels take this descriptor (16-byte aligned operands
+ * and strides, D == 64), else 0. */
+int tl_flash_attention_supported(const tl_flash_desc *d);
+/* q, k, v, divisor, mask -> o, lse */
+int tl_flash_attention_fwd(const tl_flash_desc *d, void *stream);
+/* q, k, v, o, d_o, lse, divisor, mask -> dq, dk, dv (delta scratch) */
+int tl_flash_attention_bwd(const tl_flash_desc *d, void *stream);
+/* P = softmax of the scores ([B, H, T, T] dense) from q, k and lse: the
+ * forward's probabilities for a reader other than the flash backward. */
+int tl_flash_attention_probs(const tl_flash_desc *d, float *p, void *stream);
+/* *flag (device word) = 1 when mask ([T, T]) is nn::causal_mask's (-inf
+ * above the diagonal, 0 elsewhere; include/nn/attention.h:10-22), else 0. */
+int tl_attention_mask_check(const float *mask, uint32_t T, uint32_t *flag, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -72,6 +72,14 @@ class TlAttnDesc(Structure):
                 ("workspace", c_void_p), ("workspace_bytes", c_uint64)]
 
 
+class TlFlashDesc(Structure):
+    _fields_ = [("B", c_uint32), ("T", c_uint32), ("H", c_uint32), ("D", c_uint32),
+                ("q", TlAttnView), ("k", TlAttnView), ("v", TlAttnView), ("o", TlAttnView),
+                ("d_o", TlAttnView), ("dq", TlAttnView), ("dk", TlAttnView), ("dv", TlAttnView),
+                ("divisor", c_void_p), ("mask", c_void_p), ("mask_flag", c_void_p),
+                ("lse", c_void_p), ("delta", c_void_p)]
+
+
 class TlgConfig(Structure):
     _fields_ = [("family", c_uint32), ("batch", c_uint32), ("seq", c_uint32),
                 ("seed", c_uint32), ("init_std", c_float), ("lr", c_float),
@@ -115,6 +123,11 @@ CUDA_ABI = {
     "tl_attention_workspace_size": (c_size_t, [c_uint32, c_uint32, c_uint32, c_uint32]),
     "tl_attention_fused_supported": (c_int, [c_void_p]),
     "tl_attention_fused": (c_int, [c_void_p, c_void_p]),
+    "tl_flash_attention_supported": (c_int, [POINTER(TlFlashDesc)]),
+    "tl_flash_attention_fwd": (c_int, [POINTER(TlFlashDesc), c_void_p]),
+    "tl_flash_attention_bwd": (c_int, [POINTER(TlFlashDesc), c_void_p]),
+    "tl_flash_attention_probs": (c_int, [POINTER(TlFlashDesc), c_void_p, c_void_p]),
+    "tl_attention_mask_check": (c_int, [c_void_p, c_uint32, c_void_p, c_void_p]),
     "tl_graph_capture_begin": (c_int, [c_void_p]),
     "tl_graph_capture_end": (c_int, [c_void_p, POINTER(c_void_p)]),
     "tl_graph_launch": (c_int, [c_void_p, c_void_p]),

@@ -44,4 +44,27 @@ int launch_attention_bwd_kv_tc(const AttnDims &d, const float *ds, const HeadVie
                                const HeadView &dk, const float *p, const HeadView &d_o,
                                const HeadView &dv, cudaStream_t s);
 
+// ---- flash attention (k_flash_attn.cu): any T, D == 64, no T x T tensor
+// True when the flash kernels take these operands (16-byte aligned pointers
+// and strides; only K may be stored transposed).
+bool flash_attention_fits(const AttnDims &d, const HeadView *views, int n);
+// O = softmax(Q K^T / divisor + mask) V and the row log-sum-exp lse
+// ([B, H, T], natural log).  mask_flag (optional device word): nonzero when
+// the mask is the causal one, applied by position without reading it.
+int launch_flash_fwd(const AttnDims &d, const HeadView &q, const HeadView &k, const HeadView &v,
+                     const float *divisor, const float *mask, const uint32_t *mask_flag,
+                     const HeadView &o, float *lse, cudaStream_t s);
+// dQ, dK, dV from Q, K, V, O, dO and lse; delta ([B, H, T]) is scratch.
+int launch_flash_bwd(const AttnDims &d, const HeadView &q, const HeadView &k, const HeadView &v,
+                     const HeadView &o, const HeadView &d_o, const float *divisor,
+                     const float *mask, const uint32_t *mask_flag, const float *lse,
+                     float *delta, const HeadView &dq, const HeadView &dk, const HeadView &dv,
+                     cudaStream_t s);
+// P = exp(Q K^T / divisor + mask - lse), dense [B, H, T, T].
+int launch_flash_probs(const AttnDims &d, const HeadView &q, const HeadView &k,
+                       const float *divisor, const float *mask, const uint32_t *mask_flag,
+                       const float *lse, float *p, cudaStream_t s);
+// *flag = 1 when mask ([T, T]) is the causal mask, else 0.
+int launch_mask_check(const float *mask, uint32_t T, uint32_t *flag, cudaStream_t s);
+
 }  // namespace tl

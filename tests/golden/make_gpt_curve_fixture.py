@@ -7,9 +7,12 @@ a double-accumulating CPU restatement of every runtime op) needs minutes for
 these 100 steps, so its curve is recorded once here and the GPU test
 (tests/test_gpt_gpu.py) compares the CUDA runtime's curve with it.  The
 fixture holds the ten Zipf(1.1) batches the curve cycles through, the
-oracle's per-step losses, and the SHA-256 of the initial parameters (both
-sides draw them from the same seed; the GPU test checks that it starts from
-exactly these).
+oracle's per-step losses, and the SHA-256 of the oracle's initial
+parameters: the GPU test re-creates them with the oracle (the same seed),
+checks the hash and loads them into the CUDA model, so both curves start
+from the same bits (the two libraries draw the seed's normal variates with
+different floating-point contraction, so their own draws differ in the last
+bits).
 
 Run:  make -C oracle/cpu_gpt && python tests/golden/make_gpt_curve_fixture.py
 """

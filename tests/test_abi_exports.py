@@ -73,7 +73,7 @@ def test_struct_layouts_match_the_headers(tmp_path):
     caller's struct)."""
     structs = {"tl_gemm_desc": capi.TlGemmDesc, "tl_param_slot": capi.TlParamSlot,
                "tlg_config": capi.TlgConfig, "tl_attn_view": capi.TlAttnView,
-               "tl_attn_desc": capi.TlAttnDesc}
+               "tl_attn_desc": capi.TlAttnDesc, "tl_flash_desc": capi.TlFlashDesc}
     lines = ['#include <stddef.h>', '#include <stdio.h>', '#include "templit_cuda.h"',
              '#include "templit_gpt.h"', "int main(void) {"]
     for cname, py in structs.items():

@@ -337,28 +337,32 @@ def test_grouped_products(dev, precision):
     for their weight gradients (N groups, split K), and for the input
     gradient summed over the three (K groups)."""
     r = np.random.default_rng(23)
-    check = check_tf32 if precision == capi.TL_GEMM_TF32 else (
-        lambda g, w: np.testing.assert_allclose(g, w, rtol=1e-4, atol=1e-3))
+
+    def check(g, w, a, b, ta=False, tb=False):
+        if precision == capi.TL_GEMM_TF32:
+            check_tf32(g, w)
+        else:  # FP32 and 3xTF32: the exact-fp32 bound
+            check_fp32(g, w, a, b, ta, tb)
     x = r.standard_normal((2048, 384)).astype(np.float32)
     ws = [r.standard_normal((384, 384)).astype(np.float32) for _ in range(3)]
     bs = [r.standard_normal((384,)).astype(np.float32) for _ in range(3)]
     outs = _grouped(dev, capi.TL_GEMM_GROUP_N, [x], ws, 2048, 384, 384, False, False, bs,
                     precision)
     for o, w, b in zip(outs, ws, bs):
-        check(o, ops.gemm(x, w, bias=b))
+        check(o - b, ops.gemm(x, w), x, w)
     # weight gradients: X^T dY_g, K = 12288 (split-K slices per group)
     xl = r.standard_normal((12288, 384)).astype(np.float32)
     dys = [r.standard_normal((12288, 384)).astype(np.float32) for _ in range(3)]
     outs = _grouped(dev, capi.TL_GEMM_GROUP_N, [xl], dys, 384, 384, 12288, True, False,
                     precision=precision)
     for o, dy in zip(outs, dys):
-        check(o, ops.gemm(xl, dy, True, False))
+        check(o, ops.gemm(xl, dy, True, False), xl, dy, True, False)
     # input gradient: sum_g dY_g W_g^T over the concatenated K
     gs = [r.standard_normal((2048, 384)).astype(np.float32) for _ in range(3)]
     (out,) = _grouped(dev, capi.TL_GEMM_GROUP_K, gs, ws, 2048, 384, 384, False, True,
                       precision=precision)
     want = sum(ops.gemm(g, w, False, True) for g, w in zip(gs, ws))
-    check(out, want)
+    check(out, want, np.concatenate(gs, axis=1), np.concatenate(ws, axis=1), False, True)
 
 
 @pytest.mark.parametrize("m,n,k,form,precision", [

