@@ -44,6 +44,9 @@ struct RuntimeStats {
   uint64_t host_record_ns = 0;  // host time from start() to submit(), in total
   uint64_t host_submit_ns = 0;  // host time inside submit() (optimise + launch), in total
   uint64_t optimiser_cache_hits = 0;  // programs whose optimised form was reused
+  uint64_t flash_forward = 0;   // flash attention forwards launched (P left virtual)
+  uint64_t flash_backward = 0;  // flash attention backwards launched (P recomputed)
+  uint64_t flash_rebuilt = 0;   // virtual P tensors written out for another reader
 };
 
 class Runtime {
@@ -115,6 +118,11 @@ public:
   // GEMM arithmetic of mult: TL_GEMM_TF32 (tcgen05 tensor cores, default)
   // or TL_GEMM_FP32 (exact fp32 products on CUDA cores).
   void set_gemm_precision(int precision);
+  // Attention composites on the flash kernels (default on; the environment
+  // variable TL_FLASH_ATTENTION=0 turns it off): the forward keeps the
+  // softmax output P as its recipe (row log-sum-exp) instead of writing it,
+  // the backward recomputes it, and any other reader gets it rebuilt first.
+  void set_flash_attention(bool enabled);
   // Data parallelism: an NCCL communicator (ncclComm_t as void*).  When set,
   // the program of a window that updates parameters (AdamW) first
   // sum-reduces every gradient it reads across the communicator's ranks, so

@@ -14,6 +14,7 @@
 #include "internal.h"
 
 #include <cstdlib>
+#include <algorithm>
 #include <cstring>
 #include <iterator>
 #include <map>
@@ -37,6 +38,7 @@ struct State {
   uint64_t next_id = 1;
   uint64_t window_counter = 0;
   internal::Recorder *recorder = nullptr;
+  std::vector<internal::HostAccessHook *> hooks;
   // blocks whose value was read outside a recorded program (host reads,
   // immediate device copies), until released
   std::unordered_set<uint64_t> observed;
@@ -83,6 +85,11 @@ void ensure_init() {
 }
 
 Recorder *active_recorder() { return state().recorder; }
+void add_host_access_hook(HostAccessHook *h) { state().hooks.push_back(h); }
+void remove_host_access_hook(HostAccessHook *h) {
+  auto &v = state().hooks;
+  v.erase(std::remove(v.begin(), v.end(), h), v.end());
+}
 void set_active_recorder(Recorder *r) { state().recorder = r; }
 uint64_t next_window_id() { return ++state().window_counter; }
 bool host_observed(uint64_t id) { return state().observed.count(id) != 0; }
@@ -169,6 +176,7 @@ Block allocate(size_t bytes) {
 void release(const Block &block) noexcept {
   if (!block.ptr) return;
   State &s = state();
+  for (internal::HostAccessHook *h : s.hooks) h->on_release(block.id);
   if (s.recorder) s.recorder->record_release(block);
   s.observed.erase(block.id);
   s.in_use -= block.bytes;
@@ -184,6 +192,10 @@ bool recorded_here(const Block &b) {
 
 void device_changed() { ++state().epoch; }
 
+void host_access(const Block &b, bool write, bool full) {
+  for (internal::HostAccessHook *h : state().hooks) h->before_host_access(b.id, write, full);
+}
+
 void write(const Block &dst, size_t offset_bytes, const void *src, size_t bytes) {
   if (bytes == 0) return;
   device_changed();
@@ -191,6 +203,7 @@ void write(const Block &dst, size_t offset_bytes, const void *src, size_t bytes)
     state().recorder->record_write(dst, offset_bytes, src, bytes);
     return;
   }
+  host_access(dst, true, offset_bytes == 0 && bytes >= dst.bytes);
   internal::check(tl_memcpy_h2d(static_cast<char *>(dst.ptr) + offset_bytes, src, bytes,
                                 state().stream),
                   "Storage::write");
@@ -199,6 +212,7 @@ void write(const Block &dst, size_t offset_bytes, const void *src, size_t bytes)
 void read(const Block &src, size_t offset_bytes, void *dst, size_t bytes) {
   if (bytes == 0) return;
   State &s = state();
+  if (!s.hooks.empty()) host_access(src, false, false);
   s.observed.insert(src.id);
   State::Mirror &m = s.mirror;
   const bool fresh = m.id == src.id && m.epoch == s.epoch && m.launches == tl_kernel_launches();
@@ -232,6 +246,7 @@ void fill32(const Block &dst, uint32_t pattern, size_t count) {
     state().recorder->record_fill(dst, pattern, count);
     return;
   }
+  host_access(dst, true, count * 4 >= dst.bytes);
   internal::check(tl_fill_u32(dst.ptr, pattern, count, state().stream), "Storage::fill");
 }
 
@@ -242,6 +257,8 @@ void copy(const Block &dst, const Block &src, size_t bytes) {
     state().recorder->record_copy(dst, src, bytes);
     return;
   }
+  host_access(src, false, false);
+  host_access(dst, true, bytes >= dst.bytes);
   state().observed.insert(src.id);
   internal::check(tl_memcpy_d2d(dst.ptr, src.ptr, bytes, state().stream), "Storage::clone");
 }

@@ -28,6 +28,18 @@ struct Recorder {
 
 Recorder *active_recorder();
 void set_active_recorder(Recorder *r);
+
+// Told about immediate (not recorded) host accesses to device blocks, before
+// they happen: a runtime whose programs leave a tensor's value implicit (a
+// flash attention P kept as its recipe) makes it real before the host reads
+// it or a write replaces part of it, and forgets it when it is released.
+struct HostAccessHook {
+  virtual ~HostAccessHook() = default;
+  virtual void before_host_access(uint64_t id, bool write, bool full) = 0;
+  virtual void on_release(uint64_t id) = 0;
+};
+void add_host_access_hook(HostAccessHook *h);
+void remove_host_access_hook(HostAccessHook *h);
 uint64_t next_window_id();
 // True when the block's value has been read outside a recorded program
 // (Storage::read / compare on the host, or an immediate clone) since it

@@ -66,6 +66,18 @@ Access access(const Op &op) {
         a.write(t[5]); a.write(t[6]);
       }
       break;
+    case Kind::FlashFwd:  // P (t5) is defined here, though not stored
+      for (int i = 0; i < 5; ++i) a.read(t[i]);
+      a.write(t[5]); a.write(t[6]); break;
+    case Kind::FlashBwd:
+      for (int i = 0; i < 7; ++i) a.read(t[i]);
+      if (op.group_refs.size() > 1) a.read(op.group_refs[1]);
+      a.write(t[7]); a.write(t[8]);
+      if (!op.group_refs.empty()) a.write(op.group_refs[0]);
+      break;
+    case Kind::FlashProbs:
+      for (int i = 0; i < 4; ++i) a.read(t[i]);
+      a.write(t[4]); break;
     default: break;  // Release, MultiAdamW, AllReduce: handled by their passes
   }
   return a;
@@ -1050,6 +1062,326 @@ uint64_t fuse_attention(std::vector<Op> &p) {
   return folded;
 }
 
+// ---------------------------------------------------------- flash attention
+// The attention composite on the flash kernels (any sequence length):
+//   forward   S = Q K^T, softmax(S / divisor + mask) -> P, O = P V  ->  one
+//             FlashFwd at O's product, writing O and P's row log-sum-exp
+//             only; P stays virtual (FlashRecord) for the backward window
+//   backward  dP = dO V^T, softmax derivative(dP, P) / divisor -> dS,
+//             dQ = dS K, dK = dS^T Q, dV = P^T dO  ->  one FlashBwd at the
+//             last of the three products, P of a virtual record
+//             recomputed from Q, K and the log-sum-exp, dP and dS never
+//             written
+// resolve_flash then rebuilds a virtual P (FlashProbs) in front of any other
+// reader, and before any write or release of its recipe's inputs.
+
+thread_local FlashState *g_flash = nullptr;
+
+bool same_view(const tl_attn_view &a, const tl_attn_view &b) {
+  return a.p == b.p && a.batch_stride == b.batch_stride && a.head_stride == b.head_stride &&
+         a.row_stride == b.row_stride && a.transposed == b.transposed;
+}
+
+const FlashRecord *flash_record(uint64_t p_id) {
+  if (!g_flash) return nullptr;
+  for (const FlashRecord &r : g_flash->records())
+    if (r.p_id == p_id) return &r;
+  return nullptr;
+}
+
+uint64_t fuse_flash_forward(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  std::unordered_set<uint64_t> checked_masks;  // one causal check per mask per program
+  for (size_t k = 0; k < p.size(); ++k) {
+    Op &sm = p[k];
+    if (sm.dead || sm.kind != Kind::Softmax || !sm.t[2].p) continue;
+    const TRef X = sm.t[0], Y = sm.t[1], div = sm.t[2], mask = sm.t[3];
+    uint32_t B, H, T;
+    if (!score_dims(Y, B, H, T) || !is_scalar_tensor(div)) continue;
+    if (mask.p && mask.numel() != static_cast<uint64_t>(T) * T) continue;
+    const size_t i = last_writer(p, k, X.id);
+    if (i == kNone || !plain_product(p[i]) || first_reader(p, i, X.id) != k ||
+        !dead_after(p, k, X.id))
+      continue;
+    const size_t j = first_reader(p, k, Y.id);
+    if (j == kNone || !plain_product(p[j]) || !same(p[j].t[0], Y) || same(p[j].t[1], Y))
+      continue;
+    const tl_gemm_desc &g1 = p[i].gemm, &g2 = p[j].gemm;
+    if (g1.m != T || g1.n != T || g1.k != kFusedHeadDimHost || g1.trans_a || g2.m != T ||
+        g2.k != T || g2.n != kFusedHeadDimHost || g2.trans_a || g2.trans_b)
+      continue;
+    tl_flash_desc d{};
+    d.B = B;
+    d.H = H;
+    d.T = T;
+    d.D = kFusedHeadDimHost;
+    tl_attn_view sv, pv;
+    if (!head_view(g1, 0, B, H, g1.k, false, d.q) ||
+        !head_view(g1, 1, B, H, g1.trans_b ? g1.k : g1.n, !g1.trans_b, d.k) ||
+        !head_view(g1, 2, B, H, T, false, sv) || !dense_scores(sv, H, T) ||
+        !head_view(g2, 0, B, H, T, false, pv) || !dense_scores(pv, H, T) ||
+        !head_view(g2, 1, B, H, g2.n, false, d.v) || !head_view(g2, 2, B, H, g2.n, false, d.o))
+      continue;
+    const TRef Q = p[i].t[0], K = p[i].t[1];
+    if (!unchanged_between(p, i, j, Q.id) || !unchanged_between(p, i, j, K.id) ||
+        !unchanged_between(p, k, j, div.id) || (mask.p && !unchanged_between(p, k, j, mask.id)) ||
+        !untouched_between(p, k, j, Y.id))
+      continue;
+    d.divisor = div.f();
+    d.mask = mask.p ? mask.f() : nullptr;
+    d.mask_flag = mask.p ? g_flash->mask_word(mask.id) : nullptr;
+    d.lse = g_flash->lse_buffer(Y.id, static_cast<size_t>(B) * H * T * 4);
+    if (tl_flash_attention_supported(&d) != 1 || !d.lse || (mask.p && !d.mask_flag)) continue;
+    Op fused{};
+    fused.kind = Kind::FlashFwd;
+    fused.code = mask.p && checked_masks.insert(mask.id).second ? 1 : 0;  // 1: check the mask
+    fused.flash = d;
+    fused.t[0] = Q;
+    fused.t[1] = K;
+    fused.t[2] = p[j].t[1];
+    fused.t[3] = div;
+    fused.t[4] = mask;
+    fused.t[5] = Y;
+    fused.t[6] = p[j].t[2];
+    fused.src = p[j].src;
+    p[i].dead = true;
+    sm.dead = true;
+    p[j] = std::move(fused);
+    folded += 2;
+  }
+  return folded;
+}
+
+// Readers of `id` after op `after`: their positions (live ops only, up to
+// the allocation's release or a full rewrite).
+std::vector<size_t> readers_after(const std::vector<Op> &p, size_t after, uint64_t id) {
+  std::vector<size_t> out;
+  for (size_t j = after + 1; j < p.size(); ++j) {
+    const Op &op = p[j];
+    if (op.dead) continue;
+    if (op.kind == Kind::Release) {
+      if (op.t[0].id == id) break;
+      continue;
+    }
+    if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce) continue;
+    const Access a = access(op);
+    if (reads(a, id)) out.push_back(j);
+    if (writes(a, id) && !reads(a, id) && full_write(op)) break;
+  }
+  return out;
+}
+
+uint64_t fuse_flash_backward(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t k = 0; k < p.size(); ++k) {
+    Op &sm = p[k];
+    if (sm.dead || sm.kind != Kind::SoftmaxBwd || !sm.t[3].p) continue;
+    const TRef dP = sm.t[0], P = sm.t[1], dS = sm.t[2], div = sm.t[3];
+    const FlashRecord *rec = flash_record(P.id);
+    uint32_t B, H, T;
+    if (!rec || !rec->o_valid || !score_dims(P, B, H, T) || !dS.same_shape(P) ||
+        B != rec->desc.B || H != rec->desc.H || T != rec->desc.T || !same(div, rec->divisor))
+      continue;
+    // dP = dO V^T, read only by the softmax derivative
+    const size_t i = last_writer(p, k, dP.id);
+    if (i == kNone || !plain_product(p[i]) || first_reader(p, i, dP.id) != k ||
+        !dead_after(p, k, dP.id))
+      continue;
+    const tl_gemm_desc &g1 = p[i].gemm;
+    if (g1.m != T || g1.n != T || g1.k != kFusedHeadDimHost || g1.trans_a || !g1.trans_b)
+      continue;
+    // dS read by exactly dQ = dS K and dK = dS^T Q, then dead; P^T dO -> dV
+    const std::vector<size_t> ds_readers = readers_after(p, k, dS.id);
+    if (ds_readers.size() != 2) continue;
+    size_t jq = kNone, jk = kNone, jv = kNone;
+    for (size_t r : ds_readers) {
+      const Op &op = p[r];
+      if (!plain_product(op) || !same(op.t[0], dS) || same(op.t[1], dS)) continue;
+      const tl_gemm_desc &g = op.gemm;
+      if (g.m != T || g.k != T || g.n != kFusedHeadDimHost) continue;
+      if (!g.trans_a) jq = r;
+      else if (!g.trans_b) jk = r;
+    }
+    if (jq == kNone || jk == kNone || !dead_after(p, std::max(jq, jk), dS.id)) continue;
+    for (size_t r : readers_after(p, k, P.id)) {
+      const Op &op = p[r];
+      if (plain_product(op) && same(op.t[0], P) && op.gemm.trans_a && !op.gemm.trans_b &&
+          op.gemm.m == T && op.gemm.k == T && op.gemm.n == kFusedHeadDimHost &&
+          same(op.t[1], p[i].t[0])) {
+        jv = r;
+        break;
+      }
+    }
+    if (jv == kNone) continue;
+    const tl_gemm_desc &gq = p[jq].gemm, &gk = p[jk].gemm, &gv = p[jv].gemm;
+    tl_flash_desc d = rec->desc;
+    tl_attn_view kq, qk, dov, vv, dov2;
+    if (!head_view(g1, 0, B, H, g1.k, false, dov) || !head_view(g1, 1, B, H, g1.k, true, vv) ||
+        !head_view(gq, 1, B, H, gq.trans_b ? gq.k : gq.n, gq.trans_b, kq) ||
+        !head_view(gq, 2, B, H, gq.n, false, d.dq) ||
+        !head_view(gk, 1, B, H, gk.n, false, qk) || !head_view(gk, 2, B, H, gk.n, false, d.dk) ||
+        !head_view(gv, 1, B, H, gv.n, false, dov2) || !head_view(gv, 2, B, H, gv.n, false, d.dv))
+      continue;
+    // the backward's operands are the recipe's tensors, read the same way
+    vv.transposed = 0;
+    if (!same(p[jq].t[1], rec->k) || !same_view(kq, rec->desc.k) || !same(p[jk].t[1], rec->q) ||
+        !same_view(qk, rec->desc.q) || !same(p[i].t[1], rec->v) || !same_view(vv, rec->desc.v) ||
+        !same_view(dov, dov2))
+      continue;
+    d.d_o = dov;
+    const size_t J = std::max({jq, jk, jv});
+    const size_t first = std::min({i, jq, jk, jv});
+    const TRef dO = p[i].t[0], dQ = p[jq].t[2], dK = p[jk].t[2], dV = p[jv].t[2];
+    bool ok = true;
+    for (const TRef *in : {&rec->q, &rec->k, &rec->v, &rec->divisor, &dO, &P})
+      ok = ok && unchanged_between(p, first, J, in->id);
+    ok = ok && (!rec->mask.p || unchanged_between(p, first, J, rec->mask.id));
+    // O: not written in this program before the backward (from op 0 on)
+    ok = ok && unchanged_between(p, kNone, J, rec->o.id);
+    for (size_t r : {jq, jk, jv}) {
+      const TRef &out = p[r].t[2];
+      ok = ok && untouched_between(p, r, J, out.id);
+      for (const TRef *in : {&rec->q, &rec->k, &rec->v, &rec->o, &dO, &P})
+        ok = ok && out.id != in->id;
+    }
+    ok = ok && dQ.id != dK.id && dQ.id != dV.id && dK.id != dV.id;
+    if (!ok) continue;
+    Op fused{};
+    fused.kind = Kind::FlashBwd;
+    fused.flash = d;
+    fused.t[0] = rec->q;
+    fused.t[1] = rec->k;
+    fused.t[2] = rec->v;
+    fused.t[3] = rec->o;
+    fused.t[4] = dO;
+    fused.t[5] = rec->divisor;
+    fused.t[6] = P;
+    fused.t[7] = dK;
+    fused.t[8] = dV;
+    fused.group_refs = {dQ, rec->mask};
+    fused.workspace = static_cast<size_t>(B) * H * T * 4;  // delta = rowsum(dO * O)
+    fused.src = p[J].src;
+    for (size_t r : {i, k, jq, jk, jv})
+      if (r != J) p[r].dead = true;
+    p[J] = std::move(fused);
+    folded += 4;
+  }
+  return folded;
+}
+
+// One op's effect on the virtual-P records.  Returns the records that must
+// be rebuilt before the op (it reads P, writes part of it, or changes or
+// releases an input of P's recipe); those leave the list.
+std::vector<FlashRecord> step_flash_records(const Op &op, std::vector<FlashRecord> &records) {
+  std::vector<FlashRecord> rebuild;
+  if (op.dead) return rebuild;
+  if (op.kind == Kind::Release) {
+    const uint64_t id = op.t[0].id;
+    for (size_t r = 0; r < records.size();) {
+      const FlashRecord &f = records[r];
+      if (f.p_id == id) {
+        records.erase(records.begin() + static_cast<std::ptrdiff_t>(r));
+        continue;
+      }
+      if (id == f.q.id || id == f.k.id || id == f.divisor.id || (f.mask.p && id == f.mask.id)) {
+        rebuild.push_back(f);
+        records.erase(records.begin() + static_cast<std::ptrdiff_t>(r));
+        continue;
+      }
+      if (id == f.o.id) records[r].o_valid = false;
+      ++r;
+    }
+    return rebuild;
+  }
+  const bool opaque = op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce;
+  const Access a = access(op);
+  for (size_t r = 0; r < records.size();) {
+    FlashRecord &f = records[r];
+    bool touches = false;
+    if (opaque) {
+      for (const auto &m : op.multi)
+        for (const TRef *t : {&m.param, &m.out, &m.grad, &m.m1, &m.m2})
+          touches = touches || (t->p && (t->id == f.p_id || t->id == f.q.id ||
+                                         t->id == f.k.id || t->id == f.divisor.id ||
+                                         (f.mask.p && t->id == f.mask.id)));
+    }
+    const bool fwd_here = op.kind == Kind::FlashFwd && op.t[5].id == f.p_id;
+    const bool reads_p = op.kind != Kind::FlashBwd && !fwd_here && reads(a, f.p_id);
+    const bool writes_p = writes(a, f.p_id);
+    const bool recipe = writes(a, f.q.id) || writes(a, f.k.id) || writes(a, f.divisor.id) ||
+                        (f.mask.p && writes(a, f.mask.id));
+    if (op.kind == Kind::FlashProbs && op.t[4].id == f.p_id) {
+      records.erase(records.begin() + static_cast<std::ptrdiff_t>(r));
+      continue;
+    }
+    if (touches || reads_p || recipe || (writes_p && !fwd_here && !full_write(op))) {
+      rebuild.push_back(f);
+      records.erase(records.begin() + static_cast<std::ptrdiff_t>(r));
+      continue;
+    }
+    if (writes_p) {  // P redefined (a FlashFwd replaces the record below)
+      records.erase(records.begin() + static_cast<std::ptrdiff_t>(r));
+      continue;
+    }
+    if (writes(a, f.o.id)) f.o_valid = false;
+    ++r;
+  }
+  if (op.kind == Kind::FlashFwd) {
+    FlashRecord f;
+    f.p_id = op.t[5].id;
+    f.p = op.t[5];
+    f.q = op.t[0];
+    f.k = op.t[1];
+    f.v = op.t[2];
+    f.divisor = op.t[3];
+    f.mask = op.t[4];
+    f.o = op.t[6];
+    f.desc = op.flash;
+    records.push_back(f);
+  }
+  return rebuild;
+}
+
+Op flash_probs_op(const FlashRecord &f) {
+  Op op{};
+  op.kind = Kind::FlashProbs;
+  op.flash = f.desc;
+  op.t[0] = f.q;
+  op.t[1] = f.k;
+  op.t[2] = f.divisor;
+  op.t[3] = f.mask;
+  op.t[4] = f.p;
+  return op;
+}
+
+// Inserts FlashProbs where a virtual P must exist (see step_flash_records).
+uint64_t resolve_flash(std::vector<Op> &p) {
+  std::vector<FlashRecord> records = g_flash ? g_flash->records() : std::vector<FlashRecord>{};
+  bool any = !records.empty();
+  for (const Op &op : p) any = any || (!op.dead && op.kind == Kind::FlashFwd);
+  if (!any) return 0;
+  std::vector<Op> out;
+  out.reserve(p.size() + 4);
+  uint64_t added = 0;
+  for (Op &op : p) {
+    for (const FlashRecord &f : step_flash_records(op, records)) {
+      out.push_back(flash_probs_op(f));
+      ++added;
+    }
+    out.push_back(std::move(op));
+  }
+  p = std::move(out);
+  return added;
+}
+
+}  // namespace
+
+void update_flash_records(const std::vector<Op> &prog, std::vector<FlashRecord> &records) {
+  for (const Op &op : prog) step_flash_records(op, records);
+}
+
+namespace {
+
 // ------------------------------------------------------- grouped products
 // (flattened products, op.i1 = 1, are ordinary M x N x K products here)
 // mult(X, W -> C) [+ bias]; transpose(C viewed as [B, T, H, D], 1, 2 -> Y)
@@ -1667,8 +1999,9 @@ void add_gradient_allreduce(std::vector<Op> &prog) {
   prog.insert(prog.begin() + static_cast<std::ptrdiff_t>(first), std::move(ar));
 }
 
-uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live) {
+uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live, FlashState *flash) {
   g_live = live;
+  g_flash = flash && flash->enabled() ? flash : nullptr;
   uint64_t folded = 0;
   // Two rounds: fusion exposes further repeats (a repeated product whose
   // transposed operand lived in a released temporary reads the weight itself
@@ -1694,13 +2027,19 @@ uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live) {
   folded += fuse_row_backward_tails(prog);
   folded += fuse_gemm_gelu_backward(prog);
   folded += fuse_score_softmax(prog);
+  if (g_flash) {
+    folded += fuse_flash_forward(prog);
+    folded += fuse_flash_backward(prog);
+  }
   folded += fuse_attention(prog);
   folded += fuse_head_split_store(prog);
   folded += group_summed_products(prog);
   folded += group_shared_input(prog);
   folded += fuse_step(prog);
   if (comm) add_gradient_allreduce(prog);
+  if (g_flash) resolve_flash(prog);
   g_live = nullptr;
+  g_flash = nullptr;
   return folded;
 }
 

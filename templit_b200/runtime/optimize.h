@@ -10,7 +10,7 @@ namespace cuda::internal {
 
 // Allocation ids an op reads / writes.
 struct Access {
-  uint64_t r[16];
+  uint64_t r[20];
   int nr = 0;
   uint64_t w[6];
   int nw = 0;
@@ -37,6 +37,36 @@ struct Liveness {
   virtual bool window_local(uint64_t id) const = 0;
 };
 
+// A softmax output P = softmax(Q K^T / divisor + mask) of the attention
+// composite that a flash forward left unwritten: P is defined by its
+// recipe (the inputs below and the row log-sum-exp in desc.lse) until an op
+// other than the flash backward reads it, which first rebuilds it
+// (FlashProbs).  Writing or releasing a recipe input also rebuilds P first.
+struct FlashRecord {
+  uint64_t p_id = 0;
+  TRef p, q, k, v, o, divisor, mask;
+  tl_flash_desc desc{};  // q, k, v, o views; divisor, mask, mask_flag, lse; B, H, T, D
+  bool o_valid = true;   // O still holds the forward's output
+};
+
+// The runtime's side of flash attention: the records earlier windows left
+// and the buffers the kernels need beyond their operands.
+struct FlashState {
+  virtual ~FlashState() = default;
+  virtual bool enabled() const = 0;
+  // records of P tensors left virtual by programs already launched
+  virtual const std::vector<FlashRecord> &records() const = 0;
+  // runtime-owned [B, H, T] log-sum-exp buffer of P (stable per P)
+  virtual float *lse_buffer(uint64_t p_id, size_t bytes) = 0;
+  // a device word for the causal-mask check of mask allocation `mask_id`
+  virtual uint32_t *mask_word(uint64_t mask_id) = 0;
+};
+
+// Applies a launched program's effect on the flash records in order:
+// FlashFwd adds (or replaces) P's record, FlashProbs, a write of P or its
+// release removes it, a write of O marks it stale.
+void update_flash_records(const std::vector<Op> &prog, std::vector<FlashRecord> &records);
+
 // Rewrites a recorded program in place (ops folded into fused kernels are
 // marked dead) and returns the number of recorded ops that were folded.
 // Every rewrite preserves the values of all tensors that outlive the
@@ -44,7 +74,10 @@ struct Liveness {
 // window-local according to `live` (may be null: nothing is window-local).
 // With a communicator, gradients read by the optimiser are first summed
 // across ranks (see add_gradient_allreduce).
-uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live = nullptr);
+// With `flash` enabled, the attention composite runs on the flash kernels
+// (any sequence length) and its P stays virtual.
+uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live = nullptr,
+                  FlashState *flash = nullptr);
 
 // Inserts one AllReduce op ahead of the first optimiser op of a program
 // that updates parameters, covering every gradient that op sequence reads.

@@ -75,6 +75,18 @@ enum class Kind : uint8_t {
   //   backward Q    t0 dO, t1 v, t2 k, t3 p, t4 divisor, t5 ds, t6 dq
   //   product TN    t0 ds (or p), t1 q (or dO), t2 dk (or dv)
   Attention,
+  // flash attention (tl_flash_attention_*, `flash` holds the descriptor):
+  //   FlashFwd    t0 q, t1 k, t2 v, t3 divisor, t4 mask (optional), t5 P, t6 o:
+  //               writes o and P's log-sum-exp (a runtime buffer), not P;
+  //               P becomes a virtual tensor (FlashRecord) until something
+  //               other than FlashBwd reads it
+  //   FlashBwd    t0 q, t1 k, t2 v, t3 o, t4 dO, t5 divisor, t6 P (virtual),
+  //               t7 dk, t8 dv; group_refs: [0] dq, [1] mask (optional)
+  //   FlashProbs  t0 q, t1 k, t2 divisor, t3 mask (optional), t4 P: writes
+  //               P from the log-sum-exp (a virtual P is read by another op)
+  FlashFwd,
+  FlashBwd,
+  FlashProbs,
 };
 
 const char *kind_name(Kind k);
@@ -95,6 +107,7 @@ struct Op {
   size_t workspace = 0;    // device scratch bytes this op needs
   tl_gemm_desc gemm{};
   tl_attn_desc attn{};             // Attention
+  tl_flash_desc flash{};           // FlashFwd, FlashBwd, FlashProbs
   std::vector<uint8_t> host;       // HostWrite payload
   std::vector<MultiSlot> multi;    // MultiAdamW / AllReduce
   // grouped GEMM operands beyond group 0 (gemm.group_mode): N groups

@@ -73,7 +73,7 @@ const char *const kKindNames[] = {
     "softmax", "rms",       "rmsnorm",    "xent",       "xent_bwd",  "gather",   "scatter",
     "sqnorm",  "clip",      "adamw",      "gemm",       "host_write", "fill",    "dev_copy",
     "release", "gelu_bwd",  "softmax_bwd", "rmsnorm_bwd", "multi_adamw", "allreduce",
-    "attention"};
+    "attention", "flash_fwd", "flash_bwd", "flash_probs"};
 
 }  // namespace
 
@@ -82,7 +82,8 @@ const char *kind_name(Kind k) { return kKindNames[static_cast<int>(k)]; }
 }  // namespace internal
 
 // ---------------------------------------------------------------------------
-struct Runtime::Impl : internal::Recorder, internal::Liveness {
+struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashState,
+                       internal::HostAccessHook {
   enum class State { Idle, Recording, Submitted };
   State state = State::Idle;
   uint64_t window_id = 0;
@@ -92,6 +93,80 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
   bool graphs = true;
   int gemm_precision = TL_GEMM_TF32;
   void *comm = nullptr;
+
+  // flash attention: P tensors left virtual by launched programs, their
+  // log-sum-exp buffers, and one causal-check word per mask allocation
+  bool flash = [] {
+    const char *e = std::getenv("TL_FLASH_ATTENTION");
+    return !e || std::string(e) != "0";
+  }();
+  std::vector<internal::FlashRecord> flash_records;
+  std::unordered_map<uint64_t, detail::Block> lse_blocks, mask_words;
+
+  bool enabled() const override { return flash; }
+  const std::vector<internal::FlashRecord> &records() const override { return flash_records; }
+  float *lse_buffer(uint64_t p_id, size_t bytes) override {
+    auto it = lse_blocks.find(p_id);
+    if (it != lse_blocks.end() && it->second.bytes >= bytes) return static_cast<float *>(it->second.ptr);
+    if (it != lse_blocks.end()) detail::release(it->second);
+    detail::Block b = detail::allocate(bytes);
+    lse_blocks[p_id] = b;
+    return static_cast<float *>(b.ptr);
+  }
+  uint32_t *mask_word(uint64_t mask_id) override {
+    auto it = mask_words.find(mask_id);
+    if (it == mask_words.end()) it = mask_words.emplace(mask_id, detail::allocate(16)).first;
+    return static_cast<uint32_t *>(it->second.ptr);
+  }
+  // P of `f` from its recipe, now, on the runtime's stream
+  void materialise(const internal::FlashRecord &f) {
+    check(tl_flash_attention_probs(&f.desc, f.p.f(), cuda::stream()), "flash attention P");
+    ++stats.flash_rebuilt;
+  }
+  void before_host_access(uint64_t id, bool write, bool full) override {
+    for (size_t r = 0; r < flash_records.size();) {
+      internal::FlashRecord &f = flash_records[r];
+      const bool recipe = id == f.q.id || id == f.k.id || id == f.divisor.id ||
+                          (f.mask.p && id == f.mask.id);
+      if ((id == f.p_id && !(write && full)) || (write && recipe)) materialise(f);
+      if (id == f.p_id || (write && recipe)) {
+        flash_records.erase(flash_records.begin() + static_cast<std::ptrdiff_t>(r));
+        continue;
+      }
+      if (write && id == f.o.id) f.o_valid = false;
+      ++r;
+    }
+  }
+  void on_release(uint64_t id) noexcept override {
+    for (size_t r = 0; r < flash_records.size();) {
+      const internal::FlashRecord &f = flash_records[r];
+      const bool recipe = id == f.q.id || id == f.k.id || id == f.divisor.id ||
+                          (f.mask.p && id == f.mask.id);
+      if (recipe && cuda::initialised()) {
+        try {
+          materialise(f);  // its input is about to go
+        } catch (...) {
+        }
+      }
+      if (id == f.p_id || recipe) {
+        flash_records.erase(flash_records.begin() + static_cast<std::ptrdiff_t>(r));
+        continue;
+      }
+      ++r;
+    }
+    auto it = lse_blocks.find(id);
+    if (it != lse_blocks.end()) {
+      const detail::Block b = it->second;
+      lse_blocks.erase(it);
+      detail::release(b);
+    }
+    auto mw = mask_words.find(id);
+    if (mw != mask_words.end()) {
+      const detail::Block b = mw->second;
+      mask_words.erase(mw);
+      detail::release(b);
+    }
+  }
 
   // scratch shared by the ops of a program (they run one after another)
   detail::Block workspace;
@@ -200,6 +275,11 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
     std::string key = signature(prog);
     key += optimizer_windows >= 2 ? 'L' : '-';
     key += comm ? 'C' : '-';
+    // the optimised form depends on which P tensors are virtual
+    for (const internal::FlashRecord &f : flash_records) {
+      key.append(reinterpret_cast<const char *>(&f.p_id), sizeof(f.p_id));
+      key += f.o_valid ? 'o' : '-';
+    }
     auto it = plans.find(key);
     if (it != plans.end()) {
       bool valid = true;
@@ -225,7 +305,7 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
     for (size_t i = 0; i < prog.size(); ++i) prog[i].src = static_cast<uint32_t>(i);
     NotingLiveness live(this);
     Plan plan;
-    plan.folded = internal::optimize(prog, comm, &live);
+    plan.folded = internal::optimize(prog, comm, &live, this);
     stats.fused_ops += plan.folded;
     // small programs re-optimise cheaply; optimiser-step programs carry the
     // step count in their signature and never recur
@@ -399,6 +479,13 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
 
   void release_resources() noexcept {
     for (auto &kv : graph_cache) tl_graph_destroy(kv.second.exec);
+    flash_records.clear();
+    for (auto *m : {&lse_blocks, &mask_words}) {
+      std::vector<detail::Block> blocks;
+      for (auto &kv : *m) blocks.push_back(kv.second);
+      m->clear();
+      for (const detail::Block &b : blocks) detail::release(b);
+    }
     if (status_host) {
       if (cuda::initialised()) {
         tl_stream_sync(cuda::stream());
@@ -607,6 +694,22 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
         check(tl_attention_fused(&d, s), "attention");
         break;
       }
+      case Kind::FlashFwd:
+        if (op.code & 1)
+          check(tl_attention_mask_check(op.flash.mask, op.flash.T,
+                                        const_cast<uint32_t *>(op.flash.mask_flag), s),
+                "attention mask check");
+        check(tl_flash_attention_fwd(&op.flash, s), "flash attention");
+        break;
+      case Kind::FlashBwd: {
+        tl_flash_desc d = op.flash;
+        d.delta = static_cast<float *>(ws);
+        check(tl_flash_attention_bwd(&d, s), "flash attention backward");
+        break;
+      }
+      case Kind::FlashProbs:
+        check(tl_flash_attention_probs(&op.flash, t[4].f(), s), "flash attention P");
+        break;
     }
   }
 
@@ -635,6 +738,8 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
       if (op.kind == Kind::Fill) put(&op.u0, sizeof(op.u0));
       if (op.kind == Kind::Gemm) put(&op.gemm, sizeof(op.gemm));
       if (op.kind == Kind::Attention) put(&op.attn, sizeof(op.attn));
+      if (op.kind == Kind::FlashFwd || op.kind == Kind::FlashBwd || op.kind == Kind::FlashProbs)
+        put(&op.flash, sizeof(op.flash));
       if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce) {
         for (const auto &s : op.multi) {
           put(&s.param.p, sizeof(void *));
@@ -683,6 +788,10 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
       key += "#" + std::to_string(op.code) + " " + std::to_string(op.attn.B) + "x" +
              std::to_string(op.attn.H) + "x" + std::to_string(op.attn.T) + "x" +
              std::to_string(op.attn.D);
+    } else if (op.kind == Kind::FlashFwd || op.kind == Kind::FlashBwd ||
+               op.kind == Kind::FlashProbs) {
+      key += " " + std::to_string(op.flash.B) + "x" + std::to_string(op.flash.H) + "x" +
+             std::to_string(op.flash.T) + "x" + std::to_string(op.flash.D);
     } else if (op.kind != Kind::MultiAdamW && op.kind != Kind::AllReduce) {
       // element-wise and row ops: code and the shapes that set the traffic
       if (op.kind == Kind::Binary || op.kind == Kind::Unary || op.kind == Kind::Scalar ||
@@ -811,9 +920,15 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness {
 };
 
 // ---------------------------------------------------------------- lifecycle
-Runtime::Runtime() : impl_(std::make_unique<Impl>()) { internal::ensure_init(); }
+Runtime::Runtime() : impl_(std::make_unique<Impl>()) {
+  internal::ensure_init();
+  internal::add_host_access_hook(impl_.get());
+}
 
-Runtime::~Runtime() { cleanup(); }
+Runtime::~Runtime() {
+  cleanup();
+  internal::remove_host_access_hook(impl_.get());
+}
 
 // src/my_metal/runtime.cpp:290-297
 void Runtime::start() {
@@ -855,6 +970,15 @@ void Runtime::submit() {
   } catch (...) {
     impl_->prog.clear();
     throw;
+  }
+  if (impl_->flash) {
+    for (const Op &op : impl_->prog) {
+      if (op.dead) continue;
+      impl_->stats.flash_forward += op.kind == Kind::FlashFwd;
+      impl_->stats.flash_backward += op.kind == Kind::FlashBwd;
+      impl_->stats.flash_rebuilt += op.kind == Kind::FlashProbs;
+    }
+    internal::update_flash_records(impl_->prog, impl_->flash_records);
   }
   impl_->prog.clear();
   if (!impl_->trace_path.empty()) {
@@ -920,6 +1044,7 @@ void Runtime::end_profile() {
 }
 
 void Runtime::set_fusion(bool enabled) { impl_->fusion = enabled; }
+void Runtime::set_flash_attention(bool enabled) { impl_->flash = enabled; }
 void Runtime::set_deferred_wait(bool enabled) { impl_->deferred_wait = enabled; }
 void Runtime::set_graphs(bool enabled) { impl_->graphs = enabled; }
 void Runtime::set_gemm_precision(int precision) {

@@ -11,6 +11,7 @@
 #include "optimiser/AdamW.h"
 #include "passes/concepts.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -516,6 +517,92 @@ void graph_replay(cuda::Runtime &rt) {
   require(after.graph_replays >= before.graph_replays + 2, "the graph was replayed");
 }
 
+// The attention composite of nn::MultiHeadAttention (include/nn/
+// multi_head.h:45-52) recorded op by op: the forward runs as one flash
+// attention launch that leaves P unwritten (its recipe is kept), and P is
+// rebuilt exactly when something else needs it: a host read, and an op of a
+// later window that reads it.
+void flash_attention_virtual_probs(cuda::Runtime &rt) {
+  const uint32_t H = 2, T = 128, D = 64;
+  Tensor q({1, H, T, D}), k({1, H, T, D}), v({1, H, T, D}), div({1, 1}), mask({1, 1, T, T});
+  Tensor p({1, H, T, T}), o({1, H, T, D}), p2({1, H, T, T});
+  std::vector<float> qv(H * T * D), kv(H * T * D), vv(H * T * D), mv(T * T);
+  for (size_t i = 0; i < qv.size(); ++i) {
+    qv[i] = std::sin(0.37f * float(i)) * 1.5f;
+    kv[i] = std::cos(0.23f * float(i)) * 1.5f;
+    vv[i] = std::sin(0.11f * float(i) + 1.0f);
+  }
+  for (uint32_t r = 0; r < T; ++r)
+    for (uint32_t c = 0; c < T; ++c) mv[r * T + c] = c > r ? -INFINITY : 0.0f;
+  q.set(qv);
+  k.set(kv);
+  v.set(vv);
+  mask.set(mv);
+  put(div, {8.0f});
+  auto forward = [&] {
+    Tensor kt({1, H, D, T}), s({1, H, T, T}), sd({1, H, T, T}), sm({1, H, T, T});
+    rt.transpose(k, kt);
+    rt.mult(q, kt, s);
+    rt.divide(s, div, sd);
+    rt.add(sd, mask, sm);
+    rt.softmax(sm, p);
+    rt.mult(p, v, o);
+  };
+  // the softmax of the scores in double precision
+  std::vector<double> want(H * T * T), ov(H * T * D, 0.0);
+  for (uint32_t h = 0; h < H; ++h)
+    for (uint32_t r = 0; r < T; ++r) {
+      double mx = -1e300;
+      std::vector<double> row(T);
+      for (uint32_t c = 0; c < T; ++c) {
+        double acc = 0;
+        for (uint32_t d = 0; d < D; ++d)
+          acc += double(qv[(h * T + r) * D + d]) * double(kv[(h * T + c) * D + d]);
+        row[c] = c > r ? -1e300 : acc / 8.0;
+        mx = std::max(mx, row[c]);
+      }
+      double sum = 0;
+      for (uint32_t c = 0; c < T; ++c) sum += row[c] <= -1e299 ? 0.0 : std::exp(row[c] - mx);
+      for (uint32_t c = 0; c < T; ++c) {
+        const double pv = row[c] <= -1e299 ? 0.0 : std::exp(row[c] - mx) / sum;
+        want[(h * T + r) * T + c] = pv;
+        for (uint32_t d = 0; d < D; ++d) ov[(h * T + r) * D + d] += pv * vv[(h * T + c) * D + d];
+      }
+    }
+  auto close = [&](const std::vector<float> &got, const std::vector<double> &ref,
+                   const std::string &what) {
+    double num = 0, den = 0;
+    for (size_t i = 0; i < got.size(); ++i) {
+      num += (got[i] - ref[i]) * (got[i] - ref[i]);
+      den += ref[i] * ref[i];
+    }
+    require(std::sqrt(num / den) < 2e-3, what + ": relative error " +
+                                             std::to_string(std::sqrt(num / den)));
+  };
+  const auto s0 = rt.stats();
+  for (int it = 0; it < 3; ++it) {
+    run(rt, forward);
+    close(get(o), ov, "attention output");
+  }
+  const auto s1 = rt.stats();
+  require(s1.flash_forward >= s0.flash_forward + 3, "the forward ran on the flash kernels");
+  // the host reads P: it is written out from the recipe first
+  close(get(p), want, "P read by the host");
+  require(rt.stats().flash_rebuilt == s1.flash_rebuilt + 1, "P rebuilt for the host read");
+  // an op of a later window reads P
+  run(rt, forward);
+  const auto s2 = rt.stats();
+  run(rt, [&] { rt.add(p, p, p2); });
+  require(rt.stats().flash_rebuilt == s2.flash_rebuilt + 1, "P rebuilt for the reading op");
+  std::vector<double> twice(want.size());
+  for (size_t i = 0; i < want.size(); ++i) twice[i] = 2 * want[i];
+  close(get(p2), twice, "P read by a later op");
+  // a window that writes the recipe's input first rebuilds P from the old one
+  run(rt, forward);
+  run(rt, [&] { rt.add(q, q, q); });
+  close(get(p), want, "P kept across a change of Q");
+}
+
 }  // namespace
 
 int main(int argc, char **argv) {
@@ -549,6 +636,7 @@ int main(int argc, char **argv) {
         {"storage_semantics", storage_semantics},
         {"alias_safety", alias_safety},
         {"graph_replay", graph_replay},
+        {"flash_attention_virtual_probs", flash_attention_virtual_probs},
     };
     for (const auto &[name, fn] : cases) {
       if (!only.empty() && only != name) continue;

@@ -12,8 +12,9 @@ probabilities rebuilt from the log-sum-exp.
 
 Tolerance, ||X - X_ref||_F / ||X_ref||_F per output, TF32 products: 1e-3
 per TF32 product on the output's path (as the fused-attention tests): P 1,
-O 2, dV 2, dQ and dK 3; the log-sum-exp within 1e-3 absolute (it is a
-log).  Repeated runs are bit-identical (no atomics)."""
+O 2, dV 2, dQ and dK 3; the log-sum-exp within 1e-3 relative (its error is
+the TF32 error of the largest scores of the row).  Repeated runs are
+bit-identical (no atomics)."""
 import ctypes
 
 import numpy as np
@@ -111,7 +112,7 @@ def run(dev, B, H, T, seed=0, causal=True, mask=None, layout="bhtd", k_trans=Fal
         return np.swapaxes(x, 1, 2) if layout == "bthd" else x
     got = {"o": host(to), "dq": host(tdq), "dk": host(tdk), "dv": host(tdv)}
     errs = {n: fro(got[n], want[n]) for n in want}
-    lse_err = float(np.abs(dev.host(lse) - lse_want).max())
+    lse_err = float((np.abs(dev.host(lse) - lse_want) / np.abs(lse_want).clip(1.0)).max())
     print(f"B {B} H {H} T {T} {layout}{' K^T' if k_trans else ''}: {errs}, lse {lse_err:.2e}")
     for n, e in errs.items():
         assert e <= 1e-3 * CHAIN[n], (n, e, errs)
