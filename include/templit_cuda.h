@@ -457,6 +457,13 @@ int tl_attention_fused_supported(const tl_attn_desc *d);
 /* TL_ERR_UNSUPPORTED when they do not. */
 int tl_attention_fused(const tl_attn_desc *d, void *stream);
 
+/* Test of the bounded on-device waits (no counterpart in the reference):
+ * one CTA allocates TMEM, waits on an mbarrier nothing arrives at for at
+ * most limit_ns (<= 1 s), raises TL_FLAG_TIMEOUT, frees TMEM and returns;
+ * *waited_us (device memory) receives how long it waited.  The path every
+ * tensor-core kernel of this library takes when a wait gives up. */
+int tl_check_wait_timeout(uint64_t limit_ns, uint32_t *waited_us, void *stream);
+
 /* Flash attention for any T and 64-wide heads: the same attention as
  * tl_attention_fused (the executor's composite of include/nn/multi_head.h:
  * 45-52 and its backward through SFTMX_DERIVATIVE, include/passes/

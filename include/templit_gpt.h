@@ -12,9 +12,10 @@
  *
  * Model families: `family` 4 is the reference's 4-block GPT (d_model 384,
  * 6 heads, vocab 2048, max sequence 192); `family` 12 the 12-block,
- * d_model 768, 12-head, max-sequence-1024 variant of the data-parallel
- * configuration.  All calls return 0 on success; tlg_last_error() explains
- * a failure.
+ * d_model 768, 12-head, FFN 3072, max-sequence-1024 variant of the
+ * data-parallel configuration (the reference's decoder blocks, embedding
+ * and projection, generalised from GPT.h's four blocks).  All calls return
+ * 0 on success; tlg_last_error() explains a failure.
  */
 #ifndef TEMPLIT_GPT_H
 #define TEMPLIT_GPT_H
@@ -37,15 +38,23 @@ typedef struct tlg_config {
   uint32_t world;        /* data-parallel ranks sharing the global batch       */
   int32_t fusion;        /* runtime program fusion on/off                      */
   int32_t graphs;        /* CUDA-graph replay on/off                           */
-  int32_t gemm_precision; /* TL_GEMM_TF32 (0, tensor cores) or TL_GEMM_FP32 (1) */
+  int32_t gemm_precision; /* TL_GEMM_TF32 (0, tensor cores), TL_GEMM_FP32 (1) or
+                             TL_GEMM_3XTF32 (2, split tf32 operands)            */
   int32_t deferred_wait; /* cuda::Runtime::set_deferred_wait: the host records the
                             next window while the GPU runs the current one     */
+  uint32_t micro_batches; /* > 1: a train step is this many forward / backward
+                             passes of `batch` sequences, their gradients
+                             summed (the reference's gradient accumulation
+                             across backward calls, include/passes/context.h:
+                             74-89), then one optimiser step; tlg_set_batch
+                             takes micro_batches * batch sequences           */
 } tlg_config;
 
 const char *tlg_last_error(void);
 int tlg_create(const tlg_config *config, void **handle);
 int tlg_destroy(void *handle);
-/* Host token ids and targets, batch*seq each (row-major [batch, seq]). */
+/* Host token ids and targets, micro_batches*batch*seq each (row-major
+ * [micro_batches * batch, seq]; micro_batches 0 counts as 1). */
 int tlg_set_batch(void *handle, const uint32_t *tokens, const uint32_t *targets);
 /* One training iteration; *mean_loss receives the mean loss of this rank's batch. */
 int tlg_train_step(void *handle, float *mean_loss);

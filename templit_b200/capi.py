@@ -86,7 +86,8 @@ class TlgConfig(Structure):
                 ("beta1", c_float), ("beta2", c_float), ("eps", c_float),
                 ("weight_decay", c_float), ("clip", c_float),
                 ("world", c_uint32), ("fusion", c_int32), ("graphs", c_int32),
-                ("gemm_precision", c_int32), ("deferred_wait", c_int32)]
+                ("gemm_precision", c_int32), ("deferred_wait", c_int32),
+                ("micro_batches", c_uint32)]
 
 
 U32P = POINTER(c_uint32)
@@ -128,6 +129,7 @@ CUDA_ABI = {
     "tl_flash_attention_bwd": (c_int, [POINTER(TlFlashDesc), c_void_p]),
     "tl_flash_attention_probs": (c_int, [POINTER(TlFlashDesc), c_void_p, c_void_p]),
     "tl_attention_mask_check": (c_int, [c_void_p, c_uint32, c_void_p, c_void_p]),
+    "tl_check_wait_timeout": (c_int, [c_uint64, c_void_p, c_void_p]),
     "tl_graph_capture_begin": (c_int, [c_void_p]),
     "tl_graph_capture_end": (c_int, [c_void_p, POINTER(c_void_p)]),
     "tl_graph_launch": (c_int, [c_void_p, c_void_p]),

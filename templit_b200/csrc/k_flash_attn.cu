@@ -891,44 +891,30 @@ flash_bwd_kv_kernel(const __grid_constant__ Maps maps, const Args a) {
 }
 
 // ============================================== probabilities (fallback)
-// P[b, h, t, :] = exp(S / divisor + mask - L) of one query row per warp,
-// lanes over keys (CUDA-core dot products): the softmax output a reader
-// other than the fused backward asks for.
+// P[b, h, t, :] = exp(S[b, h, t, :] / divisor + mask - L[b, h, t]) in place
+// over the scores S = Q K^T that a tensor-core product wrote into p: one
+// warp per row, the softmax output a reader other than the fused backward
+// asks for.
 __global__ void __launch_bounds__(256)
-flash_probs_kernel(View q, View k, bool k_trans, const float *divisor, const float *mask,
-                   const uint32_t *mask_flag, const float *lse, uint32_t T, uint32_t H,
-                   uint64_t rows, float *p) {
+flash_probs_rows_kernel(float *p, const float *divisor, const float *mask,
+                        const uint32_t *mask_flag, const float *lse, uint32_t T, uint64_t rows) {
   pdl_enter();
   const float inv = 1.0f / *divisor;
   const bool causal = mask && mask_flag && *mask_flag != 0;
   const uint64_t warps = static_cast<uint64_t>(gridDim.x) * (blockDim.x / 32);
   const uint32_t lane = threadIdx.x & 31;
   for (uint64_t r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < rows; r += warps) {
-    const uint32_t t = static_cast<uint32_t>(r % T), bh = static_cast<uint32_t>(r / T);
-    const uint32_t b = bh / H, h = bh % H;
-    float qr[64];
-    const float *qp = row_ptr(q, b, h, t);
-#pragma unroll
-    for (int d = 0; d < 64; ++d) qr[d] = qp[d];
+    const uint32_t t = static_cast<uint32_t>(r % T);
     const float L = lse[r];
+    float *row = p + r * T;
     for (uint32_t key = lane; key < T; key += 32) {
-      float s = 0.0f;
-      if (k_trans) {
-        const float *kp = k.p + b * k.sb + h * k.sh + key;
-#pragma unroll
-        for (int d = 0; d < 64; ++d) s = fmaf(qr[d], kp[static_cast<uint64_t>(d) * k.ld], s);
-      } else {
-        const float *kp = row_ptr(k, b, h, key);
-#pragma unroll
-        for (int d = 0; d < 64; ++d) s = fmaf(qr[d], kp[d], s);
-      }
-      float v = s * inv;
+      float v = row[key] * inv;
       if (causal) {
         if (key > t) v = -INFINITY;
       } else if (mask) {
         v = v + mask[static_cast<uint64_t>(t) * T + key];
       }
-      p[r * T + key] = expf(v - L);
+      row[key] = expf(v - L);
     }
   }
 }
@@ -1059,9 +1045,33 @@ int launch_flash_bwd(const AttnDims &d, const HeadView &q, const HeadView &k, co
 int launch_flash_probs(const AttnDims &d, const HeadView &q, const HeadView &k,
                        const float *divisor, const float *mask, const uint32_t *mask_flag,
                        const float *lse, float *p, cudaStream_t s) {
+  // S = Q K^T per (batch, head) on the tensor cores, straight into p
+  tl_gemm_desc g{};
+  g.a = q.p;
+  g.b = k.p;
+  g.c = p;
+  g.m = d.T;
+  g.n = d.T;
+  g.k = HD;
+  g.trans_b = k.trans ? 0 : 1;  // K rows [T, D] are B stored [N, K]; K^T is [K, N]
+  g.precision = TL_GEMM_TF32;
+  g.batch_rank = 2;
+  g.batch_shape[0] = d.B;
+  g.batch_shape[1] = d.H;
+  g.a_batch_stride[0] = q.sb;
+  g.a_batch_stride[1] = q.sh;
+  g.b_batch_stride[0] = k.sb;
+  g.b_batch_stride[1] = k.sh;
+  g.c_batch_stride[0] = static_cast<uint64_t>(d.H) * d.T * d.T;
+  g.c_batch_stride[1] = static_cast<uint64_t>(d.T) * d.T;
+  g.lda = q.ld;
+  g.ldb = k.ld;
+  g.ldc = d.T;
+  int rc = tl_gemm(&g, s);
+  if (rc) return rc;
   const uint64_t rows = static_cast<uint64_t>(d.B) * d.H * d.T;
-  launch_pdl(flash_probs_kernel, grid_for(rows * 32, 256), 256, 0, s, view_of(q), view_of(k),
-             k.trans, divisor, mask, mask ? mask_flag : nullptr, lse, d.T, d.H, rows, p);
+  launch_pdl(flash_probs_rows_kernel, grid_for(rows * 32, 256), 256, 0, s, p, divisor, mask,
+             mask ? mask_flag : nullptr, lse, d.T, rows);
   return launch_status("flash attention probabilities");
 }
 

@@ -177,6 +177,8 @@ class GptDriver final : public DriverBase {
   std::unique_ptr<CompiledT> compiled_;
   Mat root_grad_;
   std::vector<float> losses_;
+  uint32_t micro_;                         // forward / backward passes per step
+  std::vector<uint32_t> tokens_, targets_host_;  // all micro-batches of a step
 
   static std::unique_ptr<CompiledT> build(const Model &model, Indices &input, Indices &targets,
                                           Run &runtime, const tlg_config &c) {
@@ -192,15 +194,17 @@ public:
         targets_(IndexMat({c.batch, c.seq})), gen_(c.seed), model_(c.batch, c.seq, gen_),
         compiled_(build(model_, input_, targets_, runtime_, c)),
         root_grad_(Mat({c.batch, c.seq, 1})),
-        losses_(static_cast<size_t>(c.batch) * c.seq) {
+        losses_(static_cast<size_t>(c.batch) * c.seq),
+        micro_(c.micro_batches > 1 ? c.micro_batches : 1) {
     // zero ids so prepare() sees valid inputs
     std::vector<uint32_t> zeros(losses_.size(), 0);
     input_.get_value().set(zeros);
     targets_.get_value().set(zeros);
     compiled_->prepare();
     const float world = static_cast<float>(c.world ? c.world : 1);
-    root_grad_.set(std::vector<float>(losses_.size(),
-                                      1.0f / (static_cast<float>(losses_.size()) * world)));
+    root_grad_.set(std::vector<float>(
+        losses_.size(), 1.0f / (static_cast<float>(losses_.size()) * world *
+                                static_cast<float>(micro_))));
     if (c.init_std > 0.0f) redraw(c.init_std);
   }
 
@@ -208,6 +212,11 @@ public:
 
   void set_batch(const uint32_t *tokens, const uint32_t *targets) override {
     const size_t n = losses_.size();
+    if (micro_ > 1) {  // kept on the host; each pass loads its slice
+      tokens_.assign(tokens, tokens + n * micro_);
+      targets_host_.assign(targets, targets + n * micro_);
+      return;
+    }
     input_.get_value().set(std::span<const uint32_t>(tokens, n));
     targets_.get_value().set(std::span<const uint32_t>(targets, n));
   }
@@ -218,6 +227,7 @@ public:
   // loss tensor), so with a deferred wait the host records those windows
   // while the GPU still runs the forward pass.
   float train_step() override {
+    if (micro_ > 1) return train_step_micro();
     compiled_->zero_grad();
     const Mat loss = compiled_->forward();
     compiled_->backward(root_grad_);
@@ -227,6 +237,27 @@ public:
     double acc = 0.0;
     for (float v : losses_) acc += v;
     return static_cast<float>(acc / static_cast<double>(losses_.size()));
+  }
+
+  // Gradient accumulation: one zero_grad, micro_ forward / backward passes
+  // (later backward calls add to the gradients, include/passes/context.h:
+  // 74-89) with root gradient 1 / (all tokens of the step), one step.
+  float train_step_micro() {
+    const size_t n = losses_.size();
+    if (tokens_.size() != n * micro_) throw std::logic_error("no batch set for the step");
+    compiled_->zero_grad();
+    double acc = 0.0;
+    for (uint32_t m = 0; m < micro_; ++m) {
+      input_.get_value().set(std::span<const uint32_t>(tokens_.data() + m * n, n));
+      targets_.get_value().set(std::span<const uint32_t>(targets_host_.data() + m * n, n));
+      const Mat loss = compiled_->forward();
+      compiled_->backward(root_grad_);
+      loss.read(losses_);
+      for (float v : losses_) acc += v;
+    }
+    if (cfg_.clip > 0.0f) compiled_->step(cfg_.clip);
+    else compiled_->step();
+    return static_cast<float>(acc / static_cast<double>(n * micro_));
   }
 
   void forward(float *losses) override {

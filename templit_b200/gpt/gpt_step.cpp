@@ -55,9 +55,7 @@ std::unique_ptr<templit_b200::DriverBase> make_driver(const tlg_config &c, cuda:
     if (c.seq == 0 || c.seq > 192) throw std::invalid_argument("family 4 takes seq in [1, 192]");
     return std::make_unique<templit_b200::GptDriver<Mat, cuda::Runtime, GPT4>>(c, rt);
   }
-#ifdef TLG_WITH_DEEP
   if (c.family == 12) return templit_b200::make_deep_driver(c, rt);
-#endif
   throw std::invalid_argument("unsupported GPT family " + std::to_string(c.family));
 }
 

@@ -7,6 +7,7 @@
 // Runs on a GPU; prints one "PASS <name>" line per case and exits non-zero
 // on the first failure.
 #include "my_cuda/runtime.h"
+#include "templit_cuda.h"
 #include "my_cuda/storage.h"
 #include "optimiser/AdamW.h"
 #include "passes/concepts.h"
@@ -603,6 +604,24 @@ void flash_attention_virtual_probs(cuda::Runtime &rt) {
   close(get(p), want, "P kept across a change of Q");
 }
 
+// A kernel wait that runs out inside a window: wait() throws
+// std::runtime_error (src/my_metal/runtime.cpp:310-317 raises on command
+// buffer errors), and the runtime keeps working afterwards.
+void wait_timeout(cuda::Runtime &rt) {
+  uint32_t *waited = nullptr;
+  require(tl_malloc(reinterpret_cast<void **>(&waited), 16) == TL_OK, "scratch");
+  rt.start();
+  require(tl_check_wait_timeout(2000000, waited, cuda::stream()) == TL_OK, "launch");
+  rt.submit();
+  require(throws<std::runtime_error>([&] { rt.wait(); }), "wait() reports the timeout");
+  tl_free(waited);
+  Tensor a({2, 2}), b({2, 2}), c({2, 2});
+  put(a, {1, 2, 3, 4});
+  put(b, {1, 0, 0, 1});
+  run(rt, [&] { rt.mult(a, b, c); });
+  expect(c, {1, 2, 3, 4}, "runtime usable after a timeout");
+}
+
 }  // namespace
 
 int main(int argc, char **argv) {
@@ -637,6 +656,7 @@ int main(int argc, char **argv) {
         {"alias_safety", alias_safety},
         {"graph_replay", graph_replay},
         {"flash_attention_virtual_probs", flash_attention_virtual_probs},
+        {"wait_timeout", wait_timeout},
     };
     for (const auto &[name, fn] : cases) {
       if (!only.empty() && only != name) continue;

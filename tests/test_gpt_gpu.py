@@ -11,9 +11,10 @@ Tolerances (relative, stated per test below):
     steps within 1e-5 (FP32), 3e-5 (3xTF32) and 3e-3 (TF32).  AdamW's first
     steps move each parameter by lr * g / (|g| + eps): about lr * sign(g),
     so an element whose gradient is within rounding of zero (or of eps) may
-    move differently; the parameters after two steps agree within 1e-5
-    relative per element except at most 0.5 % of them (FP32, 3xTF32), and
-    the parameter updates agree within 1 % in norm (10 % for TF32).
+    move differently.  The parameter updates agree within 1e-4 in norm for
+    FP32 (measured 1.3e-5; and within 1e-5 relative per element except at
+    most 0.5 % of the elements, measured 0.14 %), 1e-3 for 3xTF32 (measured
+    5.0e-4) and 0.1 for TF32 (measured 1.75e-2).
   * The 100-step loss curve at batch 4, T 192 (the oracle's curve is a
     committed fixture, tests/golden/make_gpt_curve_fixture.py): within
     1e-3 of the oracle at every step for FP32 and 3xTF32 products.  Plain
@@ -244,7 +245,10 @@ def test_config4_step_matches_oracle(config4_oracle, precision, rtol, rtol_after
         # sign-like first steps differ on more elements
         assert upd <= 0.1
         return
-    assert upd <= 1e-2
+    if precision == capi.TL_GEMM_3XTF32:
+        assert upd <= 1e-3
+        return
+    assert upd <= 1e-4
     flipped, worst, off = 0, 0.0, 0
     for n in sizes:
         g, c = p2[off:off + n].astype(np.float64), o["p2"][off:off + n].astype(np.float64)
