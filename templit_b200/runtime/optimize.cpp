@@ -1069,13 +1069,16 @@ uint64_t fuse_attention(std::vector<Op> &p) {
 //             only; P stays virtual (FlashRecord) for the backward window
 //   backward  dP = dO V^T, softmax derivative(dP, P) / divisor -> dS,
 //             dQ = dS K, dK = dS^T Q, dV = P^T dO  ->  one FlashBwd at the
-//             last of the three products, P of a virtual record
-//             recomputed from Q, K and the log-sum-exp, dP and dS never
-//             written
+//             first of these ops (the gradients are consumed right after
+//             each is made, so they are written early, never late), P of a
+//             virtual record recomputed from Q, K and the log-sum-exp, dP
+//             and dS never written
 // resolve_flash then rebuilds a virtual P (FlashProbs) in front of any other
 // reader, and before any write or release of its recipe's inputs.
 
 thread_local FlashState *g_flash = nullptr;
+
+bool no_reuse_between(const std::vector<Op> &p, size_t i, size_t j, const TRef &dst);
 
 bool same_view(const tl_attn_view &a, const tl_attn_view &b) {
   return a.p == b.p && a.batch_stride == b.batch_stride && a.head_stride == b.head_stride &&
@@ -1229,18 +1232,22 @@ uint64_t fuse_flash_backward(std::vector<Op> &p) {
         !same_view(dov, dov2))
       continue;
     d.d_o = dov;
+    // the fused op runs at F, the first of the group; its inputs exist there
+    // (dO is the dP product's input) and are read-only up to the last one
+    const size_t F = std::min({i, k, jq, jk, jv});
     const size_t J = std::max({jq, jk, jv});
-    const size_t first = std::min({i, jq, jk, jv});
     const TRef dO = p[i].t[0], dQ = p[jq].t[2], dK = p[jk].t[2], dV = p[jv].t[2];
     bool ok = true;
     for (const TRef *in : {&rec->q, &rec->k, &rec->v, &rec->divisor, &dO, &P})
-      ok = ok && unchanged_between(p, first, J, in->id);
-    ok = ok && (!rec->mask.p || unchanged_between(p, first, J, rec->mask.id));
+      ok = ok && unchanged_between(p, F, J, in->id);
+    ok = ok && (!rec->mask.p || unchanged_between(p, F, J, rec->mask.id));
     // O: not written in this program before the backward (from op 0 on)
-    ok = ok && unchanged_between(p, kNone, J, rec->o.id);
+    ok = ok && unchanged_between(p, kNone, F, rec->o.id);
+    // each gradient is written at F instead of at its product: nothing in
+    // between may read or write its buffer, or reuse its addresses
     for (size_t r : {jq, jk, jv}) {
       const TRef &out = p[r].t[2];
-      ok = ok && untouched_between(p, r, J, out.id);
+      ok = ok && untouched_between(p, F, r, out.id) && no_reuse_between(p, F, r, out);
       for (const TRef *in : {&rec->q, &rec->k, &rec->v, &rec->o, &dO, &P})
         ok = ok && out.id != in->id;
     }
@@ -1260,10 +1267,10 @@ uint64_t fuse_flash_backward(std::vector<Op> &p) {
     fused.t[8] = dV;
     fused.group_refs = {dQ, rec->mask};
     fused.workspace = static_cast<size_t>(B) * H * T * 4;  // delta = rowsum(dO * O)
-    fused.src = p[J].src;
+    fused.src = p[F].src;
     for (size_t r : {i, k, jq, jk, jv})
-      if (r != J) p[r].dead = true;
-    p[J] = std::move(fused);
+      if (r != F) p[r].dead = true;
+    p[F] = std::move(fused);
     folded += 4;
   }
   return folded;
