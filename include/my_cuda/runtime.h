@@ -118,11 +118,13 @@ public:
   // GEMM arithmetic of mult: TL_GEMM_TF32 (tcgen05 tensor cores, default)
   // or TL_GEMM_FP32 (exact fp32 products on CUDA cores).
   void set_gemm_precision(int precision);
-  // Attention composites on the flash kernels (default on; the environment
-  // variable TL_FLASH_ATTENTION=0 turns it off): the forward keeps the
+  // Attention composites on the flash kernels: the forward keeps the
   // softmax output P as its recipe (row log-sum-exp) instead of writing it,
   // the backward recomputes it, and any other reader gets it rebuilt first.
-  void set_flash_attention(bool enabled);
+  // Mode 0: never; 1 (default): sequences longer than the short-sequence
+  // fused kernels take (T > 192), which are faster up to there; 2: always.
+  // The environment variable TL_FLASH_ATTENTION sets the initial mode.
+  void set_flash_attention(int mode);
   // Data parallelism: an NCCL communicator (ncclComm_t as void*).  When set,
   // the program of a window that updates parameters (AdamW) first
   // sum-reduces every gradient it reads across the communicator's ranks, so

@@ -141,6 +141,9 @@ enum tl_reduce_op { TL_REDUCE_SUM = 0, TL_REDUCE_MAX = 1 };
  * Reduce x to out_shape (trailing-aligned; every out dim equal to the x dim
  * or 1).  Replaces Runtime::sum_to_shape / max_to_shape / reduce_to_shape
  * (src/my_metal/runtime.cpp:595-745; math.metal:618-714).  Deterministic.
+ * A column reduction split over many CTAs folds its partials in the same
+ * launch, counting arrivals in counters inside the library: reductions of
+ * one process must not run concurrently on several streams. 
  * workspace may be NULL when tl_reduce_workspace_size() returns 0.
  */
 int tl_reduce(int op, const float *x, const uint32_t *x_shape, int x_rank,

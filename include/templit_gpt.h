@@ -48,6 +48,10 @@ typedef struct tlg_config {
                              across backward calls, include/passes/context.h:
                              74-89), then one optimiser step; tlg_set_batch
                              takes micro_batches * batch sequences           */
+  int32_t flash_attention; /* attention on the flash kernels: 0 where the short-
+                              sequence fused kernels cannot run (T > 192), 1
+                              always, -1 never (cuda::Runtime::
+                              set_flash_attention modes 1, 2, 0)               */
 } tlg_config;
 
 const char *tlg_last_error(void);

@@ -87,7 +87,7 @@ class TlgConfig(Structure):
                 ("weight_decay", c_float), ("clip", c_float),
                 ("world", c_uint32), ("fusion", c_int32), ("graphs", c_int32),
                 ("gemm_precision", c_int32), ("deferred_wait", c_int32),
-                ("micro_batches", c_uint32)]
+                ("micro_batches", c_uint32), ("flash_attention", c_int32)]
 
 
 U32P = POINTER(c_uint32)

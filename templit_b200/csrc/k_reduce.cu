@@ -105,17 +105,28 @@ cols_kernel(const float *__restrict__ x, float *out, uint32_t K1, uint32_t R,
   }
 }
 
+// Arrival counters of the single-launch column reduction: one per (k1,
+// column block), back at zero after every launch (atomicInc wraps), so the
+// launches of a stream reuse them; reductions that run concurrently on
+// several streams must not share the library (documented in the header).
+constexpr uint32_t kColTickets = 1u << 16;
+static __device__ unsigned int g_col_tickets[kColTickets];
+
 // [K1, R, K2] column reduction by blocks: CTA (c, k1, cb) folds rows
 // [c * rchunk, (c + 1) * rchunk) of columns [128 cb, 128 cb + 128): warp w
 // takes rows w, w + 8, ... (float4 per lane, 128-byte rows per warp) and the
 // 8 warp results are folded in warp order, so each split costs one pass over
-// its rows with all 8 warps' loads in flight and the order is fixed.
+// its rows with all 8 warps' loads in flight and the order is fixed.  With
+// `fold` (several splits), the partial goes to part[c]; the last CTA of the
+// (k1, column block) to finish folds all splits' partials in split order
+// into out, in the same launch.
 template <int OP>
 __global__ void __launch_bounds__(256)
 cols_block_kernel(const float *__restrict__ x, float *out, uint32_t K1, uint32_t R,
-                  uint32_t K2, uint32_t rchunk) {
+                  uint32_t K2, uint32_t rchunk, float *fold_out) {
   pdl_enter();
   __shared__ float4 part[8][32];
+  __shared__ bool last;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t c = blockIdx.x, k1 = blockIdx.y;
   const uint32_t col = blockIdx.z * 128 + lane * 4;
@@ -134,6 +145,47 @@ cols_block_kernel(const float *__restrict__ x, float *out, uint32_t K1, uint32_t
   }
   part[warp][lane] = acc;
   __syncthreads();
+  if (warp == 0 && col < K2) {
+    float4 r = part[0][lane];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) {
+      const float4 v = part[w][lane];
+      r.x = rcomb<OP>(r.x, v.x);
+      r.y = rcomb<OP>(r.y, v.y);
+      r.z = rcomb<OP>(r.z, v.z);
+      r.w = rcomb<OP>(r.w, v.w);
+    }
+    *reinterpret_cast<float4 *>(out + static_cast<size_t>(c) * K1 * K2 +
+                                static_cast<size_t>(k1) * K2 + col) = r;
+  }
+  if (!fold_out) return;
+  // publish this split's partial, then count arrivals of the column block
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned slot = k1 * gridDim.z + blockIdx.z;
+    last = atomicInc(&g_col_tickets[slot], gridDim.x - 1) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // fold the splits: warp w takes splits w, w + 8, ... in order, then the
+  // warp results in warp order (the order is fixed: deterministic)
+  const size_t plane = static_cast<size_t>(K1) * K2;
+  float4 a = make_float4(rinit<OP>(), rinit<OP>(), rinit<OP>(), rinit<OP>());
+  if (col < K2) {
+    const float *src = out + static_cast<size_t>(k1) * K2 + col;
+#pragma unroll 4
+    for (uint32_t sp = warp; sp < gridDim.x; sp += 8) {
+      const float4 v = __ldcg(reinterpret_cast<const float4 *>(src + sp * plane));
+      a.x = rcomb<OP>(a.x, v.x);
+      a.y = rcomb<OP>(a.y, v.y);
+      a.z = rcomb<OP>(a.z, v.z);
+      a.w = rcomb<OP>(a.w, v.w);
+    }
+  }
+  part[warp][lane] = a;
+  __syncthreads();
   if (warp != 0 || col >= K2) return;
   float4 r = part[0][lane];
 #pragma unroll
@@ -144,8 +196,7 @@ cols_block_kernel(const float *__restrict__ x, float *out, uint32_t K1, uint32_t
     r.z = rcomb<OP>(r.z, v.z);
     r.w = rcomb<OP>(r.w, v.w);
   }
-  *reinterpret_cast<float4 *>(out + static_cast<size_t>(c) * K1 * K2 +
-                              static_cast<size_t>(k1) * K2 + col) = r;
+  *reinterpret_cast<float4 *>(fold_out + static_cast<size_t>(k1) * K2 + col) = r;
 }
 
 // Sums `splits` partial planes part[s, i] into out[i].  A CTA of W warps
@@ -293,10 +344,11 @@ int make_plan(const uint32_t *x_shape, int x_rank, const uint32_t *out_shape,
     pl.K2 = g == 2 ? gs[1] : gs[2];
     const uint64_t outs = static_cast<uint64_t>(pl.K1) * pl.K2;
     if (pl.K2 % 4 == 0 && pl.K1 <= 65535 && pl.K2 / 128 < 65535) {
-      // blocks of 8 warps x 128 columns: about four CTAs per SM, >= 64 rows
+      // blocks of 8 warps x 128 columns: about two CTAs per SM, >= 128 rows
+      // (the last CTA of a column block folds the splits' partials)
       const uint64_t colblocks = (pl.K2 + 127) / 128;
-      uint64_t want = (4ull * kNumSMs + pl.K1 * colblocks - 1) / (pl.K1 * colblocks);
-      const uint64_t max_splits = (pl.R + 63) / 64;
+      uint64_t want = (2ull * kNumSMs + pl.K1 * colblocks - 1) / (pl.K1 * colblocks);
+      const uint64_t max_splits = (pl.R + 127) / 128;
       if (want > max_splits) want = max_splits;
       if (want < 1) want = 1;
       uint32_t chunk = static_cast<uint32_t>((pl.R + want - 1) / want);
@@ -365,9 +417,16 @@ int run_plan(const ReducePlan &pl, const float *x, float *out, void *ws,
       float *dst = pl.splits > 1 ? static_cast<float *>(ws) : out;
       const uint64_t outs = static_cast<uint64_t>(pl.K1) * pl.K2;
       const uint64_t work = (vec ? outs / 4 : outs) * pl.splits;
+      const uint64_t slots = static_cast<uint64_t>(pl.K1) * ((pl.K2 + 127) / 128);
+      if (pl.block && vec && pl.splits > 1 && slots <= kColTickets) {
+        // one launch: the last CTA of each column block folds the splits
+        launch_pdl(cols_block_kernel<OP>, dim3(pl.splits, pl.K1, (pl.K2 + 127) / 128), 256, 0, s,
+                   x, dst, pl.K1, pl.R, pl.K2, pl.chunk, out);
+        return launch_status("reduce cols");
+      }
       if (pl.block && vec)
         launch_pdl(cols_block_kernel<OP>, dim3(pl.splits, pl.K1, (pl.K2 + 127) / 128), 256, 0, s, 
-            x, dst, pl.K1, pl.R, pl.K2, pl.chunk);
+            x, dst, pl.K1, pl.R, pl.K2, pl.chunk, static_cast<float *>(nullptr));
       else if (vec)
         launch_pdl(cols_kernel<OP, 4>, grid_for(work, 256, 16), 256, 0, s, x, dst, pl.K1, pl.R, pl.K2, pl.splits, pl.chunk);
       else

@@ -76,6 +76,9 @@ int tlg_create(const tlg_config *config, void **handle) {
     h->runtime->set_graphs(config->graphs != 0);
     h->runtime->set_gemm_precision(config->gemm_precision);
     h->runtime->set_deferred_wait(config->deferred_wait != 0);
+    if (config->flash_attention < -1 || config->flash_attention > 1)
+      throw std::invalid_argument("flash_attention is -1, 0 or 1");
+    if (config->flash_attention != 0) h->runtime->set_flash_attention(config->flash_attention + 1);
     h->driver = make_driver(*config, *h->runtime);
     *handle = h.release();
   });

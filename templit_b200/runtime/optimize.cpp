@@ -97,6 +97,7 @@ namespace {
 
 constexpr size_t kNone = static_cast<size_t>(-1);
 constexpr uint32_t kFusedHeadDimHost = 64;  // head width of tl_attention_fused
+constexpr uint32_t kFusedMaxKeysHost = 192;  // longest sequence of tl_attention_fused
 
 // Window liveness of the program being optimised (null: none known).
 thread_local const Liveness *g_live = nullptr;
@@ -1101,6 +1102,7 @@ uint64_t fuse_flash_forward(std::vector<Op> &p) {
     const TRef X = sm.t[0], Y = sm.t[1], div = sm.t[2], mask = sm.t[3];
     uint32_t B, H, T;
     if (!score_dims(Y, B, H, T) || !is_scalar_tensor(div)) continue;
+    if (!g_flash->always() && T <= kFusedMaxKeysHost) continue;  // the fused kernels' range
     if (mask.p && mask.numel() != static_cast<uint64_t>(T) * T) continue;
     const size_t i = last_writer(p, k, X.id);
     if (i == kNone || !plain_product(p[i]) || first_reader(p, i, X.id) != k ||
@@ -1361,7 +1363,28 @@ Op flash_probs_op(const FlashRecord &f) {
   return op;
 }
 
-// Inserts FlashProbs where a virtual P must exist (see step_flash_records).
+// True when, from op `from` on, allocation `id` is redefined (fully
+// written, or defined anew by a flash forward) or released before anything
+// reads it: its current value is dead.
+bool redefined_before_read(const std::vector<Op> &p, size_t from, uint64_t id) {
+  for (size_t j = from; j < p.size(); ++j) {
+    const Op &op = p[j];
+    if (op.dead) continue;
+    if (op.kind == Kind::Release) {
+      if (op.t[0].id == id) return true;
+      continue;
+    }
+    if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce) return false;
+    if (op.kind == Kind::FlashFwd && op.t[5].id == id) return true;
+    const Access a = access(op);
+    if (reads(a, id)) return false;
+    if (writes(a, id) && full_write(op)) return true;
+  }
+  return false;  // alive at the end: a later window may read it
+}
+
+// Inserts FlashProbs where a virtual P must exist (see step_flash_records);
+// a P whose value is dead there (the next forward redefines it) is dropped.
 uint64_t resolve_flash(std::vector<Op> &p) {
   std::vector<FlashRecord> records = g_flash ? g_flash->records() : std::vector<FlashRecord>{};
   bool any = !records.empty();
@@ -1370,12 +1393,13 @@ uint64_t resolve_flash(std::vector<Op> &p) {
   std::vector<Op> out;
   out.reserve(p.size() + 4);
   uint64_t added = 0;
-  for (Op &op : p) {
-    for (const FlashRecord &f : step_flash_records(op, records)) {
+  for (size_t j = 0; j < p.size(); ++j) {
+    for (const FlashRecord &f : step_flash_records(p[j], records)) {
+      if (redefined_before_read(p, j, f.p_id)) continue;
       out.push_back(flash_probs_op(f));
       ++added;
     }
-    out.push_back(std::move(op));
+    out.push_back(std::move(p[j]));
   }
   p = std::move(out);
   return added;

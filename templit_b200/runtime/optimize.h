@@ -54,6 +54,9 @@ struct FlashRecord {
 struct FlashState {
   virtual ~FlashState() = default;
   virtual bool enabled() const = 0;
+  // true: every attention composite the flash kernels take; false: only
+  // those the short-sequence fused kernels cannot (T above 192)
+  virtual bool always() const = 0;
   // records of P tensors left virtual by programs already launched
   virtual const std::vector<FlashRecord> &records() const = 0;
   // runtime-owned [B, H, T] log-sum-exp buffer of P (stable per P)

@@ -96,14 +96,17 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashSt
 
   // flash attention: P tensors left virtual by launched programs, their
   // log-sum-exp buffers, and one causal-check word per mask allocation
-  bool flash = [] {
+  // 0 off, 1 where the short-sequence fused kernels cannot run (T > 192;
+  // they are faster up to there), 2 always; TL_FLASH_ATTENTION overrides
+  int flash = [] {
     const char *e = std::getenv("TL_FLASH_ATTENTION");
-    return !e || std::string(e) != "0";
+    return e ? std::atoi(e) : 1;
   }();
   std::vector<internal::FlashRecord> flash_records;
   std::unordered_map<uint64_t, detail::Block> lse_blocks, mask_words;
 
-  bool enabled() const override { return flash; }
+  bool enabled() const override { return flash != 0; }
+  bool always() const override { return flash >= 2; }
   const std::vector<internal::FlashRecord> &records() const override { return flash_records; }
   float *lse_buffer(uint64_t p_id, size_t bytes) override {
     auto it = lse_blocks.find(p_id);
@@ -1044,7 +1047,10 @@ void Runtime::end_profile() {
 }
 
 void Runtime::set_fusion(bool enabled) { impl_->fusion = enabled; }
-void Runtime::set_flash_attention(bool enabled) { impl_->flash = enabled; }
+void Runtime::set_flash_attention(int mode) {
+  if (mode < 0 || mode > 2) throw std::invalid_argument("flash attention mode is 0, 1 or 2");
+  impl_->flash = mode;
+}
 void Runtime::set_deferred_wait(bool enabled) { impl_->deferred_wait = enabled; }
 void Runtime::set_graphs(bool enabled) { impl_->graphs = enabled; }
 void Runtime::set_gemm_precision(int precision) {

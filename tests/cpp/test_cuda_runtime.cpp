@@ -524,6 +524,7 @@ void graph_replay(cuda::Runtime &rt) {
 // rebuilt exactly when something else needs it: a host read, and an op of a
 // later window that reads it.
 void flash_attention_virtual_probs(cuda::Runtime &rt) {
+  rt.set_flash_attention(2);  // T = 128 would take the short-sequence kernels
   const uint32_t H = 2, T = 128, D = 64;
   Tensor q({1, H, T, D}), k({1, H, T, D}), v({1, H, T, D}), div({1, 1}), mask({1, 1, T, T});
   Tensor p({1, H, T, T}), o({1, H, T, D}), p2({1, H, T, T});
@@ -602,6 +603,7 @@ void flash_attention_virtual_probs(cuda::Runtime &rt) {
   run(rt, forward);
   run(rt, [&] { rt.add(q, q, q); });
   close(get(p), want, "P kept across a change of Q");
+  rt.set_flash_attention(1);
 }
 
 // A kernel wait that runs out inside a window: wait() throws

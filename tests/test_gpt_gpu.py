@@ -34,11 +34,12 @@ from templit_b200 import capi
 pytestmark = pytest.mark.gpu
 
 
-def config(batch, seq, precision=capi.TL_GEMM_TF32, fusion=1, graphs=1, seed=11, deferred=1):
+def config(batch, seq, precision=capi.TL_GEMM_TF32, fusion=1, graphs=1, seed=11, deferred=1,
+           flash=0):
     return capi.TlgConfig(family=4, batch=batch, seq=seq, seed=seed, init_std=0.02, lr=3e-4,
                           beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, clip=1.0, world=1,
                           fusion=fusion, graphs=graphs, gemm_precision=precision,
-                          deferred_wait=deferred)
+                          deferred_wait=deferred, flash_attention=flash)
 
 
 class CudaGPT:
@@ -142,14 +143,15 @@ CURVE_FIXTURE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden
                              "gpt_curve_b4_t192.npz")
 
 
-@pytest.mark.parametrize("precision,rtol", [
-    (capi.TL_GEMM_FP32, 1e-3),    # exact fp32 products (CUDA cores)
-    (capi.TL_GEMM_3XTF32, 1e-3),  # split tf32 operands on the tensor cores
-    (capi.TL_GEMM_TF32, 0.3)])    # plain TF32: the benchmark path's drift
-def test_loss_curve_100_steps_tracks_oracle(precision, rtol):
+@pytest.mark.parametrize("precision,rtol,flash", [
+    (capi.TL_GEMM_FP32, 1e-3, 0),    # exact fp32 products (CUDA cores)
+    (capi.TL_GEMM_3XTF32, 1e-3, 0),  # split tf32 operands on the tensor cores
+    (capi.TL_GEMM_TF32, 0.3, 0),     # plain TF32: the benchmark path's drift
+    (capi.TL_GEMM_TF32, 0.3, 1)])    # ... with attention on the flash kernels
+def test_loss_curve_100_steps_tracks_oracle(precision, rtol, flash):
     fx = np.load(CURVE_FIXTURE)
     B, T = int(fx["batch"]), int(fx["seq"])
-    cfg = config(B, T, precision=precision, seed=int(fx["seed"]))
+    cfg = config(B, T, precision=precision, seed=int(fx["seed"]), flash=flash)
     # the oracle's initial weights (the ones the fixture's curve starts from)
     cpu = oracle().OracleGPT(config(B, T, precision=capi.TL_GEMM_FP32, seed=int(fx["seed"])))
     p0 = cpu.params()
@@ -212,13 +214,15 @@ def param_sizes(g, tmp_path):
     return [int(np.prod(shapes[i])) for i in range(len(shapes))]
 
 
-@pytest.mark.parametrize("precision,rtol,rtol_after", [
-    (capi.TL_GEMM_FP32, 1e-5, 1e-5),
-    (capi.TL_GEMM_3XTF32, 1e-5, 3e-5),
-    (capi.TL_GEMM_TF32, 1e-3, 3e-3)])
-def test_config4_step_matches_oracle(config4_oracle, precision, rtol, rtol_after, tmp_path):
+@pytest.mark.parametrize("precision,rtol,rtol_after,flash", [
+    (capi.TL_GEMM_FP32, 1e-5, 1e-5, 0),
+    (capi.TL_GEMM_3XTF32, 1e-5, 3e-5, 0),
+    (capi.TL_GEMM_TF32, 1e-3, 3e-3, 0),
+    (capi.TL_GEMM_TF32, 1e-3, 3e-3, 1)])  # attention on the flash kernels (P never stored)
+def test_config4_step_matches_oracle(config4_oracle, precision, rtol, rtol_after, flash,
+                                     tmp_path):
     o = config4_oracle
-    gpu = CudaGPT(config(64, 192, precision=precision))
+    gpu = CudaGPT(config(64, 192, precision=precision, flash=flash))
     p0 = o["p0"]
     gpu.set_params(p0)  # the oracle's initial weights
     assert np.array_equal(gpu.params(), p0)
@@ -299,3 +303,21 @@ def test_full_size_step_runs():
         last = g.train_step()
     assert abs(first - np.log(2048)) < 0.5 and last < first
     g.close()
+
+
+def test_flash_attention_replay_is_bit_exact():
+    """Attention on the flash kernels (P kept as its recipe between the
+    forward and backward windows): graph replay equals eager launches bit
+    for bit, run to run, and tracks the short-sequence kernels' step."""
+    rng = np.random.default_rng(4)
+    x, y = zipf(rng, 4, 128)
+    runs = []
+    for graphs, flash in ((1, 1), (0, 1), (1, 1), (1, 0)):
+        g = CudaGPT(config(4, 128, graphs=graphs, flash=flash))
+        g.set_batch(x, y)
+        runs.append(([g.train_step() for _ in range(4)], g.params()))
+        g.close()
+    (l1, p1), (l2, p2), (l3, p3), (l4, _) = runs
+    assert l1 == l2 and np.array_equal(p1, p2)  # replay == eager
+    assert l1 == l3 and np.array_equal(p1, p3)  # run to run
+    np.testing.assert_allclose(l1, l4, rtol=1e-3)  # flash vs fused short-sequence kernels
