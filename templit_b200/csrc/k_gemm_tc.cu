@@ -32,6 +32,8 @@
 
 #include <cuda.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 namespace tl {
@@ -100,10 +102,16 @@ struct TcArgs {
   bool aux_prefetch;
 };
 
-template <int BN, bool SPLIT>
+// PAIR: a CTA pair (cluster of 2) computes a 256 x BN tile with cta_group::2
+// products; each CTA loads its 128 rows of A and BN / 2 columns of B and
+// holds its 128 rows of the accumulator.
+template <int BN, bool SPLIT, bool PAIR = false>
 struct Cfg {
+  static_assert(!(SPLIT && PAIR), "3xTF32 runs on single CTAs");
   static constexpr int THREADS = 64 + 32 * kEpiWarps + (SPLIT ? 32 * kConvWarps : 0);
-  static constexpr uint32_t B_BYTES = BN * BK * 4;
+  static constexpr int BN_LOAD = PAIR ? BN / 2 : BN;  // columns of B this CTA loads
+  static constexpr uint32_t BMT = PAIR ? 256 : 128;    // rows of a tile
+  static constexpr uint32_t B_BYTES = BN_LOAD * BK * 4;
   // bytes TMA brings per stage (A then B); a 3xTF32 stage holds their
   // small parts after them in the same layout
   static constexpr uint32_t LOAD_BYTES = kA_BYTES + B_BYTES;
@@ -171,10 +179,10 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t j) {
   return r * 128u + ((j ^ (r & 7u)) << 4);
 }
 
-template <int BN, bool A_MN, bool B_MN, bool SPLIT>
-__global__ void __launch_bounds__(Cfg<BN, SPLIT>::THREADS, 1)
+template <int BN, bool A_MN, bool B_MN, bool SPLIT, bool PAIR>
+__global__ void __launch_bounds__(Cfg<BN, SPLIT, PAIR>::THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
-  using C = Cfg<BN, SPLIT>;
+  using C = Cfg<BN, SPLIT, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -192,6 +200,10 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const GemmArgs &g = t.g;
+  // CTA pairs: rank in the pair, and the pair's place in the tile loop
+  const uint32_t rank = PAIR ? ptx::cluster_rank() : 0u;
+  const uint64_t tile0 = PAIR ? blockIdx.x / 2 : blockIdx.x;
+  const uint64_t tile_step = PAIR ? gridDim.x / 2 : gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -201,7 +213,8 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&tfull[a], 1);
-      ptx::mbar_init(&tempty[a], 32 * kEpiWarps);
+      // a pair's accumulator is free once the epilogues of both CTAs read it
+      ptx::mbar_init(&tempty[a], (PAIR ? 2 : 1) * 32 * kEpiWarps);
     }
     for (int w = 0; w < kEpiWarps; ++w) ptx::mbar_init(&abar[w], 1);
     *abort_flag = 0;
@@ -214,11 +227,18 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
     }
   }
   if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, C::TMEM_COLS);
-    ptx::tmem_relinquish();
+    if constexpr (PAIR) {
+      ptx::tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+      ptx::tmem_relinquish_pair();
+    } else {
+      ptx::tmem_alloc(tmem_slot, C::TMEM_COLS);
+      ptx::tmem_relinquish();
+    }
   }
   ptx::tc_fence_before();
   __syncthreads();
+  // a pair: both CTAs' barriers exist before either signals the other's
+  if constexpr (PAIR) ptx::cluster_sync();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t ktiles = t.kgroups ? t.g.groups * t.kb_per_group : (g.k + BK - 1) / BK;
@@ -235,8 +255,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
       uint64_t issued = 0;
-      for (uint64_t tile = blockIdx.x; tile < t.num_tiles && !*abort_flag;
-           tile += gridDim.x) {
+      for (uint64_t tile = tile0; tile < t.num_tiles && !*abort_flag; tile += tile_step) {
         uint64_t z;
         uint32_t s, mb, nb, kb0, kb1, grp;
         decode_tile(t, tile, z, s, mb, nb, grp);
@@ -245,7 +264,10 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
         batch_coords(g, z, cz);
         map_coords(t.ma, cz, za);
         map_coords(t.mb, cz, zb);
-        const int32_t m0 = static_cast<int32_t>(mb * BM), n0 = static_cast<int32_t>(nb * BN);
+        // this CTA's rows of A; its columns of B (a pair splits them)
+        const int32_t m0 = static_cast<int32_t>(mb * C::BMT + rank * BM);
+        const int32_t n0 = static_cast<int32_t>(nb * BN);
+        const int32_t nl = n0 + static_cast<int32_t>(rank * C::BN_LOAD);
         if (t.aux_prefetch) {
           // the epilogue's addend / GELU-input boxes of this tile: into L2
           // while the mainloop runs, so its per-chunk loads hit L2
@@ -262,7 +284,12 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
           }
           uint8_t *sa = stage_base + stage * C::STAGE_BYTES;
           uint8_t *sb = sa + kA_BYTES;
-          ptx::mbar_arrive_expect_tx(&full[stage], C::LOAD_BYTES);
+          if constexpr (PAIR) {
+            // both CTAs' loads count on the first CTA's barrier
+            if (rank == 0) ptx::mbar_arrive_expect_tx(&full[stage], 2 * C::LOAD_BYTES);
+          } else {
+            ptx::mbar_arrive_expect_tx(&full[stage], C::LOAD_BYTES);
+          }
           // K groups walk group after group; N groups use their own B
           uint32_t kg = 0, kl = kb;
           if (t.kgroups) {
@@ -272,25 +299,38 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
           const CUtensorMap *tmA = &maps.a[kg];
           const CUtensorMap *tmB = &maps.b[t.kgroups ? kg : grp];
           const int32_t k0 = static_cast<int32_t>(kl * BK);
+          // a box at (x, y) (+ batch coordinates z) of map m into dst
+          auto load2 = [&](void *dst, const CUtensorMap *m, int32_t x, int32_t y, int nz,
+                           const int32_t *zz) {
+            if constexpr (PAIR) {
+              const int32_t c[5] = {x, y, zz[0], zz[1], zz[2]};
+              ptx::tma_load_pair(dst, m, ptx::mapa_shared(&full[stage], 0), 2 + nz, c);
+            } else {
+              ptx::tma_load_nd(dst, m, &full[stage], x, y, nz, zz);
+            }
+          };
+          auto loadr = [&](void *dst, const CUtensorMap *m, int r, const int32_t *c) {
+            if constexpr (PAIR) ptx::tma_load_pair(dst, m, ptx::mapa_shared(&full[stage], 0), r, c);
+            else ptx::tma_load_rank(dst, m, &full[stage], r, c);
+          };
           if (!A_MN) {
-            ptx::tma_load_nd(sa, tmA, &full[stage], k0, m0, t.ma.nb, za);
+            load2(sa, tmA, k0, m0, t.ma.nb, za);
           } else if (t.ma.chunked) {
             const int32_t c[5] = {0, k0, m0 / 32, za[0], za[1]};
-            ptx::tma_load_rank(sa, tmA, &full[stage], 3 + t.ma.nb, c);
+            loadr(sa, tmA, 3 + t.ma.nb, c);
           } else {
 #pragma unroll
-            for (int j = 0; j < BM / 32; ++j)
-              ptx::tma_load_nd(sa + j * 4096, tmA, &full[stage], m0 + 32 * j, k0, t.ma.nb, za);
+            for (int j = 0; j < BM / 32; ++j) load2(sa + j * 4096, tmA, m0 + 32 * j, k0, t.ma.nb, za);
           }
           if (!B_MN) {
-            ptx::tma_load_nd(sb, tmB, &full[stage], k0, n0, t.mb.nb, zb);
+            load2(sb, tmB, k0, nl, t.mb.nb, zb);
           } else if (t.mb.chunked) {
-            const int32_t c[5] = {0, k0, n0 / 32, zb[0], zb[1]};
-            ptx::tma_load_rank(sb, tmB, &full[stage], 3 + t.mb.nb, c);
+            const int32_t c[5] = {0, k0, nl / 32, zb[0], zb[1]};
+            loadr(sb, tmB, 3 + t.mb.nb, c);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / 32; ++j)
-              ptx::tma_load_nd(sb + j * 4096, tmB, &full[stage], n0 + 32 * j, k0, t.mb.nb, zb);
+            for (int j = 0; j < C::BN_LOAD / 32; ++j)
+              load2(sb + j * 4096, tmB, nl + 32 * j, k0, t.mb.nb, zb);
           }
           ++issued;
           if (++stage == C::STAGES) {
@@ -299,8 +339,11 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
           }
         }
       }
-      // Drain: every issued k-tile must have landed before the CTA may exit.
+      // Drain: every issued k-tile must have landed before the CTA may exit
+      // (a pair's second CTA: its loads count on the first CTA's barriers,
+      // which that CTA drains; the pair meets at a cluster barrier at exit).
       uint64_t back = issued < static_cast<uint64_t>(C::STAGES) ? issued : C::STAGES;
+      if (PAIR && rank != 0) back = 0;
       uint32_t s = stage, p = phase;
       for (uint64_t i = 0; i < back; ++i) {
         if (s == 0) {
@@ -317,12 +360,12 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = ptx::idesc_tf32(BM, BN, A_MN, B_MN);
+    // (a pair's products are issued by its first CTA)
+    if (lane == 0 && (!PAIR || rank == 0)) {
+      constexpr uint32_t idesc = ptx::idesc_tf32(C::BMT, BN, A_MN, B_MN);
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool issued_any = false;
-      for (uint64_t tile = blockIdx.x; tile < t.num_tiles && !*abort_flag;
-           tile += gridDim.x) {
+      for (uint64_t tile = tile0; tile < t.num_tiles && !*abort_flag; tile += tile_step) {
         if (!ptx::mbar_wait_bounded(&tempty[acc], acc_phase ^ 1, kWaitLimitNs)) {
           timeout();
           break;
@@ -361,19 +404,25 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
               ptx::mma_tf32(d_tmem, ad, b_desc(sb + C::LOAD_BYTES, kk), idesc, acc_in);
               ptx::mma_tf32(d_tmem, a_desc(sa + C::LOAD_BYTES, kk), bd, idesc, 1u);
               ptx::mma_tf32(d_tmem, ad, bd, idesc, 1u);
+            } else if constexpr (PAIR) {
+              ptx::mma_tf32_pair(d_tmem, ad, bd, idesc, acc_in);
             } else {
               ptx::mma_tf32(d_tmem, ad, bd, idesc, acc_in);
             }
           }
           issued_any = true;
-          ptx::mma_commit(&empty[stage]);  // stage reusable once these MMAs finish
+          // stage reusable (in both CTAs of a pair) once these MMAs finish
+          if constexpr (PAIR) ptx::mma_commit_pair(&empty[stage], 0x3);
+          else ptx::mma_commit(&empty[stage]);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        ptx::mma_commit(&tfull[acc]);  // accumulator ready for the epilogue
+        // accumulator ready for the epilogue (of both CTAs of a pair)
+        if constexpr (PAIR) ptx::mma_commit_pair(&tfull[acc], 0x3);
+        else ptx::mma_commit(&tfull[acc]);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
@@ -381,7 +430,8 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
       }
       if (*abort_flag && issued_any) {
         // let in-flight MMAs finish before TMEM is released
-        ptx::mma_commit(&tfull[acc]);
+        if constexpr (PAIR) ptx::mma_commit_pair(&tfull[acc], 0x1);
+        else ptx::mma_commit(&tfull[acc]);
         ptx::mbar_wait_bounded(&tfull[acc], acc_phase, kWaitLimitNs);
       }
     }
@@ -444,10 +494,16 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
     const bool early_aux = kBoxPerChunk && t.tma_epi && t.partial == nullptr &&
                            (g.addend != nullptr || g.gelu_grad_x != nullptr) &&
                            g.gelu_out == nullptr;
-    for (uint64_t tile = blockIdx.x; tile < t.num_tiles; tile += gridDim.x) {
+    // a pair's first CTA counts both CTAs' releases of an accumulator
+    auto release_acc = [&](uint32_t a) {
+      if (PAIR && rank != 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(&tempty[a], 0));
+      else ptx::mbar_arrive(&tempty[a]);
+    };
+    for (uint64_t tile = tile0; tile < t.num_tiles; tile += tile_step) {
       uint64_t z;
       uint32_t s, mb, nb, grp;
       decode_tile(t, tile, z, s, mb, nb, grp);
+      const uint32_t row0 = mb * C::BMT + rank * BM;  // this CTA's rows of the tile
       int32_t zc[3];
       int ncz;
       {
@@ -465,7 +521,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
           for (uint32_t i = 0; i < early_chunks; ++i)
             ptx::tma_load_nd(obuf + i * 4096, &maps.addend, my_abar,
                              static_cast<int32_t>(nb * BN + (c0 + 2 * i) * 32),
-                             static_cast<int32_t>(mb * BM + q * 32), ncz, zc);
+                             static_cast<int32_t>(row0 + q * 32), ncz, zc);
         }
         __syncwarp();
       }
@@ -497,7 +553,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
       float *Cb = raw ? t.partial + static_cast<size_t>(slice) * g.m * g.n : g.c + oc;
       // N groups: this tile's product has its own output and bias
       const float *bias = t.g.groups > 1 && !t.kgroups ? t.g.biasg[grp] : g.bias;
-      const uint32_t m = mb * BM + q * 32 + lane;
+      const uint32_t m = row0 + q * 32 + lane;
       const uint32_t n_base = nb * BN;
       const bool row_ok = m < g.m;
       // 128-bit path: raw partials, or the full epilogue on float4 groups
@@ -514,7 +570,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
         // store of the 32 x 32 box (rows and columns past M, N are clipped).
         // A warp's boxes alternate (two per warp; one for 256-wide tiles) so
         // a store is in flight while the next box is filled.
-        const int32_t y0 = static_cast<int32_t>(mb * BM + q * 32);
+        const int32_t y0 = static_cast<int32_t>(row0 + q * 32);
         if (raw) {  // split-K slices: [groups x splits][M][N]
           zc[0] = static_cast<int32_t>(slice);
           zc[1] = zc[2] = 0;
@@ -619,7 +675,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
           }
         }
         ptx::tc_fence_before();
-        ptx::mbar_arrive(&tempty[acc]);
+        release_acc(acc);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
@@ -674,7 +730,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
         }
       }
       ptx::tc_fence_before();
-      ptx::mbar_arrive(&tempty[acc]);
+      release_acc(acc);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
@@ -686,8 +742,14 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
   if (warp >= 2 && lane == 0) ptx::bulk_wait_group<0>();
   ptx::tc_fence_before();
   __syncthreads();
+  // a pair: neither CTA leaves while the other may still use its shared
+  // memory (products) or barriers (loads, releases)
+  if constexpr (PAIR) ptx::cluster_sync();
   ptx::tc_fence_after();
-  if (warp == 1) ptx::tmem_dealloc(tmem_base, C::TMEM_COLS);
+  if (warp == 1) {
+    if constexpr (PAIR) ptx::tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    else ptx::tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
 }
 
 // ---------------------------------------------------------------- host side
@@ -764,6 +826,7 @@ struct TcPlan {
   int bn;
   uint32_t splits, kb_per_split;
   size_t workspace;
+  bool pair;  // 256-row tiles on CTA pairs (cta_group::2)
 };
 
 TcPlan plan_width(const GemmArgs &g, int max_bn) {
@@ -826,27 +889,50 @@ bool make_head_map(CUtensorMap *map, float *base, const GemmArgs &g) {
          CUDA_SUCCESS;
 }
 
+// Whether CTA pairs should take the product: 256-row tiles halve the B
+// columns each SM loads per k-step (the operand fill from L2 bounds the
+// small-K products), for unsplit TF32 products with many full 256-row
+// tiles: at least one wave of pairs.
+bool use_pairs(const GemmArgs &g, const TcPlan &p) {
+  if (g.split_tf32 || p.splits != 1 || g.m % 256 || (p.bn != 128 && p.bn != 256)) return false;
+  static const bool enabled = [] {
+    const char *e = std::getenv("TL_GEMM_PAIRS");
+    return e && std::strcmp(e, "1") == 0;
+  }();
+  if (!enabled) return false;
+  const bool kgroups = g.groups > 1 && g.group_mode == TL_GEMM_GROUP_K;
+  const uint64_t outs = g.batch_count * (g.groups > 1 && !kgroups ? g.groups : 1);
+  const uint64_t tiles = outs * (g.m / 256) * ((g.n + p.bn - 1) / p.bn);
+  return tiles >= static_cast<uint64_t>(kNumSMs) / 2;
+}
+
 TcPlan plan_tc(const GemmArgs &g) {
   // 3xTF32 stages are twice as large: tiles of at most 128 columns
-  const TcPlan p = plan_width(g, g.split_tf32 ? 128 : 256);
+  TcPlan p = plan_width(g, g.split_tf32 ? 128 : 256);
+  if (p.bn == 192) {  // pairs split the columns of B in halves of 32-multiples
+    const TcPlan q = plan_width(g, 128);
+    if (use_pairs(g, q)) p = q;
+  }
+  p.pair = use_pairs(g, p);
   // An epilogue that loads a box per chunk (addend, GELU-backward input)
   // loads all of a tile's boxes while the tile's MMAs run when it has a
   // staging box per chunk, which only tiles up to 128 wide have.  Only
   // unsplit products narrow their tiles: the K slicing, and so the
   // summation order, stays the one the same product has without epilogue.
   if (p.splits == 1 && (g.addend || g.gelu_grad_x) && !g.gelu_out) {
-    const TcPlan q = plan_width(g, 128);
+    TcPlan q = plan_width(g, 128);
+    q.pair = use_pairs(g, q);
     if (q.splits == 1) return q;
   }
   return p;
 }
 
-template <int BN, bool A_MN, bool B_MN, bool SPLIT>
+template <int BN, bool A_MN, bool B_MN, bool SPLIT, bool PAIR>
 int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaStream_t s) {
-  using C = Cfg<BN, SPLIT>;
+  using C = Cfg<BN, SPLIT, PAIR>;
   TcArgs t{};
   t.g = g;
-  t.mt = (g.m + BM - 1) / BM;
+  t.mt = (g.m + C::BMT - 1) / C::BMT;
   t.nt = (g.n + BN - 1) / BN;
   t.kgroups = g.groups > 1 && g.group_mode == TL_GEMM_GROUP_K;
   t.kb_per_group = (g.k + BK - 1) / BK;
@@ -872,9 +958,9 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
                                    32, BM, CU_TENSOR_MAP_SWIZZLE_128B, t.ma);
     ok = ok && (B_MN ? make_operand_map(&maps.b[i], g.bg[i] ? g.bg[i] : g.b, g.n, g.k, g.ldb, g,
                                         g.sb, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, t.mb,
-                                        BN / 32)
+                                        C::BN_LOAD / 32)
                      : make_operand_map(&maps.b[i], g.bg[i] ? g.bg[i] : g.b, g.k, g.n, g.ldb, g,
-                                        g.sb, 32, BN, CU_TENSOR_MAP_SWIZZLE_128B, t.mb));
+                                        g.sb, 32, C::BN_LOAD, CU_TENSOR_MAP_SWIZZLE_128B, t.mb));
   }
   if (!ok) return fail(TL_ERR_UNSUPPORTED, "tl_gemm: tensor map rejected");
   // epilogue through TMA stores when C (and gelu_out, addend: same layout)
@@ -918,16 +1004,23 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
     return fail(TL_ERR_UNSUPPORTED, "tl_gemm: grouped outputs need 16-byte rows");
   static bool attr_set = false;
   if (!attr_set) {
-    int rc = check_cuda(cudaFuncSetAttribute(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT>,
+    int rc = check_cuda(cudaFuncSetAttribute(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT, PAIR>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(C::SMEM)),
                         "tl_gemm smem attribute");
     if (rc) return rc;
     attr_set = true;
   }
-  const uint64_t grid = t.num_tiles < static_cast<uint64_t>(kNumSMs) ? t.num_tiles : kNumSMs;
-  launch_pdl(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT>, static_cast<unsigned>(grid), C::THREADS,
-             C::SMEM, s, maps, t);
+  if constexpr (PAIR) {
+    const uint64_t pairs = kNumSMs / 2;
+    const uint64_t grid = 2 * (t.num_tiles < pairs ? t.num_tiles : pairs);
+    launch_pdl_cluster(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT, PAIR>, static_cast<unsigned>(grid),
+                       C::THREADS, C::SMEM, s, 2u, maps, t);
+  } else {
+    const uint64_t grid = t.num_tiles < static_cast<uint64_t>(kNumSMs) ? t.num_tiles : kNumSMs;
+    launch_pdl(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT, PAIR>, static_cast<unsigned>(grid),
+               C::THREADS, C::SMEM, s, maps, t);
+  }
   int rc = launch_status("tl_gemm tf32");
   if (rc || !partial) return rc;
   const uint64_t mn = static_cast<uint64_t>(g.m) * g.n;
@@ -945,13 +1038,13 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
   return TL_OK;
 }
 
-template <int BN, bool SPLIT = false>
+template <int BN, bool SPLIT = false, bool PAIR = false>
 int launch_bn(const GemmArgs &g, const TcPlan &plan, float *partial, cudaStream_t s) {
   const bool a_mn = g.trans_a != 0, b_mn = g.trans_b == 0;
-  if (a_mn && b_mn) return launch_variant<BN, true, true, SPLIT>(g, plan, partial, s);
-  if (a_mn) return launch_variant<BN, true, false, SPLIT>(g, plan, partial, s);
-  if (b_mn) return launch_variant<BN, false, true, SPLIT>(g, plan, partial, s);
-  return launch_variant<BN, false, false, SPLIT>(g, plan, partial, s);
+  if (a_mn && b_mn) return launch_variant<BN, true, true, SPLIT, PAIR>(g, plan, partial, s);
+  if (a_mn) return launch_variant<BN, true, false, SPLIT, PAIR>(g, plan, partial, s);
+  if (b_mn) return launch_variant<BN, false, true, SPLIT, PAIR>(g, plan, partial, s);
+  return launch_variant<BN, false, false, SPLIT, PAIR>(g, plan, partial, s);
 }
 
 }  // namespace
@@ -987,6 +1080,9 @@ int launch_tc_gemm(const GemmArgs &g, void *workspace, size_t workspace_bytes, c
   if (g.split_tf32)
     return plan.bn == 128 ? launch_bn<128, true>(g, plan, partial, s)
                           : launch_bn<64, true>(g, plan, partial, s);
+  if (plan.pair)
+    return plan.bn == 256 ? launch_bn<256, false, true>(g, plan, partial, s)
+                          : launch_bn<128, false, true>(g, plan, partial, s);
   if (plan.bn == 256) return launch_bn<256>(g, plan, partial, s);
   if (plan.bn == 192) return launch_bn<192>(g, plan, partial, s);
   if (plan.bn == 128) return launch_bn<128>(g, plan, partial, s);

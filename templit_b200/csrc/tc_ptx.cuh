@@ -80,6 +80,32 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
   }
 }
 
+// ----------------------------------------------------- CTA pairs (clusters)
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// The shared::cluster address of `local`'s counterpart in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(const void *local, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_addr(local)), "r"(rank));
+  return a;
+}
+
+// Every thread of every CTA of the cluster arrives, then waits for all.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+
+// Arrive on an mbarrier of another CTA of the cluster (shared::cluster address).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
 // ----------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *map,
                                             uint64_t *bar, int32_t c0, int32_t c1,
@@ -125,6 +151,46 @@ __device__ __forceinline__ void tma_load_nd(void *smem_dst, const CUtensorMap *m
           "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
           " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(d),
           "l"(m), "r"(c0), "r"(c1), "r"(zc[0]), "r"(zc[1]), "r"(zc[2]), "r"(b)
+          : "memory");
+      break;
+  }
+}
+
+// Tiled TMA load into this CTA's shared memory whose completion is counted
+// on an mbarrier of the pair's first CTA (`bar` a shared::cluster address):
+// the loads of both CTAs of a cta_group::2 product signal one barrier.  No
+// multicast.
+__device__ __forceinline__ void tma_load_pair(void *smem_dst, const CUtensorMap *map,
+                                              uint32_t bar, int rank, const int32_t *c) {
+  const uint64_t m = reinterpret_cast<uint64_t>(map);
+  const uint32_t d = smem_addr(smem_dst);
+  switch (rank) {
+    case 2:
+      asm volatile(
+          "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+          " [%0], [%1, {%2, %3}], [%4];" ::"r"(d),
+          "l"(m), "r"(c[0]), "r"(c[1]), "r"(bar)
+          : "memory");
+      break;
+    case 3:
+      asm volatile(
+          "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+          " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(d),
+          "l"(m), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(bar)
+          : "memory");
+      break;
+    case 4:
+      asm volatile(
+          "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+          " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(d),
+          "l"(m), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]), "r"(bar)
+          : "memory");
+      break;
+    default:
+      asm volatile(
+          "cp.async.bulk.tensor.5d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+          " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(d),
+          "l"(m), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]), "r"(c[4]), "r"(bar)
           : "memory");
       break;
   }
@@ -282,6 +348,46 @@ __device__ __forceinline__ void tc_fence_before() {
 
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// TMEM of a CTA pair: allocated, released and freed by the same warp of
+// both CTAs together.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_addr(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// D (+)= A * B on a CTA pair (cta_group::2): M = 256, rows 0-127 of A and the
+// first N/2 columns of B in the issuing (first) CTA's shared memory, the
+// rest at the same offsets in its peer's; each CTA's TMEM holds its 128
+// rows of D.  Issued by one thread of the first CTA.
+__device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` (same offset) in every CTA of `mask` once all previously
+// issued pair MMAs of this thread complete.
+__device__ __forceinline__ void mma_commit_pair(uint64_t *bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_addr(bar)),
+      "h"(mask)
+      : "memory");
 }
 
 // D[tmem] (+)= A[smem desc] * B[smem desc], kind::tf32, one CTA.
