@@ -35,6 +35,23 @@ METRIC = "GPT d384 train tokens/s at 1/2/4/8 B200; GEMM/attn/HBM % roofline"
 VOCAB, SEQ, DMODEL, BLOCKS, HEADS, FFN = 2048, 192, 384, 4, 6, 1536
 WORKLOAD = ("configs[3] GPT train step: vocab 2048, T=192, d=384, 4 pre-RMSNorm blocks, "
             "6 heads, GELU FFN 1536, batch 64 per GPU, AdamW 3e-4 (0.9,0.95) wd 0.1, clip 1.0")
+WORKLOAD5 = ("configs[4] data-parallel GPT train step: vocab 2048, T=1024, d=768, 12 pre-RMSNorm "
+             "blocks, 12 heads, GELU FFN 3072, global batch 256 sequences split over the GPUs, "
+             "micro-batches of 32 sequences accumulated before one clipped AdamW step, NCCL "
+             "gradient all-reduce, AdamW 3e-4 (0.9,0.95) wd 0.1, clip 1.0")
+
+
+def _measured_hbm_gbs():
+    """HBM copy bandwidth of this pool's B200s (MEASURED_PEAKS.json, written
+    by the pool's driver; 6546.2 GB/s when it was measured for this repo)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return 6546.2
+
+
+HBM_PEAK_GBS = _measured_hbm_gbs()
 
 
 def parse_args():
@@ -43,13 +60,18 @@ def parse_args():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
-    p.add_argument("--batch", type=int, default=64, help="sequences per GPU")
+    p.add_argument("--batch", type=int, default=64, help="sequences per GPU (configuration 4)")
+    p.add_argument("--config", type=int, choices=[4, 5], default=4,
+                   help="4: the d384 GPT of configs[3] (the headline); 5: the 12-block d768 "
+                        "T=1024 data-parallel GPT of configs[4]")
     p.add_argument("--no-fusion", action="store_true")
     p.add_argument("--no-graphs", action="store_true")
     p.add_argument("--profile", default="", help="write the per-op profile JSON here")
-    p.add_argument("--kernel", choices=["gemm", "attention", "infer"], default="",
+    p.add_argument("--kernel", choices=["gemm", "attention", "flash", "hbm", "infer"], default="",
                    help="time one kernel case instead of the training step (profiling "
-                        "driver): a tl_gemm shape, or configuration 3's attention")
+                        "driver): a tl_gemm shape, configuration 3's attention (short-"
+                        "sequence fused kernels), the flash kernels at configurations 3 and "
+                        "5, or the step's memory-bound kernels at configuration 4's shapes")
     p.add_argument("--shape", default="12288x384x384:NN",
                    help="--kernel gemm: MxNxK:form[:gelu_grad|:addend|:bias_gelu]")
     return p.parse_args()
@@ -221,6 +243,31 @@ def gemm_roofline(profile_path, peak_tflops, peak_source, timed_ms_per_step=None
                           if a_ms and peak_tflops else None}}, prof
 
 
+def hbm_roofline(prof):
+    """The memory-bound ops of the profiled step (the runtime records each
+    op's algorithmic bytes: operands read once, outputs written once):
+    the one with the most device time, and all of them together, against
+    the measured HBM copy bandwidth.  Times are per-op CUDA events of the
+    profiled step, where events between the ops keep a kernel's launch from
+    overlapping the previous kernel's tail (the timed steps overlap them)."""
+    mem = [o for o in prof if o.get("bytes", 0) > 0 and o["ms"] > 0]
+    if not mem:
+        return None
+    top = max(mem, key=lambda o: o["ms"])
+    gbs = lambda b, ms: b / (ms * 1e-3) / 1e9
+    tb, tms = sum(o["bytes"] for o in mem), sum(o["ms"] for o in mem)
+    return {"bound": "hbm", "kernel": top["op"], "launches_per_step": top["calls"],
+            "achieved": round(gbs(top["bytes"], top["ms"]), 1), "peak": HBM_PEAK_GBS,
+            "unit": "GB/s", "frac": round(gbs(top["bytes"], top["ms"]) / HBM_PEAK_GBS, 4),
+            "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)",
+            "bytes_per_step": top["bytes"], "ms_per_step": round(top["ms"], 4),
+            "traffic": None,
+            "all_memory_bound_ops": {"ms_per_step": round(tms, 4), "bytes_per_step": tb,
+                                     "achieved": round(gbs(tb, tms), 1),
+                                     "frac": round(gbs(tb, tms) / HBM_PEAK_GBS, 4)},
+            "timing": "per-op CUDA events of one profiled step"}
+
+
 def measure_tf32_peak(torch):
     """cuBLAS TF32 dense throughput on this GPU (8192^3, best of 10): the
     denominator for the TF32 GEMM (MEASURED_PEAKS.json holds bf16 only)."""
@@ -259,11 +306,16 @@ def run_kernel_case(args):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     def timed(fn):
+        """Median device time of fn's launches: L2 flushed before each, and
+        a 0.1 ms spin kernel ahead of the start event, so the launches are
+        queued behind it and the events see device time only (not the host's
+        launch latency, which the step's CUDA graphs do not have)."""
         for _ in range(max(3, args.warmup)):
             fn()
         ts = []
         for _ in range(args.steps):
             flush.zero_()
+            torch.cuda._sleep(200_000)
             a, b = torch.cuda.Event(True), torch.cuda.Event(True)
             a.record()
             fn()
@@ -275,6 +327,10 @@ def run_kernel_case(args):
     g = torch.Generator(device=dev).manual_seed(0)
     if args.kernel == "infer":
         return run_inference_case(args)
+    if args.kernel == "hbm":
+        return run_hbm_case(args, lib, dev, stream, timed)
+    if args.kernel == "flash":
+        return run_flash_case(args, lib, dev, stream, timed)
     if args.kernel == "gemm":
         parts = args.shape.split(":")  # MxNxK:form[:gelu_grad|:addend|:bias_gelu]
         dims, form = parts[0], parts[1]
@@ -324,6 +380,148 @@ def run_kernel_case(args):
                 "bwd_us": round(us_b, 2), "fwd_tflops_dense": round(flops / us_f / 1e6, 1),
                 "bwd_tflops_dense": round(2 * flops / us_b / 1e6, 1)}
     print(json.dumps(line))
+    return 0
+
+
+def run_hbm_case(args, lib, dev, stream, timed):
+    """The memory-bound kernels of the configuration-4 step at the step's own
+    shapes (12288 token rows, d 384, FFN 1536, vocab 2048, 8.74 M
+    parameters), L2 flushed before every timed launch.  Algorithmic bytes:
+    every input element read once and every output element written once."""
+    import torch
+    from templit_b200 import capi
+    P = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+    c = lambda rc, what: capi.check(rc, lib, what)
+    g = torch.Generator(device=dev).manual_seed(1)
+    rnd = lambda *shape: torch.randn(*shape, device=dev, generator=g)
+    R, D, F, V = 64 * SEQ, DMODEL, FFN, VOCAB
+    out = []
+
+    def case(name, nbytes, fn):
+        us = timed(fn)
+        gbs = nbytes / us / 1e3
+        out.append({"kernel": name, "us": round(us, 2), "bytes": int(nbytes),
+                    "GB_s": round(gbs, 1), "frac": round(gbs / HBM_PEAK_GBS, 3)})
+
+    x, gr, y, add, o = (rnd(R, D) for _ in range(5))
+    case("rmsnorm_rows [12288,384]", 8 * R * D,
+         lambda: c(lib.tl_rmsnorm_rows(P(x), P(o), P(None), R, D, stream), "rmsnorm"))
+    case("rmsnorm_backward_rows + residual [12288,384]", 20 * R * D,
+         lambda: c(lib.tl_rmsnorm_backward_rows(P(gr), P(x), P(y), P(add), P(o), R, D, stream),
+                   "rmsnorm backward"))
+    sh = capi.shape_arr([R, D])
+    case("binary add [12288,384]", 12 * R * D,
+         lambda: c(lib.tl_binary(capi.TL_ADD, P(x), sh, 2, P(gr), sh, 2, P(o), sh, 2, stream),
+                   "add"))
+    for cols in (D, F, V):
+        xs, os_ = capi.shape_arr([R, cols]), capi.shape_arr([1, cols])
+        src = rnd(R, cols)
+        wsb = lib.tl_reduce_workspace_size(xs, 2, os_, 2)
+        ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
+        dst = torch.empty(cols, device=dev)
+        case(f"reduce (bias gradient) [12288,{cols}]->[{cols}]", 4 * R * cols,
+             lambda src=src, xs=xs, os_=os_, ws=ws, wsb=wsb, dst=dst: c(lib.tl_reduce(
+                 capi.TL_REDUCE_SUM, P(src), xs, 2, P(dst), os_, 2, P(ws), wsb, stream), "reduce"))
+        del src
+    z = rnd(R, V)
+    dz = torch.empty_like(z)
+    tg = torch.randint(0, V, (R,), device=dev, dtype=torch.int32, generator=g)
+    loss = torch.empty(R, device=dev)
+    case("xent_rows [12288,2048]", 4 * R * V,
+         lambda: c(lib.tl_xent_rows(P(z), P(tg), P(loss), R, V, stream), "xent"))
+    case("xent_backward_rows [12288,2048]", 8 * R * V,
+         lambda: c(lib.tl_xent_backward_rows(P(z), P(tg), P(None), P(dz), R, V, stream),
+                   "xent backward"))
+    del z, dz
+    table = rnd(V, D)
+    emb = torch.empty(R, D, device=dev)
+    case("embedding gather [2048,384] x 12288 ids", R * D * 4 + V * D * 4 + R * 4,
+         lambda: c(lib.tl_embedding_gather(P(table), V, D, P(tg), R, P(emb), stream), "gather"))
+    base = rnd(V, D)
+    dst = torch.empty_like(base)
+    swb = lib.tl_embedding_scatter_workspace_size(R, V, D)
+    sws = torch.empty(max(swb, 16), dtype=torch.uint8, device=dev)
+    case("embedding scatter-add 12288 x 384 -> [2048,384]", R * D * 4 + R * 4 + 2 * V * D * 4,
+         lambda: c(lib.tl_embedding_scatter_add(P(emb), P(tg), R, D, P(base), P(dst), V, P(sws),
+                                                swb, stream), "scatter"))
+    # the optimiser pass over nn::GPT<2048,192,384,6>'s 52 parameter tensors
+    sizes = [V * D, SEQ * D]
+    for _ in range(BLOCKS):
+        sizes += [D * D, D] * 4 + [D * F, F, F * D, D]
+    sizes += [D * V, V]
+    n_par = sum(sizes)
+    flat = [rnd(n_par) * 0.02, rnd(n_par) * 0.05, rnd(n_par) * 1e-3, rnd(n_par).abs() * 1e-4]
+    slots = (capi.TlParamSlot * len(sizes))()
+    off = chunk = 0
+    for i, n in enumerate(sizes):
+        sl = slots[i]
+        sl.param = sl.out = flat[0].data_ptr() + 4 * off
+        sl.grad, sl.m1, sl.m2 = (t.data_ptr() + 4 * off for t in flat[1:])
+        sl.count, sl.chunk0, sl.step = n, chunk, 3
+        chunk += (n + capi.TL_OPT_CHUNK - 1) // capi.TL_OPT_CHUNK
+        off += n
+    dslots = torch.frombuffer(bytearray(bytes(slots)), dtype=torch.uint8).to(dev)
+    sq = torch.zeros(1, device=dev)
+    scal = [torch.tensor([v], device=dev) for v in (0.9, 0.95, 1 - 3e-4 * 0.1, 3e-4)]
+    owb = lib.tl_multi_clip_adamw_workspace_size(chunk)
+    ows = torch.empty(max(owb, 16), dtype=torch.uint8, device=dev)
+
+    def adamw():  # sqnorm accumulates over the calls: the clip factor only changes
+        c(lib.tl_multi_clip_adamw(P(dslots), len(sizes), chunk, P(sq), ctypes.c_float(1.0),
+                                  *[P(t) for t in scal], ctypes.c_float(1e-8), P(ows), owb,
+                                  stream), "adamw")
+    case(f"multi-tensor norm + clip + AdamW ({n_par} parameters, 52 tensors)", 32 * n_par, adamw)
+    print(json.dumps({"kernel": "memory-bound kernels of the configuration-4 step",
+                      "peak_GB_s": HBM_PEAK_GBS, "peak_source": "MEASURED_PEAKS.json hbm_gbs",
+                      "l2": "flushed (256 MB written) before every timed launch",
+                      "cases": out}))
+    return 0
+
+
+def run_flash_case(args, lib, dev, stream, timed):
+    """The flash attention kernels (tl_flash_attention_fwd / _bwd, causal
+    mask, divisor 8) at configuration 3 (B 64, H 6, T 192) and at
+    configuration 5's T = 1024 (B 8 and B 32, H 12).  FLOPs are the dense
+    count of the algorithm's products: forward S = QK^T and O = PV (4 B H T^2
+    D); backward dP = dO V^T, dQ = dS K, dK = dS^T Q, dV = P^T dO (8 B H T^2
+    D; the recomputation of S is not counted).  The causal kernels skip the
+    key blocks above the diagonal, so half of those FLOPs are executed."""
+    import torch
+    from templit_b200 import capi
+    out = []
+    for B, H, T in ((64, 6, 192), (8, 12, 1024), (32, 12, 1024)):
+        D = 64
+        g = torch.Generator(device=dev).manual_seed(T)
+        q, k, v, d_o = (torch.randn(B, H, T, D, device=dev, generator=g) for _ in range(4))
+        o, dq, dk, dv = (torch.empty_like(q) for _ in range(4))
+        mask = torch.triu(torch.full((T, T), float("-inf"), device=dev), 1)
+        div = torch.tensor([8.0], device=dev)
+        flag = torch.zeros(4, dtype=torch.int32, device=dev)
+        lse, delta = torch.empty(B, H, T, device=dev), torch.empty(B, H, T, device=dev)
+
+        def view(t):
+            w = capi.TlAttnView()
+            w.p = t.data_ptr()
+            w.batch_stride, w.head_stride, w.row_stride = t.stride()[:3]
+            return w
+        d = capi.TlFlashDesc(B=B, T=T, H=H, D=D)
+        d.q, d.k, d.v, d.o, d.d_o, d.dq, d.dk, d.dv = (view(t) for t in (q, k, v, o, d_o, dq, dk,
+                                                                             dv))
+        d.divisor, d.mask, d.mask_flag = div.data_ptr(), mask.data_ptr(), flag.data_ptr()
+        d.lse, d.delta = lse.data_ptr(), delta.data_ptr()
+        capi.check(lib.tl_attention_mask_check(ctypes.c_void_p(mask.data_ptr()), T,
+                                               ctypes.c_void_p(flag.data_ptr()), stream),
+                   lib, "mask check")
+        fwd = lambda: capi.check(lib.tl_flash_attention_fwd(ctypes.byref(d), stream), lib, "fwd")
+        bwd = lambda: capi.check(lib.tl_flash_attention_bwd(ctypes.byref(d), stream), lib, "bwd")
+        fwd()
+        us_f, us_b = timed(fwd), timed(bwd)
+        dense = 4.0 * B * H * T * T * D
+        out.append({"B": B, "H": H, "T": T, "fwd_us": round(us_f, 2), "bwd_us": round(us_b, 2),
+                    "fwd_tflops_dense": round(dense / us_f / 1e6, 1),
+                    "bwd_tflops_dense": round(2 * dense / us_b / 1e6, 1)})
+        del q, k, v, d_o, o, dq, dk, dv
+    print(json.dumps({"kernel": "tl_flash_attention (causal, D 64)", "cases": out}))
     return 0
 
 
@@ -394,10 +592,18 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     lib = capi.gpt_lib()
-    cfg = capi.TlgConfig(family=4, batch=args.batch, seq=SEQ, seed=1234, init_std=0.02,
+    if args.config == 5:
+        if 256 % world:
+            raise SystemExit("configuration 5 splits 256 sequences: use 1, 2, 4 or 8 GPUs")
+        family, seq, batch = 12, 1024, 32
+        micro = max(1, (256 // world) // batch)
+    else:
+        family, seq, batch, micro = 4, SEQ, args.batch, 1
+    cfg = capi.TlgConfig(family=family, batch=batch, seq=seq, seed=1234, init_std=0.02,
                          lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, clip=1.0,
                          world=world, fusion=0 if args.no_fusion else 1,
-                         graphs=0 if args.no_graphs else 1, deferred_wait=1)
+                         graphs=0 if args.no_graphs else 1, deferred_wait=1,
+                         micro_batches=micro)
     h = ctypes.c_void_p()
     capi.check(lib.tlg_create(ctypes.byref(cfg), ctypes.byref(h)), lib, "tlg_create")
     if world > 1:
@@ -411,7 +617,7 @@ def main():
 
     stream = torch.cuda.ExternalStream(lib.tlg_stream(h))
     rng = np.random.default_rng(1000 + rank)
-    B, T = args.batch, SEQ
+    B, T = batch * micro, seq  # sequences of one rank's step (all micro-batches)
     n_tok = B * T
     pin_x = torch.empty(n_tok, dtype=torch.int32).pin_memory()
     pin_y = torch.empty(n_tok, dtype=torch.int32).pin_memory()
@@ -490,7 +696,7 @@ def main():
     value = total_tokens / (ms_value * 1e-3)
     e2e = total_tokens / (ms_e2e * 1e-3)
 
-    roof = None
+    roof = roof_hbm = None
     prof_path = args.profile or os.path.join(tempfile.gettempdir(),
                                              f"templit_gpt_profile_{os.getpid()}_rank{rank}.json")
     try:
@@ -499,9 +705,10 @@ def main():
         step()
         if rank == 0:
             peak = measure_tf32_peak(torch)
-            roof, _ = gemm_roofline(prof_path, round(peak, 1),
-                                    "cuBLAS TF32 8192^3 measured in this run (burst)",
-                                    ms_value / args.steps)
+            roof, prof = gemm_roofline(prof_path, round(peak, 1),
+                                       "cuBLAS TF32 8192^3 measured in this run (burst)",
+                                       ms_value / args.steps)
+            roof_hbm = hbm_roofline(prof)
     except Exception as exc:  # the bench line still prints
         roof = {"error": str(exc)}
     # GEMM launches by path over the whole run (eager windows and captures;
@@ -524,9 +731,11 @@ def main():
         return 1
     if rank != 0:
         return 0
-    cpu = cpu_baseline_gpt(steps=1, batch=2) if world == 1 else None
+    cpu = cpu_baseline_gpt(steps=1, batch=2) if world == 1 and args.config == 4 else None
     line = {
-        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "metric": METRIC if args.config == 4 else
+                  "GPT d768 12-block T1024 data-parallel train tokens/s (configs[4])",
+        "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": max(3, args.warmup),
         "ms_per_step": round(ms_value / args.steps, 4),
         "ms_per_step_median": round(statistics.median(per_value), 4),
@@ -536,7 +745,10 @@ def main():
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (Zipf(1.1) token windows; e2e draws them with the token pipeline "
                 "from a Zipf(1.1) token file; N(0,0.02) weights, zero biases)",
-        "config": {"workload": WORKLOAD, "model": "nn::GPT<2048,192,384,6> (4 blocks)",
+        "config": {"workload": WORKLOAD if args.config == 4 else WORKLOAD5,
+                   "model": "nn::GPT<2048,192,384,6> (4 blocks)" if args.config == 4 else
+                            "12 nn::DecoderBlock<768,12> (d768, FFN 3072, vocab 2048, T 1024)",
+                   "micro_batches": micro,
                    "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world}",
                    "gemm_operands": "tf32 tensor cores, fp32 accumulate",
                    "l2": "per-step activations (GBs) exceed the 126 MB L2"},
@@ -545,7 +757,7 @@ def main():
                 "ms_per_step_median": round(statistics.median(per_e2e), 4)},
         "gemm_launches_by_path": {"tensor_core": g_tc.value, "cuda_core": g_simt.value},
         "gpu_launches": kernels,
-        "roofline": roof, "cpu_baseline": cpu, "clocks": clocks.summary(),
+        "roofline": roof, "roofline_hbm": roof_hbm, "cpu_baseline": cpu, "clocks": clocks.summary(),
         "loss_first_last": [round(losses[0], 4), round(losses[-1], 4)],
         "runtime": {"windows": int(stats1[0]), "ops_recorded": int(stats1[1]),
                     "ops_launched": int(stats1[2]), "graph_replays": int(stats1[4]),

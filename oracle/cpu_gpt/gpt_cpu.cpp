@@ -10,6 +10,8 @@
 #include "model_utils/archive.h"
 #include "model_utils/loader.h"
 
+#include <dlfcn.h>
+
 #include <fstream>
 
 #include <chrono>
@@ -47,15 +49,45 @@ template <typename F> int guarded(F &&f) {
 
 static_assert(passes::Runnable<Mat, cpu_ref::Runtime>);
 
+extern "C" int tlo_create(const tlg_config *c, void **handle);
+
+namespace {
+
+// Family 12 lives in libgpt_cpu_deep.so beside this library (see
+// gpt_cpu_deep.cpp), opened on the first request.
+templit_b200::DriverBase *deep_driver(const tlg_config *c, cpu_ref::Runtime *rt) {
+  using Fn = templit_b200::DriverBase *(*)(const tlg_config *, cpu_ref::Runtime *, std::string *);
+  static Fn fn = [] {
+    Dl_info info{};
+    if (!dladdr(reinterpret_cast<void *>(&tlo_create), &info) || !info.dli_fname) return Fn{};
+    std::string dir(info.dli_fname);
+    dir = dir.substr(0, dir.find_last_of('/') + 1);
+    void *lib = dlopen((dir + "libgpt_cpu_deep.so").c_str(), RTLD_NOW | RTLD_GLOBAL);
+    return lib ? reinterpret_cast<Fn>(dlsym(lib, "tlo_deep_driver_new")) : Fn{};
+  }();
+  if (!fn) throw std::runtime_error("family 12 needs oracle/_build/libgpt_cpu_deep.so");
+  std::string error;
+  templit_b200::DriverBase *d = fn(c, rt, &error);
+  if (!d) throw std::runtime_error(error);
+  return d;
+}
+
+}  // namespace
+
 extern "C" {
 
 const char *tlo_last_error(void) { return g_error.c_str(); }
 
 int tlo_create(const tlg_config *c, void **handle) {
   return guarded([&] {
-    if (c->family != 4) throw std::invalid_argument("oracle GPT supports family 4");
+    if (c->family != 4 && c->family != 12)
+      throw std::invalid_argument("oracle GPT supports families 4 and 12");
     auto h = std::make_unique<Handle>();
-    h->driver = std::make_unique<templit_b200::GptDriver<Mat, cpu_ref::Runtime, GPT4>>(*c, h->runtime);
+    if (c->family == 12)
+      h->driver.reset(deep_driver(c, &h->runtime));
+    else
+      h->driver =
+          std::make_unique<templit_b200::GptDriver<Mat, cpu_ref::Runtime, GPT4>>(*c, h->runtime);
     *handle = h.release();
   });
 }

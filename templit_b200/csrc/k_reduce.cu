@@ -134,8 +134,22 @@ cols_block_kernel(const float *__restrict__ x, float *out, uint32_t K1, uint32_t
   float4 acc = make_float4(rinit<OP>(), rinit<OP>(), rinit<OP>(), rinit<OP>());
   if (col < K2) {
     const float *base = x + static_cast<size_t>(k1) * R * K2 + col;
-#pragma unroll 4
-    for (uint32_t r = r0 + warp; r < r1; r += 8) {
+    // 16 rows per warp in flight: loads first, then the adds in row order
+    uint32_t r = r0 + warp;
+    for (; r + 15 * 8 < r1; r += 16 * 8) {
+      float4 v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        v[i] = __ldcs(reinterpret_cast<const float4 *>(base + static_cast<size_t>(r + 8 * i) * K2));
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        acc.x = rcomb<OP>(acc.x, v[i].x);
+        acc.y = rcomb<OP>(acc.y, v[i].y);
+        acc.z = rcomb<OP>(acc.z, v[i].z);
+        acc.w = rcomb<OP>(acc.w, v[i].w);
+      }
+    }
+    for (; r < r1; r += 8) {
       const float4 v = *reinterpret_cast<const float4 *>(base + static_cast<size_t>(r) * K2);
       acc.x = rcomb<OP>(acc.x, v.x);
       acc.y = rcomb<OP>(acc.y, v.y);
@@ -175,13 +189,22 @@ cols_block_kernel(const float *__restrict__ x, float *out, uint32_t K1, uint32_t
   float4 a = make_float4(rinit<OP>(), rinit<OP>(), rinit<OP>(), rinit<OP>());
   if (col < K2) {
     const float *src = out + static_cast<size_t>(k1) * K2 + col;
-#pragma unroll 4
-    for (uint32_t sp = warp; sp < gridDim.x; sp += 8) {
-      const float4 v = __ldcg(reinterpret_cast<const float4 *>(src + sp * plane));
-      a.x = rcomb<OP>(a.x, v.x);
-      a.y = rcomb<OP>(a.y, v.y);
-      a.z = rcomb<OP>(a.z, v.z);
-      a.w = rcomb<OP>(a.w, v.w);
+    // up to 16 of the warp's partials loaded at once, then added in order
+    for (uint32_t sp0 = warp; sp0 < gridDim.x; sp0 += 16 * 8) {
+      float4 v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t sp = sp0 + 8 * i;
+        v[i] = sp < gridDim.x ? __ldcg(reinterpret_cast<const float4 *>(src + sp * plane))
+                              : make_float4(rinit<OP>(), rinit<OP>(), rinit<OP>(), rinit<OP>());
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        a.x = rcomb<OP>(a.x, v[i].x);
+        a.y = rcomb<OP>(a.y, v[i].y);
+        a.z = rcomb<OP>(a.z, v[i].z);
+        a.w = rcomb<OP>(a.w, v[i].w);
+      }
     }
   }
   part[warp][lane] = a;

@@ -123,19 +123,48 @@ __device__ __forceinline__ void online_merge(float &m, float &s, float m2,
   m = mn;
 }
 
+// 2^x and 1/x by the SFU (PTX ex2.approx / rcp.approx, subnormals flushed).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // GELU, tanh approximation, with the constants of the reference kernels
-// (include/my_metal/math.metal:821-855).
+// (include/my_metal/math.metal:821-855): 0.5 x (1 + tanh u), u = a (x +
+// b x^3), a = sqrt(2 / 3.14159265), b = 0.044715.  Evaluated through the
+// identity 0.5 (1 + tanh u) = 1 / (1 + e^{-2u}) = s: GELU = x s and
+// GELU' = s + 0.5 x (1 - tanh^2 u) u' = s (1 + 2 a x e s (1 + 3 b x^2)),
+// with e = e^{-2u} = 2^{-2u log2(e)} (so 1 - s = e s exactly, without the
+// cancellation of 1 - s).  The exponent is clamped to +-126: beyond it s is
+// 0 or 1 to float precision.  About 1e-6 relative to the exact formula
+// (the SFU's 2^x and 1/x are within a few ulp; the exponent's rounding
+// grows with |u|).
+constexpr float kGeluA = 0.7978845612587234f;       // sqrt(2 / 3.14159265)
+constexpr float kGeluB = 0.044715f;
+constexpr float kGeluNeg2ALog2e = -2.302208199459653f;  // -2 a log2(e)
+
+__device__ __forceinline__ float gelu_exp_term(float x, float x2) {
+  const float z = kGeluNeg2ALog2e * fmaf(kGeluB * x2, x, x);
+  return ex2_approx(fminf(fmaxf(z, -126.0f), 126.0f));
+}
+
 __device__ __forceinline__ float gelu_f(float x) {
-  const float k = sqrtf(2.0f / 3.14159265f);
-  return 0.5f * x * (1.0f + tanhf(k * (x + 0.044715f * x * x * x)));
+  const float e = gelu_exp_term(x, x * x);
+  return x * rcp_approx(1.0f + e);
 }
 
 __device__ __forceinline__ float gelu_deriv_f(float x) {
-  const float a = 0.7978845608f;
-  const float b = 0.044715f;
   const float x2 = x * x;
-  const float t = tanhf(a * (x + b * x2 * x));
-  return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * a * (1.0f + 3.0f * b * x2);
+  const float e = gelu_exp_term(x, x2);
+  const float s = rcp_approx(1.0f + e);
+  const float q = fmaf(3.0f * kGeluB, x2, 1.0f);
+  return fmaf(s, (2.0f * kGeluA) * x * (e * s) * q, s);
 }
 
 }  // namespace tl

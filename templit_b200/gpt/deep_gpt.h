@@ -13,12 +13,8 @@
 #include "nn/embedding.h"
 #include "nn/layer.h"
 
-#include "my_cuda/runtime.h"
-#include "templit_gpt.h"
-
 #include <array>
 #include <cstdint>
-#include <memory>
 #include <random>
 #include <stdexcept>
 #include <utility>
@@ -78,11 +74,5 @@ public:
     return projection_(expr::rms_norm(apply_blocks<0>(std::move(hidden))));
   }
 };
-
-// The configuration-5 model (vocab 2048, max sequence 1024, d_model 768, 12
-// heads, 12 blocks) on cuda::Runtime, built in its own translation unit
-// (gpt_deep.cpp).
-struct DriverBase;
-std::unique_ptr<DriverBase> make_deep_driver(const tlg_config &c, cuda::Runtime &rt);
 
 }  // namespace templit_b200

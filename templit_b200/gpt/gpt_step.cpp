@@ -2,16 +2,16 @@
 // include/templit_gpt.h.  Family 4 is the reference's own nn::GPT
 // (include/nn/GPT.h: vocab 2048, max sequence 192, d_model 384, 6 heads,
 // 4 blocks - the model of src/train.cpp:23-27,98-99); family 12 the
-// 12-block d_model 768 variant (deep_gpt.h).
+// 12-block d_model 768 variant (deep_gpt.h, in libtemplit_gpt_deep.so).
 #include "templit_gpt.h"
 
-#include "deep_gpt.h"
 #include "gpt_driver.h"
 #include "gpt_infer.h"
 #include "input_pipeline.h"
 #include "my_cuda/runtime.h"
 #include "my_cuda/storage.h"
 
+#include <dlfcn.h>
 #include <nccl.h>
 
 #include <cstring>
@@ -50,12 +50,34 @@ template <typename F> int guarded(F &&f) {
   return 1;
 }
 
+// The 12-block model lives in libtemplit_gpt_deep.so beside this library
+// (its compile takes over an hour, so it is built on its own); opened on
+// the first family-12 request.
+std::unique_ptr<templit_b200::DriverBase> deep_driver(const tlg_config &c, cuda::Runtime &rt) {
+  using Fn = templit_b200::DriverBase *(*)(const tlg_config *, cuda::Runtime *, std::string *);
+  static Fn fn = [] {
+    Dl_info info{};
+    if (!dladdr(reinterpret_cast<void *>(&tlg_create), &info) || !info.dli_fname) return Fn{};
+    std::string dir(info.dli_fname);
+    dir = dir.substr(0, dir.find_last_of('/') + 1);
+    void *lib = dlopen((dir + "libtemplit_gpt_deep.so").c_str(), RTLD_NOW | RTLD_GLOBAL);
+    return lib ? reinterpret_cast<Fn>(dlsym(lib, "tlg_deep_driver_new")) : Fn{};
+  }();
+  if (!fn)
+    throw std::runtime_error("family 12 needs libtemplit_gpt_deep.so (make -C templit_b200 "
+                             "gpt-deep)");
+  std::string error;
+  templit_b200::DriverBase *d = fn(&c, &rt, &error);
+  if (!d) throw std::runtime_error(error);
+  return std::unique_ptr<templit_b200::DriverBase>(d);
+}
+
 std::unique_ptr<templit_b200::DriverBase> make_driver(const tlg_config &c, cuda::Runtime &rt) {
   if (c.family == 4) {
     if (c.seq == 0 || c.seq > 192) throw std::invalid_argument("family 4 takes seq in [1, 192]");
     return std::make_unique<templit_b200::GptDriver<Mat, cuda::Runtime, GPT4>>(c, rt);
   }
-  if (c.family == 12) return templit_b200::make_deep_driver(c, rt);
+  if (c.family == 12) return deep_driver(c, rt);
   throw std::invalid_argument("unsupported GPT family " + std::to_string(c.family));
 }
 

@@ -196,6 +196,7 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashSt
   struct Prof {
     uint64_t calls = 0;
     double ms = 0.0;
+    double bytes = 0.0;  // algorithmic HBM bytes of the memory-bound ops
   };
   std::map<std::string, Prof> profile;
 
@@ -811,6 +812,29 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashSt
     return key;
   }
 
+  // Algorithmic bytes of a memory-bound op: every operand it reads read
+  // once and every output written once (an in-place operand counts twice);
+  // 0 for the tensor-core ops and data movement.
+  static double op_bytes(const Op &op) {
+    switch (op.kind) {
+      case Kind::Gemm: case Kind::Attention: case Kind::FlashFwd: case Kind::FlashBwd:
+      case Kind::FlashProbs: case Kind::AllReduce: case Kind::HostWrite: case Kind::Release:
+        return 0.0;
+      case Kind::MultiAdamW: {
+        double n = 0.0;
+        for (const internal::MultiSlot &m : op.multi) n += static_cast<double>(m.param.numel());
+        // param, grad, m1, m2 read; out, m1, m2 written; + the norm's read
+        return n * 4.0 * (7.0 + (op.t[0].p ? 1.0 : 0.0));
+      }
+      default: {
+        double b = 0.0;
+        for (const TRef &r : op.t)
+          if (r.p) b += static_cast<double>(r.numel()) * 4.0;
+        return b;
+      }
+    }
+  }
+
   void run_profiled(void *s) {
     std::vector<const Op *> ops;
     for (const Op &op : prog)
@@ -830,6 +854,7 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashSt
       Prof &p = profile[profile_key(*ops[i])];
       ++p.calls;
       p.ms += ms;
+      p.bytes += op_bytes(*ops[i]);
     }
     for (void *e : ev) tl_event_destroy(e);
   }
@@ -915,7 +940,8 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashSt
     bool first = true;
     for (const auto &kv : profile) {
       out << (first ? "" : ",\n") << "    {\"op\": \"" << kv.first << "\", \"calls\": "
-          << kv.second.calls << ", \"ms\": " << kv.second.ms << "}";
+          << kv.second.calls << ", \"ms\": " << kv.second.ms
+          << ", \"bytes\": " << static_cast<uint64_t>(kv.second.bytes) << "}";
       first = false;
     }
     out << "\n  ]\n}\n";

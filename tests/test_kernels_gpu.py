@@ -154,6 +154,34 @@ def test_unary_scalar(dev, n):
     close(dev.gelu_backward(x, g), ops.gelu_backward(x, g), rtol=2e-6, atol=2e-6)
 
 
+def test_gelu_accuracy_sweep(dev):
+    """GELU and GELU' (k_elementwise, and through tl_common.cuh every GEMM
+    epilogue) over a dense grid and extreme inputs against the float64
+    formula in its stable form (x / (1 + e^{-2u}): the tanh form cancels
+    for very negative x): GELU within 2e-6 relative (plus 1e-30 absolute:
+    below x = -9.5 the kernels return about 1e-37 where the exact value
+    underflows and the reference's float tanh form gives 0), GELU' within
+    5e-7 absolute plus 2e-6 relative."""
+    x = np.concatenate([np.linspace(-12, 12, (1 << 20) + 1),
+                        [-1e4, -100.0, -30.0, 0.0, 1e-30, -1e-30, 30.0, 100.0, 1e4]])
+    x = x.astype(np.float32)
+    xd = x.astype(np.float64)
+    u = np.sqrt(2 / 3.14159265) * (xd + 0.044715 * xd ** 3)
+    with np.errstate(over="ignore"):
+        e = np.exp(-2 * u)
+    s = 1 / (1 + e)
+    want_g = xd * s
+    with np.errstate(invalid="ignore"):
+        es = np.where(np.isinf(e), 1.0, e * s)
+    want_d = s * (1 + 2 * np.sqrt(2 / 3.14159265) * xd * es * (1 + 3 * 0.044715 * xd ** 2))
+    got_g = dev.unary("gelu", x).astype(np.float64)
+    got_d = dev.unary("gelu_derivative", x).astype(np.float64)
+    assert np.all(np.abs(got_g - want_g) <= 2e-6 * np.abs(want_g) + 1e-30)
+    assert np.all(np.abs(got_d - want_d) <= 5e-7 + 2e-6 * np.abs(want_d))
+    # the float64 oracle (tanh form) on ordinary inputs
+    close(got_g[np.abs(x) < 5], ops.gelu(xd[np.abs(x) < 5]), rtol=2e-6, atol=2e-7)
+
+
 @pytest.mark.parametrize("shape,out", [
     ((12288, 384), (12288, 1)),       # RMS row sums
     ((73728, 192), (73728, 1)),       # softmax-backward row sums
