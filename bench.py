@@ -37,8 +37,8 @@ WORKLOAD = ("configs[3] GPT train step: vocab 2048, T=192, d=384, 4 pre-RMSNorm 
             "6 heads, GELU FFN 1536, batch 64 per GPU, AdamW 3e-4 (0.9,0.95) wd 0.1, clip 1.0")
 WORKLOAD5 = ("configs[4] data-parallel GPT train step: vocab 2048, T=1024, d=768, 12 pre-RMSNorm "
              "blocks, 12 heads, GELU FFN 3072, global batch 256 sequences split over the GPUs, "
-             "micro-batches of 32 sequences accumulated before one clipped AdamW step, NCCL "
-             "gradient all-reduce, AdamW 3e-4 (0.9,0.95) wd 0.1, clip 1.0")
+             "micro-batches (config.micro_batch sequences each) accumulated before one clipped "
+             "AdamW step, NCCL gradient all-reduce, AdamW 3e-4 (0.9,0.95) wd 0.1, clip 1.0")
 
 
 def _measured_hbm_gbs():
@@ -61,6 +61,9 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     p.add_argument("--batch", type=int, default=64, help="sequences per GPU (configuration 4)")
+    p.add_argument("--micro-batch", type=int, default=2,
+                   help="configuration 5: sequences per forward/backward pass; the GPU's 256 / "
+                        "n_gpus sequences of a step run as micro-batches of this size")
     p.add_argument("--config", type=int, choices=[4, 5], default=4,
                    help="4: the d384 GPT of configs[3] (the headline); 5: the 12-block d768 "
                         "T=1024 data-parallel GPT of configs[4]")
@@ -593,10 +596,11 @@ def main():
                                 device_id=torch.device("cuda", local))
     lib = capi.gpt_lib()
     if args.config == 5:
-        if 256 % world:
-            raise SystemExit("configuration 5 splits 256 sequences: use 1, 2, 4 or 8 GPUs")
-        family, seq, batch = 12, 1024, 32
-        micro = max(1, (256 // world) // batch)
+        if 256 % world or (256 // world) % args.micro_batch:
+            raise SystemExit("configuration 5 splits 256 sequences: use 1, 2, 4 or 8 GPUs and a "
+                             "micro-batch that divides 256 / n_gpus")
+        family, seq, batch = 12, 1024, args.micro_batch
+        micro = (256 // world) // batch
     else:
         family, seq, batch, micro = 4, SEQ, args.batch, 1
     cfg = capi.TlgConfig(family=family, batch=batch, seq=seq, seed=1234, init_std=0.02,
@@ -748,7 +752,7 @@ def main():
         "config": {"workload": WORKLOAD if args.config == 4 else WORKLOAD5,
                    "model": "nn::GPT<2048,192,384,6> (4 blocks)" if args.config == 4 else
                             "12 nn::DecoderBlock<768,12> (d768, FFN 3072, vocab 2048, T 1024)",
-                   "micro_batches": micro,
+                   "micro_batches": micro, "micro_batch": batch,
                    "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world}",
                    "gemm_operands": "tf32 tensor cores, fp32 accumulate",
                    "l2": "per-step activations (GBs) exceed the 126 MB L2"},

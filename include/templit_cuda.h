@@ -288,7 +288,10 @@ typedef struct tl_param_slot {
  * in two launches: sqnorm[0] += sum over all slots of grad^2, then for every
  * slot grad = clip(grad), and the AdamW update.  max_norm <= 0 skips the norm
  * and the clip (Compiled::step() without clipping, compile.h:223-234).
- * `slots` is device memory holding n_slots records.
+ * `slots` is device memory holding n_slots records.  The norm's CTAs count
+ * their arrivals in a counter inside the library (the last one adds the
+ * partials): calls of one process must not run concurrently on several
+ * streams.
  */
 int tl_multi_clip_adamw(const tl_param_slot *slots, uint32_t n_slots,
                         uint32_t n_chunks, float *sqnorm, float max_norm,

@@ -8,7 +8,8 @@
 //   m   = b1*m + (1-b1)*g';   v = b2*v + (1-b2)*g'*g'
 //   p'  = p*decay - lr*(m/(1-b1^t)) / (sqrt(v/(1-b2^t)) + eps)
 // The norm here is deterministic: per-CTA partial sums in a workspace,
-// combined in CTA order by a single-CTA pass.
+// combined in CTA order (by a single-CTA pass, or in the multi-tensor
+// kernel by its last CTA).
 #include "tl_common.cuh"
 
 namespace tl {
@@ -135,17 +136,35 @@ __device__ __forceinline__ uint32_t find_slot(const tl_param_slot *slots,
   return lo;
 }
 
+// Arrival counter of multi_sqnorm_kernel's CTAs (self-resetting: the last
+// CTA of a launch wraps it back to 0).
+static __device__ unsigned int g_norm_ticket;
+
+// sqnorm[0] += sum over all slots of grad^2.  CTA b sums the chunks b, b +
+// grid, ... (a full, aligned chunk as 8 float4 loads per thread in flight),
+// writes its partial, and the last CTA to arrive adds the partials in CTA
+// order with a fixed-shape tree: deterministic, one launch.
 __global__ void __launch_bounds__(kNormThreads)
 multi_sqnorm_kernel(const tl_param_slot *__restrict__ slots, uint32_t n_slots,
-                    uint32_t n_chunks, float *partial) {
+                    uint32_t n_chunks, float *partial, float *sqnorm) {
   pdl_enter();
+  __shared__ bool last;
+  constexpr uint32_t kPer = TL_OPT_CHUNK / (kNormThreads * 4);  // float4 per thread
   float acc = 0.0f;
   for (uint32_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
     const tl_param_slot &sl = slots[find_slot(slots, n_slots, c)];
     const uint64_t begin = static_cast<uint64_t>(c - sl.chunk0) * TL_OPT_CHUNK;
     const uint64_t end = min(sl.count, begin + TL_OPT_CHUNK);
     const float *g = sl.grad;
-    if (aligned16(g) && (begin % 4) == 0) {
+    if (aligned16(g) && (begin % 4) == 0 && end - begin == TL_OPT_CHUNK) {
+      float4 v[kPer];
+#pragma unroll
+      for (uint32_t j = 0; j < kPer; ++j)
+        v[j] = *reinterpret_cast<const float4 *>(g + begin + (j * kNormThreads + threadIdx.x) * 4);
+#pragma unroll
+      for (uint32_t j = 0; j < kPer; ++j)
+        acc += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+    } else if (aligned16(g) && (begin % 4) == 0) {
       const uint64_t e4 = begin + ((end - begin) / 4) * 4;
       for (uint64_t i = begin + threadIdx.x * 4; i < e4; i += blockDim.x * 4) {
         const float4 v = *reinterpret_cast<const float4 *>(g + i);
@@ -157,7 +176,18 @@ multi_sqnorm_kernel(const tl_param_slot *__restrict__ slots, uint32_t n_slots,
     }
   }
   const float total = block_sum(acc);
-  if (threadIdx.x == 0) partial[blockIdx.x] = total;
+  if (threadIdx.x == 0) {
+    partial[blockIdx.x] = total;
+    __threadfence();
+    last = atomicInc(&g_norm_ticket, gridDim.x - 1) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  float a = 0.0f;
+  for (uint32_t i = threadIdx.x; i < gridDim.x; i += blockDim.x) a += __ldcg(partial + i);
+  const float all = block_sum(a);
+  if (threadIdx.x == 0) *sqnorm += all;
 }
 
 __global__ void __launch_bounds__(256)
@@ -307,11 +337,9 @@ int tl_multi_clip_adamw(const tl_param_slot *slots, uint32_t n_slots, uint32_t n
     if (!workspace || workspace_bytes < blocks * sizeof(float))
       return fail(TL_ERR_INVALID, "tl_multi_clip_adamw: workspace too small");
     float *partial = static_cast<float *>(workspace);
-    launch_pdl(multi_sqnorm_kernel, blocks, kNormThreads, 0, s, slots, n_slots, n_chunks, partial);
-    int rc = launch_status("tl_multi_clip_adamw norm");
-    if (rc) return rc;
-    launch_pdl(sqnorm_combine_kernel, 1, kNormThreads, 0, s, partial, blocks, sqnorm);
-    rc = launch_status("tl_multi_clip_adamw combine");
+    launch_pdl(multi_sqnorm_kernel, blocks, kNormThreads, 0, s, slots, n_slots, n_chunks, partial,
+               sqnorm);
+    const int rc = launch_status("tl_multi_clip_adamw norm");
     if (rc) return rc;
   }
   launch_pdl(multi_clip_adamw_kernel, blocks, 256, 0, s, slots, n_slots, n_chunks, sqnorm, max_norm,

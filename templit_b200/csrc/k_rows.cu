@@ -314,6 +314,109 @@ xent_backward_kernel(const float *__restrict__ z, const uint32_t *__restrict__ t
   }
 }
 
+// Register-resident cross-entropy (vocab <= 128 * NV, 128-bit rows): the
+// warp loads the whole row of logits at once (NV float4 per lane in
+// flight), then the row maximum, the sum of exp(z - max) and the loss
+// max + log(sum) - z[target] (math.metal:884-911) from registers: one pass
+// over memory instead of a latency-bound online pass.
+template <int NV>
+__device__ __forceinline__ void load_row_regs(const float *zr, uint32_t cols, uint32_t lane,
+                                              float4 (&v)[NV], float &m, float &s) {
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const uint32_t c = (i * 32 + lane) * 4;
+    v[i] = c < cols ? *reinterpret_cast<const float4 *>(zr + c)
+                    : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+  }
+  m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) m = fmaxf(m, fmaxf(fmaxf(v[i].x, v[i].y), fmaxf(v[i].z, v[i].w)));
+  m = warp_max(m);
+  s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const uint32_t c = (i * 32 + lane) * 4;
+    if (c < cols) s += (expf(v[i].x - m) + expf(v[i].y - m)) + (expf(v[i].z - m) + expf(v[i].w - m));
+  }
+  s = warp_sum(s);
+}
+
+// z[target] from the lane holding it (register select, then a shuffle).
+template <int NV>
+__device__ __forceinline__ float target_logit(const float4 (&v)[NV], uint32_t target,
+                                              uint32_t lane) {
+  const uint32_t it = target >> 7, comp = target & 3u;
+  float z = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if (static_cast<uint32_t>(i) == it)
+      z = comp == 0 ? v[i].x : comp == 1 ? v[i].y : comp == 2 ? v[i].z : v[i].w;
+  }
+  (void)lane;
+  return __shfl_sync(0xffffffffu, z, (target >> 2) & 31u);
+}
+
+template <int NV>
+__global__ void __launch_bounds__(256)
+xent_regs_kernel(const float *__restrict__ z, const uint32_t *__restrict__ t, float *loss,
+                 uint32_t rows, uint32_t vocab) {
+  pdl_enter();
+  ROW_LOOP {
+    const uint32_t target = t[row];
+    if (target >= vocab) {
+      if (lane == 0) loss[row] = INFINITY;
+      continue;
+    }
+    float4 v[NV];
+    float m, s;
+    load_row_regs<NV>(z + static_cast<size_t>(row) * vocab, vocab, lane, v, m, s);
+    const float zt = target_logit<NV>(v, target, lane);
+    if (lane == 0) loss[row] = m + logf(s) - zt;
+  }
+}
+
+// dz = (softmax(z) - onehot(target)) (* row_scale): math.metal:912-953 (and
+// the executor's hadamard by the root gradient) from the registers.
+template <int NV>
+__global__ void __launch_bounds__(256, 2)
+xent_backward_regs_kernel(const float *__restrict__ z, const uint32_t *__restrict__ t,
+                          const float *__restrict__ scale, float *dz, uint32_t rows,
+                          uint32_t vocab) {
+  pdl_enter();
+  ROW_LOOP {
+    const uint32_t target = t[row];
+    float *dr = dz + static_cast<size_t>(row) * vocab;
+    if (target >= vocab) {
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const uint32_t c = (i * 32 + lane) * 4;
+        if (c < vocab)
+          *reinterpret_cast<float4 *>(dr + c) = make_float4(INFINITY, INFINITY, INFINITY, INFINITY);
+      }
+      continue;
+    }
+    float4 v[NV];
+    float m, s;
+    load_row_regs<NV>(z + static_cast<size_t>(row) * vocab, vocab, lane, v, m, s);
+    const bool scaled = scale != nullptr;
+    const float k = scaled ? scale[row] : 1.0f;
+    const float inv_s = 1.0f / s;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint32_t c = (i * 32 + lane) * 4;
+      if (c >= vocab) continue;
+      float p[4] = {expf(v[i].x - m) * inv_s, expf(v[i].y - m) * inv_s,
+                    expf(v[i].z - m) * inv_s, expf(v[i].w - m) * inv_s};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (c + j == target) p[j] -= 1.0f;
+        if (scaled) p[j] = k * p[j];
+      }
+      *reinterpret_cast<float4 *>(dr + c) = make_float4(p[0], p[1], p[2], p[3]);
+    }
+  }
+}
+
 // ---- register-resident rows (cols <= 128 * NV, 128-bit rows) ----------
 // One warp per row keeps the whole row in registers (NV float4 per lane,
 // lane l holding columns 4l + 128i): one pass over memory.  The backward
@@ -607,6 +710,15 @@ int regs_for(uint32_t cols) {
     default: LAUNCH(8); break;          \
   }
 
+// float4 registers per lane of the register-resident cross-entropy (0: the
+// online kernels for longer rows)
+int xent_regs_for(uint32_t vocab) {
+  if (vocab <= 512) return 4;
+  if (vocab <= 1024) return 8;
+  if (vocab <= 2048) return 16;
+  return 0;
+}
+
 unsigned row_grid(uint32_t rows) {
   return grid_for(rows, kWarpsPerBlock, 16);
 }
@@ -753,8 +865,19 @@ int tl_xent_rows(const float *logits, const uint32_t *targets, float *loss,
     return fail(TL_ERR_INVALID, "cross_entropy requires logits with a non-empty final dimension");
   if (rows == 0) return TL_OK;
   if (!logits || !targets || !loss) return fail(TL_ERR_INVALID, "tl_xent_rows: null pointer");
-  launch_pdl(xent_kernel, row_grid(rows), 256, 0, as_stream(stream), 
-      logits, targets, loss, rows, vocab, row_vec(vocab, {logits}));
+  const int nv = row_vec(vocab, {logits}) ? xent_regs_for(vocab) : 0;
+  if (nv == 4)
+    launch_pdl(xent_regs_kernel<4>, row_grid(rows), 256, 0, as_stream(stream), logits, targets,
+               loss, rows, vocab);
+  else if (nv == 8)
+    launch_pdl(xent_regs_kernel<8>, row_grid(rows), 256, 0, as_stream(stream), logits, targets,
+               loss, rows, vocab);
+  else if (nv == 16)
+    launch_pdl(xent_regs_kernel<16>, row_grid(rows), 256, 0, as_stream(stream), logits, targets,
+               loss, rows, vocab);
+  else
+    launch_pdl(xent_kernel, row_grid(rows), 256, 0, as_stream(stream),
+               logits, targets, loss, rows, vocab, row_vec(vocab, {logits}));
   return launch_status("tl_xent_rows");
 }
 
@@ -767,8 +890,19 @@ int tl_xent_backward_rows(const float *logits, const uint32_t *targets,
   if (rows == 0) return TL_OK;
   if (!logits || !targets || !dlogits)
     return fail(TL_ERR_INVALID, "tl_xent_backward_rows: null pointer");
-  launch_pdl(xent_backward_kernel, row_grid(rows), 256, 0, as_stream(stream), 
-      logits, targets, row_scale, dlogits, rows, vocab, row_vec(vocab, {logits, dlogits}));
+  const int nv = row_vec(vocab, {logits, dlogits}) ? xent_regs_for(vocab) : 0;
+  if (nv == 4)
+    launch_pdl(xent_backward_regs_kernel<4>, row_grid(rows), 256, 0, as_stream(stream), logits,
+               targets, row_scale, dlogits, rows, vocab);
+  else if (nv == 8)
+    launch_pdl(xent_backward_regs_kernel<8>, row_grid(rows), 256, 0, as_stream(stream), logits,
+               targets, row_scale, dlogits, rows, vocab);
+  else if (nv == 16)
+    launch_pdl(xent_backward_regs_kernel<16>, row_grid(rows), 256, 0, as_stream(stream), logits,
+               targets, row_scale, dlogits, rows, vocab);
+  else
+    launch_pdl(xent_backward_kernel, row_grid(rows), 256, 0, as_stream(stream),
+               logits, targets, row_scale, dlogits, rows, vocab, row_vec(vocab, {logits, dlogits}));
   return launch_status("tl_xent_backward_rows");
 }
 
