@@ -919,7 +919,16 @@ TcPlan plan_tc(const GemmArgs &g) {
   // staging box per chunk, which only tiles up to 128 wide have.  Only
   // unsplit products narrow their tiles: the K slicing, and so the
   // summation order, stays the one the same product has without epilogue.
-  if (p.splits == 1 && (g.addend || g.gelu_grad_x) && !g.gelu_out) {
+  // TL_GEMM_EPI_TILES (tuning): 0 keeps the widest tile for these products
+  // too, 2 also narrows the GELU-output products (two staging boxes per
+  // warp: the pre-activation and the activation stores overlap).
+  static const int epi_tiles = [] {
+    const char *e = std::getenv("TL_GEMM_EPI_TILES");
+    return e ? std::atoi(e) : 1;
+  }();
+  const bool narrow = epi_tiles >= 1 && (g.addend || g.gelu_grad_x) && !g.gelu_out;
+  const bool narrow_gelu = epi_tiles >= 2 && g.gelu_out;
+  if (p.splits == 1 && (narrow || narrow_gelu)) {
     TcPlan q = plan_width(g, 128);
     q.pair = use_pairs(g, q);
     if (q.splits == 1) return q;

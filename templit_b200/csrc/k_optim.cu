@@ -178,12 +178,10 @@ multi_sqnorm_kernel(const tl_param_slot *__restrict__ slots, uint32_t n_slots,
   const float total = block_sum(acc);
   if (threadIdx.x == 0) {
     partial[blockIdx.x] = total;
-    __threadfence();
-    last = atomicInc(&g_norm_ticket, gridDim.x - 1) == gridDim.x - 1;
+    last = ticket_acq_rel(&g_norm_ticket, gridDim.x - 1) == gridDim.x - 1;
   }
   __syncthreads();
   if (!last) return;
-  __threadfence();
   float a = 0.0f;
   for (uint32_t i = threadIdx.x; i < gridDim.x; i += blockDim.x) a += __ldcg(partial + i);
   const float all = block_sum(a);

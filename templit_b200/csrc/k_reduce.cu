@@ -174,15 +174,13 @@ cols_block_kernel(const float *__restrict__ x, float *out, uint32_t K1, uint32_t
   }
   if (!fold_out) return;
   // publish this split's partial, then count arrivals of the column block
-  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
     const unsigned slot = k1 * gridDim.z + blockIdx.z;
-    last = atomicInc(&g_col_tickets[slot], gridDim.x - 1) == gridDim.x - 1;
+    last = ticket_acq_rel(&g_col_tickets[slot], gridDim.x - 1) == gridDim.x - 1;
   }
   __syncthreads();
   if (!last) return;
-  __threadfence();
   // fold the splits: warp w takes splits w, w + 8, ... in order, then the
   // warp results in warp order (the order is fixed: deterministic)
   const size_t plane = static_cast<size_t>(K1) * K2;

@@ -95,6 +95,22 @@ __host__ __device__ inline bool aligned16(const void *p) {
 // instead of faulting.
 uint32_t *device_status_ptr();
 
+// Arrival ticket of a "last CTA folds the partials" reduction: atomicInc
+// (wraps to 0 after `limit`) with acquire-release semantics at GPU scope.
+// Called by one thread after a __syncthreads() that follows the CTA's
+// partial stores, the release covers those stores (release is cumulative);
+// in the CTA that draws the last ticket, a __syncthreads() after the call
+// orders every thread's reads of the partials after the acquire.  No
+// per-thread memory fence is needed on either side.
+__device__ __forceinline__ unsigned ticket_acq_rel(unsigned *p, unsigned limit) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;"
+               : "=r"(old)
+               : "l"(p), "r"(limit)
+               : "memory");
+  return old;
+}
+
 __device__ __forceinline__ void raise_flag(uint32_t *status, uint32_t flag) {
   atomicOr(status, flag);
 }
