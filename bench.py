@@ -61,7 +61,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     p.add_argument("--batch", type=int, default=64, help="sequences per GPU (configuration 4)")
-    p.add_argument("--micro-batch", type=int, default=2,
+    p.add_argument("--micro-batch", type=int, default=4,
                    help="configuration 5: sequences per forward/backward pass; the GPU's 256 / "
                         "n_gpus sequences of a step run as micro-batches of this size")
     p.add_argument("--config", type=int, choices=[4, 5], default=4,
@@ -211,12 +211,20 @@ def gemm_roofline(profile_path, peak_tflops, peak_source, timed_ms_per_step=None
     # for the key-side product
     a_flops = a_ms = 0.0
     a_launches = 0
+    # flash ops: forward 4 B H T^2 D, backward 8 B H T^2 D (the four
+    # products; the recomputed S is not counted), a rebuilt P 2 B H T^2 D
+    flash_mult = {"flash_fwd": 4.0, "flash_bwd": 8.0, "flash_probs": 2.0}
     for o in prof:
-        if not o["op"].startswith("attention#"):
+        name = o["op"].split()[0]
+        if o["op"].startswith("attention#"):
+            code, dims = o["op"][len("attention#"):].split()
+            mult = 2.0 if code == "2" else 4.0
+        elif name in flash_mult:
+            dims, mult = o["op"].split()[1], flash_mult[name]
+        else:
             continue
-        code, dims = o["op"][len("attention#"):].split()
         b, h, t, d = (int(v) for v in dims.split("x"))
-        a_flops += (2.0 if code == "2" else 4.0) * b * h * t * t * d * o["calls"]
+        a_flops += mult * b * h * t * t * d * o["calls"]
         a_ms += o["ms"]
         a_launches += o["calls"]
     share = ms / total_ms if total_ms else 1.0
@@ -237,7 +245,8 @@ def gemm_roofline(profile_path, peak_tflops, peak_source, timed_ms_per_step=None
             "timing": "GEMM share of the profiled step x the timed steps' ms per step",
             "gemm_launches_per_step": launches,
             "gemm_share_of_step": round(ms / total_ms, 3) if total_ms else None,
-            "attention": {"kernel": "attn_fwd / attn_bwd_q / attn_bwd_kv (tcgen05 kind::tf32)",
+            "attention": {"kernel": "attn_fwd / attn_bwd_q / attn_bwd_kv, or the flash kernels "
+                                    "above T = 192 (tcgen05 kind::tf32; dense-count FLOPs)",
                           "flops_per_step": a_flops, "ms_per_step": round(a_ms, 4),
                           "launches_per_step": a_launches,
                           "achieved_tflops": round(a_flops / (a_ms * 1e-3) / 1e12, 1)

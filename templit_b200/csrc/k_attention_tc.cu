@@ -328,6 +328,11 @@ attn_fwd_kernel(const __grid_constant__ FwdMaps maps, const FwdArgs a) {
       if (issued) {
         ptx::mma_commit(bar_o);
         ptx::mbar_wait_bounded(bar_o, 0, kWaitLimitNs);  // before TMEM is released
+        // The last blocks' mma_done arrivals are waited for nowhere else:
+        // an arrival still in flight when the CTA exits would land on the
+        // barrier of the next CTA to take this shared memory.
+        for (uint32_t c = nkb > 2 ? nkb - 2 : 0; ok && c < nkb; ++c)
+          ok = ptx::mbar_wait_bounded(&mma_done[c & 1], (c >> 1) & 1, kWaitLimitNs);
       } else {
         ptx::mbar_arrive(bar_o);
       }
@@ -620,6 +625,12 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
       if (issued) {
         ptx::mma_commit(bar_dq);
         ptx::mbar_wait_bounded(bar_dq, 0, kWaitLimitNs);
+        // The last S blocks' mma_done arrivals are waited for nowhere else:
+        // one still in flight when the CTA exits would land on the barrier
+        // of the next CTA to take this shared memory (seen as dS rows that
+        // changed from run to run in CTAs that started mid-launch).
+        for (uint32_t c = nkb > S ? nkb - S : 0; ok && c < nkb; ++c)
+          ok = ptx::mbar_wait_bounded(&mma_done[(nkb + c) % S], (c / S) & 1, kWaitLimitNs);
       } else {
         ptx::mbar_arrive(bar_dq);
       }
@@ -642,9 +653,9 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
       ptx::tc_fence_after();
       for (uint32_t c = 0; c < nkb; ++c) {
         const uint32_t slot = c % S, piece = 2 * c + half;
+        const bool got = ptx::mbar_wait_bounded(&loaded[slot], (c / S) & 1, kWaitLimitNs);
         uint32_t r[16];
         ptx::tmem_load_32x32b_x16(tmem_dp + lane_base + piece * 16, r);
-        const bool got = ptx::mbar_wait_bounded(&loaded[slot], (c / S) & 1, kWaitLimitNs);
         ptx::tmem_load_wait();
         if (!__all_sync(0xffffffffu, got)) {
           if (lane == 0) timeout();
@@ -669,9 +680,9 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
       sum = red[row] + red[BMQ + row];  // same order in both halves
       for (uint32_t c = 0; c < nkb; ++c) {
         const uint32_t i = nkb + c, slot = i % S, piece = 2 * c + half;
+        const bool got = ptx::mbar_wait_bounded(&loaded[slot], (i / S) & 1, kWaitLimitNs);
         uint32_t r[16];
         ptx::tmem_load_32x32b_x16(tmem_dp + lane_base + piece * 16, r);
-        const bool got = ptx::mbar_wait_bounded(&loaded[slot], (i / S) & 1, kWaitLimitNs);
         ptx::tmem_load_wait();
         if (!__all_sync(0xffffffffu, got)) {
           if (lane == 0) timeout();
@@ -826,7 +837,7 @@ attn_bwd_kv_kernel(const __grid_constant__ BwdKvMaps maps, const BwdKvArgs a) {
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = ptx::idesc_tf32(128, HD, true, true);
-      uint32_t stage = 0, phase = 0;
+      uint32_t stage = 0, phase = 0, committed = 0;
       bool issued = false;
       for (uint32_t qb = 0; qb < a.qblocks && !*abort_flag; ++qb) {
         if (!ptx::mbar_wait_bounded(&full[stage], phase, kWaitLimitNs)) {
@@ -853,6 +864,7 @@ attn_bwd_kv_kernel(const __grid_constant__ BwdKvMaps maps, const BwdKvArgs a) {
                           idesc, acc);
         }
         issued = true;
+        ++committed;
         ptx::mma_commit(&empty[stage]);
         if (++stage == kKvStages) {
           stage = 0;
@@ -862,6 +874,22 @@ attn_bwd_kv_kernel(const __grid_constant__ BwdKvMaps maps, const BwdKvArgs a) {
       if (issued) {
         ptx::mma_commit(done);
         if (!ptx::mbar_wait_bounded(done, 0, kWaitLimitNs)) timeout();
+        // the releases of the last stages (their arrivals must not be in
+        // flight when the CTA exits: they would reach the next CTA's barriers)
+        const uint32_t back = committed < kKvStages ? committed : kKvStages;
+        uint32_t s = stage, p = phase;
+        for (uint32_t i = 0; i < back; ++i) {
+          if (s == 0) {
+            s = kKvStages - 1;
+            p ^= 1;
+          } else {
+            --s;
+          }
+          if (!ptx::mbar_wait_bounded(&empty[s], p, kWaitLimitNs)) {
+            timeout();
+            break;
+          }
+        }
       } else {
         ptx::mbar_arrive(done);  // nothing issued: release the epilogue
       }

@@ -318,6 +318,18 @@ flash_fwd_kernel(const __grid_constant__ Maps maps, const Args a) {
           ptx::mma_commit(drain);
           ptx::mbar_wait_bounded(drain, 0, kWaitLimitNs);
         }
+      } else if (issued) {
+        // the stage releases nobody waits for (the last kFwdStages K and V
+        // stages): their arrivals must have landed before the CTA exits, or
+        // they would reach the barriers of the next CTA in this shared memory
+        ptx::mma_commit(drain);
+        ok = ptx::mbar_wait_bounded(drain, 0, kWaitLimitNs);
+        for (uint32_t j = nkb > kFwdStages ? nkb - kFwdStages : 0; ok && j < nkb; ++j)
+          ok = ptx::mbar_wait_bounded(&kempty[j % kFwdStages], (j / kFwdStages) & 1,
+                                      kWaitLimitNs) &&
+               ptx::mbar_wait_bounded(&vempty[j % kFwdStages], (j / kFwdStages) & 1,
+                                      kWaitLimitNs);
+        if (!ok) timeout();
       }
     }
   } else {
@@ -578,6 +590,16 @@ flash_bwd_q_kernel(const __grid_constant__ Maps maps, const Args a) {
       if (!ok) {
         timeout();
         ptx::mbar_wait_bounded(dqdone, 0, kWaitLimitNs);  // in-flight MMAs finish first
+      } else if (issued) {
+        // releases nobody waits for (the last dS buffers and K/V stages):
+        // landed before the CTA exits, not on the next CTA's barriers
+        ok = ptx::mbar_wait_bounded(dqdone, 0, kWaitLimitNs);
+        for (uint32_t i = nkb > 2 ? nkb - 2 : 0; ok && i < nkb; ++i)
+          ok = ptx::mbar_wait_bounded(&dsfree[i & 1], (i >> 1) & 1, kWaitLimitNs);
+        for (uint32_t i = nkb > kBqStages ? nkb - kBqStages : 0; ok && i < nkb; ++i)
+          ok = ptx::mbar_wait_bounded(&kvempty[i % kBqStages], (i / kBqStages) & 1,
+                                      kWaitLimitNs);
+        if (!ok) timeout();
       }
     }
   } else {
@@ -827,6 +849,16 @@ flash_bwd_kv_kernel(const __grid_constant__ Maps maps, const Args a) {
       if (!ok) {
         timeout();
         ptx::mbar_wait_bounded(done, 0, kWaitLimitNs);
+      } else if (issued && nblk > 0) {
+        // releases nobody waits for (the last Q / dO stages, P^T / dS^T
+        // buffer and MN-major set): landed before the CTA exits, not on the
+        // next CTA's barriers
+        ok = ptx::mbar_wait_bounded(done, 0, kWaitLimitNs) &&
+             ptx::mbar_wait_bounded(pdfree, (nblk - 1) & 1, kWaitLimitNs) &&
+             ptx::mbar_wait_bounded(mnempty, (nblk - 1) & 1, kWaitLimitNs);
+        for (uint32_t t = nblk > kBkStages ? nblk - kBkStages : 0; ok && t < nblk; ++t)
+          ok = ptx::mbar_wait_bounded(&aempty[t % kBkStages], (t / kBkStages) & 1, kWaitLimitNs);
+        if (!ok) timeout();
       }
     }
   } else {

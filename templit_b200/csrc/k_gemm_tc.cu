@@ -339,11 +339,13 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
           }
         }
       }
-      // Drain: every issued k-tile must have landed before the CTA may exit
-      // (a pair's second CTA: its loads count on the first CTA's barriers,
-      // which that CTA drains; the pair meets at a cluster barrier at exit).
-      uint64_t back = issued < static_cast<uint64_t>(C::STAGES) ? issued : C::STAGES;
-      if (PAIR && rank != 0) back = 0;
+      // Drain: every issued k-tile must have landed (full; a pair's second
+      // CTA: its loads count on the first CTA's barriers, which that CTA
+      // drains) and, unless aborting, been released by the MMAs (empty: the
+      // commit's arrival must not be in flight when the CTA exits, or it
+      // would land on the barrier of the next CTA to take this shared
+      // memory; a pair's commits reach both CTAs).
+      const uint64_t back = issued < static_cast<uint64_t>(C::STAGES) ? issued : C::STAGES;
       uint32_t s = stage, p = phase;
       for (uint64_t i = 0; i < back; ++i) {
         if (s == 0) {
@@ -352,7 +354,11 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
         } else {
           --s;
         }
-        if (!ptx::mbar_wait_bounded(&full[s], p, kWaitLimitNs)) {
+        if ((!PAIR || rank == 0) && !ptx::mbar_wait_bounded(&full[s], p, kWaitLimitNs)) {
+          timeout();
+          break;
+        }
+        if (!*abort_flag && !ptx::mbar_wait_bounded(&empty[s], p, kWaitLimitNs)) {
           timeout();
           break;
         }
@@ -587,8 +593,6 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
         for (int c = c0; c < BN / 32; c += 2) {
           const uint32_t n0 = n_base + c * 32;
           if (n0 >= g.n) break;  // warp-uniform
-          uint32_t r[32];
-          ptx::tmem_load_32x32b_x32(tmem_base + acc * C::ACC_COLS + c * 32 + ((q * 32u) << 16), r);
           uint8_t *box;
           if (early_aux) {
             box = obuf + ((c - c0) >> 1) * 4096;  // loaded before the tile began
@@ -612,6 +616,8 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
               failed = true;
             }
           }
+          uint32_t r[32];
+          ptx::tmem_load_32x32b_x32(tmem_base + acc * C::ACC_COLS + c * 32 + ((q * 32u) << 16), r);
           ptx::tmem_load_wait();
           if (failed) break;
           float4 v[8];

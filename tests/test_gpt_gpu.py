@@ -86,6 +86,15 @@ class CudaGPT:
         return dict(zip(["windows", "recorded", "launched", "kernels", "replays", "captures",
                          "fused", "peak_bytes", "record_ns", "submit_ns", "plan_hits"], list(s)))
 
+    def profile_ops(self, tmp_path):
+        """Names of the ops of the next train step (per-op profile)."""
+        import json
+        path = str(tmp_path / "profile.json")
+        capi.check(self.lib.tlg_profile(self.h, path.encode(), 1), self.lib, "profile")
+        self.train_step()
+        with open(path) as f:
+            return [o["op"] for o in json.load(f)["ops"]]
+
     def save(self, path, optimiser=True):
         capi.check(self.lib.tlg_save(self.h, str(path).encode(), int(optimiser)), self.lib, "save")
 
