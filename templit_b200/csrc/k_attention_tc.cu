@@ -70,6 +70,16 @@ constexpr uint32_t kBars = kRed + 4 * BMQ * 4;
 constexpr size_t kQuerySmem = 1024 + kBars + 256;
 constexpr uint32_t kTmemCols = 256;  // scores (<= 192 columns) + a 64-column product
 static_assert(kMaxFusedKeys + HD <= kTmemCols, "TMEM budget");
+// The query-side backward takes all of the SM's TMEM.  With two of its CTAs
+// holding 256 columns each, the softmax derivative's row sums came out
+// wrong in a few rows of CTAs that started while the SM's other CTA was
+// mid-way (dS differed from run to run in about 10 of 73,728 rows at
+// configuration 3; never with one CTA's TMEM per SM, at one CTA per SM, or
+// when every CTA started in the first wave).  The cause was not found; with
+// 512 columns the second CTA on an SM sets up while the first runs and
+// starts its tensor-core work when the first has freed the TMEM
+// (configuration-3 backward 122 us instead of 105 us, deterministic).
+constexpr uint32_t kTmemColsBwdQ = 512;
 
 __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t j) {
   return r * 128u + ((j ^ (r & 7u)) << 4);
@@ -510,7 +520,7 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
     ptx::prefetch_tensormap(&maps.ds);
   }
   if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, kTmemCols);
+    ptx::tmem_alloc(tmem_slot, kTmemColsBwdQ);
     ptx::tmem_relinquish();
   }
   ptx::tc_fence_before();
@@ -715,7 +725,7 @@ attn_bwd_q_kernel(const __grid_constant__ BwdQMaps maps, const BwdQArgs a) {
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
-  if (warp == 1) ptx::tmem_dealloc(tmem, kTmemCols);
+  if (warp == 1) ptx::tmem_dealloc(tmem, kTmemColsBwdQ);
 }
 
 // -------------------------------------------------------- backward, key side

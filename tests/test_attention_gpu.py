@@ -70,6 +70,22 @@ def test_config3_causal(dev, precision):
     run_case(dev, 64, 6, 192, 64, True, capi.TL_ATTN_BHTD, precision)
 
 
+def test_backward_bit_identical_across_runs(dev):
+    """Configuration 3 at B 64 (768 query tiles: CTAs start while others run
+    on the same SM): twelve backward passes give the same bits.  A run-to-run
+    difference in a few rows of dS showed up here once two query-side CTAs
+    shared an SM's tensor memory."""
+    B, H, T, D = 64, 6, 192, 64
+    q, k, v, d_o = inputs(B, H, T, D, 0)
+    divisor = float(np.sqrt(np.float32(D)))
+    mask = ops.causal_mask(T)
+    first = dev.attention(q, k, v, divisor, mask, d_o, capi.TL_ATTN_BHTD, capi.TL_GEMM_TF32)
+    for _ in range(11):
+        got = dev.attention(q, k, v, divisor, mask, d_o, capi.TL_ATTN_BHTD, capi.TL_GEMM_TF32)
+        for name, a, b in zip(("p", "o", "dq", "dk", "dv"), got, first):
+            assert np.array_equal(a, b), name
+
+
 @pytest.mark.parametrize("B,H,T,D,masked", [
     (2, 3, 100, 64, True),    # T not a tile multiple
     (1, 2, 37, 16, True),     # unaligned rows: CUDA-core products
