@@ -69,12 +69,12 @@ struct OpMap {
 };
 
 // Tensor maps of one launch: per group the A, B and C maps (N groups share
-// A; K groups share C), plus the addend / GELU-backward input (C's layout).
-// The GELU output leaves by plain stores.
+// A; K groups share C), plus GELU output and addend (C's layout).
 struct TcMaps {
   CUtensorMap a[TL_GEMM_MAX_GROUPS];
   CUtensorMap b[TL_GEMM_MAX_GROUPS];
   CUtensorMap c[TL_GEMM_MAX_GROUPS];
+  CUtensorMap gelu;
   CUtensorMap addend;
 };
 
@@ -659,26 +659,24 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
             ptx::bulk_commit_group();
           }
           if (with_gelu) {
-            // the activations leave straight from registers (a thread's 32
-            // values are 128 contiguous bytes of its row) while the store
-            // above reads the box: no second box, no wait for it
+            // the activations are computed while the store above reads
+            // the box (the only one of a 256-wide tile's warp)
 #pragma unroll
             for (int j = 0; j < 8; ++j)
               v[j] = make_float4(gelu_f(v[j].x), gelu_f(v[j].y), gelu_f(v[j].z), gelu_f(v[j].w));
-            if (row_ok) {
-              float *gr = g.gelu_out + oc + static_cast<size_t>(m) * g.ldc + n0;
-              if (n0 + 32 <= g.n) {
+            uint8_t *gbox = obuf + (C::BOXES == 2 ? (nbuf++ & 1u) * 4096 : 0);
+            if (lane == 0) {
+              if constexpr (C::BOXES == 2) ptx::bulk_wait_group_read<1>();
+              else ptx::bulk_wait_group_read<0>();
+            }
+            __syncwarp();
 #pragma unroll
-                for (int j = 0; j < 8; ++j) reinterpret_cast<float4 *>(gr)[j] = v[j];
-              } else {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  const float e4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-                  for (int e = 0; e < 4; ++e)
-                    if (n0 + 4 * j + e < g.n) gr[4 * j + e] = e4[e];
-                }
-              }
+            for (int j = 0; j < 8; ++j) *reinterpret_cast<float4 *>(gbox + swz(lane, j)) = v[j];
+            ptx::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              ptx::tma_store_nd(&maps.gelu, gbox, static_cast<int32_t>(n0), y0, ncz, zc);
+              ptx::bulk_commit_group();
             }
           }
         }
@@ -995,12 +993,13 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
     bool strides_ok = g.ldc % 4 == 0;
     for (uint32_t d = 0; d < g.batch_rank; ++d) strides_ok = strides_ok && g.sc[d] % 4 == 0;
     const float *aux = g.addend ? g.addend : g.gelu_grad_x;  // one epilogue input box
-    OpMap od{};
+    OpMap og{}, od{};
     t.tma_epi = g.n % 4 == 0 && strides_ok && aligned16(g.c) &&
                 (!g.bias || aligned16(g.bias)) && (!g.gelu_out || aligned16(g.gelu_out)) &&
                 (!g.addend || aligned16(g.addend)) &&
                 (!g.gelu_grad_x || aligned16(g.gelu_grad_x)) &&
-
+                (!g.gelu_out || make_operand_map(&maps.gelu, g.gelu_out, g.n, g.m, g.ldc, g,
+                                                 g.sc, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, og)) &&
                 (!aux || make_operand_map(&maps.addend, aux, g.n, g.m, g.ldc, g, g.sc, 32, 32,
                                           CU_TENSOR_MAP_SWIZZLE_128B, od));
     for (uint32_t i = 0; i < ngroups && t.tma_epi; ++i) {
