@@ -457,6 +457,10 @@ typedef struct tl_attn_desc {
    * key blocks */
   void *workspace;
   uint64_t workspace_bytes;
+  /* optional: a word tl_attention_mask_check has already set for `mask`;
+   * the forward then reads it and runs no check of its own (a program
+   * checks its mask once, not once per layer) */
+  const uint32_t *mask_flag;
 } tl_attn_desc;
 /* 1 when the fused kernels take this descriptor, 0 when not (no launch). */
 int tl_attention_fused_supported(const tl_attn_desc *d);

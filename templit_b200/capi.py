@@ -69,7 +69,8 @@ class TlAttnDesc(Structure):
                 ("D", c_uint32), ("q", TlAttnView), ("k", TlAttnView), ("v", TlAttnView),
                 ("o", TlAttnView), ("d_o", TlAttnView), ("dq", TlAttnView), ("dk", TlAttnView),
                 ("divisor", c_void_p), ("mask", c_void_p), ("p", c_void_p), ("ds", c_void_p),
-                ("workspace", c_void_p), ("workspace_bytes", c_uint64)]
+                ("workspace", c_void_p), ("workspace_bytes", c_uint64),
+                ("mask_flag", c_void_p)]
 
 
 class TlFlashDesc(Structure):

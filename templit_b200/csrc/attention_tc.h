@@ -33,7 +33,8 @@ bool fused_attention_fits(const AttnDims &d, const HeadView *views, const bool *
 // causal one, which the kernel then applies arithmetically.
 int launch_attention_fwd_tc(const AttnDims &d, const HeadView &q, const HeadView &k,
                             const HeadView &v, const float *divisor, const float *mask, float *p,
-                            const HeadView &o, uint32_t *mask_flag, cudaStream_t s);
+                            const HeadView &o, uint32_t *mask_flag, cudaStream_t s,
+                            bool mask_checked = false);
 // dS = P * (dP - rowsum(dP * P)) / divisor with dP = dO V^T (written to ds,
 // dense [B, H, T, T]); dQ = dS K.
 int launch_attention_bwd_q_tc(const AttnDims &d, const HeadView &d_o, const HeadView &v,

@@ -227,11 +227,13 @@ int tl_attention_fused(const tl_attn_desc *d, void *stream) {
   cudaStream_t s = as_stream(stream);
   switch (d->pass) {
     case TL_ATTN_FORWARD: {
-      uint32_t *flag = d->workspace && d->workspace_bytes >= 16 && tl::aligned16(d->workspace)
+      // a flag the caller has checked already, else the workspace's word
+      uint32_t *flag = d->mask_flag ? const_cast<uint32_t *>(d->mask_flag)
+                       : d->workspace && d->workspace_bytes >= 16 && tl::aligned16(d->workspace)
                            ? static_cast<uint32_t *>(d->workspace)
                            : nullptr;
       return tl::launch_attention_fwd_tc(dims, hv(d->q), hv(d->k), hv(d->v), d->divisor, d->mask,
-                                         d->p, hv(d->o), flag, s);
+                                         d->p, hv(d->o), flag, s, d->mask_flag != nullptr);
     }
     case TL_ATTN_BACKWARD_Q:
       return tl::launch_attention_bwd_q_tc(dims, hv(d->d_o), hv(d->v), hv(d->k), d->p,

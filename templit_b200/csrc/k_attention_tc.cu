@@ -1005,7 +1005,8 @@ bool fused_attention_fits(const AttnDims &d, const HeadView *views, const bool *
 
 int launch_attention_fwd_tc(const AttnDims &d, const HeadView &q, const HeadView &k,
                             const HeadView &v, const float *divisor, const float *mask, float *p,
-                            const HeadView &o, uint32_t *mask_flag, cudaStream_t s) {
+                            const HeadView &o, uint32_t *mask_flag, cudaStream_t s,
+                            bool mask_checked) {
   FwdMaps maps{};
   FwdArgs a{};
   if (mask && !aligned16(mask))  // rows of the mask are read as float4
@@ -1032,7 +1033,7 @@ int launch_attention_fwd_tc(const AttnDims &d, const HeadView &q, const HeadView
   int rc = kt ? set_smem(attn_fwd_kernel<true>, kQuerySmem, attr[1], "attention forward: smem")
               : set_smem(attn_fwd_kernel<false>, kQuerySmem, attr[0], "attention forward: smem");
   if (rc) return rc;
-  if (a.mask_flag) {
+  if (a.mask_flag && !mask_checked) {
     launch_pdl(mask_causal_kernel, 1, 1024, 0, s, mask, d.T, mask_flag);
     rc = launch_status("attention forward (mask check)");
     if (rc) return rc;

@@ -105,7 +105,10 @@ struct TcArgs {
 // PAIR: a CTA pair (cluster of 2) computes a 256 x BN tile with cta_group::2
 // products; each CTA loads its 128 rows of A and BN / 2 columns of B and
 // holds its 128 rows of the accumulator.
-template <int BN, bool SPLIT, bool PAIR = false>
+// EPI2: two staging boxes per epilogue warp even for 256-wide tiles (one
+// fewer pipeline stage), for the GELU-output products, whose chunks leave
+// by two stores.
+template <int BN, bool SPLIT, bool PAIR = false, bool EPI2 = false>
 struct Cfg {
   static_assert(!(SPLIT && PAIR), "3xTF32 runs on single CTAs");
   static constexpr int THREADS = 64 + 32 * kEpiWarps + (SPLIT ? 32 * kConvWarps : 0);
@@ -119,7 +122,7 @@ struct Cfg {
   // staging boxes for the TMA stores: per epilogue warp two 32 x 32 fp32
   // boxes (4 KB each, 128-byte swizzled rows), one for the widest tile and
   // for 3xTF32 (whose stages are twice as large)
-  static constexpr int BOXES = (BN == 256 || SPLIT) ? 1 : 2;
+  static constexpr int BOXES = ((BN == 256 && !EPI2) || SPLIT) ? 1 : 2;
   static constexpr uint32_t OUT_BYTES = kEpiWarps * BOXES * 4096;
   static constexpr uint32_t BAR_BYTES = 384;
   static constexpr int STAGES_FIT =
@@ -179,10 +182,10 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t j) {
   return r * 128u + ((j ^ (r & 7u)) << 4);
 }
 
-template <int BN, bool A_MN, bool B_MN, bool SPLIT, bool PAIR>
-__global__ void __launch_bounds__(Cfg<BN, SPLIT, PAIR>::THREADS, 1)
+template <int BN, bool A_MN, bool B_MN, bool SPLIT, bool PAIR, bool EPI2 = false>
+__global__ void __launch_bounds__(Cfg<BN, SPLIT, PAIR, EPI2>::THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
-  using C = Cfg<BN, SPLIT, PAIR>;
+  using C = Cfg<BN, SPLIT, PAIR, EPI2>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -942,9 +945,9 @@ TcPlan plan_tc(const GemmArgs &g) {
   return p;
 }
 
-template <int BN, bool A_MN, bool B_MN, bool SPLIT, bool PAIR>
+template <int BN, bool A_MN, bool B_MN, bool SPLIT, bool PAIR, bool EPI2 = false>
 int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaStream_t s) {
-  using C = Cfg<BN, SPLIT, PAIR>;
+  using C = Cfg<BN, SPLIT, PAIR, EPI2>;
   TcArgs t{};
   t.g = g;
   t.mt = (g.m + C::BMT - 1) / C::BMT;
@@ -1019,7 +1022,7 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
     return fail(TL_ERR_UNSUPPORTED, "tl_gemm: grouped outputs need 16-byte rows");
   static bool attr_set = false;
   if (!attr_set) {
-    int rc = check_cuda(cudaFuncSetAttribute(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT, PAIR>,
+    int rc = check_cuda(cudaFuncSetAttribute(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT, PAIR, EPI2>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(C::SMEM)),
                         "tl_gemm smem attribute");
@@ -1029,11 +1032,11 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
   if constexpr (PAIR) {
     const uint64_t pairs = kNumSMs / 2;
     const uint64_t grid = 2 * (t.num_tiles < pairs ? t.num_tiles : pairs);
-    launch_pdl_cluster(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT, PAIR>, static_cast<unsigned>(grid),
+    launch_pdl_cluster(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT, PAIR, EPI2>, static_cast<unsigned>(grid),
                        C::THREADS, C::SMEM, s, 2u, maps, t);
   } else {
     const uint64_t grid = t.num_tiles < static_cast<uint64_t>(kNumSMs) ? t.num_tiles : kNumSMs;
-    launch_pdl(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT, PAIR>, static_cast<unsigned>(grid),
+    launch_pdl(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT, PAIR, EPI2>, static_cast<unsigned>(grid),
                C::THREADS, C::SMEM, s, maps, t);
   }
   int rc = launch_status("tl_gemm tf32");
@@ -1098,6 +1101,14 @@ int launch_tc_gemm(const GemmArgs &g, void *workspace, size_t workspace_bytes, c
   if (plan.pair)
     return plan.bn == 256 ? launch_bn<256, false, true>(g, plan, partial, s)
                           : launch_bn<128, false, true>(g, plan, partial, s);
+  // the FFN's first product (NN, unsplit, GELU output): two boxes per warp
+  // (TL_GEMM_EPI2=0 keeps the one-box tile)
+  static const bool epi2 = [] {
+    const char *e = std::getenv("TL_GEMM_EPI2");
+    return !(e && std::strcmp(e, "0") == 0);
+  }();
+  if (plan.bn == 256 && epi2 && g.gelu_out && !g.trans_a && !g.trans_b && !partial)
+    return launch_variant<256, false, true, false, false, true>(g, plan, partial, s);
   if (plan.bn == 256) return launch_bn<256>(g, plan, partial, s);
   if (plan.bn == 192) return launch_bn<192>(g, plan, partial, s);
   if (plan.bn == 128) return launch_bn<128>(g, plan, partial, s);

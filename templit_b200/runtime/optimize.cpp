@@ -916,6 +916,11 @@ bool score_dims(const TRef &t, uint32_t &B, uint32_t &H, uint32_t &T) {
 //             key-side kernel in place of the product
 // Each only when the fused kernels take the operands' strides and the
 // values read at the fused op's position are those the originals read.
+// The runtime's flash-attention state (records of virtual P tensors, LSE
+// buffers, per-mask causal words) for the program being optimised; null
+// when the caller keeps none.
+thread_local FlashState *g_flash = nullptr;
+
 uint64_t fuse_attention(std::vector<Op> &p) {
   uint64_t folded = 0;
   for (size_t k = 0; k < p.size(); ++k) {
@@ -958,11 +963,14 @@ uint64_t fuse_attention(std::vector<Op> &p) {
           !unchanged_between(p, k, j, div.id) || (mask.p && !unchanged_between(p, k, j, mask.id)) ||
           !untouched_between(p, k, j, Y.id) || tl_attention_fused_supported(&d) != 1)
         continue;
+      // the causal check of the mask: one runtime word per mask, checked
+      // once per program (assign_mask_checks)
+      if (mask.p && g_flash) d.mask_flag = g_flash->mask_word(mask.id);
       Op fused{};
       fused.kind = Kind::Attention;
       fused.code = TL_ATTN_FORWARD;
       fused.attn = d;
-      fused.workspace = 256;  // the causal-mask word
+      fused.workspace = 256;  // the causal-mask word when the runtime keeps none
       fused.t[0] = Q;
       fused.t[1] = K;
       fused.t[2] = p[j].t[1];
@@ -1077,7 +1085,6 @@ uint64_t fuse_attention(std::vector<Op> &p) {
 // resolve_flash then rebuilds a virtual P (FlashProbs) in front of any other
 // reader, and before any write or release of its recipe's inputs.
 
-thread_local FlashState *g_flash = nullptr;
 
 bool no_reuse_between(const std::vector<Op> &p, size_t i, size_t j, const TRef &dst);
 
@@ -1095,7 +1102,6 @@ const FlashRecord *flash_record(uint64_t p_id) {
 
 uint64_t fuse_flash_forward(std::vector<Op> &p) {
   uint64_t folded = 0;
-  std::unordered_set<uint64_t> checked_masks;  // one causal check per mask per program
   for (size_t k = 0; k < p.size(); ++k) {
     Op &sm = p[k];
     if (sm.dead || sm.kind != Kind::Softmax || !sm.t[2].p) continue;
@@ -1139,7 +1145,7 @@ uint64_t fuse_flash_forward(std::vector<Op> &p) {
     if (tl_flash_attention_supported(&d) != 1 || !d.lse || (mask.p && !d.mask_flag)) continue;
     Op fused{};
     fused.kind = Kind::FlashFwd;
-    fused.code = mask.p && checked_masks.insert(mask.id).second ? 1 : 0;  // 1: check the mask
+    fused.code = 0;  // bit 0, check the mask first: assign_mask_checks
     fused.flash = d;
     fused.t[0] = Q;
     fused.t[1] = K;
@@ -2030,6 +2036,30 @@ void add_gradient_allreduce(std::vector<Op> &prog) {
   prog.insert(prog.begin() + static_cast<std::ptrdiff_t>(first), std::move(ar));
 }
 
+// One causal-mask check per mask per program: the first attention forward
+// (fused or flash) that reads a mask through a runtime word checks it
+// (Attention: u0 bit 0; FlashFwd: code bit 0), later ones read the word,
+// until an op writes the mask.
+void assign_mask_checks(std::vector<Op> &p) {
+  std::unordered_set<uint64_t> checked;
+  for (Op &op : p) {
+    if (op.dead) continue;
+    const bool fused = op.kind == Kind::Attention && op.code == TL_ATTN_FORWARD &&
+                       op.attn.mask_flag != nullptr;
+    const bool flash = op.kind == Kind::FlashFwd && op.flash.mask_flag != nullptr;
+    if (fused || flash) {
+      const bool first = checked.insert(op.t[4].id).second;
+      if (fused) op.u0 = first ? 1u : 0u;
+      else op.code = first ? 1 : 0;
+      continue;
+    }
+    if (checked.empty()) continue;
+    const Access a = access(op);
+    for (int w = 0; w < a.nw; ++w) checked.erase(a.w[w]);
+    if (op.kind == Kind::Release && op.t[0].p) checked.erase(op.t[0].id);
+  }
+}
+
 uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live, FlashState *flash) {
   g_live = live;
   g_flash = flash && flash->enabled() ? flash : nullptr;
@@ -2069,6 +2099,7 @@ uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live, Flash
   folded += fuse_step(prog);
   if (comm) add_gradient_allreduce(prog);
   if (g_flash) resolve_flash(prog);
+  assign_mask_checks(prog);
   g_live = nullptr;
   g_flash = nullptr;
   return folded;

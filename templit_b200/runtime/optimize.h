@@ -82,6 +82,11 @@ void update_flash_records(const std::vector<Op> &prog, std::vector<FlashRecord> 
 uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live = nullptr,
                   FlashState *flash = nullptr);
 
+// Marks the first attention forward (fused: u0 bit 0; flash: code bit 0)
+// that reads each runtime-checked mask in a program, and the first after
+// any write to the mask, as the one that runs the causal-mask check.
+void assign_mask_checks(std::vector<Op> &prog);
+
 // Inserts one AllReduce op ahead of the first optimiser op of a program
 // that updates parameters, covering every gradient that op sequence reads.
 void add_gradient_allreduce(std::vector<Op> &prog);

@@ -695,6 +695,9 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashSt
         tl_attn_desc d = op.attn;
         d.workspace = ws;
         d.workspace_bytes = wsb;
+        if (d.pass == TL_ATTN_FORWARD && d.mask_flag && (op.u0 & 1))
+          check(tl_attention_mask_check(d.mask, d.T, const_cast<uint32_t *>(d.mask_flag), s),
+                "attention mask check");
         check(tl_attention_fused(&d, s), "attention");
         break;
       }

@@ -695,6 +695,29 @@ void gelu_backward_into_gemm() {
 
 }  // namespace
 
+// One causal check per mask per program, again after the mask is written.
+void mask_checked_once_per_program() {
+  const TRef q = tensor({64, 6, 192, 64}), mask = tensor({192, 192}), o = tensor({64, 6, 192, 64});
+  uint32_t word = 0;
+  auto fwd = [&]() {
+    Op a = op(Kind::Attention);
+    a.code = TL_ATTN_FORWARD;
+    a.attn.pass = TL_ATTN_FORWARD;
+    a.attn.mask_flag = &word;
+    a.t[0] = q;
+    a.t[4] = mask;
+    a.t[6] = o;
+    return a;
+  };
+  Op fill = op(Kind::Fill);
+  fill.t[0] = mask;
+  fill.n = mask.numel();
+  std::vector<Op> p = {fwd(), fwd(), fill, fwd(), fwd()};
+  assign_mask_checks(p);
+  require(p[0].u0 == 1 && p[1].u0 == 0, "first forward checks, the second reads the word");
+  require(p[3].u0 == 1 && p[4].u0 == 0, "a write to the mask calls for a new check");
+}
+
 int main() {
   int failures = 0;
   const std::vector<std::pair<const char *, void (*)()>> cases = {
@@ -724,6 +747,7 @@ int main() {
       {"attention_forward_fused", attention_forward_fused},
       {"attention_backward_fused", attention_backward_fused},
       {"gelu_backward_into_gemm", gelu_backward_into_gemm},
+      {"mask_checked_once_per_program", mask_checked_once_per_program},
   };
   for (const auto &[name, fn] : cases) {
     try {
