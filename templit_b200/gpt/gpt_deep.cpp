@@ -6,6 +6,7 @@
 // a while, and the four-block library should not wait for them.
 #include "deep_gpt.h"
 #include "gpt_driver.h"
+#include "my_cuda/runtime.h"
 #include "my_cuda/storage.h"
 
 #include <stdexcept>
