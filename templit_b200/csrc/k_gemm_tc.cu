@@ -1101,11 +1101,12 @@ int launch_tc_gemm(const GemmArgs &g, void *workspace, size_t workspace_bytes, c
   if (plan.pair)
     return plan.bn == 256 ? launch_bn<256, false, true>(g, plan, partial, s)
                           : launch_bn<128, false, true>(g, plan, partial, s);
-  // the FFN's first product (NN, unsplit, GELU output): two boxes per warp
-  // (TL_GEMM_EPI2=0 keeps the one-box tile)
+  // the FFN's first product (NN, unsplit, GELU output) with two boxes per
+  // warp: opt-in (TL_GEMM_EPI2=1), measured no faster than one box (63.5 us
+  // both at 12288 x 1536 x 384, 96.2 us both at 8192 x 3072 x 768)
   static const bool epi2 = [] {
     const char *e = std::getenv("TL_GEMM_EPI2");
-    return !(e && std::strcmp(e, "0") == 0);
+    return e && std::strcmp(e, "1") == 0;
   }();
   if (plan.bn == 256 && epi2 && g.gelu_out && !g.trans_a && !g.trans_b && !partial)
     return launch_variant<256, false, true, false, false, true>(g, plan, partial, s);
