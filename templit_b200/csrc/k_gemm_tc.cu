@@ -105,10 +105,12 @@ struct TcArgs {
 // PAIR: a CTA pair (cluster of 2) computes a 256 x BN tile with cta_group::2
 // products; each CTA loads its 128 rows of A and BN / 2 columns of B and
 // holds its 128 rows of the accumulator.
-// EPI2: two staging boxes per epilogue warp even for 256-wide tiles (one
-// fewer pipeline stage), for the GELU-output products, whose chunks leave
-// by two stores.
-template <int BN, bool SPLIT, bool PAIR = false, bool EPI2 = false>
+// BX: staging boxes per epilogue warp, 0 for the default (one for 256-wide
+// and 3xTF32 tiles, else two); 2 gives 256-wide tiles two (one fewer
+// pipeline stage, for the GELU-output products, whose chunks leave by two
+// stores); 1 gives narrower tiles one (one more pipeline stage, for
+// products whose epilogue reads no box).
+template <int BN, bool SPLIT, bool PAIR = false, int BX = 0>
 struct Cfg {
   static_assert(!(SPLIT && PAIR), "3xTF32 runs on single CTAs");
   static constexpr int THREADS = 64 + 32 * kEpiWarps + (SPLIT ? 32 * kConvWarps : 0);
@@ -122,7 +124,7 @@ struct Cfg {
   // staging boxes for the TMA stores: per epilogue warp two 32 x 32 fp32
   // boxes (4 KB each, 128-byte swizzled rows), one for the widest tile and
   // for 3xTF32 (whose stages are twice as large)
-  static constexpr int BOXES = ((BN == 256 && !EPI2) || SPLIT) ? 1 : 2;
+  static constexpr int BOXES = BX ? BX : ((BN == 256 || SPLIT) ? 1 : 2);
   static constexpr uint32_t OUT_BYTES = kEpiWarps * BOXES * 4096;
   static constexpr uint32_t BAR_BYTES = 384;
   static constexpr int STAGES_FIT =
@@ -182,10 +184,10 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t j) {
   return r * 128u + ((j ^ (r & 7u)) << 4);
 }
 
-template <int BN, bool A_MN, bool B_MN, bool SPLIT, bool PAIR, bool EPI2 = false>
-__global__ void __launch_bounds__(Cfg<BN, SPLIT, PAIR, EPI2>::THREADS, 1)
+template <int BN, bool A_MN, bool B_MN, bool SPLIT, bool PAIR, int BX = 0>
+__global__ void __launch_bounds__(Cfg<BN, SPLIT, PAIR, BX>::THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ TcMaps maps, const TcArgs t) {
-  using C = Cfg<BN, SPLIT, PAIR, EPI2>;
+  using C = Cfg<BN, SPLIT, PAIR, BX>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -945,9 +947,9 @@ TcPlan plan_tc(const GemmArgs &g) {
   return p;
 }
 
-template <int BN, bool A_MN, bool B_MN, bool SPLIT, bool PAIR, bool EPI2 = false>
+template <int BN, bool A_MN, bool B_MN, bool SPLIT, bool PAIR, int BX = 0>
 int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaStream_t s) {
-  using C = Cfg<BN, SPLIT, PAIR, EPI2>;
+  using C = Cfg<BN, SPLIT, PAIR, BX>;
   TcArgs t{};
   t.g = g;
   t.mt = (g.m + C::BMT - 1) / C::BMT;
@@ -1022,7 +1024,7 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
     return fail(TL_ERR_UNSUPPORTED, "tl_gemm: grouped outputs need 16-byte rows");
   static bool attr_set = false;
   if (!attr_set) {
-    int rc = check_cuda(cudaFuncSetAttribute(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT, PAIR, EPI2>,
+    int rc = check_cuda(cudaFuncSetAttribute(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT, PAIR, BX>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(C::SMEM)),
                         "tl_gemm smem attribute");
@@ -1032,11 +1034,11 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
   if constexpr (PAIR) {
     const uint64_t pairs = kNumSMs / 2;
     const uint64_t grid = 2 * (t.num_tiles < pairs ? t.num_tiles : pairs);
-    launch_pdl_cluster(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT, PAIR, EPI2>, static_cast<unsigned>(grid),
+    launch_pdl_cluster(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT, PAIR, BX>, static_cast<unsigned>(grid),
                        C::THREADS, C::SMEM, s, 2u, maps, t);
   } else {
     const uint64_t grid = t.num_tiles < static_cast<uint64_t>(kNumSMs) ? t.num_tiles : kNumSMs;
-    launch_pdl(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT, PAIR, EPI2>, static_cast<unsigned>(grid),
+    launch_pdl(tc_gemm_kernel<BN, A_MN, B_MN, SPLIT, PAIR, BX>, static_cast<unsigned>(grid),
                C::THREADS, C::SMEM, s, maps, t);
   }
   int rc = launch_status("tl_gemm tf32");
@@ -1109,9 +1111,22 @@ int launch_tc_gemm(const GemmArgs &g, void *workspace, size_t workspace_bytes, c
     return e && std::strcmp(e, "1") == 0;
   }();
   if (plan.bn == 256 && epi2 && g.gelu_out && !g.trans_a && !g.trans_b && !partial)
-    return launch_variant<256, false, true, false, false, true>(g, plan, partial, s);
+    return launch_variant<256, false, true, false, false, 2>(g, plan, partial, s);
   if (plan.bn == 256) return launch_bn<256>(g, plan, partial, s);
   if (plan.bn == 192) return launch_bn<192>(g, plan, partial, s);
+  // 128-wide products whose epilogue reads no box: one staging box per
+  // warp and one more pipeline stage (TL_GEMM_BOX1=1, tuning)
+  static const bool box1 = [] {
+    const char *e = std::getenv("TL_GEMM_BOX1");
+    return e && std::strcmp(e, "1") == 0;
+  }();
+  if (plan.bn == 128 && box1 && !g.addend && !g.gelu_grad_x && !g.gelu_out) {
+    const bool a_mn = g.trans_a != 0, b_mn = g.trans_b == 0;
+    if (a_mn && b_mn) return launch_variant<128, true, true, false, false, 1>(g, plan, partial, s);
+    if (a_mn) return launch_variant<128, true, false, false, false, 1>(g, plan, partial, s);
+    if (b_mn) return launch_variant<128, false, true, false, false, 1>(g, plan, partial, s);
+    return launch_variant<128, false, false, false, false, 1>(g, plan, partial, s);
+  }
   if (plan.bn == 128) return launch_bn<128>(g, plan, partial, s);
   return launch_bn<64>(g, plan, partial, s);
 }
