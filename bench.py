@@ -103,6 +103,7 @@ class ClockSampler:
         self.rows = []
         self.proc = None
         self.thread = None
+        self.start = 0
 
     def __enter__(self):
         try:
@@ -112,6 +113,12 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # nvidia-smi takes a moment to start: wait (at most 10 s) for its
+            # first row, so samples cover the timed region that follows
+            t0 = time.monotonic()
+            while not self.rows and self.proc.poll() is None and time.monotonic() - t0 < 10:
+                time.sleep(0.02)
+            self.start = len(self.rows)
         except OSError:
             self.proc = None
         return self
@@ -122,6 +129,11 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.proc:
+            # one more row when the region was shorter than the interval
+            t0, n = time.monotonic(), len(self.rows)
+            while (len(self.rows) == n and len(self.rows) < 3 and self.proc.poll() is None
+                   and time.monotonic() - t0 < 1):
+                time.sleep(0.02)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -132,14 +144,16 @@ class ClockSampler:
     def summary(self):
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
+        # the rows taken during the region (the one after it if none was)
+        rows = self.rows[self.start:] or self.rows[-1:]
+        sm = [float(r[1]) for r in rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows if len(r) >= 9
+        reasons = sorted({names[i] for r in rows if len(r) >= 9
                           for i in range(4) if r[5 + i].lower().startswith("active")})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(self.rows)}
+                "samples": len(rows)}
 
 
 # ------------------------------------------------------------ CPU baseline

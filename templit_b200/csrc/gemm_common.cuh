@@ -56,14 +56,19 @@ __device__ __forceinline__ void batch_offsets(const GemmArgs &g, uint64_t z,
 // backward, in the order of the reference's hadamard) - the reference adds the bias after
 // the product (EXPR_LINEAR: mult then add, include/passes/execute.h:241-252)
 // and gradient accumulation adds the new term to the old (context.h:74-89).
-__device__ __forceinline__ void epilogue_store(const GemmArgs &g, float *Cb,
-                                               uint64_t oc, size_t idx,
-                                               uint32_t n, float v) {
-  if (g.bias) v = v + g.bias[n];
+// `bias`: g.bias, or a group's bias of a grouped product.
+__device__ __forceinline__ void epilogue_store(const GemmArgs &g, float *Cb, const float *bias,
+                                               uint64_t oc, size_t idx, uint32_t n, float v) {
+  if (bias) v = v + bias[n];
   if (g.addend) v = g.addend[oc + idx] + v;
   if (g.gelu_grad_x) v = gelu_deriv_f(g.gelu_grad_x[oc + idx]) * v;
   Cb[idx] = v;
   if (g.gelu_out) g.gelu_out[oc + idx] = gelu_f(v);
+}
+__device__ __forceinline__ void epilogue_store(const GemmArgs &g, float *Cb,
+                                               uint64_t oc, size_t idx,
+                                               uint32_t n, float v) {
+  epilogue_store(g, Cb, g.bias, oc, idx, n, v);
 }
 
 int launch_sgemm(const GemmArgs &g, cudaStream_t s);

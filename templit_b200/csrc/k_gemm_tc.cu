@@ -818,18 +818,46 @@ bool make_operand_map(CUtensorMap *map, const float *base, uint64_t inner, uint6
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Slice sums of a split-K product in slice order, then the epilogue.
+// Slice sums of a split-K product in slice order, then the epilogue; one
+// launch for all groups of an N-grouped product (blockIdx.y: group, whose
+// slices follow the previous group's).  VEC: four columns per thread (N,
+// ldc and every epilogue operand 16-byte aligned).
+template <bool VEC>
 __global__ void __launch_bounds__(256)
-splitk_epilogue_kernel(const float *__restrict__ part, uint32_t splits, GemmArgs g) {
+splitk_epilogue_kernel(const float *__restrict__ part, uint32_t splits, uint32_t ngroups,
+                       const GemmArgs g) {
   pdl_enter();
+  const uint32_t grp = blockIdx.y;
+  float *C = ngroups > 1 ? g.cg[grp] : g.c;
+  const float *bias = ngroups > 1 ? g.biasg[grp] : g.bias;
   const uint64_t mn = static_cast<uint64_t>(g.m) * g.n;
+  const float *P = part + static_cast<uint64_t>(grp) * splits * mn;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
-  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < mn;
+  const uint64_t count = VEC ? mn / 4 : mn;
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
        i += stride) {
-    float v = part[i];
-    for (uint32_t s = 1; s < splits; ++s) v += part[s * mn + i];
-    const uint32_t n = static_cast<uint32_t>(i % g.n);
-    epilogue_store(g, g.c, 0, (i / g.n) * g.ldc + n, n, v);
+    if constexpr (VEC) {
+      const uint64_t e = 4 * i;
+      float4 v = __ldcg(reinterpret_cast<const float4 *>(P + e));
+      for (uint32_t s = 1; s < splits; ++s) {
+        const float4 w = __ldcg(reinterpret_cast<const float4 *>(P + s * mn + e));
+        v.x += w.x;
+        v.y += w.y;
+        v.z += w.z;
+        v.w += w.w;
+      }
+      const uint32_t n = static_cast<uint32_t>(e % g.n);
+      const size_t idx = (e / g.n) * g.ldc + n;
+      epilogue_store(g, C, bias, 0, idx, n, v.x);
+      epilogue_store(g, C, bias, 0, idx + 1, n + 1, v.y);
+      epilogue_store(g, C, bias, 0, idx + 2, n + 2, v.z);
+      epilogue_store(g, C, bias, 0, idx + 3, n + 3, v.w);
+    } else {
+      float v = P[i];
+      for (uint32_t s = 1; s < splits; ++s) v += P[s * mn + i];
+      const uint32_t n = static_cast<uint32_t>(i % g.n);
+      epilogue_store(g, C, bias, 0, (i / g.n) * g.ldc + n, n, v);
+    }
   }
 }
 
@@ -867,19 +895,37 @@ TcPlan plan_width(const GemmArgs &g, int max_bn) {
   p.splits = 1;
   p.kb_per_split = ktiles;
   // Few output tiles but a long K (weight gradients: K = every token of the
-  // batch): cut K so the tiles times slices fill the GPU, keeping at least 8
-  // k-tiles (256 of K) per slice.
+  // batch): cut K into slices of at least 8 k-tiles (256 of K).  The grid
+  // is persistent, one CTA per SM, so tiles x slices stay within one wave
+  // (148 + 14 CTAs would run a second pass of 14); the tile width and the
+  // slice count are picked together for the least work per SM, waves x
+  // k-tiles per slice x (width + ~64 columns of fixed cost): N = 384 as two
+  // 192-wide tiles, not two 256-wide ones with a quarter of the MMAs wasted.
   if (g.batch_count == 1 && tiles < static_cast<uint64_t>(kNumSMs) / 2 && ktiles >= 16 &&
       !g.c_heads) {
-    uint64_t want = (kNumSMs + tiles - 1) / tiles;
-    const uint64_t cap = ktiles / 8;
-    if (want > cap) want = cap;
-    if (want > 1) {
-      p.kb_per_split = static_cast<uint32_t>((ktiles + want - 1) / want);
-      p.splits = (ktiles + p.kb_per_split - 1) / p.kb_per_split;
+    uint64_t best = ~0ull;
+    const uint64_t mt = (g.m + BM - 1) / BM;
+    for (int bn : {64, 128, 192, 256}) {
+      if (bn > max_bn || (bn < p.bn && bn < 128) || (bn >= 2 * static_cast<int>(g.n) && bn > 64))
+        continue;
+      const uint64_t tl = outs * mt * ((g.n + bn - 1) / bn);
+      uint64_t want = kNumSMs / tl;
+      if (want > ktiles / 8) want = ktiles / 8;
+      if (want < 1) want = 1;
+      const uint64_t kb = (ktiles + want - 1) / want;
+      const uint64_t splits = (ktiles + kb - 1) / kb;
+      const uint64_t waves = (tl * splits + kNumSMs - 1) / kNumSMs;
+      const uint64_t cost = waves * kb * static_cast<uint64_t>(bn + 64);
+      if (cost < best) {
+        best = cost;
+        p.bn = bn;
+        p.kb_per_split = static_cast<uint32_t>(kb);
+        p.splits = static_cast<uint32_t>(splits);
+      }
+    }
+    if (p.splits > 1)
       p.workspace = static_cast<size_t>(p.splits) * (outs / g.batch_count) * g.m * g.n *
                     sizeof(float);
-    }
   }
   return p;
 }
@@ -1044,18 +1090,20 @@ int launch_variant(const GemmArgs &g, const TcPlan &plan, float *partial, cudaSt
   int rc = launch_status("tl_gemm tf32");
   if (rc || !partial) return rc;
   const uint64_t mn = static_cast<uint64_t>(g.m) * g.n;
-  for (uint32_t i = 0; i < ngroups; ++i) {
-    GemmArgs gi = g;
-    if (ngroups > 1) {
-      gi.c = gi.cg[i];
-      gi.bias = gi.biasg[i];
-    }
-    launch_pdl(splitk_epilogue_kernel, grid_for(mn, 256), 256, 0, s,
-               partial + static_cast<size_t>(i) * t.splits * mn, t.splits, gi);
-    rc = launch_status("tl_gemm split-K sum");
-    if (rc) return rc;
+  bool vec = g.n % 4 == 0 && g.ldc % 4 == 0;
+  for (uint32_t i = 0; i < ngroups && vec; ++i) {
+    const float *ci = ngroups > 1 ? g.cg[i] : g.c;
+    const float *bi = ngroups > 1 ? g.biasg[i] : g.bias;
+    vec = aligned16(ci) && (!bi || aligned16(bi));
   }
-  return TL_OK;
+  vec = vec && (!g.addend || aligned16(g.addend)) && (!g.gelu_out || aligned16(g.gelu_out)) &&
+        (!g.gelu_grad_x || aligned16(g.gelu_grad_x));
+  const dim3 grid(vec ? grid_for(mn / 4, 256) : grid_for(mn, 256), ngroups);
+  if (vec)
+    launch_pdl(splitk_epilogue_kernel<true>, grid, 256, 0, s, partial, t.splits, ngroups, g);
+  else
+    launch_pdl(splitk_epilogue_kernel<false>, grid, 256, 0, s, partial, t.splits, ngroups, g);
+  return launch_status("tl_gemm split-K sum");
 }
 
 template <int BN, bool SPLIT = false, bool PAIR = false>

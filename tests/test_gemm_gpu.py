@@ -353,10 +353,10 @@ def test_grouped_products(dev, precision):
     # weight gradients: X^T dY_g, K = 12288 (split-K slices per group)
     xl = r.standard_normal((12288, 384)).astype(np.float32)
     dys = [r.standard_normal((12288, 384)).astype(np.float32) for _ in range(3)]
-    outs = _grouped(dev, capi.TL_GEMM_GROUP_N, [xl], dys, 384, 384, 12288, True, False,
+    outs = _grouped(dev, capi.TL_GEMM_GROUP_N, [xl], dys, 384, 384, 12288, True, False, bs,
                     precision=precision)
-    for o, dy in zip(outs, dys):
-        check(o, ops.gemm(xl, dy, True, False), xl, dy, True, False)
+    for o, dy, b in zip(outs, dys, bs):  # one slice-sum launch, each group its bias
+        check(o - b, ops.gemm(xl, dy, True, False), xl, dy, True, False)
     # input gradient: sum_g dY_g W_g^T over the concatenated K
     gs = [r.standard_normal((2048, 384)).astype(np.float32) for _ in range(3)]
     (out,) = _grouped(dev, capi.TL_GEMM_GROUP_K, gs, ws, 2048, 384, 384, False, True,
