@@ -153,6 +153,22 @@ size_t tl_reduce_workspace_size(const uint32_t *x_shape, int x_rank,
                                 const uint32_t *out_shape, int out_rank);
 
 /*
+ * tl_reduce of up to TL_REDUCE_MAX_GROUPS tensors of one shape, x[i] ->
+ * out[i], each result bit-identical to tl_reduce(x[i]); the column
+ * reductions that fold their partials in-launch run as one launch for all
+ * groups.  Replaces consecutive Runtime::sum_to_shape calls on same-shape
+ * tensors (src/my_metal/runtime.cpp:595-745), which the runtime's optimiser
+ * groups: the bias gradients of the query, key and value projections.
+ * Workspace: tl_reduce_group_workspace_size() (groups x the single one).
+ */
+#define TL_REDUCE_MAX_GROUPS 4
+int tl_reduce_group(int op, uint32_t groups, const float *const *x, const uint32_t *x_shape,
+                    int x_rank, float *const *out, const uint32_t *out_shape, int out_rank,
+                    void *workspace, size_t workspace_bytes, void *stream);
+size_t tl_reduce_group_workspace_size(uint32_t groups, const uint32_t *x_shape, int x_rank,
+                                      const uint32_t *out_shape, int out_rank);
+
+/*
  * tl_reduce without a workspace argument; it allocates nothing.  No
  * counterpart in the reference: it exists for callers that cannot allocate
  * device memory when they reduce - code running while a CUDA stream is

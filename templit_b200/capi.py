@@ -30,6 +30,7 @@ TL_ADD, TL_SUB, TL_MUL, TL_DIV = range(4)
 TL_SCALAR_ADD, TL_SCALAR_DIV, TL_SCALAR_POW = range(3)
 TL_SIGMOID, TL_SQRT, TL_EXP, TL_GELU, TL_GELU_DERIVATIVE = range(5)
 TL_REDUCE_SUM, TL_REDUCE_MAX = range(2)
+TL_REDUCE_MAX_GROUPS = 4
 TL_GEMM_TF32, TL_GEMM_FP32, TL_GEMM_3XTF32 = range(3)
 
 
@@ -145,6 +146,9 @@ CUDA_ABI = {
     "tl_reduce": (c_int, [c_int, c_void_p, U32P, c_int, c_void_p, U32P, c_int,
                           c_void_p, c_size_t, c_void_p]),
     "tl_reduce_workspace_size": (c_size_t, [U32P, c_int, U32P, c_int]),
+    "tl_reduce_group": (c_int, [c_int, ctypes.c_uint32, c_void_p, U32P, c_int, c_void_p, U32P,
+                                c_int, c_void_p, c_size_t, c_void_p]),
+    "tl_reduce_group_workspace_size": (c_size_t, [ctypes.c_uint32, U32P, c_int, U32P, c_int]),
     "tl_reduce_noalloc": (c_int, [c_int, c_void_p, U32P, c_int, c_void_p, U32P, c_int,
                                   c_void_p]),
     "tl_reduce_noalloc_max_workspace": (c_size_t, []),

@@ -1112,11 +1112,13 @@ int launch_flash_probs(const AttnDims &d, const HeadView &q, const HeadView &k,
 __global__ void __launch_bounds__(1024)
 flash_mask_check_kernel(const float *__restrict__ mask, uint32_t T, uint32_t *flag) {
   pdl_enter();
+  // no early exit: the loads of an unrolled batch are all in flight at once
   bool ok = true;
   const uint64_t n = static_cast<uint64_t>(T) * T;
-  for (uint64_t i = threadIdx.x; i < n && ok; i += blockDim.x) {
+#pragma unroll 12
+  for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) {
     const uint32_t r = static_cast<uint32_t>(i / T), c = static_cast<uint32_t>(i % T);
-    ok = mask[i] == (c > r ? -INFINITY : 0.0f);
+    ok = ok & (__ldg(mask + i) == (c > r ? -INFINITY : 0.0f));
   }
   ok = __syncthreads_and(ok);
   if (threadIdx.x == 0) *flag = ok ? 1u : 0u;

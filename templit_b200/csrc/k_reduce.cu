@@ -120,15 +120,29 @@ static __device__ unsigned int g_col_tickets[kColTickets];
 // `fold` (several splits), the partial goes to part[c]; the last CTA of the
 // (k1, column block) to finish folds all splits' partials in split order
 // into out, in the same launch.
+// Grouped (g.grouped): blockIdx.y picks one of up to TL_REDUCE_MAX_GROUPS
+// independent [R, K2] reductions (K1 = 1), each with its own input,
+// partials and output; otherwise blockIdx.y is k1 of the one reduction.
+struct ColsGroups {
+  const float *x[TL_REDUCE_MAX_GROUPS];
+  float *part[TL_REDUCE_MAX_GROUPS];      // partials (`out` below)
+  float *fold_out[TL_REDUCE_MAX_GROUPS];  // null: no in-launch fold
+  uint32_t grouped;
+};
+
 template <int OP>
 __global__ void __launch_bounds__(256)
-cols_block_kernel(const float *__restrict__ x, float *out, uint32_t K1, uint32_t R,
-                  uint32_t K2, uint32_t rchunk, float *fold_out) {
+cols_block_kernel(const __grid_constant__ ColsGroups g, uint32_t K1, uint32_t R, uint32_t K2,
+                  uint32_t rchunk) {
   pdl_enter();
   __shared__ float4 part[8][32];
   __shared__ bool last;
+  const uint32_t gi = g.grouped ? blockIdx.y : 0;
+  const float *__restrict__ x = g.x[gi];
+  float *out = g.part[gi];
+  float *fold_out = g.fold_out[gi];
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t c = blockIdx.x, k1 = blockIdx.y;
+  const uint32_t c = blockIdx.x, k1 = g.grouped ? 0 : blockIdx.y;
   const uint32_t col = blockIdx.z * 128 + lane * 4;
   const uint32_t r0 = c * rchunk, r1 = min(R, r0 + rchunk);
   float4 acc = make_float4(rinit<OP>(), rinit<OP>(), rinit<OP>(), rinit<OP>());
@@ -176,7 +190,7 @@ cols_block_kernel(const float *__restrict__ x, float *out, uint32_t K1, uint32_t
   // publish this split's partial, then count arrivals of the column block
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned slot = k1 * gridDim.z + blockIdx.z;
+    const unsigned slot = blockIdx.y * gridDim.z + blockIdx.z;
     last = ticket_acq_rel(&g_col_tickets[slot], gridDim.x - 1) == gridDim.x - 1;
   }
   __syncthreads();
@@ -439,15 +453,19 @@ int run_plan(const ReducePlan &pl, const float *x, float *out, void *ws,
       const uint64_t outs = static_cast<uint64_t>(pl.K1) * pl.K2;
       const uint64_t work = (vec ? outs / 4 : outs) * pl.splits;
       const uint64_t slots = static_cast<uint64_t>(pl.K1) * ((pl.K2 + 127) / 128);
+      ColsGroups cg{};
+      cg.x[0] = x;
+      cg.part[0] = dst;
       if (pl.block && vec && pl.splits > 1 && slots <= kColTickets) {
         // one launch: the last CTA of each column block folds the splits
+        cg.fold_out[0] = out;
         launch_pdl(cols_block_kernel<OP>, dim3(pl.splits, pl.K1, (pl.K2 + 127) / 128), 256, 0, s,
-                   x, dst, pl.K1, pl.R, pl.K2, pl.chunk, out);
+                   cg, pl.K1, pl.R, pl.K2, pl.chunk);
         return launch_status("reduce cols");
       }
       if (pl.block && vec)
-        launch_pdl(cols_block_kernel<OP>, dim3(pl.splits, pl.K1, (pl.K2 + 127) / 128), 256, 0, s, 
-            x, dst, pl.K1, pl.R, pl.K2, pl.chunk, static_cast<float *>(nullptr));
+        launch_pdl(cols_block_kernel<OP>, dim3(pl.splits, pl.K1, (pl.K2 + 127) / 128), 256, 0, s,
+                   cg, pl.K1, pl.R, pl.K2, pl.chunk);
       else if (vec)
         launch_pdl(cols_kernel<OP, 4>, grid_for(work, 256, 16), 256, 0, s, x, dst, pl.K1, pl.R, pl.K2, pl.splits, pl.chunk);
       else
@@ -580,6 +598,62 @@ int tl_reduce(int op, const float *x, const uint32_t *x_shape, int x_rank,
   cudaStream_t s = as_stream(stream);
   return op == TL_REDUCE_SUM ? run_plan<TL_REDUCE_SUM>(pl, x, out, workspace, s)
                              : run_plan<TL_REDUCE_MAX>(pl, x, out, workspace, s);
+}
+
+size_t tl_reduce_group_workspace_size(uint32_t groups, const uint32_t *x_shape, int x_rank,
+                                      const uint32_t *out_shape, int out_rank) {
+  return groups * tl_reduce_workspace_size(x_shape, x_rank, out_shape, out_rank);
+}
+
+int tl_reduce_group(int op, uint32_t groups, const float *const *x, const uint32_t *x_shape,
+                    int x_rank, float *const *out, const uint32_t *out_shape, int out_rank,
+                    void *workspace, size_t workspace_bytes, void *stream) {
+  if (op != TL_REDUCE_SUM && op != TL_REDUCE_MAX)
+    return fail(TL_ERR_INVALID, "tl_reduce_group: unknown op");
+  if (groups < 1 || groups > TL_REDUCE_MAX_GROUPS)
+    return fail(TL_ERR_INVALID, "tl_reduce_group: 1 to TL_REDUCE_MAX_GROUPS groups");
+  if (!x || !out) return fail(TL_ERR_INVALID, "tl_reduce_group: null pointer");
+  ReducePlan pl;
+  int rc = make_plan(x_shape, x_rank, out_shape, out_rank, pl);
+  if (rc) return rc;
+  if (pl.numel == 0 || pl.out_count == 0) return TL_OK;
+  for (uint32_t i = 0; i < groups; ++i)
+    if (!x[i] || !out[i]) return fail(TL_ERR_INVALID, "tl_reduce_group: null pointer");
+  if (groups * pl.workspace > workspace_bytes || (pl.workspace && !workspace))
+    return fail(TL_ERR_INVALID, "tl_reduce_group: workspace too small");
+  if (pl.numel > 0xffffffffull)
+    return fail(TL_ERR_RANGE, "tl_reduce_group: more than 2^32-1 elements");
+  cudaStream_t s = as_stream(stream);
+  float *ws = static_cast<float *>(workspace);
+  const size_t ws_floats = pl.workspace / sizeof(float);
+  // one launch when every group folds its split partials in-launch: the
+  // same plan, grid and fold order as tl_reduce of each group alone
+  const uint64_t colblocks = (pl.K2 + 127) / 128;
+  bool one = pl.kind == kCols && pl.block && pl.K1 == 1 && pl.splits > 1 && pl.K2 % 4 == 0 &&
+             groups * colblocks <= kColTickets && aligned16(ws);
+  for (uint32_t i = 0; i < groups && one; ++i) one = aligned16(x[i]) && aligned16(out[i]);
+  if (one) {
+    ColsGroups cg{};
+    cg.grouped = 1;
+    for (uint32_t i = 0; i < groups; ++i) {
+      cg.x[i] = x[i];
+      cg.part[i] = ws + i * ws_floats;
+      cg.fold_out[i] = out[i];
+    }
+    const dim3 grid(pl.splits, groups, static_cast<unsigned>(colblocks));
+    if (op == TL_REDUCE_SUM)
+      launch_pdl(cols_block_kernel<TL_REDUCE_SUM>, grid, 256, 0, s, cg, 1u, pl.R, pl.K2, pl.chunk);
+    else
+      launch_pdl(cols_block_kernel<TL_REDUCE_MAX>, grid, 256, 0, s, cg, 1u, pl.R, pl.K2, pl.chunk);
+    return launch_status("reduce cols grouped");
+  }
+  for (uint32_t i = 0; i < groups; ++i) {
+    float *wi = pl.workspace ? ws + i * ws_floats : nullptr;
+    rc = op == TL_REDUCE_SUM ? run_plan<TL_REDUCE_SUM>(pl, x[i], out[i], wi, s)
+                             : run_plan<TL_REDUCE_MAX>(pl, x[i], out[i], wi, s);
+    if (rc) return rc;
+  }
+  return TL_OK;
 }
 
 size_t tl_argmax_workspace_size(size_t count) {

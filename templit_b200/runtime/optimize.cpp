@@ -25,7 +25,14 @@ Access access(const Op &op) {
   const auto &t = op.t;
   switch (op.kind) {
     case Kind::Binary: a.read(t[0]); a.read(t[1]); a.write(t[2]); break;
-    case Kind::Scalar: case Kind::Unary: case Kind::Copy: case Kind::Reduce: case Kind::Argmax:
+    case Kind::Reduce:  // + grouped reductions' (input, output) pairs
+      a.read(t[0]); a.write(t[1]);
+      for (size_t k = 0; k + 1 < op.group_refs.size(); k += 2) {
+        a.read(op.group_refs[k]);
+        a.write(op.group_refs[k + 1]);
+      }
+      break;
+    case Kind::Scalar: case Kind::Unary: case Kind::Copy: case Kind::Argmax:
     case Kind::Transpose: case Kind::Rms: case Kind::RmsNorm:
       a.read(t[0]); a.write(t[1]); break;
     case Kind::Softmax: a.read(t[0]); a.read(t[2]); a.read(t[3]); a.write(t[1]); break;
@@ -1920,6 +1927,67 @@ uint64_t eliminate_common(std::vector<Op> &p) {
   return folded;
 }
 
+// A sum over every dim but the last of a tensor whose rows are 16-byte
+// multiples: the bias gradient that Runtime::sum_to_shape computes for a
+// linear layer (include/nn/layer.h:16-39, bias [1, C]: [.., C] -> [1, C]).
+bool column_sum(const Op &op) {
+  if (op.dead || op.kind != Kind::Reduce || op.code != TL_REDUCE_SUM || !op.group_refs.empty())
+    return false;
+  const TRef &x = op.t[0], &y = op.t[1];
+  return x.p && y.p && x.rank >= 2 && y.numel() == x.last() && x.numel() > x.last() &&
+         x.last() % 4 == 0;
+}
+
+bool same_shape(const TRef &a, const TRef &b) {
+  if (a.rank != b.rank) return false;
+  for (int d = 0; d < a.rank; ++d)
+    if (a.shape[d] != b.shape[d]) return false;
+  return true;
+}
+
+// Column sums of same-shape tensors recorded close together (the bias
+// gradients of the query, key and value projections after the attention
+// backward) run as one grouped launch (tl_reduce_group, each result
+// bit-identical to its own reduction) at the last member's position: every
+// earlier member's input must be unchanged and its output untouched (not
+// read, written or released) until then, and no member may read or write
+// another's output.
+uint64_t group_column_sums(std::vector<Op> &p) {
+  uint64_t folded = 0;
+  for (size_t i = 0; i < p.size(); ++i) {
+    if (!column_sum(p[i])) continue;
+    std::vector<size_t> members{i};
+    for (size_t j = i + 1;
+         j < p.size() && j < i + 128 && members.size() < TL_REDUCE_MAX_GROUPS; ++j) {
+      const Op &y = p[j];
+      if (y.kind == Kind::MultiAdamW || y.kind == Kind::AllReduce) break;
+      if (!column_sum(y) || !same_shape(y.t[0], p[i].t[0]) || !same_shape(y.t[1], p[i].t[1]))
+        continue;
+      bool ok = true;
+      for (size_t k : members) {
+        const Op &z = p[k];
+        if (y.t[1].id == z.t[0].id || y.t[1].id == z.t[1].id || y.t[0].id == z.t[1].id ||
+            !unchanged_between(p, k, j, z.t[0].id) || !untouched_between(p, k, j, z.t[1].id))
+          ok = false;
+      }
+      if (ok) members.push_back(j);
+    }
+    if (members.size() < 2) continue;
+    const size_t at = members.back();
+    Op grouped = p[members.front()];
+    grouped.group_refs.clear();
+    for (size_t k = 1; k < members.size(); ++k) {
+      grouped.group_refs.push_back(p[members[k]].t[0]);
+      grouped.group_refs.push_back(p[members[k]].t[1]);
+    }
+    grouped.workspace = members.size() * p[members.front()].workspace;
+    for (size_t k : members) p[k].dead = true;
+    p[at] = std::move(grouped);
+    folded += members.size() - 1;
+  }
+  return folded;
+}
+
 bool is_opt(Kind k) {
   return k == Kind::SqNorm || k == Kind::Clip || k == Kind::AdamW;
 }
@@ -2096,6 +2164,7 @@ uint64_t optimize(std::vector<Op> &prog, void *comm, const Liveness *live, Flash
   folded += fuse_head_split_store(prog);
   folded += group_summed_products(prog);
   folded += group_shared_input(prog);
+  folded += group_column_sums(prog);
   folded += fuse_step(prog);
   if (comm) add_gradient_allreduce(prog);
   if (g_flash) resolve_flash(prog);

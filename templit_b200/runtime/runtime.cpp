@@ -574,6 +574,19 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashSt
         check(tl_copy(t[0].f(), t[1].f(), t[1].numel(), s), "copy");
         break;
       case Kind::Reduce:
+        if (!op.group_refs.empty()) {  // same-shape reductions grouped by the optimiser
+          const float *xs[TL_REDUCE_MAX_GROUPS] = {t[0].f()};
+          float *outs[TL_REDUCE_MAX_GROUPS] = {t[1].f()};
+          uint32_t n = 1;
+          for (size_t k = 0; k + 1 < op.group_refs.size() && n < TL_REDUCE_MAX_GROUPS; k += 2, ++n) {
+            xs[n] = op.group_refs[k].f();
+            outs[n] = op.group_refs[k + 1].f();
+          }
+          check(tl_reduce_group(op.code, n, xs, t[0].shape, t[0].rank, outs, t[1].shape,
+                                t[1].rank, ws, wsb, s),
+                "reduce group");
+          break;
+        }
         check(tl_reduce(op.code, t[0].f(), t[0].shape, t[0].rank, t[1].f(), t[1].shape, t[1].rank,
                         ws, wsb, s),
               "reduce");
@@ -804,6 +817,8 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashSt
       if (op.kind == Kind::Binary || op.kind == Kind::Unary || op.kind == Kind::Scalar ||
           op.kind == Kind::Reduce)
         key += "#" + std::to_string(op.code);
+      if (op.kind == Kind::Reduce && !op.group_refs.empty())
+        key += " g" + std::to_string(1 + op.group_refs.size() / 2);
       for (int i = 0; i < 3; ++i) {
         const TRef &r = op.t[i];
         if (!r.p || r.rank == 0) continue;
@@ -832,6 +847,8 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashSt
       default: {
         double b = 0.0;
         for (const TRef &r : op.t)
+          if (r.p) b += static_cast<double>(r.numel()) * 4.0;
+        for (const TRef &r : op.group_refs)  // grouped reductions
           if (r.p) b += static_cast<double>(r.numel()) * 4.0;
         return b;
       }

@@ -718,6 +718,48 @@ void mask_checked_once_per_program() {
   require(p[3].u0 == 1 && p[4].u0 == 0, "a write to the mask calls for a new check");
 }
 
+// bias gradients of the query, key and value projections (sum_to_shape of
+// dQ, dK, dV to [1, 384]) with other work between: one grouped reduction
+// at the last one's position; kept apart when an input changes or an output
+// is read in between
+void bias_gradients_grouped() {
+  auto sum = [](const TRef &x, const TRef &y) {
+    Op o = op(Kind::Reduce);
+    o.code = TL_REDUCE_SUM;
+    o.t[0] = x;
+    o.t[1] = y;
+    o.workspace = 4096;
+    return o;
+  };
+  auto dq = tensor({64, 192, 384}), dk = tensor({64, 192, 384}), dv = tensor({64, 192, 384});
+  auto bq = tensor({1, 384}), bk = tensor({1, 384}), bv = tensor({1, 384});
+  auto w = tensor({384, 384}), dx = tensor({64, 192, 384}), other = tensor({64, 192, 384});
+  std::vector<Op> p = {sum(dv, bv), gemm(dv, w, dx, 12288, 384, 384), sum(dk, bk),
+                       binary(TL_ADD, dx, dq, other), sum(dq, bq)};
+  optimize(p, nullptr);
+  auto l = live(p);
+  require(l.size() == 3 && l[2]->kind == Kind::Reduce && l[2]->group_refs.size() == 4 &&
+              l[2]->t[0].id == dv.id && l[2]->group_refs[0].id == dk.id &&
+              l[2]->group_refs[3].id == bq.id && l[2]->workspace == 3 * 4096,
+          "three column sums, one launch after the last");
+  // dk rewritten before its sum's group position: dv's sum stays alone
+  std::vector<Op> q = {sum(dv, bv), binary(TL_ADD, dq, dq, dv), sum(dk, bk)};
+  optimize(q, nullptr);
+  auto m = live(q);
+  require(m.size() == 3 && m[0]->group_refs.empty() && m[2]->group_refs.empty(),
+          "an input written in between keeps the sums apart");
+  // an output read before the group position
+  std::vector<Op> r = {sum(dv, bv), binary(TL_ADD, bv, bv, bk), sum(dk, bq)};
+  optimize(r, nullptr);
+  auto n = live(r);
+  require(n.size() == 3 && n[0]->group_refs.empty(), "an output read in between keeps them apart");
+  // different shapes
+  auto wide = tensor({64, 192, 1536}), bw = tensor({1, 1536});
+  std::vector<Op> s2 = {sum(dv, bv), sum(wide, bw)};
+  optimize(s2, nullptr);
+  require(live(s2).size() == 2, "different shapes are not grouped");
+}
+
 int main() {
   int failures = 0;
   const std::vector<std::pair<const char *, void (*)()>> cases = {
@@ -748,6 +790,7 @@ int main() {
       {"attention_backward_fused", attention_backward_fused},
       {"gelu_backward_into_gemm", gelu_backward_into_gemm},
       {"mask_checked_once_per_program", mask_checked_once_per_program},
+      {"bias_gradients_grouped", bias_gradients_grouped},
   };
   for (const auto &[name, fn] : cases) {
     try {

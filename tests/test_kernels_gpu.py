@@ -6,10 +6,13 @@ inputs, including ragged sizes and the edge cases the reference tests
 Tolerances: fp32 kernels vs the float64 oracle within rtol 1e-5 (the
 reference suite's eps 1e-5 / 1e-4 where it states them); integer and index
 results bit-exact."""
+import ctypes
+
 import numpy as np
 import pytest
 
 from oracle import ops
+from templit_b200 import capi
 from tests.helpers import Dev, known_answers
 from tests.test_oracle_golden import compare
 
@@ -207,6 +210,40 @@ def test_reduce_sum(dev, shape, out):
     # fp32 accumulation of n terms: bound by sum |x| (not by the result)
     scale = ops.sum_to_shape(np.abs(x), out).max()
     close(got, want, rtol=0, atol=1e-6 * scale + 1e-6)
+
+
+@pytest.mark.parametrize("shape,out,groups,op", [
+    ((64, 192, 384), (1, 384), 3, capi.TL_REDUCE_SUM),    # the q / k / v bias gradients
+    ((64, 192, 1536), (1536,), 4, capi.TL_REDUCE_SUM),
+    ((3000, 100), (1, 100), 2, capi.TL_REDUCE_MAX),       # ragged column block
+    ((1029, 36), (36,), 2, capi.TL_REDUCE_SUM),           # one launch per group
+    ((5, 7, 3), (5, 1, 3), 3, capi.TL_REDUCE_SUM),        # not a column reduction
+])
+def test_reduce_group_matches_single(dev, shape, out, groups, op):
+    """tl_reduce_group: each group's result bit-identical to tl_reduce of
+    that tensor alone (same plan, same fold order), on two calls in a row."""
+    r = rng(6)
+    xs = [r.standard_normal(shape).astype(np.float32) for _ in range(groups)]
+    kind = "sum" if op == capi.TL_REDUCE_SUM else "max"
+    want = [dev.reduce(kind, x, out) for x in xs]
+    sa, oa = capi.shape_arr(shape), capi.shape_arr(out)
+    nbytes = dev.lib.tl_reduce_group_workspace_size(groups, sa, len(shape), oa, len(out))
+    assert nbytes == groups * dev.lib.tl_reduce_workspace_size(sa, len(shape), oa, len(out))
+    ws = dev.ws(nbytes)
+    txs = [dev.t(x) for x in xs]
+    for _ in range(2):
+        outs = [dev.empty(out) for _ in range(groups)]
+        xp = (ctypes.c_void_p * groups)(*[t.data_ptr() for t in txs])
+        op_ = (ctypes.c_void_p * groups)(*[o.data_ptr() for o in outs])
+        dev.call("tl_reduce_group", op, groups, xp, sa, len(shape), op_, oa, len(out),
+                 dev.p(ws), nbytes, dev.stream)
+        for o, w in zip(outs, want):
+            np.testing.assert_array_equal(dev.host(o), w)
+    bad = (ctypes.c_void_p * 5)(*([txs[0].data_ptr()] * 5))
+    assert dev.lib.tl_reduce_group(op, 5, bad, sa, len(shape), bad, oa, len(out), dev.p(ws),
+                                   nbytes, dev.stream) == capi.TL_ERR_INVALID
+    assert dev.lib.tl_reduce_group(op, 0, bad, sa, len(shape), bad, oa, len(out), dev.p(ws),
+                                   nbytes, dev.stream) == capi.TL_ERR_INVALID
 
 
 @pytest.mark.parametrize("shape,out", [((2, 3), (2, 1)), ((64, 6, 192, 192), (64, 6, 192, 1)),
