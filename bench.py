@@ -157,7 +157,7 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------ CPU baseline
-def cpu_baseline_gpt(steps=1, batch=2):
+def cpu_baseline_gpt(steps=1, batch=2, warmup=1):
     """The same GPT step on the host: the oracle port of the reference's
     runtime ops (oracle/cpu_ref) driven by the reference's passes::Compiled,
     all host threads.  Bounded sample: `batch` sequences of 192 tokens."""
@@ -165,28 +165,32 @@ def cpu_baseline_gpt(steps=1, batch=2):
     if not cpu_gpt.available():
         return None
     threads = os.cpu_count() or 1
-    tok_s, secs = cpu_gpt.train_tokens_per_s(batch=batch, seq=SEQ, steps=steps, threads=threads)
+    tok_s, secs = cpu_gpt.train_tokens_per_s(batch=batch, seq=SEQ, steps=steps, threads=threads,
+                                             warmup=warmup)
     return {"value": tok_s, "unit": "tokens/s", "cores": threads, "kind": "port",
             "sample": f"{steps} GPT d384 train step(s) at batch {batch} x T {SEQ} "
-                      f"({secs:.1f} s of CPU work), oracle port of the reference runtime ops "
-                      "under the reference passes::Compiled executor"}
+                      f"({secs:.1f} s of CPU work) after {warmup} untimed, oracle port of the "
+                      "reference runtime ops under the reference passes::Compiled executor"}
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    base = cpu_baseline_gpt(steps=max(1, min(args.steps, 3)), batch=2)
+    warm = max(3, min(args.warmup, 5))
+    base = cpu_baseline_gpt(steps=max(1, min(args.steps, 3)), batch=2, warmup=warm)
     if base is None:
         print(json.dumps({"impl": "reference", "unavailable":
                           "oracle CPU GPT port (oracle/_build/libgpt_cpu.so) is not built"}))
         return 0
     line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tokens/s",
-            "n_gpus": args.gpus, "steps": max(1, min(args.steps, 3)), "warmup": 0,
+            "n_gpus": args.gpus, "steps": max(1, min(args.steps, 3)), "warmup": warm,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (Zipf(1.1) tokens, N(0,0.02) weights)",
-            "config": {"workload": WORKLOAD, "global_batch": 2, "seq_len": SEQ,
-                       "parallelism": "host threads"},
+            # the workload of the cuda arm; what ran is cpu_baseline.sample
+            "config": {"workload": WORKLOAD, "model": "nn::GPT<2048,192,384,6> (4 blocks)",
+                       "global_batch": args.batch * args.gpus, "seq_len": SEQ,
+                       "parallelism": f"dp{args.gpus}"},
             "cpu_baseline": base,
             "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}

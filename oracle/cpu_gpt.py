@@ -119,9 +119,10 @@ class OracleGPT:
             self.h = c_void_p()
 
 
-def train_tokens_per_s(batch, seq, steps, threads):
+def train_tokens_per_s(batch, seq, steps, threads, warmup=0):
     """Times `steps` GPT d384 training steps on the host oracle (all
-    `threads` OpenMP threads); returns (tokens/s, seconds)."""
+    `threads` OpenMP threads) after `warmup` untimed ones; returns
+    (tokens/s, seconds)."""
     from templit_b200.capi import TlgConfig
     os.environ.setdefault("OMP_NUM_THREADS", str(threads))
     cfg = TlgConfig(family=4, batch=batch, seq=seq, seed=1234, init_std=0.02, lr=3e-4,
@@ -133,6 +134,8 @@ def train_tokens_per_s(batch, seq, steps, threads):
         x = rng.integers(0, 2048, (batch, seq))
         y = rng.integers(0, 2048, (batch, seq))
         g.set_batch(x, y)
+        for _ in range(warmup):
+            g.train_step()
         t0 = time.perf_counter()
         for _ in range(steps):
             g.train_step()

@@ -1112,13 +1112,15 @@ int launch_flash_probs(const AttnDims &d, const HeadView &q, const HeadView &k,
 __global__ void __launch_bounds__(1024)
 flash_mask_check_kernel(const float *__restrict__ mask, uint32_t T, uint32_t *flag) {
   pdl_enter();
-  // no early exit: the loads of an unrolled batch are all in flight at once
+  // warp w takes rows w, w + 32, ...; its lanes read 32 consecutive columns
+  // at a time, a batch of them in flight (no early exit, no division)
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   bool ok = true;
-  const uint64_t n = static_cast<uint64_t>(T) * T;
-#pragma unroll 12
-  for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) {
-    const uint32_t r = static_cast<uint32_t>(i / T), c = static_cast<uint32_t>(i % T);
-    ok = ok & (__ldg(mask + i) == (c > r ? -INFINITY : 0.0f));
+  for (uint32_t r = warp; r < T; r += blockDim.x >> 5) {
+    const float *row = mask + static_cast<size_t>(r) * T;
+#pragma unroll 8
+    for (uint32_t c = lane; c < T; c += 32)
+      ok = ok & (__ldg(row + c) == (c > r ? -INFINITY : 0.0f));
   }
   ok = __syncthreads_and(ok);
   if (threadIdx.x == 0) *flag = ok ? 1u : 0u;
