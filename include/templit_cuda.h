@@ -315,6 +315,18 @@ int tl_multi_clip_adamw(const tl_param_slot *slots, uint32_t n_slots,
                         const float *decay, const float *lr, float epsilon,
                         void *workspace, size_t workspace_bytes, void *stream);
 size_t tl_multi_clip_adamw_workspace_size(uint32_t n_chunks);
+/*
+ * Copies every slot's gradient into one flat buffer (unpack = 0) or back
+ * out of it (unpack = 1), in the slots' chunk layout: slot i's element e at
+ * flat[chunk0 * TL_OPT_CHUNK + e]; `flat` holds n_chunks * TL_OPT_CHUNK
+ * floats (16-byte aligned) and the padding after each slot is left as it
+ * is.  Only `grad`, `count` and `chunk0` of the (device) slots are read.
+ * No counterpart in the reference, which has no multi-device path: the
+ * data-parallel gradient exchange runs as one NCCL all-reduce over `flat`
+ * instead of one per tensor.
+ */
+int tl_multi_grad_flat(const tl_param_slot *slots, uint32_t n_slots, uint32_t n_chunks,
+                       float *flat, int unpack, void *stream);
 
 /* ------------------------------------------------------------------- GEMM */
 enum tl_gemm_precision {

@@ -184,6 +184,7 @@ CUDA_ABI = {
                                     c_void_p, c_void_p, c_void_p, c_void_p, c_float,
                                     c_void_p, c_size_t, c_void_p]),
     "tl_multi_clip_adamw_workspace_size": (c_size_t, [c_uint32]),
+    "tl_multi_grad_flat": (c_int, [c_void_p, c_uint32, c_uint32, c_void_p, c_int, c_void_p]),
     "tl_gemm": (c_int, [POINTER(TlGemmDesc), c_void_p]),
     "tl_gemm_workspace_size": (c_size_t, [POINTER(TlGemmDesc)]),
     "tl_gemm_on_tensor_cores": (c_int, [POINTER(TlGemmDesc)]),

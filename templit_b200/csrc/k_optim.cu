@@ -253,6 +253,41 @@ multi_clip_adamw_kernel(const tl_param_slot *__restrict__ slots, uint32_t n_slot
 
 uint32_t norm_blocks(size_t n) { return grid_for((n + 3) / 4, kNormThreads, 4); }
 
+// Gradients <-> one flat buffer in the slots' chunk layout (slot i's
+// element e at flat[chunk0 * TL_OPT_CHUNK + e]): CTA b moves chunks b,
+// b + grid, ... (float4 when the gradient is 16-byte aligned).
+__global__ void __launch_bounds__(256)
+multi_grad_flat_kernel(const tl_param_slot *__restrict__ slots, uint32_t n_slots,
+                       uint32_t n_chunks, float *flat, int unpack) {
+  pdl_enter();
+  for (uint32_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+    const tl_param_slot &sl = slots[find_slot(slots, n_slots, c)];
+    const uint64_t begin = static_cast<uint64_t>(c - sl.chunk0) * TL_OPT_CHUNK;
+    const uint64_t end = min(sl.count, begin + TL_OPT_CHUNK);
+    float *g = sl.grad;
+    float *f = flat + static_cast<uint64_t>(sl.chunk0) * TL_OPT_CHUNK;
+    if (aligned16(g)) {  // begin is a multiple of TL_OPT_CHUNK: f + i is aligned too
+      const uint64_t vend = begin + ((end - begin) & ~static_cast<uint64_t>(3));
+      for (uint64_t i = begin + 4 * threadIdx.x; i < vend; i += 4 * blockDim.x) {
+        if (unpack)
+          *reinterpret_cast<float4 *>(g + i) = __ldcs(reinterpret_cast<const float4 *>(f + i));
+        else
+          *reinterpret_cast<float4 *>(f + i) = *reinterpret_cast<const float4 *>(g + i);
+      }
+      const uint64_t i = vend + threadIdx.x;  // the last 0 - 3 elements
+      if (i < end) {
+        if (unpack) g[i] = f[i];
+        else f[i] = g[i];
+      }
+    } else {
+      for (uint64_t i = begin + threadIdx.x; i < end; i += blockDim.x) {
+        if (unpack) g[i] = f[i];
+        else f[i] = g[i];
+      }
+    }
+  }
+}
+
 uint32_t multi_blocks(uint32_t n_chunks) {
   return n_chunks < static_cast<uint32_t>(kNumSMs * 4) ? n_chunks : kNumSMs * 4;
 }
@@ -316,6 +351,16 @@ int tl_adamw(const float *param, const float *grad, float *out, float *m1, float
 
 size_t tl_multi_clip_adamw_workspace_size(uint32_t n_chunks) {
   return static_cast<size_t>(multi_blocks(n_chunks)) * sizeof(float);
+}
+
+int tl_multi_grad_flat(const tl_param_slot *slots, uint32_t n_slots, uint32_t n_chunks,
+                       float *flat, int unpack, void *stream) {
+  if (n_slots == 0 || n_chunks == 0) return TL_OK;
+  if (!slots || !flat) return fail(TL_ERR_INVALID, "tl_multi_grad_flat: null pointer");
+  if (!aligned16(flat)) return fail(TL_ERR_INVALID, "tl_multi_grad_flat: flat not 16-byte aligned");
+  launch_pdl(multi_grad_flat_kernel, multi_blocks(n_chunks), 256, 0, as_stream(stream), slots,
+             n_slots, n_chunks, flat, unpack ? 1 : 0);
+  return launch_status("tl_multi_grad_flat");
 }
 
 int tl_multi_clip_adamw(const tl_param_slot *slots, uint32_t n_slots, uint32_t n_chunks,

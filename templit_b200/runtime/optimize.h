@@ -93,6 +93,10 @@ void add_gradient_allreduce(std::vector<Op> &prog);
 
 // Executes an AllReduce op: in-place ncclAllReduce(sum) of each gradient
 // in op.multi, grouped into one NCCL launch.
+// In-place sum across ranks of every gradient of an AllReduce op (one NCCL
+// group of per-tensor all-reduces).
 void all_reduce_gradients(const Op &op, void *comm, void *stream);
+// In-place sum across ranks of `count` floats at `flat` (one NCCL call).
+void all_reduce_flat(float *flat, size_t count, void *comm, void *stream);
 
 }  // namespace cuda::internal

@@ -177,6 +177,8 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashSt
   detail::Block slot_dev;
   void *slot_host = nullptr;
   size_t slot_capacity = 0;
+  // gradients packed for the data-parallel all-reduce (one NCCL call)
+  detail::Block flat_dev;
 
   // graph cache: program signature -> instantiated graph
   struct Cached {
@@ -515,6 +517,10 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashSt
       slot_host = nullptr;
     }
     slot_capacity = 0;
+    if (flat_dev.ptr) {
+      detail::release(flat_dev);
+      flat_dev = detail::Block{};
+    }
   }
 
   // ---- execution
@@ -522,6 +528,37 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashSt
     if (bytes <= workspace.bytes) return;
     if (workspace.ptr) detail::release(workspace);
     workspace = detail::allocate(bytes);
+  }
+
+  // TL_FLAT_ALLREDUCE=1: the packed all-reduce (one NCCL call over one
+  // flat buffer) instead of one NCCL group of per-tensor all-reduces.
+  static bool flat_allreduce() {
+    static const bool on = [] {
+      const char *e = std::getenv("TL_FLAT_ALLREDUCE");
+      return e && std::strcmp(e, "1") == 0;
+    }();
+    return on;
+  }
+
+  void ensure_flat(size_t bytes) {
+    if (bytes <= flat_dev.bytes) return;
+    if (flat_dev.ptr) detail::release(flat_dev);
+    flat_dev = detail::allocate(bytes);
+  }
+
+  // The all-reduce's slot table (gradient, count, chunk0 per tensor);
+  // returns the chunk count of the packed layout.
+  uint32_t stage_grad_slots(const Op &op, size_t base) {
+    tl_param_slot *h = static_cast<tl_param_slot *>(slot_host) + base;
+    uint32_t chunk = 0;
+    for (size_t i = 0; i < op.multi.size(); ++i) {
+      h[i] = tl_param_slot{};
+      h[i].grad = op.multi[i].grad.f();
+      h[i].count = op.multi[i].grad.numel();
+      h[i].chunk0 = chunk;
+      chunk += static_cast<uint32_t>((h[i].count + TL_OPT_CHUNK - 1) / TL_OPT_CHUNK);
+    }
+    return chunk;
   }
 
   void ensure_slots(size_t count) {
@@ -701,9 +738,24 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashSt
               "fused clip + AdamW");
         break;
       }
-      case Kind::AllReduce:
-        internal::all_reduce_gradients(op, comm, s);
+      case Kind::AllReduce: {
+        if (!flat_allreduce()) {
+          internal::all_reduce_gradients(op, comm, s);
+          break;
+        }
+        // pack every gradient into one buffer, one NCCL sum, unpack
+        const uint32_t chunks = stage_grad_slots(op, slot_base);
+        tl_param_slot *dev = static_cast<tl_param_slot *>(slot_dev.ptr) + slot_base;
+        check(tl_memcpy_h2d(dev, static_cast<tl_param_slot *>(slot_host) + slot_base,
+                            op.multi.size() * sizeof(tl_param_slot), s),
+              "all-reduce slots");
+        const uint32_t n = static_cast<uint32_t>(op.multi.size());
+        float *flat = static_cast<float *>(flat_dev.ptr);
+        check(tl_multi_grad_flat(dev, n, chunks, flat, 0, s), "gradient pack");
+        internal::all_reduce_flat(flat, static_cast<size_t>(chunks) * TL_OPT_CHUNK, comm, s);
+        check(tl_multi_grad_flat(dev, n, chunks, flat, 1, s), "gradient unpack");
         break;
+      }
       case Kind::Attention: {
         tl_attn_desc d = op.attn;
         d.workspace = ws;
@@ -784,7 +836,8 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashSt
     for (const Op &op : prog) {
       if (op.dead) continue;
       execute(op, s, slot_base);
-      if (op.kind == Kind::MultiAdamW) slot_base += op.multi.size();
+      if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce)
+        slot_base += op.multi.size();
     }
   }
 
@@ -865,7 +918,8 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashSt
     for (size_t i = 0; i < ops.size(); ++i) {
       check(tl_event_record(ev[i], s), "profile event");
       execute(*ops[i], s, slot_base);
-      if (ops[i]->kind == Kind::MultiAdamW) slot_base += ops[i]->multi.size();
+      if (ops[i]->kind == Kind::MultiAdamW || ops[i]->kind == Kind::AllReduce)
+        slot_base += ops[i]->multi.size();
     }
     check(tl_event_record(ev.back(), s), "profile event");
     for (size_t i = 0; i < ops.size(); ++i) {
@@ -881,16 +935,22 @@ struct Runtime::Impl : internal::Recorder, internal::Liveness, internal::FlashSt
 
   void run_program() {
     void *s = cuda::stream();
-    size_t ws = 0, slots = 0;
+    size_t ws = 0, slots = 0, flat_chunks = 0;
     uint64_t live = 0;
     for (const Op &op : prog) {
       if (op.dead) continue;
       ws = std::max(ws, op.kind == Kind::Gemm ? tl_gemm_workspace_size(&op.gemm) : op.workspace);
-      if (op.kind == Kind::MultiAdamW) slots += op.multi.size();
+      if (op.kind == Kind::MultiAdamW || op.kind == Kind::AllReduce) slots += op.multi.size();
+      if (op.kind == Kind::AllReduce) {
+        size_t c = 0;
+        for (const auto &m : op.multi) c += (m.grad.numel() + TL_OPT_CHUNK - 1) / TL_OPT_CHUNK;
+        flat_chunks = std::max(flat_chunks, c);
+      }
       if (op.kind != Kind::Release) ++live;
     }
     ensure_workspace(ws);
     if (slots) ensure_slots(slots);
+    if (flat_chunks && flat_allreduce()) ensure_flat(flat_chunks * TL_OPT_CHUNK * sizeof(float));
     stats.ops_launched += live;
     const uint64_t k0 = tl_kernel_launches();
     if (profiling) {

@@ -396,6 +396,45 @@ def test_embedding_ids_out_of_range_flag(dev):
     assert dev.status() == 0
 
 
+def test_multi_grad_flat_round_trip(dev):
+    """tl_multi_grad_flat: every gradient lands at chunk0 * TL_OPT_CHUNK of
+    the flat buffer, padding untouched, and unpacking writes the buffer back
+    (the packed all-reduce of the data-parallel step); one gradient starts
+    4 bytes past an aligned address (the element-wise path)."""
+    r = rng(12)
+    sizes = [384 * 384, 384, 1, 8191, 8193, 5, 3 * 8192]
+    base = dev.t(np.zeros(sum(sizes) + 64 * (len(sizes) + 1), np.float32))
+    grads, off = [], 0
+    for i, s in enumerate(sizes):
+        if i == 5:
+            off += 1  # unaligned
+        grads.append(base[off:off + s])
+        off = (off + s + 63) // 64 * 64
+    vals = [r.standard_normal(s).astype(np.float32) for s in sizes]
+    for g, v in zip(grads, vals):
+        g.copy_(dev.t(v))
+    slots = (capi.TlParamSlot * len(sizes))()
+    chunk = 0
+    for i, s in enumerate(sizes):
+        slots[i].grad = grads[i].data_ptr()
+        slots[i].count = s
+        slots[i].chunk0 = chunk
+        chunk += (s + capi.TL_OPT_CHUNK - 1) // capi.TL_OPT_CHUNK
+    dslots = dev.t(np.frombuffer(bytes(slots), np.uint8), dtype=np.uint8)
+    flat = dev.t(np.full(chunk * capi.TL_OPT_CHUNK, 7.0, np.float32))
+    dev.call("tl_multi_grad_flat", dev.p(dslots), len(sizes), chunk, dev.p(flat), 0, dev.stream)
+    f = dev.host(flat)
+    for i, s in enumerate(sizes):
+        o = slots[i].chunk0 * capi.TL_OPT_CHUNK
+        np.testing.assert_array_equal(f[o:o + s], vals[i])
+        nxt = slots[i + 1].chunk0 * capi.TL_OPT_CHUNK if i + 1 < len(sizes) else f.size
+        assert np.all(f[o + s:nxt] == 7.0)
+    flat.mul_(2.0)
+    dev.call("tl_multi_grad_flat", dev.p(dslots), len(sizes), chunk, dev.p(flat), 1, dev.stream)
+    for g, v in zip(grads, vals):
+        np.testing.assert_array_equal(dev.host(g), 2.0 * v)
+
+
 def test_multi_tensor_clip_adamw_matches_per_tensor(dev):
     """tl_multi_clip_adamw == norm + clip + AdamW per tensor (compile.h:236-258)."""
     import ctypes
